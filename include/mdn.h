@@ -1,0 +1,255 @@
+/*
+ * mdn.h - C-ABI of the B200-native metal-drone-nav rollout/PPO hot path.
+ *
+ * The reference exposes this path as an Objective-C++ class API:
+ *   Metal   (main.mm:44-72)    device, buffers, dispatch, finish()
+ *   Sim     (main.mm:516-603)  batched environment: reset/set_config/collect/report
+ *   PPOTrainer (main.mm:1110-1476) GAE, clipped PPO, clip+Adam, checkpoints
+ * consumed by navigation_training.hpp:7-170 and train_navigation (main.mm:1805-1862).
+ * Each entry point below replaces one method of those classes; the comment names
+ * the reference member it stands in for. Plain pointers and sizes only: no CUDA,
+ * torch or C++ types cross this boundary.
+ *
+ * Conventions
+ *  - Every call returns an int status (MDN_OK == 0). On failure a message is kept
+ *    per thread and returned by mdn_last_error().
+ *  - Host memory passed in is owned by the caller; device memory is owned by the
+ *    library (mdn_sim owns every per-environment buffer, mdn_ppo its optimizer
+ *    state), mirroring Sim/PPOTrainer ownership in main.mm.
+ *  - One CUDA stream per mdn_sim. Calls are stream-ordered; mdn_sync() is the
+ *    reference's Metal::finish (commit + wait + error check).
+ *  - Handles are not thread-safe; one host thread drives one handle.
+ */
+#ifndef MDN_H
+#define MDN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MDN_ABI_VERSION 1u
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+    MDN_OK = 0,
+    MDN_ERR_INVALID = 1,   /* bad argument or unsupported configuration      */
+    MDN_ERR_CUDA = 2,      /* CUDA runtime error (message has the cause)      */
+    MDN_ERR_NOMEM = 3,     /* device or host allocation failed                */
+    MDN_ERR_TIMEOUT = 4,   /* a bounded device or host wait gave up           */
+    MDN_ERR_IO = 5,        /* file read/write failed                          */
+    MDN_ERR_MISMATCH = 6,  /* checkpoint/config mismatch on resume            */
+    MDN_ERR_NCCL = 7,      /* NCCL communicator error                         */
+    MDN_ERR_STATE = 8      /* call out of order (e.g. update before collect)  */
+};
+
+/* ---- byte-identical POD layouts (the on-disk and device ABI) ----------- */
+
+/* RLPhysicsState, physics.hpp:12-18 (68 bytes). */
+typedef struct mdn_physics_state {
+    float position[3];
+    float orientation_wxyz[4];
+    float linear_velocity[3];
+    float angular_velocity_body[3];
+    float rpm[4];
+} mdn_physics_state;
+
+/* RLPhysicsParams, physics.hpp:20-38 (352 bytes). */
+typedef struct mdn_physics_params {
+    float rotor_positions[12];
+    float rotor_thrust_directions[12];
+    float rotor_torque_directions[12];
+    float rotor_thrust_coefficients[12];
+    float rotor_torque_constants[4];
+    float rotor_time_constants_rising[4];
+    float rotor_time_constants_falling[4];
+    float inertia[9];
+    float inertia_inverse[9];
+    float gravity_world[3];
+    float mass;
+    float action_min;
+    float action_max;
+    float dt;
+    float position_limit;
+    float velocity_limit;
+    float angular_velocity_limit;
+} mdn_physics_params;
+
+/* WObstacle / WWorld, world.hpp:28-29 (40 and 676 bytes). kind: 0 box,
+ * 1 sphere, 2 vertical cylinder, 3 bounded moving sphere. */
+typedef struct mdn_obstacle {
+    uint32_t kind;
+    float center[3], size[3], velocity[3];
+} mdn_obstacle;
+typedef struct mdn_world {
+    mdn_obstacle obstacles[16];
+    uint32_t count, seed, family;
+    float goal[3], wind[3];
+} mdn_world;
+
+/* SimRun, sim.metal:2-8 / main.mm:454-459 (184 bytes). */
+typedef struct mdn_sim_run {
+    float hidden[16], motors[4], previous_nav[4], desired_velocity[3], yaw;
+    uint32_t rng, steps;
+    float path, elapsed, peak_speed, min_clearance, initial_distance;
+    uint32_t successes, collisions, timeouts, episodes;
+    float success_time, total_path, total_elapsed, final_progress, reference_position[3];
+} mdn_sim_run;
+
+/* SimConfig, main.mm:461-464 (84 bytes). Defaults in mdn_sim_config_default. */
+typedef struct mdn_sim_config {
+    uint32_t n, tick, mode, family, substeps, sensor_period, sensor_delay, command_delay, max_steps, seed, eval;
+    float speed, distance, wind, depth_noise, dropout, risk_coef, entropy_coef, learning_rate;
+    uint32_t velocity_contract, geometry_memory;
+} mdn_sim_config;
+
+/* RaptorWeights, raptor.hpp:11-21 (2,084 floats, 8,336 bytes). */
+typedef struct mdn_raptor_weights {
+    float input_weights[16 * 22];
+    float input_bias[16];
+    float gru_input_weights[48 * 16];
+    float gru_hidden_weights[48 * 16];
+    float gru_input_bias[48];
+    float gru_hidden_bias[48];
+    float initial_hidden_state[16];
+    float output_weights[4 * 16];
+    float output_bias[4];
+} mdn_raptor_weights;
+
+/* Shape of one rollout that the reference fixes at compile time or hard-codes.
+ * Zero-initialised fields take the reference value (listed). */
+typedef struct mdn_rollout_shape {
+    uint32_t actor_obs_dim;     /* 184: 2x80 pooled depth + 21 context + 3 hint (ppo.hpp:26-34) */
+    uint32_t critic_obs_dim;    /* 32 (ppo.hpp:14-16)                                        */
+    uint32_t actor_hidden;      /* 64 (ppo.hpp:17-19)                                        */
+    uint32_t critic_hidden;     /* 64                                                        */
+    uint32_t flags;             /* MDN_SHAPE_* bits                                          */
+    float room_min[3];          /* wray/wclearance room, world.hpp:73-74,85: (-2,-5,0)       */
+    float room_max[3];          /*                                        (14, 5,5)          */
+} mdn_rollout_shape;
+#define MDN_SHAPE_CUSTOM_ROOM 1u /* use room_min/room_max instead of the reference room */
+
+/* PpoCheckpointHeader prefix layout, main.mm:984-991 (136 bytes). */
+typedef struct mdn_checkpoint_header {
+    char magic[8];
+    uint32_t version, actor_count, critic_count, horizon, n, family;
+    uint32_t base_seed, completed_rollouts;
+    uint64_t optimizer_step;
+    mdn_sim_config config;
+} mdn_checkpoint_header;
+
+/* Buffer ids for mdn_sim_buffer / download / upload. They name the public
+ * members of the reference Sim (main.mm:517-518). */
+enum {
+    MDN_BUF_STATES = 0,       /* mdn_physics_state[n]                         */
+    MDN_BUF_RUNS = 1,         /* mdn_sim_run[n]                               */
+    MDN_BUF_WORLDS = 2,       /* mdn_world[n]                                 */
+    MDN_BUF_SENSORS = 3,      /* float[n][8][320] range ring (metres)         */
+    MDN_BUF_POSES = 4,        /* float[n][8][12] camera pose ring             */
+    MDN_BUF_COMMANDS = 5,     /* float[n][8][4] command ring                  */
+    MDN_BUF_ACTOR = 6,        /* float[actor_param_count]                     */
+    MDN_BUF_CRITIC = 7,       /* float[critic_param_count]                    */
+    MDN_BUF_OBS = 8,          /* float[T][n][actor_obs_dim]                   */
+    MDN_BUF_CO = 9,           /* float[T][n][critic_obs_dim]                  */
+    MDN_BUF_ACTIONS = 10,     /* float[T][n][4]                               */
+    MDN_BUF_LOGP = 11,        /* float[T][n]                                  */
+    MDN_BUF_VALUES = 12,      /* float[T][n]                                  */
+    MDN_BUF_REWARDS = 13,     /* float[T][n]                                  */
+    MDN_BUF_NEXT_VALUES = 14, /* float[T][n]                                  */
+    MDN_BUF_TERMINATED = 15,  /* uint8[T][n]                                  */
+    MDN_BUF_TRUNCATED = 16,   /* uint8[T][n]                                  */
+    MDN_BUF_ADVANTAGES = 17,  /* float[T][n]                                  */
+    MDN_BUF_RETURNS = 18,     /* float[T][n]                                  */
+    MDN_BUF_RAPTOR = 19,      /* mdn_raptor_weights                           */
+    MDN_BUF_PHYSICS = 20,     /* mdn_physics_params                           */
+    MDN_BUF_CONTACT_ID = 21,  /* int32[T][n] nearest-obstacle id at the step's
+                                 closest approach (-1 = room walls)           */
+    MDN_BUF_COUNT = 22
+};
+
+/* ---- library / device --------------------------------------------------- */
+const char* mdn_last_error(void);
+uint32_t mdn_abi_version(void);
+void mdn_sim_config_default(mdn_sim_config* out);              /* SimConfig{} defaults, main.mm:462-463 */
+void mdn_rollout_shape_default(mdn_rollout_shape* out);
+void mdn_physics_crazyflie_default(mdn_physics_params* out);   /* rl_physics_crazyflie_default, physics.hpp:184-219 */
+/* Parse a RAPTOR1 file (raptor.hpp:25-40). Returns MDN_ERR_IO on a bad file. */
+int mdn_raptor_load(const char* path, mdn_raptor_weights* out);
+
+typedef struct mdn_device mdn_device;
+typedef struct mdn_sim mdn_sim;
+typedef struct mdn_ppo mdn_ppo;
+
+int mdn_device_open(int gpu, mdn_device** out);                 /* Metal::Metal, main.mm:50-52 */
+int mdn_device_close(mdn_device* dev);
+/* Metal::finish (main.mm:71): wait for all work queued on the device's sims and
+ * trainers, raise any device error, return the GPU time since the last sync. */
+int mdn_sync(mdn_device* dev, double* gpu_seconds);
+
+/* ---- simulator: Sim (main.mm:516-603) ----------------------------------- */
+/* Sim::Sim(Metal&, SimConfig, horizon) main.mm:529-566. raptor/physics may be
+ * NULL (then: weights from mdn_raptor_load of the packaged RAPTOR1 file is
+ * required, so NULL raptor is MDN_ERR_INVALID; physics NULL = Crazyflie). The
+ * actor and critic are initialised exactly as main.mm:548-555 (seed 1789). */
+int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const mdn_rollout_shape* shape,
+                   uint32_t horizon, const mdn_raptor_weights* raptor,
+                   const mdn_physics_params* physics, mdn_sim** out);
+int mdn_sim_destroy(mdn_sim* sim);
+int mdn_sim_reset(mdn_sim* sim);                                 /* Sim::reset, main.mm:568 */
+int mdn_sim_set_config(mdn_sim* sim, const mdn_sim_config* cfg); /* Sim::set_config, main.mm:567 */
+int mdn_sim_get_config(mdn_sim* sim, mdn_sim_config* out);       /* Sim::cfg */
+/* Sim::collect(cb, count), main.mm:576-598: `steps` policy steps (0 = horizon)
+ * starting at tick 0, rows written at tick % horizon. */
+int mdn_sim_collect(mdn_sim* sim, uint32_t steps);
+/* One policy step at an explicit tick (teacher-forced parity runs). */
+int mdn_sim_step(mdn_sim* sim, uint32_t tick);
+int mdn_sim_buffer(mdn_sim* sim, int id, void** dev_ptr, size_t* bytes);
+/* Replacements for host access to MTLBuffer.contents (navigation_training.hpp:23-24). */
+int mdn_sim_download(mdn_sim* sim, int id, void* host, size_t offset, size_t bytes);
+int mdn_sim_upload(mdn_sim* sim, int id, const void* host, size_t offset, size_t bytes);
+/* Sim::report aggregates (main.mm:599-602): out[0..9] = episodes, successes,
+ * collisions, timeouts, success_time, total_path, total_elapsed, final_progress,
+ * min_clearance, peak_speed. */
+int mdn_sim_report(mdn_sim* sim, double out[10]);
+int mdn_sim_dims(mdn_sim* sim, uint32_t* n, uint32_t* horizon, uint32_t* actor_params, uint32_t* critic_params);
+/* Device time of the last mdn_sim_collect (CUDA events on the sim stream). */
+int mdn_sim_last_collect_ms(mdn_sim* sim, float* ms);
+
+/* ---- trainer: PPOTrainer (main.mm:1110-1476) ----------------------------- */
+/* PPOTrainer(Sim&, epochs) main.mm:1159-1208; epochs 1..4; minibatch_rows 0 =
+ * the reference's 256 rows (main.mm:1115). */
+int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_rows, mdn_ppo** out);
+int mdn_ppo_destroy(mdn_ppo* ppo);
+/* PPOTrainer::rollout_update(cb, rollout_index), main.mm:1321-1384. */
+int mdn_ppo_rollout_update(mdn_ppo* ppo, uint32_t rollout_index);
+/* PPOTrainer::metric_mean: policy, value, entropy, ratio means (main.mm:1383). */
+int mdn_ppo_metrics(mdn_ppo* ppo, float out[4]);
+int mdn_ppo_state(mdn_ppo* ppo, uint64_t* optimizer_step, uint32_t* completed_rollouts);
+int mdn_ppo_set_state(mdn_ppo* ppo, uint64_t optimizer_step, uint32_t completed_rollouts);
+/* Adam moments: which = 0 actor m, 1 actor v, 2 critic m, 3 critic v. */
+int mdn_ppo_moments(mdn_ppo* ppo, int which, float* host, size_t count, int upload);
+/* Pre-clip gradient norms of the last update (actor, critic), grad_norm_rows. */
+int mdn_ppo_grad_norms(mdn_ppo* ppo, float* host_rows, size_t count);
+/* Device time of the last rollout update (CUDA events). */
+int mdn_ppo_last_update_ms(mdn_ppo* ppo, float* ms);
+/* PPOTrainer::save_checkpoint / load_checkpoint (main.mm:1209-1320): PPOFIX1 v6. */
+int mdn_ppo_checkpoint_save(mdn_ppo* ppo, const char* path, uint32_t family, uint32_t seed,
+                            uint32_t completed_rollouts);
+int mdn_ppo_checkpoint_load(mdn_ppo* ppo, const char* path, uint32_t family, uint32_t horizon,
+                            uint32_t n, uint32_t seed);
+
+/* ---- multi-GPU (no reference counterpart: the reference is one Apple GPU) */
+/* Fill a 128-byte NCCL unique id (rank 0) to share through any host channel. */
+int mdn_comm_unique_id(uint8_t id[128]);
+/* Attach a communicator to the device. Sims created afterwards on this device
+ * hold global env ids [rank*n, (rank+1)*n) and their PPO updates allreduce
+ * gradients and advantage statistics across `world` ranks. */
+int mdn_comm_init(mdn_device* dev, int rank, int world, const uint8_t id[128]);
+int mdn_comm_destroy(mdn_device* dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MDN_H */
