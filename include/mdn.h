@@ -232,6 +232,14 @@ int mdn_ppo_set_state(mdn_ppo* ppo, uint64_t optimizer_step, uint32_t completed_
 int mdn_ppo_moments(mdn_ppo* ppo, int which, float* host, size_t count, int upload);
 /* Pre-clip gradient norms of the last update (actor, critic), grad_norm_rows. */
 int mdn_ppo_grad_norms(mdn_ppo* ppo, float* host_rows, size_t count);
+/* Host-only form of the same order (no device needed): `rows` rollout rows
+ * split into `minibatch`-row chunks. `count` must be epochs*ceil(rows/minibatch). */
+int mdn_minibatch_order(uint32_t rows, uint32_t minibatch, uint32_t epochs, uint32_t rollout_index, uint32_t* out,
+                        size_t count);
+/* Minibatch chunk order the trainer uses for `rollout_index`: epochs x chunks
+ * first-row indices, drawn as main.mm:1331-1337 draws them (std::mt19937 +
+ * std::shuffle, reshuffled at epoch 1). `count` must be epochs*chunks. */
+int mdn_ppo_minibatch_order(mdn_ppo* ppo, uint32_t rollout_index, uint32_t* out, size_t count);
 /* Device time of the last rollout update (CUDA events). */
 int mdn_ppo_last_update_ms(mdn_ppo* ppo, float* ms);
 /* PPOTrainer::save_checkpoint / load_checkpoint (main.mm:1209-1320): PPOFIX1 v6. */

@@ -1,7 +1,21 @@
 """B200-native metal-drone-nav rollout/PPO hot path (host side).
 
-The compute path is libmdn.so (CUDA kernels for sm_100a behind the C-ABI in
-include/mdn.h). This package is a thin Python veneer over that C-ABI with the
-reference's host API names (Sim, PPOTrainer; main.mm:516-603,1110-1476).
+The compute path is libmdn.so: CUDA kernels for sm_100a behind the C-ABI in
+include/mdn.h (built from csrc/ by build()). This package is a thin Python
+veneer over that C-ABI with the reference's host API names (Sim, PPOTrainer;
+main.mm:516-603,1110-1476). There is no CPU fallback: without libmdn.so the
+constructors raise.
 """
+import pathlib
+import subprocess
+
 from . import layouts  # noqa: F401
+from .capi import Device, MdnError, PPOTrainer, Sim, default_raptor, lib  # noqa: F401
+
+PACKAGE_DIR = pathlib.Path(__file__).resolve().parent
+
+
+def build(jobs=8):
+    """Compile libmdn.so for sm_100a in-tree (nvcc cross-compiles without a GPU)."""
+    subprocess.run(["make", "-s", "-j", str(jobs), "-C", str(PACKAGE_DIR / "csrc")], check=True)
+    return PACKAGE_DIR / "libmdn.so"

@@ -1,0 +1,284 @@
+"""ctypes binding of libmdn.so (include/mdn.h) with the reference host API.
+
+`Device`, `Sim` and `PPOTrainer` mirror the reference's Metal, Sim and
+PPOTrainer classes (main.mm:44-72, 516-603, 1110-1476): same method names and
+argument meaning, errors raised as exceptions (the reference's require()
+throws std::runtime_error, main.mm:27). Buffers the reference exposes as
+MTLBuffer.contents are reached with download/upload (host copies).
+
+The CUDA library is required: constructing a Device without libmdn.so raises.
+"""
+import ctypes
+import os
+import pathlib
+
+import numpy as np
+
+from . import layouts
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = HERE / "libmdn.so"
+RAPTOR_PATH = HERE / "assets" / "raptor.bin"
+
+_P = ctypes.c_void_p
+_U = ctypes.c_uint32
+_lib = None
+
+
+class MdnError(RuntimeError):
+    """A non-zero status from libmdn; .code is the MDN_ERR_* value."""
+
+    def __init__(self, code, message):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+
+
+ERR = dict(OK=0, INVALID=1, CUDA=2, NOMEM=3, TIMEOUT=4, IO=5, MISMATCH=6, NCCL=7, STATE=8)
+
+# exported symbol -> (restype, argtypes)
+SIGNATURES = {
+    "mdn_last_error": (ctypes.c_char_p, []),
+    "mdn_abi_version": (_U, []),
+    "mdn_sim_config_default": (None, [_P]),
+    "mdn_rollout_shape_default": (None, [_P]),
+    "mdn_physics_crazyflie_default": (None, [_P]),
+    "mdn_raptor_load": (ctypes.c_int, [ctypes.c_char_p, _P]),
+    "mdn_device_open": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(_P)]),
+    "mdn_device_close": (ctypes.c_int, [_P]),
+    "mdn_sync": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_double)]),
+    "mdn_sim_create": (ctypes.c_int, [_P, _P, _P, _U, _P, _P, ctypes.POINTER(_P)]),
+    "mdn_sim_destroy": (ctypes.c_int, [_P]),
+    "mdn_sim_reset": (ctypes.c_int, [_P]),
+    "mdn_sim_set_config": (ctypes.c_int, [_P, _P]),
+    "mdn_sim_get_config": (ctypes.c_int, [_P, _P]),
+    "mdn_sim_collect": (ctypes.c_int, [_P, _U]),
+    "mdn_sim_step": (ctypes.c_int, [_P, _U]),
+    "mdn_sim_buffer": (ctypes.c_int, [_P, ctypes.c_int, ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_size_t)]),
+    "mdn_sim_download": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_size_t, ctypes.c_size_t]),
+    "mdn_sim_upload": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_size_t, ctypes.c_size_t]),
+    "mdn_sim_report": (ctypes.c_int, [_P, _P]),
+    "mdn_sim_dims": (ctypes.c_int, [_P, _P, _P, _P, _P]),
+    "mdn_sim_last_collect_ms": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float)]),
+    "mdn_ppo_create": (ctypes.c_int, [_P, _U, _U, ctypes.POINTER(_P)]),
+    "mdn_ppo_destroy": (ctypes.c_int, [_P]),
+    "mdn_ppo_rollout_update": (ctypes.c_int, [_P, _U]),
+    "mdn_ppo_metrics": (ctypes.c_int, [_P, _P]),
+    "mdn_ppo_state": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_U)]),
+    "mdn_ppo_set_state": (ctypes.c_int, [_P, ctypes.c_uint64, _U]),
+    "mdn_ppo_moments": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_size_t, ctypes.c_int]),
+    "mdn_ppo_grad_norms": (ctypes.c_int, [_P, _P, ctypes.c_size_t]),
+    "mdn_minibatch_order": (ctypes.c_int, [_U, _U, _U, _U, _P, ctypes.c_size_t]),
+    "mdn_ppo_minibatch_order": (ctypes.c_int, [_P, _U, _P, ctypes.c_size_t]),
+    "mdn_ppo_last_update_ms": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float)]),
+    "mdn_ppo_checkpoint_save": (ctypes.c_int, [_P, ctypes.c_char_p, _U, _U, _U]),
+    "mdn_ppo_checkpoint_load": (ctypes.c_int, [_P, ctypes.c_char_p, _U, _U, _U, _U]),
+    "mdn_comm_unique_id": (ctypes.c_int, [_P]),
+    "mdn_comm_init": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, _P]),
+    "mdn_comm_destroy": (ctypes.c_int, [_P]),
+}
+
+
+def lib(path=None):
+    """Load libmdn.so (in-tree). Raises when it is missing: there is no fallback."""
+    global _lib
+    if _lib is None:
+        p = pathlib.Path(path or os.environ.get("MDN_LIB", LIB_PATH))
+        if not p.exists():
+            raise MdnError(ERR["INVALID"], f"libmdn.so not built at {p}; run __graft_entry__.build()")
+        L = ctypes.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status):
+    if status != 0:
+        raise MdnError(status, lib().mdn_last_error().decode())
+
+
+def _ptr(a):
+    return a.ctypes.data_as(_P)
+
+
+def minibatch_order(rows, minibatch, epochs, rollout_index):
+    """Chunk order of one rollout update, computed on the host (mdn_minibatch_order)."""
+    chunks = -(-rows // minibatch)
+    out = np.zeros(chunks * epochs, np.uint32)
+    check(lib().mdn_minibatch_order(rows, minibatch, epochs, rollout_index, _ptr(out), out.size))
+    return out
+
+
+def default_raptor():
+    w = np.zeros((), layouts.RAPTOR)
+    check(lib().mdn_raptor_load(str(RAPTOR_PATH).encode(), _ptr(w)))
+    return w
+
+
+class Device:
+    """The reference's `Metal` object: one CUDA device (main.mm:44-72)."""
+
+    def __init__(self, gpu=0):
+        self.h = _P()
+        check(lib().mdn_device_open(gpu, ctypes.byref(self.h)))
+        self.gpu = gpu
+
+    def finish(self):
+        """Metal::finish: wait for queued work, raise device errors, return GPU seconds."""
+        s = ctypes.c_double()
+        check(lib().mdn_sync(self.h, ctypes.byref(s)))
+        return s.value
+
+    def comm_init(self, rank, world, unique_id):
+        buf = np.frombuffer(bytes(unique_id), np.uint8).copy()
+        check(lib().mdn_comm_init(self.h, rank, world, _ptr(buf)))
+
+    @staticmethod
+    def comm_unique_id():
+        buf = np.zeros(128, np.uint8)
+        check(lib().mdn_comm_unique_id(_ptr(buf)))
+        return buf.tobytes()
+
+    def close(self):
+        if self.h:
+            lib().mdn_comm_destroy(self.h)
+            check(lib().mdn_device_close(self.h))
+            self.h = _P()
+
+
+class Sim:
+    """Batched environment, the reference Sim (main.mm:516-603)."""
+
+    def __init__(self, device, cfg, horizon, raptor=None, physics=None, room=None):
+        self.device = device
+        self.cfg = np.array(cfg, layouts.CONFIG)
+        self.horizon = int(horizon)
+        self.raptor = default_raptor() if raptor is None else np.array(raptor, layouts.RAPTOR)
+        shape = None
+        if room is not None:
+            shape = np.zeros((), layouts.SHAPE)
+            lib().mdn_rollout_shape_default(_ptr(shape))
+            shape["flags"] = 1
+            shape["room_min"] = room[:3]
+            shape["room_max"] = room[3:]
+        phys = None if physics is None else np.array(physics, layouts.PARAMS)
+        self.h = _P()
+        check(lib().mdn_sim_create(device.h, _ptr(self.cfg), None if shape is None else _ptr(shape), self.horizon,
+                                   _ptr(self.raptor), None if phys is None else _ptr(phys), ctypes.byref(self.h)))
+        self.n = int(self.cfg["n"])
+
+    def close(self):
+        if self.h:
+            check(lib().mdn_sim_destroy(self.h))
+            self.h = _P()
+
+    def reset(self):
+        check(lib().mdn_sim_reset(self.h))
+
+    def set_config(self, cfg):
+        c = np.array(cfg, layouts.CONFIG)
+        check(lib().mdn_sim_set_config(self.h, _ptr(c)))
+        self.cfg = c
+
+    def collect(self, count=0):
+        check(lib().mdn_sim_collect(self.h, count))
+
+    def step(self, tick):
+        check(lib().mdn_sim_step(self.h, tick))
+
+    def last_collect_ms(self):
+        ms = ctypes.c_float()
+        check(lib().mdn_sim_last_collect_ms(self.h, ctypes.byref(ms)))
+        return ms.value
+
+    def buffer(self, name):
+        """Device pointer and size of a buffer (mdn_sim_buffer)."""
+        ptr, nbytes = _P(), ctypes.c_size_t()
+        check(lib().mdn_sim_buffer(self.h, layouts.BUF[name], ctypes.byref(ptr), ctypes.byref(nbytes)))
+        return ptr.value, nbytes.value
+
+    def download(self, name):
+        _, nbytes = self.buffer(name)
+        dt = layouts.BUF_DTYPE.get(name, np.dtype(np.float32))
+        out = np.zeros(nbytes // dt.itemsize, dt)
+        check(lib().mdn_sim_download(self.h, layouts.BUF[name], _ptr(out), 0, nbytes))
+        return out
+
+    def upload(self, name, array, offset=0):
+        a = np.ascontiguousarray(array)
+        check(lib().mdn_sim_upload(self.h, layouts.BUF[name], _ptr(a), offset, a.nbytes))
+
+    def report(self):
+        out = np.zeros(10, np.float64)
+        check(lib().mdn_sim_report(self.h, _ptr(out)))
+        keys = ("episodes", "successes", "collisions", "timeouts", "success_time", "total_path", "total_elapsed",
+                "final_progress", "min_clearance", "peak_speed")
+        return dict(zip(keys, out.tolist()))
+
+
+class PPOTrainer:
+    """The reference PPOTrainer (main.mm:1110-1476)."""
+
+    def __init__(self, sim, epochs=2, minibatch=0):
+        self.sim = sim
+        self.h = _P()
+        check(lib().mdn_ppo_create(sim.h, epochs, minibatch, ctypes.byref(self.h)))
+
+    def close(self):
+        if self.h:
+            check(lib().mdn_ppo_destroy(self.h))
+            self.h = _P()
+
+    def rollout_update(self, rollout_index):
+        check(lib().mdn_ppo_rollout_update(self.h, rollout_index))
+
+    @property
+    def metric_mean(self):
+        out = np.zeros(4, np.float32)
+        check(lib().mdn_ppo_metrics(self.h, _ptr(out)))
+        return out
+
+    def state(self):
+        step, done = ctypes.c_uint64(), _U()
+        check(lib().mdn_ppo_state(self.h, ctypes.byref(step), ctypes.byref(done)))
+        return step.value, done.value
+
+    @property
+    def optimizer_step(self):
+        return self.state()[0]
+
+    def set_state(self, optimizer_step, completed_rollouts):
+        check(lib().mdn_ppo_set_state(self.h, optimizer_step, completed_rollouts))
+
+    def moments(self, which):
+        n = layouts.ACTOR_PARAMS if which < 2 else layouts.CRITIC_PARAMS
+        out = np.zeros(n, np.float32)
+        check(lib().mdn_ppo_moments(self.h, which, _ptr(out), n, 0))
+        return out
+
+    def set_moments(self, which, values):
+        v = np.ascontiguousarray(values, np.float32)
+        check(lib().mdn_ppo_moments(self.h, which, _ptr(v), v.size, 1))
+
+    def grad_norms(self, updates):
+        out = np.zeros(2 * updates, np.float32)
+        check(lib().mdn_ppo_grad_norms(self.h, _ptr(out), out.size))
+        return out.reshape(updates, 2)
+
+    def minibatch_order(self, rollout_index, updates):
+        out = np.zeros(updates, np.uint32)
+        check(lib().mdn_ppo_minibatch_order(self.h, rollout_index, _ptr(out), out.size))
+        return out
+
+    def last_update_ms(self):
+        ms = ctypes.c_float()
+        check(lib().mdn_ppo_last_update_ms(self.h, ctypes.byref(ms)))
+        return ms.value
+
+    def save_checkpoint(self, path, family, seed, completed_rollouts):
+        check(lib().mdn_ppo_checkpoint_save(self.h, str(path).encode(), family, seed, completed_rollouts))
+
+    def load_checkpoint(self, path, family, horizon, n, seed):
+        check(lib().mdn_ppo_checkpoint_load(self.h, str(path).encode(), family, horizon, n, seed))

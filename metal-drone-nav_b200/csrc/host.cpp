@@ -1,0 +1,513 @@
+// C-ABI implementation: device, simulator and the shared helpers.
+// Stands in for the reference's Metal (main.mm:44-72) and Sim
+// (main.mm:516-603) host classes; see include/mdn.h for the mapping.
+//
+// Compiled with -ffp-contract=off: the policy initialisation and camera
+// tables below must round exactly like the reference's host code.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <fstream>
+#include <memory>
+
+#include "host_common.h"
+
+namespace mdn {
+static thread_local std::string g_last_error;
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace mdn
+
+using namespace mdn;
+
+extern "C" const char* mdn_last_error(void) { return g_last_error.c_str(); }
+extern "C" uint32_t mdn_abi_version(void) { return MDN_ABI_VERSION; }
+
+extern "C" void mdn_sim_config_default(mdn_sim_config* c) {
+    // SimConfig member initialisers, main.mm:462-463
+    *c = mdn_sim_config{};
+    c->n = 128; c->tick = 0; c->mode = 0; c->family = 0; c->substeps = 5; c->sensor_period = 1;
+    c->sensor_delay = 0; c->command_delay = 0; c->max_steps = 200; c->seed = 42; c->eval = 0;
+    c->speed = 2; c->distance = 4; c->wind = 0; c->depth_noise = 0; c->dropout = 0; c->risk_coef = 0;
+    c->entropy_coef = .005f; c->learning_rate = .0003f; c->velocity_contract = 1; c->geometry_memory = 0;
+}
+
+extern "C" void mdn_rollout_shape_default(mdn_rollout_shape* s) {
+    *s = mdn_rollout_shape{};
+    s->actor_obs_dim = kActorObs;
+    s->critic_obs_dim = kCriticObs;
+    s->actor_hidden = kHidden;
+    s->critic_hidden = kHidden;
+    s->flags = 0;
+    const float lo[3] = {-2.0f, -5.0f, 0.0f}, hi[3] = {14.0f, 5.0f, 5.0f};  // world.hpp:73-74,85
+    for (int j = 0; j < 3; j++) {
+        s->room_min[j] = lo[j];
+        s->room_max[j] = hi[j];
+    }
+}
+
+extern "C" void mdn_physics_crazyflie_default(mdn_physics_params* p) {
+    // Crazyflie profile of rl-tools L2F as transcribed at physics.hpp:184-219.
+    *p = mdn_physics_params{};
+    const float positions[12] = {.028f, -.028f, 0, -.028f, -.028f, 0, -.028f, .028f, 0, .028f, .028f, 0};
+    const float torque_z[4] = {-1, 1, -1, 1};
+    const float inertia_diag[3] = {9.416556729130406e-6f, 9.644051701582312e-6f, 1.745951732253285e-5f};
+    const float inertia_inv_diag[3] = {106195.93007988465f, 103690.85846314249f, 57275.35197719487f};
+    for (int r = 0; r < 4; ++r) {
+        const int i = 3 * r;
+        p->rotor_positions[i] = positions[i];
+        p->rotor_positions[i + 1] = positions[i + 1];
+        p->rotor_thrust_directions[i + 2] = 1.0f;
+        p->rotor_torque_directions[i + 2] = torque_z[r];
+        p->rotor_thrust_coefficients[i] = 0.00352526f;
+        p->rotor_thrust_coefficients[i + 1] = 0.01437313f;
+        p->rotor_thrust_coefficients[i + 2] = 0.09223048f;
+        p->rotor_torque_constants[r] = 4.665e-3f;
+        p->rotor_time_constants_rising[r] = 0.05545454545454546f;
+        p->rotor_time_constants_falling[r] = 0.24939393939393945f;
+    }
+    for (int i = 0; i < 3; ++i) {
+        p->inertia[4 * i] = inertia_diag[i];
+        p->inertia_inverse[4 * i] = inertia_inv_diag[i];
+    }
+    p->gravity_world[2] = -9.81f;
+    p->mass = 0.027f + 0.0017f + 0.0003f + 0.0016f;
+    p->action_min = 0.0f;
+    p->action_max = 1.0f;
+    p->dt = 0.01f;
+    p->position_limit = 100000.0f;
+    p->velocity_limit = 100000.0f;
+    p->angular_velocity_limit = 100000.0f;
+}
+
+extern "C" int mdn_raptor_load(const char* path, mdn_raptor_weights* out) {
+    return guarded([&] {
+        require(path && out, MDN_ERR_INVALID, "mdn_raptor_load: null argument");
+        std::ifstream f(path, std::ios::binary);
+        require(bool(f), MDN_ERR_IO, std::string("cannot open RAPTOR file ") + path);
+        unsigned char header[16];
+        f.read(reinterpret_cast<char*>(header), 16);
+        static const unsigned char magic[8] = {'R', 'A', 'P', 'T', 'O', 'R', '1', 0};
+        require(bool(f) && std::memcmp(header, magic, 8) == 0, MDN_ERR_IO, "not a RAPTOR1 file");
+        uint32_t version, count;
+        std::memcpy(&version, header + 8, 4);
+        std::memcpy(&count, header + 12, 4);
+        require(version == 1 && count == 2084, MDN_ERR_IO, "RAPTOR1 version/count mismatch");
+        f.read(reinterpret_cast<char*>(out), sizeof(*out));
+        require(bool(f), MDN_ERR_IO, "RAPTOR1 file truncated");
+    });
+}
+
+// ---------------------------------------------------------------- device
+namespace {
+uint32_t xorshift(uint32_t& s) {
+    s ^= s << 13;
+    s ^= s >> 17;
+    s ^= s << 5;
+    return s;
+}
+float unit(uint32_t& s) { return float(xorshift(s) >> 8) * (1.0f / 16777216.0f); }
+
+// Camera tables: nav_sensor_pixel_ray (sensor_profile.hpp:81-91 with the
+// legacy profile tan_h=1, tan_v=0.75) and the pooled guidance rays
+// (guidance.hpp:22-26).
+void camera_tables(std::vector<float>& pixel, std::vector<float>& pool) {
+    pixel.resize(kPixels * 3);
+    pool.resize(80 * 3);
+    for (uint32_t k = 0; k < uint32_t(kPixels); k++) {
+        const uint32_t row = k / 20u, col = k % 20u;
+        const float y = ((float(col) + 0.5f) / 20.0f * 2.0f - 1.0f) * 1.0f;
+        const float z = ((float(row) + 0.5f) / 16.0f * 2.0f - 1.0f) * kTanV;
+        const float d[3] = {1.0f, -y, -z};
+        const float inv = 1.0f / std::fmax(std::sqrt(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]), 1e-8f);
+        for (int j = 0; j < 3; j++) pixel[3 * k + j] = d[j] * inv;
+    }
+    for (uint32_t row = 0; row < 8; row++)
+        for (uint32_t col = 0; col < 10; col++) {
+            const float y = 0.9f - 0.2f * float(col), z = (0.875f - 0.25f * float(row)) * kTanV;
+            const float inv = 1.0f / std::sqrt(1.0f + y * y + z * z);
+            const uint32_t k = row * 10 + col;
+            pool[3 * k] = inv;
+            pool[3 * k + 1] = y * inv;
+            pool[3 * k + 2] = z * inv;
+        }
+}
+
+void use_device(mdn_device* dev) { cuda_check(cudaSetDevice(dev->gpu), "cudaSetDevice"); }
+}  // namespace
+
+extern "C" int mdn_device_open(int gpu, mdn_device** out) {
+    return guarded([&] {
+        require(out != nullptr, MDN_ERR_INVALID, "mdn_device_open: null out");
+        int count = 0;
+        cuda_check(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+        require(gpu >= 0 && gpu < count, MDN_ERR_INVALID, "mdn_device_open: no such GPU");
+        auto dev = std::make_unique<mdn_device>();
+        dev->gpu = gpu;
+        use_device(dev.get());
+        cudaDeviceProp prop{};
+        cuda_check(cudaGetDeviceProperties(&prop, gpu), "cudaGetDeviceProperties");
+        require(prop.major >= 10, MDN_ERR_INVALID,
+                std::string("libmdn is built for sm_100a (B200); device is ") + prop.name);
+        dev->sm_count = prop.multiProcessorCount;
+        std::vector<float> pixel, pool;
+        camera_tables(pixel, pool);
+        cuda_check(upload_camera_tables(pixel.data(), pool.data()), "camera tables");
+        cuda_check(configure_kernels(), "kernel attributes");
+        dev->tables_ready = true;
+        *out = dev.release();
+    });
+}
+
+extern "C" int mdn_device_close(mdn_device* dev) {
+    return guarded([&] {
+        if (!dev) return;
+        require(dev->sims.empty() && dev->trainers.empty(), MDN_ERR_STATE,
+                "mdn_device_close: destroy trainers and sims first");
+        delete dev;
+    });
+}
+
+extern "C" int mdn_sync(mdn_device* dev, double* gpu_seconds) {
+    return guarded([&] {
+        require(dev != nullptr, MDN_ERR_INVALID, "mdn_sync: null device");
+        use_device(dev);
+        double total = 0.0;
+        for (mdn_sim* s : dev->sims) {
+            cuda_check(cudaStreamSynchronize(s->stream), "stream synchronize");
+            total += s->last_collect_ms * 1e-3;
+        }
+        cuda_check(cudaGetLastError(), "device error");
+        if (gpu_seconds) *gpu_seconds = total;
+    });
+}
+
+// ------------------------------------------------------------- simulator
+mdn::SimArgs mdn_sim::args(uint32_t tick) const {
+    SimArgs a{};
+    a.cfg = cfg;
+    a.cfg.tick = tick;
+    a.n = n;
+    a.env_base = env_base;
+    a.tick = tick;
+    for (int j = 0; j < 3; j++) {
+        a.room_lo[j] = room_lo[j];
+        a.room_hi[j] = room_hi[j];
+        a.room_c[j] = room_c[j];
+        a.room_e[j] = room_e[j];
+    }
+    a.states = static_cast<mdn_physics_state*>(buf[MDN_BUF_STATES]);
+    a.runs = static_cast<mdn_sim_run*>(buf[MDN_BUF_RUNS]);
+    a.worlds = static_cast<mdn_world*>(buf[MDN_BUF_WORLDS]);
+    a.sensors = static_cast<float*>(buf[MDN_BUF_SENSORS]);
+    a.poses = static_cast<float*>(buf[MDN_BUF_POSES]);
+    a.commands = static_cast<float*>(buf[MDN_BUF_COMMANDS]);
+    a.actor = static_cast<const float*>(buf[MDN_BUF_ACTOR]);
+    a.critic = static_cast<const float*>(buf[MDN_BUF_CRITIC]);
+    a.raptor = static_cast<const mdn_raptor_weights*>(buf[MDN_BUF_RAPTOR]);
+    a.physics = static_cast<const mdn_physics_params*>(buf[MDN_BUF_PHYSICS]);
+    a.obs = static_cast<float*>(buf[MDN_BUF_OBS]);
+    a.co = static_cast<float*>(buf[MDN_BUF_CO]);
+    a.actions = static_cast<float*>(buf[MDN_BUF_ACTIONS]);
+    a.logp = static_cast<float*>(buf[MDN_BUF_LOGP]);
+    a.values = static_cast<float*>(buf[MDN_BUF_VALUES]);
+    a.rewards = static_cast<float*>(buf[MDN_BUF_REWARDS]);
+    a.next_values = static_cast<float*>(buf[MDN_BUF_NEXT_VALUES]);
+    a.terminated = static_cast<uint8_t*>(buf[MDN_BUF_TERMINATED]);
+    a.truncated = static_cast<uint8_t*>(buf[MDN_BUF_TRUNCATED]);
+    a.contact = static_cast<int32_t*>(buf[MDN_BUF_CONTACT_ID]);
+    return a;
+}
+
+void mdn_sim::release_graphs() {
+    for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+    graphs.clear();
+}
+
+namespace {
+void validate_config(const mdn_sim_config& c) {
+    require(c.n >= 1, MDN_ERR_INVALID, "SimConfig.n must be positive");
+    require(c.substeps >= 1 && c.substeps <= 64, MDN_ERR_INVALID, "SimConfig.substeps must be 1..64");
+    require(c.sensor_period >= 1, MDN_ERR_INVALID, "SimConfig.sensor_period must be positive");
+    // main.mm:727 (sim_evaluate): the 8-deep rings hold <=6 sensor frames and <=7 command steps.
+    require(c.sensor_delay <= 6 && c.command_delay <= 7, MDN_ERR_INVALID,
+            "delay rings support <=6 sensor frames and <=7 command steps");
+    require(c.mode == 0 || c.mode == 1 || c.mode == 20, MDN_ERR_INVALID,
+            "SimConfig.mode: this build implements the training modes 0 (stochastic policy) and 1 "
+            "(random actions) and mode 20's tight arrival radius");
+    require(c.geometry_memory == 0, MDN_ERR_INVALID, "SimConfig.geometry_memory=1 is not supported by this build");
+    require(std::isfinite(c.speed) && std::isfinite(c.distance), MDN_ERR_INVALID, "SimConfig speed/distance");
+}
+
+void init_policy(std::vector<float>& actor, std::vector<float>& critic) {
+    // main.mm:548-555 / cpu_reference.hpp:89-103: seed 1789 Box-Muller draws.
+    actor.assign(kActorParams, 0.0f);
+    critic.assign(kCriticParams, 0.0f);
+    uint32_t seed = 1789;
+    auto normal = [&]() {
+        const float u = std::max(unit(seed), 1e-7f);
+        const float a = std::sqrt(-2.0f * std::log(u));
+        return a * std::cos(6.2831853f * unit(seed));
+    };
+    for (int i = 0; i < kActorB1; i++) actor[i] = normal() * 0.04f;
+    for (int i = kActorW2; i < kActorB2; i++) actor[i] = normal() * 0.01f;
+    for (int i = 0; i < kActions; i++) actor[kActorLogStd + i] = -1.0f;
+    for (int i = 0; i < kCriticB1; i++) critic[i] = normal() * 0.15f;
+    for (int i = kCriticW2; i < kCriticB2; i++) critic[i] = normal() * 0.1f;
+}
+
+mdn_sim* checked(mdn_sim* s) {
+    require(s != nullptr, MDN_ERR_INVALID, "null mdn_sim");
+    use_device(s->dev);
+    return s;
+}
+}  // namespace
+
+extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const mdn_rollout_shape* shape,
+                              uint32_t horizon, const mdn_raptor_weights* raptor, const mdn_physics_params* physics,
+                              mdn_sim** out) {
+    return guarded([&] {
+        require(dev && cfg && out, MDN_ERR_INVALID, "mdn_sim_create: null argument");
+        require(raptor != nullptr, MDN_ERR_INVALID, "mdn_sim_create: RAPTOR weights are required (mdn_raptor_load)");
+        require(horizon >= 1, MDN_ERR_INVALID, "mdn_sim_create: horizon must be positive");
+        validate_config(*cfg);
+        use_device(dev);
+        auto sim = std::make_unique<mdn_sim>();
+        sim->dev = dev;
+        sim->cfg = *cfg;
+        sim->cfg.tick = 0;
+        sim->horizon = horizon;
+        sim->n = cfg->n;
+        sim->env_base = uint32_t(dev->rank) * cfg->n;
+        mdn_rollout_shape_default(&sim->shape);
+        if (shape) {
+            require(shape->actor_obs_dim == 0 || shape->actor_obs_dim == kActorObs, MDN_ERR_INVALID,
+                    "actor_obs_dim: this build implements the 184-input guided actor");
+            require(shape->critic_obs_dim == 0 || shape->critic_obs_dim == kCriticObs, MDN_ERR_INVALID,
+                    "critic_obs_dim: this build implements the 32-input critic");
+            require((shape->actor_hidden == 0 || shape->actor_hidden == kHidden) &&
+                        (shape->critic_hidden == 0 || shape->critic_hidden == kHidden),
+                    MDN_ERR_INVALID, "hidden widths: this build implements 64-unit actor and critic");
+            if (shape->flags & MDN_SHAPE_CUSTOM_ROOM) {
+                for (int j = 0; j < 3; j++) {
+                    require(shape->room_max[j] > shape->room_min[j], MDN_ERR_INVALID, "room bounds");
+                    sim->shape.room_min[j] = shape->room_min[j];
+                    sim->shape.room_max[j] = shape->room_max[j];
+                }
+                sim->shape.flags |= MDN_SHAPE_CUSTOM_ROOM;
+            }
+        }
+        for (int j = 0; j < 3; j++) {
+            sim->room_lo[j] = sim->shape.room_min[j];
+            sim->room_hi[j] = sim->shape.room_max[j];
+            sim->room_c[j] = (sim->room_lo[j] + sim->room_hi[j]) * 0.5f;
+            sim->room_e[j] = (sim->room_hi[j] - sim->room_lo[j]) * 0.5f;
+        }
+        const size_t n = sim->n, rows = n * horizon;
+        size_t* b = sim->bytes;
+        b[MDN_BUF_STATES] = n * sizeof(mdn_physics_state);
+        b[MDN_BUF_RUNS] = n * sizeof(mdn_sim_run);
+        b[MDN_BUF_WORLDS] = n * sizeof(mdn_world);
+        b[MDN_BUF_SENSORS] = n * kFrames * kPixels * sizeof(float);
+        b[MDN_BUF_POSES] = n * kFrames * 12 * sizeof(float);
+        b[MDN_BUF_COMMANDS] = n * kFrames * kActions * sizeof(float);
+        b[MDN_BUF_ACTOR] = kActorParams * sizeof(float);
+        b[MDN_BUF_CRITIC] = kCriticParams * sizeof(float);
+        b[MDN_BUF_OBS] = rows * kActorObs * sizeof(float);
+        b[MDN_BUF_CO] = rows * kCriticObs * sizeof(float);
+        b[MDN_BUF_ACTIONS] = rows * kActions * sizeof(float);
+        for (int id : {MDN_BUF_LOGP, MDN_BUF_VALUES, MDN_BUF_REWARDS, MDN_BUF_NEXT_VALUES, MDN_BUF_ADVANTAGES,
+                       MDN_BUF_RETURNS, MDN_BUF_CONTACT_ID})
+            b[id] = rows * sizeof(float);
+        b[MDN_BUF_TERMINATED] = rows;
+        b[MDN_BUF_TRUNCATED] = rows;
+        b[MDN_BUF_RAPTOR] = sizeof(mdn_raptor_weights);
+        b[MDN_BUF_PHYSICS] = sizeof(mdn_physics_params);
+        for (int id = 0; id < MDN_BUF_COUNT; id++) {
+            const cudaError_t e = cudaMalloc(&sim->buf[id], std::max<size_t>(b[id], 16));
+            if (e != cudaSuccess) {
+                for (int k = 0; k < id; k++) cudaFree(sim->buf[k]);
+                throw Error(MDN_ERR_NOMEM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
+            }
+        }
+        cuda_check(cudaStreamCreateWithFlags(&sim->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        cuda_check(cudaEventCreate(&sim->ev_start), "cudaEventCreate");
+        cuda_check(cudaEventCreate(&sim->ev_stop), "cudaEventCreate");
+        std::vector<float> actor, critic;
+        init_policy(actor, critic);
+        mdn_physics_params params;
+        if (physics) params = *physics;
+        else mdn_physics_crazyflie_default(&params);
+        cuda_check(cudaMemcpyAsync(sim->buf[MDN_BUF_ACTOR], actor.data(), b[MDN_BUF_ACTOR], cudaMemcpyHostToDevice,
+                                   sim->stream), "upload actor");
+        cuda_check(cudaMemcpyAsync(sim->buf[MDN_BUF_CRITIC], critic.data(), b[MDN_BUF_CRITIC], cudaMemcpyHostToDevice,
+                                   sim->stream), "upload critic");
+        cuda_check(cudaMemcpyAsync(sim->buf[MDN_BUF_RAPTOR], raptor, sizeof(*raptor), cudaMemcpyHostToDevice, sim->stream),
+                   "upload raptor");
+        cuda_check(cudaMemcpyAsync(sim->buf[MDN_BUF_PHYSICS], &params, sizeof(params), cudaMemcpyHostToDevice, sim->stream),
+                   "upload physics");
+        for (int id : {MDN_BUF_OBS, MDN_BUF_CO, MDN_BUF_ACTIONS, MDN_BUF_LOGP, MDN_BUF_VALUES, MDN_BUF_REWARDS,
+                       MDN_BUF_NEXT_VALUES, MDN_BUF_TERMINATED, MDN_BUF_TRUNCATED, MDN_BUF_ADVANTAGES, MDN_BUF_RETURNS,
+                       MDN_BUF_CONTACT_ID})
+            cuda_check(cudaMemsetAsync(sim->buf[id], 0, b[id], sim->stream), "clear rollout buffers");
+        // Persistent act kernel: enough CTAs to fill every SM twice.
+        sim->act_grid = int(std::min<size_t>((n + 7) / 8, size_t(dev->sm_count) * 2));
+        cuda_check(launch_reset(sim->args(0), true, sim->stream), "reset");
+        cuda_check(cudaStreamSynchronize(sim->stream), "mdn_sim_create");
+        dev->sims.push_back(sim.get());
+        *out = sim.release();
+    });
+}
+
+extern "C" int mdn_sim_destroy(mdn_sim* sim) {
+    return guarded([&] {
+        if (!sim) return;
+        use_device(sim->dev);
+        cudaStreamSynchronize(sim->stream);
+        sim->release_graphs();
+        for (int id = 0; id < MDN_BUF_COUNT; id++) cudaFree(sim->buf[id]);
+        cudaEventDestroy(sim->ev_start);
+        cudaEventDestroy(sim->ev_stop);
+        cudaStreamDestroy(sim->stream);
+        auto& v = sim->dev->sims;
+        v.erase(std::remove(v.begin(), v.end(), sim), v.end());
+        delete sim;
+    });
+}
+
+extern "C" int mdn_sim_reset(mdn_sim* sim) {
+    return guarded([&] {
+        checked(sim);
+        cuda_check(launch_reset(sim->args(0), true, sim->stream), "reset");
+    });
+}
+
+extern "C" int mdn_sim_set_config(mdn_sim* sim, const mdn_sim_config* cfg) {
+    return guarded([&] {
+        checked(sim);
+        require(cfg != nullptr, MDN_ERR_INVALID, "null config");
+        require(cfg->n == sim->cfg.n, MDN_ERR_INVALID, "cannot resize simulator");  // main.mm:567
+        validate_config(*cfg);
+        cuda_check(cudaStreamSynchronize(sim->stream), "set_config");
+        sim->cfg = *cfg;
+        sim->cfg.tick = 0;
+        sim->release_graphs();  // kernel arguments captured by value
+    });
+}
+
+extern "C" int mdn_sim_get_config(mdn_sim* sim, mdn_sim_config* out) {
+    return guarded([&] {
+        checked(sim);
+        require(out != nullptr, MDN_ERR_INVALID, "null out");
+        *out = sim->cfg;
+    });
+}
+
+extern "C" int mdn_sim_step(mdn_sim* sim, uint32_t tick) {
+    return guarded([&] {
+        checked(sim);
+        require(tick < sim->horizon, MDN_ERR_INVALID, "tick must be below the horizon");
+        cuda_check(launch_step(sim->args(tick), sim->act_grid, sim->stream), "step");
+    });
+}
+
+extern "C" int mdn_sim_collect(mdn_sim* sim, uint32_t steps) {
+    return guarded([&] {
+        checked(sim);
+        if (steps == 0) steps = sim->horizon;
+        cudaGraphExec_t exec = nullptr;
+        for (auto& g : sim->graphs)
+            if (g.first == steps) exec = g.second;
+        if (!exec) {
+            // Sim::collect (main.mm:576-598): one command stream of `steps`
+            // policy steps, rows at tick % horizon. Captured once per length.
+            cudaGraph_t graph;
+            cuda_check(cudaStreamBeginCapture(sim->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+            cudaError_t launch = cudaSuccess;
+            for (uint32_t t = 0; t < steps && launch == cudaSuccess; t++)
+                launch = launch_step(sim->args(t % sim->horizon), sim->act_grid, sim->stream);
+            const cudaError_t end = cudaStreamEndCapture(sim->stream, &graph);
+            cuda_check(launch, "capture step");
+            cuda_check(end, "end capture");
+            const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            cuda_check(inst, "graph instantiate");
+            sim->graphs.emplace_back(steps, exec);
+        }
+        cuda_check(cudaEventRecord(sim->ev_start, sim->stream), "event");
+        cuda_check(cudaGraphLaunch(exec, sim->stream), "graph launch");
+        cuda_check(cudaEventRecord(sim->ev_stop, sim->stream), "event");
+    });
+}
+
+extern "C" int mdn_sim_last_collect_ms(mdn_sim* sim, float* ms) {
+    return guarded([&] {
+        checked(sim);
+        cuda_check(cudaEventSynchronize(sim->ev_stop), "event sync");
+        cuda_check(cudaEventElapsedTime(&sim->last_collect_ms, sim->ev_start, sim->ev_stop), "elapsed");
+        if (ms) *ms = sim->last_collect_ms;
+    });
+}
+
+extern "C" int mdn_sim_buffer(mdn_sim* sim, int id, void** dev_ptr, size_t* bytes) {
+    return guarded([&] {
+        checked(sim);
+        require(id >= 0 && id < MDN_BUF_COUNT, MDN_ERR_INVALID, "unknown buffer id");
+        if (dev_ptr) *dev_ptr = sim->buf[id];
+        if (bytes) *bytes = sim->bytes[id];
+    });
+}
+
+extern "C" int mdn_sim_download(mdn_sim* sim, int id, void* host, size_t offset, size_t bytes) {
+    return guarded([&] {
+        checked(sim);
+        require(id >= 0 && id < MDN_BUF_COUNT, MDN_ERR_INVALID, "unknown buffer id");
+        require(host != nullptr || bytes == 0, MDN_ERR_INVALID, "null host pointer");
+        require(offset <= sim->bytes[id] && bytes <= sim->bytes[id] - offset, MDN_ERR_INVALID, "download out of range");
+        cuda_check(cudaMemcpyAsync(host, static_cast<char*>(sim->buf[id]) + offset, bytes, cudaMemcpyDeviceToHost,
+                                   sim->stream), "download");
+        cuda_check(cudaStreamSynchronize(sim->stream), "download");
+    });
+}
+
+extern "C" int mdn_sim_upload(mdn_sim* sim, int id, const void* host, size_t offset, size_t bytes) {
+    return guarded([&] {
+        checked(sim);
+        require(id >= 0 && id < MDN_BUF_COUNT, MDN_ERR_INVALID, "unknown buffer id");
+        require(host != nullptr || bytes == 0, MDN_ERR_INVALID, "null host pointer");
+        require(offset <= sim->bytes[id] && bytes <= sim->bytes[id] - offset, MDN_ERR_INVALID, "upload out of range");
+        cuda_check(cudaMemcpyAsync(static_cast<char*>(sim->buf[id]) + offset, host, bytes, cudaMemcpyHostToDevice,
+                                   sim->stream), "upload");
+        cuda_check(cudaStreamSynchronize(sim->stream), "upload");
+    });
+}
+
+extern "C" int mdn_sim_report(mdn_sim* sim, double out[10]) {
+    return guarded([&] {
+        checked(sim);
+        require(out != nullptr, MDN_ERR_INVALID, "null out");
+        std::vector<mdn_sim_run> runs(sim->n);
+        cuda_check(cudaMemcpyAsync(runs.data(), sim->buf[MDN_BUF_RUNS], sim->bytes[MDN_BUF_RUNS], cudaMemcpyDeviceToHost,
+                                   sim->stream), "report");
+        cuda_check(cudaStreamSynchronize(sim->stream), "report");
+        // Sim::report, main.mm:599-602
+        double v[10] = {0, 0, 0, 0, 0, 0, 0, 0, 12.0, 0.0};
+        for (const auto& r : runs) {
+            v[0] += r.episodes; v[1] += r.successes; v[2] += r.collisions; v[3] += r.timeouts;
+            v[4] += r.success_time; v[5] += r.total_path; v[6] += r.total_elapsed; v[7] += r.final_progress;
+            v[8] = std::fmin(v[8], r.min_clearance);
+            v[9] = std::fmax(v[9], r.peak_speed);
+        }
+        std::memcpy(out, v, sizeof(v));
+    });
+}
+
+extern "C" int mdn_sim_dims(mdn_sim* sim, uint32_t* n, uint32_t* horizon, uint32_t* actor_params,
+                            uint32_t* critic_params) {
+    return guarded([&] {
+        checked(sim);
+        if (n) *n = sim->n;
+        if (horizon) *horizon = sim->horizon;
+        if (actor_params) *actor_params = kActorParams;
+        if (critic_params) *critic_params = kCriticParams;
+    });
+}

@@ -1,0 +1,83 @@
+// Internal host-side declarations shared by the C-ABI implementation files.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "mdn.h"
+#include "mdn_shared.h"
+
+namespace mdn {
+
+// Errors are raised as exceptions inside the library and converted to status
+// codes at the C boundary (the reference's require(), main.mm:27).
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+inline void require(bool ok, int code, const std::string& msg) {
+    if (!ok) throw Error(code, msg);
+}
+inline void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw Error(MDN_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+void set_last_error(const std::string& msg);
+
+template <class F>
+int guarded(F&& fn) {
+    try {
+        fn();
+        return MDN_OK;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        set_last_error("host allocation failed");
+        return MDN_ERR_NOMEM;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return MDN_ERR_INVALID;
+    }
+}
+
+// Kernel launchers (rollout.cu, ppo.cu).
+cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays);
+cudaError_t configure_kernels();
+cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s);
+cudaError_t launch_step(const SimArgs& a, int act_grid, cudaStream_t s);
+size_t act_smem_bytes();
+
+}  // namespace mdn
+
+struct mdn_device {
+    int gpu = 0;
+    int sm_count = 0;
+    bool tables_ready = false;
+    // multi-GPU
+    int rank = 0, world = 1;
+    void* nccl_comm = nullptr;
+    std::vector<struct mdn_sim*> sims;
+    std::vector<struct mdn_ppo*> trainers;
+};
+
+struct mdn_sim {
+    mdn_device* dev = nullptr;
+    mdn_sim_config cfg{};
+    mdn_rollout_shape shape{};
+    uint32_t horizon = 0, n = 0, env_base = 0;
+    cudaStream_t stream = nullptr;
+    void* buf[MDN_BUF_COUNT] = {};
+    size_t bytes[MDN_BUF_COUNT] = {};
+    float room_lo[3], room_hi[3], room_c[3], room_e[3];
+    int act_grid = 1;
+    // collect() graphs cached by step count
+    std::vector<std::pair<uint32_t, cudaGraphExec_t>> graphs;
+    cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
+    float last_collect_ms = 0.0f;
+    mdn::SimArgs args(uint32_t tick) const;
+    void release_graphs();
+};

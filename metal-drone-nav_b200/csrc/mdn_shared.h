@@ -1,0 +1,58 @@
+// Constants and kernel-argument layouts shared by the host (g++) and device
+// (nvcc) sides of libmdn. No device code here.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "mdn.h"
+
+namespace mdn {
+
+constexpr int kPixels = 320;
+constexpr int kFrames = 8;
+constexpr int kActorObs = 184;
+constexpr int kCriticObs = 32;
+constexpr int kHidden = 64;
+constexpr int kActions = 4;
+constexpr int kActorB1 = kHidden * kActorObs;
+constexpr int kActorW2 = kActorB1 + kHidden;
+constexpr int kActorB2 = kActorW2 + kActions * kHidden;
+constexpr int kActorLogStd = kActorB2 + kActions;
+constexpr int kActorParams = kActorLogStd + kActions;
+constexpr int kCriticB1 = kHidden * kCriticObs;
+constexpr int kCriticW2 = kCriticB1 + kHidden;
+constexpr int kCriticB2 = kCriticW2 + kHidden;
+constexpr int kCriticParams = kCriticB2 + 1;
+constexpr float kLogTwoPi = 1.8378770664093453f;
+constexpr float kTanV = 0.75f;  // legacy camera, sensor_profile.hpp:44-45
+
+// Everything one launch of a rollout kernel needs (passed by value).
+struct SimArgs {
+    mdn_sim_config cfg;
+    uint32_t n;          // local environments on this GPU
+    uint32_t env_base;   // global id of local env 0 (seeds, clean-env parity)
+    uint32_t tick;       // row block tick*n .. tick*n+n-1
+    float room_lo[3], room_hi[3], room_c[3], room_e[3];
+    mdn_physics_state* states;
+    mdn_sim_run* runs;
+    mdn_world* worlds;
+    float* sensors;
+    float* poses;
+    float* commands;
+    const float* actor;
+    const float* critic;
+    const mdn_raptor_weights* raptor;
+    const mdn_physics_params* physics;
+    float* obs;
+    float* co;
+    float* actions;
+    float* logp;
+    float* values;
+    float* rewards;
+    float* next_values;
+    uint8_t* terminated;
+    uint8_t* truncated;
+    int32_t* contact;
+};
+
+}  // namespace mdn

@@ -1,0 +1,502 @@
+// C-ABI implementation of the trainer: PPOTrainer (main.mm:1110-1476).
+//
+// One rollout update = GAE + advantage normalisation + epochs x minibatch
+// chunks of (forward/loss, gradients, [allreduce], clip+Adam). The kernel
+// sequence is captured once into a CUDA graph; what changes between rollouts
+// (chunk order, batch sizes, Adam bias corrections) lives in small device
+// arrays uploaded before each launch, so the graph is replayed unchanged.
+//
+// Compiled with -ffp-contract=off: the bias corrections 1 - beta^step are
+// computed here with std::pow(float, float), as cpu_reference.hpp:558-559 does.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <filesystem>
+#include <fstream>
+#include <memory>
+#include <random>
+
+#include "host_common.h"
+#include "ppo_args.h"
+
+using namespace mdn;
+
+namespace mdn {
+// NCCL hooks (comm.cpp); no-ops on a single GPU.
+cudaError_t comm_allreduce_double(mdn_device* dev, double* buf, size_t count, cudaStream_t s, std::string& err);
+cudaError_t comm_allreduce_float(mdn_device* dev, float* buf, size_t count, cudaStream_t s, std::string& err);
+}  // namespace mdn
+
+struct mdn_ppo {
+    mdn_sim* sim = nullptr;
+    uint32_t epochs = 2, minibatch = 256, rows = 0, minibatches = 0, updates = 0;
+    uint32_t fwd_grid = 1, grad_chunk = 64, grad_chunks = 1;
+    uint64_t optimizer_step = 0;
+    uint32_t completed_rollouts = 0;
+    std::vector<uint32_t> starts;
+    // device memory
+    void* mem = nullptr;
+    PpoArgs args{};
+    uint32_t* d_starts = nullptr;  // [updates*3]: starts, batch, global batch
+    float* d_bias = nullptr;       // [updates*2]
+    // pinned staging for the per-rollout arrays
+    uint32_t* h_idx = nullptr;
+    float* h_bias = nullptr;
+    cudaEvent_t staged = nullptr, ev_start = nullptr, ev_stop = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    float last_update_ms = 0.0f;
+};
+
+namespace {
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+mdn_ppo* checked(mdn_ppo* p) {
+    require(p != nullptr && p->sim != nullptr, MDN_ERR_INVALID, "null mdn_ppo");
+    cuda_check(cudaSetDevice(p->sim->dev->gpu), "cudaSetDevice");
+    return p;
+}
+
+// Enqueue one whole rollout update on the sim stream (captured into a graph).
+void enqueue_update(mdn_ppo* t) {
+    mdn_sim* sim = t->sim;
+    mdn_device* dev = sim->dev;
+    cudaStream_t s = sim->stream;
+    const PpoArgs& p = t->args;
+    std::string err;
+    cuda_check(launch_gae_sum(p, s), "gae");
+    cuda_check(launch_adv_stats(p, 0, s), "advantage sum");
+    cuda_check(comm_allreduce_double(dev, p.stats, 1, s, err), err.c_str());
+    cuda_check(launch_adv_finalize(p, 0, s), "advantage mean");
+    cuda_check(launch_adv_sq(p, s), "advantage variance");
+    cuda_check(launch_adv_stats(p, 1, s), "advantage variance sum");
+    cuda_check(comm_allreduce_double(dev, p.stats + 1, 1, s, err), err.c_str());
+    cuda_check(launch_adv_finalize(p, 1, s), "advantage scale");
+    cuda_check(launch_adv_apply(p, dev->sm_count, s), "advantage normalise");
+    const bool multi = dev->world > 1;
+    const uint32_t chunks = multi ? std::max<uint32_t>(t->grad_chunks, 2) : t->grad_chunks;
+    for (uint32_t u = 0; u < t->updates; u++) {
+        cuda_check(launch_minibatch(p, u, chunks, s), "minibatch");
+        if (multi) cuda_check(comm_allreduce_float(dev, p.grad, kPpoParams, s, err), err.c_str());
+        cuda_check(launch_clip_adam(p, u, chunks, s), "clip+adam");
+    }
+    cuda_check(launch_metrics_mean(p, t->updates, s), "metrics");
+}
+}  // namespace
+
+extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_rows, mdn_ppo** out) {
+    return guarded([&] {
+        require(sim && out, MDN_ERR_INVALID, "mdn_ppo_create: null argument");
+        cuda_check(cudaSetDevice(sim->dev->gpu), "cudaSetDevice");
+        require(epochs >= 1 && epochs <= 4, MDN_ERR_INVALID, "PPO epochs must be 1..4");  // main.mm:1160
+        auto t = std::make_unique<mdn_ppo>();
+        t->sim = sim;
+        t->epochs = epochs;
+        t->minibatch = minibatch_rows ? minibatch_rows : 256u;
+        t->rows = sim->n * sim->horizon;
+        require(t->rows > 0, MDN_ERR_INVALID, "PPO requires at least one rollout row");
+        t->minibatch = std::min(t->minibatch, t->rows);
+        t->minibatches = (t->rows + t->minibatch - 1) / t->minibatch;
+        t->updates = t->epochs * t->minibatches;
+        t->starts.resize(t->minibatches);
+        const uint32_t sms = uint32_t(sim->dev->sm_count);
+        t->fwd_grid = std::max<uint32_t>(1, std::min<uint32_t>((t->minibatch + 63) / 64, 2 * sms));
+        const uint32_t per = (t->minibatch + 2 * sms - 1) / (2 * sms);
+        t->grad_chunk = std::max<uint32_t>(64, (per + 31) / 32 * 32);
+        t->grad_chunks = (t->minibatch + t->grad_chunk - 1) / t->grad_chunk;
+        const uint32_t chunk_bufs = std::max<uint32_t>(t->grad_chunks, 2);
+        const size_t mb = t->minibatch, U = t->updates, P = kPpoParams;
+        // One allocation for all trainer-owned device memory.
+        PpoArgs& a = t->args;
+        size_t off = 0;
+        auto carve = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+        const size_t o_am = carve(kActorParams * 4), o_av = carve(kActorParams * 4), o_cm = carve(kCriticParams * 4),
+                     o_cv = carve(kCriticParams * 4), o_sp = carve(gae_blocks(sim->n) * 8), o_st = carve(2 * 8),
+                     o_sv = carve(2 * 4), o_idx = carve(U * 3 * 4), o_bias = carve(U * 2 * 4), o_ah = carve(mb * 64 * 4),
+                     o_ch = carve(mb * 64 * 4), o_ad = carve(mb * 64 * 4), o_cd = carve(mb * 64 * 4),
+                     o_dm = carve(mb * 4 * 4), o_dls = carve(mb * 4 * 4), o_dv = carve(mb * 4),
+                     o_gp = carve(size_t(chunk_bufs) * P * 4), o_g = carve(P * 4), o_lp = carve(U * t->fwd_grid * 4 * 4),
+                     o_mr = carve(U * 4 * 4), o_mm = carve(4 * 4), o_gn = carve(U * 2 * 4);
+        const cudaError_t e = cudaMalloc(&t->mem, off);
+        require(e == cudaSuccess, MDN_ERR_NOMEM, std::string("cudaMalloc trainer: ") + cudaGetErrorString(e));
+        char* base = static_cast<char*>(t->mem);
+        cuda_check(cudaMemsetAsync(base, 0, off, sim->stream), "clear trainer memory");
+        a.n = sim->n;
+        a.horizon = sim->horizon;
+        a.global_rows = uint64_t(t->rows) * uint64_t(sim->dev->world);
+        a.gamma = .99f;        // main.mm:1193
+        a.lambda = .95f;
+        a.clip = .2f;
+        a.value_coef = .5f;
+        a.entropy_coef = sim->cfg.entropy_coef;
+        a.learning_rate = sim->cfg.learning_rate;
+        a.max_norm = .5f;      // main.mm:1202
+        a.rewards = static_cast<float*>(sim->buf[MDN_BUF_REWARDS]);
+        a.values = static_cast<float*>(sim->buf[MDN_BUF_VALUES]);
+        a.next_values = static_cast<float*>(sim->buf[MDN_BUF_NEXT_VALUES]);
+        a.terminated = static_cast<uint8_t*>(sim->buf[MDN_BUF_TERMINATED]);
+        a.truncated = static_cast<uint8_t*>(sim->buf[MDN_BUF_TRUNCATED]);
+        a.advantages = static_cast<float*>(sim->buf[MDN_BUF_ADVANTAGES]);
+        a.returns = static_cast<float*>(sim->buf[MDN_BUF_RETURNS]);
+        a.obs = static_cast<float*>(sim->buf[MDN_BUF_OBS]);
+        a.co = static_cast<float*>(sim->buf[MDN_BUF_CO]);
+        a.actions = static_cast<float*>(sim->buf[MDN_BUF_ACTIONS]);
+        a.logp = static_cast<float*>(sim->buf[MDN_BUF_LOGP]);
+        a.actor = static_cast<float*>(sim->buf[MDN_BUF_ACTOR]);
+        a.critic = static_cast<float*>(sim->buf[MDN_BUF_CRITIC]);
+        a.actor_m = reinterpret_cast<float*>(base + o_am);
+        a.actor_v = reinterpret_cast<float*>(base + o_av);
+        a.critic_m = reinterpret_cast<float*>(base + o_cm);
+        a.critic_v = reinterpret_cast<float*>(base + o_cv);
+        a.stat_partials = reinterpret_cast<double*>(base + o_sp);
+        a.stats = reinterpret_cast<double*>(base + o_st);
+        a.stat_values = reinterpret_cast<float*>(base + o_sv);
+        t->d_starts = reinterpret_cast<uint32_t*>(base + o_idx);
+        t->d_bias = reinterpret_cast<float*>(base + o_bias);
+        a.starts = t->d_starts;
+        a.batch = t->d_starts + U;
+        a.global_batch = t->d_starts + 2 * U;
+        a.bias_corr = t->d_bias;
+        a.mb_ah = reinterpret_cast<float*>(base + o_ah);
+        a.mb_ch = reinterpret_cast<float*>(base + o_ch);
+        a.mb_adelta = reinterpret_cast<float*>(base + o_ad);
+        a.mb_cdelta = reinterpret_cast<float*>(base + o_cd);
+        a.mb_dm = reinterpret_cast<float*>(base + o_dm);
+        a.mb_dls = reinterpret_cast<float*>(base + o_dls);
+        a.mb_dv = reinterpret_cast<float*>(base + o_dv);
+        a.grad_partials = reinterpret_cast<float*>(base + o_gp);
+        a.grad = reinterpret_cast<float*>(base + o_g);
+        a.loss_partials = reinterpret_cast<float*>(base + o_lp);
+        a.metric_rows = reinterpret_cast<float*>(base + o_mr);
+        a.metric_mean = reinterpret_cast<float*>(base + o_mm);
+        a.grad_norms = reinterpret_cast<float*>(base + o_gn);
+        a.fwd_grid = t->fwd_grid;
+        a.grad_chunk = t->grad_chunk;
+        cuda_check(cudaMallocHost(&t->h_idx, U * 3 * 4), "pinned staging");
+        cuda_check(cudaMallocHost(&t->h_bias, U * 2 * 4), "pinned staging");
+        cuda_check(cudaEventCreateWithFlags(&t->staged, cudaEventDisableTiming), "event");
+        cuda_check(cudaEventCreate(&t->ev_start), "event");
+        cuda_check(cudaEventCreate(&t->ev_stop), "event");
+        cuda_check(cudaEventRecord(t->staged, sim->stream), "event");
+        cuda_check(configure_ppo_kernels(), "ppo kernel attributes");
+        cuda_check(cudaStreamSynchronize(sim->stream), "mdn_ppo_create");
+        sim->dev->trainers.push_back(t.get());
+        *out = t.release();
+    });
+}
+
+extern "C" int mdn_ppo_destroy(mdn_ppo* t) {
+    return guarded([&] {
+        if (!t) return;
+        cuda_check(cudaSetDevice(t->sim->dev->gpu), "cudaSetDevice");
+        cudaStreamSynchronize(t->sim->stream);
+        if (t->graph) cudaGraphExecDestroy(t->graph);
+        cudaFree(t->mem);
+        cudaFreeHost(t->h_idx);
+        cudaFreeHost(t->h_bias);
+        cudaEventDestroy(t->staged);
+        cudaEventDestroy(t->ev_start);
+        cudaEventDestroy(t->ev_stop);
+        auto& v = t->sim->dev->trainers;
+        v.erase(std::remove(v.begin(), v.end(), t), v.end());
+        delete t;
+    });
+}
+
+namespace {
+// main.mm:1331-1337: canonical chunk starts, shuffled by the rollout-seeded
+// mt19937, reshuffled once at epoch 1 (later epochs reuse that order).
+void chunk_order(uint32_t rows, uint32_t minibatch, uint32_t epochs, uint32_t rollout_index,
+                 std::vector<uint32_t>& starts, std::vector<uint32_t>& out) {
+    starts.clear();
+    for (uint32_t s0 = 0; s0 < rows; s0 += minibatch) starts.push_back(s0);
+    std::mt19937 rng(0x9e3779b9u + rollout_index * 0x85ebca6bu);
+    std::shuffle(starts.begin(), starts.end(), rng);
+    out.clear();
+    for (uint32_t epoch = 0; epoch < epochs; epoch++) {
+        if (epoch == 1) std::shuffle(starts.begin(), starts.end(), rng);
+        out.insert(out.end(), starts.begin(), starts.end());
+    }
+}
+void chunk_order(mdn_ppo* t, uint32_t rollout_index, std::vector<uint32_t>& out) {
+    chunk_order(t->rows, t->minibatch, t->epochs, rollout_index, t->starts, out);
+}
+}  // namespace
+
+extern "C" int mdn_minibatch_order(uint32_t rows, uint32_t minibatch, uint32_t epochs, uint32_t rollout_index,
+                                   uint32_t* out, size_t count) {
+    return guarded([&] {
+        require(rows > 0 && minibatch > 0 && epochs > 0 && out, MDN_ERR_INVALID, "minibatch order: bad argument");
+        const size_t chunks = (size_t(rows) + minibatch - 1) / minibatch;
+        require(count == chunks * epochs, MDN_ERR_INVALID, "minibatch order: count must be epochs*chunks");
+        std::vector<uint32_t> starts, order;
+        chunk_order(rows, minibatch, epochs, rollout_index, starts, order);
+        std::copy(order.begin(), order.end(), out);
+    });
+}
+
+extern "C" int mdn_ppo_minibatch_order(mdn_ppo* t, uint32_t rollout_index, uint32_t* out, size_t count) {
+    return guarded([&] {
+        checked(t);
+        require(out && count == size_t(t->updates), MDN_ERR_INVALID, "minibatch order: count must be epochs*chunks");
+        std::vector<uint32_t> order;
+        chunk_order(t, rollout_index, order);
+        std::copy(order.begin(), order.end(), out);
+    });
+}
+
+extern "C" int mdn_ppo_rollout_update(mdn_ppo* t, uint32_t rollout_index) {
+    return guarded([&] {
+        checked(t);
+        mdn_sim* sim = t->sim;
+        // PPOTrainer reads the learning rate and entropy coefficient from the
+        // simulator config (main.mm:1193,1368); they are graph arguments here.
+        if (sim->cfg.learning_rate != t->args.learning_rate || sim->cfg.entropy_coef != t->args.entropy_coef) {
+            t->args.learning_rate = sim->cfg.learning_rate;
+            t->args.entropy_coef = sim->cfg.entropy_coef;
+            if (t->graph) {
+                cudaGraphExecDestroy(t->graph);
+                t->graph = nullptr;
+            }
+        }
+        std::vector<uint32_t> order;
+        chunk_order(t, rollout_index, order);
+        cuda_check(cudaEventSynchronize(t->staged), "staging reuse");
+        const uint32_t U = t->updates;
+        for (uint32_t u = 0; u < U; u++) {
+            const uint32_t begin = order[u];
+            const uint32_t b = std::min(t->minibatch, t->rows - begin);
+            require(t->optimizer_step < uint64_t(UINT32_MAX), MDN_ERR_STATE, "PPO Adam step overflow");
+            const uint32_t step = uint32_t(++t->optimizer_step);
+            t->h_idx[u] = begin;
+            t->h_idx[U + u] = b;
+            t->h_idx[2 * U + u] = b * uint32_t(sim->dev->world);
+            // cpu_reference.hpp:558-559
+            t->h_bias[2 * u] = 1.0f - std::pow(0.9f, float(step));
+            t->h_bias[2 * u + 1] = 1.0f - std::pow(0.999f, float(step));
+        }
+        cuda_check(cudaMemcpyAsync(t->d_starts, t->h_idx, U * 3 * 4, cudaMemcpyHostToDevice, sim->stream), "stage");
+        cuda_check(cudaMemcpyAsync(t->d_bias, t->h_bias, U * 2 * 4, cudaMemcpyHostToDevice, sim->stream), "stage");
+        cuda_check(cudaEventRecord(t->staged, sim->stream), "event");
+        if (!t->graph) {
+            cudaGraph_t g;
+            cuda_check(cudaStreamBeginCapture(sim->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+            try {
+                enqueue_update(t);
+            } catch (...) {
+                cudaStreamEndCapture(sim->stream, &g);
+                throw;
+            }
+            cuda_check(cudaStreamEndCapture(sim->stream, &g), "end capture");
+            const cudaError_t inst = cudaGraphInstantiate(&t->graph, g, 0);
+            cudaGraphDestroy(g);
+            cuda_check(inst, "graph instantiate");
+        }
+        cuda_check(cudaEventRecord(t->ev_start, sim->stream), "event");
+        cuda_check(cudaGraphLaunch(t->graph, sim->stream), "update graph");
+        cuda_check(cudaEventRecord(t->ev_stop, sim->stream), "event");
+        t->completed_rollouts = rollout_index + 1;
+    });
+}
+
+extern "C" int mdn_ppo_last_update_ms(mdn_ppo* t, float* ms) {
+    return guarded([&] {
+        checked(t);
+        cuda_check(cudaEventSynchronize(t->ev_stop), "event sync");
+        cuda_check(cudaEventElapsedTime(&t->last_update_ms, t->ev_start, t->ev_stop), "elapsed");
+        if (ms) *ms = t->last_update_ms;
+    });
+}
+
+extern "C" int mdn_ppo_metrics(mdn_ppo* t, float out[4]) {
+    return guarded([&] {
+        checked(t);
+        require(out != nullptr, MDN_ERR_INVALID, "null out");
+        cuda_check(cudaMemcpyAsync(out, t->args.metric_mean, 16, cudaMemcpyDeviceToHost, t->sim->stream), "metrics");
+        cuda_check(cudaStreamSynchronize(t->sim->stream), "metrics");
+    });
+}
+
+extern "C" int mdn_ppo_state(mdn_ppo* t, uint64_t* optimizer_step, uint32_t* completed_rollouts) {
+    return guarded([&] {
+        checked(t);
+        if (optimizer_step) *optimizer_step = t->optimizer_step;
+        if (completed_rollouts) *completed_rollouts = t->completed_rollouts;
+    });
+}
+
+extern "C" int mdn_ppo_set_state(mdn_ppo* t, uint64_t optimizer_step, uint32_t completed_rollouts) {
+    return guarded([&] {
+        checked(t);
+        t->optimizer_step = optimizer_step;
+        t->completed_rollouts = completed_rollouts;
+    });
+}
+
+extern "C" int mdn_ppo_moments(mdn_ppo* t, int which, float* host, size_t count, int upload) {
+    return guarded([&] {
+        checked(t);
+        require(which >= 0 && which < 4 && host, MDN_ERR_INVALID, "moments: bad argument");
+        float* d = which == 0 ? t->args.actor_m : which == 1 ? t->args.actor_v : which == 2 ? t->args.critic_m : t->args.critic_v;
+        const size_t n = which < 2 ? kActorParams : kCriticParams;
+        require(count == n, MDN_ERR_INVALID, "moments: count mismatch");
+        cuda_check(upload ? cudaMemcpyAsync(d, host, n * 4, cudaMemcpyHostToDevice, t->sim->stream)
+                          : cudaMemcpyAsync(host, d, n * 4, cudaMemcpyDeviceToHost, t->sim->stream),
+                   "moments");
+        cuda_check(cudaStreamSynchronize(t->sim->stream), "moments");
+    });
+}
+
+extern "C" int mdn_ppo_grad_norms(mdn_ppo* t, float* host_rows, size_t count) {
+    return guarded([&] {
+        checked(t);
+        require(host_rows && count == size_t(t->updates) * 2, MDN_ERR_INVALID, "grad norms: count must be 2*updates");
+        cuda_check(cudaMemcpyAsync(host_rows, t->args.grad_norms, count * 4, cudaMemcpyDeviceToHost, t->sim->stream),
+                   "grad norms");
+        cuda_check(cudaStreamSynchronize(t->sim->stream), "grad norms");
+    });
+}
+
+// ------------------------------------------------------------ checkpoints
+namespace {
+template <class T>
+void download(void* dst, const T* src, size_t bytes, cudaStream_t s) {
+    cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s), "checkpoint download");
+}
+}  // namespace
+
+// PPOTrainer::save_checkpoint (main.mm:1287-1320), version 6 layout: header,
+// actor, critic, Adam moments, then the full simulator state.
+extern "C" int mdn_ppo_checkpoint_save(mdn_ppo* t, const char* path, uint32_t family, uint32_t seed,
+                                       uint32_t completed_rollouts) {
+    return guarded([&] {
+        checked(t);
+        require(path != nullptr, MDN_ERR_INVALID, "null path");
+        require(t->sim->dev->world == 1, MDN_ERR_INVALID, "checkpoint save: gather sharded state with world == 1");
+        mdn_sim* sim = t->sim;
+        const std::filesystem::path p(path);
+        if (p.has_parent_path()) std::filesystem::create_directories(p.parent_path());
+        mdn_checkpoint_header h;
+        std::memset(&h, 0, sizeof(h));
+        std::memcpy(h.magic, "PPOFIX1", 7);
+        h.version = 6;
+        h.actor_count = kActorParams;
+        h.critic_count = kCriticParams;
+        h.horizon = sim->horizon;
+        h.n = sim->n;
+        h.family = family;
+        h.base_seed = seed;
+        h.completed_rollouts = completed_rollouts;
+        h.optimizer_step = t->optimizer_step;
+        h.config = sim->cfg;
+        h.config.tick = 0;
+        std::vector<char> blob;
+        auto append_device = [&](const void* dptr, size_t bytes) {
+            const size_t o = blob.size();
+            blob.resize(o + bytes);
+            download(blob.data() + o, dptr, bytes, sim->stream);
+        };
+        blob.resize(sizeof(h));
+        std::memcpy(blob.data(), &h, sizeof(h));
+        append_device(sim->buf[MDN_BUF_ACTOR], kActorParams * 4);
+        append_device(sim->buf[MDN_BUF_CRITIC], kCriticParams * 4);
+        append_device(t->args.actor_m, kActorParams * 4);
+        append_device(t->args.actor_v, kActorParams * 4);
+        append_device(t->args.critic_m, kCriticParams * 4);
+        append_device(t->args.critic_v, kCriticParams * 4);
+        for (int id : {MDN_BUF_STATES, MDN_BUF_RUNS, MDN_BUF_WORLDS, MDN_BUF_SENSORS, MDN_BUF_POSES, MDN_BUF_COMMANDS})
+            append_device(sim->buf[id], sim->bytes[id]);
+        cuda_check(cudaStreamSynchronize(sim->stream), "checkpoint download");
+        const std::string tmp = std::string(path) + ".tmp";
+        {
+            std::ofstream f(tmp, std::ios::binary | std::ios::trunc);
+            require(bool(f), MDN_ERR_IO, "cannot write PPO checkpoint: " + tmp);
+            f.write(blob.data(), std::streamsize(blob.size()));
+            f.flush();
+            require(bool(f), MDN_ERR_IO, "PPO checkpoint write failed: " + tmp);
+        }
+        require(std::rename(tmp.c_str(), path) == 0, MDN_ERR_IO, std::string("cannot replace PPO checkpoint: ") + path);
+    });
+}
+
+// PPOTrainer::load_checkpoint (main.mm:1209-1286) and read_checkpoint_header
+// (main.mm:993-1000) for versions 3..6 (no runtime/task/shaping blocks).
+extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t family, uint32_t horizon, uint32_t n,
+                                       uint32_t seed) {
+    return guarded([&] {
+        checked(t);
+        require(path != nullptr, MDN_ERR_INVALID, "null path");
+        mdn_sim* sim = t->sim;
+        std::ifstream f(path, std::ios::binary);
+        require(bool(f), MDN_ERR_IO, std::string("cannot open checkpoint ") + path);
+        mdn_checkpoint_header h;
+        std::memset(&h, 0, sizeof(h));
+        f.read(reinterpret_cast<char*>(&h), 48);
+        require(bool(f) && std::memcmp(h.magic, "PPOFIX1", 7) == 0 && h.version >= 3 && h.version <= 10, MDN_ERR_IO,
+                "checkpoint prefix/version");
+        f.read(reinterpret_cast<char*>(&h.config), 64);
+        if (h.version >= 4) {
+            f.read(reinterpret_cast<char*>(&h) + 112, 16);
+            if (h.version >= 6) f.read(reinterpret_cast<char*>(&h) + 128, 8);
+            else h.config.geometry_memory = 0;
+            if (h.version == 4) h.config.velocity_contract = 0;
+        } else {
+            h.config.risk_coef = 0;
+            h.config.entropy_coef = h.family == 7 ? .002f : .005f;
+            h.config.learning_rate = .0003f;
+            h.config.velocity_contract = 0;
+            h.config.geometry_memory = 0;
+        }
+        require(bool(f), MDN_ERR_IO, "checkpoint header truncated");
+        require(h.version <= 6, MDN_ERR_MISMATCH,
+                "checkpoint version 7+ carries runtime/task/shaping state this build does not implement");
+        require(h.actor_count == kActorParams && h.critic_count == kCriticParams, MDN_ERR_MISMATCH,
+                "PPO checkpoint dimensions mismatch");
+        require(h.family == family && h.horizon == horizon && h.n == n && h.base_seed == seed, MDN_ERR_MISMATCH,
+                "PPO checkpoint config mismatch");
+        require(horizon == sim->horizon && n == sim->n, MDN_ERR_MISMATCH, "PPO checkpoint does not fit this simulator");
+        const mdn_sim_config& c = sim->cfg;
+        require(h.config.family == c.family && h.config.n == c.n && h.config.substeps == c.substeps &&
+                    h.config.sensor_period == c.sensor_period && h.config.sensor_delay == c.sensor_delay &&
+                    h.config.command_delay == c.command_delay && h.config.max_steps == c.max_steps &&
+                    h.config.mode == c.mode && h.config.speed == c.speed && h.config.distance == c.distance &&
+                    h.config.wind == c.wind && h.config.depth_noise == c.depth_noise && h.config.dropout == c.dropout &&
+                    h.config.risk_coef == c.risk_coef && h.config.entropy_coef == c.entropy_coef &&
+                    h.config.learning_rate == c.learning_rate && h.config.velocity_contract == c.velocity_contract &&
+                    h.config.geometry_memory == c.geometry_memory,
+                MDN_ERR_MISMATCH, "PPO checkpoint simulator settings mismatch");
+        std::vector<char> tmp;
+        auto read_to_device = [&](void* dptr, size_t bytes) {
+            tmp.resize(bytes);
+            f.read(tmp.data(), std::streamsize(bytes));
+            require(bool(f), MDN_ERR_IO, "truncated PPO checkpoint");
+            cuda_check(cudaMemcpyAsync(dptr, tmp.data(), bytes, cudaMemcpyHostToDevice, sim->stream), "checkpoint upload");
+            cuda_check(cudaStreamSynchronize(sim->stream), "checkpoint upload");
+        };
+        read_to_device(sim->buf[MDN_BUF_ACTOR], kActorParams * 4);
+        read_to_device(sim->buf[MDN_BUF_CRITIC], kCriticParams * 4);
+        read_to_device(t->args.actor_m, kActorParams * 4);
+        read_to_device(t->args.actor_v, kActorParams * 4);
+        read_to_device(t->args.critic_m, kCriticParams * 4);
+        read_to_device(t->args.critic_v, kCriticParams * 4);
+        for (int id : {MDN_BUF_STATES, MDN_BUF_RUNS, MDN_BUF_WORLDS, MDN_BUF_SENSORS}) read_to_device(sim->buf[id], sim->bytes[id]);
+        if (h.version >= 6) read_to_device(sim->buf[MDN_BUF_POSES], sim->bytes[MDN_BUF_POSES]);
+        else cuda_check(cudaMemsetAsync(sim->buf[MDN_BUF_POSES], 0, sim->bytes[MDN_BUF_POSES], sim->stream), "poses");
+        read_to_device(sim->buf[MDN_BUF_COMMANDS], sim->bytes[MDN_BUF_COMMANDS]);
+        char extra;
+        require(!f.read(&extra, 1), MDN_ERR_IO, "PPO checkpoint has trailing data");
+        require(h.optimizer_step <= uint64_t(UINT32_MAX), MDN_ERR_MISMATCH, "PPO checkpoint Adam step is too large");
+        mdn_sim_config next = h.config;
+        next.tick = 0;
+        sim->cfg = next;
+        sim->release_graphs();
+        t->args.entropy_coef = next.entropy_coef;
+        t->args.learning_rate = next.learning_rate;
+        if (t->graph) {
+            cudaGraphExecDestroy(t->graph);
+            t->graph = nullptr;
+        }
+        t->optimizer_step = h.optimizer_step;
+        t->completed_rollouts = h.completed_rollouts;
+        cuda_check(cudaStreamSynchronize(sim->stream), "checkpoint load");
+    });
+}

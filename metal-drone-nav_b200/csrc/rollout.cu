@@ -1,0 +1,644 @@
+// Rollout kernels for sm_100a: reset, sense (depth + observation), act (actor
+// + critic + sampling), advance (5 RAPTOR/L2F substeps, reward, next value,
+// in-kernel reset). One policy step = sense -> act -> advance; a rollout of T
+// steps is captured once into a CUDA graph by the host (host.cpp).
+//
+// Reference kernels restated: sim_reset/sim_depth/sim_observe/sim_act/
+// sim_advance (sim.metal:142-332) with the CPU path's semantics
+// (cpu_reference.hpp:240-513).
+#include <cuda_runtime.h>
+
+#include "mdn_device.cuh"
+#include "world_gen.cuh"
+
+namespace mdn {
+
+__constant__ float c_pixel_ray[kPixels * 3];  // nav_sensor_pixel_ray(1, 0.75, k), sensor_profile.hpp:89-91
+__constant__ float c_pool_ray[80 * 3];        // nav_ray(row, col, 0.75), guidance.hpp:22-26
+
+// ------------------------------------------------------------------ reset
+__global__ void k_reset(SimArgs a, int first) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool active = i < a.n;
+    if (active) reset_env(a, i, first != 0);
+    const unsigned mask = __ballot_sync(0xffffffffu, active);
+    refill_rings(a, (blockIdx.x * blockDim.x) + (threadIdx.x & ~31u), mask);
+}
+
+// ------------------------------------------------------------------ sense
+// One warp per environment. Lanes cast 10 of the 320 rays each (world.hpp:71-83)
+// against the room and the env's obstacles staged in shared memory, write the
+// range ring frame and camera pose (sim.metal:145-158), then build the 184-float
+// actor observation with the 2x2 min pool, 21 context features and the
+// geometry-prior hint (sim.metal:182-228, guidance.hpp:39-90) and the 32-float
+// critic observation (sim.metal:159-165).
+constexpr int kSenseWarps = 8;
+
+struct WarpScene {
+    float cx[16], cy[16], cz[16];   // obstacle centres at the step's time
+    float sx[16], sy[16], sz[16];   // sizes
+    uint32_t kind[16];
+    float cur[80], prev[80];        // pooled ranges (metres, obs*12 as the reference re-derives them)
+    float ctx[24];
+};
+
+__device__ __forceinline__ void warp_argmax_first(float& score, int& index) {
+    // Max score; equal scores keep the smaller index, matching a sequential
+    // scan that replaces only on a strictly greater score.
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float os = __shfl_xor_sync(0xffffffffu, score, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, index, off);
+        if (os > score || (os == score && oi < index)) {
+            score = os;
+            index = oi;
+        }
+    }
+}
+
+__device__ __forceinline__ float pooled_min3x3(const float* range, int row, int col) {  // guidance.hpp:27-34
+    float nearest = 12.0f;
+#pragma unroll
+    for (int dr = -1; dr <= 1; dr++)
+#pragma unroll
+        for (int dc = -1; dc <= 1; dc++) {
+            const int r = row + dr, c = col + dc;
+            if (r >= 0 && r < 8 && c >= 0 && c < 10) nearest = fminf(nearest, range[r * 10 + c]);
+        }
+    return nearest;
+}
+
+__device__ __forceinline__ float cell_risk(const WarpScene& ws, int row, int col, const float vel[3], float sensor_dt) {
+    float risk = 0.0f;  // guidance.hpp:58-67
+    if (sensor_dt > 1e-4f) {
+        for (int dr = -1; dr <= 1; dr++)
+            for (int dc = -1; dc <= 1; dc++) {
+                const int r = row + dr, c = col + dc;
+                if (r < 0 || r >= 8 || c < 0 || c >= 10) continue;
+                const int k = r * 10 + c;
+                const float old = ws.prev[k], now = ws.cur[k];
+                if (old < 11.9f && now < 11.9f) {
+                    const float* ray = c_pool_ray + 3 * k;
+                    const float unexpected = (old - now) / fmaxf(sensor_dt, 1e-3f) -
+                                             (vel[0] * ray[0] + vel[1] * ray[1] + vel[2] * ray[2]);
+                    if (unexpected > 0.5f) risk = fmaxf(risk, fminf(0.20f * unexpected, 1.0f));
+                }
+            }
+    }
+    return risk;
+}
+
+__global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
+    __shared__ WarpScene scenes[kSenseWarps];
+    const int lane = threadIdx.x & 31;
+    const int wid = threadIdx.x >> 5;
+    const uint32_t i = blockIdx.x * kSenseWarps + wid;
+    if (i >= a.n) return;
+    const mdn_sim_config& c = a.cfg;
+    const mdn_sim_run& run = a.runs[i];
+    const uint32_t episodes = run.episodes, steps = run.steps;
+    if (c.eval && episodes) return;
+    const uint32_t gid = a.env_base + i;
+    WarpScene& ws = scenes[wid];
+    const mdn_physics_state& st = a.states[i];
+    const float pos[3] = {st.position[0], st.position[1], st.position[2]};
+    const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2], st.orientation_wxyz[3]};
+    float r[9];
+    rotation(q, r);
+    const float elapsed = run.elapsed;
+    const mdn_world& w = a.worlds[i];
+    const uint32_t count = w.count < 16u ? w.count : 16u;
+    if (lane < int(count)) {
+        const mdn_obstacle& o = w.obstacles[lane];
+        float cc[3];
+        obstacle_center(o.kind, o.center, o.size, o.velocity, elapsed, cc);
+        ws.cx[lane] = cc[0]; ws.cy[lane] = cc[1]; ws.cz[lane] = cc[2];
+        ws.sx[lane] = o.size[0]; ws.sy[lane] = o.size[1]; ws.sz[lane] = o.size[2];
+        ws.kind[lane] = o.kind;
+    }
+    __syncwarp();
+    float* ring = a.sensors + size_t(i) * kFrames * kPixels;
+
+    // ---- depth (sim_depth): only on sensor ticks
+    if (steps % c.sensor_period == 0) {
+        const uint32_t frame = (steps / c.sensor_period) % kFrames;
+        const float ox = pos[0] + 0.0f * r[0], oy = pos[1] + 0.0f * r[3], oz = pos[2] + 0.0f * r[6];  // mount 0
+        const float noise = clean_env(c, gid) ? 0.0f : c.depth_noise;
+        const float dropout = clean_env(c, gid) ? 0.0f : c.dropout;
+        for (int k = lane; k < kPixels; k += 32) {
+            const float rx = c_pixel_ray[3 * k], ry = c_pixel_ray[3 * k + 1], rz = c_pixel_ray[3 * k + 2];
+            const float dx = r[0] * rx + r[1] * ry + r[2] * rz;
+            const float dy = r[3] * rx + r[4] * ry + r[5] * rz;
+            const float dz = r[6] * rx + r[7] * ry + r[8] * rz;
+            float best = 12.0f;
+            best = fminf(best, ray_box(ox, oy, oz, dx, dy, dz, a.room_c[0], a.room_c[1], a.room_c[2], a.room_e[0],
+                                       a.room_e[1], a.room_e[2]));
+            for (uint32_t o = 0; o < count; o++) {
+                const uint32_t kind = ws.kind[o];
+                float t = 1000.0f;
+                if (kind == 0)
+                    t = ray_box(ox, oy, oz, dx, dy, dz, ws.cx[o], ws.cy[o], ws.cz[o], ws.sx[o], ws.sy[o], ws.sz[o]);
+                else if (kind == 1 || kind == 3)
+                    t = ray_sphere(ox, oy, oz, dx, dy, dz, ws.cx[o], ws.cy[o], ws.cz[o], ws.sx[o]);
+                else if (kind == 2)
+                    t = ray_cylinder(ox, oy, oz, dx, dy, dz, ws.cx[o], ws.cy[o], ws.cz[o], ws.sx[o], ws.sz[o]);
+                best = fminf(best, t);
+            }
+            float depth = fmaxf(0.0f, best);
+            if (noise != 0.0f || dropout != 0.0f) {
+                uint32_t rng = run.rng + uint32_t(k) * 1664525u + steps * 1013904223u;
+                depth = clampf(depth + noise * sim_normal(rng), 0.0f, 12.0f);
+                if (wurand(rng) < dropout) depth = 12.0f;
+            }
+            ring[frame * kPixels + k] = depth;
+        }
+        float* pose = a.poses + (size_t(i) * kFrames + frame) * 12;
+        if (lane < 3) pose[lane] = lane == 0 ? ox : (lane == 1 ? oy : oz);
+        else if (lane < 12) pose[lane] = r[lane - 3];
+        __syncwarp();
+    }
+
+    // ---- observation (sim_observe)
+    const uint32_t delay = clean_env(c, gid) ? 0u : c.sensor_delay;
+    const uint32_t available = steps / c.sensor_period;
+    const uint32_t frame = available > delay ? available - delay : 0;
+    const uint32_t prevf = frame > 0 ? frame - 1 : 0;
+    const bool have = available >= delay;
+    const size_t row = size_t(a.tick) * a.n + i;
+    float* obs = a.obs + row * kActorObs;
+    const float* cur_frame = ring + (frame % kFrames) * kPixels;
+    const float* prev_frame = ring + (prevf % kFrames) * kPixels;
+    for (int k = lane; k < 80; k += 32) {
+        const int y = (k / 10) * 2, x = (k % 10) * 2;
+        float cur = 12.0f, pre = 12.0f;
+#pragma unroll
+        for (int dy = 0; dy < 2; dy++)
+#pragma unroll
+            for (int dx = 0; dx < 2; dx++) {
+                const int px = (y + dy) * 20 + x + dx;
+                cur = smin(cur, cur_frame[px]);
+                pre = smin(pre, prev_frame[px]);
+            }
+        const float oc = have ? cur / 12.0f : 1.0f;
+        float op = have ? pre / 12.0f : 1.0f;
+        if (c.mode == 18) op = oc;
+        obs[k] = oc;
+        obs[80 + k] = op;
+        ws.cur[k] = oc * 12.0f;
+        ws.prev[k] = op * 12.0f;
+    }
+    // Context features (every lane computes the shared scalars; lane j writes feature j).
+    const float vel[3] = {st.linear_velocity[0], st.linear_velocity[1], st.linear_velocity[2]};
+    const float delta[3] = {w.goal[0] - pos[0], w.goal[1] - pos[1], w.goal[2] - pos[2]};
+    const float distance = smax(len3(delta[0], delta[1], delta[2]), 1.0e-6f);
+    if (lane < 21) {
+        float v;
+        const int j = lane;
+        if (j < 3) v = (r[j] * delta[0] + r[3 + j] * delta[1] + r[6 + j] * delta[2]) / distance;
+        else if (j == 3) v = smin(distance / 10.0f, 1.5f);
+        else if (j < 7) v = (r[j - 4] * vel[0] + r[3 + j - 4] * vel[1] + r[6 + j - 4] * vel[2]) / 4.0f;
+        else if (j < 10) v = st.angular_velocity_body[j - 7] / 4.0f;
+        else if (j < 13) v = r[6 + j - 10];
+        else if (j < 17) v = run.previous_nav[j - 13];
+        else if (j == 17) v = float(steps - frame * c.sensor_period) * a.physics->dt * float(c.substeps);
+        else {
+            const int k = j - 18;
+            const float ref0 = run.reference_position[0] - pos[0], ref1 = run.reference_position[1] - pos[1],
+                        ref2 = run.reference_position[2] - pos[2];
+            v = clampf((r[k] * ref0 + r[3 + k] * ref1 + r[6 + k] * ref2) * 2.0f, -1.0f, 1.0f);
+        }
+        obs[160 + j] = v;
+        ws.ctx[j] = v;
+    }
+    __syncwarp();
+    // Geometry-prior hint, nav_guidance (guidance.hpp:39-90), 80 cells over the lanes.
+    {
+        const float g0 = ws.ctx[0], g1 = ws.ctx[1], g2 = ws.ctx[2];
+        const float gvel[3] = {ws.ctx[4] * 4.0f, ws.ctx[5] * 4.0f, ws.ctx[6] * 4.0f};
+        const float sensor_dt = float(c.sensor_period) * a.physics->dt * float(c.substeps);
+        const float gnorm = sqrtf(g0 * g0 + g1 * g1 + g2 * g2);
+        float hint[3] = {0, 0, 0};
+        if (!(gnorm < 1e-6f || distance < 0.05f)) {
+            const float goal[3] = {g0 / gnorm, g1 / gnorm, g2 / gnorm};
+            const float speed = sqrtf(gvel[0] * gvel[0] + gvel[1] * gvel[1] + gvel[2] * gvel[2]);
+            const float stop_margin = 0.28f + speed * fmaxf(sensor_dt, 0.0f) + 0.25f * speed * speed;
+            float best_score = -1e20f, goal_dot = -1e20f;
+            int best_cell = 1 << 20, goal_cell = 1 << 20;
+            float best_range_lane = 0.0f;
+            for (int k = lane; k < 80; k += 32) {
+                const int row_ = k / 10, col = k % 10;
+                const float* d = c_pool_ray + 3 * k;
+                const float alignment = d[0] * goal[0] + d[1] * goal[1] + d[2] * goal[2];
+                const float nearby = pooled_min3x3(ws.cur, row_, col);
+                const float risk = cell_risk(ws, row_, col, gvel, sensor_dt);
+                const float safe_range = fmaxf(nearby - risk, 0.0f);
+                const float score = 1.4f * alignment + 0.12f * fminf(safe_range, 6.0f);
+                if (score > best_score) {
+                    best_score = score;
+                    best_cell = k;
+                    best_range_lane = safe_range;
+                }
+                if (alignment > goal_dot) {
+                    goal_dot = alignment;
+                    goal_cell = k;
+                }
+            }
+            const int my_best = best_cell;
+            warp_argmax_first(best_score, best_cell);
+            warp_argmax_first(goal_dot, goal_cell);
+            // the lane that owns the winning cell holds its safe range
+            const int owner = best_cell < 80 ? (best_cell & 31) : 0;
+            const float best_range = best_cell < 80 ? __shfl_sync(0xffffffffu, best_range_lane, owner) : 0.0f;
+            (void)my_best;
+            float best_dir[3] = {1, 0, 0};
+            if (best_cell < 80) {
+                best_dir[0] = c_pool_ray[3 * best_cell];
+                best_dir[1] = c_pool_ray[3 * best_cell + 1];
+                best_dir[2] = c_pool_ray[3 * best_cell + 2];
+            }
+            const int grow = goal_cell < 80 ? goal_cell / 10 : 0, gcol = goal_cell < 80 ? goal_cell % 10 : 0;
+            const float desired_speed = fminf(1.6f, sqrtf(4.0f * fmaxf(distance - 0.28f, 0.0f)));
+            const float direct_range = fmaxf(pooled_min3x3(ws.cur, grow, gcol), 0.0f);
+            float dir[3] = {best_dir[0], best_dir[1], best_dir[2]}, available_range = best_range;
+            if (goal[0] > 0.0f && direct_range > stop_margin + 0.25f * desired_speed * desired_speed) {
+                dir[0] = goal[0]; dir[1] = goal[1]; dir[2] = goal[2];
+                available_range = direct_range;
+            }
+            const float after_stop = fmaxf(available_range - stop_margin - 0.15f, 0.0f);
+            const float command_speed = fminf(desired_speed, sqrtf(4.0f * after_stop));
+            const float fraction = fminf(0.8f, command_speed * 0.5f);
+            if (direct_range < 1.2f && available_range > direct_range + 0.25f) {
+                const float advance = fmaxf(0.05f, fminf(1.0f, (direct_range - 0.25f) / 0.95f));
+                dir[0] *= advance;
+                const float norm = sqrtf(dir[0] * dir[0] + dir[1] * dir[1] + dir[2] * dir[2]);
+                for (int j = 0; j < 3; j++) dir[j] /= fmaxf(norm, 1e-6f);
+            }
+            for (int j = 0; j < 3; j++) {
+                const float x = fraction * dir[j];
+                hint[j] = 0.5f * logf((1.0f + x) / (1.0f - x));  // guidance.hpp:35
+            }
+        }
+        if (lane < 3) obs[181 + lane] = hint[lane];
+    }
+    // Critic observation (sim_critic_obs, sim.metal:159-165): clearance over lanes.
+    {
+        float cand = 3.0e38f;
+        if (lane < int(count)) {
+            const float size[3] = {ws.sx[lane], ws.sy[lane], ws.sz[lane]};
+            cand = obstacle_clearance(ws.kind[lane], size, pos[0] - ws.cx[lane], pos[1] - ws.cy[lane], pos[2] - ws.cz[lane]);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) cand = fminf(cand, __shfl_xor_sync(0xffffffffu, cand, off));
+        const float clearance = count ? fminf(room_clearance(a, pos), cand) : room_clearance(a, pos);
+        float* co = a.co + row * kCriticObs;
+        float v = 0.0f;
+        const int j = lane;
+        if (j < 3) v = (w.goal[j] - pos[j]) / 10.0f;
+        else if (j < 6) v = vel[j - 3] / 4.0f;
+        else if (j < 9) v = st.angular_velocity_body[j - 6] / 4.0f;
+        else if (j < 13) v = q[j - 9];
+        else if (j < 16) v = pos[j - 13] / 10.0f;
+        else if (j < 19) v = (run.reference_position[j - 16] - pos[j - 16]) * 2.0f;
+        else if (j == 19) v = clearance / 5.0f;
+        else if (j == 20) v = float(steps) / 200.0f;
+        else if (j < 30) {
+            const int o = (j - 21) / 3, axis = (j - 21) % 3;
+            if (o < int(count < 3u ? count : 3u)) {
+                const float cc = axis == 0 ? ws.cx[o] : (axis == 1 ? ws.cy[o] : ws.cz[o]);
+                v = (cc - pos[axis]) / 10.0f;
+            }
+        } else if (j == 30) v = w.wind[0];
+        else v = w.wind[1];
+        co[j] = v;
+    }
+}
+
+// -------------------------------------------------------------------- act
+// Actor mean (tanh MLP 184->64->4 plus geometry prior, ppo.hpp:65-80), critic
+// value (32->64->1, ppo.hpp:82-93), Gaussian sample, log-prob, command ring,
+// command delay and desired velocity (sim.metal:229-271). One warp per env;
+// the CTA keeps W1 transposed in shared memory and loops over envs.
+constexpr int kActWarps = 8;
+constexpr int kActSmemFloats = kActorObs * kHidden + kHidden + kActions * kHidden + 2 * kActions +
+                               kCriticObs * kHidden + kHidden + kHidden + 1 + kActWarps * (kActorObs + kCriticObs);
+
+__global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
+    extern __shared__ float sm[];
+    float* w1t = sm;                                  // [184][64]
+    float* b1 = w1t + kActorObs * kHidden;            // [64]
+    float* w2 = b1 + kHidden;                         // [4][64]
+    float* b2 = w2 + kActions * kHidden;              // [4]
+    float* log_std = b2 + kActions;                   // [4]
+    float* cw1t = log_std + kActions;                 // [32][64]
+    float* cb1 = cw1t + kCriticObs * kHidden;         // [64]
+    float* cw2 = cb1 + kHidden;                       // [64]
+    float* cb2 = cw2 + kHidden;                       // [1]
+    float* rows = cb2 + 1;                            // per warp obs[184] + co[32]
+    const int tid = threadIdx.x;
+    for (int k = tid; k < kActorObs * kHidden; k += blockDim.x) {
+        const int h = k / kActorObs, col = k % kActorObs;
+        w1t[col * kHidden + h] = a.actor[k];
+    }
+    for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
+        const int h = k / kCriticObs, col = k % kCriticObs;
+        cw1t[col * kHidden + h] = a.critic[k];
+    }
+    for (int k = tid; k < kHidden; k += blockDim.x) {
+        b1[k] = a.actor[kActorB1 + k];
+        cb1[k] = a.critic[kCriticB1 + k];
+        cw2[k] = a.critic[kCriticW2 + k];
+    }
+    for (int k = tid; k < kActions * kHidden; k += blockDim.x) w2[k] = a.actor[kActorW2 + k];
+    if (tid < kActions) {
+        b2[tid] = a.actor[kActorB2 + tid];
+        log_std[tid] = a.actor[kActorLogStd + tid];
+    }
+    if (tid == 0) cb2[0] = a.critic[kCriticB2];
+    __syncthreads();
+    const int lane = tid & 31, wid = tid >> 5;
+    float* my_obs = rows + wid * (kActorObs + kCriticObs);
+    float* my_co = my_obs + kActorObs;
+    const mdn_sim_config& c = a.cfg;
+    for (uint32_t i = blockIdx.x * kActWarps + wid; i < a.n; i += gridDim.x * kActWarps) {
+        mdn_sim_run& run = a.runs[i];
+        if (c.eval && run.episodes) continue;
+        const size_t row = size_t(a.tick) * a.n + i;
+        const float* obs_g = a.obs + row * kActorObs;
+        const float* co_g = a.co + row * kCriticObs;
+        for (int k = lane; k < kActorObs; k += 32) my_obs[k] = obs_g[k];
+        my_co[lane] = co_g[lane];
+        __syncwarp();
+        // actor hidden units lane and lane+32: in-order dot from zero, then the bias (cpu_reference.hpp:437-442)
+        float z0 = 0.0f, z1 = 0.0f;
+#pragma unroll 8
+        for (int k = 0; k < kActorObs; k++) {
+            const float o = my_obs[k];
+            z0 = fmaf(o, w1t[k * kHidden + lane], z0);
+            z1 = fmaf(o, w1t[k * kHidden + lane + 32], z1);
+        }
+        const float h0 = tanhf(z0 + b1[lane]), h1 = tanhf(z1 + b1[lane + 32]);
+        float mean[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            float part = fmaf(h0, w2[j * kHidden + lane], h1 * w2[j * kHidden + lane + 32]);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+            mean[j] = part + b2[j];
+            if (j < 3) mean[j] += my_obs[kActorObs - 3 + j];
+        }
+        // critic value (cpu_reference.hpp:449-458)
+        float y0 = 0.0f, y1 = 0.0f;
+#pragma unroll 8
+        for (int k = 0; k < kCriticObs; k++) {
+            const float o = my_co[k];
+            y0 = fmaf(o, cw1t[k * kHidden + lane], y0);
+            y1 = fmaf(o, cw1t[k * kHidden + lane + 32], y1);
+        }
+        float vpart = fmaf(tanhf(y0 + cb1[lane]), cw2[lane], tanhf(y1 + cb1[lane + 32]) * cw2[lane + 32]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) vpart += __shfl_xor_sync(0xffffffffu, vpart, off);
+        if (lane == 0) {
+            a.values[row] = vpart + cb2[0];
+            uint32_t rng = run.rng;
+            const uint32_t steps = run.steps;
+            float act[4];
+            float* cmd = a.commands + size_t(i) * kFrames * kActions;
+            for (int j = 0; j < 4; j++) {
+                act[j] = mean[j] + ((c.mode == 0 || c.mode == 22) ? expf(log_std[j]) * sim_normal(rng) : 0.0f);
+                if (c.mode == 1) act[j] = sim_normal(rng);
+                a.actions[row * kActions + j] = act[j];
+                cmd[(steps % kFrames) * kActions + j] = tanhf(act[j]);
+            }
+            float lp = 0.0f;  // gaussian_log_prob, ppo.hpp:95-103
+            for (int j = 0; j < 4; j++) {
+                const float inv_std = expf(-log_std[j]);
+                const float d = (act[j] - mean[j]) * inv_std;
+                lp += -0.5f * (d * d + 2.0f * log_std[j] + kLogTwoPi);
+            }
+            a.logp[row] = lp;
+            run.rng = rng;
+            const uint32_t gid = a.env_base + i;
+            const uint32_t delay = clean_env(c, gid) ? 0u : c.command_delay;
+            const uint32_t applied = steps > delay ? steps - delay : 0;
+            float pn[4];
+            for (int j = 0; j < 4; j++) {
+                pn[j] = steps < delay ? 0.0f : cmd[(applied % kFrames) * kActions + j];
+                run.previous_nav[j] = pn[j];
+            }
+            float r[9];
+            const mdn_physics_state& st = a.states[i];
+            const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2], st.orientation_wxyz[3]};
+            rotation(q, r);
+            float v[3] = {pn[0] * c.speed, pn[1] * c.speed, pn[2] * c.speed * (c.velocity_contract == 0 ? 0.5f : 1.0f)};
+            if (c.velocity_contract == 1) {
+                const float scale = smin(1.0f, c.speed / smax(len3(v[0], v[1], v[2]), 1e-8f));
+                for (int j = 0; j < 3; j++) v[j] *= scale;
+            }
+            for (int j = 0; j < 3; j++) run.desired_velocity[j] = r[j * 3] * v[0] + r[j * 3 + 1] * v[1] + r[j * 3 + 2] * v[2];
+            run.yaw += pn[3] * a.physics->dt * float(c.substeps) * 0.5f;
+        }
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------- advance
+// One thread per environment: 5 substeps of reference integration, RAPTOR
+// GRU and L2F RK4 with finiteness and sphere-contact checks, reward and
+// termination flags, bootstrap value, episode statistics and in-kernel reset
+// (sim.metal:272-332, cpu_reference.hpp:460-513). Also records the id of the
+// obstacle nearest at the step's closest approach.
+constexpr int kAdvanceThreads = 128;
+
+__global__ void __launch_bounds__(kAdvanceThreads) k_advance(SimArgs a) {
+    __shared__ float raptor_w[2084];
+    __shared__ float critic_w[kCriticParams];
+    __shared__ mdn_physics_params params;
+    const int tid = threadIdx.x;
+    const float* rw = reinterpret_cast<const float*>(a.raptor);
+    for (int k = tid; k < 2084; k += blockDim.x) raptor_w[k] = rw[k];
+    for (int k = tid; k < kCriticParams; k += blockDim.x) critic_w[k] = a.critic[k];
+    const float* pw = reinterpret_cast<const float*>(a.physics);
+    float* pd = reinterpret_cast<float*>(&params);
+    for (int k = tid; k < 88; k += blockDim.x) pd[k] = pw[k];
+    __syncthreads();
+
+    const uint32_t i = blockIdx.x * blockDim.x + tid;
+    const mdn_sim_config& c = a.cfg;
+    bool active = i < a.n;
+    if (active && c.eval && a.runs[i].episodes) active = false;
+    bool refill = false;
+    if (active) {
+        mdn_sim_run& run = a.runs[i];
+        const mdn_world& w = a.worlds[i];
+        const size_t row = size_t(a.tick) * a.n + i;
+        float s[17];
+        {
+            const float* sp = reinterpret_cast<const float*>(&a.states[i]);
+#pragma unroll
+            for (int k = 0; k < 17; k++) s[k] = sp[k];
+        }
+        float h[16], motors[4];
+#pragma unroll
+        for (int k = 0; k < 16; k++) h[k] = run.hidden[k];
+#pragma unroll
+        for (int k = 0; k < 4; k++) motors[k] = run.motors[k];
+        const float goal[3] = {w.goal[0], w.goal[1], w.goal[2]};
+        const float before = len3(goal[0] - s[0], goal[1] - s[1], goal[2] - s[2]);
+        const float yaw = run.yaw, cy = cosf(yaw), sy = sinf(yaw);
+        const float ch = cosf(yaw * .5f), sh = sinf(yaw * .5f);
+        bool collision = false;
+        float step_clearance = 12.0f;
+        int32_t contact = -1;
+        const float wind[3] = {w.wind[0] * params.mass, w.wind[1] * params.mass, w.wind[2] * params.mass};
+        float refp[3] = {run.reference_position[0], run.reference_position[1], run.reference_position[2]};
+        const float dv_[3] = {run.desired_velocity[0], run.desired_velocity[1], run.desired_velocity[2]};
+        float path = run.path, elapsed = run.elapsed, min_clear = run.min_clearance, peak = run.peak_speed;
+        for (uint32_t step = 0; step < c.substeps; step++) {
+            float mo[22];
+            for (int j = 0; j < 3; j++) refp[j] += dv_[j] * params.dt;
+            const float dp0 = s[0] - refp[0], dp1 = s[1] - refp[1], dp2 = s[2] - refp[2];
+            const float dvx = s[7] - dv_[0], dvy = s[8] - dv_[1], dvz = s[9] - dv_[2];
+            mo[0] = clampf(cy * dp0 + sy * dp1, -.5f, .5f);
+            mo[1] = clampf(-sy * dp0 + cy * dp1, -.5f, .5f);
+            mo[2] = clampf(dp2, -.5f, .5f);
+            const float qy[4] = {ch * s[3] + sh * s[6], ch * s[4] + sh * s[5], ch * s[5] - sh * s[4], ch * s[6] - sh * s[3]};
+            float rr[9];
+            rotation(qy, rr);
+#pragma unroll
+            for (int j = 0; j < 9; j++) mo[3 + j] = rr[j];
+            mo[12] = clampf(cy * dvx + sy * dvy, -1.0f, 1.0f);
+            mo[13] = clampf(-sy * dvx + cy * dvy, -1.0f, 1.0f);
+            mo[14] = clampf(dvz, -1.0f, 1.0f);
+            mo[15] = s[10]; mo[16] = s[11]; mo[17] = s[12];
+#pragma unroll
+            for (int j = 0; j < 4; j++) mo[18 + j] = motors[j];
+            raptor_forward(raptor_w, mo, h, motors);
+#pragma unroll
+            for (int j = 0; j < 4; j++) motors[j] = smax(-1.0f, smin(1.0f, motors[j]));
+            float nx[17];
+            l2f_step(params, s, motors, wind, nx);
+            bool valid = true;
+#pragma unroll
+            for (int j = 0; j < 17; j++) valid = valid && isfinite(nx[j]);
+            if (!valid) {
+                collision = true;
+                break;
+            }
+            path += len3(s[0] - nx[0], s[1] - nx[1], s[2] - nx[2]);
+#pragma unroll
+            for (int j = 0; j < 17; j++) s[j] = nx[j];
+            elapsed += params.dt;
+            int32_t id;
+            const float clearance = world_clearance(a, w, s, elapsed, &id);
+            if (clearance < step_clearance) contact = id;
+            step_clearance = smin(step_clearance, clearance);
+            min_clear = smin(min_clear, clearance);
+            peak = smax(peak, len3(s[7], s[8], s[9]));
+            if (clearance <= 0 || !isfinite(s[0]) || !isfinite(s[1]) || !isfinite(s[2])) {
+                collision = true;
+                break;
+            }
+        }
+        const uint32_t steps = run.steps + 1;
+        run.steps = steps;
+        {
+            float* sp = reinterpret_cast<float*>(&a.states[i]);
+#pragma unroll
+            for (int k = 0; k < 17; k++) sp[k] = s[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 16; k++) run.hidden[k] = h[k];
+#pragma unroll
+        for (int k = 0; k < 4; k++) run.motors[k] = motors[k];
+        for (int j = 0; j < 3; j++) run.reference_position[j] = refp[j];
+        run.path = path;
+        run.elapsed = elapsed;
+        run.min_clearance = min_clear;
+        run.peak_speed = peak;
+        const float after = len3(goal[0] - s[0], goal[1] - s[1], goal[2] - s[2]);
+        const bool success = after < (c.mode == 20 ? .10f : .35f) && !collision;
+        const bool timeout = steps >= c.max_steps;
+        a.rewards[row] = (before - after) * 2.0f - .01f - c.risk_coef * clampf((0.6f - step_clearance) / 0.6f, 0.0f, 1.0f) +
+                         (success ? 10.0f : 0.0f) - (collision ? 10.0f : 0.0f);
+        const bool term = collision || success;
+        a.terminated[row] = term;
+        a.truncated[row] = timeout && !term;
+        a.contact[row] = contact;
+        // Bootstrap value of the post-step critic observation (sim.metal:327).
+        {
+            float co[kCriticObs];
+            for (int j = 0; j < 3; j++) {
+                co[j] = (goal[j] - s[j]) / 10.0f;
+                co[j + 3] = s[7 + j] / 4.0f;
+                co[j + 6] = s[10 + j] / 4.0f;
+                co[j + 13] = s[j] / 10.0f;
+                co[j + 16] = (refp[j] - s[j]) * 2.0f;
+            }
+            for (int j = 0; j < 4; j++) co[9 + j] = s[3 + j];
+            co[19] = world_clearance(a, w, s, elapsed, nullptr) / 5.0f;
+            co[20] = float(steps) / 200.0f;
+            for (int j = 21; j < 30; j++) co[j] = 0.0f;
+            const uint32_t m = w.count < 3u ? w.count : 3u;
+            for (uint32_t o = 0; o < m; o++) {
+                float cc[3];
+                const mdn_obstacle& ob = w.obstacles[o];
+                obstacle_center(ob.kind, ob.center, ob.size, ob.velocity, elapsed, cc);
+                co[21 + o * 3] = (cc[0] - s[0]) / 10.0f;
+                co[22 + o * 3] = (cc[1] - s[1]) / 10.0f;
+                co[23 + o * 3] = (cc[2] - s[2]) / 10.0f;
+            }
+            co[30] = w.wind[0];
+            co[31] = w.wind[1];
+            float value = 0.0f;
+            for (int hh = 0; hh < kHidden; hh++) {
+                float z = 0.0f;
+#pragma unroll
+                for (int k = 0; k < kCriticObs; k++) z = fmaf(co[k], critic_w[hh * kCriticObs + k], z);
+                value = fmaf(tanhf(z + critic_w[kCriticB1 + hh]), critic_w[kCriticW2 + hh], value);
+            }
+            a.next_values[row] = value + critic_w[kCriticB2];
+        }
+        if (success || collision || timeout) {
+            run.successes += success;
+            run.collisions += collision;
+            run.timeouts += timeout && !term;
+            run.episodes++;
+            run.success_time += success ? elapsed : 0.0f;
+            run.total_path += path;
+            run.total_elapsed += elapsed;
+            run.final_progress += 1.0f - after / smax(run.initial_distance, 1.0e-4f);
+            if (!c.eval) refill = reset_env(a, i, false);
+        }
+    }
+    const unsigned mask = __ballot_sync(0xffffffffu, refill);
+    if (mask) refill_rings(a, blockIdx.x * blockDim.x + (tid & ~31), mask);
+}
+
+// ------------------------------------------------------------- launchers
+static inline unsigned blocks_for(uint32_t n, int per_block) { return (n + per_block - 1) / per_block; }
+
+cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays) {
+    cudaError_t e = cudaMemcpyToSymbol(c_pixel_ray, pixel_rays, sizeof(float) * kPixels * 3);
+    if (e != cudaSuccess) return e;
+    return cudaMemcpyToSymbol(c_pool_ray, pool_rays, sizeof(float) * 80 * 3);
+}
+
+cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s) {
+    k_reset<<<blocks_for(a.n, 128), 128, 0, s>>>(a, first ? 1 : 0);
+    return cudaGetLastError();
+}
+
+size_t act_smem_bytes() { return sizeof(float) * kActSmemFloats; }
+
+cudaError_t launch_step(const SimArgs& a, int act_grid, cudaStream_t s) {
+    k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
+    k_act<<<act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
+    k_advance<<<blocks_for(a.n, kAdvanceThreads), kAdvanceThreads, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t configure_kernels() {
+    return cudaFuncSetAttribute(k_act, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
+}
+
+}  // namespace mdn

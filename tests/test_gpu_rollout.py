@@ -1,0 +1,216 @@
+"""Rollout kernels on the GPU against the CPU oracle (through the C-ABI).
+
+Parity bar (north_star): integer outputs bit-exact (termination, truncation,
+contact id, counters); fp32 state, depth and observations within 1e-5 relative
+per step. Geometry, the range ring, poses and the depth/context part of the
+observation are compared bitwise (same IEEE operations). Per-step comparison is
+teacher-forced: after every step the oracle's full simulator state is uploaded
+into the GPU simulator, so each step starts from identical inputs.
+
+Tolerances, stated: RTOL = 1e-5 relative, ATOL = 1e-5 absolute (|x| <= 1e-5 +
+1e-5*|ref|) for everything that passes through a learned network or a
+transcendental function (CUDA and libm differ in the last ulp).
+"""
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, load_oracle_module, load_package
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+ATOL = 1e-5
+STATE_KEYS = ("states", "runs", "worlds", "sensors", "poses", "commands")
+RUN_FLOATS = ("hidden", "motors", "previous_nav", "desired_velocity", "yaw", "path", "elapsed", "peak_speed",
+              "min_clearance", "initial_distance", "success_time", "total_path", "total_elapsed", "final_progress",
+              "reference_position")
+
+
+@pytest.fixture(scope="module")
+def pkg():
+    return load_package()
+
+
+@pytest.fixture(scope="module")
+def device(pkg):
+    d = pkg.Device(0)
+    yield d
+
+
+@pytest.fixture(scope="module")
+def om():
+    return load_oracle_module()
+
+
+def close(a, b, what, rtol=RTOL, atol=ATOL):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    bad = ~(np.abs(a - b) <= atol + rtol * np.abs(b))
+    bad &= ~(np.isnan(a) & np.isnan(b))
+    assert not bad.any(), f"{what}: {bad.sum()} of {bad.size} differ; worst |d|={np.nanmax(np.abs(a - b)):.3e}"
+
+
+def floats(structured):
+    return np.frombuffer(np.ascontiguousarray(structured).tobytes(), np.float32)
+
+
+def make_pair(pkg, om, raptor, cfg, horizon):
+    L = pkg.layouts
+    gpu = pkg.Sim(pkg_device(), cfg, horizon, raptor=raptor)
+    ora = om.OracleSim(L, cfg, horizon, raptor)
+    return gpu, ora
+
+
+_DEV = {}
+
+
+def pkg_device():
+    return _DEV["dev"]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _register(device):
+    _DEV["dev"] = device
+
+
+@pytest.fixture(scope="module")
+def raptor(pkg):
+    return pkg.default_raptor()
+
+
+CONFIGS = [
+    dict(family=1),
+    dict(family=2),
+    dict(family=3),
+    dict(family=0),
+    dict(family=1, sensor_delay=2, command_delay=2, wind=0.3),
+    dict(family=12, sensor_delay=1, command_delay=1, wind=0.5, depth_noise=0.05, dropout=0.1),
+    dict(family=13),
+    dict(family=7, risk_coef=0.5, max_steps=7),
+    dict(family=1, sensor_period=2, velocity_contract=0, speed=2.0),
+    dict(family=1, mode=1),
+    dict(family=4, eval=1, max_steps=9),
+]
+
+
+@pytest.mark.parametrize("extra", CONFIGS, ids=[str(c) for c in CONFIGS])
+def test_reset_bitwise(pkg, om, raptor, extra):
+    cfg = pkg.layouts.default_config(n=300, speed=1.0, distance=3.0, seed=5, **extra)
+    gpu, ora = make_pair(pkg, om, raptor, cfg, 4)
+    try:
+        for name in STATE_KEYS + ("actor", "critic"):
+            assert gpu.download(name).tobytes() == ora.buf(name).tobytes(), name
+    finally:
+        gpu.close()
+
+
+@pytest.mark.parametrize("extra", CONFIGS, ids=[str(c) for c in CONFIGS])
+def test_teacher_forced_steps(pkg, om, raptor, extra):
+    n, T = 256, 12
+    cfg = pkg.layouts.default_config(n=n, speed=1.0, distance=3.0, seed=9, **extra)
+    gpu, ora = make_pair(pkg, om, raptor, cfg, T)
+    try:
+        for t in range(T):
+            # identical inputs: the oracle's state becomes the GPU's state
+            for name in STATE_KEYS:
+                gpu.upload(name, ora.buf(name))
+            gpu.step(t)
+            ora.step(t)
+            rows = slice(t * n, (t + 1) * n)
+            obs_g = gpu.download("obs").reshape(T * n, 184)[rows]
+            obs_o = ora.buf("obs").reshape(T * n, 184)[rows]
+            # depth pool + 21 context features: same IEEE operations -> bitwise
+            assert np.array_equal(obs_g[:, :181], obs_o[:, :181]), f"t={t} obs[:181]"
+            close(obs_g[:, 181:], obs_o[:, 181:], f"t={t} guidance hint")
+            assert np.array_equal(gpu.download("co").reshape(T * n, 32)[rows],
+                                  ora.buf("co").reshape(T * n, 32)[rows]), f"t={t} critic obs"
+            for name in ("actions", "logp", "values", "rewards", "next_values"):
+                g = gpu.download(name).reshape(T * n, -1)[rows]
+                o = ora.buf(name).reshape(T * n, -1)[rows]
+                close(g, o, f"t={t} {name}", atol=1e-4 if name == "logp" else ATOL)
+            for name in ("terminated", "truncated", "contact_id"):
+                g = gpu.download(name)[rows]
+                o = ora.buf(name)[rows]
+                assert np.array_equal(g, o), f"t={t} {name}"
+            # post-step simulator state
+            rs_g, rs_o = gpu.download("runs"), ora.buf("runs")
+            for f in ("steps", "successes", "collisions", "timeouts", "episodes"):
+                assert np.array_equal(rs_g[f], rs_o[f]), f"t={t} runs.{f}"
+            assert np.array_equal(rs_g["rng"], rs_o["rng"]), f"t={t} runs.rng"
+            close(floats(gpu.download("states")), floats(ora.buf("states")), f"t={t} states")
+            for f in RUN_FLOATS:
+                close(rs_g[f], rs_o[f], f"t={t} runs.{f}")
+            assert gpu.download("worlds").tobytes() == ora.buf("worlds").tobytes(), f"t={t} worlds"
+            assert np.array_equal(gpu.download("sensors"), ora.buf("sensors")), f"t={t} sensors"
+            assert np.array_equal(gpu.download("poses"), ora.buf("poses")), f"t={t} poses"
+            close(gpu.download("commands"), ora.buf("commands"), f"t={t} commands")
+    finally:
+        gpu.close()
+
+
+def test_collect_graph_equals_steps(pkg, raptor):
+    """collect() replays a captured CUDA graph; it must equal step-by-step launches."""
+    cfg = pkg.layouts.default_config(n=1000, family=1, speed=1.0, distance=4.0, seed=3)
+    a = pkg.Sim(pkg_device(), cfg, 16, raptor=raptor)
+    b = pkg.Sim(pkg_device(), cfg, 16, raptor=raptor)
+    try:
+        a.collect()
+        for t in range(16):
+            b.step(t)
+        for name in STATE_KEYS + ("obs", "co", "actions", "logp", "values", "rewards", "next_values",
+                                  "terminated", "truncated", "contact_id"):
+            assert a.download(name).tobytes() == b.download(name).tobytes(), name
+        a.collect()  # second replay continues the episodes
+        assert a.download("runs")["steps"].max() > 16 or a.download("runs")["episodes"].sum() > 0
+    finally:
+        a.close()
+        b.close()
+
+
+def test_free_run_vs_reference_trace(pkg, raptor):
+    """The reference's own CPU path (compiled unmodified, recorded in
+    tests/golden/ref_trace.npz) free-running from reset: the first observation
+    row is bit-exact; later steps stay within a loose drift bound."""
+    ref = np.load(GOLDEN / "ref_trace.npz")
+    for family in (1, 3):
+        cfg = pkg.layouts.default_config(n=24, family=family, speed=1.0, distance=3.0, seed=42)
+        sim = pkg.Sim(pkg_device(), cfg, 6, raptor=raptor)
+        try:
+            assert sim.download("worlds").tobytes() == ref[f"f{family}_worlds0"].tobytes()
+            assert sim.download("states").tobytes() == ref[f"f{family}_states0"].tobytes()
+            sim.collect()
+            obs = sim.download("obs").reshape(6, 24, 184)
+            robs = ref[f"f{family}_obs"].reshape(6, 24, 184)
+            assert np.array_equal(obs[0, :, :181], robs[0, :, :181])
+            close(obs, robs, f"family {family} obs over 6 steps", rtol=1e-3, atol=1e-3)
+            assert np.array_equal(sim.download("terminated"), ref[f"f{family}_terminated"])
+            close(floats(sim.download("states")), floats(ref[f"f{family}_states6"]), "final states", rtol=1e-3,
+                  atol=1e-3)
+        finally:
+            sim.close()
+
+
+def test_custom_room_matches_oracle(pkg, om, raptor):
+    """BASELINE room x[-2,8] y[-5,5] z[0,4] as a parameter (world.hpp:73-74,85 generalised)."""
+    room = np.array([-2, -5, 0, 8, 5, 4], np.float32)
+    cfg = pkg.layouts.default_config(n=128, family=1, speed=1.0, distance=3.0, seed=2)
+    gpu = pkg.Sim(pkg_device(), cfg, 4, raptor=raptor, room=room)
+    ora = om.OracleSim(pkg.layouts, cfg, 4, raptor, room=room)
+    try:
+        for t in range(4):
+            for name in STATE_KEYS:
+                gpu.upload(name, ora.buf(name))
+            gpu.step(t)
+            ora.step(t)
+        assert np.array_equal(gpu.download("sensors"), ora.buf("sensors"))
+        assert np.array_equal(gpu.download("co"), ora.buf("co"))
+        assert np.array_equal(gpu.download("terminated"), ora.buf("terminated"))
+    finally:
+        gpu.close()
+
+
+def test_rejects_unsupported_config(pkg, raptor):
+    with pytest.raises(pkg.MdnError):
+        pkg.Sim(pkg_device(), pkg.layouts.default_config(n=8, sensor_delay=7), 4, raptor=raptor)
+    with pytest.raises(pkg.MdnError):
+        pkg.Sim(pkg_device(), pkg.layouts.default_config(n=0), 4, raptor=raptor)
