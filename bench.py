@@ -1,0 +1,433 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 rollout/PPO hot path (BASELINE.json metric).
+
+Metric: policy env-steps/s at 65,536 environments, one env-step = depth ray
+casting + observation + actor + 5 RAPTOR/L2F substeps (the reference's
+Sim::collect, main.mm:576-598); PPO update ms reported beside it
+(PPOTrainer::rollout_update, main.mm:1321-1384).
+
+One bench step = one rollout of `--horizon` policy steps over all
+environments, then one PPO update (4 epochs x 16 minibatches by default).
+`value` = env-steps of the K timed rollouts / device time of those rollouts
+(CUDA events on the simulator stream, max over ranks). `e2e` = the same
+metric through the public C-ABI with the policy uploaded from pinned host
+memory and the episode report read back every step, host wall clock.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mdn|reference]
+
+Under torchrun each rank drives one GPU with envs/N environments (global env
+ids, identical worlds to the 1-GPU run); PPO gradients and advantage
+statistics are allreduced with NCCL.
+"""
+import argparse
+import ctypes
+import importlib.util
+import json
+import os
+import pathlib
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+METRIC = "policy env-steps/sec at 65,536 envs (physics+RAPTOR+depth+actor); PPO update ms"
+
+
+def _load(name, path, package_dir=None):
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(
+        name, path, submodule_search_locations=[str(package_dir)] if package_dir else None)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def package():
+    d = ROOT / "metal-drone-nav_b200"
+    return _load("mdn_b200", d / "__init__.py", d)
+
+
+def oracle_module():
+    return _load("mdn_oracle_py", ROOT / "oracle" / "oracle.py")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mdn", choices=["mdn", "reference"])
+    ap.add_argument("--envs", type=int, default=65536, help="environments over all ranks")
+    ap.add_argument("--horizon", type=int, default=128)
+    ap.add_argument("--epochs", type=int, default=4)
+    ap.add_argument("--minibatches", type=int, default=16)
+    ap.add_argument("--family", type=int, default=17)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus=None):
+        self.bus = bus  # PCI bus number of the benchmarked GPU (torch reports an int)
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        rows = [r for r in self.rows if len(r) >= 9]
+        if self.bus is not None:
+            def bus_of(field):
+                try:
+                    return int(field.split(":")[-2], 16)
+                except (ValueError, IndexError):
+                    return None
+            mine = [r for r in rows if bus_of(r[1]) == int(self.bus)]
+            rows = mine or rows
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# -------------------------------------------------------------- distributed
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self):
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, values):
+        if not self.pg:
+            return list(values)
+        import torch
+        t = torch.tensor(list(values), dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return t.tolist()
+
+    def broadcast_bytes(self, data):
+        if not self.pg:
+            return data
+        obj = [data]
+        self.pg.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ------------------------------------------------------------ work counts
+def sense_bytes_per_env():
+    # state 68 + run 184 + world 676 + previous range frame 1280 read; range frame
+    # 1280 + pose 48 + actor obs 736 + critic obs 128 written.
+    return 68 + 184 + 676 + 1280 + 1280 + 48 + 736 + 128
+
+
+def kernel_work(mean_obstacles):
+    """Algorithmic FLOP and bytes per environment of each rollout kernel
+    (the per-unit figures stated in DESIGN.md)."""
+    rays = 320
+    depth = rays * (mean_obstacles + 1) * 26 + rays * 30
+    return {
+        "sense": {"flop": depth + 10400, "bytes": sense_bytes_per_env()},
+        "act": {"flop": 2 * (184 * 64 + 64 * 4) + 2 * (32 * 64 + 64), "bytes": 736 + 128 + 184 + 16 + 4 + 4 + 16 + 184},
+        "advance": {"flop": 19520 + 2200 + 1260 + 2 * (32 * 64 + 64), "bytes": 2 * (68 + 184) + 676 + 4 * 4 + 2 + 4},
+    }
+
+
+def read_profile_traffic(kernel):
+    """DRAM bytes per environment measured by ncu (profiles/<kernel>_traffic.txt)."""
+    f = ROOT / "profiles" / f"{kernel}_traffic.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("dram_bytes_per_env:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_reference_sample(layouts, n, policy_steps, family, warmup=0, threads=None):
+    """The reference's own CPU path (oracle/_ref: cpu_reference.hpp compiled
+    unmodified) on a bounded sample: `n` environments with the benchmark's
+    family-17 worlds, `warmup` untimed then `policy_steps` timed policy steps,
+    then the PPO cost per row-epoch."""
+    om = oracle_module()
+    ref = om.load_ref()
+    kind = "reference"
+    if ref is None:
+        return None
+    olib = om.load_oracle()
+    threads = threads or os.cpu_count()
+    ref.ref_set_threads(threads)
+    cfg = layouts.default_config(n=n, family=1, seed=42)
+    raptor = layouts.load_raptor_file(ROOT / "metal-drone-nav_b200" / "assets" / "raptor.bin")
+    tr = om.RefTrainer(layouts, cfg, warmup + policy_steps, raptor, lib=ref)
+    worlds = tr.buf("worlds")
+    # Family-17 worlds drawn as the simulator's reset draws them (seed per env,
+    # sim.metal:56-58), generated by the C restatement: the reference has no
+    # generator for this family. Later resets inside the sample use family 1.
+    rng = np.zeros(1, np.uint32)
+    for i in range(n):
+        rng[0] = (42 + i * 747796405 + 2891336453) & 0xFFFFFFFF
+        fam = olib.o_wtraining_family(family, om.ptr(rng))
+        seed = olib.o_wrng(om.ptr(rng))
+        olib.o_wgenerate(om.ptr(worlds[i:i + 1]), seed, fam, 4.0)
+    for t in range(warmup):
+        ref.ref_step(tr.h, t)
+    t0 = time.perf_counter()
+    for t in range(warmup, warmup + policy_steps):
+        ref.ref_step(tr.h, t)
+    collect_s = time.perf_counter() - t0
+    # PPO: one train_rollout over a small trainer -> seconds per row-epoch
+    small = om.RefTrainer(layouts, layouts.default_config(n=1024, family=1, seed=42), 4, raptor, lib=ref)
+    for t in range(4):
+        ref.ref_step(small.h, t)
+    ref.ref_gae_normalize(small.h)
+    loss = np.zeros(4, np.float32)
+    t1 = time.perf_counter()
+    ref.ref_train_rollout(small.h, 0, om.ptr(loss))
+    update_s = time.perf_counter() - t1
+    per_row_epoch = update_s / (1024 * 4 * 2)
+    return {"env_steps_per_s": n * policy_steps / collect_s, "collect_s": collect_s, "threads": threads,
+            "per_row_epoch_s": per_row_epoch, "kind": kind,
+            "sample": f"{n} envs x {policy_steps} policy steps of cpu_reference::Trainer (compiled unmodified, "
+                      f"OpenMP stand-ins for GCD/Accelerate) on family-17 worlds; PPO cost from one "
+                      f"train_rollout over 1024x4 rows (2 epochs x 256-row chunks)"}
+
+
+def run_reference_arm(args, dist):
+    if dist.rank != 0:
+        return 0
+    layouts = package().layouts
+    envs = args.envs
+    om = oracle_module()
+    if om.load_ref() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
+        return 0
+    # warm-up and timed steps: each step = one policy step over all environments
+    samples = []
+    per_row = None
+    s = cpu_reference_sample(layouts, envs, args.steps, args.family, warmup=args.warmup)
+    value = s["env_steps_per_s"]
+    per_row = s["per_row_epoch_s"]
+    rows = envs * args.horizon
+    ppo_ms = per_row * rows * args.epochs * 1e3
+    line = {
+        "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": envs * args.horizon / value * 1e3 + ppo_ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": workload_config(args),
+        "ppo_update_ms": ppo_ms,
+        "cpu_baseline": {"value": value, "unit": "env-steps/s", "cores": s["threads"], "kind": s["kind"],
+                         "sample": s["sample"] + f" ({args.warmup} untimed warm-up steps)"},
+        "e2e": {"value": value, "unit": "env-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def workload_config(args):
+    return {"workload": "BASELINE config 4 on one shard set: 65,536 envs, family-17 clutter rooms (16 static boxes), "
+                        "20x16 depth rays, 184->64->4 tanh actor, 32->64->1 critic, T=128 rollouts, "
+                        f"PPO {args.epochs} epochs x {args.minibatches} minibatches",
+            "envs": args.envs, "horizon": args.horizon, "family": args.family, "epochs": args.epochs,
+            "minibatches": args.minibatches, "parallelism": f"dp{args.gpus} (envs sharded)",
+            "l2": "inputs larger than L2 (obs buffer > 6 GB per rollout)"}
+
+
+# ------------------------------------------------------------------ main
+def main():
+    args = parse()
+    dist = Dist()
+    if args.impl == "reference":
+        return run_reference_arm(args, dist)
+    dist.init()
+    pkg = package()
+    L = pkg.layouts
+    world = dist.world
+    assert args.envs % world == 0, "envs must divide evenly over ranks"
+    n = args.envs // world
+    dev = pkg.Device(dist.local)
+    if world > 1:
+        uid = dist.broadcast_bytes(pkg.Device.comm_unique_id() if dist.rank == 0 else None)
+        dev.comm_init(dist.rank, world, uid)
+    cfg = L.default_config(n=n, family=args.family, seed=42)
+    sim = pkg.Sim(dev, cfg, args.horizon)
+    rows = n * args.horizon
+    minibatch = rows // args.minibatches
+    trainer = pkg.PPOTrainer(sim, epochs=args.epochs, minibatch=minibatch)
+
+    for w in range(args.warmup):
+        sim.collect()
+        trainer.rollout_update(w)
+    dev.finish()
+    per_step, per_update = trainer.launch_counts()
+
+    # ---- device-timed region
+    import torch
+    torch.cuda.set_device(dist.local)
+    bus = None
+    try:
+        bus = torch.cuda.get_device_properties(dist.local).pci_bus_id
+    except Exception:
+        pass
+    clocks = ClockSampler(bus)
+    clocks.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    collect_ms, update_ms = [], []
+    for k in range(args.steps):
+        sim.collect()
+        collect_ms.append(sim.last_collect_ms())
+        trainer.rollout_update(args.warmup + k)
+        update_ms.append(trainer.last_update_ms())
+    dev.finish()
+    torch.cuda.synchronize()
+    dist.barrier()
+    wall = time.perf_counter() - wall0
+    clk = clocks.stop()
+    c_ms, u_ms, wall_max = dist.max([sum(collect_ms), sum(update_ms), wall])
+    env_steps = args.envs * args.horizon * args.steps
+    value = env_steps / (c_ms * 1e-3)
+
+    # ---- end to end through the C-ABI: policy from pinned host memory in,
+    # episode report out, every step; host wall clock.
+    actor = sim.download("actor")
+    critic = sim.download("critic")
+    pinned_a = torch.from_numpy(actor).pin_memory()
+    pinned_c = torch.from_numpy(critic).pin_memory()
+    h2d = actor.nbytes + critic.nbytes
+    d2h = n * L.RUN.itemsize
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0 = time.perf_counter()
+    for k in range(args.steps):
+        sim.upload_raw("actor", pinned_a.data_ptr(), actor.nbytes)
+        sim.upload_raw("critic", pinned_c.data_ptr(), critic.nbytes)
+        sim.collect()
+        sim.report()
+    dev.finish()
+    torch.cuda.synchronize()
+    dist.barrier()
+    (e2e_wall,) = dist.max([time.perf_counter() - e0])
+    e2e_value = env_steps / e2e_wall
+
+    # ---- per-kernel roofline of one policy step (CUDA events between launches)
+    prof = np.mean([sim.profile_step(t % args.horizon) for t in range(8)], axis=0)
+    prof = dist.max(prof.tolist())
+    names = ("sense", "act", "advance")
+    dominant = int(np.argmax(prof))
+    worlds = sim.download("worlds")
+    mean_obstacles = float(np.mean(worlds["count"]))
+    work = kernel_work(mean_obstacles)
+    peaks_file = ROOT / "MEASURED_PEAKS.json"
+    peaks = json.loads(peaks_file.read_text()) if peaks_file.exists() else {}
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    hbm_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    fp32_peak = dev.fp32_peak_tflops()
+    dom = names[dominant]
+    t_s = prof[dominant] * 1e-3
+    achieved_gbs = work[dom]["bytes"] * n / t_s / 1e9
+    traffic = read_profile_traffic(dom)
+    kernels = {}
+    for i, nm in enumerate(names):
+        ts = prof[i] * 1e-3
+        kernels[nm] = {"ms": prof[i], "gb_s": work[nm]["bytes"] * n / ts / 1e9,
+                       "tflop_s": work[nm]["flop"] * n / ts / 1e12,
+                       "fp32_frac": work[nm]["flop"] * n / ts / 1e12 / fp32_peak}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": (c_ms + u_ms) / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (procedural worlds, seeded)",
+        "config": workload_config(args),
+        "ppo_update_ms": u_ms / args.steps,
+        "rollout_ms": c_ms / args.steps,
+        "wall_s": wall_max,
+        "e2e": {"value": e2e_value, "unit": "env-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "note": "policy uploaded from pinned host memory, rollout, Sim::report read back; PPO update excluded "
+                        "as in the metric"},
+        "gpu_launches": args.steps * (args.horizon * per_step + per_update),
+        "roofline": {"bound": "hbm", "kernel": "k_" + dom, "achieved": achieved_gbs,
+                     "peak": hbm_peak, "unit": "GB/s", "frac": achieved_gbs / hbm_peak,
+                     "traffic": None if traffic is None else traffic * n, "peak_source": hbm_src},
+        "compute_roofline": {"bound": "fp32", "kernel": "k_" + dom, "achieved": kernels[dom]["tflop_s"],
+                             "peak": fp32_peak, "unit": "TFLOP/s", "frac": kernels[dom]["fp32_frac"],
+                             "peak_source": "measured (pure-FMA kernel, this run)"},
+        "kernels": kernels,
+        "clocks": clk,
+    }
+    if world == 1 and dist.rank == 0 and not args.no_cpu_baseline:
+        s = cpu_reference_sample(L, args.envs, 2, args.family, warmup=1)
+        if s is not None:
+            line["cpu_baseline"] = {"value": s["env_steps_per_s"], "unit": "env-steps/s", "cores": s["threads"],
+                                    "kind": s["kind"], "sample": s["sample"],
+                                    "ppo_update_ms_extrapolated": s["per_row_epoch_s"] * args.envs * args.horizon
+                                    * args.epochs * 1e3}
+    if dist.rank == 0:
+        print(json.dumps(line))
+    trainer.close()
+    sim.close()
+    dev.close()
+    dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

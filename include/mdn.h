@@ -217,6 +217,16 @@ int mdn_sim_dims(mdn_sim* sim, uint32_t* n, uint32_t* horizon, uint32_t* actor_p
 /* Device time of the last mdn_sim_collect (CUDA events on the sim stream). */
 int mdn_sim_last_collect_ms(mdn_sim* sim, float* ms);
 
+/* Per-kernel device time of one policy step at `tick` (sense, act, advance),
+ * CUDA events on the sim stream between the launches. Stands in for the
+ * reference's per-encoder timestamp profiler (profile.hpp:13-126). */
+int mdn_sim_profile_step(mdn_sim* sim, uint32_t tick, float ms[3]);
+/* Kernel launches one collect() step and one rollout update enqueue. */
+int mdn_launch_counts(mdn_sim* sim, mdn_ppo* ppo, uint32_t* per_policy_step, uint32_t* per_update);
+/* Measured dense FP32 FMA throughput of this device (TFLOP/s), a pure-FMA
+ * kernel over every SM: the denominator of the CUDA-core roofline. */
+int mdn_device_fp32_peak(mdn_device* dev, double* tflops);
+
 /* ---- trainer: PPOTrainer (main.mm:1110-1476) ----------------------------- */
 /* PPOTrainer(Sim&, epochs) main.mm:1159-1208; epochs 1..4; minibatch_rows 0 =
  * the reference's 256 rows (main.mm:1115). */

@@ -59,6 +59,9 @@ SIGNATURES = {
     "mdn_sim_report": (ctypes.c_int, [_P, _P]),
     "mdn_sim_dims": (ctypes.c_int, [_P, _P, _P, _P, _P]),
     "mdn_sim_last_collect_ms": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float)]),
+    "mdn_sim_profile_step": (ctypes.c_int, [_P, _U, _P]),
+    "mdn_launch_counts": (ctypes.c_int, [_P, _P, ctypes.POINTER(_U), ctypes.POINTER(_U)]),
+    "mdn_device_fp32_peak": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_double)]),
     "mdn_ppo_create": (ctypes.c_int, [_P, _U, _U, ctypes.POINTER(_P)]),
     "mdn_ppo_destroy": (ctypes.c_int, [_P]),
     "mdn_ppo_rollout_update": (ctypes.c_int, [_P, _U]),
@@ -131,6 +134,11 @@ class Device:
         check(lib().mdn_sync(self.h, ctypes.byref(s)))
         return s.value
 
+    def fp32_peak_tflops(self):
+        v = ctypes.c_double()
+        check(lib().mdn_device_fp32_peak(self.h, ctypes.byref(v)))
+        return v.value
+
     def comm_init(self, rank, world, unique_id):
         buf = np.frombuffer(bytes(unique_id), np.uint8).copy()
         check(lib().mdn_comm_init(self.h, rank, world, _ptr(buf)))
@@ -192,6 +200,16 @@ class Sim:
         ms = ctypes.c_float()
         check(lib().mdn_sim_last_collect_ms(self.h, ctypes.byref(ms)))
         return ms.value
+
+    def profile_step(self, tick):
+        """Device ms of (sense, act, advance) for one policy step (CUDA events)."""
+        ms = np.zeros(3, np.float32)
+        check(lib().mdn_sim_profile_step(self.h, tick, _ptr(ms)))
+        return ms
+
+    def upload_raw(self, name, host_ptr, nbytes, offset=0):
+        """Upload from a raw host pointer (e.g. pinned memory)."""
+        check(lib().mdn_sim_upload(self.h, layouts.BUF[name], _P(host_ptr), offset, nbytes))
 
     def buffer(self, name):
         """Device pointer and size of a buffer (mdn_sim_buffer)."""
@@ -271,6 +289,11 @@ class PPOTrainer:
         out = np.zeros(updates, np.uint32)
         check(lib().mdn_ppo_minibatch_order(self.h, rollout_index, _ptr(out), out.size))
         return out
+
+    def launch_counts(self):
+        a, b = _U(), _U()
+        check(lib().mdn_launch_counts(self.sim.h, self.h, ctypes.byref(a), ctypes.byref(b)))
+        return a.value, b.value
 
     def last_update_ms(self):
         ms = ctypes.c_float()

@@ -511,3 +511,26 @@ extern "C" int mdn_sim_dims(mdn_sim* sim, uint32_t* n, uint32_t* horizon, uint32
         if (critic_params) *critic_params = kCriticParams;
     });
 }
+
+extern "C" int mdn_sim_profile_step(mdn_sim* sim, uint32_t tick, float ms[3]) {
+    return guarded([&] {
+        checked(sim);
+        require(ms != nullptr && tick < sim->horizon, MDN_ERR_INVALID, "profile_step: bad argument");
+        cudaEvent_t ev[4];
+        for (auto& e : ev) cuda_check(cudaEventCreate(&e), "event");
+        const cudaError_t launch = launch_step_profiled(sim->args(tick), sim->act_grid, sim->stream, ev);
+        const cudaError_t wait = cudaEventSynchronize(ev[3]);
+        for (int k = 0; k < 3 && launch == cudaSuccess && wait == cudaSuccess; k++) cudaEventElapsedTime(&ms[k], ev[k], ev[k + 1]);
+        for (auto& e : ev) cudaEventDestroy(e);
+        cuda_check(launch, "profiled step");
+        cuda_check(wait, "profiled step");
+    });
+}
+
+extern "C" int mdn_device_fp32_peak(mdn_device* dev, double* tflops) {
+    return guarded([&] {
+        require(dev && tflops, MDN_ERR_INVALID, "null argument");
+        use_device(dev);
+        cuda_check(fp32_peak(dev->sm_count, tflops), "fp32 peak");
+    });
+}

@@ -50,6 +50,9 @@ cudaError_t configure_kernels();
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s);
 cudaError_t launch_step(const SimArgs& a, int act_grid, cudaStream_t s);
 size_t act_smem_bytes();
+cudaError_t launch_step_profiled(const SimArgs& a, int act_grid, cudaStream_t s, cudaEvent_t ev[4]);
+cudaError_t fp32_peak(int sm_count, double* tflops);
+int kernels_per_step();
 
 }  // namespace mdn
 

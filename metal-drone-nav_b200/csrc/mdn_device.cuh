@@ -110,6 +110,13 @@ __device__ __forceinline__ float ray_cylinder(float px, float py, float pz, floa
     return best;
 }
 
+// Signed distance from a point (offset q from the centre) to a box of half
+// extents e, world.hpp:93-94.
+__device__ __forceinline__ float box_distance(const float* e, float qx, float qy, float qz) {
+    const float kx = fabsf(qx) - e[0], ky = fabsf(qy) - e[1], kz = fabsf(qz) - e[2];
+    return len3(fmaxf(kx, 0.0f), fmaxf(ky, 0.0f), fmaxf(kz, 0.0f)) + fminf(fmaxf(kx, fmaxf(ky, kz)), 0.0f);
+}
+
 // Signed distance minus the 0.18 m drone radius to one obstacle, world.hpp:86-96.
 __device__ __forceinline__ float obstacle_clearance(uint32_t kind, const float* size, float qx, float qy, float qz) {
     float distance;
@@ -119,8 +126,7 @@ __device__ __forceinline__ float obstacle_clearance(uint32_t kind, const float* 
         const float a = sqrtf(qx * qx + qy * qy) - size[0], b = fabsf(qz) - size[2];
         distance = sqrtf(fmaxf(a, 0.0f) * fmaxf(a, 0.0f) + fmaxf(b, 0.0f) * fmaxf(b, 0.0f)) + fminf(fmaxf(a, b), 0.0f);
     } else {
-        const float kx = fabsf(qx) - size[0], ky = fabsf(qy) - size[1], kz = fabsf(qz) - size[2];
-        distance = len3(fmaxf(kx, 0.0f), fmaxf(ky, 0.0f), fmaxf(kz, 0.0f)) + fminf(fmaxf(kx, fmaxf(ky, kz)), 0.0f);
+        distance = box_distance(size, qx, qy, qz);
     }
     return distance - 0.18f;
 }

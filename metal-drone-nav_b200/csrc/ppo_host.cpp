@@ -45,6 +45,7 @@ struct mdn_ppo {
     cudaEvent_t staged = nullptr, ev_start = nullptr, ev_stop = nullptr;
     cudaGraphExec_t graph = nullptr;
     float last_update_ms = 0.0f;
+    uint32_t launches = 0;  // kernel nodes in the update graph
 };
 
 namespace {
@@ -287,6 +288,15 @@ extern "C" int mdn_ppo_rollout_update(mdn_ppo* t, uint32_t rollout_index) {
                 throw;
             }
             cuda_check(cudaStreamEndCapture(sim->stream, &g), "end capture");
+            size_t nodes = 0;
+            cudaGraphGetNodes(g, nullptr, &nodes);
+            std::vector<cudaGraphNode_t> list(nodes);
+            if (nodes) cudaGraphGetNodes(g, list.data(), &nodes);
+            t->launches = 0;
+            for (auto node : list) {
+                cudaGraphNodeType type;
+                if (cudaGraphNodeGetType(node, &type) == cudaSuccess && type == cudaGraphNodeTypeKernel) t->launches++;
+            }
             const cudaError_t inst = cudaGraphInstantiate(&t->graph, g, 0);
             cudaGraphDestroy(g);
             cuda_check(inst, "graph instantiate");
@@ -498,5 +508,17 @@ extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t fa
         t->optimizer_step = h.optimizer_step;
         t->completed_rollouts = h.completed_rollouts;
         cuda_check(cudaStreamSynchronize(sim->stream), "checkpoint load");
+    });
+}
+
+extern "C" int mdn_launch_counts(mdn_sim* sim, mdn_ppo* t, uint32_t* per_policy_step, uint32_t* per_update) {
+    return guarded([&] {
+        if (per_policy_step) *per_policy_step = uint32_t(kernels_per_step());
+        if (per_update) {
+            require(t != nullptr, MDN_ERR_INVALID, "launch counts: null trainer");
+            require(t->graph != nullptr, MDN_ERR_STATE, "launch counts: run one rollout update first");
+            *per_update = t->launches;
+        }
+        (void)sim;
     });
 }

@@ -637,6 +637,62 @@ cudaError_t launch_step(const SimArgs& a, int act_grid, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+cudaError_t launch_step_profiled(const SimArgs& a, int act_grid, cudaStream_t s, cudaEvent_t ev[4]) {
+    cudaEventRecord(ev[0], s);
+    k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
+    cudaEventRecord(ev[1], s);
+    k_act<<<act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
+    cudaEventRecord(ev[2], s);
+    k_advance<<<blocks_for(a.n, kAdvanceThreads), kAdvanceThreads, 0, s>>>(a);
+    cudaEventRecord(ev[3], s);
+    return cudaGetLastError();
+}
+
+// Pure FP32 FMA stream: 8 independent chains per thread, `iters` rounds.
+__global__ void k_fma_peak(float* out, int iters, float seed) {
+    float a[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) a[j] = seed + float(threadIdx.x + j);
+    const float m = 0.999999f, c = 1e-7f;
+    for (int i = 0; i < iters; i++) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) a[j] = fmaf(a[j], m, c);
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) s += a[j];
+    if (s == 12345.678f) out[0] = s;  // keeps the chains live
+}
+
+cudaError_t fp32_peak(int sm_count, double* tflops) {
+    float* out = nullptr;
+    cudaError_t e = cudaMalloc(&out, 16);
+    if (e != cudaSuccess) return e;
+    const int blocks = sm_count * 8, threads = 256, iters = 4096;
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    k_fma_peak<<<blocks, threads>>>(out, iters, 1.0f);  // warm-up
+    float best = 1e30f;
+    for (int r = 0; r < 5; r++) {
+        cudaEventRecord(a);
+        k_fma_peak<<<blocks, threads>>>(out, iters, 1.0f);
+        cudaEventRecord(b);
+        cudaEventSynchronize(b);
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, a, b);
+        best = fminf(best, ms);
+    }
+    e = cudaGetLastError();
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    cudaFree(out);
+    *tflops = 2.0 * 8.0 * double(iters) * double(blocks) * threads / (double(best) * 1e-3) / 1e12;
+    return e;
+}
+
+int kernels_per_step() { return 3; }
+
 cudaError_t configure_kernels() {
     return cudaFuncSetAttribute(k_act, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
 }

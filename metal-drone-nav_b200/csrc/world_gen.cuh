@@ -189,6 +189,36 @@ __device__ void generate_world(mdn_world& w, uint32_t seed, uint32_t family, flo
         }
         return;
     }
+    if (family == 17) {  // baseline clutter (no reference generator; see oracle/mdn_oracle.c)
+        w.count = 0;
+        float dx = 1.0f, dy = 0.0f;
+        for (int attempt = 0; attempt < 8; attempt++) {
+            const float ux = 2.0f * wurand(rng) - 1.0f, uy = 2.0f * wurand(rng) - 1.0f;
+            const float norm = sqrtf(ux * ux + uy * uy);
+            if (norm > 0.1f && norm <= 1.0f) {
+                dx = ux / norm;
+                dy = uy / norm;
+                break;
+            }
+        }
+        const float dist = 2.0f + 6.0f * wurand(rng);
+        w.goal[0] = fminf(fmaxf(dist * dx, -1.5f), 7.5f);
+        w.goal[1] = fminf(fmaxf(dist * dy, -4.5f), 4.5f);
+        w.goal[2] = 1.0f + wurand(rng);
+        for (int i = 0; i < 16; i++)
+            for (int attempt = 0; attempt < 8; attempt++) {
+                const float cx = -2.0f + 10.0f * wurand(rng), cy = -5.0f + 10.0f * wurand(rng), cz = 4.0f * wurand(rng);
+                const float ex = 0.2f + 0.8f * wurand(rng), ey = 0.2f + 0.8f * wurand(rng), ez = 0.2f + 0.8f * wurand(rng);
+                const float size[3] = {ex, ey, ez};
+                const float ds = box_distance(size, 0.0f - cx, 0.0f - cy, 1.5f - cz);
+                const float dg = box_distance(size, w.goal[0] - cx, w.goal[1] - cy, w.goal[2] - cz);
+                if (ds > 0.5f && dg > 0.5f) {
+                    b.box(cx, cy, cz, ex, ey, ez);
+                    break;
+                }
+            }
+        return;
+    }
     // Families 0-3 (and any other id): 16 random primitives, :311-317.
     for (int i = 0; i < 16; i++) {
         mdn_obstacle& o = w.obstacles[i];

@@ -373,6 +373,44 @@ static void wgenerate_vertical_choices(mdn_world* w, uint32_t* rng, float distan
     wadd_box(w, overhead_x, 0, overhead_bottom + overhead_half_z, 0.12f, 5.0f, overhead_half_z);
     wadd_box(w, choice_x, 0, 2.0f + choice_half_z, 0.10f, 5.0f, choice_half_z);
 }
+/* Family 17, "baseline clutter": the scene of the benchmark configuration
+ * (16 static boxes, centres uniform in x[-2,8] y[-5,5] z[0,4], half-extents
+ * U(0.2,1.0) per axis, goal 2-8 m from the (0,0,1.5) start). No reference
+ * generator exists for it; it uses only IEEE-exact operations so the CUDA
+ * generator reproduces it bit for bit. Boxes whose surface lies within 0.5 m
+ * of the start or the goal are redrawn (8 tries), else left out. */
+static float box_sdf(const float p[3], const float c[3], const float e[3]) {
+    const float k[3] = {fabsf(p[0] - c[0]) - e[0], fabsf(p[1] - c[1]) - e[1], fabsf(p[2] - c[2]) - e[2]};
+    return len3(fmaxf(k[0], 0.0f), fmaxf(k[1], 0.0f), fmaxf(k[2], 0.0f)) + fminf(fmaxf(k[0], fmaxf(k[1], k[2])), 0.0f);
+}
+static void wgenerate_baseline_clutter(mdn_world* w, uint32_t* rng) {
+    w->count = 0;
+    float dx = 1.0f, dy = 0.0f;
+    for (int attempt = 0; attempt < 8; attempt++) {
+        const float ux = 2.0f * o_wurand(rng) - 1.0f, uy = 2.0f * o_wurand(rng) - 1.0f;
+        const float norm = sqrtf(ux * ux + uy * uy);
+        if (norm > 0.1f && norm <= 1.0f) {
+            dx = ux / norm;
+            dy = uy / norm;
+            break;
+        }
+    }
+    const float dist = 2.0f + 6.0f * o_wurand(rng);
+    w->goal[0] = fminf(fmaxf(dist * dx, -1.5f), 7.5f);
+    w->goal[1] = fminf(fmaxf(dist * dy, -4.5f), 4.5f);
+    w->goal[2] = 1.0f + o_wurand(rng);
+    const float start[3] = {0.0f, 0.0f, 1.5f};
+    for (int i = 0; i < 16; i++)
+        for (int attempt = 0; attempt < 8; attempt++) {
+            const float c[3] = {-2.0f + 10.0f * o_wurand(rng), -5.0f + 10.0f * o_wurand(rng), 4.0f * o_wurand(rng)};
+            const float e[3] = {0.2f + 0.8f * o_wurand(rng), 0.2f + 0.8f * o_wurand(rng), 0.2f + 0.8f * o_wurand(rng)};
+            if (box_sdf(start, c, e) > 0.5f && box_sdf(w->goal, c, e) > 0.5f) {
+                wadd_box(w, c[0], c[1], c[2], e[0], e[1], e[2]);
+                break;
+            }
+        }
+}
+
 uint32_t o_wtraining_family(uint32_t family, uint32_t* rng) { /* world.hpp:293-298 */
     if (family == 7) return o_wrng(rng) % 7;
     if (family == 9 || family == 12) {
@@ -406,6 +444,7 @@ void o_wgenerate(mdn_world* w, uint32_t seed, uint32_t family, float distance) {
         case 14: w->count = 0; wgenerate_bent_hallway(w, &rng, distance); return;
         case 15: w->count = 0; wgenerate_connected_rooms(w, &rng, distance); return;
         case 16: w->count = 0; wgenerate_vertical_choices(w, &rng, distance); return;
+        case 17: wgenerate_baseline_clutter(w, &rng); return;
         default: break;
     }
     for (int i = 0; i < 16; i++) {

@@ -56,6 +56,7 @@ def load_oracle():
     d("o_wgenerate", None, _P, _U, _U, _F)
     d("o_wtraining_family", _U, _U, _P)
     d("o_set_argument_order", None, ctypes.c_int)
+    d("o_wrng", _U, _P)
     d("o_pixel_ray", None, _F, _F, _U, _P)
     d("o_nav_guidance", None, _P, _P, _P, _F, _P, _F, _F, _P)
     d("o_nav_guidance_memory", None, _P, _P, _P, _F, _P, _F, _F, _P, _P, _P, _U, _U, _P, _F)

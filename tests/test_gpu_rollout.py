@@ -87,15 +87,16 @@ CONFIGS = [
     dict(family=12, sensor_delay=1, command_delay=1, wind=0.5, depth_noise=0.05, dropout=0.1),
     dict(family=13),
     dict(family=7, risk_coef=0.5, max_steps=7),
-    dict(family=1, sensor_period=2, velocity_contract=0, speed=2.0),
+    dict(family=1, sensor_period=2, velocity_contract=0, distance=5.0),
     dict(family=1, mode=1),
     dict(family=4, eval=1, max_steps=9),
+    dict(family=17),
 ]
 
 
 @pytest.mark.parametrize("extra", CONFIGS, ids=[str(c) for c in CONFIGS])
 def test_reset_bitwise(pkg, om, raptor, extra):
-    cfg = pkg.layouts.default_config(n=300, speed=1.0, distance=3.0, seed=5, **extra)
+    cfg = pkg.layouts.default_config(**{**dict(n=300, speed=1.0, distance=3.0, seed=5), **extra})
     gpu, ora = make_pair(pkg, om, raptor, cfg, 4)
     try:
         for name in STATE_KEYS + ("actor", "critic"):
@@ -107,8 +108,11 @@ def test_reset_bitwise(pkg, om, raptor, extra):
 @pytest.mark.parametrize("extra", CONFIGS, ids=[str(c) for c in CONFIGS])
 def test_teacher_forced_steps(pkg, om, raptor, extra):
     n, T = 256, 12
-    cfg = pkg.layouts.default_config(n=n, speed=1.0, distance=3.0, seed=9, **extra)
+    cfg = pkg.layouts.default_config(**{**dict(n=n, speed=1.0, distance=3.0, seed=9), **extra})
     gpu, ora = make_pair(pkg, om, raptor, cfg, T)
+    # Depth noise draws Box-Muller normals (logf/cosf, sim.metal:154-156): the
+    # noisy ranges then match to the last ulp only, so compare them with RTOL.
+    exact_depth = float(cfg["depth_noise"]) == 0.0
     try:
         for t in range(T):
             # identical inputs: the oracle's state becomes the GPU's state
@@ -120,7 +124,10 @@ def test_teacher_forced_steps(pkg, om, raptor, extra):
             obs_g = gpu.download("obs").reshape(T * n, 184)[rows]
             obs_o = ora.buf("obs").reshape(T * n, 184)[rows]
             # depth pool + 21 context features: same IEEE operations -> bitwise
-            assert np.array_equal(obs_g[:, :181], obs_o[:, :181]), f"t={t} obs[:181]"
+            if exact_depth:
+                assert np.array_equal(obs_g[:, :181], obs_o[:, :181]), f"t={t} obs[:181]"
+            else:
+                close(obs_g[:, :181], obs_o[:, :181], f"t={t} obs[:181]")
             close(obs_g[:, 181:], obs_o[:, 181:], f"t={t} guidance hint")
             assert np.array_equal(gpu.download("co").reshape(T * n, 32)[rows],
                                   ora.buf("co").reshape(T * n, 32)[rows]), f"t={t} critic obs"
@@ -141,7 +148,10 @@ def test_teacher_forced_steps(pkg, om, raptor, extra):
             for f in RUN_FLOATS:
                 close(rs_g[f], rs_o[f], f"t={t} runs.{f}")
             assert gpu.download("worlds").tobytes() == ora.buf("worlds").tobytes(), f"t={t} worlds"
-            assert np.array_equal(gpu.download("sensors"), ora.buf("sensors")), f"t={t} sensors"
+            if exact_depth:
+                assert np.array_equal(gpu.download("sensors"), ora.buf("sensors")), f"t={t} sensors"
+            else:
+                close(gpu.download("sensors"), ora.buf("sensors"), f"t={t} sensors")
             assert np.array_equal(gpu.download("poses"), ora.buf("poses")), f"t={t} poses"
             close(gpu.download("commands"), ora.buf("commands"), f"t={t} commands")
     finally:
