@@ -13,8 +13,12 @@
 
 namespace mdn {
 
-__constant__ float c_pixel_ray[kPixels * 3];  // nav_sensor_pixel_ray(1, 0.75, k), sensor_profile.hpp:89-91
-__constant__ float c_pool_ray[80 * 3];        // nav_ray(row, col, 0.75), guidance.hpp:22-26
+// Camera tables in global memory, read through the L1: lanes index them with
+// different pixels, which the constant cache would serialise.
+__device__ float g_pixel_ray[kPixels * 3];  // nav_sensor_pixel_ray(1, 0.75, k), sensor_profile.hpp:89-91
+__device__ float g_pool_ray[80 * 3];        // nav_ray(row, col, 0.75), guidance.hpp:22-26
+#define c_pixel_ray_at(i) __ldg(&g_pixel_ray[(i)])
+#define c_pool_ray_at(i) __ldg(&g_pool_ray[(i)])
 
 // ------------------------------------------------------------------ reset
 __global__ void k_reset(SimArgs a, int first) {
@@ -38,6 +42,10 @@ struct WarpScene {
     float cx[16], cy[16], cz[16];   // obstacle centres at the step's time
     float sx[16], sy[16], sz[16];   // sizes
     uint32_t kind[16];
+    // obstacles that can be seen this step, compacted: index, centre relative
+    // to the camera, squared distance, inflated bounding radius (and square)
+    int cand[16];
+    float qx[16], qy[16], qz[16], q2[16], rb[16], rb2[16];
     float cur[80], prev[80];        // pooled ranges (metres, obs*12 as the reference re-derives them)
     float ctx[24];
 };
@@ -78,9 +86,9 @@ __device__ __forceinline__ float cell_risk(const WarpScene& ws, int row, int col
                 const int k = r * 10 + c;
                 const float old = ws.prev[k], now = ws.cur[k];
                 if (old < 11.9f && now < 11.9f) {
-                    const float* ray = c_pool_ray + 3 * k;
                     const float unexpected = (old - now) / fmaxf(sensor_dt, 1e-3f) -
-                                             (vel[0] * ray[0] + vel[1] * ray[1] + vel[2] * ray[2]);
+                                             (vel[0] * c_pool_ray_at(3 * k) + vel[1] * c_pool_ray_at(3 * k + 1) +
+                                              vel[2] * c_pool_ray_at(3 * k + 2));
                     if (unexpected > 0.5f) risk = fmaxf(risk, fminf(0.20f * unexpected, 1.0f));
                 }
             }
@@ -125,15 +133,64 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
         const float ox = pos[0] + 0.0f * r[0], oy = pos[1] + 0.0f * r[3], oz = pos[2] + 0.0f * r[6];  // mount 0
         const float noise = clean_env(c, gid) ? 0.0f : c.depth_noise;
         const float dropout = clean_env(c, gid) ? 0.0f : c.dropout;
-        for (int k = lane; k < kPixels; k += 32) {
-            const float rx = c_pixel_ray[3 * k], ry = c_pixel_ray[3 * k + 1], rz = c_pixel_ray[3 * k + 2];
+        // Visibility cull, one obstacle per lane: the obstacle's bounding sphere
+        // (inflated by 0.01% + 1 mm, far above the float error of the exact
+        // tests) must reach into the camera frustum |y| <= x, |z| <= 0.75 x
+        // (a superset of every pixel ray, sensor_profile.hpp:81-85) and lie
+        // nearer than the 12 m range cap. A culled obstacle cannot lower any
+        // ray's minimum, so the ranges stay bit-identical to testing all.
+        int ncand = 0;
+        {
+            bool visible = false;
+            float qx = 0.0f, qy = 0.0f, qz = 0.0f, q2 = 0.0f, rbi = 0.0f;
+            if (lane < int(count)) {
+                const uint32_t kind = ws.kind[lane];
+                const float e0 = ws.sx[lane], e1 = ws.sy[lane], e2 = ws.sz[lane];
+                const float bound = kind == 0 ? sqrtf(e0 * e0 + e1 * e1 + e2 * e2)
+                                  : (kind == 2 ? sqrtf(e0 * e0 + e2 * e2) : e0);
+                rbi = bound * 1.0001f + 1e-3f;
+                qx = ws.cx[lane] - ox;
+                qy = ws.cy[lane] - oy;
+                qz = ws.cz[lane] - oz;
+                q2 = qx * qx + qy * qy + qz * qz;
+                const float bx = r[0] * qx + r[3] * qy + r[6] * qz;  // body frame = R^T q
+                const float by = r[1] * qx + r[4] * qy + r[7] * qz;
+                const float bz = r[2] * qx + r[5] * qy + r[8] * qz;
+                visible = (bx - by) * 0.70710678f >= -rbi && (bx + by) * 0.70710678f >= -rbi &&
+                          (0.75f * bx - bz) * 0.8f >= -rbi && (0.75f * bx + bz) * 0.8f >= -rbi &&
+                          sqrtf(q2) - rbi < 12.0f;
+            }
+            const unsigned vis = __ballot_sync(0xffffffffu, visible);
+            if (visible) {
+                const int slot = __popc(vis & ((1u << lane) - 1u));
+                ws.cand[slot] = lane;
+                ws.qx[slot] = qx; ws.qy[slot] = qy; ws.qz[slot] = qz;
+                ws.q2[slot] = q2; ws.rb[slot] = rbi; ws.rb2[slot] = rbi * rbi;
+            }
+            ncand = __popc(vis);
+            __syncwarp();
+        }
+        // Each pass covers one 4-column x 8-row pixel tile (10 tiles = 20x16),
+        // so a warp's rays are angular neighbours and share their culls.
+        for (int tile = 0; tile < kPixels / 32; tile++) {
+            const int col = (tile % 5) * 4 + (lane & 3), prow = (tile / 5) * 8 + (lane >> 2);
+            const int k = prow * 20 + col;
+            const float rx = c_pixel_ray_at(3 * k), ry = c_pixel_ray_at(3 * k + 1), rz = c_pixel_ray_at(3 * k + 2);
             const float dx = r[0] * rx + r[1] * ry + r[2] * rz;
             const float dy = r[3] * rx + r[4] * ry + r[5] * rz;
             const float dz = r[6] * rx + r[7] * ry + r[8] * rz;
             float best = 12.0f;
             best = fminf(best, ray_box(ox, oy, oz, dx, dy, dz, a.room_c[0], a.room_c[1], a.room_c[2], a.room_e[0],
                                        a.room_e[1], a.room_e[2]));
-            for (uint32_t o = 0; o < count; o++) {
+            for (int j = 0; j < ncand; j++) {
+                // Per-ray bounding-sphere test: behind the camera, beyond the
+                // current nearest hit, or passing outside the sphere -> the
+                // exact test could only return a miss or a larger range.
+                const float tc = ws.qx[j] * dx + ws.qy[j] * dy + ws.qz[j] * dz;
+                const float rbj = ws.rb[j];
+                if (tc + rbj < 0.0f || tc - rbj >= best) continue;
+                if (ws.q2[j] - tc * tc > ws.rb2[j]) continue;
+                const int o = ws.cand[j];
                 const uint32_t kind = ws.kind[o];
                 float t = 1000.0f;
                 if (kind == 0)
@@ -227,7 +284,7 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
             float best_range_lane = 0.0f;
             for (int k = lane; k < 80; k += 32) {
                 const int row_ = k / 10, col = k % 10;
-                const float* d = c_pool_ray + 3 * k;
+                const float d[3] = {c_pool_ray_at(3 * k), c_pool_ray_at(3 * k + 1), c_pool_ray_at(3 * k + 2)};
                 const float alignment = d[0] * goal[0] + d[1] * goal[1] + d[2] * goal[2];
                 const float nearby = pooled_min3x3(ws.cur, row_, col);
                 const float risk = cell_risk(ws, row_, col, gvel, sensor_dt);
@@ -252,9 +309,9 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
             (void)my_best;
             float best_dir[3] = {1, 0, 0};
             if (best_cell < 80) {
-                best_dir[0] = c_pool_ray[3 * best_cell];
-                best_dir[1] = c_pool_ray[3 * best_cell + 1];
-                best_dir[2] = c_pool_ray[3 * best_cell + 2];
+                best_dir[0] = c_pool_ray_at(3 * best_cell);
+                best_dir[1] = c_pool_ray_at(3 * best_cell + 1);
+                best_dir[2] = c_pool_ray_at(3 * best_cell + 2);
             }
             const int grow = goal_cell < 80 ? goal_cell / 10 : 0, gcol = goal_cell < 80 ? goal_cell % 10 : 0;
             const float desired_speed = fminf(1.6f, sqrtf(4.0f * fmaxf(distance - 0.28f, 0.0f)));
@@ -618,9 +675,9 @@ __global__ void __launch_bounds__(kAdvanceThreads) k_advance(SimArgs a) {
 static inline unsigned blocks_for(uint32_t n, int per_block) { return (n + per_block - 1) / per_block; }
 
 cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays) {
-    cudaError_t e = cudaMemcpyToSymbol(c_pixel_ray, pixel_rays, sizeof(float) * kPixels * 3);
+    cudaError_t e = cudaMemcpyToSymbol(g_pixel_ray, pixel_rays, sizeof(float) * kPixels * 3);
     if (e != cudaSuccess) return e;
-    return cudaMemcpyToSymbol(c_pool_ray, pool_rays, sizeof(float) * 80 * 3);
+    return cudaMemcpyToSymbol(g_pool_ray, pool_rays, sizeof(float) * 80 * 3);
 }
 
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s) {
