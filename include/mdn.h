@@ -205,6 +205,9 @@ int mdn_sim_get_config(mdn_sim* sim, mdn_sim_config* out);       /* Sim::cfg */
 int mdn_sim_collect(mdn_sim* sim, uint32_t steps);
 /* One policy step at an explicit tick (teacher-forced parity runs). */
 int mdn_sim_step(mdn_sim* sim, uint32_t tick);
+/* Device pointer and size of a buffer. A caller that writes MDN_BUF_WORLDS
+ * through this pointer must then call mdn_sim_upload(sim, MDN_BUF_WORLDS,
+ * NULL, 0, 0), which refreshes the simulator's internal copy of the worlds. */
 int mdn_sim_buffer(mdn_sim* sim, int id, void** dev_ptr, size_t* bytes);
 /* Replacements for host access to MTLBuffer.contents (navigation_training.hpp:23-24). */
 int mdn_sim_download(mdn_sim* sim, int id, void* host, size_t offset, size_t bytes);

@@ -198,6 +198,7 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
     a.states = static_cast<mdn_physics_state*>(buf[MDN_BUF_STATES]);
     a.runs = static_cast<mdn_sim_run*>(buf[MDN_BUF_RUNS]);
     a.worlds = static_cast<mdn_world*>(buf[MDN_BUF_WORLDS]);
+    a.world_soa = world_soa;
     a.sensors = static_cast<float*>(buf[MDN_BUF_SENSORS]);
     a.poses = static_cast<float*>(buf[MDN_BUF_POSES]);
     a.commands = static_cast<float*>(buf[MDN_BUF_COMMANDS]);
@@ -329,6 +330,13 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
                 throw Error(MDN_ERR_NOMEM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
             }
         }
+        {
+            const cudaError_t e = cudaMalloc(&sim->world_soa, n * kWorldSoaWords * sizeof(float));
+            if (e != cudaSuccess) {
+                for (int k = 0; k < MDN_BUF_COUNT; k++) cudaFree(sim->buf[k]);
+                throw Error(MDN_ERR_NOMEM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
+            }
+        }
         cuda_check(cudaStreamCreateWithFlags(&sim->stream, cudaStreamNonBlocking), "cudaStreamCreate");
         cuda_check(cudaEventCreate(&sim->ev_start), "cudaEventCreate");
         cuda_check(cudaEventCreate(&sim->ev_stop), "cudaEventCreate");
@@ -350,7 +358,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
                        MDN_BUF_CONTACT_ID})
             cuda_check(cudaMemsetAsync(sim->buf[id], 0, b[id], sim->stream), "clear rollout buffers");
         // Persistent act kernel: enough CTAs to fill every SM twice.
-        sim->act_grid = int(std::min<size_t>((n + 7) / 8, size_t(dev->sm_count) * 2));
+        sim->act_grid = int(std::min<size_t>((n + 31) / 32, size_t(dev->sm_count) * 2));
         cuda_check(launch_reset(sim->args(0), true, sim->stream), "reset");
         cuda_check(cudaStreamSynchronize(sim->stream), "mdn_sim_create");
         dev->sims.push_back(sim.get());
@@ -365,6 +373,7 @@ extern "C" int mdn_sim_destroy(mdn_sim* sim) {
         cudaStreamSynchronize(sim->stream);
         sim->release_graphs();
         for (int id = 0; id < MDN_BUF_COUNT; id++) cudaFree(sim->buf[id]);
+        cudaFree(sim->world_soa);
         cudaEventDestroy(sim->ev_start);
         cudaEventDestroy(sim->ev_stop);
         cudaStreamDestroy(sim->stream);
@@ -448,6 +457,11 @@ extern "C" int mdn_sim_last_collect_ms(mdn_sim* sim, float* ms) {
     });
 }
 
+namespace mdn {
+// Callers that wrote the worlds buffer directly (checkpoint load) refresh the mirror.
+void refresh_world_mirror(mdn_sim* sim) { cuda_check(launch_world_mirror(sim->args(0), sim->stream), "world mirror"); }
+}  // namespace mdn
+
 extern "C" int mdn_sim_buffer(mdn_sim* sim, int id, void** dev_ptr, size_t* bytes) {
     return guarded([&] {
         checked(sim);
@@ -477,6 +491,7 @@ extern "C" int mdn_sim_upload(mdn_sim* sim, int id, const void* host, size_t off
         require(offset <= sim->bytes[id] && bytes <= sim->bytes[id] - offset, MDN_ERR_INVALID, "upload out of range");
         cuda_check(cudaMemcpyAsync(static_cast<char*>(sim->buf[id]) + offset, host, bytes, cudaMemcpyHostToDevice,
                                    sim->stream), "upload");
+        if (id == MDN_BUF_WORLDS) cuda_check(launch_world_mirror(sim->args(0), sim->stream), "world mirror");
         cuda_check(cudaStreamSynchronize(sim->stream), "upload");
     });
 }

@@ -48,6 +48,7 @@ int guarded(F&& fn) {
 cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays);
 cudaError_t configure_kernels();
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s);
+cudaError_t launch_world_mirror(const SimArgs& a, cudaStream_t s);
 cudaError_t launch_step(const SimArgs& a, int act_grid, cudaStream_t s);
 size_t act_smem_bytes();
 cudaError_t launch_step_profiled(const SimArgs& a, int act_grid, cudaStream_t s, cudaEvent_t ev[4]);
@@ -74,6 +75,7 @@ struct mdn_sim {
     uint32_t horizon = 0, n = 0, env_base = 0;
     cudaStream_t stream = nullptr;
     void* buf[MDN_BUF_COUNT] = {};
+    float* world_soa = nullptr;  // device mirror of the worlds, structure of arrays
     size_t bytes[MDN_BUF_COUNT] = {};
     float room_lo[3], room_hi[3], room_c[3], room_e[3];
     int act_grid = 1;

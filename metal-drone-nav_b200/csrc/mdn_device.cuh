@@ -157,6 +157,32 @@ __device__ __forceinline__ float world_clearance(const SimArgs& a, const mdn_wor
     return best;
 }
 
+// wclearance (world.hpp:84-99) reading the structure-of-arrays mirror: thread
+// i's loads of word w across a warp are contiguous.
+__device__ __forceinline__ float world_clearance_soa(const SimArgs& a, uint32_t i, const float p[3], float t,
+                                                     int32_t* argmin) {
+    const float* soa = a.world_soa;
+    const size_t n = a.n;
+    float best = room_clearance(a, p);
+    int32_t id = -1;
+    uint32_t count = __float_as_uint(__ldg(&soa[160 * n + i]));
+    count = count < 16u ? count : 16u;
+    for (uint32_t o = 0; o < count; o++) {
+        const float* f = soa + size_t(o) * 10 * n + i;
+        const uint32_t kind = __float_as_uint(__ldg(f));
+        const float c[3] = {__ldg(f + n), __ldg(f + 2 * n), __ldg(f + 3 * n)};
+        const float size[3] = {__ldg(f + 4 * n), __ldg(f + 5 * n), __ldg(f + 6 * n)};
+        const float v[3] = {__ldg(f + 7 * n), __ldg(f + 8 * n), __ldg(f + 9 * n)};
+        float cc[3];
+        obstacle_center(kind, c, size, v, t, cc);
+        const float cand = obstacle_clearance(kind, size, p[0] - cc[0], p[1] - cc[1], p[2] - cc[2]);
+        if (cand < best) id = int32_t(o);
+        best = fminf(best, cand);
+    }
+    if (argmin) *argmin = id;
+    return best;
+}
+
 // Body-to-world rotation from a wxyz quaternion, sim.metal:43-48.
 __device__ __forceinline__ void rotation(const float q[4], float r[9]) {
     const float w = q[0], x = q[1], y = q[2], z = q[3];
@@ -251,20 +277,30 @@ __device__ __forceinline__ void l2f_step(const mdn_physics_params& p, const floa
         if (a > 1.0f) a = 1.0f;
         sp[i] = a * half_range + p.action_min + half_range;
     }
-    float k1[17], k2[17], k3[17], k4[17], tmp[17];
-    l2f_derivative(p, s, sp, wind, k1);
+    // k1 + 2 k2 + 2 k3 + k4 accumulated left to right, the reference's order.
+    float k[17], acc[17], tmp[17];
+    l2f_derivative(p, s, sp, wind, k);
     const float hdt = 0.5f * p.dt;
 #pragma unroll
-    for (int i = 0; i < 17; ++i) tmp[i] = s[i] + hdt * k1[i];
-    l2f_derivative(p, tmp, sp, wind, k2);
+    for (int i = 0; i < 17; ++i) {
+        acc[i] = k[i];
+        tmp[i] = s[i] + hdt * k[i];
+    }
+    l2f_derivative(p, tmp, sp, wind, k);
 #pragma unroll
-    for (int i = 0; i < 17; ++i) tmp[i] = s[i] + hdt * k2[i];
-    l2f_derivative(p, tmp, sp, wind, k3);
+    for (int i = 0; i < 17; ++i) {
+        acc[i] = acc[i] + 2.0f * k[i];
+        tmp[i] = s[i] + hdt * k[i];
+    }
+    l2f_derivative(p, tmp, sp, wind, k);
 #pragma unroll
-    for (int i = 0; i < 17; ++i) tmp[i] = s[i] + p.dt * k3[i];
-    l2f_derivative(p, tmp, sp, wind, k4);
+    for (int i = 0; i < 17; ++i) {
+        acc[i] = acc[i] + 2.0f * k[i];
+        tmp[i] = s[i] + p.dt * k[i];
+    }
+    l2f_derivative(p, tmp, sp, wind, k);
 #pragma unroll
-    for (int i = 0; i < 17; ++i) out[i] = s[i] + p.dt * (k1[i] + 2.0f * k2[i] + 2.0f * k3[i] + k4[i]) / 6.0f;
+    for (int i = 0; i < 17; ++i) out[i] = s[i] + p.dt * (acc[i] + k[i]) / 6.0f;
     const float norm = sqrtf(out[3] * out[3] + out[4] * out[4] + out[5] * out[5] + out[6] * out[6]);
 #pragma unroll
     for (int i = 3; i < 7; ++i) out[i] /= norm;
@@ -306,7 +342,7 @@ __device__ __forceinline__ void raptor_forward(const float* __restrict__ w, cons
         x[row] = smax(value, 0.0f);
     }
     float nh[16];
-#pragma unroll 4
+#pragma unroll
     for (int i = 0; i < 16; ++i) {
         float ir = gi_b[i], hr = gh_b[i], iz = gi_b[16 + i], hz = gh_b[16 + i], in_ = gi_b[32 + i], hn = gh_b[32 + i];
 #pragma unroll

@@ -25,6 +25,7 @@ constexpr int kCriticB2 = kCriticW2 + kHidden;
 constexpr int kCriticParams = kCriticB2 + 1;
 constexpr float kLogTwoPi = 1.8378770664093453f;
 constexpr float kTanV = 0.75f;  // legacy camera, sensor_profile.hpp:44-45
+constexpr int kWorldSoaWords = 161;
 
 // Everything one launch of a rollout kernel needs (passed by value).
 struct SimArgs {
@@ -36,6 +37,11 @@ struct SimArgs {
     mdn_physics_state* states;
     mdn_sim_run* runs;
     mdn_world* worlds;
+    // Structure-of-arrays mirror of `worlds` for thread-per-environment
+    // readers: word w of env i's obstacle block at world_soa[w * n + i],
+    // w = obstacle * 10 + field (kind bits, centre xyz, size xyz, velocity xyz),
+    // w = 160 the obstacle count. Written wherever a world is written.
+    float* world_soa;
     float* sensors;
     float* poses;
     float* commands;

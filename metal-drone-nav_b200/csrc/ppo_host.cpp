@@ -25,6 +25,7 @@ namespace mdn {
 // NCCL hooks (comm.cpp); no-ops on a single GPU.
 cudaError_t comm_allreduce_double(mdn_device* dev, double* buf, size_t count, cudaStream_t s, std::string& err);
 cudaError_t comm_allreduce_float(mdn_device* dev, float* buf, size_t count, cudaStream_t s, std::string& err);
+void refresh_world_mirror(mdn_sim* sim);
 }  // namespace mdn
 
 struct mdn_ppo {
@@ -492,6 +493,7 @@ extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t fa
         if (h.version >= 6) read_to_device(sim->buf[MDN_BUF_POSES], sim->bytes[MDN_BUF_POSES]);
         else cuda_check(cudaMemsetAsync(sim->buf[MDN_BUF_POSES], 0, sim->bytes[MDN_BUF_POSES], sim->stream), "poses");
         read_to_device(sim->buf[MDN_BUF_COMMANDS], sim->bytes[MDN_BUF_COMMANDS]);
+        refresh_world_mirror(sim);
         char extra;
         require(!f.read(&extra, 1), MDN_ERR_IO, "PPO checkpoint has trailing data");
         require(h.optimizer_step <= uint64_t(UINT32_MAX), MDN_ERR_MISMATCH, "PPO checkpoint Adam step is too large");

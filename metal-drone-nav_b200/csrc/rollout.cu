@@ -29,6 +29,13 @@ __global__ void k_reset(SimArgs a, int first) {
     refill_rings(a, (blockIdx.x * blockDim.x) + (threadIdx.x & ~31u), mask);
 }
 
+// Refresh the structure-of-arrays mirror from the AoS worlds (after an upload
+// or a checkpoint load replaced them).
+__global__ void k_world_mirror(SimArgs a) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < a.n) mirror_world(a, i);
+}
+
 // ------------------------------------------------------------------ sense
 // One warp per environment. Lanes cast 10 of the 320 rays each (world.hpp:71-83)
 // against the room and the env's obstacles staged in shared memory, write the
@@ -47,6 +54,7 @@ struct WarpScene {
     int cand[16];
     float qx[16], qy[16], qz[16], q2[16], rb[16], rb2[16];
     float cur[80], prev[80];        // pooled ranges (metres, obs*12 as the reference re-derives them)
+    float risk_term[80];            // guidance.hpp:59-66 contribution of each cell as a neighbour
     float ctx[24];
 };
 
@@ -76,21 +84,29 @@ __device__ __forceinline__ float pooled_min3x3(const float* range, int row, int 
     return nearest;
 }
 
-__device__ __forceinline__ float cell_risk(const WarpScene& ws, int row, int col, const float vel[3], float sensor_dt) {
-    float risk = 0.0f;  // guidance.hpp:58-67
+// Contribution of cell k to the temporal risk of the cells around it
+// (guidance.hpp:59-66): the per-neighbour term depends only on the neighbour.
+__device__ __forceinline__ float neighbour_risk(const WarpScene& ws, int k, const float vel[3], float sensor_dt) {
+    const float old = ws.prev[k], now = ws.cur[k];
+    if (!(old < 11.9f && now < 11.9f)) return 0.0f;
+    const float unexpected = (old - now) / fmaxf(sensor_dt, 1e-3f) -
+                             (vel[0] * c_pool_ray_at(3 * k) + vel[1] * c_pool_ray_at(3 * k + 1) +
+                              vel[2] * c_pool_ray_at(3 * k + 2));
+    return unexpected > 0.5f ? fminf(0.20f * unexpected, 1.0f) : 0.0f;
+}
+
+// risk = max(0, max over in-grid 3x3 neighbours of their terms): the same
+// fmaxf chain as the reference's loop, in any order (fmaxf is exact).
+__device__ __forceinline__ float cell_risk(const WarpScene& ws, int row, int col, float sensor_dt) {
+    float risk = 0.0f;
     if (sensor_dt > 1e-4f) {
+#pragma unroll
         for (int dr = -1; dr <= 1; dr++)
+#pragma unroll
             for (int dc = -1; dc <= 1; dc++) {
                 const int r = row + dr, c = col + dc;
                 if (r < 0 || r >= 8 || c < 0 || c >= 10) continue;
-                const int k = r * 10 + c;
-                const float old = ws.prev[k], now = ws.cur[k];
-                if (old < 11.9f && now < 11.9f) {
-                    const float unexpected = (old - now) / fmaxf(sensor_dt, 1e-3f) -
-                                             (vel[0] * c_pool_ray_at(3 * k) + vel[1] * c_pool_ray_at(3 * k + 1) +
-                                              vel[2] * c_pool_ray_at(3 * k + 2));
-                    if (unexpected > 0.5f) risk = fmaxf(risk, fminf(0.20f * unexpected, 1.0f));
-                }
+                risk = fmaxf(risk, ws.risk_term[r * 10 + c]);
             }
     }
     return risk;
@@ -170,6 +186,9 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
             ncand = __popc(vis);
             __syncwarp();
         }
+        const float rp[3] = {ox - a.room_c[0], oy - a.room_c[1], oz - a.room_c[2]};
+        const float re[3] = {a.room_e[0], a.room_e[1], a.room_e[2]};
+        const bool inside_room = fabsf(rp[0]) < re[0] && fabsf(rp[1]) < re[1] && fabsf(rp[2]) < re[2];
         // Each pass covers one 4-column x 8-row pixel tile (10 tiles = 20x16),
         // so a warp's rays are angular neighbours and share their culls.
         for (int tile = 0; tile < kPixels / 32; tile++) {
@@ -180,8 +199,21 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
             const float dy = r[3] * rx + r[4] * ry + r[5] * rz;
             const float dz = r[6] * rx + r[7] * ry + r[8] * rz;
             float best = 12.0f;
-            best = fminf(best, ray_box(ox, oy, oz, dx, dy, dz, a.room_c[0], a.room_c[1], a.room_c[2], a.room_e[0],
-                                       a.room_e[1], a.room_e[2]));
+            if (inside_room) {
+                // Origin strictly inside the room box: on every axis the two slab
+                // distances have opposite signs, lo < 0, and ray_box returns
+                // hi = min over axes of the non-negative one. Computing only that
+                // division gives the same float as world.hpp:48-57.
+                float hi = 1e20f;
+                const float dd[3] = {dx, dy, dz};
+#pragma unroll
+                for (int j = 0; j < 3; j++)
+                    if (!(fabsf(dd[j]) < 1e-8f)) hi = fminf(hi, ((dd[j] > 0.0f ? re[j] : -re[j]) - rp[j]) / dd[j]);
+                best = fminf(best, hi);
+            } else {
+                best = fminf(best, ray_box(ox, oy, oz, dx, dy, dz, a.room_c[0], a.room_c[1], a.room_c[2], a.room_e[0],
+                                           a.room_e[1], a.room_e[2]));
+            }
             for (int j = 0; j < ncand; j++) {
                 // Per-ray bounding-sphere test: behind the camera, beyond the
                 // current nearest hit, or passing outside the sphere -> the
@@ -282,12 +314,14 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
             float best_score = -1e20f, goal_dot = -1e20f;
             int best_cell = 1 << 20, goal_cell = 1 << 20;
             float best_range_lane = 0.0f;
+            for (int k = lane; k < 80; k += 32) ws.risk_term[k] = neighbour_risk(ws, k, gvel, sensor_dt);
+            __syncwarp();
             for (int k = lane; k < 80; k += 32) {
                 const int row_ = k / 10, col = k % 10;
                 const float d[3] = {c_pool_ray_at(3 * k), c_pool_ray_at(3 * k + 1), c_pool_ray_at(3 * k + 2)};
                 const float alignment = d[0] * goal[0] + d[1] * goal[1] + d[2] * goal[2];
                 const float nearby = pooled_min3x3(ws.cur, row_, col);
-                const float risk = cell_risk(ws, row_, col, gvel, sensor_dt);
+                const float risk = cell_risk(ws, row_, col, sensor_dt);
                 const float safe_range = fmaxf(nearby - risk, 0.0f);
                 const float score = 1.4f * alignment + 0.12f * fminf(safe_range, 6.0f);
                 if (score > best_score) {
@@ -373,11 +407,22 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
 // -------------------------------------------------------------------- act
 // Actor mean (tanh MLP 184->64->4 plus geometry prior, ppo.hpp:65-80), critic
 // value (32->64->1, ppo.hpp:82-93), Gaussian sample, log-prob, command ring,
-// command delay and desired velocity (sim.metal:229-271). One warp per env;
-// the CTA keeps W1 transposed in shared memory and loops over envs.
+// command delay and desired velocity (sim.metal:229-271). A warp handles four
+// environments per pass: lanes own hidden units (lane, lane+32), so every
+// weight loaded from shared memory feeds four environments; lanes 0-3 then
+// sample the four environments' actions in parallel. The CTA keeps W1
+// transposed in shared memory and loops over the environments.
 constexpr int kActWarps = 8;
+constexpr int kActEnvs = 4;
 constexpr int kActSmemFloats = kActorObs * kHidden + kHidden + kActions * kHidden + 2 * kActions +
-                               kCriticObs * kHidden + kHidden + kHidden + 1 + kActWarps * (kActorObs + kCriticObs);
+                               kCriticObs * kHidden + kHidden + kHidden + 1 +
+                               kActWarps * kActEnvs * (kActorObs + kCriticObs);
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
 
 __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
     extern __shared__ float sm[];
@@ -390,7 +435,7 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
     float* cb1 = cw1t + kCriticObs * kHidden;         // [64]
     float* cw2 = cb1 + kHidden;                       // [64]
     float* cb2 = cw2 + kHidden;                       // [1]
-    float* rows = cb2 + 1;                            // per warp obs[184] + co[32]
+    float* rows = cb2 + 1;                            // per warp: obs[4][184], co[4][32]
     const int tid = threadIdx.x;
     for (int k = tid; k < kActorObs * kHidden; k += blockDim.x) {
         const int h = k / kActorObs, col = k % kActorObs;
@@ -413,86 +458,107 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
     if (tid == 0) cb2[0] = a.critic[kCriticB2];
     __syncthreads();
     const int lane = tid & 31, wid = tid >> 5;
-    float* my_obs = rows + wid * (kActorObs + kCriticObs);
-    float* my_co = my_obs + kActorObs;
+    float* my_obs = rows + wid * kActEnvs * (kActorObs + kCriticObs);  // [4][184]
+    float* my_co = my_obs + kActEnvs * kActorObs;                        // [4][32]
     const mdn_sim_config& c = a.cfg;
-    for (uint32_t i = blockIdx.x * kActWarps + wid; i < a.n; i += gridDim.x * kActWarps) {
-        mdn_sim_run& run = a.runs[i];
-        if (c.eval && run.episodes) continue;
-        const size_t row = size_t(a.tick) * a.n + i;
-        const float* obs_g = a.obs + row * kActorObs;
-        const float* co_g = a.co + row * kCriticObs;
-        for (int k = lane; k < kActorObs; k += 32) my_obs[k] = obs_g[k];
-        my_co[lane] = co_g[lane];
+    const uint32_t stride = gridDim.x * kActWarps * kActEnvs;
+    for (uint32_t base = (blockIdx.x * kActWarps + wid) * kActEnvs; base < a.n; base += stride) {
+        const size_t row0 = size_t(a.tick) * a.n + base;
+        const int envs = int(min(uint32_t(kActEnvs), a.n - base));
+        for (int e = 0; e < kActEnvs; e++) {
+            const float* og = a.obs + (row0 + e) * kActorObs;
+            for (int k = lane; k < kActorObs; k += 32) my_obs[e * kActorObs + k] = e < envs ? og[k] : 0.0f;
+            my_co[e * kCriticObs + lane] = e < envs ? a.co[(row0 + e) * kCriticObs + lane] : 0.0f;
+        }
         __syncwarp();
-        // actor hidden units lane and lane+32: in-order dot from zero, then the bias (cpu_reference.hpp:437-442)
-        float z0 = 0.0f, z1 = 0.0f;
-#pragma unroll 8
+        // actor pre-activations, in-order dot from zero then the bias (cpu_reference.hpp:437-442)
+        float z0[kActEnvs], z1[kActEnvs];
+#pragma unroll
+        for (int e = 0; e < kActEnvs; e++) z0[e] = z1[e] = 0.0f;
+#pragma unroll 4
         for (int k = 0; k < kActorObs; k++) {
-            const float o = my_obs[k];
-            z0 = fmaf(o, w1t[k * kHidden + lane], z0);
-            z1 = fmaf(o, w1t[k * kHidden + lane + 32], z1);
-        }
-        const float h0 = tanhf(z0 + b1[lane]), h1 = tanhf(z1 + b1[lane + 32]);
-        float mean[4];
+            const float wa = w1t[k * kHidden + lane], wb = w1t[k * kHidden + lane + 32];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            float part = fmaf(h0, w2[j * kHidden + lane], h1 * w2[j * kHidden + lane + 32]);
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-            mean[j] = part + b2[j];
-            if (j < 3) mean[j] += my_obs[kActorObs - 3 + j];
+            for (int e = 0; e < kActEnvs; e++) {
+                const float o = my_obs[e * kActorObs + k];
+                z0[e] = fmaf(o, wa, z0[e]);
+                z1[e] = fmaf(o, wb, z1[e]);
+            }
         }
-        // critic value (cpu_reference.hpp:449-458)
-        float y0 = 0.0f, y1 = 0.0f;
-#pragma unroll 8
+        float y0[kActEnvs], y1[kActEnvs];
+#pragma unroll
+        for (int e = 0; e < kActEnvs; e++) y0[e] = y1[e] = 0.0f;
+#pragma unroll 4
         for (int k = 0; k < kCriticObs; k++) {
-            const float o = my_co[k];
-            y0 = fmaf(o, cw1t[k * kHidden + lane], y0);
-            y1 = fmaf(o, cw1t[k * kHidden + lane + 32], y1);
-        }
-        float vpart = fmaf(tanhf(y0 + cb1[lane]), cw2[lane], tanhf(y1 + cb1[lane + 32]) * cw2[lane + 32]);
+            const float wa = cw1t[k * kHidden + lane], wb = cw1t[k * kHidden + lane + 32];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) vpart += __shfl_xor_sync(0xffffffffu, vpart, off);
-        if (lane == 0) {
-            a.values[row] = vpart + cb2[0];
-            uint32_t rng = run.rng;
-            const uint32_t steps = run.steps;
-            float act[4];
-            float* cmd = a.commands + size_t(i) * kFrames * kActions;
+            for (int e = 0; e < kActEnvs; e++) {
+                const float o = my_co[e * kCriticObs + k];
+                y0[e] = fmaf(o, wa, y0[e]);
+                y1[e] = fmaf(o, wb, y1[e]);
+            }
+        }
+        // heads: every lane ends with all four environments' means and values
+        float mean_mine[4] = {0, 0, 0, 0}, value_mine = 0.0f;
+#pragma unroll
+        for (int e = 0; e < kActEnvs; e++) {
+            const float h0 = tanhf(z0[e] + b1[lane]), h1 = tanhf(z1[e] + b1[lane + 32]);
+#pragma unroll
             for (int j = 0; j < 4; j++) {
-                act[j] = mean[j] + ((c.mode == 0 || c.mode == 22) ? expf(log_std[j]) * sim_normal(rng) : 0.0f);
-                if (c.mode == 1) act[j] = sim_normal(rng);
-                a.actions[row * kActions + j] = act[j];
-                cmd[(steps % kFrames) * kActions + j] = tanhf(act[j]);
+                float m = warp_sum(fmaf(h0, w2[j * kHidden + lane], h1 * w2[j * kHidden + lane + 32])) + b2[j];
+                if (j < 3) m += my_obs[e * kActorObs + kActorObs - 3 + j];
+                if (lane == e) mean_mine[j] = m;
             }
-            float lp = 0.0f;  // gaussian_log_prob, ppo.hpp:95-103
-            for (int j = 0; j < 4; j++) {
-                const float inv_std = expf(-log_std[j]);
-                const float d = (act[j] - mean[j]) * inv_std;
-                lp += -0.5f * (d * d + 2.0f * log_std[j] + kLogTwoPi);
+            const float v = warp_sum(fmaf(tanhf(y0[e] + cb1[lane]), cw2[lane],
+                                          tanhf(y1[e] + cb1[lane + 32]) * cw2[lane + 32])) + cb2[0];
+            if (lane == e) value_mine = v;
+        }
+        __syncwarp();
+        const uint32_t i = base + uint32_t(lane);
+        if (lane < envs) {
+            mdn_sim_run& run = a.runs[i];
+            if (!(c.eval && run.episodes)) {
+                const size_t row = row0 + lane;
+                a.values[row] = value_mine;
+                uint32_t rng = run.rng;
+                const uint32_t steps = run.steps;
+                float act[4];
+                float* cmd = a.commands + size_t(i) * kFrames * kActions;
+                for (int j = 0; j < 4; j++) {
+                    act[j] = mean_mine[j] + ((c.mode == 0 || c.mode == 22) ? expf(log_std[j]) * sim_normal(rng) : 0.0f);
+                    if (c.mode == 1) act[j] = sim_normal(rng);
+                    a.actions[row * kActions + j] = act[j];
+                    cmd[(steps % kFrames) * kActions + j] = tanhf(act[j]);
+                }
+                float lp = 0.0f;  // gaussian_log_prob, ppo.hpp:95-103
+                for (int j = 0; j < 4; j++) {
+                    const float inv_std = expf(-log_std[j]);
+                    const float d = (act[j] - mean_mine[j]) * inv_std;
+                    lp += -0.5f * (d * d + 2.0f * log_std[j] + kLogTwoPi);
+                }
+                a.logp[row] = lp;
+                run.rng = rng;
+                const uint32_t gid = a.env_base + i;
+                const uint32_t delay = clean_env(c, gid) ? 0u : c.command_delay;
+                const uint32_t applied = steps > delay ? steps - delay : 0;
+                float pn[4];
+                for (int j = 0; j < 4; j++) {
+                    pn[j] = steps < delay ? 0.0f : cmd[(applied % kFrames) * kActions + j];
+                    run.previous_nav[j] = pn[j];
+                }
+                float r[9];
+                const mdn_physics_state& st = a.states[i];
+                const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2],
+                                    st.orientation_wxyz[3]};
+                rotation(q, r);
+                float v[3] = {pn[0] * c.speed, pn[1] * c.speed, pn[2] * c.speed * (c.velocity_contract == 0 ? 0.5f : 1.0f)};
+                if (c.velocity_contract == 1) {
+                    const float scale = smin(1.0f, c.speed / smax(len3(v[0], v[1], v[2]), 1e-8f));
+                    for (int j = 0; j < 3; j++) v[j] *= scale;
+                }
+                for (int j = 0; j < 3; j++) run.desired_velocity[j] = r[j * 3] * v[0] + r[j * 3 + 1] * v[1] + r[j * 3 + 2] * v[2];
+                run.yaw += pn[3] * a.physics->dt * float(c.substeps) * 0.5f;
             }
-            a.logp[row] = lp;
-            run.rng = rng;
-            const uint32_t gid = a.env_base + i;
-            const uint32_t delay = clean_env(c, gid) ? 0u : c.command_delay;
-            const uint32_t applied = steps > delay ? steps - delay : 0;
-            float pn[4];
-            for (int j = 0; j < 4; j++) {
-                pn[j] = steps < delay ? 0.0f : cmd[(applied % kFrames) * kActions + j];
-                run.previous_nav[j] = pn[j];
-            }
-            float r[9];
-            const mdn_physics_state& st = a.states[i];
-            const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2], st.orientation_wxyz[3]};
-            rotation(q, r);
-            float v[3] = {pn[0] * c.speed, pn[1] * c.speed, pn[2] * c.speed * (c.velocity_contract == 0 ? 0.5f : 1.0f)};
-            if (c.velocity_contract == 1) {
-                const float scale = smin(1.0f, c.speed / smax(len3(v[0], v[1], v[2]), 1e-8f));
-                for (int j = 0; j < 3; j++) v[j] *= scale;
-            }
-            for (int j = 0; j < 3; j++) run.desired_velocity[j] = r[j * 3] * v[0] + r[j * 3 + 1] * v[1] + r[j * 3 + 2] * v[2];
-            run.yaw += pn[3] * a.physics->dt * float(c.substeps) * 0.5f;
         }
         __syncwarp();
     }
@@ -506,7 +572,7 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
 // obstacle nearest at the step's closest approach.
 constexpr int kAdvanceThreads = 128;
 
-__global__ void __launch_bounds__(kAdvanceThreads) k_advance(SimArgs a) {
+__global__ void __launch_bounds__(kAdvanceThreads, 4) k_advance(SimArgs a) {
     __shared__ float raptor_w[2084];
     __shared__ float critic_w[kCriticParams];
     __shared__ mdn_physics_params params;
@@ -586,7 +652,7 @@ __global__ void __launch_bounds__(kAdvanceThreads) k_advance(SimArgs a) {
             for (int j = 0; j < 17; j++) s[j] = nx[j];
             elapsed += params.dt;
             int32_t id;
-            const float clearance = world_clearance(a, w, s, elapsed, &id);
+            const float clearance = world_clearance_soa(a, i, s, elapsed, &id);
             if (clearance < step_clearance) contact = id;
             step_clearance = smin(step_clearance, clearance);
             min_clear = smin(min_clear, clearance);
@@ -632,17 +698,23 @@ __global__ void __launch_bounds__(kAdvanceThreads) k_advance(SimArgs a) {
                 co[j + 16] = (refp[j] - s[j]) * 2.0f;
             }
             for (int j = 0; j < 4; j++) co[9 + j] = s[3 + j];
-            co[19] = world_clearance(a, w, s, elapsed, nullptr) / 5.0f;
+            co[19] = world_clearance_soa(a, i, s, elapsed, nullptr) / 5.0f;
             co[20] = float(steps) / 200.0f;
             for (int j = 21; j < 30; j++) co[j] = 0.0f;
             const uint32_t m = w.count < 3u ? w.count : 3u;
-            for (uint32_t o = 0; o < m; o++) {
-                float cc[3];
-                const mdn_obstacle& ob = w.obstacles[o];
-                obstacle_center(ob.kind, ob.center, ob.size, ob.velocity, elapsed, cc);
-                co[21 + o * 3] = (cc[0] - s[0]) / 10.0f;
-                co[22 + o * 3] = (cc[1] - s[1]) / 10.0f;
-                co[23 + o * 3] = (cc[2] - s[2]) / 10.0f;
+#pragma unroll
+            for (uint32_t o = 0; o < 3; o++) {
+                if (o < m) {
+                    float cc[3];
+                    const float* f = a.world_soa + size_t(o) * 10 * a.n + i;
+                    const float c3[3] = {f[a.n], f[2 * a.n], f[3 * a.n]};
+                    const float s3[3] = {f[4 * a.n], f[5 * a.n], f[6 * a.n]};
+                    const float v3[3] = {f[7 * a.n], f[8 * a.n], f[9 * a.n]};
+                    obstacle_center(__float_as_uint(f[0]), c3, s3, v3, elapsed, cc);
+                    co[21 + o * 3] = (cc[0] - s[0]) / 10.0f;
+                    co[22 + o * 3] = (cc[1] - s[1]) / 10.0f;
+                    co[23 + o * 3] = (cc[2] - s[2]) / 10.0f;
+                }
             }
             co[30] = w.wind[0];
             co[31] = w.wind[1];
@@ -678,6 +750,11 @@ cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays
     cudaError_t e = cudaMemcpyToSymbol(g_pixel_ray, pixel_rays, sizeof(float) * kPixels * 3);
     if (e != cudaSuccess) return e;
     return cudaMemcpyToSymbol(g_pool_ray, pool_rays, sizeof(float) * 80 * 3);
+}
+
+cudaError_t launch_world_mirror(const SimArgs& a, cudaStream_t s) {
+    k_world_mirror<<<blocks_for(a.n, 128), 128, 0, s>>>(a);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s) {

@@ -257,6 +257,14 @@ __device__ __forceinline__ bool clean_env(const mdn_sim_config& c, uint32_t gid)
     return c.eval == 0 && ((c.family == 12 || c.family == 13) && gid % 2 == 0);
 }
 
+// Copy env i's obstacle block into the structure-of-arrays mirror.
+__device__ __forceinline__ void mirror_world(const SimArgs& a, uint32_t i) {
+    const mdn_world& w = a.worlds[i];
+    const float* words = reinterpret_cast<const float*>(w.obstacles);
+    for (int k = 0; k < 160; k++) a.world_soa[size_t(k) * a.n + i] = words[k];
+    a.world_soa[size_t(160) * a.n + i] = __uint_as_float(w.count);
+}
+
 // sim_reset_one (sim.metal:55-94) for one environment, except the 8x320 range
 // ring refill, which the caller performs cooperatively (returns true when the
 // ring must be refilled with 12 m).
@@ -311,6 +319,7 @@ __device__ bool reset_env(const SimArgs& a, uint32_t i, bool first) {
         float* pose = a.poses + size_t(i) * kFrames * 12;
         for (int j = 0; j < kFrames * 12; j++) pose[j] = 0;
     }
+    mirror_world(a, i);
     return true;
 }
 
