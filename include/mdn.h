@@ -261,6 +261,27 @@ int mdn_ppo_checkpoint_save(mdn_ppo* ppo, const char* path, uint32_t family, uin
 int mdn_ppo_checkpoint_load(mdn_ppo* ppo, const char* path, uint32_t family, uint32_t horizon,
                             uint32_t n, uint32_t seed);
 
+/* GAE + advantage normalisation of one rollout that allocates no memory.
+ * No counterpart in the reference. For callers that cannot call cudaMalloc:
+ * code whose device memory is all owned by its own pool (a framework's caching
+ * allocator), or code that must not allocate on its hot path (inside a stream
+ * capture, or a fixed-latency training/evaluation loop). It computes what the
+ * first phase of mdn_ppo_rollout_update computes, from device pointers in the
+ * reference's T-major [horizon][envs] layout: rewards, values, next_values
+ * (float), terminated, truncated (uint8) in; advantages (normalised) and
+ * returns (float) out. gamma/lambda as ppo.hpp:108-126 (0.99/0.95 in the
+ * trainer). `stream` is a cudaStream_t or NULL for the default stream.
+ * Its scratch is a fixed device array inside libmdn (33 KB on every GPU that
+ * loads the library, held until exit): envs <= 1,048,576 (4,096 blocks of
+ * 256); larger sizes return MDN_ERR_INVALID. The first call on a device looks
+ * up that array's address, so make it before any stream capture. All calls
+ * share the array: calls that overlap on the GPU (different streams, or
+ * different host threads) race and must be serialised by the caller. */
+int mdn_gae_normalize_static(const float* rewards, const float* values, const float* next_values,
+                             const uint8_t* terminated, const uint8_t* truncated, float* advantages,
+                             float* returns, uint32_t horizon, uint32_t envs, float gamma, float lambda,
+                             void* stream);
+
 /* ---- multi-GPU (no reference counterpart: the reference is one Apple GPU) */
 /* Fill a 128-byte NCCL unique id (rank 0) to share through any host channel. */
 int mdn_comm_unique_id(uint8_t id[128]);

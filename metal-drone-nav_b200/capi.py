@@ -75,6 +75,8 @@ SIGNATURES = {
     "mdn_ppo_last_update_ms": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float)]),
     "mdn_ppo_checkpoint_save": (ctypes.c_int, [_P, ctypes.c_char_p, _U, _U, _U]),
     "mdn_ppo_checkpoint_load": (ctypes.c_int, [_P, ctypes.c_char_p, _U, _U, _U, _U]),
+    "mdn_gae_normalize_static": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _U, _U, ctypes.c_float,
+                                                 ctypes.c_float, _P]),
     "mdn_comm_unique_id": (ctypes.c_int, [_P]),
     "mdn_comm_init": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, _P]),
     "mdn_comm_destroy": (ctypes.c_int, [_P]),

@@ -14,6 +14,10 @@
 // All reductions use a fixed tree/order: results do not depend on scheduling.
 #include <cuda_runtime.h>
 
+#include <mutex>
+#include <string>
+
+#include "host_common.h"
 #include "mdn_device.cuh"
 #include "ppo_args.h"
 
@@ -557,4 +561,83 @@ cudaError_t launch_metrics_mean(const PpoArgs& p, uint32_t updates, cudaStream_t
     return cudaGetLastError();
 }
 
+// ------------------------------------------------- allocation-free entry
+// Scratch of mdn_gae_normalize_static: one fp64 partial sum per 256-env block,
+// the two fp64 totals and the two float statistics. A fixed file-scope device
+// array, so the entry point never allocates. Every kernel writes the slots it
+// later reads before reading them (partials by block, totals, statistics), so
+// nothing has to start at zero; leftovers of an earlier call are overwritten.
+constexpr uint32_t kStaticGaeMaxBlocks = 4096;  // envs <= 4096 * 256
+struct StaticGaeScratch {
+    double partials[kStaticGaeMaxBlocks];
+    double stats[2];
+    float values[2];
+};
+static __device__ __align__(256) StaticGaeScratch g_static_gae_scratch;
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+StaticGaeScratch* g_static_ptr[kMaxDevices] = {};
+int g_static_sms[kMaxDevices] = {};
+
+}  // namespace
 }  // namespace mdn
+
+extern "C" int mdn_gae_normalize_static(const float* rewards, const float* values, const float* next_values,
+                                        const uint8_t* terminated, const uint8_t* truncated, float* advantages,
+                                        float* returns, uint32_t horizon, uint32_t envs, float gamma, float lambda,
+                                        void* stream) {
+    using namespace mdn;
+    return guarded([&] {
+        require(rewards && values && next_values && terminated && truncated && advantages && returns, MDN_ERR_INVALID,
+                "mdn_gae_normalize_static: null pointer");
+        require(horizon >= 1 && envs >= 1, MDN_ERR_INVALID, "mdn_gae_normalize_static: empty rollout");
+        require(gae_blocks(envs) <= kStaticGaeMaxBlocks, MDN_ERR_INVALID,
+                "mdn_gae_normalize_static: envs exceeds the fixed scratch limit of 1,048,576 (4,096 blocks of 256)");
+        int dev = 0;
+        cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+        require(dev >= 0 && dev < kMaxDevices, MDN_ERR_INVALID, "mdn_gae_normalize_static: device index too large");
+        StaticGaeScratch* scratch;
+        int sms;
+        {
+            // Set-up, once per device with that device current: the host-side
+            // name of the array is not a device address; ask the runtime.
+            std::lock_guard<std::mutex> lock(g_static_mu);
+            if (!g_static_ptr[dev]) {
+                void* ptr = nullptr;
+                cuda_check(cudaGetSymbolAddress(&ptr, g_static_gae_scratch), "cudaGetSymbolAddress(scratch)");
+                int count = 0;
+                cuda_check(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev), "SM count");
+                g_static_sms[dev] = count;
+                g_static_ptr[dev] = static_cast<StaticGaeScratch*>(ptr);
+            }
+            scratch = g_static_ptr[dev];
+            sms = g_static_sms[dev];
+        }
+        PpoArgs p{};
+        p.n = envs;
+        p.horizon = horizon;
+        p.global_rows = uint64_t(envs) * horizon;
+        p.gamma = gamma;
+        p.lambda = lambda;
+        p.rewards = rewards;
+        p.values = values;
+        p.next_values = next_values;
+        p.terminated = terminated;
+        p.truncated = truncated;
+        p.advantages = advantages;
+        p.returns = returns;
+        p.stat_partials = scratch->partials;
+        p.stats = scratch->stats;
+        p.stat_values = scratch->values;
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        cuda_check(launch_gae_sum(p, s), "gae");
+        cuda_check(launch_adv_stats(p, 0, s), "advantage sum");
+        cuda_check(launch_adv_finalize(p, 0, s), "advantage mean");
+        cuda_check(launch_adv_sq(p, s), "advantage variance");
+        cuda_check(launch_adv_stats(p, 1, s), "advantage variance sum");
+        cuda_check(launch_adv_finalize(p, 1, s), "advantage scale");
+        cuda_check(launch_adv_apply(p, sms, s), "advantage normalise");
+    });
+}

@@ -1,0 +1,54 @@
+"""mdn_gae_normalize_static: the allocation-free GAE + advantage normalisation.
+
+Some callers cannot call cudaMalloc on their hot path: a framework whose caching
+allocator owns all device memory, or a loop that runs inside a stream capture or
+under a fixed latency budget. For them libmdn offers this one entry point, whose
+scratch is a fixed array compiled into the library. This test calls it through
+the C-ABI on a real rollout, twice in a row (the shared scratch keeps the first
+call's contents), and checks each result against the existing entry point,
+mdn_ppo_rollout_update, whose first phase computes the same advantages and
+returns from the same buffers. Tolerance: bit-exact, as the GPU GAE tests use.
+It also checks the size limit is refused with an error, not a fault.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import load_package
+
+pytestmark = pytest.mark.gpu
+
+
+def test_static_gae_matches_trainer():
+    import torch
+
+    pkg = load_package()
+    lib = pkg.lib()
+    dev = pkg.Device(0)
+    n, T = 512, 32
+    cfg = pkg.layouts.default_config(n=n, family=17, seed=3)
+    sim = pkg.Sim(dev, cfg, T)
+    tr = pkg.PPOTrainer(sim, epochs=1, minibatch=n * T)
+    try:
+        inputs = [sim.buffer(name)[0] for name in ("rewards", "values", "next_values", "terminated", "truncated")]
+        for call in range(2):
+            sim.collect()
+            dev.finish()
+            adv = torch.empty(n * T, dtype=torch.float32, device="cuda")
+            ret = torch.empty(n * T, dtype=torch.float32, device="cuda")
+            status = lib.mdn_gae_normalize_static(*[ctypes.c_void_p(p) for p in inputs], ctypes.c_void_p(adv.data_ptr()),
+                                                  ctypes.c_void_p(ret.data_ptr()), T, n, 0.99, 0.95, None)
+            assert status == 0, lib.mdn_last_error()
+            torch.cuda.synchronize()
+            tr.rollout_update(call)
+            dev.finish()
+            assert np.array_equal(adv.cpu().numpy(), sim.download("advantages")), f"call {call}: advantages"
+            assert np.array_equal(ret.cpu().numpy(), sim.download("returns")), f"call {call}: returns"
+        too_many = 4096 * 256 + 1
+        status = lib.mdn_gae_normalize_static(*[ctypes.c_void_p(p) for p in inputs], ctypes.c_void_p(adv.data_ptr()),
+                                              ctypes.c_void_p(ret.data_ptr()), 1, too_many, 0.99, 0.95, None)
+        assert status == 1 and b"scratch limit" in lib.mdn_last_error()
+    finally:
+        tr.close()
+        sim.close()
