@@ -87,7 +87,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
@@ -249,14 +249,14 @@ def cpu_reference_sample(layouts, n, policy_steps, family, warmup=0, threads=Non
                       f"train_rollout over 1024x4 rows (2 epochs x 256-row chunks)"}
 
 
-def run_reference_arm(args, dist):
+def run_reference_arm(args, dist, out_fd):
     if dist.rank != 0:
         return 0
     layouts = package().layouts
     envs = args.envs
     om = oracle_module()
     if om.load_ref() is None:
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
+        emit({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}, out_fd)
         return 0
     # warm-up and timed steps: each step = one policy step over all environments
     samples = []
@@ -277,7 +277,7 @@ def run_reference_arm(args, dist):
                          "sample": s["sample"] + f" ({args.warmup} untimed warm-up steps)"},
         "e2e": {"value": value, "unit": "env-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line))
+    emit(line, out_fd)
     return 0
 
 
@@ -291,11 +291,22 @@ def workload_config(args):
 
 
 # ------------------------------------------------------------------ main
+def emit(line, fd):
+    """Write the one JSON result line to the saved stdout."""
+    os.write(fd, (json.dumps(line) + "\n").encode())
+
+
 def main():
+    # Libraries (NCCL's version banner, warnings) may print to fd 1; the driver
+    # reads exactly one JSON line from stdout. Keep the real stdout for that line
+    # and send everything else to stderr.
+    out_fd = os.dup(1)
+    sys.stdout.flush()
+    os.dup2(2, 1)
     args = parse()
     dist = Dist()
     if args.impl == "reference":
-        return run_reference_arm(args, dist)
+        return run_reference_arm(args, dist, out_fd)
     dist.init()
     pkg = package()
     L = pkg.layouts
@@ -421,7 +432,7 @@ def main():
                                     "ppo_update_ms_extrapolated": s["per_row_epoch_s"] * args.envs * args.horizon
                                     * args.epochs * 1e3}
     if dist.rank == 0:
-        print(json.dumps(line))
+        emit(line, out_fd)
     trainer.close()
     sim.close()
     dev.close()

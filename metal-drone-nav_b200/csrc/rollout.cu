@@ -570,9 +570,9 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
 // termination flags, bootstrap value, episode statistics and in-kernel reset
 // (sim.metal:272-332, cpu_reference.hpp:460-513). Also records the id of the
 // obstacle nearest at the step's closest approach.
-constexpr int kAdvanceThreads = 128;
+constexpr int kAdvanceThreads = 64;
 
-__global__ void __launch_bounds__(kAdvanceThreads, 4) k_advance(SimArgs a) {
+__global__ void __launch_bounds__(kAdvanceThreads, 8) k_advance(SimArgs a) {
     __shared__ float raptor_w[2084];
     __shared__ float critic_w[kCriticParams];
     __shared__ mdn_physics_params params;
