@@ -939,6 +939,7 @@ void o_adam_update(float* params, const float* grad, float* m, float* v, size_t 
 struct o_sim {
     mdn_sim_config cfg;
     uint32_t horizon;
+    uint32_t env_base; /* global id of local env 0 (a rank's shard) */
     mdn_raptor_weights raptor;
     mdn_physics_params physics;
     float room[6];
@@ -968,7 +969,12 @@ static void* zalloc(size_t bytes) { return calloc(bytes ? bytes : 1, 1); }
 
 o_sim* o_sim_create(const mdn_sim_config* cfg, uint32_t horizon, const mdn_raptor_weights* raptor,
                     const mdn_physics_params* physics, const float* room) {
+    return o_sim_create_shard(cfg, horizon, raptor, physics, room, 0);
+}
+o_sim* o_sim_create_shard(const mdn_sim_config* cfg, uint32_t horizon, const mdn_raptor_weights* raptor,
+                          const mdn_physics_params* physics, const float* room, uint32_t env_base) {
     o_sim* s = (o_sim*)zalloc(sizeof(o_sim));
+    s->env_base = env_base;
     s->cfg = *cfg;
     s->horizon = horizon;
     s->raptor = *raptor;
@@ -1073,10 +1079,11 @@ static void reset_one(o_sim* s, uint32_t n, int first) {
     mdn_physics_state* st = &s->states[n];
     mdn_sim_run* run = &s->runs[n];
     mdn_world* w = &s->worlds[n];
-    uint32_t rng = first ? (c->seed + n * 747796405u + 2891336453u) : run->rng;
+    const uint32_t gid = s->env_base + n;
+    uint32_t rng = first ? (c->seed + gid * 747796405u + 2891336453u) : run->rng;
     const uint32_t family = o_wtraining_family(c->family, &rng);
     o_wgenerate(w, o_wrng(&rng), family, c->distance);
-    w->wind[0] = clean_env(c, n) ? 0.0f : c->wind;
+    w->wind[0] = clean_env(c, gid) ? 0.0f : c->wind;
     w->wind[1] = 0;
     w->wind[2] = 0;
     for (int j = 0; j < 3; j++) {
@@ -1136,7 +1143,8 @@ static void depth_env(o_sim* s, uint32_t n) {
     float* pose = s->poses + ((size_t)n * NFRAMES + frame) * 12;
     pose[0] = origin[0]; pose[1] = origin[1]; pose[2] = origin[2];
     for (int j = 0; j < 9; j++) pose[3 + j] = r[j];
-    const float noise = clean_env(c, n) ? 0.0f : c->depth_noise, dropout = clean_env(c, n) ? 0.0f : c->dropout;
+    const uint32_t gid = s->env_base + n;
+    const float noise = clean_env(c, gid) ? 0.0f : c->depth_noise, dropout = clean_env(c, gid) ? 0.0f : c->dropout;
     for (uint32_t k = 0; k < NPIX; k++) {
         const float* ray = s->pixel_rays + 3 * k;
         const float d[3] = {r[0] * ray[0] + r[1] * ray[1] + r[2] * ray[2], r[3] * ray[0] + r[4] * ray[1] + r[5] * ray[2],
@@ -1186,7 +1194,7 @@ static void observe_env(o_sim* s, uint32_t t, uint32_t n) {
     const mdn_world* w = &s->worlds[n];
     float r[9];
     rotation(st->orientation_wxyz, r);
-    const uint32_t delay = clean_env(c, n) ? 0 : c->sensor_delay;
+    const uint32_t delay = clean_env(c, s->env_base + n) ? 0 : c->sensor_delay;
     const uint32_t available = run->steps / c->sensor_period;
     const uint32_t frame = available > delay ? available - delay : 0;
     const uint32_t prev = frame > 0 ? frame - 1 : 0;
@@ -1292,7 +1300,7 @@ static void act_env(o_sim* s, uint32_t t, uint32_t n) {
     lp = gaussian_log_prob(s->actions + row * ACT, mean, log_std);
     s->logp[row] = lp;
     run->rng = rng;
-    const uint32_t delay = clean_env(c, n) ? 0 : c->command_delay;
+    const uint32_t delay = clean_env(c, s->env_base + n) ? 0 : c->command_delay;
     const uint32_t applied = run->steps > delay ? run->steps - delay : 0;
     for (uint32_t j = 0; j < ACT; j++)
         run->previous_nav[j] = run->steps < delay ? 0.0f : s->commands[((size_t)n * NFRAMES + applied % NFRAMES) * ACT + j];
@@ -1541,4 +1549,42 @@ void o_sim_train_rollout(o_sim* s, uint32_t mb, uint32_t epochs, const uint32_t*
     out[2] = entropy_sum * scale;
     out[3] = ratio_sum * scale;
     free(ah); free(am); free(ch); free(cv); free(dm); free(dls); free(dv); free(adelta); free(cdelta); free(ag); free(cg);
+}
+
+/* Raw gradient [actor | critic] of the clipped-PPO objective over the listed
+ * rollout rows, each row's loss scaled by 1/batch (ppo.hpp:144-181 with
+ * cpu_reference.hpp:515-551 as the per-row sums). Used to check the sharded
+ * update: a global minibatch is the union of the ranks' chunks. */
+void o_sim_rows_grad(o_sim* s, const uint32_t* rows, uint32_t count, float batch, float* grad) {
+    memset(grad, 0, (A_P + C_P) * 4);
+    float* ag = grad;
+    float* cg = grad + A_P;
+    float h[HID], ch[HID], mean[ACT];
+    for (uint32_t k = 0; k < count; k++) {
+        const uint32_t r = rows[k];
+        const float* ob = s->obs + (size_t)r * AOBS;
+        const float* co = s->co + (size_t)r * COBS;
+        actor_forward_row(s->actor, ob, h, mean);
+        const float v = critic_forward_row(s->critic, co, ch);
+        float dm[ACT], dls[ACT], dv, l[4];
+        o_sample_loss_and_grad(s->actions + (size_t)r * ACT, mean, s->actor + A_LS, s->logp[r], v, s->adv[r], s->ret[r],
+                               batch, 0.2f, 0.5f, s->cfg.entropy_coef, dm, dls, &dv, l);
+        for (uint32_t j = 0; j < HID; j++) {
+            float acc = 0.0f;
+            for (uint32_t a = 0; a < ACT; a++) acc += dm[a] * s->actor[A_W2 + a * HID + j];
+            const float d = acc * (1.0f - h[j] * h[j]);
+            for (uint32_t i = 0; i < AOBS; i++) ag[j * AOBS + i] += d * ob[i];
+            ag[A_B1 + j] += d;
+            const float cd = dv * s->critic[C_W2 + j] * (1.0f - ch[j] * ch[j]);
+            for (uint32_t i = 0; i < COBS; i++) cg[j * COBS + i] += cd * co[i];
+            cg[C_B1 + j] += cd;
+            cg[C_W2 + j] += dv * ch[j];
+        }
+        for (uint32_t a = 0; a < ACT; a++) {
+            for (uint32_t j = 0; j < HID; j++) ag[A_W2 + a * HID + j] += dm[a] * h[j];
+            ag[A_B2 + a] += dm[a];
+            ag[A_LS + a] += dls[a];
+        }
+        cg[C_B2] += dv;
+    }
 }

@@ -63,6 +63,10 @@ float o_pow_correction(float beta, uint64_t step);
 typedef struct o_sim o_sim;
 o_sim* o_sim_create(const mdn_sim_config* cfg, uint32_t horizon, const mdn_raptor_weights* raptor,
                     const mdn_physics_params* physics, const float* room);
+/* A rank's shard: local env i is global env env_base + i (seeds, clean-env parity). */
+o_sim* o_sim_create_shard(const mdn_sim_config* cfg, uint32_t horizon, const mdn_raptor_weights* raptor,
+                          const mdn_physics_params* physics, const float* room, uint32_t env_base);
+void o_sim_rows_grad(o_sim* s, const uint32_t* rows, uint32_t count, float batch, float* grad);
 void o_sim_destroy(o_sim* s);
 void* o_sim_buffer(o_sim* s, int id, size_t* bytes);
 void o_sim_reset(o_sim* s);

@@ -69,6 +69,8 @@ def load_oracle():
     d("o_adam_update", None, _P, _P, _P, _P, ctypes.c_size_t, _F, _F, _F)
     d("o_pow_correction", _F, _F, ctypes.c_uint64)
     d("o_sim_create", _P, _P, _U, _P, _P, _P)
+    d("o_sim_create_shard", _P, _P, _U, _P, _P, _P, _U)
+    d("o_sim_rows_grad", None, _P, _P, _U, _F, _P)
     d("o_sim_destroy", None, _P)
     d("o_sim_buffer", _P, _P, ctypes.c_int, ctypes.POINTER(ctypes.c_size_t))
     d("o_sim_reset", None, _P)
@@ -147,7 +149,7 @@ class _Buffers:
 class OracleSim(_Buffers):
     """The C restatement driven like the product Sim (same buffer ids)."""
 
-    def __init__(self, layouts, cfg, horizon, raptor, physics=None, room=None, lib=None):
+    def __init__(self, layouts, cfg, horizon, raptor, physics=None, room=None, lib=None, env_base=0):
         self.layouts = layouts
         self.lib = lib or load_oracle()
         self.cfg = np.array(cfg, layouts.CONFIG)
@@ -158,7 +160,8 @@ class OracleSim(_Buffers):
         self.raptor = np.array(raptor, layouts.RAPTOR)
         self.room = None if room is None else np.asarray(room, np.float32)
         self.horizon = horizon
-        self.h = self.lib.o_sim_create(ptr(self.cfg), horizon, ptr(self.raptor), ptr(self.physics), ptr(self.room))
+        self.h = self.lib.o_sim_create_shard(ptr(self.cfg), horizon, ptr(self.raptor), ptr(self.physics),
+                                             ptr(self.room), env_base)
 
     def __del__(self):
         if getattr(self, "h", None):
@@ -189,6 +192,13 @@ class OracleSim(_Buffers):
 
     def gae(self, normalize=True):
         self.lib.o_sim_gae_normalize(self.h, int(normalize))
+
+    def rows_grad(self, rows, batch):
+        """Raw [actor | critic] gradient over explicit rollout rows, loss scale 1/batch."""
+        rows = np.ascontiguousarray(rows, np.uint32)
+        out = np.zeros(self.layouts.ACTOR_PARAMS + self.layouts.CRITIC_PARAMS, np.float32)
+        self.lib.o_sim_rows_grad(self.h, ptr(rows), rows.size, float(batch), ptr(out))
+        return out
 
     def train_rollout(self, minibatch, epochs, order, b1corr, b2corr):
         order = np.ascontiguousarray(order, np.uint32)
