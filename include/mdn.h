@@ -140,6 +140,34 @@ typedef struct mdn_checkpoint_header {
     mdn_sim_config config;
 } mdn_checkpoint_header;
 
+/* NavigationTaskConfig (navigation_tasks.hpp:61-89, 144 bytes): goal-arrival
+ * task curriculum. NavigationTaskControl (:91-94, 148 bytes). */
+typedef struct mdn_task_config {
+    uint32_t family, stage, objective, require_detour, max_generation_attempts, max_nav_steps;
+    float scene_distance_m, difficulty, goal_distance_min_m, goal_distance_max_m;
+    float minimum_endpoint_clearance_m, minimum_witness_clearance_m, goal_radius_m, stable_speed_mps;
+    float stable_hold_s, nav_period_s, initial_speed_min_mps, initial_speed_max_mps;
+    float progress_reward_per_m, time_cost_per_s, contact_penalty, stable_arrival_bonus, command_smoothness_weight;
+    float start_min_xyz[3], start_max_xyz[3], goal_min_xyz[3], goal_max_xyz[3];
+    uint32_t generation_version;
+} mdn_task_config;
+typedef struct mdn_task_control {
+    uint32_t enabled;
+    mdn_task_config config;
+} mdn_task_control;
+
+/* NavigationTaskState (navigation_tasks.hpp:147-177, 192 bytes), one per env. */
+typedef struct mdn_task_state {
+    uint32_t generation_status, valid, generation_attempts, family, stage, objective, max_nav_steps, step_count;
+    uint32_t stable_ticks, was_inside_goal, waypoint_event_latched, terminal;
+    float start_position[3], start_yaw_rad, start_velocity_world[3], goal_position[3];
+    float initial_distance_m, previous_distance_m, difficulty, start_clearance_m, goal_clearance_m;
+    float direct_segment_clearance_m, witness_min_clearance_m, witness_length_m, stable_time_s;
+    float last_executed_world_command[4];
+    uint32_t witness_point_count;
+    float witness_points[4][3];
+} mdn_task_state;
+
 /* Buffer ids for mdn_sim_buffer / download / upload. They name the public
  * members of the reference Sim (main.mm:517-518). */
 enum {
@@ -166,7 +194,8 @@ enum {
     MDN_BUF_PHYSICS = 20,     /* mdn_physics_params                           */
     MDN_BUF_CONTACT_ID = 21,  /* int32[T][n] nearest-obstacle id at the step's
                                  closest approach (-1 = room walls)           */
-    MDN_BUF_COUNT = 22
+    MDN_BUF_TASK_STATES = 22, /* mdn_task_state[n] (task_states, main.mm:535) */
+    MDN_BUF_COUNT = 23
 };
 
 /* ---- library / device --------------------------------------------------- */
@@ -217,6 +246,19 @@ int mdn_sim_upload(mdn_sim* sim, int id, const void* host, size_t offset, size_t
  * min_clearance, peak_speed. */
 int mdn_sim_report(mdn_sim* sim, double out[10]);
 int mdn_sim_dims(mdn_sim* sim, uint32_t* n, uint32_t* horizon, uint32_t* actor_params, uint32_t* critic_params);
+/* navigation_task_default_config (navigation_tasks.hpp:97-142) followed by the
+ * overrides of navigation_training::task_settings (navigation_training.hpp:7-14).
+ * Returns MDN_ERR_INVALID for an unsupported stage/family/difficulty. */
+int mdn_task_settings(uint32_t stage, uint32_t family, float difficulty, mdn_task_config* out);
+/* navigation_training::configure (navigation_training.hpp:16-25): enable the
+ * goal-arrival task generator and reward for every env and reset the sim.
+ * domain_amplitude must be 0 in this build (per-episode plant randomisation,
+ * physics_domain.hpp, is not implemented); the task's nav period must equal
+ * substeps x 10 ms. Passing control->enabled == 0 returns to legacy episodes. */
+int mdn_sim_configure_tasks(mdn_sim* sim, const mdn_task_control* control, float domain_amplitude);
+/* navigation_training::validate_rollout (navigation_training.hpp:27-35):
+ * MDN_ERR_STATE naming the first env whose task generation was rejected. */
+int mdn_sim_validate_tasks(mdn_sim* sim);
 /* Device time of the last mdn_sim_collect (CUDA events on the sim stream). */
 int mdn_sim_last_collect_ms(mdn_sim* sim, float* ms);
 

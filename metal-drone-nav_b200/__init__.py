@@ -10,7 +10,7 @@ import pathlib
 import subprocess
 
 from . import layouts  # noqa: F401
-from .capi import Device, MdnError, PPOTrainer, Sim, default_raptor, lib  # noqa: F401
+from .capi import Device, MdnError, PPOTrainer, Sim, default_raptor, lib, task_control, task_settings  # noqa: F401
 
 PACKAGE_DIR = pathlib.Path(__file__).resolve().parent
 

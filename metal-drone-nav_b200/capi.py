@@ -58,6 +58,9 @@ SIGNATURES = {
     "mdn_sim_upload": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_size_t, ctypes.c_size_t]),
     "mdn_sim_report": (ctypes.c_int, [_P, _P]),
     "mdn_sim_dims": (ctypes.c_int, [_P, _P, _P, _P, _P]),
+    "mdn_task_settings": (ctypes.c_int, [_U, _U, ctypes.c_float, _P]),
+    "mdn_sim_configure_tasks": (ctypes.c_int, [_P, _P, ctypes.c_float]),
+    "mdn_sim_validate_tasks": (ctypes.c_int, [_P]),
     "mdn_sim_last_collect_ms": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float)]),
     "mdn_sim_profile_step": (ctypes.c_int, [_P, _U, _P]),
     "mdn_launch_counts": (ctypes.c_int, [_P, _P, ctypes.POINTER(_U), ctypes.POINTER(_U)]),
@@ -114,6 +117,21 @@ def minibatch_order(rows, minibatch, epochs, rollout_index):
     out = np.zeros(chunks * epochs, np.uint32)
     check(lib().mdn_minibatch_order(rows, minibatch, epochs, rollout_index, _ptr(out), out.size))
     return out
+
+
+def task_settings(stage, family, difficulty=0.5):
+    """navigation_training::task_settings: a ready task config (mdn_task_settings)."""
+    c = np.zeros((), layouts.TASK_CONFIG)
+    check(lib().mdn_task_settings(stage, family, difficulty, _ptr(c)))
+    return c
+
+
+def task_control(stage, family, difficulty=0.5):
+    """navigation_training::task_settings as an enabled task control."""
+    ctl = np.zeros((), layouts.TASK_CONTROL)
+    ctl["enabled"] = 1
+    ctl["config"] = task_settings(stage, family, difficulty)
+    return ctl
 
 
 def default_raptor():
@@ -229,6 +247,15 @@ class Sim:
     def upload(self, name, array, offset=0):
         a = np.ascontiguousarray(array)
         check(lib().mdn_sim_upload(self.h, layouts.BUF[name], _ptr(a), offset, a.nbytes))
+
+    def configure_tasks(self, control, domain_amplitude=0.0):
+        """navigation_training::configure: enable goal-arrival tasks and reset."""
+        ctl = np.array(control, layouts.TASK_CONTROL)
+        check(lib().mdn_sim_configure_tasks(self.h, _ptr(ctl), domain_amplitude))
+
+    def validate_tasks(self):
+        """navigation_training::validate_rollout."""
+        check(lib().mdn_sim_validate_tasks(self.h))
 
     def report(self):
         out = np.zeros(10, np.float64)

@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <fstream>
 #include <memory>
+#include <string>
 
 #include "host_common.h"
 
@@ -216,6 +217,9 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
     a.terminated = static_cast<uint8_t*>(buf[MDN_BUF_TERMINATED]);
     a.truncated = static_cast<uint8_t*>(buf[MDN_BUF_TRUNCATED]);
     a.contact = static_cast<int32_t*>(buf[MDN_BUF_CONTACT_ID]);
+    a.task_ctl = task_ctl;
+    a.tasks = static_cast<mdn_task_state*>(buf[MDN_BUF_TASK_STATES]);
+    a.task_config_ok = task_config_ok;
     return a;
 }
 
@@ -232,9 +236,7 @@ void validate_config(const mdn_sim_config& c) {
     // main.mm:727 (sim_evaluate): the 8-deep rings hold <=6 sensor frames and <=7 command steps.
     require(c.sensor_delay <= 6 && c.command_delay <= 7, MDN_ERR_INVALID,
             "delay rings support <=6 sensor frames and <=7 command steps");
-    require(c.mode == 0 || c.mode == 1 || c.mode == 20, MDN_ERR_INVALID,
-            "SimConfig.mode: this build implements the training modes 0 (stochastic policy) and 1 "
-            "(random actions) and mode 20's tight arrival radius");
+    require(c.mode <= 22, MDN_ERR_INVALID, "SimConfig.mode: sim_act defines modes 0..22");
     require(c.geometry_memory == 0, MDN_ERR_INVALID, "SimConfig.geometry_memory=1 is not supported by this build");
     require(std::isfinite(c.speed) && std::isfinite(c.distance), MDN_ERR_INVALID, "SimConfig speed/distance");
 }
@@ -323,6 +325,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         b[MDN_BUF_TRUNCATED] = rows;
         b[MDN_BUF_RAPTOR] = sizeof(mdn_raptor_weights);
         b[MDN_BUF_PHYSICS] = sizeof(mdn_physics_params);
+        b[MDN_BUF_TASK_STATES] = n * sizeof(mdn_task_state);
         for (int id = 0; id < MDN_BUF_COUNT; id++) {
             const cudaError_t e = cudaMalloc(&sim->buf[id], std::max<size_t>(b[id], 16));
             if (e != cudaSuccess) {
@@ -355,7 +358,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
                    "upload physics");
         for (int id : {MDN_BUF_OBS, MDN_BUF_CO, MDN_BUF_ACTIONS, MDN_BUF_LOGP, MDN_BUF_VALUES, MDN_BUF_REWARDS,
                        MDN_BUF_NEXT_VALUES, MDN_BUF_TERMINATED, MDN_BUF_TRUNCATED, MDN_BUF_ADVANTAGES, MDN_BUF_RETURNS,
-                       MDN_BUF_CONTACT_ID})
+                       MDN_BUF_CONTACT_ID, MDN_BUF_TASK_STATES})
             cuda_check(cudaMemsetAsync(sim->buf[id], 0, b[id], sim->stream), "clear rollout buffers");
         // Persistent act kernel: enough CTAs to fill every SM twice.
         sim->act_grid = int(std::min<size_t>((n + 31) / 32, size_t(dev->sm_count) * 2));
@@ -547,5 +550,147 @@ extern "C" int mdn_device_fp32_peak(mdn_device* dev, double* tflops) {
         require(dev && tflops, MDN_ERR_INVALID, "null argument");
         use_device(dev);
         cuda_check(fp32_peak(dev->sm_count, tflops), "fp32 peak");
+    });
+}
+
+// navigation_task_default_config (navigation_tasks.hpp:97-142) with the
+// overrides of navigation_training::task_settings (navigation_training.hpp:7-14).
+extern "C" int mdn_task_settings(uint32_t stage, uint32_t family, float difficulty, mdn_task_config* out) {
+    return guarded([&] {
+        require(out != nullptr, MDN_ERR_INVALID, "null out");
+        require(stage <= 2u && std::isfinite(difficulty) && difficulty >= 0.0f && difficulty <= 1.0f, MDN_ERR_INVALID,
+                "unsupported task stage/difficulty");
+        if (stage == 0u || stage == 1u) require(family == 0u, MDN_ERR_INVALID, "open/hold stages use family 0");
+        else
+            require(family == 1u || family == 2u || family == 4u || family == 5u || family == 12u, MDN_ERR_INVALID,
+                    "clutter stage supports families 1, 2, 4, 5, 12");
+        mdn_task_config c{};
+        c.generation_version = 1u;
+        c.family = family;
+        c.stage = stage;
+        c.objective = 1u;  // final hold
+        c.require_detour = 0u;
+        c.max_generation_attempts = 64u;
+        c.max_nav_steps = 400u;
+        c.scene_distance_m = 8.0f;
+        c.difficulty = difficulty;
+        c.minimum_endpoint_clearance_m = 0.30f;
+        c.minimum_witness_clearance_m = 0.02f;
+        c.goal_radius_m = 0.35f;
+        c.stable_speed_mps = 0.50f;
+        c.stable_hold_s = 0.20f;
+        c.nav_period_s = 0.05f;
+        c.initial_speed_min_mps = 0.0f;
+        c.initial_speed_max_mps = 0.0f;
+        c.progress_reward_per_m = 2.0f;
+        c.time_cost_per_s = 0.20f;
+        c.contact_penalty = 10.0f;
+        c.stable_arrival_bonus = 10.0f;
+        c.command_smoothness_weight = 0.05f;
+        const float start_low[3] = {-1.0f, -2.0f, 0.8f}, start_high[3] = {1.0f, 2.0f, 2.4f};
+        const float goal_low[3] = {-1.2f, -4.0f, 0.5f}, goal_high[3] = {13.2f, 4.0f, 4.5f};
+        for (int a = 0; a < 3; a++) {
+            c.start_min_xyz[a] = start_low[a];
+            c.start_max_xyz[a] = start_high[a];
+            c.goal_min_xyz[a] = goal_low[a];
+            c.goal_max_xyz[a] = goal_high[a];
+        }
+        if (stage == 1u) {
+            c.goal_distance_min_m = 0.8f;
+            c.goal_distance_max_m = 2.0f;
+            for (int a = 0; a < 3; a++) {
+                c.start_min_xyz[a] = goal_low[a];
+                c.start_max_xyz[a] = goal_high[a];
+            }
+        } else if (stage == 2u) {
+            c.goal_distance_min_m = 2.0f;
+            c.goal_distance_max_m = 7.0f;
+        } else {
+            c.goal_distance_min_m = 2.0f;
+            c.goal_distance_max_m = 6.0f;
+        }
+        // navigation_training::task_settings overrides
+        c.time_cost_per_s = .2f;
+        c.command_smoothness_weight = .05f;
+        c.initial_speed_max_mps = stage == 1u ? .5f : 1.0f;
+        *out = c;
+    });
+}
+
+namespace {
+// The configuration checks of navigation_generate_task
+// (navigation_tasks.hpp:347-379): validity of every field, family 0 for the
+// open/hold stages, the clutter families, and start/goal boxes inside the
+// room by the endpoint clearance.
+bool task_config_ok(const mdn_task_config& c) {
+    using std::isfinite;
+    if (c.generation_version != 1u || c.stage > 2u || c.objective > 1u || c.family > 16u || c.require_detour > 1u ||
+        !isfinite(c.scene_distance_m) || c.scene_distance_m < 3.0f || c.scene_distance_m > 10.0f ||
+        !isfinite(c.difficulty) || c.difficulty < 0.0f || c.difficulty > 1.0f || !isfinite(c.goal_distance_min_m) ||
+        !isfinite(c.goal_distance_max_m) || c.goal_distance_min_m <= c.goal_radius_m ||
+        c.goal_distance_max_m < c.goal_distance_min_m || !isfinite(c.minimum_endpoint_clearance_m) ||
+        c.minimum_endpoint_clearance_m < 0.30f || !isfinite(c.minimum_witness_clearance_m) ||
+        c.minimum_witness_clearance_m < 0.02f || !isfinite(c.goal_radius_m) || c.goal_radius_m <= 0.0f ||
+        !isfinite(c.stable_speed_mps) || c.stable_speed_mps < 0.0f || !isfinite(c.stable_hold_s) ||
+        c.stable_hold_s < 0.0f || !isfinite(c.nav_period_s) || c.nav_period_s <= 0.0f ||
+        !isfinite(c.initial_speed_min_mps) || !isfinite(c.initial_speed_max_mps) || c.initial_speed_min_mps < 0.0f ||
+        c.initial_speed_max_mps < c.initial_speed_min_mps || !isfinite(c.progress_reward_per_m) ||
+        c.progress_reward_per_m < 0.0f || !isfinite(c.time_cost_per_s) || c.time_cost_per_s < 0.0f ||
+        !isfinite(c.contact_penalty) || c.contact_penalty < 0.0f || !isfinite(c.stable_arrival_bonus) ||
+        c.stable_arrival_bonus < 0.0f || !isfinite(c.command_smoothness_weight) || c.command_smoothness_weight < 0.0f ||
+        c.max_nav_steps == 0u || c.max_generation_attempts == 0u)
+        return false;
+    if ((c.stage == 0u || c.stage == 1u) && c.family != 0u) return false;
+    if (c.stage == 2u && !(c.family == 1u || c.family == 2u || c.family == 4u || c.family == 5u || c.family == 12u))
+        return false;
+    for (int axis = 0; axis < 3; axis++) {
+        const float room_min = axis == 0 ? -2.0f : (axis == 1 ? -5.0f : 0.0f);
+        const float room_max = axis == 0 ? 14.0f : 5.0f;
+        const float m = c.minimum_endpoint_clearance_m;
+        if (!isfinite(c.start_min_xyz[axis]) || !isfinite(c.start_max_xyz[axis]) || !isfinite(c.goal_min_xyz[axis]) ||
+            !isfinite(c.goal_max_xyz[axis]) || c.start_min_xyz[axis] >= c.start_max_xyz[axis] ||
+            c.goal_min_xyz[axis] >= c.goal_max_xyz[axis] || c.start_min_xyz[axis] < room_min + m ||
+            c.start_max_xyz[axis] > room_max - m || c.goal_min_xyz[axis] < room_min + m ||
+            c.goal_max_xyz[axis] > room_max - m)
+            return false;
+    }
+    return true;
+}
+}  // namespace
+
+// navigation_training::configure (navigation_training.hpp:16-25): install the
+// task control and reset every environment.
+extern "C" int mdn_sim_configure_tasks(mdn_sim* sim, const mdn_task_control* control, float domain_amplitude) {
+    return guarded([&] {
+        checked(sim);
+        require(control != nullptr, MDN_ERR_INVALID, "null task control");
+        require(std::isfinite(domain_amplitude) && domain_amplitude >= 0.0f && domain_amplitude <= 1.0f,
+                MDN_ERR_INVALID, "domain amplitude must be 0..1");
+        require(domain_amplitude == 0.0f, MDN_ERR_INVALID,
+                "domain amplitude > 0 (per-episode plant randomisation) is not supported by this build");
+        if (control->enabled) {
+            require(std::fabs(control->config.nav_period_s - float(sim->cfg.substeps) * 0.01f) < 1e-6f,
+                    MDN_ERR_INVALID, "task/simulator clock mismatch");
+        }
+        cuda_check(cudaStreamSynchronize(sim->stream), "configure tasks");
+        sim->task_ctl = *control;
+        sim->task_config_ok = task_config_ok(control->config) ? 1u : 0u;
+        sim->release_graphs();  // kernel arguments captured by value
+        cuda_check(launch_reset(sim->args(0), true, sim->stream), "reset");
+    });
+}
+
+// navigation_training::validate_rollout (navigation_training.hpp:27-35).
+extern "C" int mdn_sim_validate_tasks(mdn_sim* sim) {
+    return guarded([&] {
+        checked(sim);
+        std::vector<mdn_task_state> tasks(sim->n);
+        cuda_check(cudaMemcpyAsync(tasks.data(), sim->buf[MDN_BUF_TASK_STATES], sim->bytes[MDN_BUF_TASK_STATES],
+                                   cudaMemcpyDeviceToHost, sim->stream), "download task states");
+        cuda_check(cudaStreamSynchronize(sim->stream), "validate tasks");
+        for (uint32_t env = 0; env < sim->n; env++)
+            require(tasks[env].valid && tasks[env].generation_status == 4u, MDN_ERR_STATE,
+                    "task generation rejected env=" + std::to_string(env) +
+                        " status=" + std::to_string(tasks[env].generation_status));
     });
 }

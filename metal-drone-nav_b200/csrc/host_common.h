@@ -83,6 +83,8 @@ struct mdn_sim {
     std::vector<std::pair<uint32_t, cudaGraphExec_t>> graphs;
     cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
     float last_collect_ms = 0.0f;
+    mdn_task_control task_ctl{};  // goal-arrival tasks, set by mdn_sim_configure_tasks
+    uint32_t task_config_ok = 0;
     mdn::SimArgs args(uint32_t tick) const;
     void release_graphs();
 };

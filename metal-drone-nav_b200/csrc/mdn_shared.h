@@ -59,6 +59,9 @@ struct SimArgs {
     uint8_t* terminated;
     uint8_t* truncated;
     int32_t* contact;
+    mdn_task_control task_ctl;  // goal-arrival tasks (enabled = 0: legacy episodes)
+    mdn_task_state* tasks;
+    uint32_t task_config_ok;  // host-side navigation_generate_task config checks (:347-379) passed
 };
 
 }  // namespace mdn

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include "mdn_device.cuh"
+#include "task.cuh"
 #include "world_gen.cuh"
 
 namespace mdn {
@@ -24,7 +25,7 @@ __device__ float g_pool_ray[80 * 3];        // nav_ray(row, col, 0.75), guidance
 __global__ void k_reset(SimArgs a, int first) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     const bool active = i < a.n;
-    if (active) reset_env(a, i, first != 0);
+    if (active) episode_reset(a, i, first != 0);
     const unsigned mask = __ballot_sync(0xffffffffu, active);
     refill_rings(a, (blockIdx.x * blockDim.x) + (threadIdx.x & ~31u), mask);
 }
@@ -424,6 +425,14 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// Share of the 20 overhead cells whose range exceeds 2.5 m, mapped to the
+// mode-17 blend scale .25 + .75 * share (sim.metal:233, 235-240).
+__device__ __forceinline__ float overhead_scale(const float* ob) {
+    float overhead = 0.0f;
+    for (int k = 0; k < 20; k++) overhead += ob[k] * 12.0f > 2.5f ? 1.0f : 0.0f;
+    return 0.25f + 0.75f * (overhead / 20.0f);
+}
+
 __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
     extern __shared__ float sm[];
     float* w1t = sm;                                  // [184][64]
@@ -520,24 +529,67 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
             if (!(c.eval && run.episodes)) {
                 const size_t row = row0 + lane;
                 a.values[row] = value_mine;
+                const float* ob = my_obs + lane * kActorObs;
+                const float* prior = ob + kActorObs - 3;
+                const uint32_t mode = c.mode;
+                float mean[4] = {mean_mine[0], mean_mine[1], mean_mine[2], mean_mine[3]};
+                // Geometry-prior blends of the evaluation modes 9-21 (sim.metal:233).
+                if (mode >= 9u && mode <= 21u) {
+                    float scale = (mode == 9u || mode == 13u) ? 0.0f
+                                : ((mode == 10u || mode == 14u || mode == 16u) ? 0.25f : (mode == 15u ? 1.0f : 0.5f));
+                    if (mode >= 17u) scale = overhead_scale(ob);
+                    if (mode == 12u) {
+                        float near_ = 12.0f;
+                        for (int k = 0; k < 80; k++) near_ = smin(near_, ob[k] * 12.0f);
+                        scale = clampf((near_ - 0.3f) / 2.0f, 0.2f, 1.0f);
+                    }
+                    for (int j = 0; j < 3; j++) mean[j] = prior[j] + scale * (mean[j] - prior[j]);
+                    mean[3] *= scale;
+                    if (mode == 16u) {
+                        const float yaw = atan2f(ob[161], ob[160]);
+                        const float x = clampf(yaw * 1.5f, -0.85f, 0.85f);
+                        mean[3] += 0.5f * logf((1.0f + x) / (1.0f - x));  // nav_atanh, guidance.hpp:35
+                    }
+                }
+                // Mode 22 trains the deployed mode-17 action map (sim.metal:235-256).
+                const float deployed = mode == 22u ? overhead_scale(ob) : 1.0f;
                 uint32_t rng = run.rng;
                 const uint32_t steps = run.steps;
                 float act[4];
                 float* cmd = a.commands + size_t(i) * kFrames * kActions;
                 for (int j = 0; j < 4; j++) {
-                    act[j] = mean_mine[j] + ((c.mode == 0 || c.mode == 22) ? expf(log_std[j]) * sim_normal(rng) : 0.0f);
-                    if (c.mode == 1) act[j] = sim_normal(rng);
+                    act[j] = mean[j] + ((mode == 0u || mode == 22u) ? expf(log_std[j]) * sim_normal(rng) : 0.0f);
+                    if (mode == 1u) act[j] = sim_normal(rng);
                     a.actions[row * kActions + j] = act[j];
-                    cmd[(steps % kFrames) * kActions + j] = tanhf(act[j]);
+                    float executed = act[j];
+                    if (mode == 22u) executed = j < 3 ? prior[j] + deployed * (act[j] - prior[j]) : deployed * act[j];
+                    cmd[(steps % kFrames) * kActions + j] = tanhf(executed);
                 }
                 float lp = 0.0f;  // gaussian_log_prob, ppo.hpp:95-103
                 for (int j = 0; j < 4; j++) {
                     const float inv_std = expf(-log_std[j]);
-                    const float d = (act[j] - mean_mine[j]) * inv_std;
+                    const float d = (act[j] - mean[j]) * inv_std;
                     lp += -0.5f * (d * d + 2.0f * log_std[j] + kLogTwoPi);
                 }
                 a.logp[row] = lp;
                 run.rng = rng;
+                const mdn_physics_state& st = a.states[i];
+                const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2],
+                                    st.orientation_wxyz[3]};
+                float r[9];
+                rotation(q, r);
+                if (mode == 2u || mode == 3u || mode == 20u) {  // scripted goal pursuit, sim.metal:257-263
+                    const mdn_world& w = a.worlds[i];
+                    float d[3] = {w.goal[0] - st.position[0], w.goal[1] - st.position[1], w.goal[2] - st.position[2]};
+                    const float len = len3(d[0], d[1], d[2]);
+                    const float inv = 1.0f / len, keep = smin(len, c.speed);
+                    for (int j = 0; j < 3; j++) d[j] = d[j] * inv * keep;
+                    float* slot = cmd + (steps % kFrames) * kActions;
+                    slot[0] = (r[0] * d[0] + r[3] * d[1] + r[6] * d[2]) / c.speed;
+                    slot[1] = (r[1] * d[0] + r[4] * d[1] + r[7] * d[2]) / c.speed;
+                    slot[2] = (r[2] * d[0] + r[5] * d[1] + r[8] * d[2]) / c.speed;
+                    slot[3] = 0.0f;
+                }
                 const uint32_t gid = a.env_base + i;
                 const uint32_t delay = clean_env(c, gid) ? 0u : c.command_delay;
                 const uint32_t applied = steps > delay ? steps - delay : 0;
@@ -546,15 +598,17 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
                     pn[j] = steps < delay ? 0.0f : cmd[(applied % kFrames) * kActions + j];
                     run.previous_nav[j] = pn[j];
                 }
-                float r[9];
-                const mdn_physics_state& st = a.states[i];
-                const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2],
-                                    st.orientation_wxyz[3]};
-                rotation(q, r);
                 float v[3] = {pn[0] * c.speed, pn[1] * c.speed, pn[2] * c.speed * (c.velocity_contract == 0 ? 0.5f : 1.0f)};
                 if (c.velocity_contract == 1) {
                     const float scale = smin(1.0f, c.speed / smax(len3(v[0], v[1], v[2]), 1e-8f));
                     for (int j = 0; j < 3; j++) v[j] *= scale;
+                }
+                if (mode == 19u) {  // fixed-speed command, sim.metal:269
+                    const float magnitude = len3(v[0], v[1], v[2]);
+                    if (magnitude > 1e-8f) {
+                        const float scale = c.speed / magnitude;
+                        for (int j = 0; j < 3; j++) v[j] *= scale;
+                    }
                 }
                 for (int j = 0; j < 3; j++) run.desired_velocity[j] = r[j * 3] * v[0] + r[j * 3 + 1] * v[1] + r[j * 3 + 2] * v[2];
                 run.yaw += pn[3] * a.physics->dt * float(c.substeps) * 0.5f;
@@ -679,14 +733,25 @@ __global__ void __launch_bounds__(kAdvanceThreads, 8) k_advance(SimArgs a) {
         run.min_clearance = min_clear;
         run.peak_speed = peak;
         const float after = len3(goal[0] - s[0], goal[1] - s[1], goal[2] - s[2]);
-        const bool success = after < (c.mode == 20 ? .10f : .35f) && !collision;
-        const bool timeout = steps >= c.max_steps;
+        bool success = after < (c.mode == 20 ? .10f : .35f) && !collision;
+        bool timeout = steps >= c.max_steps;
         a.rewards[row] = (before - after) * 2.0f - .01f - c.risk_coef * clampf((0.6f - step_clearance) / 0.6f, 0.0f, 1.0f) +
                          (success ? 10.0f : 0.0f) - (collision ? 10.0f : 0.0f);
-        const bool term = collision || success;
+        bool term = collision || success;
         a.terminated[row] = term;
         a.truncated[row] = timeout && !term;
         a.contact[row] = contact;
+        if (a.task_ctl.enabled) {  // sim.metal:307-317
+            const float executed[4] = {run.desired_velocity[0], run.desired_velocity[1], run.desired_velocity[2],
+                                       run.previous_nav[3] * 0.5f};
+            const TaskStep out = task_step(a.tasks[i], a.task_ctl.config, s, s + 7, executed, collision, timeout);
+            success = out.stable_success != 0u && !collision;
+            timeout = out.timeout != 0u;
+            a.rewards[row] = out.reward;
+            term = collision || success;
+            a.terminated[row] = term;
+            a.truncated[row] = timeout && !term;
+        }
         // Bootstrap value of the post-step critic observation (sim.metal:327).
         {
             float co[kCriticObs];
@@ -736,7 +801,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, 8) k_advance(SimArgs a) {
             run.total_path += path;
             run.total_elapsed += elapsed;
             run.final_progress += 1.0f - after / smax(run.initial_distance, 1.0e-4f);
-            if (!c.eval) refill = reset_env(a, i, false);
+            if (!c.eval) refill = episode_reset(a, i, false);
         }
     }
     const unsigned mask = __ballot_sync(0xffffffffu, refill);

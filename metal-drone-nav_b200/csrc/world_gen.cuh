@@ -319,7 +319,6 @@ __device__ bool reset_env(const SimArgs& a, uint32_t i, bool first) {
         float* pose = a.poses + size_t(i) * kFrames * 12;
         for (int j = 0; j < kFrames * 12; j++) pose[j] = 0;
     }
-    mirror_world(a, i);
     return true;
 }
 

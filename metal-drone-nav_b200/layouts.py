@@ -40,6 +40,26 @@ RAPTOR = np.dtype([
 SHAPE = np.dtype([
     ("actor_obs_dim", "<u4"), ("critic_obs_dim", "<u4"), ("actor_hidden", "<u4"), ("critic_hidden", "<u4"),
     ("flags", "<u4"), ("room_min", "<f4", 3), ("room_max", "<f4", 3)])
+TASK_CONFIG = np.dtype([
+    ("family", "<u4"), ("stage", "<u4"), ("objective", "<u4"), ("require_detour", "<u4"),
+    ("max_generation_attempts", "<u4"), ("max_nav_steps", "<u4"), ("scene_distance_m", "<f4"),
+    ("difficulty", "<f4"), ("goal_distance_min_m", "<f4"), ("goal_distance_max_m", "<f4"),
+    ("minimum_endpoint_clearance_m", "<f4"), ("minimum_witness_clearance_m", "<f4"), ("goal_radius_m", "<f4"),
+    ("stable_speed_mps", "<f4"), ("stable_hold_s", "<f4"), ("nav_period_s", "<f4"), ("initial_speed_min_mps", "<f4"),
+    ("initial_speed_max_mps", "<f4"), ("progress_reward_per_m", "<f4"), ("time_cost_per_s", "<f4"),
+    ("contact_penalty", "<f4"), ("stable_arrival_bonus", "<f4"), ("command_smoothness_weight", "<f4"),
+    ("start_min_xyz", "<f4", 3), ("start_max_xyz", "<f4", 3), ("goal_min_xyz", "<f4", 3), ("goal_max_xyz", "<f4", 3),
+    ("generation_version", "<u4")])
+TASK_CONTROL = np.dtype([("enabled", "<u4"), ("config", TASK_CONFIG)])
+TASK_STATE = np.dtype([
+    ("generation_status", "<u4"), ("valid", "<u4"), ("generation_attempts", "<u4"), ("family", "<u4"),
+    ("stage", "<u4"), ("objective", "<u4"), ("max_nav_steps", "<u4"), ("step_count", "<u4"),
+    ("stable_ticks", "<u4"), ("was_inside_goal", "<u4"), ("waypoint_event_latched", "<u4"), ("terminal", "<u4"),
+    ("start_position", "<f4", 3), ("start_yaw_rad", "<f4"), ("start_velocity_world", "<f4", 3),
+    ("goal_position", "<f4", 3), ("initial_distance_m", "<f4"), ("previous_distance_m", "<f4"), ("difficulty", "<f4"),
+    ("start_clearance_m", "<f4"), ("goal_clearance_m", "<f4"), ("direct_segment_clearance_m", "<f4"),
+    ("witness_min_clearance_m", "<f4"), ("witness_length_m", "<f4"), ("stable_time_s", "<f4"),
+    ("last_executed_world_command", "<f4", 4), ("witness_point_count", "<u4"), ("witness_points", "<f4", (4, 3))])
 CHECKPOINT_HEADER = np.dtype([
     ("magic", "S8"), ("version", "<u4"), ("actor_count", "<u4"), ("critic_count", "<u4"), ("horizon", "<u4"),
     ("n", "<u4"), ("family", "<u4"), ("base_seed", "<u4"), ("completed_rollouts", "<u4"),
@@ -48,17 +68,19 @@ CHECKPOINT_HEADER = np.dtype([
 assert STATE.itemsize == 68 and PARAMS.itemsize == 352 and OBSTACLE.itemsize == 40
 assert WORLD.itemsize == 676 and RUN.itemsize == 184 and CONFIG.itemsize == 84
 assert RAPTOR.itemsize == 8336 and SHAPE.itemsize == 44 and CHECKPOINT_HEADER.itemsize == 136
+assert TASK_CONFIG.itemsize == 144 and TASK_CONTROL.itemsize == 148 and TASK_STATE.itemsize == 192
 
 # Buffer ids (mdn.h MDN_BUF_*) with their element dtype and per-row shape.
 BUF = {
     "states": 0, "runs": 1, "worlds": 2, "sensors": 3, "poses": 4, "commands": 5, "actor": 6, "critic": 7,
     "obs": 8, "co": 9, "actions": 10, "logp": 11, "values": 12, "rewards": 13, "next_values": 14,
     "terminated": 15, "truncated": 16, "advantages": 17, "returns": 18, "raptor": 19, "physics": 20,
-    "contact_id": 21,
+    "contact_id": 21, "task_states": 22,
 }
 BUF_DTYPE = {
     "states": STATE, "runs": RUN, "worlds": WORLD, "raptor": RAPTOR, "physics": PARAMS,
     "terminated": np.dtype(np.uint8), "truncated": np.dtype(np.uint8), "contact_id": np.dtype(np.int32),
+    "task_states": TASK_STATE,
 }
 
 # Fixed PPO parameter offsets for the 184/64/4 actor and 32/64/1 critic (ppo.hpp:35-45).

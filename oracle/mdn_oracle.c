@@ -462,6 +462,345 @@ void o_wgenerate(mdn_world* w, uint32_t seed, uint32_t family, float distance) {
     }
 }
 
+
+/* ------------------------------------------- goal-arrival task contract */
+/* navigation_tasks.hpp:21-48 constants */
+#define NT_STAGE_OPEN 0u
+#define NT_STAGE_HOLD 1u
+#define NT_STAGE_CLUTTER 2u
+#define NT_OBJ_WAYPOINT 0u
+#define NT_OBJ_FINAL_HOLD 1u
+#define NT_INVALID_CONFIG 1u
+#define NT_UNSUPPORTED_DYNAMIC 2u
+#define NT_EXHAUSTED 3u
+#define NT_READY 4u
+#define NT_UNSUPPORTED_FAMILY 5u
+#define NT_MAX_WITNESS 4u
+#define NT_MAX_ATTEMPTS 64u
+#define NT_MAX_DIRECTIONS 64u
+
+typedef struct { float p[NT_MAX_WITNESS][3]; uint32_t count; float min_clearance, length; } nt_witness;
+
+static float nt_clamp(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi); } /* :208-210 */
+static void nt_random_direction(uint32_t* rng, float out[3]) { /* :212-217 */
+    const float z = 2.0f * o_wurand(rng) - 1.0f;
+    const float angle = 6.28318530718f * o_wurand(rng);
+    const float radial = sqrtf(fmaxf(0.0f, 1.0f - z * z));
+    out[0] = radial * cosf(angle);
+    out[1] = radial * sinf(angle);
+    out[2] = z;
+}
+static void nt_random_point(uint32_t* rng, const float* low, const float* high, float out[3]) { /* :218-222 */
+    /* three draws inside one wv(...) argument list: reference platforms left
+     * to right, g++ right to left (see wgenerate_mixed) */
+    if (g_args_right_to_left) {
+        out[2] = low[2] + (high[2] - low[2]) * o_wurand(rng);
+        out[1] = low[1] + (high[1] - low[1]) * o_wurand(rng);
+        out[0] = low[0] + (high[0] - low[0]) * o_wurand(rng);
+    } else {
+        out[0] = low[0] + (high[0] - low[0]) * o_wurand(rng);
+        out[1] = low[1] + (high[1] - low[1]) * o_wurand(rng);
+        out[2] = low[2] + (high[2] - low[2]) * o_wurand(rng);
+    }
+}
+static int nt_inside(const float p[3], const float* low, const float* high) { /* :229-232 */
+    return p[0] >= low[0] && p[0] <= high[0] && p[1] >= low[1] && p[1] <= high[1] && p[2] >= low[2] && p[2] <= high[2];
+}
+static float nt_goal_distance(uint32_t* rng, const mdn_task_config* c) { /* :234-239 */
+    const float span = c->goal_distance_max_m - c->goal_distance_min_m;
+    const float center = c->goal_distance_min_m + c->difficulty * span;
+    const float jitter = (o_wurand(rng) - 0.5f) * 0.20f * span;
+    return nt_clamp(center + jitter, c->goal_distance_min_m, c->goal_distance_max_m);
+}
+float o_task_segment_clearance(const mdn_world* w, const float* room, const float a[3], const float b[3]) { /* :240-252 */
+    const float d[3] = {b[0] - a[0], b[1] - a[1], b[2] - a[2]};
+    const float distance = len3(d[0], d[1], d[2]);
+    uint32_t count = (uint32_t)ceilf(distance / 0.05f);
+    if (count < 1u) count = 1u;
+    if (count > 512u) return -1e6f;
+    float minimum = 1e20f;
+    for (uint32_t sample = 0; sample <= count; sample++) {
+        const float t = (float)sample / (float)count;
+        const float pt[3] = {a[0] + d[0] * t, a[1] + d[1] * t, a[2] + d[2] * t};
+        minimum = fminf(minimum, o_wclearance(w, room, pt, 0.0f, NULL));
+    }
+    return minimum;
+}
+static float nt_test_path(const mdn_world* w, const float* room, const float (*pts)[3], uint32_t count) { /* :253-259 */
+    if (count < 2u || count > NT_MAX_WITNESS) return -1e6f;
+    float minimum = 1e20f;
+    for (uint32_t k = 0; k + 1u < count; k++) minimum = fminf(minimum, o_task_segment_clearance(w, room, pts[k], pts[k + 1]));
+    return minimum;
+}
+static void nt_save(nt_witness* out, const float (*pts)[3], uint32_t count, float clearance) { /* :260-273 */
+    out->count = count;
+    out->min_clearance = clearance;
+    float total = 0;
+    for (uint32_t k = 0; k + 1u < count; k++)
+        total += len3(pts[k + 1][0] - pts[k][0], pts[k + 1][1] - pts[k][1], pts[k + 1][2] - pts[k][2]);
+    out->length = total;
+    for (uint32_t i = 0; i < NT_MAX_WITNESS; i++)
+        for (int j = 0; j < 3; j++) out->p[i][j] = i < count ? pts[i][j] : 0.0f;
+}
+static int nt_find_witness(const mdn_world* w, const float* room, const float st[3], const float gl[3],
+                           const mdn_task_config* c, nt_witness* wit, float* direct_clearance) { /* :276-333 */
+    const float direct[2][3] = {{st[0], st[1], st[2]}, {gl[0], gl[1], gl[2]}};
+    *direct_clearance = nt_test_path(w, room, direct, 2u);
+    if (*direct_clearance > c->minimum_witness_clearance_m && c->require_detour == 0u) {
+        nt_save(wit, direct, 2u, *direct_clearance);
+        return 1;
+    }
+    if (*direct_clearance > c->minimum_witness_clearance_m) return 0;
+    const float delta[3] = {gl[0] - st[0], gl[1] - st[1], gl[2] - st[2]};
+    const float x_fraction[5] = {0.10f, 0.25f, 0.50f, 0.75f, 0.90f};
+    const float side_y[2] = {-4.60f, 4.60f};
+    for (uint32_t side = 0; side < 2u; side++)
+        for (uint32_t i = 0; i < 5u; i++) {
+            const float t = x_fraction[i];
+            const float path[3][3] = {{st[0], st[1], st[2]}, {st[0] + t * delta[0], side_y[side], st[2] + t * delta[2]},
+                                      {gl[0], gl[1], gl[2]}};
+            const float cl = nt_test_path(w, room, path, 3u);
+            if (cl > c->minimum_witness_clearance_m) {
+                nt_save(wit, path, 3u, cl);
+                return 1;
+            }
+        }
+    const float side_offset[4] = {-2.4f, -1.2f, 1.2f, 2.4f};
+    for (uint32_t i = 0; i < 4u; i++) {
+        const float t = 0.5f;
+        const float path[3][3] = {{st[0], st[1], st[2]},
+                                  {st[0] + t * delta[0], nt_clamp((st[1] + gl[1]) * 0.5f + side_offset[i], -4.60f, 4.60f),
+                                   st[2] + t * delta[2]},
+                                  {gl[0], gl[1], gl[2]}};
+        const float cl = nt_test_path(w, room, path, 3u);
+        if (cl > c->minimum_witness_clearance_m) {
+            nt_save(wit, path, 3u, cl);
+            return 1;
+        }
+    }
+    const float detour_z[2] = {0.55f, 4.45f};
+    for (uint32_t i = 0; i < 2u; i++) {
+        const float path[3][3] = {{st[0], st[1], st[2]},
+                                  {st[0] + 0.5f * delta[0], st[1] + 0.5f * delta[1], detour_z[i]},
+                                  {gl[0], gl[1], gl[2]}};
+        const float cl = nt_test_path(w, room, path, 3u);
+        if (cl > c->minimum_witness_clearance_m) {
+            nt_save(wit, path, 3u, cl);
+            return 1;
+        }
+    }
+    for (uint32_t side = 0; side < 2u; side++) {
+        const float y = side_y[side];
+        const float path[4][3] = {{st[0], st[1], st[2]},
+                                  {st[0] + 0.20f * delta[0], y, st[2] + 0.20f * delta[2]},
+                                  {st[0] + 0.80f * delta[0], y, st[2] + 0.80f * delta[2]},
+                                  {gl[0], gl[1], gl[2]}};
+        const float cl = nt_test_path(w, room, path, 4u);
+        if (cl > c->minimum_witness_clearance_m) {
+            nt_save(wit, path, 4u, cl);
+            return 1;
+        }
+    }
+    return 0;
+}
+static int nt_static_world(const mdn_world* w) { /* :335-339 */
+    for (uint32_t o = 0; o < w->count; o++)
+        for (int a = 0; a < 3; a++)
+            if (fabsf(w->obstacles[o].velocity[a]) > 1e-8f) return 0;
+    return 1;
+}
+static int nt_config_valid(const mdn_task_config* c) { /* :347-369 */
+    const int valid_stage = c->stage <= NT_STAGE_CLUTTER, valid_objective = c->objective <= NT_OBJ_FINAL_HOLD;
+    if (c->generation_version != 1u || !valid_stage || !valid_objective || c->family > 16u || c->require_detour > 1u ||
+        !isfinite(c->scene_distance_m) || c->scene_distance_m < 3.0f || c->scene_distance_m > 10.0f ||
+        !isfinite(c->difficulty) || c->difficulty < 0.0f || c->difficulty > 1.0f ||
+        !isfinite(c->goal_distance_min_m) || !isfinite(c->goal_distance_max_m) ||
+        c->goal_distance_min_m <= c->goal_radius_m || c->goal_distance_max_m < c->goal_distance_min_m ||
+        !isfinite(c->minimum_endpoint_clearance_m) || c->minimum_endpoint_clearance_m < 0.30f ||
+        !isfinite(c->minimum_witness_clearance_m) || c->minimum_witness_clearance_m < 0.02f ||
+        !isfinite(c->goal_radius_m) || c->goal_radius_m <= 0.0f || !isfinite(c->stable_speed_mps) ||
+        c->stable_speed_mps < 0.0f || !isfinite(c->stable_hold_s) || c->stable_hold_s < 0.0f ||
+        !isfinite(c->nav_period_s) || c->nav_period_s <= 0.0f || !isfinite(c->initial_speed_min_mps) ||
+        !isfinite(c->initial_speed_max_mps) || c->initial_speed_min_mps < 0.0f ||
+        c->initial_speed_max_mps < c->initial_speed_min_mps || !isfinite(c->progress_reward_per_m) ||
+        c->progress_reward_per_m < 0.0f || !isfinite(c->time_cost_per_s) || c->time_cost_per_s < 0.0f ||
+        !isfinite(c->contact_penalty) || c->contact_penalty < 0.0f || !isfinite(c->stable_arrival_bonus) ||
+        c->stable_arrival_bonus < 0.0f || !isfinite(c->command_smoothness_weight) ||
+        c->command_smoothness_weight < 0.0f || c->max_nav_steps == 0u || c->max_generation_attempts == 0u)
+        return 0;
+    return 1;
+}
+uint32_t o_generate_task(mdn_world* w, mdn_task_state* task, uint32_t* rng, const mdn_task_config* c,
+                         const float* room) { /* :343-482 */
+    task->generation_status = NT_INVALID_CONFIG;
+    task->generation_attempts = 0;
+    task->valid = 0;
+    if (!nt_config_valid(c)) return NT_INVALID_CONFIG;
+    if ((c->stage == NT_STAGE_OPEN || c->stage == NT_STAGE_HOLD) && c->family != 0u) return NT_INVALID_CONFIG;
+    if (c->stage == NT_STAGE_CLUTTER &&
+        !(c->family == 1u || c->family == 2u || c->family == 4u || c->family == 5u || c->family == 12u))
+        return NT_UNSUPPORTED_FAMILY;
+    for (int axis = 0; axis < 3; axis++) {
+        const float room_min = axis == 0 ? -2.0f : (axis == 1 ? -5.0f : 0.0f);
+        const float room_max = axis == 0 ? 14.0f : 5.0f;
+        if (!isfinite(c->start_min_xyz[axis]) || !isfinite(c->start_max_xyz[axis]) || !isfinite(c->goal_min_xyz[axis]) ||
+            !isfinite(c->goal_max_xyz[axis]) || c->start_min_xyz[axis] >= c->start_max_xyz[axis] ||
+            c->goal_min_xyz[axis] >= c->goal_max_xyz[axis] ||
+            c->start_min_xyz[axis] < room_min + c->minimum_endpoint_clearance_m ||
+            c->start_max_xyz[axis] > room_max - c->minimum_endpoint_clearance_m ||
+            c->goal_min_xyz[axis] < room_min + c->minimum_endpoint_clearance_m ||
+            c->goal_max_xyz[axis] > room_max - c->minimum_endpoint_clearance_m)
+            return NT_INVALID_CONFIG;
+    }
+    uint32_t attempts = c->max_generation_attempts;
+    if (attempts > NT_MAX_ATTEMPTS) attempts = NT_MAX_ATTEMPTS;
+    for (uint32_t attempt = 0; attempt < attempts; attempt++) {
+        task->generation_attempts = attempt + 1u;
+        const uint32_t scene_seed = o_wrng(rng);
+        uint32_t scene_family = c->family;
+        if (c->family == 12u) {
+            const uint32_t sel = o_wrng(rng) % 4u;
+            scene_family = sel == 0u ? 1u : (sel == 1u ? 2u : (sel == 2u ? 4u : 5u));
+        }
+        o_wgenerate(w, scene_seed, scene_family, c->scene_distance_m);
+        if (c->stage == NT_STAGE_CLUTTER && !nt_static_world(w)) {
+            task->generation_status = NT_UNSUPPORTED_DYNAMIC;
+            return task->generation_status;
+        }
+        float dir[3];
+        nt_random_direction(rng, dir);
+        const float distance = nt_goal_distance(rng, c);
+        float st[3], gl[3];
+        if (c->stage == NT_STAGE_HOLD) {
+            nt_random_point(rng, c->goal_min_xyz, c->goal_max_xyz, gl);
+            for (int j = 0; j < 3; j++) st[j] = gl[j] - dir[j] * distance;
+        } else {
+            nt_random_point(rng, c->start_min_xyz, c->start_max_xyz, st);
+            for (int j = 0; j < 3; j++) gl[j] = st[j] + dir[j] * distance;
+            if (c->stage == NT_STAGE_CLUTTER) {
+                int in_bounds = nt_inside(gl, c->goal_min_xyz, c->goal_max_xyz);
+                for (uint32_t da = 1u; !in_bounds && da < NT_MAX_DIRECTIONS; da++) {
+                    nt_random_direction(rng, dir);
+                    for (int j = 0; j < 3; j++) gl[j] = st[j] + dir[j] * distance;
+                    in_bounds = nt_inside(gl, c->goal_min_xyz, c->goal_max_xyz);
+                }
+                if (!in_bounds) continue;
+            }
+        }
+        if (!isfinite(gl[0]) || !isfinite(gl[1]) || !isfinite(gl[2])) continue;
+        if (!nt_inside(st, c->start_min_xyz, c->start_max_xyz) || !nt_inside(gl, c->goal_min_xyz, c->goal_max_xyz)) continue;
+        const float start_clear = o_wclearance(w, room, st, 0.0f, NULL);
+        const float goal_clear = o_wclearance(w, room, gl, 0.0f, NULL);
+        if (start_clear <= c->minimum_endpoint_clearance_m || goal_clear <= c->minimum_endpoint_clearance_m) continue;
+        const float actual = len3(gl[0] - st[0], gl[1] - st[1], gl[2] - st[2]);
+        if (actual < c->goal_distance_min_m || actual > c->goal_distance_max_m) continue;
+        nt_witness wit;
+        memset(&wit, 0, sizeof(wit));
+        float direct_clearance = 0.0f;
+        if (!nt_find_witness(w, room, st, gl, c, &wit, &direct_clearance)) continue;
+        for (int j = 0; j < 3; j++) w->goal[j] = gl[j];
+        task->family = scene_family;
+        task->stage = c->stage;
+        task->objective = c->objective;
+        task->max_nav_steps = c->max_nav_steps;
+        task->step_count = 0;
+        task->stable_ticks = 0;
+        task->was_inside_goal = 0;
+        task->waypoint_event_latched = 0;
+        task->terminal = 0;
+        for (int j = 0; j < 3; j++) task->start_position[j] = st[j];
+        task->start_yaw_rad = (o_wurand(rng) * 2.0f - 1.0f) * 3.14159265359f;
+        const float speed = c->initial_speed_min_mps + (c->initial_speed_max_mps - c->initial_speed_min_mps) * o_wurand(rng);
+        for (int j = 0; j < 3; j++) task->start_velocity_world[j] = dir[j] * speed;
+        for (int j = 0; j < 3; j++) task->goal_position[j] = gl[j];
+        task->initial_distance_m = actual;
+        task->previous_distance_m = actual;
+        task->difficulty = c->difficulty;
+        task->start_clearance_m = start_clear;
+        task->goal_clearance_m = goal_clear;
+        task->direct_segment_clearance_m = direct_clearance;
+        task->witness_min_clearance_m = wit.min_clearance;
+        task->witness_length_m = wit.length;
+        task->stable_time_s = 0.0f;
+        for (int j = 0; j < 3; j++) task->last_executed_world_command[j] = task->start_velocity_world[j];
+        task->last_executed_world_command[3] = 0.0f;
+        task->witness_point_count = wit.count;
+        for (uint32_t k = 0; k < NT_MAX_WITNESS; k++)
+            for (int j = 0; j < 3; j++) task->witness_points[k][j] = k < wit.count ? wit.p[k][j] : 0.0f;
+        task->valid = 1;
+        task->generation_status = NT_READY;
+        return task->generation_status;
+    }
+    task->generation_status = NT_EXHAUSTED;
+    return task->generation_status;
+}
+void o_task_apply_start(const mdn_task_state* task, mdn_physics_state* s) { /* :486-495 */
+    for (int a = 0; a < 3; a++) {
+        s->position[a] = task->start_position[a];
+        s->linear_velocity[a] = task->start_velocity_world[a];
+        s->angular_velocity_body[a] = 0.0f;
+    }
+    const float half_yaw = task->start_yaw_rad * 0.5f;
+    s->orientation_wxyz[0] = cosf(half_yaw);
+    s->orientation_wxyz[1] = 0.0f;
+    s->orientation_wxyz[2] = 0.0f;
+    s->orientation_wxyz[3] = sinf(half_yaw);
+}
+/* out: reward, goal_distance, actual_speed as floats then waypoint, stable,
+ * collision, timeout, done as uint32 (NavigationTaskStep, :179-188) */
+void o_task_step(mdn_task_state* task, const mdn_task_config* c, const float* pos, const float* vel, const float* cmd,
+                 uint32_t contact, uint32_t forced_timeout, void* out) { /* :499-548 */
+    float r_reward = 0, r_dist = 0, r_speed = 0;
+    uint32_t waypoint = 0, stable = 0, collision = 0, timeout = 0, done = 0;
+    if (task->generation_status != NT_READY || task->terminal != 0u) {
+        done = 1u;
+    } else {
+        const float dx = task->goal_position[0] - pos[0], dy = task->goal_position[1] - pos[1], dz = task->goal_position[2] - pos[2];
+        const float distance = sqrtf(dx * dx + dy * dy + dz * dz);
+        const float speed = sqrtf(vel[0] * vel[0] + vel[1] * vel[1] + vel[2] * vel[2]);
+        if (!isfinite(distance) || !isfinite(speed)) {
+            collision = 1u;
+            done = 1u;
+            task->terminal = 1u;
+        } else {
+            task->step_count++;
+            r_dist = distance;
+            r_speed = speed;
+            const float progress = task->previous_distance_m - distance;
+            r_reward = c->progress_reward_per_m * progress - c->time_cost_per_s * c->nav_period_s;
+            task->previous_distance_m = distance;
+            const uint32_t inside = distance <= c->goal_radius_m ? 1u : 0u;
+            waypoint = (task->objective == NT_OBJ_WAYPOINT && inside != 0u && task->waypoint_event_latched == 0u) ? 1u : 0u;
+            if (waypoint) task->waypoint_event_latched = 1u;
+            const uint32_t stable_now = (inside != 0u && speed <= c->stable_speed_mps) ? 1u : 0u;
+            if (task->objective == NT_OBJ_FINAL_HOLD && stable_now != 0u) task->stable_time_s += c->nav_period_s;
+            else task->stable_time_s = 0.0f;
+            task->stable_ticks = (uint32_t)ceilf(task->stable_time_s / fmaxf(c->nav_period_s, 1e-6f) - 1e-5f);
+            stable = (task->objective == NT_OBJ_FINAL_HOLD && stable_now != 0u &&
+                      task->stable_time_s + 1e-6f >= c->stable_hold_s) ? 1u : 0u;
+            collision = contact ? 1u : 0u;
+            timeout = (forced_timeout || task->step_count >= task->max_nav_steps) ? 1u : 0u;
+            if (c->command_smoothness_weight > 0.0f) {
+                float difference = 0.0f;
+                for (int a = 0; a < 4; a++) {
+                    const float delta = cmd[a] - task->last_executed_world_command[a];
+                    difference += delta * delta;
+                    task->last_executed_world_command[a] = cmd[a];
+                }
+                r_reward -= c->command_smoothness_weight * difference * c->nav_period_s;
+            }
+            if (collision) r_reward -= c->contact_penalty;
+            if (stable && !collision) r_reward += c->stable_arrival_bonus;
+            done = (collision || stable || timeout) ? 1u : 0u;
+            task->terminal = done;
+        }
+    }
+    float* f = (float*)out;
+    uint32_t* u = (uint32_t*)out;
+    f[0] = r_reward; f[1] = r_dist; f[2] = r_speed;
+    u[3] = waypoint; u[4] = stable; u[5] = collision; u[6] = timeout; u[7] = done;
+}
+
 /* ------------------------------------------------------------- sensor */
 void o_pixel_ray(float tan_h, float tan_v, uint32_t pixel, float out[3]) { /* sensor_profile.hpp:81-91, world.hpp:25 */
     const uint32_t row = pixel / 20u, col = pixel % 20u;
@@ -952,6 +1291,8 @@ struct o_sim {
     uint8_t *term, *trunc;
     int32_t* contact;
     float* pixel_rays; /* [320][3] */
+    mdn_task_control task_ctl; /* goal-arrival tasks (navigation_training::configure) */
+    mdn_task_state* tasks;
 };
 
 uint32_t o_actor_param_count(void) { return A_P; }
@@ -997,6 +1338,7 @@ o_sim* o_sim_create_shard(const mdn_sim_config* cfg, uint32_t horizon, const mdn
     s->term = zalloc(rows); s->trunc = zalloc(rows);
     s->contact = zalloc(rows * 4);
     s->pixel_rays = zalloc(NPIX * 3 * 4);
+    s->tasks = zalloc(n * sizeof(mdn_task_state));
     for (uint32_t k = 0; k < NPIX; k++) o_pixel_ray(1.0f, 0.75f, k, s->pixel_rays + 3 * k);
     /* Policy initialisation, cpu_reference.hpp:89-103 (== main.mm:548-555). */
     uint32_t seed = 1789;
@@ -1020,11 +1362,12 @@ void o_sim_destroy(o_sim* s) {
     void* bufs[] = {s->states, s->runs, s->worlds, s->sensors, s->poses, s->commands, s->actor, s->critic,
                     s->actor_m, s->actor_v, s->critic_m, s->critic_v, s->obs, s->co, s->actions, s->logp,
                     s->values, s->rewards, s->next_values, s->adv, s->ret, s->term, s->trunc, s->contact,
-                    s->pixel_rays};
+                    s->pixel_rays, s->tasks};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++) free(bufs[i]);
     free(s);
 }
 void o_sim_set_config(o_sim* s, const mdn_sim_config* cfg) { s->cfg = *cfg; }
+void o_sim_set_task_control(o_sim* s, const mdn_task_control* ctl) { s->task_ctl = *ctl; }
 void* o_sim_buffer(o_sim* s, int id, size_t* bytes) {
     const size_t n = s->cfg.n, rows = n * s->horizon;
     switch (id) {
@@ -1050,6 +1393,7 @@ void* o_sim_buffer(o_sim* s, int id, size_t* bytes) {
         case MDN_BUF_RAPTOR: *bytes = sizeof(mdn_raptor_weights); return &s->raptor;
         case MDN_BUF_PHYSICS: *bytes = sizeof(mdn_physics_params); return &s->physics;
         case MDN_BUF_CONTACT_ID: *bytes = rows * 4; return s->contact;
+        case MDN_BUF_TASK_STATES: *bytes = n * sizeof(mdn_task_state); return s->tasks;
         case 100: *bytes = A_P * 4; return s->actor_m;
         case 101: *bytes = A_P * 4; return s->actor_v;
         case 102: *bytes = C_P * 4; return s->critic_m;
@@ -1123,6 +1467,25 @@ static void reset_one(o_sim* s, uint32_t n, int first) {
         run->successes = run->collisions = run->timeouts = run->episodes = 0;
         run->success_time = run->total_path = run->total_elapsed = run->final_progress = 0;
         for (uint32_t j = 0; j < NFRAMES * 12; j++) s->poses[(size_t)n * NFRAMES * 12 + j] = 0;
+    }
+    /* sim_reset_navigation_task, sim.metal:125-141 */
+    mdn_task_state* task = &s->tasks[n];
+    memset(task, 0, sizeof(*task));
+    if (s->task_ctl.enabled) {
+        uint32_t task_rng = c->seed ^ ((gid + 1u) * 0x27d4eb2du) ^ ((run->episodes + 1u) * 0x165667b1u);
+        o_generate_task(w, task, &task_rng, &s->task_ctl.config, s->room);
+        if (task->valid) {
+            o_task_apply_start(task, st);
+            run->yaw = task->start_yaw_rad;
+            run->initial_distance = task->initial_distance_m;
+            for (int a = 0; a < 3; a++) {
+                run->reference_position[a] = st->position[a];
+                run->desired_velocity[a] = st->linear_velocity[a];
+            }
+            w->wind[0] = clean_env(c, gid) ? 0.0f : c->wind;
+            w->wind[1] = 0;
+            w->wind[2] = 0;
+        }
     }
 }
 void o_sim_reset(o_sim* s) {
@@ -1278,39 +1641,93 @@ static float critic_forward_row(const float* critic, const float* co, float* hid
     return acc + critic[C_B2];
 }
 
-/* sim_act (sim.metal:229-271), mode 0/1 training paths and the evaluation
- * guard; sampling order as cpu_reference.hpp:404-429. */
+/* sim_act (sim.metal:229-271): value, mode-dependent mean (geometry-prior
+ * blending for modes 9-21), sampling (cpu_reference.hpp:404-429 for mode 0),
+ * deployed action map (mode 22), scripted goal velocity (modes 2, 3, 20),
+ * command delay, velocity contract, fixed-speed ablation (mode 19). */
 static void act_env(o_sim* s, uint32_t t, uint32_t n) {
     const mdn_sim_config* c = &s->cfg;
     mdn_sim_run* run = &s->runs[n];
     if (c->eval && run->episodes) return;
     const size_t row = (size_t)t * c->n + n;
+    const float* ob = s->obs + row * AOBS;
     float hidden[HID], mean[ACT], a[ACT];
-    actor_forward_row(s->actor, s->obs + row * AOBS, hidden, mean);
+    actor_forward_row(s->actor, ob, hidden, mean);
     s->values[row] = critic_forward_row(s->critic, s->co + row * COBS, hidden);
+    const uint32_t mode = c->mode;
+    if (mode >= 9 && mode <= 21) {
+        float scale = (mode == 9 || mode == 13) ? 0.0f
+                    : ((mode == 10 || mode == 14 || mode == 16) ? 0.25f : (mode == 15 ? 1.0f : 0.5f));
+        if (mode >= 17) {
+            float overhead = 0;
+            for (int k = 0; k < 20; k++) overhead += ob[k] * 12 > 2.5f;
+            scale = .25f + .75f * (overhead / 20.0f);
+        }
+        if (mode == 12) {
+            float near_ = 12;
+            for (int k = 0; k < 80; k++) near_ = fminf(near_, ob[k] * 12);
+            scale = fminf(fmaxf((near_ - .3f) / 2, 0.2f), 1.0f);
+        }
+        for (int j = 0; j < 3; j++) {
+            const float prior = ob[AOBS - 3 + j];
+            mean[j] = prior + scale * (mean[j] - prior);
+        }
+        mean[3] *= scale;
+        if (mode == 16) {
+            const float yaw = atan2f(ob[161], ob[160]);
+            mean[3] += nav_atanh(fminf(fmaxf(yaw * 1.5f, -.85f), .85f));
+        }
+    }
+    float deployed_scale = 1.0f;
+    if (mode == 22) {
+        float overhead = 0;
+        for (int k = 0; k < 20; k++) overhead += ob[k] * 12 > 2.5f;
+        deployed_scale = .25f + .75f * (overhead / 20.0f);
+    }
     const float* log_std = s->actor + A_LS;
     uint32_t rng = run->rng;
-    float lp = 0;
+    float* cmd = s->commands + (size_t)n * NFRAMES * ACT;
     for (uint32_t j = 0; j < ACT; j++) {
-        a[j] = mean[j] + ((c->mode == 0 || c->mode == 22) ? expf(log_std[j]) * sim_normal(&rng) : 0);
-        if (c->mode == 1) a[j] = sim_normal(&rng);
+        a[j] = mean[j] + ((mode == 0 || mode == 22) ? expf(log_std[j]) * sim_normal(&rng) : 0);
+        if (mode == 1) a[j] = sim_normal(&rng);
         s->actions[row * ACT + j] = a[j];
-        s->commands[((size_t)n * NFRAMES + run->steps % NFRAMES) * ACT + j] = tanhf(a[j]);
+        float executed = a[j];
+        if (mode == 22) executed = j < 3 ? ob[AOBS - 3 + j] + deployed_scale * (a[j] - ob[AOBS - 3 + j]) : deployed_scale * a[j];
+        cmd[(run->steps % NFRAMES) * ACT + j] = tanhf(executed);
     }
-    lp = gaussian_log_prob(s->actions + row * ACT, mean, log_std);
-    s->logp[row] = lp;
+    s->logp[row] = gaussian_log_prob(s->actions + row * ACT, mean, log_std);
     run->rng = rng;
+    const mdn_physics_state* st = &s->states[n];
+    if (mode == 2 || mode == 3 || mode == 20) {
+        const mdn_world* w = &s->worlds[n];
+        float d[3] = {w->goal[0] - st->position[0], w->goal[1] - st->position[1], w->goal[2] - st->position[2]};
+        const float len = len3(d[0], d[1], d[2]);
+        const float inv = 1.0f / len, keep = smin(len, c->speed);
+        for (int j = 0; j < 3; j++) d[j] = d[j] * inv * keep;
+        float r[9];
+        rotation(st->orientation_wxyz, r);
+        const float sc[4] = {(r[0] * d[0] + r[3] * d[1] + r[6] * d[2]) / c->speed,
+                             (r[1] * d[0] + r[4] * d[1] + r[7] * d[2]) / c->speed,
+                             (r[2] * d[0] + r[5] * d[1] + r[8] * d[2]) / c->speed, 0.0f};
+        for (int j = 0; j < 4; j++) cmd[(run->steps % NFRAMES) * ACT + j] = sc[j];
+    }
     const uint32_t delay = clean_env(c, s->env_base + n) ? 0 : c->command_delay;
     const uint32_t applied = run->steps > delay ? run->steps - delay : 0;
-    for (uint32_t j = 0; j < ACT; j++)
-        run->previous_nav[j] = run->steps < delay ? 0.0f : s->commands[((size_t)n * NFRAMES + applied % NFRAMES) * ACT + j];
+    for (uint32_t j = 0; j < ACT; j++) run->previous_nav[j] = run->steps < delay ? 0.0f : cmd[(applied % NFRAMES) * ACT + j];
     float r[9];
-    rotation(s->states[n].orientation_wxyz, r);
+    rotation(st->orientation_wxyz, r);
     float v[3] = {run->previous_nav[0] * c->speed, run->previous_nav[1] * c->speed,
                   run->previous_nav[2] * c->speed * (c->velocity_contract == 0 ? 0.5f : 1.0f)};
     if (c->velocity_contract == 1) {
         const float scale = smin(1.0f, c->speed / smax(len3(v[0], v[1], v[2]), 1e-8f));
         for (int j = 0; j < 3; j++) v[j] *= scale;
+    }
+    if (mode == 19) {
+        const float magnitude = len3(v[0], v[1], v[2]);
+        if (magnitude > 1e-8f) {
+            const float scale = c->speed / magnitude;
+            for (int j = 0; j < 3; j++) v[j] *= scale;
+        }
     }
     for (int j = 0; j < 3; j++) run->desired_velocity[j] = r[j * 3] * v[0] + r[j * 3 + 1] * v[1] + r[j * 3 + 2] * v[2];
     run->yaw += run->previous_nav[3] * s->physics.dt * (float)c->substeps * 0.5f;
@@ -1389,12 +1806,24 @@ static void advance_env(o_sim* s, uint32_t t, uint32_t n) {
     memcpy(run->hidden, h, sizeof(h));
     memcpy(run->motors, motors, sizeof(motors));
     const float after = len3(w->goal[0] - st.position[0], w->goal[1] - st.position[1], w->goal[2] - st.position[2]);
-    const int success = after < (c->mode == 20 ? .10f : .35f) && !collision, timeout = run->steps >= c->max_steps;
+    int success = after < (c->mode == 20 ? .10f : .35f) && !collision, timeout = run->steps >= c->max_steps;
     s->rewards[row] = (before - after) * 2.0f - .01f - c->risk_coef * clampf_((0.6f - step_clearance) / 0.6f, 0.0f, 1.0f) +
                       (success ? 10.0f : 0.0f) - (collision ? 10.0f : 0.0f);
     s->term[row] = (uint8_t)(collision || success);
     s->trunc[row] = (uint8_t)(timeout && !s->term[row]);
     s->contact[row] = contact;
+    if (s->task_ctl.enabled) {
+        const float executed[4] = {run->desired_velocity[0], run->desired_velocity[1], run->desired_velocity[2],
+                                   run->previous_nav[3] * 0.5f};
+        uint32_t outcome[8];
+        o_task_step(&s->tasks[n], &s->task_ctl.config, st.position, st.linear_velocity, executed, (uint32_t)collision,
+                    (uint32_t)timeout, outcome);
+        success = outcome[4] != 0 && !collision;
+        timeout = outcome[6] != 0;
+        memcpy(&s->rewards[row], &outcome[0], 4);
+        s->term[row] = (uint8_t)(collision || success);
+        s->trunc[row] = (uint8_t)(timeout && !s->term[row]);
+    }
     float co[COBS], hidden[HID];
     critic_obs(s, &st, w, run, co);
     s->next_values[row] = critic_forward_row(s->critic, co, hidden);

@@ -67,6 +67,13 @@ o_sim* o_sim_create(const mdn_sim_config* cfg, uint32_t horizon, const mdn_rapto
 o_sim* o_sim_create_shard(const mdn_sim_config* cfg, uint32_t horizon, const mdn_raptor_weights* raptor,
                           const mdn_physics_params* physics, const float* room, uint32_t env_base);
 void o_sim_rows_grad(o_sim* s, const uint32_t* rows, uint32_t count, float batch, float* grad);
+void o_sim_set_task_control(o_sim* s, const mdn_task_control* ctl);
+/* navigation_tasks.hpp */
+uint32_t o_generate_task(mdn_world* w, mdn_task_state* task, uint32_t* rng, const mdn_task_config* c, const float* room);
+void o_task_apply_start(const mdn_task_state* task, mdn_physics_state* s);
+void o_task_step(mdn_task_state* task, const mdn_task_config* c, const float* pos, const float* vel, const float* cmd,
+                 uint32_t contact, uint32_t forced_timeout, void* out);
+float o_task_segment_clearance(const mdn_world* w, const float* room, const float a[3], const float b[3]);
 void o_sim_destroy(o_sim* s);
 void* o_sim_buffer(o_sim* s, int id, size_t* bytes);
 void o_sim_reset(o_sim* s);

@@ -80,6 +80,11 @@ def load_oracle():
     d("o_sim_gae_normalize", None, _P, ctypes.c_int)
     d("o_sim_train_rollout", None, _P, _U, _U, _P, _U, _P, _P, _P, _P)
     d("o_set_threads", None, ctypes.c_int)
+    d("o_sim_set_task_control", None, _P, _P)
+    d("o_generate_task", _U, _P, _P, _P, _P, _P)
+    d("o_task_apply_start", None, _P, _P)
+    d("o_task_step", None, _P, _P, _P, _P, _P, _U, _U, _P)
+    d("o_task_segment_clearance", _F, _P, _P, _P, _P)
     return lib
 
 
@@ -127,6 +132,11 @@ def load_ref():
     d("ref_critic_forward", _F, _P, _P, _P)
     d("ref_adam_update", None, _P, _P, _P, _P, ctypes.c_size_t, ctypes.c_uint64, _F)
     d("ref_run_cpu_self_tests", ctypes.c_int)
+    d("ref_task_default_config", ctypes.c_int, _U, _U, _F, _P)
+    d("ref_generate_task", _U, _P, _P, _P, _P)
+    d("ref_task_apply_start", None, _P, _P)
+    d("ref_task_step", None, _P, _P, _P, _P, _P, _U, _U, _P)
+    d("ref_task_segment_clearance", _F, _P, _P, _P)
     return lib
 
 
@@ -177,6 +187,11 @@ class OracleSim(_Buffers):
     def set_config(self, cfg):
         self.cfg = np.array(cfg, self.layouts.CONFIG)
         self.lib.o_sim_set_config(self.h, ptr(self.cfg))
+
+    def set_task_control(self, control):
+        """navigation_training::configure without the reset (call reset())."""
+        self.task_control = np.array(control, self.layouts.TASK_CONTROL)
+        self.lib.o_sim_set_task_control(self.h, ptr(self.task_control))
 
     def step(self, tick):
         self.lib.o_sim_step(self.h, tick)

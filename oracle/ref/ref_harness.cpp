@@ -31,6 +31,7 @@
 #include <string>
 #include <vector>
 #include <omp.h>
+#include <math.h>  // ::isfinite for physics_domain.hpp, as Apple libc++ provides it
 
 #include "mdn.h"
 
@@ -43,6 +44,10 @@ static_assert(sizeof(SimConfig) == 84 && sizeof(SimRun) == 184, "sim layout");
 #define private public
 #include "cpu_reference.hpp"
 #undef private
+#include "navigation_runtime.hpp"
+#include "navigation_tasks.hpp"
+static_assert(sizeof(NavigationTaskConfig) == sizeof(mdn_task_config), "task config layout");
+static_assert(sizeof(NavigationTaskState) == sizeof(mdn_task_state), "task state layout");
 
 using Trainer = cpu_reference::Trainer;
 static_assert(sizeof(RLPhysicsState) == sizeof(mdn_physics_state), "state layout");
@@ -286,6 +291,27 @@ void ref_adam_update(float* params, const float* grad, float* m, float* v, size_
     fixed_ppo::adam_update(params, grad, m, v, count, step, lr, 0.9f, 0.999f, 1.0e-8f, 0.0f);
 }
 int ref_run_cpu_self_tests(void) { return fixed_ppo::run_cpu_self_tests() ? 1 : 0; }
+
+/* ---------------- goal-arrival task contract (navigation_tasks.hpp) ---------------- */
+int ref_task_default_config(uint32_t stage, uint32_t family, float difficulty, void* cfg) {
+    return navigation_task_default_config(*(NavigationTaskConfig*)cfg, stage, family, difficulty) ? 1 : 0;
+}
+uint32_t ref_generate_task(void* world, void* task, uint32_t* rng, const void* cfg) {
+    return navigation_generate_task(*(WWorld*)world, *(NavigationTaskState*)task, *rng, *(const NavigationTaskConfig*)cfg);
+}
+void ref_task_apply_start(const void* task, void* state) {
+    navigation_task_apply_start(*(const NavigationTaskState*)task, *(RLPhysicsState*)state);
+}
+/* out: reward, goal_distance, actual_speed, then 5 uint flags (waypoint, stable, collision, timeout, done) */
+void ref_task_step(void* task, const void* cfg, const float* pos, const float* vel, const float* cmd, uint32_t contact,
+                   uint32_t timeout, void* out) {
+    const NavigationTaskStep r = navigation_task_step(*(NavigationTaskState*)task, *(const NavigationTaskConfig*)cfg,
+                                                      pos, vel, cmd, contact, timeout);
+    std::memcpy(out, &r, sizeof(r));
+}
+float ref_task_segment_clearance(const void* world, const float a[3], const float b[3]) {
+    return navigation_task_segment_clearance(*(const WWorld*)world, wv(a[0], a[1], a[2]), wv(b[0], b[1], b[2]));
+}
 uint32_t ref_actor_param_count(void) { return uint32_t(fixed_ppo::actor_param_count); }
 uint32_t ref_critic_param_count(void) { return uint32_t(fixed_ppo::critic_param_count); }
 
