@@ -237,7 +237,7 @@ void validate_config(const mdn_sim_config& c) {
     require(c.sensor_delay <= 6 && c.command_delay <= 7, MDN_ERR_INVALID,
             "delay rings support <=6 sensor frames and <=7 command steps");
     require(c.mode <= 22, MDN_ERR_INVALID, "SimConfig.mode: sim_act defines modes 0..22");
-    require(c.geometry_memory == 0, MDN_ERR_INVALID, "SimConfig.geometry_memory=1 is not supported by this build");
+    require(c.geometry_memory <= 1, MDN_ERR_INVALID, "SimConfig.geometry_memory must be 0 or 1");
     require(std::isfinite(c.speed) && std::isfinite(c.distance), MDN_ERR_INVALID, "SimConfig speed/distance");
 }
 

@@ -53,7 +53,7 @@ cudaError_t launch_step(const SimArgs& a, int act_grid, cudaStream_t s);
 size_t act_smem_bytes();
 cudaError_t launch_step_profiled(const SimArgs& a, int act_grid, cudaStream_t s, cudaEvent_t ev[4]);
 cudaError_t fp32_peak(int sm_count, double* tflops);
-int kernels_per_step();
+int kernels_per_step(const mdn_sim_config& c);
 
 }  // namespace mdn
 

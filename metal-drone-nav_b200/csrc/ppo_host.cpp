@@ -515,7 +515,10 @@ extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t fa
 
 extern "C" int mdn_launch_counts(mdn_sim* sim, mdn_ppo* t, uint32_t* per_policy_step, uint32_t* per_update) {
     return guarded([&] {
-        if (per_policy_step) *per_policy_step = uint32_t(kernels_per_step());
+        if (per_policy_step) {
+            require(sim != nullptr, MDN_ERR_INVALID, "launch counts: null simulator");
+            *per_policy_step = uint32_t(kernels_per_step(sim->cfg));
+        }
         if (per_update) {
             require(t != nullptr, MDN_ERR_INVALID, "launch counts: null trainer");
             require(t->graph != nullptr, MDN_ERR_STATE, "launch counts: run one rollout update first");

@@ -405,6 +405,223 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
     }
 }
 
+// ------------------------------------------------------- geometry memory
+// Memory-guided geometry prior (sim.metal:216-218 with geometry_memory = 1;
+// nav_guidance_memory, guidance.hpp:106-194), one warp per environment, run
+// after k_sense has written the pooled ranges and the context features. The
+// up to 8 x 80 remembered obstacle points (each pooled cell's nearest pixel
+// in an older range frame, moved into the current body frame through the
+// pose ring) are built once into shared memory; lanes then own the 85
+// candidate directions and sweep every point. Only fminf/fmaxf combine the
+// points, so the split over lanes keeps the reference's values exactly.
+constexpr int kMemWarps = 4;
+constexpr int kMemPoints = kFrames * 80;
+
+struct MemScene {
+    float px[kMemPoints], py[kMemPoints], pz[kMemPoints], pr2[kMemPoints];  // point, |point|^2
+    float rad[kMemPoints], rad2[kMemPoints];                                  // memory radius and its square
+    float cur[80], prev[80], risk_term[80];
+};
+
+__global__ void __launch_bounds__(kMemWarps * 32) k_memory_hint(SimArgs a) {
+    extern __shared__ float mem_sm[];
+    MemScene& ms = reinterpret_cast<MemScene*>(mem_sm)[threadIdx.x >> 5];
+    const int lane = threadIdx.x & 31;
+    const uint32_t i = blockIdx.x * kMemWarps + (threadIdx.x >> 5);
+    if (i >= a.n) return;
+    const mdn_sim_config& c = a.cfg;
+    const mdn_sim_run& run = a.runs[i];
+    if (c.eval && run.episodes) return;
+    const uint32_t steps = run.steps, gid = a.env_base + i;
+    const mdn_physics_state& st = a.states[i];
+    const mdn_world& w = a.worlds[i];
+    const float pos[3] = {st.position[0], st.position[1], st.position[2]};
+    const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2], st.orientation_wxyz[3]};
+    float r[9];
+    rotation(q, r);
+    const size_t row = size_t(a.tick) * a.n + i;
+    float* obs = a.obs + row * kActorObs;
+    const uint32_t delay = clean_env(c, gid) ? 0u : c.sensor_delay;
+    const uint32_t available = steps / c.sensor_period;
+    const uint32_t frame = available > delay ? available - delay : 0;
+    const uint32_t valid = available >= delay ? min(frame + 1u, uint32_t(kFrames) - delay) : 0u;
+    const float sensor_dt = float(c.sensor_period) * a.physics->dt * float(c.substeps);
+    const float tan_v = 0.75f;
+    const float gvel[3] = {obs[164] * 4.0f, obs[165] * 4.0f, obs[166] * 4.0f};
+    for (int k = lane; k < 80; k += 32) {
+        ms.cur[k] = obs[k] * 12.0f;
+        ms.prev[k] = obs[80 + k] * 12.0f;
+    }
+    __syncwarp();
+    for (int k = lane; k < 80; k += 32) {
+        const float old = ms.prev[k], now = ms.cur[k];
+        float term = 0.0f;
+        if (old < 11.9f && now < 11.9f) {
+            const float unexpected = (old - now) / fmaxf(sensor_dt, 1e-3f) -
+                                     (gvel[0] * c_pool_ray_at(3 * k) + gvel[1] * c_pool_ray_at(3 * k + 1) +
+                                      gvel[2] * c_pool_ray_at(3 * k + 2));
+            if (unexpected > 0.5f) term = fminf(0.20f * unexpected, 1.0f);
+        }
+        ms.risk_term[k] = term;
+    }
+    // remembered points, compacted (nav_memory_clearance's loops, :106-140)
+    const float* ring = a.sensors + size_t(i) * kFrames * kPixels;
+    const float* poses = a.poses + size_t(i) * kFrames * 12;
+    const float cur_pose[12] = {pos[0], pos[1], pos[2], r[0], r[1], r[2], r[3], r[4], r[5], r[6], r[7], r[8]};
+    int npoints = 0;
+    for (int base = 0; base < int(valid) * 80; base += 32) {
+        const int p = base + lane;
+        bool keep = false;
+        float x = 0, y = 0, z = 0, radius = 0;
+        if (p < int(valid) * 80) {
+            const uint32_t back = uint32_t(p / 80), cell = uint32_t(p % 80);
+            const uint32_t f = (frame + 8u - back) % 8u;
+            const float* old_pose = poses + f * 12;
+            const float* ranges = ring + f * kPixels;
+            const float age = float(back) * fmaxf(sensor_dt, 0.0f);
+            const uint32_t px = (cell / 10u) * 2u * 20u + (cell % 10u) * 2u;
+            uint32_t hit = px;
+            float range = ranges[px];
+            const uint32_t others[3] = {px + 1u, px + 20u, px + 21u};
+            for (int j = 0; j < 3; j++)
+                if (ranges[others[j]] < range) {
+                    range = ranges[others[j]];
+                    hit = others[j];
+                }
+            if (!(range <= 0.01f || range >= 11.9f)) {
+                keep = true;
+                const float ry = 1.0f - (float(hit % 20u) + 0.5f) / 10.0f;
+                const float rz = tan_v * (1.0f - (float(hit / 20u) + 0.5f) / 8.0f);
+                const float inv = 1.0f / sqrtf(1.0f + ry * ry + rz * rz);
+                const float ray[3] = {inv, ry * inv, rz * inv};
+                const float wx = old_pose[3] * ray[0] + old_pose[4] * ray[1] + old_pose[5] * ray[2];
+                const float wy = old_pose[6] * ray[0] + old_pose[7] * ray[1] + old_pose[8] * ray[2];
+                const float wz = old_pose[9] * ray[0] + old_pose[10] * ray[1] + old_pose[11] * ray[2];
+                const float dx = old_pose[0] + range * wx - cur_pose[0];
+                const float dy = old_pose[1] + range * wy - cur_pose[1];
+                const float dz = old_pose[2] + range * wz - cur_pose[2];
+                x = cur_pose[3] * dx + cur_pose[6] * dy + cur_pose[9] * dz;
+                y = cur_pose[4] * dx + cur_pose[7] * dy + cur_pose[10] * dz;
+                z = cur_pose[5] * dx + cur_pose[8] * dy + cur_pose[11] * dz;
+                radius = 0.20f + 0.015f * range + 0.15f * age;  // memory_point_radius, :96-100
+            }
+        }
+        const unsigned kept = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+            const int slot = npoints + __popc(kept & ((1u << lane) - 1u));
+            ms.px[slot] = x;
+            ms.py[slot] = y;
+            ms.pz[slot] = z;
+            ms.pr2[slot] = x * x + y * y + z * z;
+            ms.rad[slot] = radius;
+            ms.rad2[slot] = radius * radius;
+        }
+        npoints += __popc(kept);
+    }
+    __syncwarp();
+    const float delta[3] = {w.goal[0] - pos[0], w.goal[1] - pos[1], w.goal[2] - pos[2]};
+    const float distance = smax(len3(delta[0], delta[1], delta[2]), 1.0e-6f);
+    const float g0 = obs[160], g1 = obs[161], g2 = obs[162];
+    const float gnorm = sqrtf(g0 * g0 + g1 * g1 + g2 * g2);
+    float hint[3] = {0, 0, 0};
+    if (!(gnorm < 1e-6f || distance < 0.05f)) {
+        const float goal[3] = {g0 / gnorm, g1 / gnorm, g2 / gnorm};
+        const float speed = sqrtf(gvel[0] * gvel[0] + gvel[1] * gvel[1] + gvel[2] * gvel[2]);
+        const float stop_margin = 0.28f + speed * fmaxf(sensor_dt, 0.0f) + 0.25f * speed * speed;
+        float goal_dot = -1e20f;
+        int goal_cell = 1 << 20;
+        for (int k = lane; k < 80; k += 32) {
+            const float al = c_pool_ray_at(3 * k) * goal[0] + c_pool_ray_at(3 * k + 1) * goal[1] +
+                             c_pool_ray_at(3 * k + 2) * goal[2];
+            if (al > goal_dot) {
+                goal_dot = al;
+                goal_cell = k;
+            }
+        }
+        warp_argmax_first(goal_dot, goal_cell);
+        const int grow = goal_cell < 80 ? goal_cell / 10 : 0, gcol = goal_cell < 80 ? goal_cell % 10 : 0;
+        const float desired_speed = fminf(1.6f, sqrtf(4.0f * fmaxf(distance - 0.28f, 0.0f)));
+        const float required = stop_margin + 0.15f + desired_speed * desired_speed * 0.25f;
+        float best_score = -1e20f, best_free = 0.0f;
+        int best = 1 << 20;
+        for (int cand = lane; cand < 85; cand += 32) {
+            float d[3];
+            int crow = grow, ccol = gcol;
+            if (cand < 80) {
+                crow = cand / 10;
+                ccol = cand % 10;
+                d[0] = c_pool_ray_at(3 * cand);
+                d[1] = c_pool_ray_at(3 * cand + 1);
+                d[2] = c_pool_ray_at(3 * cand + 2);
+            } else if (cand == 80) {
+                d[0] = goal[0]; d[1] = goal[1]; d[2] = goal[2];
+            } else {
+                d[0] = 0.0f;
+                d[1] = cand >= 83 ? (cand == 83 ? 1.0f : -1.0f) : 0.0f;
+                d[2] = cand < 83 ? (cand == 81 ? 1.0f : -1.0f) : 0.0f;
+            }
+            float sweep[3] = {1.2f * d[0] + 0.35f * gvel[0], 1.2f * d[1] + 0.35f * gvel[1], 1.2f * d[2] + 0.35f * gvel[2]};
+            const float sweep_norm = sqrtf(sweep[0] * sweep[0] + sweep[1] * sweep[1] + sweep[2] * sweep[2]);
+            for (int j = 0; j < 3; j++) sweep[j] /= fmaxf(sweep_norm, 1e-6f);
+            float nearest = 3.0f;
+            for (int p = 0; p < npoints; p++) {
+                const float along = ms.px[p] * sweep[0] + ms.py[p] * sweep[1] + ms.pz[p] * sweep[2];
+                if (along <= 0.0f || along > 3.0f + ms.rad[p]) continue;
+                const float lateral2 = fmaxf(ms.pr2[p] - along * along, 0.0f);
+                const float radius2 = ms.rad2[p];
+                if (lateral2 < radius2) nearest = fminf(nearest, fmaxf(along - sqrtf(radius2 - lateral2), 0.0f));
+            }
+            float free_ = nearest;
+            if (cand < 81) free_ = fminf(free_, pooled_min3x3(ms.cur, crow, ccol));
+            float risk = 0.0f;
+            if (sensor_dt > 1e-4f)
+                for (int dr = -1; dr <= 1; dr++)
+                    for (int dc = -1; dc <= 1; dc++) {
+                        const int rr = crow + dr, cc = ccol + dc;
+                        if (rr < 0 || rr >= 8 || cc < 0 || cc >= 10) continue;
+                        risk = fmaxf(risk, ms.risk_term[rr * 10 + cc]);
+                    }
+            free_ = fmaxf(free_ - risk, 0.0f);
+            const float alignment = d[0] * goal[0] + d[1] * goal[1] + d[2] * goal[2];
+            const float score = 1.4f * alignment + 0.20f * fminf(free_, 3.0f) -
+                                (free_ < required ? 3.0f * (required - free_) / required : 0.0f);
+            if (score > best_score) {
+                best_score = score;
+                best_free = free_;
+                best = cand;
+            }
+        }
+        const float lane_free = best_free;
+        const int lane_best = best;
+        warp_argmax_first(best_score, best);
+        const unsigned owner_mask = __ballot_sync(0xffffffffu, lane_best == best);
+        const float chosen_free = __shfl_sync(0xffffffffu, lane_free, owner_mask ? __ffs(owner_mask) - 1 : 0);
+        float dir[3] = {1.0f, 0.0f, 0.0f};
+        if (best < 80) {
+            dir[0] = c_pool_ray_at(3 * best);
+            dir[1] = c_pool_ray_at(3 * best + 1);
+            dir[2] = c_pool_ray_at(3 * best + 2);
+        } else if (best == 80) {
+            dir[0] = goal[0]; dir[1] = goal[1]; dir[2] = goal[2];
+        } else if (best < 85) {
+            dir[0] = 0.0f;
+            dir[1] = best >= 83 ? (best == 83 ? 1.0f : -1.0f) : 0.0f;
+            dir[2] = best < 83 ? (best == 81 ? 1.0f : -1.0f) : 0.0f;
+        }
+        const float chosen = best < 85 ? chosen_free : 0.0f;
+        const bool goal_in_fov = goal[0] > 0.0f && fabsf(goal[1]) <= goal[0] && fabsf(goal[2]) <= tan_v * goal[0];
+        const float after_stop = fmaxf(chosen - stop_margin - 0.15f, 0.0f);
+        float command_speed = fminf(desired_speed, sqrtf(4.0f * after_stop));
+        if (!goal_in_fov) command_speed = fminf(command_speed, 0.25f);
+        const float fraction = fminf(0.8f, command_speed * 0.5f);
+        for (int j = 0; j < 3; j++) {
+            const float x = fraction * dir[j];
+            hint[j] = 0.5f * logf((1.0f + x) / (1.0f - x));  // guidance.hpp:35
+        }
+    }
+    if (lane < 3) obs[181 + lane] = hint[lane];
+}
+
 // -------------------------------------------------------------------- act
 // Actor mean (tanh MLP 184->64->4 plus geometry prior, ppo.hpp:65-80), critic
 // value (32->64->1, ppo.hpp:82-93), Gaussian sample, log-prob, command ring,
@@ -831,6 +1048,8 @@ size_t act_smem_bytes() { return sizeof(float) * kActSmemFloats; }
 
 cudaError_t launch_step(const SimArgs& a, int act_grid, cudaStream_t s) {
     k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
+    if (a.cfg.geometry_memory)
+        k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
     k_act<<<act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
     k_advance<<<blocks_for(a.n, kAdvanceThreads), kAdvanceThreads, 0, s>>>(a);
     return cudaGetLastError();
@@ -839,6 +1058,8 @@ cudaError_t launch_step(const SimArgs& a, int act_grid, cudaStream_t s) {
 cudaError_t launch_step_profiled(const SimArgs& a, int act_grid, cudaStream_t s, cudaEvent_t ev[4]) {
     cudaEventRecord(ev[0], s);
     k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
+    if (a.cfg.geometry_memory)
+        k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
     cudaEventRecord(ev[1], s);
     k_act<<<act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
     cudaEventRecord(ev[2], s);
@@ -890,10 +1111,13 @@ cudaError_t fp32_peak(int sm_count, double* tflops) {
     return e;
 }
 
-int kernels_per_step() { return 3; }
+int kernels_per_step(const mdn_sim_config& c) { return c.geometry_memory ? 4 : 3; }
 
 cudaError_t configure_kernels() {
-    return cudaFuncSetAttribute(k_act, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
+    cudaError_t e = cudaFuncSetAttribute(k_act, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_memory_hint, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kMemWarps * sizeof(MemScene)));
 }
 
 }  // namespace mdn

@@ -91,6 +91,8 @@ CONFIGS = [
     dict(family=1, mode=1),
     dict(family=4, eval=1, max_steps=9),
     dict(family=17),
+    dict(family=13, geometry_memory=1, sensor_delay=2),
+    dict(family=1, geometry_memory=1, mode=22, command_delay=1, sensor_period=2),
 ]
 
 

@@ -86,6 +86,9 @@ TASK_CASES = [
     dict(stage=2, family=4, mode=17, eval=1),
     dict(stage=2, family=5, mode=22, wind=0.3, sensor_delay=1, command_delay=1),
     dict(stage=2, family=12, mode=22),
+    # navigation_training::train / evaluate: mode 22 / 17 with geometry memory
+    dict(stage=2, family=12, mode=22, geometry_memory=1),
+    dict(stage=1, family=0, mode=17, geometry_memory=1, eval=1),
 ]
 
 
