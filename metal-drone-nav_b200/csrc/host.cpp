@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <fstream>
 #include <memory>
 #include <string>
@@ -360,8 +361,10 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
                        MDN_BUF_NEXT_VALUES, MDN_BUF_TERMINATED, MDN_BUF_TRUNCATED, MDN_BUF_ADVANTAGES, MDN_BUF_RETURNS,
                        MDN_BUF_CONTACT_ID, MDN_BUF_TASK_STATES})
             cuda_check(cudaMemsetAsync(sim->buf[id], 0, b[id], sim->stream), "clear rollout buffers");
-        // Persistent act kernel: enough CTAs to fill every SM twice.
-        sim->act_grid = int(std::min<size_t>((n + 31) / 32, size_t(dev->sm_count) * 2));
+        // Launch shapes; MDN_ADVANCE_GROUP (1 or 2) overrides the advance
+        // kernel's lanes per environment, for tuning.
+        const char* group_env = std::getenv("MDN_ADVANCE_GROUP");
+        sim->plan = plan_step(n, dev->sm_count, group_env ? std::atoi(group_env) : 0);
         cuda_check(launch_reset(sim->args(0), true, sim->stream), "reset");
         cuda_check(cudaStreamSynchronize(sim->stream), "mdn_sim_create");
         dev->sims.push_back(sim.get());
@@ -418,7 +421,7 @@ extern "C" int mdn_sim_step(mdn_sim* sim, uint32_t tick) {
     return guarded([&] {
         checked(sim);
         require(tick < sim->horizon, MDN_ERR_INVALID, "tick must be below the horizon");
-        cuda_check(launch_step(sim->args(tick), sim->act_grid, sim->stream), "step");
+        cuda_check(launch_step(sim->args(tick), sim->plan, sim->stream), "step");
     });
 }
 
@@ -436,7 +439,7 @@ extern "C" int mdn_sim_collect(mdn_sim* sim, uint32_t steps) {
             cuda_check(cudaStreamBeginCapture(sim->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
             cudaError_t launch = cudaSuccess;
             for (uint32_t t = 0; t < steps && launch == cudaSuccess; t++)
-                launch = launch_step(sim->args(t % sim->horizon), sim->act_grid, sim->stream);
+                launch = launch_step(sim->args(t % sim->horizon), sim->plan, sim->stream);
             const cudaError_t end = cudaStreamEndCapture(sim->stream, &graph);
             cuda_check(launch, "capture step");
             cuda_check(end, "end capture");
@@ -536,7 +539,7 @@ extern "C" int mdn_sim_profile_step(mdn_sim* sim, uint32_t tick, float ms[3]) {
         require(ms != nullptr && tick < sim->horizon, MDN_ERR_INVALID, "profile_step: bad argument");
         cudaEvent_t ev[4];
         for (auto& e : ev) cuda_check(cudaEventCreate(&e), "event");
-        const cudaError_t launch = launch_step_profiled(sim->args(tick), sim->act_grid, sim->stream, ev);
+        const cudaError_t launch = launch_step_profiled(sim->args(tick), sim->plan, sim->stream, ev);
         const cudaError_t wait = cudaEventSynchronize(ev[3]);
         for (int k = 0; k < 3 && launch == cudaSuccess && wait == cudaSuccess; k++) cudaEventElapsedTime(&ms[k], ev[k], ev[k + 1]);
         for (auto& e : ev) cudaEventDestroy(e);

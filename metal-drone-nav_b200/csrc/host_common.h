@@ -49,9 +49,10 @@ cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays
 cudaError_t configure_kernels();
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s);
 cudaError_t launch_world_mirror(const SimArgs& a, cudaStream_t s);
-cudaError_t launch_step(const SimArgs& a, int act_grid, cudaStream_t s);
+StepPlan plan_step(uint32_t n, int sm_count, int group_override);
+cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s);
 size_t act_smem_bytes();
-cudaError_t launch_step_profiled(const SimArgs& a, int act_grid, cudaStream_t s, cudaEvent_t ev[4]);
+cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4]);
 cudaError_t fp32_peak(int sm_count, double* tflops);
 int kernels_per_step(const mdn_sim_config& c);
 
@@ -78,7 +79,7 @@ struct mdn_sim {
     float* world_soa = nullptr;  // device mirror of the worlds, structure of arrays
     size_t bytes[MDN_BUF_COUNT] = {};
     float room_lo[3], room_hi[3], room_c[3], room_e[3];
-    int act_grid = 1;
+    mdn::StepPlan plan;
     // collect() graphs cached by step count
     std::vector<std::pair<uint32_t, cudaGraphExec_t>> graphs;
     cudaEvent_t ev_start = nullptr, ev_stop = nullptr;

@@ -27,6 +27,13 @@ constexpr float kLogTwoPi = 1.8378770664093453f;
 constexpr float kTanV = 0.75f;  // legacy camera, sensor_profile.hpp:44-45
 constexpr int kWorldSoaWords = 161;
 
+// Launch shapes of one policy step (rollout.cu plan_step).
+struct StepPlan {
+    int act_grid = 1;       // persistent k_act CTAs
+    int advance_group = 1;  // lanes per environment in k_advance (1 or 2)
+    int advance_grid = 1;   // k_advance CTAs (grid-stride over environments)
+};
+
 // Everything one launch of a rollout kernel needs (passed by value).
 struct SimArgs {
     mdn_sim_config cfg;

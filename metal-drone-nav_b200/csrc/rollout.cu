@@ -8,6 +8,8 @@
 // (cpu_reference.hpp:240-513).
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "mdn_device.cuh"
 #include "task.cuh"
 #include "world_gen.cuh"
@@ -628,12 +630,16 @@ __global__ void __launch_bounds__(kMemWarps * 32) k_memory_hint(SimArgs a) {
 // command delay and desired velocity (sim.metal:229-271). A warp handles four
 // environments per pass: lanes own hidden units (lane, lane+32), so every
 // weight loaded from shared memory feeds four environments; lanes 0-3 then
-// sample the four environments' actions in parallel. The CTA keeps W1
-// transposed in shared memory and loops over the environments.
+// sample the four environments' actions in parallel. The CTA keeps W1 in
+// shared memory as rows padded to 185 words, so lane h reading row h and the
+// row-order fill from global memory are both free of bank conflicts, and loops
+// over the environments.
 constexpr int kActWarps = 8;
 constexpr int kActEnvs = 4;
-constexpr int kActSmemFloats = kActorObs * kHidden + kHidden + kActions * kHidden + 2 * kActions +
-                               kCriticObs * kHidden + kHidden + kHidden + 1 +
+constexpr int kActW1Pitch = kActorObs + 1;   // padded rows: lane h reads row h, bank (25 h + k) % 32
+constexpr int kActCw1Pitch = kCriticObs + 1;
+constexpr int kActSmemFloats = kHidden * kActW1Pitch + kHidden + kActions * kHidden + 2 * kActions +
+                               kHidden * kActCw1Pitch + kHidden + kHidden + 1 +
                                kActWarps * kActEnvs * (kActorObs + kCriticObs);
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -652,24 +658,24 @@ __device__ __forceinline__ float overhead_scale(const float* ob) {
 
 __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
     extern __shared__ float sm[];
-    float* w1t = sm;                                  // [184][64]
-    float* b1 = w1t + kActorObs * kHidden;            // [64]
+    float* w1p = sm;                                  // [64][185] actor W1, row-major, padded
+    float* b1 = w1p + kHidden * kActW1Pitch;          // [64]
     float* w2 = b1 + kHidden;                         // [4][64]
     float* b2 = w2 + kActions * kHidden;              // [4]
     float* log_std = b2 + kActions;                   // [4]
-    float* cw1t = log_std + kActions;                 // [32][64]
-    float* cb1 = cw1t + kCriticObs * kHidden;         // [64]
+    float* cw1p = log_std + kActions;                 // [64][33] critic W1, row-major, padded
+    float* cb1 = cw1p + kHidden * kActCw1Pitch;       // [64]
     float* cw2 = cb1 + kHidden;                       // [64]
     float* cb2 = cw2 + kHidden;                       // [1]
     float* rows = cb2 + 1;                            // per warp: obs[4][184], co[4][32]
     const int tid = threadIdx.x;
     for (int k = tid; k < kActorObs * kHidden; k += blockDim.x) {
         const int h = k / kActorObs, col = k % kActorObs;
-        w1t[col * kHidden + h] = a.actor[k];
+        w1p[h * kActW1Pitch + col] = a.actor[k];
     }
     for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
         const int h = k / kCriticObs, col = k % kCriticObs;
-        cw1t[col * kHidden + h] = a.critic[k];
+        cw1p[h * kActCw1Pitch + col] = a.critic[k];
     }
     for (int k = tid; k < kHidden; k += blockDim.x) {
         b1[k] = a.actor[kActorB1 + k];
@@ -703,7 +709,7 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
         for (int e = 0; e < kActEnvs; e++) z0[e] = z1[e] = 0.0f;
 #pragma unroll 4
         for (int k = 0; k < kActorObs; k++) {
-            const float wa = w1t[k * kHidden + lane], wb = w1t[k * kHidden + lane + 32];
+            const float wa = w1p[lane * kActW1Pitch + k], wb = w1p[(lane + 32) * kActW1Pitch + k];
 #pragma unroll
             for (int e = 0; e < kActEnvs; e++) {
                 const float o = my_obs[e * kActorObs + k];
@@ -716,7 +722,7 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
         for (int e = 0; e < kActEnvs; e++) y0[e] = y1[e] = 0.0f;
 #pragma unroll 4
         for (int k = 0; k < kCriticObs; k++) {
-            const float wa = cw1t[k * kHidden + lane], wb = cw1t[k * kHidden + lane + 32];
+            const float wa = cw1p[lane * kActCw1Pitch + k], wb = cw1p[(lane + 32) * kActCw1Pitch + k];
 #pragma unroll
             for (int e = 0; e < kActEnvs; e++) {
                 const float o = my_co[e * kCriticObs + k];
@@ -836,193 +842,399 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
 }
 
 // ---------------------------------------------------------------- advance
-// One thread per environment: 5 substeps of reference integration, RAPTOR
-// GRU and L2F RK4 with finiteness and sphere-contact checks, reward and
-// termination flags, bootstrap value, episode statistics and in-kernel reset
-// (sim.metal:272-332, cpu_reference.hpp:460-513). Also records the id of the
-// obstacle nearest at the step's closest approach.
-constexpr int kAdvanceThreads = 64;
+// 5 substeps of reference integration per policy step (sim.metal:272-332,
+// cpu_reference.hpp:460-513): RAPTOR GRU + L2F RK4 with finiteness and
+// sphere-contact checks, reward and termination flags, bootstrap value,
+// episode statistics and in-kernel reset; also records the id of the obstacle
+// nearest at the step's closest approach.
+//
+// G lanes advance one environment (G = 1 or 2, chosen by the host). The
+// serial chain of one environment bounds this kernel when few environments
+// share a GPU (one shard of a multi-GPU run), so with G = 2 the RAPTOR layers'
+// units (unit u on lane u % 2), its outputs and the bootstrap critic's hidden
+// units are split over a lane pair and exchanged with shuffles; the L2F RK4
+// step and the clearance scan run on both lanes on the same operands, so the
+// state needs no exchange. Every dot product keeps the one-thread order of
+// operations (same results bit for bit); only the bootstrap value's final sum
+// over hidden units is reassociated. Large shards use G = 1 (more
+// environments in flight, no redundant work).
+constexpr int kAdvanceThreads = 128;
 
-__global__ void __launch_bounds__(kAdvanceThreads, 8) k_advance(SimArgs a) {
-    __shared__ float raptor_w[2084];
-    __shared__ float critic_w[kCriticParams];
-    __shared__ mdn_physics_params params;
-    const int tid = threadIdx.x;
-    const float* rw = reinterpret_cast<const float*>(a.raptor);
-    for (int k = tid; k < 2084; k += blockDim.x) raptor_w[k] = rw[k];
-    for (int k = tid; k < kCriticParams; k += blockDim.x) critic_w[k] = a.critic[k];
-    const float* pw = reinterpret_cast<const float*>(a.physics);
-    float* pd = reinterpret_cast<float*>(&params);
-    for (int k = tid; k < 88; k += blockDim.x) pd[k] = pw[k];
-    __syncthreads();
+// Shared-memory layout of the RAPTOR weights for a group of G lanes with
+// U = 16 / G units each (unit j on lane j % G, slot j / G): for every weight
+// column the U units of one lane are adjacent, so one 16-byte load feeds four
+// FMAs and the lanes of a group read adjacent words
+// (raptor.hpp:11-21 holds the weights row-major).
+template <int G>
+struct RaptorSmem {
+    static constexpr int U = 16 / G;
+    static constexpr int kIn = 0;                 // [22 cols][G][U]   input layer
+    static constexpr int kInB = kIn + 22 * 16;    // [G][U]
+    static constexpr int kGi = kInB + 16;         // [3 gates][16 cols][G][U]
+    static constexpr int kGh = kGi + 3 * 256;     // [3 gates][16 cols][G][U]
+    static constexpr int kGiB = kGh + 3 * 256;    // [3 gates][G][U]
+    static constexpr int kGhB = kGiB + 48;        // [3 gates][G][U]
+    static constexpr int kOut = kGhB + 48;        // [4 rows][16 cols] (row-major)
+    static constexpr int kOutB = kOut + 64;       // [4]
+    static constexpr int kFloats = kOutB + 4;
+    __device__ static int slot(int unit) { return (unit % G) * U + unit / G; }
+    __device__ static void fill(float* s, const float* rw, int tid, int threads) {
+        for (int k = tid; k < 352; k += threads) s[kIn + (k % 22) * 16 + slot(k / 22)] = rw[k];
+        for (int k = tid; k < 16; k += threads) s[kInB + slot(k)] = rw[352 + k];
+        for (int k = tid; k < 768; k += threads) {
+            const int gate = k / 256, unit = (k / 16) % 16, col = k % 16;
+            s[kGi + gate * 256 + col * 16 + slot(unit)] = rw[368 + k];
+            s[kGh + gate * 256 + col * 16 + slot(unit)] = rw[1136 + k];
+        }
+        for (int k = tid; k < 48; k += threads) {
+            s[kGiB + (k / 16) * 16 + slot(k % 16)] = rw[1904 + k];
+            s[kGhB + (k / 16) * 16 + slot(k % 16)] = rw[1952 + k];
+        }
+        for (int k = tid; k < 64; k += threads) s[kOut + k] = rw[2016 + k];
+        if (tid < 4) s[kOutB + tid] = rw[2080 + tid];
+    }
+};
 
-    const uint32_t i = blockIdx.x * blockDim.x + tid;
-    const mdn_sim_config& c = a.cfg;
-    bool active = i < a.n;
-    if (active && c.eval && a.runs[i].episodes) active = false;
-    bool refill = false;
-    if (active) {
-        mdn_sim_run& run = a.runs[i];
-        const mdn_world& w = a.worlds[i];
-        const size_t row = size_t(a.tick) * a.n + i;
-        float s[17];
-        {
-            const float* sp = reinterpret_cast<const float*>(&a.states[i]);
+// U consecutive floats of shared memory (U = 1, 2, 4, 8 or 16; 16-byte
+// aligned for U >= 4) into registers.
+template <int U>
+__device__ __forceinline__ void load_units(const float* p, float (&out)[U]) {
+    if constexpr (U >= 4) {
 #pragma unroll
-            for (int k = 0; k < 17; k++) s[k] = sp[k];
+        for (int q = 0; q < U / 4; q++) {
+            const float4 v = reinterpret_cast<const float4*>(p)[q];
+            out[4 * q] = v.x; out[4 * q + 1] = v.y; out[4 * q + 2] = v.z; out[4 * q + 3] = v.w;
         }
-        float h[16], motors[4];
+    } else if constexpr (U == 2) {
+        const float2 v = *reinterpret_cast<const float2*>(p);
+        out[0] = v.x; out[1] = v.y;
+    } else {
+        out[0] = p[0];
+    }
+}
+
+// Dense(22,16)-ReLU -> GRU(16) -> Dense(16,4) (raptor.hpp:52-92) for one
+// environment on a group of G lanes. Each unit's dot products run in the
+// reference's column order, starting from the bias, so every unit's result is
+// the one a single thread computes.
+template <int G>
+__device__ __forceinline__ void raptor_forward_group(const float* __restrict__ w, const float obs[22], float h[16],
+                                                     float action[4], unsigned mask, int base, int r) {
+    using L = RaptorSmem<G>;
+    constexpr int U = L::U;
+    float xm[U];
+    load_units<U>(w + L::kInB + r * U, xm);
 #pragma unroll
-        for (int k = 0; k < 16; k++) h[k] = run.hidden[k];
+    for (int col = 0; col < 22; ++col) {
+        float wv[U];
+        load_units<U>(w + L::kIn + col * 16 + r * U, wv);
 #pragma unroll
-        for (int k = 0; k < 4; k++) motors[k] = run.motors[k];
-        const float goal[3] = {w.goal[0], w.goal[1], w.goal[2]};
-        const float before = len3(goal[0] - s[0], goal[1] - s[1], goal[2] - s[2]);
-        const float yaw = run.yaw, cy = cosf(yaw), sy = sinf(yaw);
-        const float ch = cosf(yaw * .5f), sh = sinf(yaw * .5f);
-        bool collision = false;
-        float step_clearance = 12.0f;
-        int32_t contact = -1;
-        const float wind[3] = {w.wind[0] * params.mass, w.wind[1] * params.mass, w.wind[2] * params.mass};
-        float refp[3] = {run.reference_position[0], run.reference_position[1], run.reference_position[2]};
-        const float dv_[3] = {run.desired_velocity[0], run.desired_velocity[1], run.desired_velocity[2]};
-        float path = run.path, elapsed = run.elapsed, min_clear = run.min_clearance, peak = run.peak_speed;
-        for (uint32_t step = 0; step < c.substeps; step++) {
-            float mo[22];
-            for (int j = 0; j < 3; j++) refp[j] += dv_[j] * params.dt;
-            const float dp0 = s[0] - refp[0], dp1 = s[1] - refp[1], dp2 = s[2] - refp[2];
-            const float dvx = s[7] - dv_[0], dvy = s[8] - dv_[1], dvz = s[9] - dv_[2];
-            mo[0] = clampf(cy * dp0 + sy * dp1, -.5f, .5f);
-            mo[1] = clampf(-sy * dp0 + cy * dp1, -.5f, .5f);
-            mo[2] = clampf(dp2, -.5f, .5f);
-            const float qy[4] = {ch * s[3] + sh * s[6], ch * s[4] + sh * s[5], ch * s[5] - sh * s[4], ch * s[6] - sh * s[3]};
-            float rr[9];
-            rotation(qy, rr);
+        for (int u = 0; u < U; u++) xm[u] = fmaf(wv[u], obs[col], xm[u]);
+    }
+    float x[16];
 #pragma unroll
-            for (int j = 0; j < 9; j++) mo[3 + j] = rr[j];
-            mo[12] = clampf(cy * dvx + sy * dvy, -1.0f, 1.0f);
-            mo[13] = clampf(-sy * dvx + cy * dvy, -1.0f, 1.0f);
-            mo[14] = clampf(dvz, -1.0f, 1.0f);
-            mo[15] = s[10]; mo[16] = s[11]; mo[17] = s[12];
+    for (int u = 0; u < U; u++) xm[u] = smax(xm[u], 0.0f);
 #pragma unroll
-            for (int j = 0; j < 4; j++) mo[18 + j] = motors[j];
-            raptor_forward(raptor_w, mo, h, motors);
+    for (int j = 0; j < 16; j++) {
+        if constexpr (G == 1) x[j] = xm[j];
+        else x[j] = __shfl_sync(mask, xm[j / G], base + j % G);
+    }
+    float ir[U], hr[U], iz[U], hz[U], in_[U], hn[U];
+    load_units<U>(w + L::kGiB + r * U, ir);
+    load_units<U>(w + L::kGhB + r * U, hr);
+    load_units<U>(w + L::kGiB + 16 + r * U, iz);
+    load_units<U>(w + L::kGhB + 16 + r * U, hz);
+    load_units<U>(w + L::kGiB + 32 + r * U, in_);
+    load_units<U>(w + L::kGhB + 32 + r * U, hn);
 #pragma unroll
-            for (int j = 0; j < 4; j++) motors[j] = smax(-1.0f, smin(1.0f, motors[j]));
-            float nx[17];
-            l2f_step(params, s, motors, wind, nx);
-            bool valid = true;
+    for (int col = 0; col < 16; ++col) {
+        float a0[U], a1[U], a2[U], b0[U], b1[U], b2[U];
+        load_units<U>(w + L::kGi + col * 16 + r * U, a0);
+        load_units<U>(w + L::kGi + 256 + col * 16 + r * U, a1);
+        load_units<U>(w + L::kGi + 512 + col * 16 + r * U, a2);
+        load_units<U>(w + L::kGh + col * 16 + r * U, b0);
+        load_units<U>(w + L::kGh + 256 + col * 16 + r * U, b1);
+        load_units<U>(w + L::kGh + 512 + col * 16 + r * U, b2);
 #pragma unroll
-            for (int j = 0; j < 17; j++) valid = valid && isfinite(nx[j]);
-            if (!valid) {
-                collision = true;
-                break;
-            }
-            path += len3(s[0] - nx[0], s[1] - nx[1], s[2] - nx[2]);
-#pragma unroll
-            for (int j = 0; j < 17; j++) s[j] = nx[j];
-            elapsed += params.dt;
-            int32_t id;
-            const float clearance = world_clearance_soa(a, i, s, elapsed, &id);
-            if (clearance < step_clearance) contact = id;
-            step_clearance = smin(step_clearance, clearance);
-            min_clear = smin(min_clear, clearance);
-            peak = smax(peak, len3(s[7], s[8], s[9]));
-            if (clearance <= 0 || !isfinite(s[0]) || !isfinite(s[1]) || !isfinite(s[2])) {
-                collision = true;
-                break;
-            }
-        }
-        const uint32_t steps = run.steps + 1;
-        run.steps = steps;
-        {
-            float* sp = reinterpret_cast<float*>(&a.states[i]);
-#pragma unroll
-            for (int k = 0; k < 17; k++) sp[k] = s[k];
-        }
-#pragma unroll
-        for (int k = 0; k < 16; k++) run.hidden[k] = h[k];
-#pragma unroll
-        for (int k = 0; k < 4; k++) run.motors[k] = motors[k];
-        for (int j = 0; j < 3; j++) run.reference_position[j] = refp[j];
-        run.path = path;
-        run.elapsed = elapsed;
-        run.min_clearance = min_clear;
-        run.peak_speed = peak;
-        const float after = len3(goal[0] - s[0], goal[1] - s[1], goal[2] - s[2]);
-        bool success = after < (c.mode == 20 ? .10f : .35f) && !collision;
-        bool timeout = steps >= c.max_steps;
-        a.rewards[row] = (before - after) * 2.0f - .01f - c.risk_coef * clampf((0.6f - step_clearance) / 0.6f, 0.0f, 1.0f) +
-                         (success ? 10.0f : 0.0f) - (collision ? 10.0f : 0.0f);
-        bool term = collision || success;
-        a.terminated[row] = term;
-        a.truncated[row] = timeout && !term;
-        a.contact[row] = contact;
-        if (a.task_ctl.enabled) {  // sim.metal:307-317
-            const float executed[4] = {run.desired_velocity[0], run.desired_velocity[1], run.desired_velocity[2],
-                                       run.previous_nav[3] * 0.5f};
-            const TaskStep out = task_step(a.tasks[i], a.task_ctl.config, s, s + 7, executed, collision, timeout);
-            success = out.stable_success != 0u && !collision;
-            timeout = out.timeout != 0u;
-            a.rewards[row] = out.reward;
-            term = collision || success;
-            a.terminated[row] = term;
-            a.truncated[row] = timeout && !term;
-        }
-        // Bootstrap value of the post-step critic observation (sim.metal:327).
-        {
-            float co[kCriticObs];
-            for (int j = 0; j < 3; j++) {
-                co[j] = (goal[j] - s[j]) / 10.0f;
-                co[j + 3] = s[7 + j] / 4.0f;
-                co[j + 6] = s[10 + j] / 4.0f;
-                co[j + 13] = s[j] / 10.0f;
-                co[j + 16] = (refp[j] - s[j]) * 2.0f;
-            }
-            for (int j = 0; j < 4; j++) co[9 + j] = s[3 + j];
-            co[19] = world_clearance_soa(a, i, s, elapsed, nullptr) / 5.0f;
-            co[20] = float(steps) / 200.0f;
-            for (int j = 21; j < 30; j++) co[j] = 0.0f;
-            const uint32_t m = w.count < 3u ? w.count : 3u;
-#pragma unroll
-            for (uint32_t o = 0; o < 3; o++) {
-                if (o < m) {
-                    float cc[3];
-                    const float* f = a.world_soa + size_t(o) * 10 * a.n + i;
-                    const float c3[3] = {f[a.n], f[2 * a.n], f[3 * a.n]};
-                    const float s3[3] = {f[4 * a.n], f[5 * a.n], f[6 * a.n]};
-                    const float v3[3] = {f[7 * a.n], f[8 * a.n], f[9 * a.n]};
-                    obstacle_center(__float_as_uint(f[0]), c3, s3, v3, elapsed, cc);
-                    co[21 + o * 3] = (cc[0] - s[0]) / 10.0f;
-                    co[22 + o * 3] = (cc[1] - s[1]) / 10.0f;
-                    co[23 + o * 3] = (cc[2] - s[2]) / 10.0f;
-                }
-            }
-            co[30] = w.wind[0];
-            co[31] = w.wind[1];
-            float value = 0.0f;
-            for (int hh = 0; hh < kHidden; hh++) {
-                float z = 0.0f;
-#pragma unroll
-                for (int k = 0; k < kCriticObs; k++) z = fmaf(co[k], critic_w[hh * kCriticObs + k], z);
-                value = fmaf(tanhf(z + critic_w[kCriticB1 + hh]), critic_w[kCriticW2 + hh], value);
-            }
-            a.next_values[row] = value + critic_w[kCriticB2];
-        }
-        if (success || collision || timeout) {
-            run.successes += success;
-            run.collisions += collision;
-            run.timeouts += timeout && !term;
-            run.episodes++;
-            run.success_time += success ? elapsed : 0.0f;
-            run.total_path += path;
-            run.total_elapsed += elapsed;
-            run.final_progress += 1.0f - after / smax(run.initial_distance, 1.0e-4f);
-            if (!c.eval) refill = episode_reset(a, i, false);
+        for (int u = 0; u < U; u++) {
+            ir[u] = fmaf(a0[u], x[col], ir[u]);
+            hr[u] = fmaf(b0[u], h[col], hr[u]);
+            iz[u] = fmaf(a1[u], x[col], iz[u]);
+            hz[u] = fmaf(b1[u], h[col], hz[u]);
+            in_[u] = fmaf(a2[u], x[col], in_[u]);
+            hn[u] = fmaf(b2[u], h[col], hn[u]);
         }
     }
-    const unsigned mask = __ballot_sync(0xffffffffu, refill);
-    if (mask) refill_rings(a, blockIdx.x * blockDim.x + (tid & ~31), mask);
+    float nm[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        const float reset = 1.0f / (1.0f + expf(-(ir[u] + hr[u])));
+        const float update = 1.0f / (1.0f + expf(-(iz[u] + hz[u])));
+        const float cand = tanhf(in_[u] + reset * hn[u]);
+        nm[u] = (1.0f - update) * cand + update * h[r + G * u];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        if constexpr (G == 1) h[j] = nm[j];
+        else h[j] = __shfl_sync(mask, nm[j / G], base + j % G);
+    }
+    {
+#pragma unroll
+        for (int row = 0; row < 4; ++row) {
+            float value = w[L::kOutB + row];
+#pragma unroll
+            for (int col = 0; col < 16; col += 4) {
+                const float4 ow = *reinterpret_cast<const float4*>(w + L::kOut + row * 16 + col);
+                value = fmaf(ow.x, h[col], value);
+                value = fmaf(ow.y, h[col + 1], value);
+                value = fmaf(ow.z, h[col + 2], value);
+                value = fmaf(ow.w, h[col + 3], value);
+            }
+            action[row] = value;
+        }
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(SimArgs a) {
+    using L = RaptorSmem<G>;
+    constexpr int kGroups = kAdvanceThreads / G;
+    constexpr int V = kHidden / G;             // bootstrap critic hidden units per lane
+    __shared__ __align__(16) float raptor_w[L::kFloats];
+    __shared__ __align__(16) float cw1p[kCriticObs * kHidden];  // [32 inputs][G][V] critic W1
+    __shared__ __align__(16) float cb1p[kHidden], cw2p[kHidden];  // [G][V]
+    __shared__ float cb2;
+    __shared__ mdn_physics_params params;
+    const int tid = threadIdx.x;
+    {
+        L::fill(raptor_w, reinterpret_cast<const float*>(a.raptor), tid, blockDim.x);
+        for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
+            const int hh = k / kCriticObs, col = k % kCriticObs;
+            cw1p[col * kHidden + (hh % G) * V + hh / G] = a.critic[k];
+        }
+        for (int k = tid; k < kHidden; k += blockDim.x) {
+            cb1p[(k % G) * V + k / G] = a.critic[kCriticB1 + k];
+            cw2p[(k % G) * V + k / G] = a.critic[kCriticW2 + k];
+        }
+        if (tid == 0) cb2 = a.critic[kCriticB2];
+        const float* pw = reinterpret_cast<const float*>(a.physics);
+        float* pd = reinterpret_cast<float*>(&params);
+        for (int k = tid; k < 88; k += blockDim.x) pd[k] = pw[k];
+    }
+    __syncthreads();
+
+    const int lane = tid & 31, r = lane & (G - 1), base = lane & ~(G - 1);
+    const unsigned mask = ((1u << G) - 1u) << base;
+    const int group = tid / G;
+    const mdn_sim_config& c = a.cfg;
+    for (uint32_t tile = blockIdx.x * kGroups; tile < a.n; tile += gridDim.x * kGroups) {
+        const uint32_t i = tile + group;
+        bool active = i < a.n;
+        if (active && c.eval && a.runs[i].episodes) active = false;
+        bool refill = false;
+        if (active) {
+            mdn_sim_run& run = a.runs[i];
+            const mdn_world& w = a.worlds[i];
+            const size_t row = size_t(a.tick) * a.n + i;
+            const uint32_t count = w.count < 16u ? w.count : 16u;
+            float s[17];
+            {
+                const float* sp = reinterpret_cast<const float*>(&a.states[i]);
+#pragma unroll
+                for (int k = 0; k < 17; k++) s[k] = sp[k];
+            }
+            float h[16], motors[4];
+#pragma unroll
+            for (int k = 0; k < 16; k++) h[k] = run.hidden[k];
+#pragma unroll
+            for (int k = 0; k < 4; k++) motors[k] = run.motors[k];
+            const float goal[3] = {w.goal[0], w.goal[1], w.goal[2]};
+            const float before = len3(goal[0] - s[0], goal[1] - s[1], goal[2] - s[2]);
+            const float yaw = run.yaw, cy = cosf(yaw), sy = sinf(yaw);
+            const float ch = cosf(yaw * .5f), sh = sinf(yaw * .5f);
+            bool collision = false;
+            float step_clearance = 12.0f;
+            int32_t contact = -1;
+            const float wind[3] = {w.wind[0] * params.mass, w.wind[1] * params.mass, w.wind[2] * params.mass};
+            float refp[3] = {run.reference_position[0], run.reference_position[1], run.reference_position[2]};
+            const float dv_[3] = {run.desired_velocity[0], run.desired_velocity[1], run.desired_velocity[2]};
+            float path = run.path, elapsed = run.elapsed, min_clear = run.min_clearance, peak = run.peak_speed;
+            for (uint32_t step = 0; step < c.substeps; step++) {
+                float mo[22];
+                for (int j = 0; j < 3; j++) refp[j] += dv_[j] * params.dt;
+                const float dp0 = s[0] - refp[0], dp1 = s[1] - refp[1], dp2 = s[2] - refp[2];
+                const float dvx = s[7] - dv_[0], dvy = s[8] - dv_[1], dvz = s[9] - dv_[2];
+                mo[0] = clampf(cy * dp0 + sy * dp1, -.5f, .5f);
+                mo[1] = clampf(-sy * dp0 + cy * dp1, -.5f, .5f);
+                mo[2] = clampf(dp2, -.5f, .5f);
+                const float qy[4] = {ch * s[3] + sh * s[6], ch * s[4] + sh * s[5], ch * s[5] - sh * s[4],
+                                     ch * s[6] - sh * s[3]};
+                float rr[9];
+                rotation(qy, rr);
+#pragma unroll
+                for (int j = 0; j < 9; j++) mo[3 + j] = rr[j];
+                mo[12] = clampf(cy * dvx + sy * dvy, -1.0f, 1.0f);
+                mo[13] = clampf(-sy * dvx + cy * dvy, -1.0f, 1.0f);
+                mo[14] = clampf(dvz, -1.0f, 1.0f);
+                mo[15] = s[10]; mo[16] = s[11]; mo[17] = s[12];
+#pragma unroll
+                for (int j = 0; j < 4; j++) mo[18 + j] = motors[j];
+                raptor_forward_group<G>(raptor_w, mo, h, motors, mask, base, r);
+#pragma unroll
+                for (int j = 0; j < 4; j++) motors[j] = smax(-1.0f, smin(1.0f, motors[j]));
+                float nx[17];
+                l2f_step(params, s, motors, wind, nx);
+                bool valid = true;
+#pragma unroll
+                for (int j = 0; j < 17; j++) valid = valid && isfinite(nx[j]);
+                if (!valid) {
+                    collision = true;
+                    break;
+                }
+                path += len3(s[0] - nx[0], s[1] - nx[1], s[2] - nx[2]);
+#pragma unroll
+                for (int j = 0; j < 17; j++) s[j] = nx[j];
+                elapsed += params.dt;
+                int32_t id;
+                const float clearance = world_clearance_soa(a, i, s, elapsed, &id);
+                if (clearance < step_clearance) contact = id;
+                step_clearance = smin(step_clearance, clearance);
+                min_clear = smin(min_clear, clearance);
+                peak = smax(peak, len3(s[7], s[8], s[9]));
+                if (clearance <= 0 || !isfinite(s[0]) || !isfinite(s[1]) || !isfinite(s[2])) {
+                    collision = true;
+                    break;
+                }
+            }
+            const uint32_t steps = run.steps + 1;
+            // Bootstrap value of the post-step critic observation (sim.metal:327),
+            // hidden units r, r+G, ... on lane r.
+            float value;
+            {
+                float co[kCriticObs];
+                for (int j = 0; j < 3; j++) {
+                    co[j] = (goal[j] - s[j]) / 10.0f;
+                    co[j + 3] = s[7 + j] / 4.0f;
+                    co[j + 6] = s[10 + j] / 4.0f;
+                    co[j + 13] = s[j] / 10.0f;
+                    co[j + 16] = (refp[j] - s[j]) * 2.0f;
+                }
+                for (int j = 0; j < 4; j++) co[9 + j] = s[3 + j];
+                co[19] = world_clearance_soa(a, i, s, elapsed, nullptr) / 5.0f;
+                co[20] = float(steps) / 200.0f;
+                for (int j = 21; j < 30; j++) co[j] = 0.0f;
+                const uint32_t m = count < 3u ? count : 3u;
+#pragma unroll
+                for (uint32_t o = 0; o < 3; o++) {
+                    if (o < m) {
+                        float f[10];
+#pragma unroll
+                        for (int k = 0; k < 10; k++) f[k] = __ldg(a.world_soa + size_t(o * 10 + k) * a.n + i);
+                        float cc[3];
+                        obstacle_center(__float_as_uint(f[0]), f + 1, f + 4, f + 7, elapsed, cc);
+                        co[21 + o * 3] = (cc[0] - s[0]) / 10.0f;
+                        co[22 + o * 3] = (cc[1] - s[1]) / 10.0f;
+                        co[23 + o * 3] = (cc[2] - s[2]) / 10.0f;
+                    }
+                }
+                co[30] = w.wind[0];
+                co[31] = w.wind[1];
+                float part = 0.0f;
+#pragma unroll
+                for (int v0 = 0; v0 < V; v0 += 4) {
+                    float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                    for (int k = 0; k < kCriticObs; k++) {
+                        const float4 wv = *reinterpret_cast<const float4*>(cw1p + k * kHidden + r * V + v0);
+                        z[0] = fmaf(co[k], wv.x, z[0]);
+                        z[1] = fmaf(co[k], wv.y, z[1]);
+                        z[2] = fmaf(co[k], wv.z, z[2]);
+                        z[3] = fmaf(co[k], wv.w, z[3]);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        part = fmaf(tanhf(z[q] + cb1p[r * V + v0 + q]), cw2p[r * V + v0 + q], part);
+                }
+                if constexpr (G > 1) {
+#pragma unroll
+                    for (int off = G / 2; off > 0; off >>= 1) part += __shfl_xor_sync(mask, part, off);
+                }
+                value = part + cb2;
+            }
+            if (r == 0) {
+                run.steps = steps;
+                {
+                    float* sp = reinterpret_cast<float*>(&a.states[i]);
+#pragma unroll
+                    for (int k = 0; k < 17; k++) sp[k] = s[k];
+                }
+#pragma unroll
+                for (int k = 0; k < 16; k++) run.hidden[k] = h[k];
+#pragma unroll
+                for (int k = 0; k < 4; k++) run.motors[k] = motors[k];
+                for (int j = 0; j < 3; j++) run.reference_position[j] = refp[j];
+                run.path = path;
+                run.elapsed = elapsed;
+                run.min_clearance = min_clear;
+                run.peak_speed = peak;
+                const float after = len3(goal[0] - s[0], goal[1] - s[1], goal[2] - s[2]);
+                bool success = after < (c.mode == 20 ? .10f : .35f) && !collision;
+                bool timeout = steps >= c.max_steps;
+                a.rewards[row] = (before - after) * 2.0f - .01f -
+                                 c.risk_coef * clampf((0.6f - step_clearance) / 0.6f, 0.0f, 1.0f) +
+                                 (success ? 10.0f : 0.0f) - (collision ? 10.0f : 0.0f);
+                bool term = collision || success;
+                a.terminated[row] = term;
+                a.truncated[row] = timeout && !term;
+                a.contact[row] = contact;
+                if (a.task_ctl.enabled) {  // sim.metal:307-317
+                    const float executed[4] = {run.desired_velocity[0], run.desired_velocity[1],
+                                               run.desired_velocity[2], run.previous_nav[3] * 0.5f};
+                    const float pv[6] = {s[0], s[1], s[2], s[7], s[8], s[9]};  // keeps s out of local memory
+                    const TaskStep out =
+                        task_step(a.tasks[i], a.task_ctl.config, pv, pv + 3, executed, collision, timeout);
+                    success = out.stable_success != 0u && !collision;
+                    timeout = out.timeout != 0u;
+                    a.rewards[row] = out.reward;
+                    term = collision || success;
+                    a.terminated[row] = term;
+                    a.truncated[row] = timeout && !term;
+                }
+                a.next_values[row] = value;
+                if (success || collision || timeout) {
+                    run.successes += success;
+                    run.collisions += collision;
+                    run.timeouts += timeout && !term;
+                    run.episodes++;
+                    run.success_time += success ? elapsed : 0.0f;
+                    run.total_path += path;
+                    run.total_elapsed += elapsed;
+                    run.final_progress += 1.0f - after / smax(run.initial_distance, 1.0e-4f);
+                    if (!c.eval) refill = episode_reset(a, i, false);
+                }
+            }
+        }
+        // Range rings of the environments that reset (their leader lanes),
+        // refilled by the whole warp.
+        const unsigned m = __ballot_sync(0xffffffffu, refill);
+        if (m) refill_rings_grouped(a, tile + uint32_t((tid & ~31) / G), m, G);
+    }
+}
+
+template <int G>
+static int advance_blocks_per_sm() {
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_advance<G>, kAdvanceThreads, 0) != cudaSuccess)
+        blocks = 1;
+    return blocks > 0 ? blocks : 1;
+}
+
+static cudaError_t launch_advance(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
+    switch (plan.advance_group) {
+        case 2: k_advance<2><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a); break;
+        default: k_advance<1><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a); break;
+    }
+    return cudaGetLastError();
 }
 
 // ------------------------------------------------------------- launchers
@@ -1046,26 +1258,42 @@ cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s) {
 
 size_t act_smem_bytes() { return sizeof(float) * kActSmemFloats; }
 
-cudaError_t launch_step(const SimArgs& a, int act_grid, cudaStream_t s) {
+cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
     k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
     if (a.cfg.geometry_memory)
         k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
-    k_act<<<act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
-    k_advance<<<blocks_for(a.n, kAdvanceThreads), kAdvanceThreads, 0, s>>>(a);
-    return cudaGetLastError();
+    k_act<<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
+    return launch_advance(a, plan, s);
 }
 
-cudaError_t launch_step_profiled(const SimArgs& a, int act_grid, cudaStream_t s, cudaEvent_t ev[4]) {
+cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4]) {
     cudaEventRecord(ev[0], s);
     k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
     if (a.cfg.geometry_memory)
         k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
     cudaEventRecord(ev[1], s);
-    k_act<<<act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
+    k_act<<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
     cudaEventRecord(ev[2], s);
-    k_advance<<<blocks_for(a.n, kAdvanceThreads), kAdvanceThreads, 0, s>>>(a);
+    const cudaError_t e = launch_advance(a, plan, s);
     cudaEventRecord(ev[3], s);
-    return cudaGetLastError();
+    return e;
+}
+
+// Launch shapes of one policy step for n environments. k_advance takes a lane
+// pair per environment for shards of at most 128 environments per SM (on a
+// B200: 18,944), where the per-environment chain sets its time (8,192
+// environments: 0.107 vs 0.140 ms per launch), and one lane per environment
+// above that, where occupancy does (65,536: 0.283 vs 0.406 ms).
+StepPlan plan_step(uint32_t n, int sm_count, int group_override) {
+    StepPlan p{};
+    p.act_grid = int(std::min<size_t>((size_t(n) + 31) / 32, size_t(sm_count) * 2));
+    int g = size_t(n) <= size_t(sm_count) * 128 ? 2 : 1;
+    if (group_override == 1 || group_override == 2) g = group_override;
+    p.advance_group = g;
+    const int per_sm = g == 1 ? advance_blocks_per_sm<1>() : advance_blocks_per_sm<2>();
+    const size_t need = (size_t(n) * g + kAdvanceThreads - 1) / kAdvanceThreads;
+    p.advance_grid = int(std::max<size_t>(1, std::min<size_t>(need, size_t(sm_count) * per_sm)));
+    return p;
 }
 
 // Pure FP32 FMA stream: 8 independent chains per thread, `iters` rounds.

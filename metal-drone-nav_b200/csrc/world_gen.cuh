@@ -322,6 +322,19 @@ __device__ bool reset_env(const SimArgs& a, uint32_t i, bool first) {
     return true;
 }
 
+// Refill when each environment is served by a group of `g` lanes and `mask`
+// holds the groups' leader lanes: lane l stands for environment first_env + l / g.
+__device__ __forceinline__ void refill_rings_grouped(const SimArgs& a, uint32_t first_env, unsigned mask, int g) {
+    const int lane = threadIdx.x & 31;
+    const float4 twelve = make_float4(12.0f, 12.0f, 12.0f, 12.0f);
+    while (mask) {
+        const int src = __ffs(mask) - 1;
+        mask &= mask - 1;
+        float4* ring = reinterpret_cast<float4*>(a.sensors + size_t(first_env + uint32_t(src / g)) * kFrames * kPixels);
+        for (int j = lane; j < kFrames * kPixels / 4; j += 32) ring[j] = twelve;
+    }
+}
+
 // Warp-cooperative refill of the range rings of the lanes in `mask` with 12 m.
 __device__ __forceinline__ void refill_rings(const SimArgs& a, uint32_t base_env, unsigned mask) {
     const int lane = threadIdx.x & 31;
