@@ -179,18 +179,25 @@ class Device:
 class Sim:
     """Batched environment, the reference Sim (main.mm:516-603)."""
 
-    def __init__(self, device, cfg, horizon, raptor=None, physics=None, room=None):
+    def __init__(self, device, cfg, horizon, raptor=None, physics=None, room=None, actor_hidden=None):
+        """actor_hidden: None/64 for the reference's 12,104-parameter actor, or a
+        multiple of 256 (5120 = the 967,688-parameter wide actor) evaluated on
+        the tensor cores."""
         self.device = device
         self.cfg = np.array(cfg, layouts.CONFIG)
         self.horizon = int(horizon)
         self.raptor = default_raptor() if raptor is None else np.array(raptor, layouts.RAPTOR)
         shape = None
-        if room is not None:
+        if room is not None or actor_hidden is not None:
             shape = np.zeros((), layouts.SHAPE)
             lib().mdn_rollout_shape_default(_ptr(shape))
-            shape["flags"] = 1
-            shape["room_min"] = room[:3]
-            shape["room_max"] = room[3:]
+            if room is not None:
+                shape["flags"] = 1
+                shape["room_min"] = room[:3]
+                shape["room_max"] = room[3:]
+            if actor_hidden is not None:
+                shape["actor_hidden"] = int(actor_hidden)
+        self.actor_hidden = 64 if actor_hidden is None else int(actor_hidden)
         phys = None if physics is None else np.array(physics, layouts.PARAMS)
         self.h = _P()
         check(lib().mdn_sim_create(device.h, _ptr(self.cfg), None if shape is None else _ptr(shape), self.horizon,

@@ -155,6 +155,7 @@ extern "C" int mdn_device_open(int gpu, mdn_device** out) {
         camera_tables(pixel, pool);
         cuda_check(upload_camera_tables(pixel.data(), pool.data()), "camera tables");
         cuda_check(configure_kernels(), "kernel attributes");
+        cuda_check(configure_wide_kernels(), "wide kernel attributes");
         dev->tables_ready = true;
         *out = dev.release();
     });
@@ -177,6 +178,12 @@ extern "C" int mdn_sync(mdn_device* dev, double* gpu_seconds) {
         for (mdn_sim* s : dev->sims) {
             cuda_check(cudaStreamSynchronize(s->stream), "stream synchronize");
             total += s->last_collect_ms * 1e-3;
+            if (s->wide_error) {
+                uint32_t flag = 0;
+                cuda_check(cudaMemcpy(&flag, s->wide_error, sizeof(flag), cudaMemcpyDeviceToHost), "wide error flag");
+                require(flag == 0, MDN_ERR_TIMEOUT,
+                        "wide actor kernel: a barrier wait gave up (flag " + std::to_string(flag) + ")");
+            }
         }
         cuda_check(cudaGetLastError(), "device error");
         if (gpu_seconds) *gpu_seconds = total;
@@ -221,6 +228,11 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
     a.task_ctl = task_ctl;
     a.tasks = static_cast<mdn_task_state*>(buf[MDN_BUF_TASK_STATES]);
     a.task_config_ok = task_config_ok;
+    a.actor_hidden = actor_hidden;
+    a.actor_b2 = actor_hidden * (kActorObs + 1 + kActions);
+    a.actor_log_std = a.actor_b2 + kActions;
+    a.wide_partials = wide_partials;
+    a.wide_slices = wide ? actor_hidden / 128 : 0;
     return a;
 }
 
@@ -242,9 +254,11 @@ void validate_config(const mdn_sim_config& c) {
     require(std::isfinite(c.speed) && std::isfinite(c.distance), MDN_ERR_INVALID, "SimConfig speed/distance");
 }
 
-void init_policy(std::vector<float>& actor, std::vector<float>& critic) {
-    // main.mm:548-555 / cpu_reference.hpp:89-103: seed 1789 Box-Muller draws.
-    actor.assign(kActorParams, 0.0f);
+void init_policy(std::vector<float>& actor, std::vector<float>& critic, uint32_t hidden) {
+    // main.mm:548-555 / cpu_reference.hpp:89-103: seed 1789 Box-Muller draws,
+    // with the parameter offsets of an actor `hidden` units wide (ppo.hpp:35-40).
+    const size_t b1 = size_t(hidden) * kActorObs, w2 = b1 + hidden, b2 = w2 + size_t(kActions) * hidden, ls = b2 + kActions;
+    actor.assign(actor_param_count(hidden), 0.0f);
     critic.assign(kCriticParams, 0.0f);
     uint32_t seed = 1789;
     auto normal = [&]() {
@@ -252,9 +266,9 @@ void init_policy(std::vector<float>& actor, std::vector<float>& critic) {
         const float a = std::sqrt(-2.0f * std::log(u));
         return a * std::cos(6.2831853f * unit(seed));
     };
-    for (int i = 0; i < kActorB1; i++) actor[i] = normal() * 0.04f;
-    for (int i = kActorW2; i < kActorB2; i++) actor[i] = normal() * 0.01f;
-    for (int i = 0; i < kActions; i++) actor[kActorLogStd + i] = -1.0f;
+    for (size_t i = 0; i < b1; i++) actor[i] = normal() * 0.04f;
+    for (size_t i = w2; i < b2; i++) actor[i] = normal() * 0.01f;
+    for (int i = 0; i < kActions; i++) actor[ls + i] = -1.0f;
     for (int i = 0; i < kCriticB1; i++) critic[i] = normal() * 0.15f;
     for (int i = kCriticW2; i < kCriticB2; i++) critic[i] = normal() * 0.1f;
 }
@@ -288,9 +302,12 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
                     "actor_obs_dim: this build implements the 184-input guided actor");
             require(shape->critic_obs_dim == 0 || shape->critic_obs_dim == kCriticObs, MDN_ERR_INVALID,
                     "critic_obs_dim: this build implements the 32-input critic");
-            require((shape->actor_hidden == 0 || shape->actor_hidden == kHidden) &&
-                        (shape->critic_hidden == 0 || shape->critic_hidden == kHidden),
-                    MDN_ERR_INVALID, "hidden widths: this build implements 64-unit actor and critic");
+            const uint32_t ah = shape->actor_hidden;
+            require(ah == 0 || ah == uint32_t(kHidden) || (ah % 256 == 0 && ah >= 256 && ah <= 8192), MDN_ERR_INVALID,
+                    "actor_hidden: 64, or a multiple of 256 up to 8192 (tensor-core wide actor)");
+            require(shape->critic_hidden == 0 || shape->critic_hidden == uint32_t(kHidden), MDN_ERR_INVALID,
+                    "critic_hidden: this build implements the 64-unit critic");
+            if (ah != 0) sim->shape.actor_hidden = ah;
             if (shape->flags & MDN_SHAPE_CUSTOM_ROOM) {
                 for (int j = 0; j < 3; j++) {
                     require(shape->room_max[j] > shape->room_min[j], MDN_ERR_INVALID, "room bounds");
@@ -307,6 +324,10 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
             sim->room_e[j] = (sim->room_hi[j] - sim->room_lo[j]) * 0.5f;
         }
         const size_t n = sim->n, rows = n * horizon;
+        sim->actor_hidden = sim->shape.actor_hidden;
+        sim->actor_params = actor_param_count(sim->actor_hidden);
+        const bool wide = sim->actor_hidden != uint32_t(kHidden);
+        require(!wide || rows < (size_t(1) << 31), MDN_ERR_INVALID, "wide actor: horizon x n must stay below 2^31 rows");
         size_t* b = sim->bytes;
         b[MDN_BUF_STATES] = n * sizeof(mdn_physics_state);
         b[MDN_BUF_RUNS] = n * sizeof(mdn_sim_run);
@@ -314,7 +335,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         b[MDN_BUF_SENSORS] = n * kFrames * kPixels * sizeof(float);
         b[MDN_BUF_POSES] = n * kFrames * 12 * sizeof(float);
         b[MDN_BUF_COMMANDS] = n * kFrames * kActions * sizeof(float);
-        b[MDN_BUF_ACTOR] = kActorParams * sizeof(float);
+        b[MDN_BUF_ACTOR] = size_t(sim->actor_params) * sizeof(float);
         b[MDN_BUF_CRITIC] = kCriticParams * sizeof(float);
         b[MDN_BUF_OBS] = rows * kActorObs * sizeof(float);
         b[MDN_BUF_CO] = rows * kCriticObs * sizeof(float);
@@ -341,11 +362,40 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
                 throw Error(MDN_ERR_NOMEM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
             }
         }
+        if (wide) {
+            const size_t slices = sim->actor_hidden / 128;
+            cudaError_t e = cudaMalloc(&sim->wide_partials, slices * n * 4 * sizeof(float));
+            if (e == cudaSuccess) e = cudaMalloc(&sim->wide_error, sizeof(uint32_t));
+            if (e != cudaSuccess) {
+                for (int k = 0; k < MDN_BUF_COUNT; k++) cudaFree(sim->buf[k]);
+                cudaFree(sim->world_soa);
+                cudaFree(sim->wide_partials);
+                throw Error(MDN_ERR_NOMEM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
+            }
+            cuda_check(cudaMemset(sim->wide_error, 0, sizeof(uint32_t)), "clear wide error flag");
+            sim->wide = new WideStep{};
+            const float* obs = static_cast<const float*>(sim->buf[MDN_BUF_OBS]);
+            const float* actor = static_cast<const float*>(sim->buf[MDN_BUF_ACTOR]);
+            const uint32_t h = sim->actor_hidden;
+            cuda_check(wide_make_map(&sim->wide->obs_map, obs, kActorObs, rows, kActorObs * sizeof(float), 128),
+                       "observation tensor map");
+            cuda_check(wide_make_map(&sim->wide->w1_map, actor, kActorObs, h, kActorObs * sizeof(float), 256),
+                       "actor W1 tensor map");
+            WideForwardArgs& wa = sim->wide->args;
+            wa.rows = uint32_t(n);
+            wa.row0 = 0;
+            wa.hidden = h;
+            wa.b1 = actor + size_t(h) * kActorObs;
+            wa.w2 = wa.b1 + h;
+            wa.partials = sim->wide_partials;
+            wa.error = sim->wide_error;
+            sim->wide->sm_count = dev->sm_count;
+        }
         cuda_check(cudaStreamCreateWithFlags(&sim->stream, cudaStreamNonBlocking), "cudaStreamCreate");
         cuda_check(cudaEventCreate(&sim->ev_start), "cudaEventCreate");
         cuda_check(cudaEventCreate(&sim->ev_stop), "cudaEventCreate");
         std::vector<float> actor, critic;
-        init_policy(actor, critic);
+        init_policy(actor, critic, sim->actor_hidden);
         mdn_physics_params params;
         if (physics) params = *physics;
         else mdn_physics_crazyflie_default(&params);
@@ -380,6 +430,9 @@ extern "C" int mdn_sim_destroy(mdn_sim* sim) {
         sim->release_graphs();
         for (int id = 0; id < MDN_BUF_COUNT; id++) cudaFree(sim->buf[id]);
         cudaFree(sim->world_soa);
+        cudaFree(sim->wide_partials);
+        cudaFree(sim->wide_error);
+        delete sim->wide;
         cudaEventDestroy(sim->ev_start);
         cudaEventDestroy(sim->ev_stop);
         cudaStreamDestroy(sim->stream);
@@ -421,7 +474,7 @@ extern "C" int mdn_sim_step(mdn_sim* sim, uint32_t tick) {
     return guarded([&] {
         checked(sim);
         require(tick < sim->horizon, MDN_ERR_INVALID, "tick must be below the horizon");
-        cuda_check(launch_step(sim->args(tick), sim->plan, sim->stream), "step");
+        cuda_check(launch_step(sim->args(tick), sim->plan, sim->stream, sim->wide), "step");
     });
 }
 
@@ -439,7 +492,7 @@ extern "C" int mdn_sim_collect(mdn_sim* sim, uint32_t steps) {
             cuda_check(cudaStreamBeginCapture(sim->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
             cudaError_t launch = cudaSuccess;
             for (uint32_t t = 0; t < steps && launch == cudaSuccess; t++)
-                launch = launch_step(sim->args(t % sim->horizon), sim->plan, sim->stream);
+                launch = launch_step(sim->args(t % sim->horizon), sim->plan, sim->stream, sim->wide);
             const cudaError_t end = cudaStreamEndCapture(sim->stream, &graph);
             cuda_check(launch, "capture step");
             cuda_check(end, "end capture");
@@ -528,7 +581,7 @@ extern "C" int mdn_sim_dims(mdn_sim* sim, uint32_t* n, uint32_t* horizon, uint32
         checked(sim);
         if (n) *n = sim->n;
         if (horizon) *horizon = sim->horizon;
-        if (actor_params) *actor_params = kActorParams;
+        if (actor_params) *actor_params = sim->actor_params;
         if (critic_params) *critic_params = kCriticParams;
     });
 }
@@ -539,7 +592,7 @@ extern "C" int mdn_sim_profile_step(mdn_sim* sim, uint32_t tick, float ms[3]) {
         require(ms != nullptr && tick < sim->horizon, MDN_ERR_INVALID, "profile_step: bad argument");
         cudaEvent_t ev[4];
         for (auto& e : ev) cuda_check(cudaEventCreate(&e), "event");
-        const cudaError_t launch = launch_step_profiled(sim->args(tick), sim->plan, sim->stream, ev);
+        const cudaError_t launch = launch_step_profiled(sim->args(tick), sim->plan, sim->stream, ev, sim->wide);
         const cudaError_t wait = cudaEventSynchronize(ev[3]);
         for (int k = 0; k < 3 && launch == cudaSuccess && wait == cudaSuccess; k++) cudaEventElapsedTime(&ms[k], ev[k], ev[k + 1]);
         for (auto& e : ev) cudaEventDestroy(e);

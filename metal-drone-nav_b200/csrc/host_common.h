@@ -10,6 +10,7 @@
 
 #include "mdn.h"
 #include "mdn_shared.h"
+#include "wide.h"
 
 namespace mdn {
 
@@ -50,11 +51,12 @@ cudaError_t configure_kernels();
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s);
 cudaError_t launch_world_mirror(const SimArgs& a, cudaStream_t s);
 StepPlan plan_step(uint32_t n, int sm_count, int group_override);
-cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s);
+cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s, const WideStep* wide);
 size_t act_smem_bytes();
-cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4]);
+cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4],
+                                 const WideStep* wide);
 cudaError_t fp32_peak(int sm_count, double* tflops);
-int kernels_per_step(const mdn_sim_config& c);
+int kernels_per_step(const mdn_sim_config& c, bool wide);
 
 }  // namespace mdn
 
@@ -77,6 +79,11 @@ struct mdn_sim {
     cudaStream_t stream = nullptr;
     void* buf[MDN_BUF_COUNT] = {};
     float* world_soa = nullptr;  // device mirror of the worlds, structure of arrays
+    uint32_t actor_hidden = mdn::kHidden;                   // 64, or a wide actor (multiple of 256)
+    uint32_t actor_params = mdn::actor_param_count(mdn::kHidden);
+    float* wide_partials = nullptr;                         // [hidden/128][n][4] slice sums of the wide forward
+    uint32_t* wide_error = nullptr;                         // barrier-timeout flag of the wide kernels
+    mdn::WideStep* wide = nullptr;                          // tensor maps + launch arguments (wide actors)
     size_t bytes[MDN_BUF_COUNT] = {};
     float room_lo[3], room_hi[3], room_c[3], room_e[3];
     mdn::StepPlan plan;

@@ -26,6 +26,8 @@ constexpr int kCriticParams = kCriticB2 + 1;
 constexpr float kLogTwoPi = 1.8378770664093453f;
 constexpr float kTanV = 0.75f;  // legacy camera, sensor_profile.hpp:44-45
 constexpr int kWorldSoaWords = 161;
+// Flat actor parameter count at hidden width h (ppo.hpp:35-40).
+constexpr uint32_t actor_param_count(uint32_t h) { return h * kActorObs + h + kActions * h + 2 * kActions; }
 
 // Launch shapes of one policy step (rollout.cu plan_step).
 struct StepPlan {
@@ -69,6 +71,13 @@ struct SimArgs {
     mdn_task_control task_ctl;  // goal-arrival tasks (enabled = 0: legacy episodes)
     mdn_task_state* tasks;
     uint32_t task_config_ok;  // host-side navigation_generate_task config checks (:347-379) passed
+    // Actor shape: hidden width and the offsets of b2 / log_std in the flat
+    // parameter vector (ppo.hpp:35-40). Wide actors (hidden > 64) are evaluated
+    // by the tensor-core forward, which leaves per-slice output sums in
+    // wide_partials[wide_slices][n][4]; k_act adds them up.
+    uint32_t actor_hidden, actor_b2, actor_log_std;
+    const float* wide_partials;
+    uint32_t wide_slices;
 };
 
 }  // namespace mdn

@@ -90,6 +90,7 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
         require(sim && out, MDN_ERR_INVALID, "mdn_ppo_create: null argument");
         cuda_check(cudaSetDevice(sim->dev->gpu), "cudaSetDevice");
         require(epochs >= 1 && epochs <= 4, MDN_ERR_INVALID, "PPO epochs must be 1..4");  // main.mm:1160
+        require(sim->wide == nullptr, MDN_ERR_INVALID, "PPO update of a wide actor: not available in this build");
         auto t = std::make_unique<mdn_ppo>();
         t->sim = sim;
         t->epochs = epochs;
@@ -517,7 +518,7 @@ extern "C" int mdn_launch_counts(mdn_sim* sim, mdn_ppo* t, uint32_t* per_policy_
     return guarded([&] {
         if (per_policy_step) {
             require(sim != nullptr, MDN_ERR_INVALID, "launch counts: null simulator");
-            *per_policy_step = uint32_t(kernels_per_step(sim->cfg));
+            *per_policy_step = uint32_t(kernels_per_step(sim->cfg, sim->wide != nullptr));
         }
         if (per_update) {
             require(t != nullptr, MDN_ERR_INVALID, "launch counts: null trainer");

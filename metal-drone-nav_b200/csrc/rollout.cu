@@ -12,6 +12,7 @@
 
 #include "mdn_device.cuh"
 #include "task.cuh"
+#include "wide.h"
 #include "world_gen.cuh"
 
 namespace mdn {
@@ -669,23 +670,26 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
     float* cb2 = cw2 + kHidden;                       // [1]
     float* rows = cb2 + 1;                            // per warp: obs[4][184], co[4][32]
     const int tid = threadIdx.x;
-    for (int k = tid; k < kActorObs * kHidden; k += blockDim.x) {
-        const int h = k / kActorObs, col = k % kActorObs;
-        w1p[h * kActW1Pitch + col] = a.actor[k];
-    }
+    const bool wide = a.wide_slices != 0;  // actor mean from the tensor-core forward's slice sums
+    if (!wide)
+        for (int k = tid; k < kActorObs * kHidden; k += blockDim.x) {
+            const int h = k / kActorObs, col = k % kActorObs;
+            w1p[h * kActW1Pitch + col] = a.actor[k];
+        }
     for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
         const int h = k / kCriticObs, col = k % kCriticObs;
         cw1p[h * kActCw1Pitch + col] = a.critic[k];
     }
     for (int k = tid; k < kHidden; k += blockDim.x) {
-        b1[k] = a.actor[kActorB1 + k];
+        if (!wide) b1[k] = a.actor[kActorB1 + k];
         cb1[k] = a.critic[kCriticB1 + k];
         cw2[k] = a.critic[kCriticW2 + k];
     }
-    for (int k = tid; k < kActions * kHidden; k += blockDim.x) w2[k] = a.actor[kActorW2 + k];
+    if (!wide)
+        for (int k = tid; k < kActions * kHidden; k += blockDim.x) w2[k] = a.actor[kActorW2 + k];
     if (tid < kActions) {
-        b2[tid] = a.actor[kActorB2 + tid];
-        log_std[tid] = a.actor[kActorLogStd + tid];
+        b2[tid] = a.actor[a.actor_b2 + tid];
+        log_std[tid] = a.actor[a.actor_log_std + tid];
     }
     if (tid == 0) cb2[0] = a.critic[kCriticB2];
     __syncthreads();
@@ -708,7 +712,7 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
 #pragma unroll
         for (int e = 0; e < kActEnvs; e++) z0[e] = z1[e] = 0.0f;
 #pragma unroll 4
-        for (int k = 0; k < kActorObs; k++) {
+        for (int k = 0; k < (wide ? 0 : kActorObs); k++) {
             const float wa = w1p[lane * kActW1Pitch + k], wb = w1p[(lane + 32) * kActW1Pitch + k];
 #pragma unroll
             for (int e = 0; e < kActEnvs; e++) {
@@ -730,16 +734,46 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
                 y1[e] = fmaf(o, wb, y1[e]);
             }
         }
-        // heads: every lane ends with all four environments' means and values
+        // heads: lane e ends with environment e's means and value
         float mean_mine[4] = {0, 0, 0, 0}, value_mine = 0.0f;
+        if (wide) {
+            // Wide actor: lanes 8e..8e+7 add environment e's slice sums (slice
+            // q, q+8, ... on lane 8e+q), then a fixed three-level tree.
+            const int e = lane >> 3, q = lane & 7;
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (e < envs)
+                for (uint32_t sl = q; sl < a.wide_slices; sl += 8) {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(a.wide_partials) + size_t(sl) * a.n + base + e);
+                    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                }
+#pragma unroll
+            for (int off = 4; off > 0; off >>= 1) {
+                acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
+                acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
+                acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
+                acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
+            }
+            const int src = (lane & 3) * 8;  // lane e < 4 takes group e's total
+            const float s0 = __shfl_sync(0xffffffffu, acc.x, src), s1 = __shfl_sync(0xffffffffu, acc.y, src);
+            const float s2 = __shfl_sync(0xffffffffu, acc.z, src), s3 = __shfl_sync(0xffffffffu, acc.w, src);
+            if (lane < kActEnvs) {
+                const float* pr = my_obs + lane * kActorObs + kActorObs - 3;  // ppo.hpp:77 geometry prior
+                mean_mine[0] = s0 + b2[0] + pr[0];
+                mean_mine[1] = s1 + b2[1] + pr[1];
+                mean_mine[2] = s2 + b2[2] + pr[2];
+                mean_mine[3] = s3 + b2[3];
+            }
+        }
 #pragma unroll
         for (int e = 0; e < kActEnvs; e++) {
-            const float h0 = tanhf(z0[e] + b1[lane]), h1 = tanhf(z1[e] + b1[lane + 32]);
+            if (!wide) {
+                const float h0 = tanhf(z0[e] + b1[lane]), h1 = tanhf(z1[e] + b1[lane + 32]);
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                float m = warp_sum(fmaf(h0, w2[j * kHidden + lane], h1 * w2[j * kHidden + lane + 32])) + b2[j];
-                if (j < 3) m += my_obs[e * kActorObs + kActorObs - 3 + j];
-                if (lane == e) mean_mine[j] = m;
+                for (int j = 0; j < 4; j++) {
+                    float m = warp_sum(fmaf(h0, w2[j * kHidden + lane], h1 * w2[j * kHidden + lane + 32])) + b2[j];
+                    if (j < 3) m += my_obs[e * kActorObs + kActorObs - 3 + j];
+                    if (lane == e) mean_mine[j] = m;
+                }
             }
             const float v = warp_sum(fmaf(tanhf(y0[e] + cb1[lane]), cw2[lane],
                                           tanhf(y1[e] + cb1[lane + 32]) * cw2[lane + 32])) + cb2[0];
@@ -1258,20 +1292,33 @@ cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s) {
 
 size_t act_smem_bytes() { return sizeof(float) * kActSmemFloats; }
 
-cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
+// The wide actor's tensor-core forward over this tick's observation rows.
+static cudaError_t launch_wide(const SimArgs& a, const WideStep* wide, cudaStream_t s) {
+    if (!wide) return cudaSuccess;
+    WideForwardArgs p = wide->args;
+    p.row0 = a.tick * a.n;
+    return launch_wide_forward(wide->obs_map, wide->w1_map, p, wide->sm_count, s);
+}
+
+cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s, const WideStep* wide) {
     k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
     if (a.cfg.geometry_memory)
         k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
+    cudaError_t e = launch_wide(a, wide, s);
+    if (e != cudaSuccess) return e;
     k_act<<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
     return launch_advance(a, plan, s);
 }
 
-cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4]) {
+cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4],
+                                 const WideStep* wide) {
     cudaEventRecord(ev[0], s);
     k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
     if (a.cfg.geometry_memory)
         k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
     cudaEventRecord(ev[1], s);
+    const cudaError_t we = launch_wide(a, wide, s);
+    if (we != cudaSuccess) return we;
     k_act<<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
     cudaEventRecord(ev[2], s);
     const cudaError_t e = launch_advance(a, plan, s);
@@ -1339,7 +1386,7 @@ cudaError_t fp32_peak(int sm_count, double* tflops) {
     return e;
 }
 
-int kernels_per_step(const mdn_sim_config& c) { return c.geometry_memory ? 4 : 3; }
+int kernels_per_step(const mdn_sim_config& c, bool wide) { return 3 + (c.geometry_memory ? 1 : 0) + (wide ? 1 : 0); }
 
 cudaError_t configure_kernels() {
     cudaError_t e = cudaFuncSetAttribute(k_act, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));

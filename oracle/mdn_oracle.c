@@ -2017,3 +2017,59 @@ void o_sim_rows_grad(o_sim* s, const uint32_t* rows, uint32_t count, float batch
         cg[C_B2] += dv;
     }
 }
+
+/* ----------------------------------------------------------- wide actor */
+/* The one-hidden-layer tanh actor of ppo.hpp:65-80 at hidden width `hidden`
+ * (the reference builds it with FIXED_PPO_HIDDEN_DIM; 5120 gives its
+ * 967,688-parameter actor, navigation_wide_deployment.hpp:54-66). Parameter
+ * offsets as ppo.hpp:35-40 with that width. */
+uint32_t o_wide_param_count(uint32_t hidden) { return hidden * AOBS + hidden + ACT * hidden + ACT + ACT; }
+
+/* main.mm:548-555 for an actor of width `hidden` and the 64-unit critic: one
+ * seed-1789 stream, actor W1, actor W2, critic W1, critic W2 in that order. */
+void o_wide_init(uint32_t hidden, float* actor, float* critic) {
+    const size_t b1 = (size_t)hidden * AOBS, w2 = b1 + hidden, b2 = w2 + (size_t)ACT * hidden, ls = b2 + ACT;
+    memset(actor, 0, o_wide_param_count(hidden) * sizeof(float));
+    memset(critic, 0, C_P * sizeof(float));
+    uint32_t seed = 1789;
+    for (size_t i = 0; i < b1; i++) {
+        const float u = smax(o_wurand(&seed), 1.0e-7f);
+        const float a = sqrtf(-2.0f * logf(u));
+        actor[i] = a * cosf(6.2831853f * o_wurand(&seed)) * 0.04f;
+    }
+    for (size_t i = w2; i < b2; i++) {
+        const float u = smax(o_wurand(&seed), 1.0e-7f);
+        const float a = sqrtf(-2.0f * logf(u));
+        actor[i] = a * cosf(6.2831853f * o_wurand(&seed)) * 0.01f;
+    }
+    for (size_t i = 0; i < ACT; i++) actor[ls + i] = -1.0f;
+    for (size_t i = 0; i < C_B1; i++) {
+        const float u = smax(o_wurand(&seed), 1.0e-7f);
+        const float a = sqrtf(-2.0f * logf(u));
+        critic[i] = a * cosf(6.2831853f * o_wurand(&seed)) * 0.15f;
+    }
+    for (size_t i = C_W2; i < C_B2; i++) {
+        const float u = smax(o_wurand(&seed), 1.0e-7f);
+        const float a = sqrtf(-2.0f * logf(u));
+        critic[i] = a * cosf(6.2831853f * o_wurand(&seed)) * 0.1f;
+    }
+}
+
+/* fixed_ppo::actor_forward, ppo.hpp:65-80: z starts at the bias, in-order dot
+ * product, tanh; mean = b2 + W2 . hidden (+ the geometry prior for a < 3). */
+void o_wide_actor_forward(uint32_t hidden, const float* obs, const float* actor, float* hid, float* mean) {
+    const size_t b1 = (size_t)hidden * AOBS, w2 = b1 + hidden, b2 = w2 + (size_t)ACT * hidden;
+    for (uint32_t h = 0; h < hidden; h++) {
+        float z = actor[b1 + h];
+        const float* row = actor + (size_t)h * AOBS;
+        for (uint32_t i = 0; i < AOBS; i++) z += row[i] * obs[i];
+        hid[h] = tanhf(z);
+    }
+    for (uint32_t a = 0; a < ACT; a++) {
+        float z = actor[b2 + a];
+        const float* row = actor + w2 + (size_t)a * hidden;
+        for (uint32_t h = 0; h < hidden; h++) z += row[h] * hid[h];
+        if (a < 3) z += obs[AOBS - 3 + a];
+        mean[a] = z;
+    }
+}

@@ -90,6 +90,10 @@ void o_sim_train_rollout(o_sim* s, uint32_t minibatch, uint32_t epochs, const ui
                          const float* b1corr, const float* b2corr, float* out, float* grad_norms);
 uint32_t o_actor_param_count(void);
 uint32_t o_critic_param_count(void);
+/* wide actor (ppo.hpp:65-80 at hidden width `hidden`) */
+uint32_t o_wide_param_count(uint32_t hidden);
+void o_wide_init(uint32_t hidden, float* actor, float* critic);
+void o_wide_actor_forward(uint32_t hidden, const float* obs, const float* actor, float* hid, float* mean);
 void o_set_threads(int n);
 
 #ifdef __cplusplus

@@ -85,6 +85,23 @@ def load_oracle():
     d("o_task_apply_start", None, _P, _P)
     d("o_task_step", None, _P, _P, _P, _P, _P, _U, _U, _P)
     d("o_task_segment_clearance", _F, _P, _P, _P, _P)
+    d("o_wide_param_count", _U, _U)
+    d("o_wide_init", None, _U, _P, _P)
+    d("o_wide_actor_forward", None, _U, _P, _P, _P, _P)
+    return lib
+
+
+def load_ref_wide():
+    """ppo.hpp compiled at the wide actor's shape (oracle/_ref/libref_wide.so),
+    or None when it was never built (no reference sources)."""
+    so = HERE / "_ref" / "libref_wide.so"
+    if not so.exists():
+        return None
+    lib = ctypes.CDLL(str(so))
+    d = lambda n, r, *a: _declare(lib, n, r, *a)
+    d("refw_hidden", _U)
+    d("refw_actor_param_count", _U)
+    d("refw_actor_forward", None, _P, _P, _U, _P, _P)
     return lib
 
 
