@@ -203,6 +203,9 @@ class Sim:
         check(lib().mdn_sim_create(device.h, _ptr(self.cfg), None if shape is None else _ptr(shape), self.horizon,
                                    _ptr(self.raptor), None if phys is None else _ptr(phys), ctypes.byref(self.h)))
         self.n = int(self.cfg["n"])
+        dims = [_U() for _ in range(4)]
+        check(lib().mdn_sim_dims(self.h, *[ctypes.byref(d) for d in dims]))
+        self.actor_params = int(dims[2].value)
 
     def close(self):
         if self.h:
@@ -307,7 +310,7 @@ class PPOTrainer:
         check(lib().mdn_ppo_set_state(self.h, optimizer_step, completed_rollouts))
 
     def moments(self, which):
-        n = layouts.ACTOR_PARAMS if which < 2 else layouts.CRITIC_PARAMS
+        n = self.sim.actor_params if which < 2 else layouts.CRITIC_PARAMS
         out = np.zeros(n, np.float32)
         check(lib().mdn_ppo_moments(self.h, which, _ptr(out), n, 0))
         return out

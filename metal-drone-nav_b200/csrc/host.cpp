@@ -381,7 +381,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
                        "observation tensor map");
             cuda_check(wide_make_map(&sim->wide->w1_map, actor, kActorObs, h, kActorObs * sizeof(float), 256),
                        "actor W1 tensor map");
-            WideForwardArgs& wa = sim->wide->args;
+            WideRowsArgs& wa = sim->wide->args;
             wa.rows = uint32_t(n);
             wa.row0 = 0;
             wa.hidden = h;

@@ -150,23 +150,26 @@ __global__ void __launch_bounds__(kMbThreads) k_mb_forward(PpoArgs p, uint32_t u
     const int tid = threadIdx.x;
     const float* actor = p.actor;
     const float* critic = p.critic;
-    for (int k = tid; k < kActorObs * kHidden; k += kMbThreads) {
-        const int h = k / kActorObs, c = k % kActorObs;
-        w1t[c * kHidden + h] = actor[k];
-    }
+    const bool wide = p.wide_slices != 0;
+    if (!wide)
+        for (int k = tid; k < kActorObs * kHidden; k += kMbThreads) {
+            const int h = k / kActorObs, c = k % kActorObs;
+            w1t[c * kHidden + h] = actor[k];
+        }
     for (int k = tid; k < kCriticObs * kHidden; k += kMbThreads) {
         const int h = k / kCriticObs, c = k % kCriticObs;
         cw1t[c * kHidden + h] = critic[k];
     }
-    for (int k = tid; k < 4 * kHidden; k += kMbThreads) w2[k] = actor[kActorW2 + k];
+    if (!wide)
+        for (int k = tid; k < 4 * kHidden; k += kMbThreads) w2[k] = actor[kActorW2 + k];
     if (tid < kHidden) {
-        b1[tid] = actor[kActorB1 + tid];
+        if (!wide) b1[tid] = actor[kActorB1 + tid];
         cb1[tid] = critic[kCriticB1 + tid];
         cw2[tid] = critic[kCriticW2 + tid];
     }
     if (tid < 4) {
-        b2[tid] = actor[kActorB2 + tid];
-        log_std[tid] = actor[kActorLogStd + tid];
+        b2[tid] = actor[p.actor_b2 + tid];
+        log_std[tid] = actor[p.actor_log_std + tid];
         sums[tid] = 0.0f;
     }
     if (tid == 0) cb2[0] = critic[kCriticB2];
@@ -181,7 +184,7 @@ __global__ void __launch_bounds__(kMbThreads) k_mb_forward(PpoArgs p, uint32_t u
         const float* og = p.obs + (size_t(begin) + tile) * kActorObs;
         for (int k = tid; k < kMbRows * kActorObs; k += kMbThreads) {
             const int r = k / kActorObs, c = k % kActorObs;
-            obs_t[r * kObsPitch + c] = r < int(rows) ? og[k] : 0.0f;
+            if (!wide || c >= kActorObs - 3) obs_t[r * kObsPitch + c] = r < int(rows) ? og[k] : 0.0f;
         }
         const float* cg = p.co + (size_t(begin) + tile) * kCriticObs;
         for (int k = tid; k < kMbRows * kCriticObs; k += kMbThreads) {
@@ -195,7 +198,7 @@ __global__ void __launch_bounds__(kMbThreads) k_mb_forward(PpoArgs p, uint32_t u
         for (int r = 0; r < 4; r++)
 #pragma unroll
             for (int h = 0; h < 4; h++) acc[r][h] = 0.0f;
-        for (int k = 0; k < kActorObs; k++) {
+        for (int k = 0; k < (wide ? 0 : kActorObs); k++) {
             const float4 w = *reinterpret_cast<const float4*>(&w1t[k * kHidden + 4 * hg]);
 #pragma unroll
             for (int r = 0; r < 4; r++) {
@@ -234,13 +237,31 @@ __global__ void __launch_bounds__(kMbThreads) k_mb_forward(PpoArgs p, uint32_t u
                 chid[h] = tanhf(cacc[r][h] + cb1[4 * hg + h]);
             }
             float mean[4];
+            if (wide) {
+                // slice sums of the tensor-core forward: slices hg, hg+16, ... on
+                // lane hg of the half-warp, then the fixed half-warp tree
+                float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (valid)
+                    for (uint32_t sl = hg; sl < p.wide_slices; sl += 16) {
+                        const float4 v = *reinterpret_cast<const float4*>(
+                            p.wide_partials + (size_t(sl) * p.wide_rows_cap + grow) * 4);
+                        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                    }
+                const float sm4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
-            for (int a = 0; a < 4; a++) {
-                float part = 0.0f;
+                for (int a = 0; a < 4; a++) {
+                    mean[a] = half_warp_sum(sm4[a]) + b2[a];
+                    if (a < 3) mean[a] += obs_t[lr * kObsPitch + kActorObs - 3 + a];
+                }
+            } else {
 #pragma unroll
-                for (int h = 0; h < 4; h++) part = fmaf(hid[h], w2[a * kHidden + 4 * hg + h], part);
-                mean[a] = half_warp_sum(part) + b2[a];
-                if (a < 3) mean[a] += obs_t[lr * kObsPitch + kActorObs - 3 + a];
+                for (int a = 0; a < 4; a++) {
+                    float part = 0.0f;
+#pragma unroll
+                    for (int h = 0; h < 4; h++) part = fmaf(hid[h], w2[a * kHidden + 4 * hg + h], part);
+                    mean[a] = half_warp_sum(part) + b2[a];
+                    if (a < 3) mean[a] += obs_t[lr * kObsPitch + kActorObs - 3 + a];
+                }
             }
             float vpart = 0.0f;
 #pragma unroll
@@ -322,8 +343,10 @@ __global__ void __launch_bounds__(kMbThreads) k_mb_forward(PpoArgs p, uint32_t u
                     chp[h] = chid[h];
                     cdp[h] = dvalue * cw2[4 * hg + h] * (1.0f - chid[h] * chid[h]);
                 }
-                *reinterpret_cast<float4*>(p.mb_ah + grow * kHidden + 4 * hg) = hv;
-                *reinterpret_cast<float4*>(p.mb_adelta + grow * kHidden + 4 * hg) = dh;
+                if (!wide) {
+                    *reinterpret_cast<float4*>(p.mb_ah + grow * kHidden + 4 * hg) = hv;
+                    *reinterpret_cast<float4*>(p.mb_adelta + grow * kHidden + 4 * hg) = dh;
+                }
                 *reinterpret_cast<float4*>(p.mb_ch + grow * kHidden + 4 * hg) = chv;
                 *reinterpret_cast<float4*>(p.mb_cdelta + grow * kHidden + 4 * hg) = cdh;
             }
@@ -398,8 +421,9 @@ __global__ void __launch_bounds__(kGradThreads) k_mb_grad(PpoArgs p, uint32_t up
         }
         if (tid < kGradTile) dvt[tid] = tid < int(nr) ? p.mb_dv[size_t(r0) + tid] : 0.0f;
         __syncthreads();
+        const bool wide = p.wide_slices != 0;  // actor W1/W2/b1 come from the tensor-core backward
         for (int r = 0; r < int(nr); r++) {
-            if (tid < kActorObs) {
+            if (tid < kActorObs && !wide) {
                 const float o = otile[r][tid];
 #pragma unroll
                 for (int h = 0; h < kHidden; h++) aw1[h] = fmaf(dtile[r][h], o, aw1[h]);
@@ -414,7 +438,7 @@ __global__ void __launch_bounds__(kGradThreads) k_mb_grad(PpoArgs p, uint32_t up
                 const int h = e / kCriticObs, c = e % kCriticObs;
                 cw1acc[j] = fmaf(cdtile[r][h], cotile[r][c], cw1acc[j]);
             }
-            if (tid < 64) misc += dtile[r][tid];
+            if (tid < 64) misc += wide ? 0.0f : dtile[r][tid];
             else if (tid < 128) misc += cdtile[r][tid - 64];
             else if (tid < 192) misc = fmaf(dvt[r], chtile[r][tid - 128], misc);
             else if (tid < 196) misc += dmt[r][tid - 192];
@@ -451,9 +475,10 @@ __global__ void k_grad_reduce(PpoArgs p, uint32_t chunks) {
 constexpr int kAdamThreads = 1024;
 constexpr int kAdamPerThread = (kActorParams + kAdamThreads - 1) / kAdamThreads;  // 12
 
-__global__ void __launch_bounds__(kAdamThreads) k_clip_adam(PpoArgs p, uint32_t update, const float* grad_src) {
+__global__ void __launch_bounds__(kAdamThreads) k_clip_adam(PpoArgs p, uint32_t update, const float* grad_src,
+                                                             int first_net) {
     __shared__ float red[32];
-    const int net = blockIdx.x;  // 0 actor, 1 critic
+    const int net = blockIdx.x + first_net;  // 0 actor, 1 critic
     const int count = net == 0 ? kActorParams : kCriticParams;
     const int base = net == 0 ? 0 : kActorParams;
     float* params = net == 0 ? p.actor : p.critic;
@@ -499,7 +524,7 @@ __global__ void __launch_bounds__(kAdamThreads) k_clip_adam(PpoArgs p, uint32_t 
         if (net == 0 && i >= kActorLogStd) pi = clampf(pi, -2.0f, 0.5f);  // ppo_clip_log_std, main.mm:934-940
         params[i] = pi;
     }
-    if (net == 0 && tid < 4) {
+    if (blockIdx.x == 0 && tid < 4) {
         float s = 0.0f;
         for (uint32_t c = 0; c < p.fwd_grid; c++) s += p.loss_partials[(size_t(update) * p.fwd_grid + c) * 4 + tid];
         if (tid == 3) s /= float(p.batch[update]);  // mean ratio, main.mm:949
@@ -553,7 +578,12 @@ cudaError_t launch_minibatch(const PpoArgs& p, uint32_t update, uint32_t chunks,
     return cudaGetLastError();
 }
 cudaError_t launch_clip_adam(const PpoArgs& p, uint32_t update, uint32_t chunks, cudaStream_t s) {
-    k_clip_adam<<<2, kAdamThreads, 0, s>>>(p, update, chunks > 1 ? p.grad : p.grad_partials);
+    k_clip_adam<<<2, kAdamThreads, 0, s>>>(p, update, chunks > 1 ? p.grad : p.grad_partials, 0);
+    return cudaGetLastError();
+}
+cudaError_t launch_clip_adam_critic(const PpoArgs& p, uint32_t update, const float* grad_critic, cudaStream_t s) {
+    // k_clip_adam reads the critic at grad_src[kActorParams + i].
+    k_clip_adam<<<1, kAdamThreads, 0, s>>>(p, update, grad_critic - kActorParams, 1);
     return cudaGetLastError();
 }
 cudaError_t launch_metrics_mean(const PpoArgs& p, uint32_t updates, cudaStream_t s) {

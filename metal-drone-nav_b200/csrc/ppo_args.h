@@ -50,6 +50,13 @@ struct PpoArgs {
     float* metric_mean;           // [4]
     float* grad_norms;            // [updates][2]
     uint32_t fwd_grid, grad_chunk;
+    // Actor shape (ppo.hpp:35-40): offsets of b2 and log_std. A wide actor
+    // (wide_slices != 0) takes its means from the tensor-core forward's slice
+    // sums wide_partials[wide_slices][wide_rows_cap][4]; the loss and gradient
+    // kernels then handle only the critic, b2 and log_std.
+    uint32_t actor_b2, actor_log_std;
+    const float* wide_partials;
+    uint32_t wide_slices, wide_rows_cap;
 };
 
 cudaError_t configure_ppo_kernels();
@@ -61,6 +68,9 @@ cudaError_t launch_adv_sq(const PpoArgs& p, cudaStream_t s);
 cudaError_t launch_adv_apply(const PpoArgs& p, int sm_count, cudaStream_t s);
 cudaError_t launch_minibatch(const PpoArgs& p, uint32_t update, uint32_t chunks, cudaStream_t s);
 cudaError_t launch_clip_adam(const PpoArgs& p, uint32_t update, uint32_t chunks, cudaStream_t s);
+// Critic-only clip + Adam (plus the update's metric row) reading the critic
+// gradient at grad_critic; the wide actor's step runs in wide.cu.
+cudaError_t launch_clip_adam_critic(const PpoArgs& p, uint32_t update, const float* grad_critic, cudaStream_t s);
 cudaError_t launch_metrics_mean(const PpoArgs& p, uint32_t updates, cudaStream_t s);
 
 }  // namespace mdn

@@ -47,6 +47,17 @@ struct mdn_ppo {
     cudaGraphExec_t graph = nullptr;
     float last_update_ms = 0.0f;
     uint32_t launches = 0;  // kernel nodes in the update graph
+    // wide actor (tensor-core update, wide.cu)
+    bool wide = false;
+    uint32_t wide_splits = 0, wide_groups = 0;
+    void* wide_mem = nullptr;
+    float* wide_partials = nullptr;   // [hidden/128][minibatch][4] forward slice sums
+    float* wide_delta = nullptr;      // [ceil128(minibatch)][hidden] hidden deltas
+    float* wide_w1_parts = nullptr;   // [splits][hidden][184] dW1 partials
+    float* wide_colsums = nullptr;    // [groups][5][hidden] db1 / dW2 partials
+    float* wide_grad = nullptr;       // [actor params + critic params]
+    float* wide_norm_parts = nullptr; // [2 * SMs]
+    WideMap obs32_map{}, delta_map{};
 };
 
 namespace {
@@ -77,6 +88,66 @@ void enqueue_update(mdn_ppo* t) {
     const bool multi = dev->world > 1;
     const uint32_t chunks = multi ? std::max<uint32_t>(t->grad_chunks, 2) : t->grad_chunks;
     for (uint32_t u = 0; u < t->updates; u++) {
+        if (t->wide) {
+            // Wide actor: tensor-core forward -> loss (+ critic, b2, log_std
+            // gradients) -> tensor-core backward (deltas, db1/dW2 partials) ->
+            // dW1 = delta^T obs -> flat gradient -> [allreduce] -> clip + Adam.
+            const uint32_t H = sim->actor_hidden;
+            const int sms = dev->sm_count;
+            const float* actor = static_cast<const float*>(sim->buf[MDN_BUF_ACTOR]);
+            WideRowsArgs fa{};
+            fa.rows = t->minibatch;
+            fa.rows_dev = p.batch;
+            fa.row0_dev = p.starts;
+            fa.index = u;
+            fa.hidden = H;
+            fa.b1 = actor + size_t(H) * kActorObs;
+            fa.w2 = fa.b1 + H;
+            fa.partials = t->wide_partials;
+            fa.error = sim->wide_error;
+            cuda_check(launch_wide_forward(sim->wide->obs_map, sim->wide->w1_map, fa, sms, s), "wide forward");
+            cuda_check(launch_minibatch(p, u, chunks, s), "minibatch");
+            WideRowsArgs ba = fa;
+            ba.partials = nullptr;
+            ba.d_mean = p.mb_dm;
+            ba.delta = t->wide_delta;
+            ba.colsum_out = t->wide_colsums;
+            cuda_check(launch_wide_backward(sim->wide->obs_map, sim->wide->w1_map, ba, sms, s), "wide backward");
+            WideGradArgs ga{};
+            ga.rows = t->minibatch;
+            ga.rows_dev = p.batch;
+            ga.row0_dev = p.starts;
+            ga.index = u;
+            ga.hidden = H;
+            ga.splits = t->wide_splits;
+            ga.out = t->wide_w1_parts;
+            ga.error = sim->wide_error;
+            cuda_check(launch_wide_wgrad(t->delta_map, t->obs32_map, ga, sms, s), "wide weight gradient");
+            WideAssembleArgs aa{};
+            aa.hidden = H;
+            aa.splits = t->wide_splits;
+            aa.groups = t->wide_groups;
+            aa.w1_parts = t->wide_w1_parts;
+            aa.colsums = t->wide_colsums;
+            aa.small_grad = chunks > 1 ? p.grad : p.grad_partials;
+            aa.grad = t->wide_grad;
+            cuda_check(launch_wide_assemble(aa, sms, s), "wide gradient");
+            const size_t total = size_t(sim->actor_params) + kCriticParams;
+            if (multi) cuda_check(comm_allreduce_float(dev, t->wide_grad, total, s, err), err.c_str());
+            WideAdamArgs ad{};
+            ad.grad = t->wide_grad;
+            ad.params = static_cast<float*>(sim->buf[MDN_BUF_ACTOR]);
+            ad.m = p.actor_m;
+            ad.v = p.actor_v;
+            ad.count = sim->actor_params;
+            ad.bias_corr = p.bias_corr + 2 * u;
+            ad.learning_rate = p.learning_rate;
+            ad.max_norm = p.max_norm;
+            ad.norm_out = p.grad_norms + 2 * u;
+            cuda_check(launch_wide_clip_adam(ad, t->wide_norm_parts, sms, s), "wide clip+adam");
+            cuda_check(launch_clip_adam_critic(p, u, t->wide_grad + sim->actor_params, s), "critic clip+adam");
+            continue;
+        }
         cuda_check(launch_minibatch(p, u, chunks, s), "minibatch");
         if (multi) cuda_check(comm_allreduce_float(dev, p.grad, kPpoParams, s, err), err.c_str());
         cuda_check(launch_clip_adam(p, u, chunks, s), "clip+adam");
@@ -90,7 +161,6 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
         require(sim && out, MDN_ERR_INVALID, "mdn_ppo_create: null argument");
         cuda_check(cudaSetDevice(sim->dev->gpu), "cudaSetDevice");
         require(epochs >= 1 && epochs <= 4, MDN_ERR_INVALID, "PPO epochs must be 1..4");  // main.mm:1160
-        require(sim->wide == nullptr, MDN_ERR_INVALID, "PPO update of a wide actor: not available in this build");
         auto t = std::make_unique<mdn_ppo>();
         t->sim = sim;
         t->epochs = epochs;
@@ -112,7 +182,8 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
         PpoArgs& a = t->args;
         size_t off = 0;
         auto carve = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
-        const size_t o_am = carve(kActorParams * 4), o_av = carve(kActorParams * 4), o_cm = carve(kCriticParams * 4),
+        const size_t AP = sim->actor_params;
+        const size_t o_am = carve(AP * 4), o_av = carve(AP * 4), o_cm = carve(kCriticParams * 4),
                      o_cv = carve(kCriticParams * 4), o_sp = carve(gae_blocks(sim->n) * 8), o_st = carve(2 * 8),
                      o_sv = carve(2 * 4), o_idx = carve(U * 3 * 4), o_bias = carve(U * 2 * 4), o_ah = carve(mb * 64 * 4),
                      o_ch = carve(mb * 64 * 4), o_ad = carve(mb * 64 * 4), o_cd = carve(mb * 64 * 4),
@@ -174,6 +245,43 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
         a.grad_norms = reinterpret_cast<float*>(base + o_gn);
         a.fwd_grid = t->fwd_grid;
         a.grad_chunk = t->grad_chunk;
+        a.actor_b2 = sim->actor_hidden * (kActorObs + 1 + kActions);
+        a.actor_log_std = a.actor_b2 + kActions;
+        if (sim->wide) {
+            t->wide = true;
+            const uint32_t H = sim->actor_hidden, sms = uint32_t(sim->dev->sm_count);
+            const size_t cap128 = (size_t(t->minibatch) + 127) / 128 * 128;
+            const uint32_t m_tiles = H / 128;
+            t->wide_splits = std::max<uint32_t>(1, std::min<uint32_t>((3 * sms + m_tiles - 1) / m_tiles,
+                                                                      (t->minibatch + 31) / 32));
+            t->wide_groups = wide_backward_groups(H, int(sms));
+            size_t woff = 0;
+            auto wcarve = [&](size_t bytes) { const size_t o = woff; woff += align256(bytes); return o; };
+            const size_t w_part = wcarve(size_t(H / 128) * t->minibatch * 16), w_delta = wcarve(cap128 * H * 4),
+                         w_w1 = wcarve(size_t(t->wide_splits) * H * kActorObs * 4),
+                         w_cs = wcarve(size_t(t->wide_groups) * 5 * H * 4),
+                         w_g = wcarve((size_t(sim->actor_params) + kCriticParams) * 4), w_np = wcarve(size_t(sms) * 2 * 4);
+            const cudaError_t we = cudaMalloc(&t->wide_mem, woff);
+            if (we != cudaSuccess) {
+                cudaFree(t->mem);
+                throw Error(MDN_ERR_NOMEM, std::string("cudaMalloc wide trainer: ") + cudaGetErrorString(we));
+            }
+            char* wb = static_cast<char*>(t->wide_mem);
+            cuda_check(cudaMemsetAsync(wb, 0, woff, sim->stream), "clear wide trainer memory");
+            t->wide_partials = reinterpret_cast<float*>(wb + w_part);
+            t->wide_delta = reinterpret_cast<float*>(wb + w_delta);
+            t->wide_w1_parts = reinterpret_cast<float*>(wb + w_w1);
+            t->wide_colsums = reinterpret_cast<float*>(wb + w_cs);
+            t->wide_grad = reinterpret_cast<float*>(wb + w_g);
+            t->wide_norm_parts = reinterpret_cast<float*>(wb + w_np);
+            a.wide_partials = t->wide_partials;
+            a.wide_slices = H / 128;
+            a.wide_rows_cap = t->minibatch;
+            cuda_check(wide_make_map(&t->obs32_map, static_cast<const float*>(sim->buf[MDN_BUF_OBS]), kActorObs,
+                                     size_t(sim->n) * sim->horizon, kActorObs * 4, 32, true),
+                       "observation tensor map (32-row boxes)");
+            cuda_check(wide_make_map(&t->delta_map, t->wide_delta, H, cap128, size_t(H) * 4, 32, true), "delta tensor map");
+        }
         cuda_check(cudaMallocHost(&t->h_idx, U * 3 * 4), "pinned staging");
         cuda_check(cudaMallocHost(&t->h_bias, U * 2 * 4), "pinned staging");
         cuda_check(cudaEventCreateWithFlags(&t->staged, cudaEventDisableTiming), "event");
@@ -194,6 +302,7 @@ extern "C" int mdn_ppo_destroy(mdn_ppo* t) {
         cudaStreamSynchronize(t->sim->stream);
         if (t->graph) cudaGraphExecDestroy(t->graph);
         cudaFree(t->mem);
+        cudaFree(t->wide_mem);
         cudaFreeHost(t->h_idx);
         cudaFreeHost(t->h_bias);
         cudaEventDestroy(t->staged);
@@ -349,7 +458,7 @@ extern "C" int mdn_ppo_moments(mdn_ppo* t, int which, float* host, size_t count,
         checked(t);
         require(which >= 0 && which < 4 && host, MDN_ERR_INVALID, "moments: bad argument");
         float* d = which == 0 ? t->args.actor_m : which == 1 ? t->args.actor_v : which == 2 ? t->args.critic_m : t->args.critic_v;
-        const size_t n = which < 2 ? kActorParams : kCriticParams;
+        const size_t n = which < 2 ? size_t(t->sim->actor_params) : size_t(kCriticParams);
         require(count == n, MDN_ERR_INVALID, "moments: count mismatch");
         cuda_check(upload ? cudaMemcpyAsync(d, host, n * 4, cudaMemcpyHostToDevice, t->sim->stream)
                           : cudaMemcpyAsync(host, d, n * 4, cudaMemcpyDeviceToHost, t->sim->stream),
@@ -391,7 +500,7 @@ extern "C" int mdn_ppo_checkpoint_save(mdn_ppo* t, const char* path, uint32_t fa
         std::memset(&h, 0, sizeof(h));
         std::memcpy(h.magic, "PPOFIX1", 7);
         h.version = 6;
-        h.actor_count = kActorParams;
+        h.actor_count = sim->actor_params;
         h.critic_count = kCriticParams;
         h.horizon = sim->horizon;
         h.n = sim->n;
@@ -409,10 +518,10 @@ extern "C" int mdn_ppo_checkpoint_save(mdn_ppo* t, const char* path, uint32_t fa
         };
         blob.resize(sizeof(h));
         std::memcpy(blob.data(), &h, sizeof(h));
-        append_device(sim->buf[MDN_BUF_ACTOR], kActorParams * 4);
+        append_device(sim->buf[MDN_BUF_ACTOR], size_t(sim->actor_params) * 4);
         append_device(sim->buf[MDN_BUF_CRITIC], kCriticParams * 4);
-        append_device(t->args.actor_m, kActorParams * 4);
-        append_device(t->args.actor_v, kActorParams * 4);
+        append_device(t->args.actor_m, size_t(sim->actor_params) * 4);
+        append_device(t->args.actor_v, size_t(sim->actor_params) * 4);
         append_device(t->args.critic_m, kCriticParams * 4);
         append_device(t->args.critic_v, kCriticParams * 4);
         for (int id : {MDN_BUF_STATES, MDN_BUF_RUNS, MDN_BUF_WORLDS, MDN_BUF_SENSORS, MDN_BUF_POSES, MDN_BUF_COMMANDS})
@@ -461,7 +570,7 @@ extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t fa
         require(bool(f), MDN_ERR_IO, "checkpoint header truncated");
         require(h.version <= 6, MDN_ERR_MISMATCH,
                 "checkpoint version 7+ carries runtime/task/shaping state this build does not implement");
-        require(h.actor_count == kActorParams && h.critic_count == kCriticParams, MDN_ERR_MISMATCH,
+        require(h.actor_count == sim->actor_params && h.critic_count == kCriticParams, MDN_ERR_MISMATCH,
                 "PPO checkpoint dimensions mismatch");
         require(h.family == family && h.horizon == horizon && h.n == n && h.base_seed == seed, MDN_ERR_MISMATCH,
                 "PPO checkpoint config mismatch");
@@ -484,10 +593,10 @@ extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t fa
             cuda_check(cudaMemcpyAsync(dptr, tmp.data(), bytes, cudaMemcpyHostToDevice, sim->stream), "checkpoint upload");
             cuda_check(cudaStreamSynchronize(sim->stream), "checkpoint upload");
         };
-        read_to_device(sim->buf[MDN_BUF_ACTOR], kActorParams * 4);
+        read_to_device(sim->buf[MDN_BUF_ACTOR], size_t(sim->actor_params) * 4);
         read_to_device(sim->buf[MDN_BUF_CRITIC], kCriticParams * 4);
-        read_to_device(t->args.actor_m, kActorParams * 4);
-        read_to_device(t->args.actor_v, kActorParams * 4);
+        read_to_device(t->args.actor_m, size_t(sim->actor_params) * 4);
+        read_to_device(t->args.actor_v, size_t(sim->actor_params) * 4);
         read_to_device(t->args.critic_m, kCriticParams * 4);
         read_to_device(t->args.critic_v, kCriticParams * 4);
         for (int id : {MDN_BUF_STATES, MDN_BUF_RUNS, MDN_BUF_WORLDS, MDN_BUF_SENSORS}) read_to_device(sim->buf[id], sim->bytes[id]);

@@ -1295,7 +1295,7 @@ size_t act_smem_bytes() { return sizeof(float) * kActSmemFloats; }
 // The wide actor's tensor-core forward over this tick's observation rows.
 static cudaError_t launch_wide(const SimArgs& a, const WideStep* wide, cudaStream_t s) {
     if (!wide) return cudaSuccess;
-    WideForwardArgs p = wide->args;
+    WideRowsArgs p = wide->args;
     p.row0 = a.tick * a.n;
     return launch_wide_forward(wide->obs_map, wide->w1_map, p, wide->sm_count, s);
 }

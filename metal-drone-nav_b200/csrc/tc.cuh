@@ -79,19 +79,30 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
 __device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// Shared-memory matrix descriptor for a tile stored in the 128-byte swizzled
-// canonical layout (rows of 128 bytes, 8-row atoms of 1024 bytes, the layout
-// a TMA load with 128-byte swizzle writes). Fields: start address, leading
-// byte offset, stride byte offset (all >> 4), descriptor version 1, swizzle
-// mode 128B.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// Shared-memory matrix descriptor. Fields: start address, leading byte
+// offset, stride byte offset (all >> 4), descriptor version 1, layout type.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
     uint64_t d = 0;
     d |= uint64_t((saddr >> 4) & 0x3FFFu);
     d |= uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16;
     d |= uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32;
     d |= uint64_t(1) << 46;  // version (Blackwell)
-    d |= uint64_t(2) << 61;  // SWIZZLE_128B
+    d |= uint64_t(layout & 7u) << 61;
     return d;
+}
+// K-major tile in the 128-byte swizzled layout: rows of 128 bytes, 8-row
+// atoms of 1024 bytes (16-byte granules XOR row % 8), as a TMA load with
+// 128-byte swizzle writes it.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return smem_desc(saddr, lbo_bytes, sbo_bytes, 2u);
+}
+// MN-major tf32 tile in the 128-byte swizzle with 32-byte atoms: rows of 128
+// bytes along M/N, 4-row atoms of 512 bytes (32-byte granules XOR row % 4),
+// as a TMA load with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B writes it; the only
+// layout the tensor cores accept for MN-major tf32 operands. lbo = stride
+// between 128-byte M/N chunks, sbo = stride between 4-row K groups.
+__device__ __forceinline__ uint64_t sw128b32_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return smem_desc(saddr, lbo_bytes, sbo_bytes, 1u);
 }
 
 // Instruction descriptor of tcgen05.mma.kind::tf32 with an fp32 accumulator:

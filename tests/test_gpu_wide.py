@@ -126,3 +126,143 @@ def test_wide_rollout_graph(layouts):
     finally:
         sim.close()
         dev.close()
+
+
+# ---------------------------------------------------------------- PPO update
+# One full-batch update (epochs = 1, minibatch = all rows): after Adam's first
+# step the actor's first moment is 0.1 x the clipped gradient, which is
+# compared with a float64 evaluation of the same gradient (loss derivatives
+# from the oracle's sample_loss_and_grad, ppo.hpp:144-181; per-sample
+# gradients summed as actor_backward_sample, ppo.hpp:269-287, sums them).
+# Tolerance for the tensor-core parts (dW1, db1, dW2: TF32 products, fp32
+# accumulation): relative L2 error <= GRAD_REL_L2 and per-element
+# |m - m_ref| <= GRAD_ABS * max|m_ref|. b2 and log_std are fp32 sums of loss
+# derivatives that depend on the TF32 means, scaled by the actor's global-norm
+# clip (whose norm carries the TF32 error too): relative 5e-3 plus 1e-3 of the
+# block's largest entry (log-std sums cancel). The critic is independent of the
+# actor's precision: relative 1e-3.
+GRAD_REL_L2 = 1e-2
+GRAD_ABS = 1e-2
+
+
+def expected_moments(olib, om, rollout, actor, critic, adv, ret, entropy_coef, hidden=HIDDEN):
+    obs, co, act, logp, values = rollout
+    rows = obs.shape[0]
+    H = hidden
+    w1 = actor[: H * OBS].reshape(H, OBS).astype(np.float64)
+    b1 = actor[H * OBS: H * OBS + H].astype(np.float64)
+    w2 = actor[H * OBS + H: H * OBS + 5 * H].reshape(4, H).astype(np.float64)
+    b2 = actor[H * OBS + 5 * H: H * OBS + 5 * H + 4].astype(np.float64)
+    log_std = actor[-4:].copy()
+    hid = np.tanh(obs.astype(np.float64) @ w1.T + b1)
+    mean = hid @ w2.T + b2
+    mean[:, :3] += obs[:, OBS - 3:]
+    mean32 = mean.astype(np.float32)
+    cw1 = critic[: 64 * 32].reshape(64, 32).astype(np.float64)
+    cb1 = critic[64 * 32: 64 * 33].astype(np.float64)
+    cw2 = critic[64 * 33: 64 * 34].astype(np.float64)
+    cb2 = float(critic[64 * 34])
+    chid = np.tanh(co.astype(np.float64) @ cw1.T + cb1)
+    value = (chid @ cw2 + cb2).astype(np.float32)
+    dm = np.zeros((rows, 4), np.float32)
+    dls = np.zeros((rows, 4), np.float32)
+    dv = np.zeros(rows, np.float32)
+    loss = np.zeros(4, np.float32)
+    for r in range(rows):
+        d_m = np.zeros(4, np.float32)
+        d_l = np.zeros(4, np.float32)
+        d_v = np.zeros(1, np.float32)
+        olib.o_sample_loss_and_grad(om.ptr(np.ascontiguousarray(act[r])), om.ptr(np.ascontiguousarray(mean32[r])),
+                                    om.ptr(log_std), float(logp[r]), float(value[r]), float(adv[r]),
+                                    float(ret[r]), float(rows), 0.2, 0.5, float(entropy_coef), om.ptr(d_m),
+                                    om.ptr(d_l), om.ptr(d_v), om.ptr(loss))
+        dm[r], dls[r], dv[r] = d_m, d_l, d_v[0]
+    dm64 = dm.astype(np.float64)
+    delta = (dm64 @ w2) * (1.0 - hid * hid)
+    g_w1 = delta.T @ obs.astype(np.float64)
+    g_b1 = delta.sum(0)
+    g_w2 = dm64.T @ hid
+    g_actor = np.concatenate([g_w1.ravel(), g_b1, g_w2.ravel(), dm64.sum(0), dls.astype(np.float64).sum(0)])
+    cdelta = np.outer(dv.astype(np.float64), cw2) * (1.0 - chid * chid)
+    g_critic = np.concatenate([(cdelta.T @ co.astype(np.float64)).ravel(), cdelta.sum(0),
+                               (dv.astype(np.float64)[:, None] * chid).sum(0), [dv.astype(np.float64).sum()]])
+    out = []
+    for g in (g_actor, g_critic):
+        norm = np.sqrt(np.sum(g * g))
+        scale = min(1.0, 0.5 / norm)
+        out.append((0.1 * scale * g, norm))
+    return out
+
+
+def test_wide_ppo_update_gradient(layouts, olib):
+    pkg = load_package()
+    om = load_oracle_module()
+    n, horizon = 256, 4
+    dev = pkg.Device(0)
+    cfg = layouts.default_config(n=n, family=17, seed=13)
+    sim = pkg.Sim(dev, cfg, horizon, actor_hidden=HIDDEN)
+    tr = pkg.PPOTrainer(sim, epochs=1, minibatch=n * horizon)
+    try:
+        actor = sim.download("actor")
+        actor[HIDDEN * OBS: HIDDEN * OBS + HIDDEN] = np.random.default_rng(2).normal(0, 0.1, HIDDEN).astype(np.float32)
+        sim.upload("actor", actor)
+        critic = sim.download("critic")
+        sim.collect()
+        dev.finish()
+        rows = n * horizon
+        rollout = (sim.download("obs").reshape(rows, OBS), sim.download("co").reshape(rows, 32),
+                   sim.download("actions").reshape(rows, 4), sim.download("logp"), sim.download("values"))
+        tr.rollout_update(0)
+        dev.finish()
+        adv, ret = sim.download("advantages"), sim.download("returns")
+        (m_actor_ref, norm_a), (m_critic_ref, norm_c) = expected_moments(
+            olib, om, rollout, actor, critic, adv, ret, float(cfg["entropy_coef"]))
+        m_actor = tr.moments(0).astype(np.float64)
+        m_critic = tr.moments(2).astype(np.float64)
+        norms = tr.grad_norms(1)[0]
+        assert m_actor.size == 967688
+        H = HIDDEN
+        tc = slice(0, H * OBS + 5 * H)          # dW1, db1, dW2: tensor-core sums
+        small = slice(H * OBS + 5 * H, None)    # b2, log_std
+        rel = np.linalg.norm(m_actor[tc] - m_actor_ref[tc]) / np.linalg.norm(m_actor_ref[tc])
+        assert rel <= GRAD_REL_L2, rel
+        assert np.max(np.abs(m_actor[tc] - m_actor_ref[tc])) <= GRAD_ABS * np.max(np.abs(m_actor_ref[tc]))
+        assert np.allclose(m_actor[small], m_actor_ref[small], rtol=5e-3, atol=1e-3 * np.max(np.abs(m_actor_ref[small])))
+        assert np.allclose(m_critic, m_critic_ref, rtol=1e-3, atol=1e-4 * np.max(np.abs(m_critic_ref)))
+        assert abs(norms[0] - norm_a) <= 1e-2 * norm_a
+        assert abs(norms[1] - norm_c) <= 1e-4 * norm_c
+        # Adam's first step moves every parameter by at most lr (plus rounding)
+        after = sim.download("actor")
+        lr = float(cfg["learning_rate"])
+        assert np.all(np.isfinite(after))
+        assert np.max(np.abs(after[:-4] - actor[:-4])) <= lr * 1.001
+    finally:
+        tr.close()
+        sim.close()
+        dev.close()
+
+
+def test_wide_ppo_update_minibatches(layouts):
+    """Several minibatches and epochs through the captured update graph: the
+    update completes, parameters stay finite, the barrier flag stays clear, and
+    a second rollout + update runs on the updated weights."""
+    pkg = load_package()
+    n, horizon = 1024, 8
+    dev = pkg.Device(0)
+    cfg = layouts.default_config(n=n, family=17, seed=17)
+    sim = pkg.Sim(dev, cfg, horizon, actor_hidden=HIDDEN)
+    tr = pkg.PPOTrainer(sim, epochs=2, minibatch=n * horizon // 4)
+    try:
+        before = sim.download("actor")
+        for k in range(2):
+            sim.collect()
+            tr.rollout_update(k)
+        dev.finish()
+        after = sim.download("actor")
+        assert np.all(np.isfinite(after)) and not np.array_equal(before, after)
+        assert np.all(np.isfinite(tr.metric_mean))
+        assert np.all(np.isfinite(tr.grad_norms(8)))
+    finally:
+        tr.close()
+        sim.close()
+        dev.close()
