@@ -67,7 +67,11 @@ def parse():
     ap.add_argument("--epochs", type=int, default=4)
     ap.add_argument("--minibatches", type=int, default=16)
     ap.add_argument("--family", type=int, default=17)
+    ap.add_argument("--actor-hidden", type=int, default=64,
+                    help="64 = the reference's 12,104-parameter actor; 5120 = the 967,688-parameter wide actor "
+                         "(BASELINE config 3), evaluated on the tcgen05 tensor cores")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-wide", action="store_true", help="skip the wide-actor (BASELINE config 3) measurement")
     return ap.parse_args()
 
 
@@ -199,6 +203,54 @@ def read_profile_traffic(kernel):
     return None
 
 
+# ------------------------------------------------------------ wide actor
+WIDE_HIDDEN = 5120
+WIDE_ENVS = 16384
+
+
+def measure_wide(pkg, dev, dist, args, peaks):
+    """BASELINE config 3 on this rank's share: 16,384 environments (over all
+    ranks), the 967,688-parameter actor (184 -> 5120 tanh -> 4) on tcgen05 TF32,
+    T=128 rollouts, PPO 4 epochs x 16 minibatches. One warm-up rollout + update,
+    then two timed ones (CUDA events on the simulator stream, max over ranks)."""
+    L = pkg.layouts
+    n = WIDE_ENVS // dist.world
+    horizon, epochs, minibatches, steps = 128, 4, 16, 2
+    cfg = L.default_config(n=n, family=args.family, seed=43)
+    sim = pkg.Sim(dev, cfg, horizon, actor_hidden=WIDE_HIDDEN)
+    tr = pkg.PPOTrainer(sim, epochs=epochs, minibatch=n * horizon // minibatches)
+    try:
+        sim.collect()
+        tr.rollout_update(0)
+        dev.finish()
+        dist.barrier()
+        c_ms, u_ms = 0.0, 0.0
+        for k in range(steps):
+            sim.collect()
+            c_ms += sim.last_collect_ms()
+            tr.rollout_update(1 + k)
+            u_ms += tr.last_update_ms()
+        dev.finish()
+        c_ms, u_ms = dist.max([c_ms, u_ms])
+        rows = WIDE_ENVS * horizon
+        # algorithmic tensor-core work per row and epoch: forward, backward
+        # recompute and dW1, each 2 x 184 x 5120 multiply-adds
+        flop = 3 * 2 * 184 * WIDE_HIDDEN * rows * epochs
+        upd_s = u_ms / steps * 1e-3
+        tf32_peak = peaks.get("bf16_tflops", 1590.0) / 2.0
+        return {"config": "BASELINE config 3: 16,384 envs, 184->5120->4 tanh actor (967,688 params) on tcgen05 TF32, "
+                          "32->64->1 critic, T=128, PPO 4 epochs x 16 minibatches",
+                "env_steps_per_s": rows * steps / (c_ms * 1e-3), "rollout_ms": c_ms / steps,
+                "ppo_update_ms": u_ms / steps,
+                "ppo_tensor_roofline": {"bound": "tensor", "achieved": flop / upd_s / 1e12, "peak": tf32_peak,
+                                        "unit": "TFLOP/s", "frac": flop / upd_s / 1e12 / tf32_peak,
+                                        "peak_source": "half the measured bf16 dense rate (tf32 issues at half the "
+                                                       "bf16 rate on tcgen05)"}}
+    finally:
+        tr.close()
+        sim.close()
+
+
 # ------------------------------------------------------------ CPU baseline
 def cpu_reference_sample(layouts, n, policy_steps, family, warmup=0, threads=None):
     """The reference's own CPU path (oracle/_ref: cpu_reference.hpp compiled
@@ -282,11 +334,14 @@ def run_reference_arm(args, dist, out_fd):
 
 
 def workload_config(args):
-    return {"workload": "BASELINE config 4 on one shard set: 65,536 envs, family-17 clutter rooms (16 static boxes), "
-                        "20x16 depth rays, 184->64->4 tanh actor, 32->64->1 critic, T=128 rollouts, "
+    actor = ("184->64->4 tanh actor" if args.actor_hidden == 64 else
+             f"184->{args.actor_hidden}->4 tanh actor on tcgen05 TF32")
+    return {"workload": f"BASELINE config 4 on one shard set: {args.envs:,} envs, family-17 clutter rooms (16 static "
+                        f"boxes), 20x16 depth rays, {actor}, 32->64->1 critic, T={args.horizon} rollouts, "
                         f"PPO {args.epochs} epochs x {args.minibatches} minibatches",
             "envs": args.envs, "horizon": args.horizon, "family": args.family, "epochs": args.epochs,
-            "minibatches": args.minibatches, "parallelism": f"dp{args.gpus} (envs sharded)",
+            "minibatches": args.minibatches, "actor_hidden": args.actor_hidden,
+            "parallelism": f"dp{args.gpus} (envs sharded)",
             "l2": "inputs larger than L2 (obs buffer > 6 GB per rollout)"}
 
 
@@ -318,7 +373,7 @@ def main():
         uid = dist.broadcast_bytes(pkg.Device.comm_unique_id() if dist.rank == 0 else None)
         dev.comm_init(dist.rank, world, uid)
     cfg = L.default_config(n=n, family=args.family, seed=42)
-    sim = pkg.Sim(dev, cfg, args.horizon)
+    sim = pkg.Sim(dev, cfg, args.horizon, actor_hidden=None if args.actor_hidden == 64 else args.actor_hidden)
     rows = n * args.horizon
     minibatch = rows // args.minibatches
     trainer = pkg.PPOTrainer(sim, epochs=args.epochs, minibatch=minibatch)
@@ -424,6 +479,8 @@ def main():
         "kernels": kernels,
         "clocks": clk,
     }
+    if not args.no_wide and args.actor_hidden == 64:
+        line["wide_actor"] = measure_wide(pkg, dev, dist, args, peaks)
     if world == 1 and dist.rank == 0 and not args.no_cpu_baseline:
         s = cpu_reference_sample(L, args.envs, 2, args.family, warmup=1)
         if s is not None:

@@ -133,6 +133,9 @@ __device__ __forceinline__ float half_warp_sum(float v) {
     return v;
 }
 
+// kWide: the actor means come from the tensor-core forward's slice sums
+// (p.wide_partials); only the critic, b2 and log_std are handled here.
+template <bool kWide>
 __global__ void __launch_bounds__(kMbThreads) k_mb_forward(PpoArgs p, uint32_t update) {
     extern __shared__ float sm[];
     float* w1t = sm;                                   // [184][64]
@@ -150,7 +153,7 @@ __global__ void __launch_bounds__(kMbThreads) k_mb_forward(PpoArgs p, uint32_t u
     const int tid = threadIdx.x;
     const float* actor = p.actor;
     const float* critic = p.critic;
-    const bool wide = p.wide_slices != 0;
+    constexpr bool wide = kWide;
     if (!wide)
         for (int k = tid; k < kActorObs * kHidden; k += kMbThreads) {
             const int h = k / kActorObs, c = k % kActorObs;
@@ -372,6 +375,7 @@ __global__ void __launch_bounds__(kMbThreads) k_mb_forward(PpoArgs p, uint32_t u
 constexpr int kGradThreads = 256;
 constexpr int kGradTile = 16;
 
+template <bool kWide>
 __global__ void __launch_bounds__(kGradThreads) k_mb_grad(PpoArgs p, uint32_t update) {
     __shared__ float dtile[kGradTile][kHidden];      // actor deltas
     __shared__ float otile[kGradTile][kActorObs];    // observations
@@ -421,7 +425,7 @@ __global__ void __launch_bounds__(kGradThreads) k_mb_grad(PpoArgs p, uint32_t up
         }
         if (tid < kGradTile) dvt[tid] = tid < int(nr) ? p.mb_dv[size_t(r0) + tid] : 0.0f;
         __syncthreads();
-        const bool wide = p.wide_slices != 0;  // actor W1/W2/b1 come from the tensor-core backward
+        constexpr bool wide = kWide;  // actor W1/W2/b1 come from the tensor-core backward
         for (int r = 0; r < int(nr); r++) {
             if (tid < kActorObs && !wide) {
                 const float o = otile[r][tid];
@@ -544,7 +548,11 @@ __global__ void k_metrics_mean(PpoArgs p, uint32_t updates) {
 size_t mb_forward_smem_bytes() { return kMbSmemFloats * sizeof(float); }
 
 cudaError_t configure_ppo_kernels() {
-    return cudaFuncSetAttribute(k_mb_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, int(mb_forward_smem_bytes()));
+    cudaError_t e = cudaFuncSetAttribute(k_mb_forward<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(mb_forward_smem_bytes()));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_mb_forward<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(mb_forward_smem_bytes()));
 }
 
 uint32_t gae_blocks(uint32_t n) { return (n + kGaeThreads - 1) / kGaeThreads; }
@@ -572,8 +580,13 @@ cudaError_t launch_adv_apply(const PpoArgs& p, int sm_count, cudaStream_t s) {
     return cudaGetLastError();
 }
 cudaError_t launch_minibatch(const PpoArgs& p, uint32_t update, uint32_t chunks, cudaStream_t s) {
-    k_mb_forward<<<p.fwd_grid, kMbThreads, mb_forward_smem_bytes(), s>>>(p, update);
-    k_mb_grad<<<chunks, kGradThreads, 0, s>>>(p, update);
+    if (p.wide_slices) {
+        k_mb_forward<true><<<p.fwd_grid, kMbThreads, mb_forward_smem_bytes(), s>>>(p, update);
+        k_mb_grad<true><<<chunks, kGradThreads, 0, s>>>(p, update);
+    } else {
+        k_mb_forward<false><<<p.fwd_grid, kMbThreads, mb_forward_smem_bytes(), s>>>(p, update);
+        k_mb_grad<false><<<chunks, kGradThreads, 0, s>>>(p, update);
+    }
     if (chunks > 1) k_grad_reduce<<<(kPpoParams + 255) / 256, 256, 0, s>>>(p, chunks);
     return cudaGetLastError();
 }

@@ -57,7 +57,7 @@ struct mdn_ppo {
     float* wide_colsums = nullptr;    // [groups][5][hidden] db1 / dW2 partials
     float* wide_grad = nullptr;       // [actor params + critic params]
     float* wide_norm_parts = nullptr; // [2 * SMs]
-    WideMap obs32_map{}, delta_map{};
+    WideMap obs32_map{}, delta_map{}, obs256_map{}, w1_128_map{};
 };
 
 namespace {
@@ -112,7 +112,7 @@ void enqueue_update(mdn_ppo* t) {
             ba.d_mean = p.mb_dm;
             ba.delta = t->wide_delta;
             ba.colsum_out = t->wide_colsums;
-            cuda_check(launch_wide_backward(sim->wide->obs_map, sim->wide->w1_map, ba, sms, s), "wide backward");
+            cuda_check(launch_wide_backward(t->obs256_map, t->w1_128_map, ba, sms, s), "wide backward");
             WideGradArgs ga{};
             ga.rows = t->minibatch;
             ga.rows_dev = p.batch;
@@ -250,14 +250,14 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
         if (sim->wide) {
             t->wide = true;
             const uint32_t H = sim->actor_hidden, sms = uint32_t(sim->dev->sm_count);
-            const size_t cap128 = (size_t(t->minibatch) + 127) / 128 * 128;
+            const size_t cap256 = (size_t(t->minibatch) + 255) / 256 * 256;
             const uint32_t m_tiles = H / 128;
             t->wide_splits = std::max<uint32_t>(1, std::min<uint32_t>((3 * sms + m_tiles - 1) / m_tiles,
                                                                       (t->minibatch + 31) / 32));
             t->wide_groups = wide_backward_groups(H, int(sms));
             size_t woff = 0;
             auto wcarve = [&](size_t bytes) { const size_t o = woff; woff += align256(bytes); return o; };
-            const size_t w_part = wcarve(size_t(H / 128) * t->minibatch * 16), w_delta = wcarve(cap128 * H * 4),
+            const size_t w_part = wcarve(size_t(H / 128) * t->minibatch * 16), w_delta = wcarve(cap256 * H * 4),
                          w_w1 = wcarve(size_t(t->wide_splits) * H * kActorObs * 4),
                          w_cs = wcarve(size_t(t->wide_groups) * 5 * H * 4),
                          w_g = wcarve((size_t(sim->actor_params) + kCriticParams) * 4), w_np = wcarve(size_t(sms) * 2 * 4);
@@ -280,7 +280,13 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
             cuda_check(wide_make_map(&t->obs32_map, static_cast<const float*>(sim->buf[MDN_BUF_OBS]), kActorObs,
                                      size_t(sim->n) * sim->horizon, kActorObs * 4, 32, true),
                        "observation tensor map (32-row boxes)");
-            cuda_check(wide_make_map(&t->delta_map, t->wide_delta, H, cap128, size_t(H) * 4, 32, true), "delta tensor map");
+            cuda_check(wide_make_map(&t->delta_map, t->wide_delta, H, cap256, size_t(H) * 4, 32, true), "delta tensor map");
+            cuda_check(wide_make_map(&t->obs256_map, static_cast<const float*>(sim->buf[MDN_BUF_OBS]), kActorObs,
+                                     size_t(sim->n) * sim->horizon, kActorObs * 4, 256),
+                       "observation tensor map (256-row boxes)");
+            cuda_check(wide_make_map(&t->w1_128_map, static_cast<const float*>(sim->buf[MDN_BUF_ACTOR]), kActorObs, H,
+                                     kActorObs * 4, 128),
+                       "actor W1 tensor map (128-row boxes)");
         }
         cuda_check(cudaMallocHost(&t->h_idx, U * 3 * 4), "pinned staging");
         cuda_check(cudaMallocHost(&t->h_bias, U * 2 * 4), "pinned staging");

@@ -657,6 +657,8 @@ __device__ __forceinline__ float overhead_scale(const float* ob) {
     return 0.25f + 0.75f * (overhead / 20.0f);
 }
 
+// kWide: the actor mean comes from the tensor-core forward's slice sums.
+template <bool kWide>
 __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
     extern __shared__ float sm[];
     float* w1p = sm;                                  // [64][185] actor W1, row-major, padded
@@ -670,7 +672,7 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
     float* cb2 = cw2 + kHidden;                       // [1]
     float* rows = cb2 + 1;                            // per warp: obs[4][184], co[4][32]
     const int tid = threadIdx.x;
-    const bool wide = a.wide_slices != 0;  // actor mean from the tensor-core forward's slice sums
+    constexpr bool wide = kWide;
     if (!wide)
         for (int k = tid; k < kActorObs * kHidden; k += blockDim.x) {
             const int h = k / kActorObs, col = k % kActorObs;
@@ -1292,6 +1294,13 @@ cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s) {
 
 size_t act_smem_bytes() { return sizeof(float) * kActSmemFloats; }
 
+static void launch_act(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
+    if (a.wide_slices)
+        k_act<true><<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
+    else
+        k_act<false><<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
+}
+
 // The wide actor's tensor-core forward over this tick's observation rows.
 static cudaError_t launch_wide(const SimArgs& a, const WideStep* wide, cudaStream_t s) {
     if (!wide) return cudaSuccess;
@@ -1306,7 +1315,7 @@ cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s, 
         k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
     cudaError_t e = launch_wide(a, wide, s);
     if (e != cudaSuccess) return e;
-    k_act<<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
+    launch_act(a, plan, s);
     return launch_advance(a, plan, s);
 }
 
@@ -1319,7 +1328,7 @@ cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStr
     cudaEventRecord(ev[1], s);
     const cudaError_t we = launch_wide(a, wide, s);
     if (we != cudaSuccess) return we;
-    k_act<<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
+    launch_act(a, plan, s);
     cudaEventRecord(ev[2], s);
     const cudaError_t e = launch_advance(a, plan, s);
     cudaEventRecord(ev[3], s);
@@ -1389,7 +1398,9 @@ cudaError_t fp32_peak(int sm_count, double* tflops) {
 int kernels_per_step(const mdn_sim_config& c, bool wide) { return 3 + (c.geometry_memory ? 1 : 0) + (wide ? 1 : 0); }
 
 cudaError_t configure_kernels() {
-    cudaError_t e = cudaFuncSetAttribute(k_act, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
+    cudaError_t e = cudaFuncSetAttribute(k_act<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_act<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_memory_hint, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(kMemWarps * sizeof(MemScene)));

@@ -3,10 +3,10 @@
 // 967,688-parameter actor is hidden = 5120, navigation_wide_deployment.hpp:54-66),
 // forward in the rollout and forward + backward in the PPO update.
 //
-// k_wide_rows<kForward> computes, for a block of observation rows,
+// k_wide_forward computes, for a block of observation rows,
 //     partial[s][row][a] = sum_{h in slice s} tanh(obs[row] . W1[h] + b1[h]) * W2[a][h]
 // for 128-unit hidden slices s (the consumer adds the slices in a fixed
-// order, then b2 and the geometry prior). k_wide_rows<kBackward> recomputes
+// order, then b2 and the geometry prior). k_wide_backward recomputes
 // the same pre-activations and, from the per-row mean derivatives d_mean of
 // ppo.hpp:144-181, writes the hidden deltas
 //     delta[row][h] = (sum_a d_mean[row][a] W2[a][h]) (1 - tanh^2)
@@ -47,85 +47,65 @@ constexpr int kRowsStageBytes = kRowsABytes + kRowsBBytes;
 constexpr int kRowsEpiWarps = 8;
 constexpr int kRowsThreads = (2 + kRowsEpiWarps) * 32;
 constexpr int kColSums = 5;           // delta, d_mean[0..3] * tanh
+constexpr int kBackHidden = 128;      // backward tile: hidden units (tensor-memory lanes)
+constexpr int kBackRows = 256;        // backward tile: rows (accumulator columns)
+static_assert(kBackHidden * 128 == kRowsABytes && kBackRows * 128 == kRowsBBytes, "backward reuses the stage sizes");
 constexpr long long kWaitLimit = 2000000000ll;  // clock cycles (~1 s) before a wait gives up
 
 // k_wide_wgrad: 128 hidden units x 192 inputs per item, 32 rows per stage.
 constexpr int kGradBM = 128;
 constexpr int kGradBN = 192;
 constexpr int kGradRows = 32;
-constexpr int kGradStages = 4;
+constexpr int kGradStages = 5;
 constexpr int kGradAPanelBytes = kGradRows * 128;  // 32 rows x 32 hidden units
 constexpr int kGradABytes = 4 * kGradAPanelBytes;
 constexpr int kGradBBytes = kObsPanels * kGradAPanelBytes;
 constexpr int kGradStageBytes = kGradABytes + kGradBBytes;
 constexpr int kGradThreads = 6 * 32;
 
+constexpr int kMaxStages = kRowsStages > kGradStages ? kRowsStages : kGradStages;
 struct Barriers {
-    uint64_t full[kRowsStages];
-    uint64_t empty[kRowsStages];
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t done;
     uint32_t tmem_base;
 };
 constexpr size_t kRowsSmemFwd = 1024 + size_t(kRowsStages) * kRowsStageBytes + sizeof(Barriers);
-constexpr size_t kRowsSmemBwd = kRowsSmemFwd + size_t(kRowsEpiWarps) * kColSums * 128 * sizeof(float);
+constexpr size_t kRowsSmemBwd = kRowsSmemFwd + size_t(kBackHidden) * kColSums * sizeof(float);
 constexpr size_t kGradSmem = 1024 + size_t(kGradStages) * kGradStageBytes + sizeof(Barriers);
 
-__device__ __forceinline__ float wide_tanh(float x) { return tanhf(x); }
-
-// Column sums of a 32 x 32 block held one row per lane (v[c] = this lane's
-// value in column c): after the call v[0] on lane c is the sum of column c
-// over the 32 lanes. Recursive halving, 31 exchanges, a fixed order.
-__device__ __forceinline__ float warp_column_sums(float (&v)[32], int lane) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        const bool upper = (lane & off) != 0;
-#pragma unroll
-        for (int i = 0; i < off; i++) {
-            const float send = upper ? v[i] : v[i + off];
-            const float keep = upper ? v[i + off] : v[i];
-            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-        }
-    }
-    return v[0];
+// tanh from the logistic identity tanh(x) = 1 - 2 / (1 + e^(2x)), with
+// e^(2x) = 2^(x * 2 log2 e) on the hardware base-2 exponential and the
+// hardware reciprocal (ex2.approx / rcp.approx, a few ulp each): absolute
+// error ~1e-7, far below the tf32 products it follows. Saturates to +-1 for
+// large |x| (e^(2x) -> inf or 0).
+constexpr float kTwoLog2e = 2.8853900817779268f;
+// tanh(z) given y = z * 2 log2 e (callers fold the bias into one FMA)
+__device__ __forceinline__ float wide_tanh_scaled(float y) {
+    float e, r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(y));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+    return fmaf(-2.0f, r, 1.0f);
 }
+__device__ __forceinline__ float wide_tanh(float x) { return wide_tanh_scaled(x * kTwoLog2e); }
 }  // namespace
 
-template <int kMode>
 __global__ void __launch_bounds__(kRowsThreads, 1)
-    k_wide_rows(const __grid_constant__ CUtensorMap obs_map, const __grid_constant__ CUtensorMap w1_map,
-                WideRowsArgs p) {
+    k_wide_forward(const __grid_constant__ CUtensorMap obs_map, const __grid_constant__ CUtensorMap w1_map,
+                   WideRowsArgs p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stage_base = smem;
     Barriers& s = *reinterpret_cast<Barriers*>(smem + size_t(kRowsStages) * kRowsStageBytes);
-    float* colsum = reinterpret_cast<float*>(smem + size_t(kRowsStages) * kRowsStageBytes + sizeof(Barriers));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const uint32_t rows = p.rows_dev ? p.rows_dev[p.index] : p.rows;
     const uint32_t row0 = p.row0_dev ? p.row0_dev[p.index] : p.row0;
     const uint32_t m_tiles = (rows + kRowsBM - 1) / kRowsBM;
     const uint32_t n_tiles = p.hidden / kRowsBN;
-    // Forward: tiles t = m * n_tiles + n, strided over the grid. Backward: CTA c
-    // keeps hidden tile n = c % n_tiles and walks m = c / n_tiles, + groups, ...
-    // so its column sums accumulate in shared memory over its row tiles.
-    const uint32_t groups = kMode == kWideBackward ? gridDim.x / n_tiles : 1;
-    const uint32_t my_n = blockIdx.x % n_tiles, my_g = blockIdx.x / n_tiles;
-    const uint32_t count = kMode == kWideBackward ? (my_g < groups && my_g < m_tiles ? (m_tiles - my_g + groups - 1) / groups : 0)
-                                                   : (m_tiles * n_tiles > blockIdx.x
-                                                          ? (m_tiles * n_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x
-                                                          : 0);
-    auto tile_mn = [&](uint32_t j, uint32_t& m, uint32_t& n) {
-        if (kMode == kWideBackward) {
-            m = my_g + j * groups;
-            n = my_n;
-        } else {
-            const uint32_t t = blockIdx.x + j * gridDim.x;
-            m = t / n_tiles;
-            n = t % n_tiles;
-        }
-    };
+    const uint32_t tiles = m_tiles * n_tiles;  // t = m * n_tiles + n, strided over the grid
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kRowsStages; i++) {
@@ -141,8 +121,6 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         tc::prefetch_tmap(&obs_map);
         tc::prefetch_tmap(&w1_map);
     }
-    if (kMode == kWideBackward)
-        for (int i = threadIdx.x; i < kRowsEpiWarps * kColSums * 128; i += blockDim.x) colsum[i] = 0.0f;
     if (warp == 1) {
         tc::tmem_alloc(&s.tmem_base, 512);
         tc::tmem_relinquish();
@@ -156,9 +134,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         // ------------------------------------------------------ TMA producer
         uint32_t it = 0;
         bool ok = true;
-        for (uint32_t j = 0; j < count && ok; j++) {
-            uint32_t m, n;
-            tile_mn(j, m, n);
+        for (uint32_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            const uint32_t m = t / n_tiles, n = t % n_tiles;
             for (int kp = 0; kp < kObsPanels; kp++, it++) {
                 const uint32_t st = it % kRowsStages, use = it / kRowsStages;
                 if (use > 0 && !tc::mbar_wait(&s.empty[st], (use - 1) & 1, kWaitLimit)) {
@@ -177,9 +154,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------- MMA issuer
         constexpr uint32_t idesc = tc::tf32_idesc(kRowsBM, kRowsBN, 0, 0);
-        uint32_t it = 0;
+        uint32_t it = 0, j = 0;
         bool ok = true;
-        for (uint32_t j = 0; j < count && ok; j++) {
+        for (uint32_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, j++) {
             const uint32_t buf = j & 1, use = j >> 1;
             if (use > 0 && !tc::mbar_wait(&s.tempty[buf], (use - 1) & 1, kWaitLimit)) {
                 ok = false;
@@ -214,11 +191,10 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         const int ew = warp - 2;
         const int quarter = warp & 3;   // tensor-memory lanes 32*quarter .. +31
         const int half = ew >> 2;       // columns [128*half, 128*half+128) of the tile
-        float* my_sums = colsum + size_t(ew) * kColSums * 128;
         bool ok = true;
-        for (uint32_t j = 0; j < count; j++) {
-            uint32_t m, n;
-            tile_mn(j, m, n);
+        uint32_t j = 0;
+        for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x, j++) {
+            const uint32_t m = t / n_tiles, n = t % n_tiles;
             const uint32_t buf = j & 1, use = j >> 1;
             if (!tc::mbar_wait(&s.tfull[buf], use & 1, kWaitLimit)) {
                 ok = false;
@@ -226,83 +202,32 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
             }
             tc::fence_after_sync();
             const uint32_t row = m * kRowsBM + quarter * 32 + lane;
-            const bool valid = row < rows;
             const uint32_t col0 = n * kRowsBN + half * 128;
             float pm0 = 0.0f, pm1 = 0.0f, pm2 = 0.0f, pm3 = 0.0f;
-            float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
-            if (kMode == kWideBackward && valid) {
-                const float4 dm = *reinterpret_cast<const float4*>(p.d_mean + size_t(row) * 4);
-                d0 = dm.x; d1 = dm.y; d2 = dm.z; d3 = dm.w;
-            }
 #pragma unroll 1
             for (int c = 0; c < 4; c++) {
                 float v[32];
                 tc::tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + buf * kRowsBN + half * 128 + c * 32, v);
-                if (kMode == kWideForward) {
 #pragma unroll
-                    for (int q = 0; q < 32; q += 4) {
-                        const uint32_t h = col0 + c * 32 + q;
-                        const float4 b = __ldg(reinterpret_cast<const float4*>(p.b1 + h));
-                        const float4 w0 = __ldg(reinterpret_cast<const float4*>(p.w2 + h));
-                        const float4 w1 = __ldg(reinterpret_cast<const float4*>(p.w2 + p.hidden + h));
-                        const float4 w2 = __ldg(reinterpret_cast<const float4*>(p.w2 + 2 * p.hidden + h));
-                        const float4 w3 = __ldg(reinterpret_cast<const float4*>(p.w2 + 3 * p.hidden + h));
-                        const float a0 = wide_tanh(v[q] + b.x), a1 = wide_tanh(v[q + 1] + b.y);
-                        const float a2 = wide_tanh(v[q + 2] + b.z), a3 = wide_tanh(v[q + 3] + b.w);
-                        pm0 = fmaf(a3, w0.w, fmaf(a2, w0.z, fmaf(a1, w0.y, fmaf(a0, w0.x, pm0))));
-                        pm1 = fmaf(a3, w1.w, fmaf(a2, w1.z, fmaf(a1, w1.y, fmaf(a0, w1.x, pm1))));
-                        pm2 = fmaf(a3, w2.w, fmaf(a2, w2.z, fmaf(a1, w2.y, fmaf(a0, w2.x, pm2))));
-                        pm3 = fmaf(a3, w3.w, fmaf(a2, w3.z, fmaf(a1, w3.y, fmaf(a0, w3.x, pm3))));
-                    }
-                } else {
-                    // tanh, delta, and the per-column products; the deltas go to HBM
-                    // (zeros for rows past the minibatch: the dW1 product reads whole
-                    // 32-row groups).
-                    float th[32];
-#pragma unroll
-                    for (int q = 0; q < 32; q += 4) {
-                        const uint32_t h = col0 + c * 32 + q;
-                        const float4 b = __ldg(reinterpret_cast<const float4*>(p.b1 + h));
-                        const float4 w0 = __ldg(reinterpret_cast<const float4*>(p.w2 + h));
-                        const float4 w1 = __ldg(reinterpret_cast<const float4*>(p.w2 + p.hidden + h));
-                        const float4 w2 = __ldg(reinterpret_cast<const float4*>(p.w2 + 2 * p.hidden + h));
-                        const float4 w3 = __ldg(reinterpret_cast<const float4*>(p.w2 + 3 * p.hidden + h));
-                        const float bb[4] = {b.x, b.y, b.z, b.w};
-                        const float ww0[4] = {w0.x, w0.y, w0.z, w0.w}, ww1[4] = {w1.x, w1.y, w1.z, w1.w};
-                        const float ww2[4] = {w2.x, w2.y, w2.z, w2.w}, ww3[4] = {w3.x, w3.y, w3.z, w3.w};
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const float a = wide_tanh(v[q + e] + bb[e]);
-                            const float g = d0 * ww0[e] + d1 * ww1[e] + d2 * ww2[e] + d3 * ww3[e];
-                            th[q + e] = a;
-                            v[q + e] = g * (1.0f - a * a);
-                        }
-                    }
-                    float4* dst = reinterpret_cast<float4*>(p.delta + size_t(row) * p.hidden + col0 + c * 32);
-#pragma unroll
-                    for (int q = 0; q < 8; q++)
-                        dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                    // column sums over this warp's 32 rows, accumulated per warp
-                    float t[32];
-                    my_sums[0 * 128 + c * 32 + lane] += warp_column_sums(v, lane);
-#pragma unroll
-                    for (int q = 0; q < 32; q++) t[q] = d0 * th[q];
-                    my_sums[1 * 128 + c * 32 + lane] += warp_column_sums(t, lane);
-#pragma unroll
-                    for (int q = 0; q < 32; q++) t[q] = d1 * th[q];
-                    my_sums[2 * 128 + c * 32 + lane] += warp_column_sums(t, lane);
-#pragma unroll
-                    for (int q = 0; q < 32; q++) t[q] = d2 * th[q];
-                    my_sums[3 * 128 + c * 32 + lane] += warp_column_sums(t, lane);
-#pragma unroll
-                    for (int q = 0; q < 32; q++) t[q] = d3 * th[q];
-                    my_sums[4 * 128 + c * 32 + lane] += warp_column_sums(t, lane);
+                for (int q = 0; q < 32; q += 4) {
+                    const uint32_t h = col0 + c * 32 + q;
+                    const float4 b = __ldg(reinterpret_cast<const float4*>(p.b1 + h));
+                    const float4 w0 = __ldg(reinterpret_cast<const float4*>(p.w2 + h));
+                    const float4 w1 = __ldg(reinterpret_cast<const float4*>(p.w2 + p.hidden + h));
+                    const float4 w2 = __ldg(reinterpret_cast<const float4*>(p.w2 + 2 * p.hidden + h));
+                    const float4 w3 = __ldg(reinterpret_cast<const float4*>(p.w2 + 3 * p.hidden + h));
+                    const float a0 = wide_tanh(v[q] + b.x), a1 = wide_tanh(v[q + 1] + b.y);
+                    const float a2 = wide_tanh(v[q + 2] + b.z), a3 = wide_tanh(v[q + 3] + b.w);
+                    pm0 = fmaf(a3, w0.w, fmaf(a2, w0.z, fmaf(a1, w0.y, fmaf(a0, w0.x, pm0))));
+                    pm1 = fmaf(a3, w1.w, fmaf(a2, w1.z, fmaf(a1, w1.y, fmaf(a0, w1.x, pm1))));
+                    pm2 = fmaf(a3, w2.w, fmaf(a2, w2.z, fmaf(a1, w2.y, fmaf(a0, w2.x, pm2))));
+                    pm3 = fmaf(a3, w3.w, fmaf(a2, w3.z, fmaf(a1, w3.y, fmaf(a0, w3.x, pm3))));
                 }
             }
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&s.tempty[buf]);
-            if (kMode == kWideForward && valid) {
+            if (row < rows) {
                 const uint32_t slice = n * 2 + half;
                 *reinterpret_cast<float4*>(p.partials + (size_t(slice) * p.rows + row) * 4) =
                     make_float4(pm0, pm1, pm2, pm3);
@@ -316,18 +241,170 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, 512);
     }
-    if (kMode == kWideBackward && my_g < groups) {
-        // This CTA's column sums: the four row quarters of each column half, in
-        // quarter order, into colsum_out[group][5][hidden].
-        for (int i = threadIdx.x; i < kColSums * kRowsBN; i += blockDim.x) {
-            const int v = i / kRowsBN, col = i % kRowsBN, hf = col / 128, cc = col % 128;
-            float acc = 0.0f;
-            for (int q = 0; q < 4; q++) {
-                const int w = hf * 4 + ((q + 2) & 3);  // epilogue warp of lane quarter q in half hf
-                acc += colsum[(size_t(w) * kColSums + v) * 128 + cc];
-            }
-            p.colsum_out[(size_t(my_g) * kColSums + v) * p.hidden + my_n * kRowsBN + col] = acc;
+}
+
+// Backward over one minibatch, transposed: tile = 128 hidden units (tensor-
+// memory lanes) x 256 rows (accumulator columns), D = W1 . obs^T, both
+// operands K-major. A thread owns one hidden unit h, so b1[h] and W2[.][h] sit
+// in registers and the column sums over rows (db1, dW2) are per-thread running
+// sums. CTA c keeps hidden tile c % h_tiles and walks row tiles
+// c / h_tiles, + groups, ...; its sums go to colsum_out[group][5][hidden].
+__global__ void __launch_bounds__(kRowsThreads, 1)
+    k_wide_backward(const __grid_constant__ CUtensorMap obs_map, const __grid_constant__ CUtensorMap w1_map,
+                    WideRowsArgs p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stage_base = smem;
+    Barriers& s = *reinterpret_cast<Barriers*>(smem + size_t(kRowsStages) * kRowsStageBytes);
+    float* halves = reinterpret_cast<float*>(smem + size_t(kRowsStages) * kRowsStageBytes + sizeof(Barriers));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const uint32_t rows = p.rows_dev ? p.rows_dev[p.index] : p.rows;
+    const uint32_t row0 = p.row0_dev ? p.row0_dev[p.index] : p.row0;
+    const uint32_t r_tiles = (rows + kBackRows - 1) / kBackRows;
+    const uint32_t h_tiles = p.hidden / kBackHidden;
+    const uint32_t groups = gridDim.x / h_tiles;
+    const uint32_t my_h = blockIdx.x % h_tiles, my_g = blockIdx.x / h_tiles;
+    const uint32_t count = my_g < r_tiles ? (r_tiles - my_g + groups - 1) / groups : 0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRowsStages; i++) {
+            tc::mbar_init(&s.full[i], 1);
+            tc::mbar_init(&s.empty[i], 1);
         }
+        for (int i = 0; i < 2; i++) {
+            tc::mbar_init(&s.tfull[i], 1);
+            tc::mbar_init(&s.tempty[i], kRowsEpiWarps);
+        }
+        tc::mbar_init(&s.done, 1);
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&obs_map);
+        tc::prefetch_tmap(&w1_map);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(&s.tmem_base, 512);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = s.tmem_base;
+
+    if (warp == 0 && lane == 0) {
+        uint32_t it = 0;
+        bool ok = true;
+        for (uint32_t j = 0; j < count && ok; j++) {
+            const uint32_t rt = my_g + j * groups;
+            for (int kp = 0; kp < kObsPanels; kp++, it++) {
+                const uint32_t st = it % kRowsStages, use = it / kRowsStages;
+                if (use > 0 && !tc::mbar_wait(&s.empty[st], (use - 1) & 1, kWaitLimit)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* a_dst = stage_base + size_t(st) * kRowsStageBytes;
+                tc::mbar_arrive_expect_tx(&s.full[st], kRowsStageBytes);
+                tc::tma_load_2d(a_dst, &w1_map, kp * kPanel, int32_t(my_h * kBackHidden), &s.full[st]);
+                tc::tma_load_2d(a_dst + kRowsABytes, &obs_map, kp * kPanel, int32_t(row0 + rt * kBackRows), &s.full[st]);
+            }
+        }
+        for (uint32_t k = it > kRowsStages ? it - kRowsStages : 0; k < it; k++)
+            if (!tc::mbar_wait(&s.full[k % kRowsStages], (k / kRowsStages) & 1, kWaitLimit)) ok = false;
+        if (!ok) atomicOr(p.error, 64u);
+    } else if (warp == 1 && lane == 0) {
+        constexpr uint32_t idesc = tc::tf32_idesc(kBackHidden, kBackRows, 0, 0);
+        uint32_t it = 0;
+        bool ok = true;
+        for (uint32_t j = 0; j < count && ok; j++) {
+            const uint32_t buf = j & 1, use = j >> 1;
+            if (use > 0 && !tc::mbar_wait(&s.tempty[buf], (use - 1) & 1, kWaitLimit)) {
+                ok = false;
+                break;
+            }
+            tc::fence_after_sync();
+            const uint32_t d = tmem + buf * kBackRows;
+            for (int kp = 0; kp < kObsPanels; kp++, it++) {
+                const uint32_t st = it % kRowsStages;
+                if (!tc::mbar_wait(&s.full[st], (it / kRowsStages) & 1, kWaitLimit)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                const uint32_t a_addr = tc::smem_u32(stage_base + size_t(st) * kRowsStageBytes);
+                const uint32_t b_addr = a_addr + kRowsABytes;
+#pragma unroll
+                for (int kk = 0; kk < kPanel / 8; kk++)
+                    tc::mma_tf32(d, tc::sw128_desc(a_addr + kk * 32, 16, 1024), tc::sw128_desc(b_addr + kk * 32, 16, 1024),
+                                 idesc, (kp | kk) != 0);
+                tc::mma_commit(&s.empty[st]);
+            }
+            if (!ok) break;
+            tc::mma_commit(&s.tfull[buf]);
+        }
+        tc::mma_commit(&s.done);
+        if (!tc::mbar_wait(&s.done, 0, kWaitLimit)) ok = false;
+        if (!ok) atomicOr(p.error, 128u);
+    } else if (warp >= 2) {
+        const int ew = warp - 2;
+        const int quarter = warp & 3;   // hidden units 32*quarter .. +31 of the tile
+        const int half = ew >> 2;       // rows [128*half, 128*half+128) of each row tile
+        const uint32_t h = my_h * kBackHidden + quarter * 32 + lane;
+        const float b1s = p.b1[h] * kTwoLog2e;
+        const float w0 = p.w2[h], w1 = p.w2[p.hidden + h], w2 = p.w2[2 * p.hidden + h], w3 = p.w2[3 * p.hidden + h];
+        float s_delta = 0.0f, s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+        bool ok = true;
+        for (uint32_t j = 0; j < count; j++) {
+            const uint32_t rt = my_g + j * groups;
+            const uint32_t buf = j & 1, use = j >> 1;
+            if (!tc::mbar_wait(&s.tfull[buf], use & 1, kWaitLimit)) {
+                ok = false;
+                break;
+            }
+            tc::fence_after_sync();
+            const uint32_t r_base = rt * kBackRows + half * 128;
+#pragma unroll 1
+            for (int c = 0; c < 4; c++) {
+                float v[32];
+                tc::tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + buf * kBackRows + half * 128 + c * 32, v);
+#pragma unroll
+                for (int q = 0; q < 32; q++) {
+                    const uint32_t row = r_base + c * 32 + q;
+                    // rows past the minibatch get d_mean = 0, hence delta = 0 (the dW1
+                    // product reads whole 32-row groups)
+                    const float4 dm = row < rows ? __ldg(reinterpret_cast<const float4*>(p.d_mean) + row)
+                                                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    const float a = wide_tanh_scaled(fmaf(v[q], kTwoLog2e, b1s));
+                    const float g = fmaf(dm.x, w0, fmaf(dm.y, w1, fmaf(dm.z, w2, dm.w * w3)));
+                    const float delta = g * fmaf(-a, a, 1.0f);
+                    p.delta[size_t(row) * p.hidden + h] = delta;
+                    s_delta += delta;
+                    s0 = fmaf(dm.x, a, s0);
+                    s1 = fmaf(dm.y, a, s1);
+                    s2 = fmaf(dm.z, a, s2);
+                    s3 = fmaf(dm.w, a, s3);
+                }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&s.tempty[buf]);
+        }
+        if (!ok) atomicOr(p.error, 256u);
+        // the two row halves of each hidden unit, half 0 first
+        float* mine = halves + (size_t(quarter) * 32 + lane) * kColSums;
+        if (half == 1) {
+            mine[0] = s_delta; mine[1] = s0; mine[2] = s1; mine[3] = s2; mine[4] = s3;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kRowsEpiWarps * 32) : "memory");
+        if (half == 0) {
+            const float out[kColSums] = {s_delta + mine[0], s0 + mine[1], s1 + mine[2], s2 + mine[3], s3 + mine[4]};
+#pragma unroll
+            for (int v = 0; v < kColSums; v++) p.colsum_out[(size_t(my_g) * kColSums + v) * p.hidden + h] = out[v];
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, 512);
     }
 }
 
@@ -600,11 +677,9 @@ cudaError_t wide_make_map(WideMap* out, const float* base, uint64_t inner, uint6
 }
 
 cudaError_t configure_wide_kernels() {
-    cudaError_t e = cudaFuncSetAttribute(k_wide_rows<kWideForward>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(kRowsSmemFwd));
+    cudaError_t e = cudaFuncSetAttribute(k_wide_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kRowsSmemFwd));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_wide_rows<kWideBackward>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 int(kRowsSmemBwd));
+        e = cudaFuncSetAttribute(k_wide_backward, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kRowsSmemBwd));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_wide_wgrad, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGradSmem));
     return e;
@@ -618,12 +693,12 @@ cudaError_t launch_wide_forward(const WideMap& obs_map, const WideMap& w1_map, c
     to_map(w1_map, wm);
     const uint32_t tiles = ((p.rows + kRowsBM - 1) / kRowsBM) * (p.hidden / kRowsBN);
     const unsigned grid = unsigned(tiles < uint32_t(sm_count) ? tiles : uint32_t(sm_count));
-    k_wide_rows<kWideForward><<<grid, kRowsThreads, kRowsSmemFwd, s>>>(om, wm, p);
+    k_wide_forward<<<grid, kRowsThreads, kRowsSmemFwd, s>>>(om, wm, p);
     return cudaGetLastError();
 }
 
 uint32_t wide_backward_groups(uint32_t hidden, int sm_count) {
-    const uint32_t n_tiles = hidden / kRowsBN;
+    const uint32_t n_tiles = hidden / kBackHidden;
     const uint32_t g = uint32_t(sm_count) / n_tiles;
     return g > 0 ? g : 1;
 }
@@ -634,8 +709,8 @@ cudaError_t launch_wide_backward(const WideMap& obs_map, const WideMap& w1_map, 
     CUtensorMap om, wm;
     to_map(obs_map, om);
     to_map(w1_map, wm);
-    const unsigned grid = (p.hidden / kRowsBN) * wide_backward_groups(p.hidden, sm_count);
-    k_wide_rows<kWideBackward><<<grid, kRowsThreads, kRowsSmemBwd, s>>>(om, wm, p);
+    const unsigned grid = (p.hidden / kBackHidden) * wide_backward_groups(p.hidden, sm_count);
+    k_wide_backward<<<grid, kRowsThreads, kRowsSmemBwd, s>>>(om, wm, p);
     return cudaGetLastError();
 }
 

@@ -11,9 +11,7 @@ struct alignas(64) WideMap {
     unsigned char bytes[128];
 };
 
-enum { kWideForward = 0, kWideBackward = 1 };
-
-// Observation rows x hidden tiles (k_wide_rows). The row count and first row
+// Observation rows x hidden units (k_wide_forward, k_wide_backward). The row count and first row
 // are either the fixed `rows`/`row0` or read on the device from
 // rows_dev[index] / row0_dev[index] (the PPO update's per-minibatch arrays,
 // so a captured graph replays unchanged); `rows` is then the capacity.
@@ -30,7 +28,7 @@ struct WideRowsArgs {
     float* partials;            // [hidden/128][rows][4] per-slice output sums
     // backward
     const float* d_mean;        // [rows][4] loss derivatives w.r.t. the means
-    float* delta;               // [ceil128(rows)][hidden] hidden deltas (zero past the rows)
+    float* delta;               // [ceil256(rows)][hidden] hidden deltas (zero past the rows)
     float* colsum_out;          // [groups][5][hidden]: sum delta, sum d_mean[a] * tanh
     uint32_t* error;            // device flag: nonzero when a barrier wait gave up
 };
@@ -88,9 +86,11 @@ cudaError_t configure_wide_kernels();
 cudaError_t launch_wide_forward(const WideMap& obs_map, const WideMap& w1_map, const WideRowsArgs& p, int sm_count,
                                 cudaStream_t s);
 uint32_t wide_backward_groups(uint32_t hidden, int sm_count);
+// obs_map: boxes of 256 rows; w1_map: boxes of 128 rows (the backward tile is
+// 128 hidden units x 256 rows).
 cudaError_t launch_wide_backward(const WideMap& obs_map, const WideMap& w1_map, const WideRowsArgs& p, int sm_count,
                                  cudaStream_t s);
-// delta_map: deltas [ceil128(rows)][hidden], boxes of 32 rows; obs_map: boxes of 32 rows.
+// delta_map: deltas [ceil256(rows)][hidden], boxes of 32 rows; obs_map: boxes of 32 rows.
 cudaError_t launch_wide_wgrad(const WideMap& delta_map, const WideMap& obs_map, const WideGradArgs& p, int sm_count,
                               cudaStream_t s);
 cudaError_t launch_wide_assemble(const WideAssembleArgs& p, int sm_count, cudaStream_t s);
