@@ -123,8 +123,13 @@ typedef struct mdn_raptor_weights {
 typedef struct mdn_rollout_shape {
     uint32_t actor_obs_dim;     /* 184: 2x80 pooled depth + 21 context + 3 hint (ppo.hpp:26-34) */
     uint32_t critic_obs_dim;    /* 32 (ppo.hpp:14-16)                                        */
-    uint32_t actor_hidden;      /* 64 (ppo.hpp:17-19)                                        */
-    uint32_t critic_hidden;     /* 64                                                        */
+    uint32_t actor_hidden;      /* 64 (ppo.hpp:17-19); or a multiple of 256 up to 8192: the
+                                   one-hidden-layer tanh actor at that width (5120 = the
+                                   967,688-parameter actor of FIXED_PPO_HIDDEN_DIM=5120,
+                                   navigation_wide_deployment.hpp:54-66), evaluated and
+                                   trained on the tensor cores (TF32 products, fp32
+                                   accumulation)                                          */
+    uint32_t critic_hidden;     /* 64 (the only critic width in this build)                  */
     uint32_t flags;             /* MDN_SHAPE_* bits                                          */
     float room_min[3];          /* wray/wclearance room, world.hpp:73-74,85: (-2,-5,0)       */
     float room_max[3];          /*                                        (14, 5,5)          */
@@ -214,7 +219,8 @@ typedef struct mdn_ppo mdn_ppo;
 int mdn_device_open(int gpu, mdn_device** out);                 /* Metal::Metal, main.mm:50-52 */
 int mdn_device_close(mdn_device* dev);
 /* Metal::finish (main.mm:71): wait for all work queued on the device's sims and
- * trainers, raise any device error, return the GPU time since the last sync. */
+ * trainers, raise any device error, return the GPU time since the last sync.
+ * MDN_ERR_TIMEOUT when a wide-actor kernel's bounded barrier wait gave up. */
 int mdn_sync(mdn_device* dev, double* gpu_seconds);
 
 /* ---- simulator: Sim (main.mm:516-603) ----------------------------------- */
