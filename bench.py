@@ -66,7 +66,11 @@ def parse():
     ap.add_argument("--horizon", type=int, default=128)
     ap.add_argument("--epochs", type=int, default=4)
     ap.add_argument("--minibatches", type=int, default=16)
-    ap.add_argument("--family", type=int, default=17)
+    ap.add_argument("--family", type=int, default=18,
+                    help="18 = mixed capability (BASELINE configs 2/4: 50%% static clutter, 25%% long-goal rooms, "
+                         "25%% combined courses with movers); 17 = static clutter only")
+    ap.add_argument("--delay", type=int, default=2,
+                    help="sensor and command delay in policy ticks (2 = the 100 ms buffers of BASELINE config 2)")
     ap.add_argument("--actor-hidden", type=int, default=64,
                     help="64 = the reference's 12,104-parameter actor; 5120 = the 967,688-parameter wide actor "
                          "(BASELINE config 3), evaluated on the tcgen05 tensor cores")
@@ -216,7 +220,7 @@ def measure_wide(pkg, dev, dist, args, peaks):
     L = pkg.layouts
     n = WIDE_ENVS // dist.world
     horizon, epochs, minibatches, steps = 128, 4, 16, 2
-    cfg = L.default_config(n=n, family=args.family, seed=43)
+    cfg = L.default_config(n=n, family=17, seed=43)
     sim = pkg.Sim(dev, cfg, horizon, actor_hidden=WIDE_HIDDEN)
     tr = pkg.PPOTrainer(sim, epochs=epochs, minibatch=n * horizon // minibatches)
     try:
@@ -252,7 +256,7 @@ def measure_wide(pkg, dev, dist, args, peaks):
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_reference_sample(layouts, n, policy_steps, family, warmup=0, threads=None):
+def cpu_reference_sample(layouts, n, policy_steps, family, warmup=0, threads=None, delay=0):
     """The reference's own CPU path (oracle/_ref: cpu_reference.hpp compiled
     unmodified) on a bounded sample: `n` environments with the benchmark's
     family-17 worlds, `warmup` untimed then `policy_steps` timed policy steps,
@@ -265,17 +269,18 @@ def cpu_reference_sample(layouts, n, policy_steps, family, warmup=0, threads=Non
     olib = om.load_oracle()
     threads = threads or os.cpu_count()
     ref.ref_set_threads(threads)
-    cfg = layouts.default_config(n=n, family=1, seed=42)
+    cfg = layouts.default_config(n=n, family=1, seed=42, sensor_delay=delay, command_delay=delay)
     raptor = layouts.load_raptor_file(ROOT / "metal-drone-nav_b200" / "assets" / "raptor.bin")
     tr = om.RefTrainer(layouts, cfg, warmup + policy_steps, raptor, lib=ref)
     worlds = tr.buf("worlds")
-    # Family-17 worlds drawn as the simulator's reset draws them (seed per env,
-    # sim.metal:56-58), generated by the C restatement: the reference has no
-    # generator for this family. Later resets inside the sample use family 1.
+    # The benchmark's worlds (families 17-20) drawn as the simulator's reset
+    # draws them (seed per env, sim.metal:56-58), generated by the C
+    # restatement: the reference has no generator for these families. Later
+    # resets inside the sample use family 1.
     rng = np.zeros(1, np.uint32)
     for i in range(n):
         rng[0] = (42 + i * 747796405 + 2891336453) & 0xFFFFFFFF
-        fam = olib.o_wtraining_family(family, om.ptr(rng))
+        fam = olib.o_mixed_lane_family(i) if family == 18 else olib.o_wtraining_family(family, om.ptr(rng))
         seed = olib.o_wrng(om.ptr(rng))
         olib.o_wgenerate(om.ptr(worlds[i:i + 1]), seed, fam, 4.0)
     for t in range(warmup):
@@ -297,7 +302,7 @@ def cpu_reference_sample(layouts, n, policy_steps, family, warmup=0, threads=Non
     return {"env_steps_per_s": n * policy_steps / collect_s, "collect_s": collect_s, "threads": threads,
             "per_row_epoch_s": per_row_epoch, "kind": kind,
             "sample": f"{n} envs x {policy_steps} policy steps of cpu_reference::Trainer (compiled unmodified, "
-                      f"OpenMP stand-ins for GCD/Accelerate) on family-17 worlds; PPO cost from one "
+                      f"OpenMP stand-ins for GCD/Accelerate) on family-{family} worlds, delays {delay}; PPO cost from one "
                       f"train_rollout over 1024x4 rows (2 epochs x 256-row chunks)"}
 
 
@@ -313,7 +318,7 @@ def run_reference_arm(args, dist, out_fd):
     # warm-up and timed steps: each step = one policy step over all environments
     samples = []
     per_row = None
-    s = cpu_reference_sample(layouts, envs, args.steps, args.family, warmup=args.warmup)
+    s = cpu_reference_sample(layouts, envs, args.steps, args.family, warmup=args.warmup, delay=args.delay)
     value = s["env_steps_per_s"]
     per_row = s["per_row_epoch_s"]
     rows = envs * args.horizon
@@ -336,10 +341,13 @@ def run_reference_arm(args, dist, out_fd):
 def workload_config(args):
     actor = ("184->64->4 tanh actor" if args.actor_hidden == 64 else
              f"184->{args.actor_hidden}->4 tanh actor on tcgen05 TF32")
-    return {"workload": f"BASELINE config 4 on one shard set: {args.envs:,} envs, family-17 clutter rooms (16 static "
-                        f"boxes), 20x16 depth rays, {actor}, 32->64->1 critic, T={args.horizon} rollouts, "
-                        f"PPO {args.epochs} epochs x {args.minibatches} minibatches",
-            "envs": args.envs, "horizon": args.horizon, "family": args.family, "epochs": args.epochs,
+    scene = ("mixed capability (50% static clutter rooms of 16 boxes, 25% long-goal rooms, 25% combined courses of "
+             "12 boxes + 4 bounded movers)" if args.family == 18 else f"family-{args.family} worlds")
+    return {"workload": f"BASELINE config 4 on one shard set: {args.envs:,} envs, {scene}, {args.delay}-tick "
+                        f"(100 ms at 2) sensor and command delays, 20x16 depth rays, {actor}, 32->64->1 critic, "
+                        f"T={args.horizon} rollouts, PPO {args.epochs} epochs x {args.minibatches} minibatches",
+            "envs": args.envs, "horizon": args.horizon, "family": args.family, "delay_ticks": args.delay,
+            "epochs": args.epochs,
             "minibatches": args.minibatches, "actor_hidden": args.actor_hidden,
             "parallelism": f"dp{args.gpus} (envs sharded)",
             "l2": "inputs larger than L2 (obs buffer > 6 GB per rollout)"}
@@ -372,7 +380,7 @@ def main():
     if world > 1:
         uid = dist.broadcast_bytes(pkg.Device.comm_unique_id() if dist.rank == 0 else None)
         dev.comm_init(dist.rank, world, uid)
-    cfg = L.default_config(n=n, family=args.family, seed=42)
+    cfg = L.default_config(n=n, family=args.family, seed=42, sensor_delay=args.delay, command_delay=args.delay)
     sim = pkg.Sim(dev, cfg, args.horizon, actor_hidden=None if args.actor_hidden == 64 else args.actor_hidden)
     rows = n * args.horizon
     minibatch = rows // args.minibatches
@@ -482,7 +490,7 @@ def main():
     if not args.no_wide and args.actor_hidden == 64:
         line["wide_actor"] = measure_wide(pkg, dev, dist, args, peaks)
     if world == 1 and dist.rank == 0 and not args.no_cpu_baseline:
-        s = cpu_reference_sample(L, args.envs, 2, args.family, warmup=1)
+        s = cpu_reference_sample(L, args.envs, 2, args.family, warmup=1, delay=args.delay)
         if s is not None:
             line["cpu_baseline"] = {"value": s["env_steps_per_s"], "unit": "env-steps/s", "cores": s["threads"],
                                     "kind": s["kind"], "sample": s["sample"],

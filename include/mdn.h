@@ -330,6 +330,20 @@ int mdn_gae_normalize_static(const float* rewards, const float* values, const fl
                              float* returns, uint32_t horizon, uint32_t envs, float gamma, float lambda,
                              void* stream);
 
+/* ---- deployment export ----------------------------------------------- */
+/* Write a trained actor in the reference's deployable format: NAVPOL1 for the
+ * 64-unit actor (nav_deployment::NavigationPolicy::write_file,
+ * deployment.hpp:166-201), NAVWID4 for wider ones (the format
+ * nav_deployment::WideNavigationPolicy::load reads,
+ * navigation_wide_deployment.hpp:15-40). `actor` is the flat parameter vector
+ * (ppo.hpp:35-40) of an actor `hidden` units wide, in host memory;
+ * `source_checkpoint` is hashed (FNV-1a 64) into the provenance trailer;
+ * max_speed_mps is the command scale of NavigationPolicy::infer. */
+int mdn_policy_write(const char* path, const float* actor, uint32_t hidden, const char* source_checkpoint,
+                     float max_speed_mps);
+/* The same for the simulator's current actor (downloaded from the device). */
+int mdn_sim_export_policy(mdn_sim* sim, const char* path, const char* source_checkpoint, float max_speed_mps);
+
 /* ---- multi-GPU (no reference counterpart: the reference is one Apple GPU) */
 /* Fill a 128-byte NCCL unique id (rank 0) to share through any host channel. */
 int mdn_comm_unique_id(uint8_t id[128]);

@@ -64,6 +64,8 @@ SIGNATURES = {
     "mdn_sim_last_collect_ms": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float)]),
     "mdn_sim_profile_step": (ctypes.c_int, [_P, _U, _P]),
     "mdn_launch_counts": (ctypes.c_int, [_P, _P, ctypes.POINTER(_U), ctypes.POINTER(_U)]),
+    "mdn_policy_write": (ctypes.c_int, [ctypes.c_char_p, _P, _U, ctypes.c_char_p, ctypes.c_float]),
+    "mdn_sim_export_policy": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_float]),
     "mdn_device_fp32_peak": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_double)]),
     "mdn_ppo_create": (ctypes.c_int, [_P, _U, _U, ctypes.POINTER(_P)]),
     "mdn_ppo_destroy": (ctypes.c_int, [_P]),
@@ -258,6 +260,10 @@ class Sim:
         a = np.ascontiguousarray(array)
         check(lib().mdn_sim_upload(self.h, layouts.BUF[name], _ptr(a), offset, a.nbytes))
 
+    def export_policy(self, path, source_checkpoint, max_speed_mps=1.5):
+        """Deployable actor file (NAVPOL1, or NAVWID4 for a wide actor)."""
+        check(lib().mdn_sim_export_policy(self.h, str(path).encode(), str(source_checkpoint).encode(), max_speed_mps))
+
     def configure_tasks(self, control, domain_amplitude=0.0):
         """navigation_training::configure: enable goal-arrival tasks and reset."""
         ctl = np.array(control, layouts.TASK_CONTROL)
@@ -344,3 +350,10 @@ class PPOTrainer:
 
     def load_checkpoint(self, path, family, horizon, n, seed):
         check(lib().mdn_ppo_checkpoint_load(self.h, str(path).encode(), family, horizon, n, seed))
+
+
+def write_policy(path, actor, hidden, source_checkpoint, max_speed_mps=1.5):
+    """mdn_policy_write: a deployable actor file from host parameters (no device needed)."""
+    a = np.ascontiguousarray(actor, np.float32)
+    check(lib().mdn_policy_write(str(path).encode(), _ptr(a), int(hidden), str(source_checkpoint).encode(),
+                                 max_speed_mps))

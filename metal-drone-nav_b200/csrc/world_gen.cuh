@@ -40,6 +40,88 @@ struct WorldBuilder {
 
 __device__ __forceinline__ float challenge_span(float d) { return fminf(fmaxf(d, 3.0f), 10.0f); }  // world.hpp:225
 
+// Mixed-capability lanes (families 19, 20; no reference generator, IEEE-exact
+// operations only, identical to the oracle's restatement). Goal: a random
+// horizontal direction (8 rejection tries) at distance dmin + dspan*U,
+// clamped into the room.
+__device__ __forceinline__ void clutter_goal(mdn_world& w, uint32_t& rng, float dmin, float dspan, float xmax) {
+    float dx = 1.0f, dy = 0.0f;
+    for (int attempt = 0; attempt < 8; attempt++) {
+        const float ux = 2.0f * wurand(rng) - 1.0f, uy = 2.0f * wurand(rng) - 1.0f;
+        const float norm = sqrtf(ux * ux + uy * uy);
+        if (norm > 0.1f && norm <= 1.0f) {
+            dx = ux / norm;
+            dy = uy / norm;
+            break;
+        }
+    }
+    const float dist = dmin + dspan * wurand(rng);
+    w.goal[0] = fminf(fmaxf(dist * dx, -1.5f), xmax);
+    w.goal[1] = fminf(fmaxf(dist * dy, -4.5f), 4.5f);
+    w.goal[2] = 1.0f + wurand(rng);
+}
+// Static boxes with centres in x[-2,-2+xspan] y[-5,5] z[0,4], half-extents
+// U(0.2,1.0); redrawn (8 tries, else left out) unless 0.5 m clear of start and goal.
+__device__ __forceinline__ void clutter_boxes(mdn_world& w, uint32_t& rng, int boxes, float xspan) {
+    WorldBuilder b{w};
+    for (int i = 0; i < boxes; i++)
+        for (int attempt = 0; attempt < 8; attempt++) {
+            const float cx = -2.0f + xspan * wurand(rng), cy = -5.0f + 10.0f * wurand(rng), cz = 4.0f * wurand(rng);
+            const float ex = 0.2f + 0.8f * wurand(rng), ey = 0.2f + 0.8f * wurand(rng), ez = 0.2f + 0.8f * wurand(rng);
+            const float size[3] = {ex, ey, ez};
+            const float ds = box_distance(size, 0.0f - cx, 0.0f - cy, 1.5f - cz);
+            const float dg = box_distance(size, w.goal[0] - cx, w.goal[1] - cy, w.goal[2] - cz);
+            if (ds > 0.5f && dg > 0.5f) {
+                b.box(cx, cy, cz, ex, ey, ez);
+                break;
+            }
+        }
+}
+// Bounded moving spheres (kind 3, world.hpp:32-41) whose whole swept segment
+// (17 samples) clears the static boxes by radius + 0.05 m, the start by
+// radius + 0.5 m and the goal by radius + 0.3 m (8 tries each, else left out).
+__device__ __forceinline__ void clutter_movers(mdn_world& w, uint32_t& rng, int movers) {
+    const uint32_t statics = w.count;
+    for (int i = 0; i < movers && w.count < 16; i++)
+        for (int attempt = 0; attempt < 8; attempt++) {
+            const float c[3] = {-2.0f + 10.0f * wurand(rng), -5.0f + 10.0f * wurand(rng), 0.5f + 3.0f * wurand(rng)};
+            const float radius = 0.2f + 0.3f * wurand(rng);
+            const float amplitude = 0.5f + 1.5f * wurand(rng);
+            const float speed = 0.5f + 1.5f * wurand(rng);
+            const float phase = 6.2831853f * wurand(rng);
+            const float ux = 2.0f * wurand(rng) - 1.0f, uy = 2.0f * wurand(rng) - 1.0f, uz = 2.0f * wurand(rng) - 1.0f;
+            const float norm = sqrtf(ux * ux + uy * uy + uz * uz);
+            if (!(norm > 0.1f && norm <= 1.0f)) continue;
+            const float d[3] = {ux / norm, uy / norm, uz / norm};
+            bool ok = true;
+            for (int k = 0; k <= 16 && ok; k++) {
+                const float f = amplitude * (float(k) / 8.0f - 1.0f);
+                const float p[3] = {c[0] + d[0] * f, c[1] + d[1] * f, c[2] + d[2] * f};
+                for (uint32_t o = 0; o < statics && ok; o++) {
+                    const mdn_obstacle& ob = w.obstacles[o];
+                    if (!(box_distance(ob.size, p[0] - ob.center[0], p[1] - ob.center[1], p[2] - ob.center[2]) >
+                          radius + 0.05f))
+                        ok = false;
+                }
+                const float ds = len3(p[0] - 0.0f, p[1] - 0.0f, p[2] - 1.5f);
+                const float dg = len3(p[0] - w.goal[0], p[1] - w.goal[1], p[2] - w.goal[2]);
+                if (!(ds > radius + 0.5f) || !(dg > radius + 0.3f)) ok = false;
+            }
+            if (ok) {
+                WorldBuilder{w}.add(3, c[0], c[1], c[2], radius, amplitude, phase, d[0] * speed, d[1] * speed,
+                                    d[2] * speed);
+                break;
+            }
+        }
+}
+
+// Family 18 (mixed capability, BASELINE configs 2 and 4): the generator family
+// of global env gid - 50% static clutter (17), 25% long-goal rooms (19), 25%
+// combined courses with movers (20).
+__device__ __forceinline__ uint32_t mixed_lane_family(uint32_t gid) {
+    return (gid & 3u) < 2u ? 17u : ((gid & 3u) == 2u ? 19u : 20u);
+}
+
 // wgenerate, world.hpp:299-318, with every family generator of world.hpp:138-291.
 __device__ void generate_world(mdn_world& w, uint32_t seed, uint32_t family, float distance) {
     uint32_t rng = seed ? seed : 1;
@@ -219,6 +301,19 @@ __device__ void generate_world(mdn_world& w, uint32_t seed, uint32_t family, flo
             }
         return;
     }
+    if (family == 19) {  // long-goal room (see clutter_goal)
+        w.count = 0;
+        clutter_goal(w, rng, 2.0f, 10.0f, 13.5f);
+        clutter_boxes(w, rng, 16, 16.0f);
+        return;
+    }
+    if (family == 20) {  // combined course: 12 static boxes + 4 movers
+        w.count = 0;
+        clutter_goal(w, rng, 2.0f, 6.0f, 7.5f);
+        clutter_boxes(w, rng, 12, 10.0f);
+        clutter_movers(w, rng, 4);
+        return;
+    }
     // Families 0-3 (and any other id): 16 random primitives, :311-317.
     for (int i = 0; i < 16; i++) {
         mdn_obstacle& o = w.obstacles[i];
@@ -275,7 +370,7 @@ __device__ bool reset_env(const SimArgs& a, uint32_t i, bool first) {
     mdn_physics_state& s = a.states[i];
     mdn_world& w = a.worlds[i];
     uint32_t rng = first ? (c.seed + gid * 747796405u + 2891336453u) : run.rng;
-    const uint32_t family = training_family(c.family, rng);
+    const uint32_t family = c.family == 18u ? mixed_lane_family(gid) : training_family(c.family, rng);
     generate_world(w, wrng(rng), family, c.distance);
     w.wind[0] = clean_env(c, gid) ? 0.0f : c.wind;
     w.wind[1] = 0;

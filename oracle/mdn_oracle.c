@@ -411,6 +411,86 @@ static void wgenerate_baseline_clutter(mdn_world* w, uint32_t* rng) {
         }
 }
 
+/* Families 19 and 20: the long-goal and combined-course lanes of the
+ * mixed-capability distribution (family 18). No reference generator exists
+ * (the reference's course runners are outside its tracked tree); IEEE-exact
+ * operations only, so the CUDA generator reproduces them bit for bit.
+ *   19: 16 static boxes over the reference room x[-2,14] y[-5,5] z[0,4],
+ *       half-extents U(0.2,1.0), goal 2-12 m from the start.
+ *   20: 12 static boxes as family 17, then 4 bounded moving spheres (kind 3,
+ *       world.hpp:32-41): centre uniform in x[-2,8] y[-5,5] z[0.5,3.5], radius
+ *       U(0.2,0.5), amplitude U(0.5,2.0) m, peak speed U(0.5,2.0) m/s, phase
+ *       U(0,2pi), random unit direction; a mover is redrawn (8 tries, else left
+ *       out) unless its whole swept segment, sampled at 17 points, stays
+ *       radius + 0.05 m clear of every static box and radius + 0.5 m clear of
+ *       the start, radius + 0.3 m clear of the goal. */
+static void wgenerate_clutter_goal(mdn_world* w, uint32_t* rng, float dmin, float dspan, float xmax) {
+    float dx = 1.0f, dy = 0.0f;
+    for (int attempt = 0; attempt < 8; attempt++) {
+        const float ux = 2.0f * o_wurand(rng) - 1.0f, uy = 2.0f * o_wurand(rng) - 1.0f;
+        const float norm = sqrtf(ux * ux + uy * uy);
+        if (norm > 0.1f && norm <= 1.0f) {
+            dx = ux / norm;
+            dy = uy / norm;
+            break;
+        }
+    }
+    const float dist = dmin + dspan * o_wurand(rng);
+    w->goal[0] = fminf(fmaxf(dist * dx, -1.5f), xmax);
+    w->goal[1] = fminf(fmaxf(dist * dy, -4.5f), 4.5f);
+    w->goal[2] = 1.0f + o_wurand(rng);
+}
+static void wgenerate_clutter_boxes(mdn_world* w, uint32_t* rng, int boxes, float xspan) {
+    const float start[3] = {0.0f, 0.0f, 1.5f};
+    for (int i = 0; i < boxes; i++)
+        for (int attempt = 0; attempt < 8; attempt++) {
+            const float c[3] = {-2.0f + xspan * o_wurand(rng), -5.0f + 10.0f * o_wurand(rng), 4.0f * o_wurand(rng)};
+            const float e[3] = {0.2f + 0.8f * o_wurand(rng), 0.2f + 0.8f * o_wurand(rng), 0.2f + 0.8f * o_wurand(rng)};
+            if (box_sdf(start, c, e) > 0.5f && box_sdf(w->goal, c, e) > 0.5f) {
+                wadd_box(w, c[0], c[1], c[2], e[0], e[1], e[2]);
+                break;
+            }
+        }
+}
+static void wgenerate_movers(mdn_world* w, uint32_t* rng, int movers) {
+    const float start[3] = {0.0f, 0.0f, 1.5f};
+    const uint32_t statics = w->count;
+    for (int i = 0; i < movers && w->count < 16; i++)
+        for (int attempt = 0; attempt < 8; attempt++) {
+            const float c[3] = {-2.0f + 10.0f * o_wurand(rng), -5.0f + 10.0f * o_wurand(rng), 0.5f + 3.0f * o_wurand(rng)};
+            const float radius = 0.2f + 0.3f * o_wurand(rng);
+            const float amplitude = 0.5f + 1.5f * o_wurand(rng);
+            const float speed = 0.5f + 1.5f * o_wurand(rng);
+            const float phase = 6.2831853f * o_wurand(rng);
+            const float ux = 2.0f * o_wurand(rng) - 1.0f, uy = 2.0f * o_wurand(rng) - 1.0f, uz = 2.0f * o_wurand(rng) - 1.0f;
+            const float norm = sqrtf(ux * ux + uy * uy + uz * uz);
+            if (!(norm > 0.1f && norm <= 1.0f)) continue;
+            const float d[3] = {ux / norm, uy / norm, uz / norm};
+            int ok = 1;
+            for (int k = 0; k <= 16 && ok; k++) {
+                const float f = amplitude * ((float)k / 8.0f - 1.0f);
+                const float p[3] = {c[0] + d[0] * f, c[1] + d[1] * f, c[2] + d[2] * f};
+                for (uint32_t b = 0; b < statics && ok; b++)
+                    if (!(box_sdf(p, w->obstacles[b].center, w->obstacles[b].size) > radius + 0.05f)) ok = 0;
+                const float ds = len3(p[0] - start[0], p[1] - start[1], p[2] - start[2]);
+                const float dg = len3(p[0] - w->goal[0], p[1] - w->goal[1], p[2] - w->goal[2]);
+                if (!(ds > radius + 0.5f) || !(dg > radius + 0.3f)) ok = 0;
+            }
+            if (ok) {
+                mdn_obstacle* o = &w->obstacles[w->count++];
+                o->kind = 3;
+                o->center[0] = c[0]; o->center[1] = c[1]; o->center[2] = c[2];
+                o->size[0] = radius; o->size[1] = amplitude; o->size[2] = phase;
+                o->velocity[0] = d[0] * speed; o->velocity[1] = d[1] * speed; o->velocity[2] = d[2] * speed;
+                break;
+            }
+        }
+}
+/* Family 18, mixed capability (BASELINE configs 2 and 4): environments
+ * alternate by global id, 50% static clutter (17), 25% long-goal rooms (19),
+ * 25% combined courses with movers (20). */
+uint32_t o_mixed_lane_family(uint32_t gid) { return (gid & 3u) < 2u ? 17u : ((gid & 3u) == 2u ? 19u : 20u); }
+
 uint32_t o_wtraining_family(uint32_t family, uint32_t* rng) { /* world.hpp:293-298 */
     if (family == 7) return o_wrng(rng) % 7;
     if (family == 9 || family == 12) {
@@ -445,6 +525,17 @@ void o_wgenerate(mdn_world* w, uint32_t seed, uint32_t family, float distance) {
         case 15: w->count = 0; wgenerate_connected_rooms(w, &rng, distance); return;
         case 16: w->count = 0; wgenerate_vertical_choices(w, &rng, distance); return;
         case 17: wgenerate_baseline_clutter(w, &rng); return;
+        case 19:
+            w->count = 0;
+            wgenerate_clutter_goal(w, &rng, 2.0f, 10.0f, 13.5f);
+            wgenerate_clutter_boxes(w, &rng, 16, 16.0f);
+            return;
+        case 20:
+            w->count = 0;
+            wgenerate_clutter_goal(w, &rng, 2.0f, 6.0f, 7.5f);
+            wgenerate_clutter_boxes(w, &rng, 12, 10.0f);
+            wgenerate_movers(w, &rng, 4);
+            return;
         default: break;
     }
     for (int i = 0; i < 16; i++) {
@@ -1425,7 +1516,7 @@ static void reset_one(o_sim* s, uint32_t n, int first) {
     mdn_world* w = &s->worlds[n];
     const uint32_t gid = s->env_base + n;
     uint32_t rng = first ? (c->seed + gid * 747796405u + 2891336453u) : run->rng;
-    const uint32_t family = o_wtraining_family(c->family, &rng);
+    const uint32_t family = c->family == 18u ? o_mixed_lane_family(gid) : o_wtraining_family(c->family, &rng);
     o_wgenerate(w, o_wrng(&rng), family, c->distance);
     w->wind[0] = clean_env(c, gid) ? 0.0f : c->wind;
     w->wind[1] = 0;

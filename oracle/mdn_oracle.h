@@ -30,6 +30,8 @@ float o_wray(const mdn_world* w, const float* room, const float p[3], const floa
 float o_wclearance(const mdn_world* w, const float* room, const float p[3], float t, int32_t* argmin);
 void o_wgenerate(mdn_world* w, uint32_t seed, uint32_t family, float distance);
 uint32_t o_wtraining_family(uint32_t family, uint32_t* rng);
+/* family 18 (mixed capability): the generator family of global env `gid` */
+uint32_t o_mixed_lane_family(uint32_t gid);
 void o_set_argument_order(int right_to_left);
 uint32_t o_wrng(uint32_t* s);
 float o_wurand(uint32_t* s);

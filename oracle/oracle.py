@@ -55,6 +55,7 @@ def load_oracle():
     d("o_wclearance", _F, _P, _P, _P, _F, _P)
     d("o_wgenerate", None, _P, _U, _U, _F)
     d("o_wtraining_family", _U, _U, _P)
+    d("o_mixed_lane_family", _U, _U)
     d("o_set_argument_order", None, ctypes.c_int)
     d("o_wrng", _U, _P)
     d("o_pixel_ray", None, _F, _F, _U, _P)
@@ -102,6 +103,20 @@ def load_ref_wide():
     d("refw_hidden", _U)
     d("refw_actor_param_count", _U)
     d("refw_actor_forward", None, _P, _P, _U, _P, _P)
+    return lib
+
+
+def load_ref_deploy():
+    """The reference's deployment readers/writer (oracle/_ref/libref_deploy.so),
+    or None when it was never built (no reference sources)."""
+    so = HERE / "_ref" / "libref_deploy.so"
+    if not so.exists():
+        return None
+    lib = ctypes.CDLL(str(so))
+    d = lambda n, r, *a: _declare(lib, n, r, *a)
+    d("refd_write_navpol", ctypes.c_int, ctypes.c_char_p, _P, _F, ctypes.c_char_p)
+    d("refd_load_navpol", ctypes.c_int, ctypes.c_char_p, _P, _P, _P)
+    d("refd_wide_eval", _U, ctypes.c_char_p, _P, _U, _P, _P, _P)
     return lib
 
 

@@ -42,12 +42,17 @@ def om():
     return load_oracle_module()
 
 
-def close(a, b, what, rtol=RTOL, atol=ATOL):
+def close(a, b, what, rtol=RTOL, atol=ATOL, grazing=0.0):
+    """Elementwise |a - b| <= atol + rtol |b|. `grazing` > 0 lets that fraction
+    of the elements (at least one) exceed it: depth rays that graze a moving
+    sphere turn a last-ulp difference of its sinf-placed centre into a larger
+    range difference (the intersection distance scales it by 1/sqrt(disc))."""
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     bad = ~(np.abs(a - b) <= atol + rtol * np.abs(b))
     bad &= ~(np.isnan(a) & np.isnan(b))
-    assert not bad.any(), f"{what}: {bad.sum()} of {bad.size} differ; worst |d|={np.nanmax(np.abs(a - b)):.3e}"
+    allowed = max(1, int(grazing * bad.size)) if grazing > 0 else 0
+    assert bad.sum() <= allowed, f"{what}: {bad.sum()} of {bad.size} differ; worst |d|={np.nanmax(np.abs(a - b)):.3e}"
 
 
 def floats(structured):
@@ -91,6 +96,9 @@ CONFIGS = [
     dict(family=1, mode=1),
     dict(family=4, eval=1, max_steps=9),
     dict(family=17),
+    dict(family=18, sensor_delay=2, command_delay=2),
+    dict(family=19),
+    dict(family=20, max_steps=40),
     dict(family=13, geometry_memory=1, sensor_delay=2),
     dict(family=1, geometry_memory=1, mode=22, command_delay=1, sensor_period=2),
 ]
@@ -112,9 +120,12 @@ def test_teacher_forced_steps(pkg, om, raptor, extra):
     n, T = 256, 12
     cfg = pkg.layouts.default_config(**{**dict(n=n, speed=1.0, distance=3.0, seed=9), **extra})
     gpu, ora = make_pair(pkg, om, raptor, cfg, T)
-    # Depth noise draws Box-Muller normals (logf/cosf, sim.metal:154-156): the
-    # noisy ranges then match to the last ulp only, so compare them with RTOL.
-    exact_depth = float(cfg["depth_noise"]) == 0.0
+    # Depth noise draws Box-Muller normals (logf/cosf, sim.metal:154-156), and
+    # the bounded moving spheres of the mixed-capability courses (families 18,
+    # 20) place their centres with sinf (world.hpp:32-41): ranges of rays that
+    # meet them match to the last ulp only, so compare those with RTOL.
+    movers = 1e-4 if int(cfg["family"]) in (18, 20) else 0.0
+    exact_depth = float(cfg["depth_noise"]) == 0.0 and movers == 0.0
     try:
         for t in range(T):
             # identical inputs: the oracle's state becomes the GPU's state
@@ -129,10 +140,14 @@ def test_teacher_forced_steps(pkg, om, raptor, extra):
             if exact_depth:
                 assert np.array_equal(obs_g[:, :181], obs_o[:, :181]), f"t={t} obs[:181]"
             else:
-                close(obs_g[:, :181], obs_o[:, :181], f"t={t} obs[:181]")
+                close(obs_g[:, :181], obs_o[:, :181], f"t={t} obs[:181]", grazing=movers)
             close(obs_g[:, 181:], obs_o[:, 181:], f"t={t} guidance hint")
-            assert np.array_equal(gpu.download("co").reshape(T * n, 32)[rows],
-                                  ora.buf("co").reshape(T * n, 32)[rows]), f"t={t} critic obs"
+            co_g = gpu.download("co").reshape(T * n, 32)[rows]
+            co_o = ora.buf("co").reshape(T * n, 32)[rows]
+            if exact_depth:
+                assert np.array_equal(co_g, co_o), f"t={t} critic obs"
+            else:  # clearance and obstacle offsets include the sinf-placed movers
+                close(co_g, co_o, f"t={t} critic obs")
             for name in ("actions", "logp", "values", "rewards", "next_values"):
                 g = gpu.download(name).reshape(T * n, -1)[rows]
                 o = ora.buf(name).reshape(T * n, -1)[rows]
@@ -153,7 +168,7 @@ def test_teacher_forced_steps(pkg, om, raptor, extra):
             if exact_depth:
                 assert np.array_equal(gpu.download("sensors"), ora.buf("sensors")), f"t={t} sensors"
             else:
-                close(gpu.download("sensors"), ora.buf("sensors"), f"t={t} sensors")
+                close(gpu.download("sensors"), ora.buf("sensors"), f"t={t} sensors", grazing=movers)
             assert np.array_equal(gpu.download("poses"), ora.buf("poses")), f"t={t} poses"
             close(gpu.download("commands"), ora.buf("commands"), f"t={t} commands")
     finally:
