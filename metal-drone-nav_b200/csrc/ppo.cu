@@ -544,12 +544,295 @@ __global__ void k_metrics_mean(PpoArgs p, uint32_t updates) {
     p.metric_mean[threadIdx.x] = updates ? s / float(updates) : 0.0f;
 }
 
+// Fused minibatch kernel of the 64-unit actor and critic: forward, clipped-PPO
+// loss and derivatives (ppo.hpp:144-181), hidden deltas and the gradient
+// partial of one contiguous run of minibatch rows (cpu_reference.hpp:515-551),
+// without writing the hidden activations or deltas to HBM. CTA c owns rows
+// [c * grad_chunk, (c+1) * grad_chunk) of the minibatch and walks them in
+// 16-row tiles (two CTAs fit an SM and overlap each other's phases); every
+// accumulator adds its rows in row order, and the forward
+// keeps the in-order k chain of the batched reference, so the results equal
+// the unfused kernels' bit for bit.
+//   forward: thread (row = t / 16, hg = t % 16) computes hidden 4hg..4hg+3 of
+//            both networks for its row; inputs are read 4 at a time.
+//   gradient: thread (ty = t / 16, tx = t % 16) accumulates actor W1[4ty+i][12tx+j]
+//            (48 values), critic W1[4ty+i][2tx+j] (8), one W2 entry and one of
+//            the small blocks (b1, critic b1 / w2, b2, log_std, critic b2).
+constexpr int kFuseRows = 16;
+constexpr int kFuseObsPitch = 192;  // 184 inputs + zero padding (12 per gradient thread)
+constexpr size_t kFuseSmemFloats = size_t(kActorObs) * kHidden + size_t(kCriticObs) * kHidden + 4 * kHidden +
+                                   3 * kHidden + 12 + size_t(kFuseRows) * kFuseObsPitch +
+                                   size_t(kFuseRows) * kCriticObs + 4 * size_t(kFuseRows) * kHidden +
+                                   size_t(kFuseRows) * 9 + 4 * kMbThreads;
+
+__global__ void __launch_bounds__(kMbThreads, 2) k_mb_fused(PpoArgs p, uint32_t update) {
+    extern __shared__ __align__(16) float fsm[];
+    float* w1t = fsm;                                   // [184][64]
+    float* cw1t = w1t + kActorObs * kHidden;            // [32][64]
+    float* w2 = cw1t + kCriticObs * kHidden;            // [4][64]
+    float* b1 = w2 + 4 * kHidden;                       // [64]
+    float* cb1 = b1 + kHidden;                          // [64]
+    float* cw2 = cb1 + kHidden;                         // [64]
+    float* small = cw2 + kHidden;                       // b2[4], log_std[4], cb2, pad
+    float* obs = small + 12;                            // [32][192]
+    float* co = obs + kFuseRows * kFuseObsPitch;        // [32][32]
+    float* hid = co + kFuseRows * kCriticObs;           // [32][64]
+    float* chid = hid + kFuseRows * kHidden;            // [32][64]
+    float* dl = chid + kFuseRows * kHidden;             // [32][64] actor hidden deltas
+    float* cdl = dl + kFuseRows * kHidden;              // [32][64] critic hidden deltas
+    float* rowv = cdl + kFuseRows * kHidden;            // [32][9]: d_mean[4], d_log_std[4], d_value
+    float* stage = rowv + kFuseRows * 9;                // [256][4] loss sums
+    float* b2 = small;
+    float* log_std = small + 4;
+    const int tid = threadIdx.x;
+    const float* actor = p.actor;
+    const float* critic = p.critic;
+    for (int k = tid; k < kActorObs * kHidden; k += kMbThreads) {
+        const int h = k / kActorObs, c = k % kActorObs;
+        w1t[c * kHidden + h] = actor[k];
+    }
+    for (int k = tid; k < kCriticObs * kHidden; k += kMbThreads) {
+        const int h = k / kCriticObs, c = k % kCriticObs;
+        cw1t[c * kHidden + h] = critic[k];
+    }
+    for (int k = tid; k < 4 * kHidden; k += kMbThreads) w2[k] = actor[kActorW2 + k];
+    if (tid < kHidden) {
+        b1[tid] = actor[kActorB1 + tid];
+        cb1[tid] = critic[kCriticB1 + tid];
+        cw2[tid] = critic[kCriticW2 + tid];
+    }
+    if (tid < 4) {
+        b2[tid] = actor[p.actor_b2 + tid];
+        log_std[tid] = actor[p.actor_log_std + tid];
+    }
+    if (tid == 0) small[8] = critic[kCriticB2];
+    for (int k = tid; k < kFuseRows * kFuseObsPitch; k += kMbThreads) obs[k] = 0.0f;  // padding stays zero
+    const float cb2 = critic[kCriticB2];
+
+    const uint32_t begin = p.starts[update];
+    const uint32_t b = p.batch[update];
+    const float scale = 1.0f / fmaxf(float(p.global_batch[update]), 1.0f);
+    const uint32_t c0 = blockIdx.x * p.grad_chunk;
+    const uint32_t c1 = min(b, c0 + p.grad_chunk);
+    const int rg = tid >> 4, hg = tid & 15;   // forward mapping
+    const int ty = tid >> 4, tx = tid & 15;   // gradient mapping
+    float acc[4][12];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 12; j++) acc[i][j] = 0.0f;
+    float cacc[4][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}};
+    float w2acc = 0.0f, misc = 0.0f;
+    float csum[4] = {0, 0, 0, 0};
+    for (uint32_t r0 = c0; r0 < c1; r0 += kFuseRows) {
+        const int nr = int(min(uint32_t(kFuseRows), c1 - r0));
+        __syncthreads();  // the previous tile's gradient loop is done with the tiles
+        {
+            const float4* og = reinterpret_cast<const float4*>(p.obs + (size_t(begin) + r0) * kActorObs);
+            for (int k = tid; k < nr * (kActorObs / 4); k += kMbThreads) {
+                const int r = k / (kActorObs / 4), c = k % (kActorObs / 4);
+                *reinterpret_cast<float4*>(obs + r * kFuseObsPitch + 4 * c) = og[k];
+            }
+            const float4* cg = reinterpret_cast<const float4*>(p.co + (size_t(begin) + r0) * kCriticObs);
+            for (int k = tid; k < nr * (kCriticObs / 4); k += kMbThreads)
+                reinterpret_cast<float4*>(co)[k] = cg[k];
+        }
+        __syncthreads();
+        // ---- forward: row rg x hidden 4hg..4hg+3 (in-order k chains from zero)
+        float za[4] = {0, 0, 0, 0}, zc[4] = {0, 0, 0, 0};
+        {
+            const float* o0 = obs + rg * kFuseObsPitch;
+#pragma unroll 2
+            for (int k = 0; k < kActorObs; k += 4) {
+                const float4 a = *reinterpret_cast<const float4*>(o0 + k);
+                const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const float4 w = *reinterpret_cast<const float4*>(w1t + (k + kk) * kHidden + 4 * hg);
+                    za[0] = fmaf(av[kk], w.x, za[0]);
+                    za[1] = fmaf(av[kk], w.y, za[1]);
+                    za[2] = fmaf(av[kk], w.z, za[2]);
+                    za[3] = fmaf(av[kk], w.w, za[3]);
+                }
+            }
+            const float* q0 = co + rg * kCriticObs;
+#pragma unroll
+            for (int k = 0; k < kCriticObs; k += 4) {
+                const float4 a = *reinterpret_cast<const float4*>(q0 + k);
+                const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const float4 w = *reinterpret_cast<const float4*>(cw1t + (k + kk) * kHidden + 4 * hg);
+                    zc[0] = fmaf(av[kk], w.x, zc[0]);
+                    zc[1] = fmaf(av[kk], w.y, zc[1]);
+                    zc[2] = fmaf(av[kk], w.z, zc[2]);
+                    zc[3] = fmaf(av[kk], w.w, zc[3]);
+                }
+            }
+        }
+        // ---- activations, loss, derivatives and deltas, one row per half-warp
+        {
+            const int lr = rg;
+            const bool valid = lr < nr;
+            float hv[4], chv[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                hv[j] = tanhf(za[j] + b1[4 * hg + j]);
+                chv[j] = tanhf(zc[j] + cb1[4 * hg + j]);
+            }
+            float mean[4];
+#pragma unroll
+            for (int a = 0; a < 4; a++) {
+                float part = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 4; j++) part = fmaf(hv[j], w2[a * kHidden + 4 * hg + j], part);
+                mean[a] = half_warp_sum(part) + b2[a];
+                if (a < 3) mean[a] += obs[lr * kFuseObsPitch + kActorObs - 3 + a];
+            }
+            float vpart = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) vpart = fmaf(chv[j], cw2[4 * hg + j], vpart);
+            const float value = half_warp_sum(vpart) + cb2;
+            float dm[4] = {0, 0, 0, 0}, dls[4] = {0, 0, 0, 0}, dvalue = 0.0f;
+            if (valid) {
+                const size_t src = size_t(begin) + r0 + lr;
+                const float* act = p.actions + src * kActions;
+                float logp = 0.0f;
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+                    const float inv_std = expf(-log_std[a]);
+                    const float d = (act[a] - mean[a]) * inv_std;
+                    logp += -0.5f * (d * d + 2.0f * log_std[a] + kLogTwoPi);
+                }
+                const float adv = p.advantages[src], ret = p.returns[src];
+                const float raw = logp - p.logp[src];
+                const float lr_ = clampf(raw, -20.0f, 20.0f);
+                const float ratio = expf(lr_);
+                const float clip = p.clip;
+                const float clipped = clampf(ratio, 1.0f - clip, 1.0f + clip);
+                const float chosen = smin(ratio * adv, clipped * adv);
+                const bool in_range = raw >= -20.0f && raw <= 20.0f;
+                const bool active = in_range && (adv >= 0.0f ? ratio <= 1.0f + clip : ratio >= 1.0f - clip);
+                float entropy = 0.0f;
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+                    const float inv_var = expf(-2.0f * log_std[a]);
+                    const float diff = act[a] - mean[a];
+                    if (active) {
+                        const float dlogp = -ratio * adv * scale;
+                        dm[a] = dlogp * diff * inv_var;
+                        dls[a] = dlogp * (diff * diff * inv_var - 1.0f);
+                    }
+                    dls[a] -= p.entropy_coef * scale;
+                    entropy += -p.entropy_coef * (log_std[a] + 0.5f * (1.0f + kLogTwoPi)) * scale;
+                }
+                dvalue = p.value_coef * (value - ret) * scale;
+                if (hg == 0) {
+                    csum[0] += -chosen * scale;
+                    csum[1] += 0.5f * p.value_coef * (value - ret) * (value - ret) * scale;
+                    csum[2] += entropy;
+                    csum[3] += ratio;
+                }
+            }
+            if (hg == 0) {
+                float* rv = rowv + lr * 9;
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+                    rv[a] = dm[a];
+                    rv[4 + a] = dls[a];
+                }
+                rv[8] = dvalue;
+            }
+            float4 hv4, dh4, chv4, cdh4;
+            float* hp = &hv4.x;
+            float* dp = &dh4.x;
+            float* chp = &chv4.x;
+            float* cdp = &cdh4.x;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float s = 0.0f;
+#pragma unroll
+                for (int a = 0; a < 4; a++) s = fmaf(dm[a], w2[a * kHidden + 4 * hg + j], s);
+                hp[j] = hv[j];
+                dp[j] = valid ? s * (1.0f - hv[j] * hv[j]) : 0.0f;
+                chp[j] = chv[j];
+                cdp[j] = valid ? dvalue * cw2[4 * hg + j] * (1.0f - chv[j] * chv[j]) : 0.0f;
+            }
+            *reinterpret_cast<float4*>(hid + lr * kHidden + 4 * hg) = hv4;
+            *reinterpret_cast<float4*>(dl + lr * kHidden + 4 * hg) = dh4;
+            *reinterpret_cast<float4*>(chid + lr * kHidden + 4 * hg) = chv4;
+            *reinterpret_cast<float4*>(cdl + lr * kHidden + 4 * hg) = cdh4;
+        }
+        __syncthreads();
+        // ---- gradient accumulation over the tile's rows, in row order
+        for (int r = 0; r < nr; r++) {
+            const float4 d = *reinterpret_cast<const float4*>(dl + r * kHidden + 4 * ty);
+            const float* orow = obs + r * kFuseObsPitch + 12 * tx;
+            const float4 oa = *reinterpret_cast<const float4*>(orow);
+            const float4 ob = *reinterpret_cast<const float4*>(orow + 4);
+            const float4 oc = *reinterpret_cast<const float4*>(orow + 8);
+            const float ov[12] = {oa.x, oa.y, oa.z, oa.w, ob.x, ob.y, ob.z, ob.w, oc.x, oc.y, oc.z, oc.w};
+            const float dv4[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 12; j++) acc[i][j] = fmaf(dv4[i], ov[j], acc[i][j]);
+            const float4 cd = *reinterpret_cast<const float4*>(cdl + r * kHidden + 4 * ty);
+            const float2 cv = *reinterpret_cast<const float2*>(co + r * kCriticObs + 2 * tx);
+            const float cdv[4] = {cd.x, cd.y, cd.z, cd.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                cacc[i][0] = fmaf(cdv[i], cv.x, cacc[i][0]);
+                cacc[i][1] = fmaf(cdv[i], cv.y, cacc[i][1]);
+            }
+            const float* rv = rowv + r * 9;
+            w2acc = fmaf(rv[tid >> 6], hid[r * kHidden + (tid & 63)], w2acc);  // W2[a][h] = sum d_mean[a] h
+            if (tid < 64) misc += dl[r * kHidden + tid];
+            else if (tid < 128) misc += cdl[r * kHidden + tid - 64];
+            else if (tid < 192) misc = fmaf(rv[8], chid[r * kHidden + tid - 128], misc);
+            else if (tid < 196) misc += rv[tid - 192];
+            else if (tid < 200) misc += rv[4 + tid - 196];
+            else if (tid == 200) misc += rv[8];
+        }
+    }
+    // gradient partial of this CTA (the same layout as k_mb_grad)
+    float* out = p.grad_partials + size_t(blockIdx.x) * kPpoParams;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 12; j++) {
+            const int c = 12 * tx + j;
+            if (c < kActorObs) out[(4 * ty + i) * kActorObs + c] = acc[i][j];
+        }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        out[kActorParams + (4 * ty + i) * kCriticObs + 2 * tx] = cacc[i][0];
+        out[kActorParams + (4 * ty + i) * kCriticObs + 2 * tx + 1] = cacc[i][1];
+    }
+    out[kActorW2 + tid] = w2acc;
+    if (tid < 64) out[kActorB1 + tid] = misc;
+    else if (tid < 128) out[kActorParams + kCriticB1 + tid - 64] = misc;
+    else if (tid < 192) out[kActorParams + kCriticW2 + tid - 128] = misc;
+    else if (tid < 196) out[kActorB2 + tid - 192] = misc;
+    else if (tid < 200) out[kActorLogStd + tid - 196] = misc;
+    else if (tid == 200) out[kActorParams + kCriticB2] = misc;
+    // loss sums of this CTA: per-thread row sums (half-warp leaders), added in thread order
+    __syncthreads();
+    for (int k = 0; k < 4; k++) stage[tid * 4 + k] = csum[k];
+    __syncthreads();
+    if (tid < 4) {
+        float s = 0.0f;
+        for (int t = 0; t < kMbThreads; t += 16) s += stage[t * 4 + tid];
+        p.loss_partials[(size_t(update) * p.fwd_grid + blockIdx.x) * 4 + tid] = s;
+    }
+}
+
 // ------------------------------------------------------------- launchers
 size_t mb_forward_smem_bytes() { return kMbSmemFloats * sizeof(float); }
 
 cudaError_t configure_ppo_kernels() {
-    cudaError_t e = cudaFuncSetAttribute(k_mb_forward<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(mb_forward_smem_bytes()));
+    cudaError_t e = cudaFuncSetAttribute(k_mb_fused, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(kFuseSmemFloats * sizeof(float)));
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_mb_forward<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(mb_forward_smem_bytes()));
@@ -584,8 +867,8 @@ cudaError_t launch_minibatch(const PpoArgs& p, uint32_t update, uint32_t chunks,
         k_mb_forward<true><<<p.fwd_grid, kMbThreads, mb_forward_smem_bytes(), s>>>(p, update);
         k_mb_grad<true><<<chunks, kGradThreads, 0, s>>>(p, update);
     } else {
-        k_mb_forward<false><<<p.fwd_grid, kMbThreads, mb_forward_smem_bytes(), s>>>(p, update);
-        k_mb_grad<false><<<chunks, kGradThreads, 0, s>>>(p, update);
+        // one kernel per minibatch: p.fwd_grid == chunks CTAs of p.grad_chunk rows
+        k_mb_fused<<<chunks, kMbThreads, kFuseSmemFloats * sizeof(float), s>>>(p, update);
     }
     if (chunks > 1) k_grad_reduce<<<(kPpoParams + 255) / 256, 256, 0, s>>>(p, chunks);
     return cudaGetLastError();

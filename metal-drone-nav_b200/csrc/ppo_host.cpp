@@ -177,6 +177,9 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
         t->grad_chunk = std::max<uint32_t>(64, (per + 31) / 32 * 32);
         t->grad_chunks = (t->minibatch + t->grad_chunk - 1) / t->grad_chunk;
         const uint32_t chunk_bufs = std::max<uint32_t>(t->grad_chunks, 2);
+        // The 64-unit actor's fused minibatch kernel (ppo.cu k_mb_fused) runs one
+        // CTA per gradient chunk and writes one loss partial per CTA.
+        if (!sim->wide) t->fwd_grid = sim->dev->world > 1 ? chunk_bufs : t->grad_chunks;
         const size_t mb = t->minibatch, U = t->updates, P = kPpoParams;
         // One allocation for all trainer-owned device memory.
         PpoArgs& a = t->args;
