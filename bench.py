@@ -241,7 +241,8 @@ def measure_wide(pkg, dev, dist, args, peaks):
         # recompute and dW1, each 2 x 184 x 5120 multiply-adds
         flop = 3 * 2 * 184 * WIDE_HIDDEN * rows * epochs
         upd_s = u_ms / steps * 1e-3
-        tf32_peak = peaks.get("bf16_tflops", 1590.0) / 2.0
+        # aggregate over the ranks against the ranks' combined peak
+        tf32_peak = peaks.get("bf16_tflops", 1590.0) / 2.0 * dist.world
         return {"config": "BASELINE config 3: 16,384 envs, 184->5120->4 tanh actor (967,688 params) on tcgen05 TF32, "
                           "32->64->1 critic, T=128, PPO 4 epochs x 16 minibatches",
                 "env_steps_per_s": rows * steps / (c_ms * 1e-3), "rollout_ms": c_ms / steps,
@@ -249,7 +250,7 @@ def measure_wide(pkg, dev, dist, args, peaks):
                 "ppo_tensor_roofline": {"bound": "tensor", "achieved": flop / upd_s / 1e12, "peak": tf32_peak,
                                         "unit": "TFLOP/s", "frac": flop / upd_s / 1e12 / tf32_peak,
                                         "peak_source": "half the measured bf16 dense rate (tf32 issues at half the "
-                                                       "bf16 rate on tcgen05)"}}
+                                                       "bf16 rate on tcgen05), times the GPU count"}}
     finally:
         tr.close()
         sim.close()
