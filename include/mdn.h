@@ -173,6 +173,17 @@ typedef struct mdn_task_state {
     float witness_points[4][3];
 } mdn_task_state;
 
+/* VGResult (vehicle_geometry.hpp:43-48, 16 bytes): one mechanical contact
+ * audit of the declared vehicle geometry against the room and the obstacles. */
+typedef struct mdn_contact_audit {
+    float physical_clearance_m; /* nonnegative gap; 0 at contact or overlap   */
+    float safety_clearance_m;   /* physical clearance minus the safety margin */
+    uint32_t contact;           /* declared mechanical contact                 */
+    uint32_t ambiguous;         /* unsupported or non-converged case, treated
+                                   conservatively (moving spheres, kind 3,
+                                   are unsupported by the reference audit)     */
+} mdn_contact_audit;
+
 /* Buffer ids for mdn_sim_buffer / download / upload. They name the public
  * members of the reference Sim (main.mm:517-518). */
 enum {
@@ -200,7 +211,9 @@ enum {
     MDN_BUF_CONTACT_ID = 21,  /* int32[T][n] nearest-obstacle id at the step's
                                  closest approach (-1 = room walls)           */
     MDN_BUF_TASK_STATES = 22, /* mdn_task_state[n] (task_states, main.mm:535) */
-    MDN_BUF_COUNT = 23
+    MDN_BUF_CONTACT_AUDIT = 23, /* mdn_contact_audit[T][n], written while the
+                                   mechanical contact audit is enabled     */
+    MDN_BUF_COUNT = 24
 };
 
 /* ---- library / device --------------------------------------------------- */
@@ -265,6 +278,14 @@ int mdn_sim_configure_tasks(mdn_sim* sim, const mdn_task_control* control, float
 /* navigation_training::validate_rollout (navigation_training.hpp:27-35):
  * MDN_ERR_STATE naming the first env whose task generation was rejected. */
 int mdn_sim_validate_tasks(mdn_sim* sim);
+/* Pose-aware mechanical contact audit (vehicle_geometry.hpp:241-376, run as
+ * navigation_contact.metal:3-25 runs it), enabled per simulator: every policy
+ * step then audits each environment's post-integration pose (before an
+ * in-step episode reset) at its episode time against the room and its
+ * obstacles and writes MDN_BUF_CONTACT_AUDIT[tick][env]. It changes no
+ * observation, reward or termination (those keep the 0.18 m sphere contact).
+ * safety_margin_m: 0.04 = VG_DEFAULT_SAFETY_MARGIN_M. enabled = 0 turns it off. */
+int mdn_sim_set_contact_audit(mdn_sim* sim, int enabled, float safety_margin_m);
 /* Device time of the last mdn_sim_collect (CUDA events on the sim stream). */
 int mdn_sim_last_collect_ms(mdn_sim* sim, float* ms);
 

@@ -66,6 +66,7 @@ SIGNATURES = {
     "mdn_launch_counts": (ctypes.c_int, [_P, _P, ctypes.POINTER(_U), ctypes.POINTER(_U)]),
     "mdn_policy_write": (ctypes.c_int, [ctypes.c_char_p, _P, _U, ctypes.c_char_p, ctypes.c_float]),
     "mdn_sim_export_policy": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_float]),
+    "mdn_sim_set_contact_audit": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_float]),
     "mdn_device_fp32_peak": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_double)]),
     "mdn_ppo_create": (ctypes.c_int, [_P, _U, _U, ctypes.POINTER(_P)]),
     "mdn_ppo_destroy": (ctypes.c_int, [_P]),
@@ -259,6 +260,10 @@ class Sim:
     def upload(self, name, array, offset=0):
         a = np.ascontiguousarray(array)
         check(lib().mdn_sim_upload(self.h, layouts.BUF[name], _ptr(a), offset, a.nbytes))
+
+    def set_contact_audit(self, enabled=True, safety_margin_m=0.04):
+        """Per-step mechanical contact audit into buffer 'contact_audit' [T][n]."""
+        check(lib().mdn_sim_set_contact_audit(self.h, 1 if enabled else 0, safety_margin_m))
 
     def export_policy(self, path, source_checkpoint, max_speed_mps=1.5):
         """Deployable actor file (NAVPOL1, or NAVWID4 for a wide actor)."""

@@ -233,6 +233,8 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
     a.actor_log_std = a.actor_b2 + kActions;
     a.wide_partials = wide_partials;
     a.wide_slices = wide ? actor_hidden / 128 : 0;
+    a.audit = audit_enabled ? static_cast<mdn_contact_audit*>(buf[MDN_BUF_CONTACT_AUDIT]) : nullptr;
+    a.audit_margin = audit_margin;
     return a;
 }
 
@@ -348,6 +350,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         b[MDN_BUF_RAPTOR] = sizeof(mdn_raptor_weights);
         b[MDN_BUF_PHYSICS] = sizeof(mdn_physics_params);
         b[MDN_BUF_TASK_STATES] = n * sizeof(mdn_task_state);
+        b[MDN_BUF_CONTACT_AUDIT] = 0;  // allocated when the audit is enabled
         for (int id = 0; id < MDN_BUF_COUNT; id++) {
             const cudaError_t e = cudaMalloc(&sim->buf[id], std::max<size_t>(b[id], 16));
             if (e != cudaSuccess) {
@@ -504,6 +507,27 @@ extern "C" int mdn_sim_collect(mdn_sim* sim, uint32_t steps) {
         cuda_check(cudaEventRecord(sim->ev_start, sim->stream), "event");
         cuda_check(cudaGraphLaunch(exec, sim->stream), "graph launch");
         cuda_check(cudaEventRecord(sim->ev_stop, sim->stream), "event");
+    });
+}
+
+extern "C" int mdn_sim_set_contact_audit(mdn_sim* sim, int enabled, float safety_margin_m) {
+    return guarded([&] {
+        checked(sim);
+        require(std::isfinite(safety_margin_m), MDN_ERR_INVALID, "contact audit: margin must be finite");
+        cuda_check(cudaStreamSynchronize(sim->stream), "contact audit");
+        if (enabled && sim->bytes[MDN_BUF_CONTACT_AUDIT] == 0) {
+            const size_t bytes = size_t(sim->n) * sim->horizon * sizeof(mdn_contact_audit);
+            void* p = nullptr;
+            const cudaError_t e = cudaMalloc(&p, bytes);
+            require(e == cudaSuccess, MDN_ERR_NOMEM, std::string("contact audit buffer: ") + cudaGetErrorString(e));
+            cudaFree(sim->buf[MDN_BUF_CONTACT_AUDIT]);
+            sim->buf[MDN_BUF_CONTACT_AUDIT] = p;
+            sim->bytes[MDN_BUF_CONTACT_AUDIT] = bytes;
+            cuda_check(cudaMemset(p, 0, bytes), "clear contact audit");
+        }
+        sim->audit_enabled = enabled != 0;
+        sim->audit_margin = safety_margin_m;
+        sim->release_graphs();  // kernel arguments are captured by value
     });
 }
 

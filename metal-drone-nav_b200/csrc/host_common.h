@@ -84,6 +84,8 @@ struct mdn_sim {
     float* wide_partials = nullptr;                         // [hidden/128][n][4] slice sums of the wide forward
     uint32_t* wide_error = nullptr;                         // barrier-timeout flag of the wide kernels
     mdn::WideStep* wide = nullptr;                          // tensor maps + launch arguments (wide actors)
+    bool audit_enabled = false;                             // mechanical contact audit (mdn_sim_set_contact_audit)
+    float audit_margin = 0.04f;
     size_t bytes[MDN_BUF_COUNT] = {};
     float room_lo[3], room_hi[3], room_c[3], room_e[3];
     mdn::StepPlan plan;

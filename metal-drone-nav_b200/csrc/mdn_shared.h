@@ -78,6 +78,9 @@ struct SimArgs {
     uint32_t actor_hidden, actor_b2, actor_log_std;
     const float* wide_partials;
     uint32_t wide_slices;
+    // Mechanical contact audit (null = off): results[tick][n], safety margin.
+    mdn_contact_audit* audit;
+    float audit_margin;
 };
 
 }  // namespace mdn

@@ -10,6 +10,7 @@
 
 #include <algorithm>
 
+#include "contact.cuh"
 #include "mdn_device.cuh"
 #include "task.cuh"
 #include "wide.h"
@@ -1143,6 +1144,10 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                 }
             }
             const uint32_t steps = run.steps + 1;
+            if (a.audit && r == 0) {  // mechanical contact audit of the post-integration pose
+                const float pos[3] = {s[0], s[1], s[2]}, orient[4] = {s[3], s[4], s[5], s[6]};
+                a.audit[row] = contact::world_contact(pos, orient, w, elapsed, a.audit_margin);
+            }
             // Bootstrap value of the post-step critic observation (sim.metal:327),
             // hidden units r, r+G, ... on lane r.
             float value;

@@ -75,12 +75,14 @@ BUF = {
     "states": 0, "runs": 1, "worlds": 2, "sensors": 3, "poses": 4, "commands": 5, "actor": 6, "critic": 7,
     "obs": 8, "co": 9, "actions": 10, "logp": 11, "values": 12, "rewards": 13, "next_values": 14,
     "terminated": 15, "truncated": 16, "advantages": 17, "returns": 18, "raptor": 19, "physics": 20,
-    "contact_id": 21, "task_states": 22,
+    "contact_id": 21, "task_states": 22, "contact_audit": 23,
 }
+CONTACT_AUDIT = np.dtype([("physical_clearance_m", "<f4"), ("safety_clearance_m", "<f4"), ("contact", "<u4"),
+                          ("ambiguous", "<u4")])
 BUF_DTYPE = {
     "states": STATE, "runs": RUN, "worlds": WORLD, "raptor": RAPTOR, "physics": PARAMS,
     "terminated": np.dtype(np.uint8), "truncated": np.dtype(np.uint8), "contact_id": np.dtype(np.int32),
-    "task_states": TASK_STATE,
+    "task_states": TASK_STATE, "contact_audit": CONTACT_AUDIT,
 }
 
 # Fixed PPO parameter offsets for the 184/64/4 actor and 32/64/1 critic (ppo.hpp:35-45).

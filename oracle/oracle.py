@@ -169,6 +169,7 @@ def load_ref():
     d("ref_task_apply_start", None, _P, _P)
     d("ref_task_step", None, _P, _P, _P, _P, _P, _U, _U, _P)
     d("ref_task_segment_clearance", _F, _P, _P, _P)
+    d("ref_vg_world_contact", None, _P, _P, _P, _F, _F, _P)
     return lib
 
 

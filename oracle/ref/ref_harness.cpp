@@ -46,6 +46,8 @@ static_assert(sizeof(SimConfig) == 84 && sizeof(SimRun) == 184, "sim layout");
 #undef private
 #include "navigation_runtime.hpp"
 #include "navigation_tasks.hpp"
+#include "vehicle_geometry.hpp"
+static_assert(sizeof(VGResult) == sizeof(mdn_contact_audit), "contact audit layout");
 static_assert(sizeof(NavigationTaskConfig) == sizeof(mdn_task_config), "task config layout");
 static_assert(sizeof(NavigationTaskState) == sizeof(mdn_task_state), "task state layout");
 
@@ -56,6 +58,14 @@ static_assert(sizeof(WWorld) == sizeof(mdn_world), "world layout");
 static_assert(sizeof(RaptorWeights) == sizeof(mdn_raptor_weights), "raptor layout");
 
 extern "C" {
+
+/* vg_world_contact (vehicle_geometry.hpp:311-376): the mechanical contact audit of one pose. */
+void ref_vg_world_contact(const float* position, const float* orientation_wxyz, const mdn_world* world, float time,
+                          float margin, mdn_contact_audit* out) {
+    VGResult r{};
+    vg_world_contact(position, orientation_wxyz, *reinterpret_cast<const WWorld*>(world), time, margin, r);
+    std::memcpy(out, &r, sizeof(r));
+}
 
 /* ---------------- whole-trainer handle ---------------- */
 void* ref_trainer_create(const mdn_sim_config* cfg, uint32_t horizon, const void* raptor, const void* physics) {
