@@ -213,7 +213,14 @@ enum {
     MDN_BUF_TASK_STATES = 22, /* mdn_task_state[n] (task_states, main.mm:535) */
     MDN_BUF_CONTACT_AUDIT = 23, /* mdn_contact_audit[T][n], written while the
                                    mechanical contact audit is enabled     */
-    MDN_BUF_COUNT = 24
+    /* Frozen challenge bank (main.mm:522, 2388); allocated by
+     * mdn_sim_set_challenge_bank, except the active ids, which always exist. */
+    MDN_BUF_BANK_WORLDS = 24,         /* mdn_world[bank_count] frozen levels      */
+    MDN_BUF_BANK_SCHEDULE = 25,       /* uint32[n][schedule_stride] level ids     */
+    MDN_BUF_BANK_ACTIVE_IDS = 26,     /* uint32[n] level each env plays           */
+    MDN_BUF_BANK_TRANSITION_IDS = 27, /* uint32[T][n] level of each transition    */
+    MDN_BUF_RAW_ADVANTAGES = 28,      /* float[T][n] GAE before normalisation     */
+    MDN_BUF_COUNT = 29
 };
 
 /* ---- library / device --------------------------------------------------- */
@@ -286,6 +293,26 @@ int mdn_sim_validate_tasks(mdn_sim* sim);
  * observation, reward or termination (those keep the 0.18 m sphere contact).
  * safety_margin_m: 0.04 = VG_DEFAULT_SAFETY_MARGIN_M. enabled = 0 turns it off. */
 int mdn_sim_set_contact_audit(mdn_sim* sim, int enabled, float safety_margin_m);
+/* ChallengeBankControl (sim.metal:13, challenge_training.hpp:33-38). */
+typedef struct mdn_bank_control {
+    uint32_t enabled, bank_count, schedule_stride, horizon;
+} mdn_bank_control;
+/* Frozen challenge-bank training for a simulator (main.mm:2351-2353,
+ * sim_apply_challenge_world sim.metal:95-122). With control->enabled != 0 the
+ * bank's bank_count worlds are copied to the device and every episode reset
+ * replaces the procedural world by the level that MDN_BUF_BANK_SCHEDULE names
+ * for the env: slot 0 at mdn_sim_reset, slot tick + 1 for a reset inside the
+ * step at `tick`. Level id 0xffffffff selects a rehearsal world (training
+ * family 12 on even, 13 on odd environments, 4 m goals). MDN_BUF_BANK_ACTIVE_IDS
+ * holds each env's level and MDN_BUF_BANK_TRANSITION_IDS[tick][env] the level of
+ * each transition; MDN_BUF_RAW_ADVANTAGES receives the GAE of each rollout update
+ * before normalisation (main.mm:1325-1328). The schedule (uint32[n][stride],
+ * zero-filled) is written with mdn_sim_upload, before mdn_sim_reset for the
+ * first rollout. control == NULL or enabled == 0 switches banks off (active ids
+ * read 0xffffffff after the next reset). schedule_stride must be 1..65536 and
+ * bank_worlds hold valid worlds (count <= 16, kinds 0..3). Under several ranks
+ * each rank passes the schedule rows of its own environments. */
+int mdn_sim_set_challenge_bank(mdn_sim* sim, const mdn_world* bank_worlds, const mdn_bank_control* control);
 /* Device time of the last mdn_sim_collect (CUDA events on the sim stream). */
 int mdn_sim_last_collect_ms(mdn_sim* sim, float* ms);
 
@@ -364,6 +391,88 @@ int mdn_policy_write(const char* path, const float* actor, uint32_t hidden, cons
                      float max_speed_mps);
 /* The same for the simulator's current actor (downloaded from the device). */
 int mdn_sim_export_policy(mdn_sim* sim, const char* path, const char* source_checkpoint, float max_speed_mps);
+
+/* ---- frozen challenge banks (challenge_evaluation.hpp, challenge_training.hpp) */
+/* SHA-256 of a file as 64 lowercase hex digits + NUL (challenge_evaluation::
+ * sha256_file, challenge_evaluation.hpp:71-89). */
+int mdn_sha256_file(const char* path, char out[65]);
+
+/* One split of a challenge-bank JSONL file, every record validated as
+ * challenge_evaluation::parse_level does (challenge_evaluation.hpp:163-280) and
+ * the file as load_split does (:282-313): schema 1, families 14/15/16 with their
+ * names and geometry contracts (identity or mirror_y transform), the simulator
+ * seed derivation, the fixed room, at most 16 AABB/sphere/cylinder obstacles
+ * inside it, safe start and goal for the 0.18 m sphere, the obstructed-route /
+ * witness contract, unique failure ids, and world_source_sha256 equal to
+ * `expected_world_sha256`. Errors are MDN_ERR_INVALID ("challenge bank: ..."
+ * with the JSONL line) or MDN_ERR_IO. */
+typedef struct mdn_bank mdn_bank;
+typedef struct mdn_bank_level {  /* challenge_evaluation::Level, numeric fields */
+    uint32_t family, seed, base_seed, environment_index;
+    float distance, difficulty, direct_route_clearance_m, witness_min_clearance_m;
+    uint32_t witness_sample_count, witness_point_count, mirrored, line_number;
+} mdn_bank_level;
+enum mdn_bank_text {
+    MDN_BANK_FAILURE_ID = 0, MDN_BANK_SPLIT = 1, MDN_BANK_FAMILY_NAME = 2, MDN_BANK_GEOMETRY_CONTRACT = 3,
+    MDN_BANK_DIFFICULTY_BAND = 4, MDN_BANK_SCENE_SHA256 = 5, MDN_BANK_WORLD_SOURCE_SHA256 = 6
+};
+int mdn_bank_load(const char* jsonl_path, const char* split, const char* expected_world_sha256, mdn_bank** out);
+int mdn_bank_free(mdn_bank* bank);
+/* Level count and the SHA-256 of the whole JSONL file (bank_hash). */
+int mdn_bank_info(const mdn_bank* bank, uint32_t* level_count, char bank_sha256[65]);
+/* Level `index` (file order within the split): numeric fields and its world
+ * (family, seed, goal, wind, obstacles as stored; either pointer may be NULL). */
+int mdn_bank_level_get(const mdn_bank* bank, uint32_t index, mdn_bank_level* level, mdn_world* world);
+/* All worlds of the split, in level order (capacity >= level count). */
+int mdn_bank_worlds(const mdn_bank* bank, mdn_world* out, uint32_t capacity);
+/* A text field of a level; valid until mdn_bank_free. NULL on a bad index. */
+const char* mdn_bank_level_text(const mdn_bank* bank, uint32_t index, int field);
+/* The witness route of a level as float[count][3] (capacity in points). */
+int mdn_bank_witness_route(const mdn_bank* bank, uint32_t index, float* xyz, uint32_t capacity, uint32_t* count);
+
+/* challenge_training::Settings (challenge_training.hpp:40-49). */
+typedef struct mdn_challenge_settings {
+    uint32_t environment_count;      /* all environments of the run (every rank) */
+    uint32_t horizon;                /* rollout length; schedules have horizon+1 slots */
+    uint32_t sampler_seed;
+    uint32_t rehearsal_environments; /* the first R envs play rehearsal worlds */
+    uint32_t selection;              /* 0 uniform over the family, 1 failure-weighted */
+    float uniform_floor;             /* [0.5, 1] */
+    float score_staleness_mix;       /* [0, 1] */
+    uint32_t focus_family;           /* 0 balanced 14/15/16, or one family for all */
+} mdn_challenge_settings;
+void mdn_challenge_settings_default(mdn_challenge_settings* out);
+/* The train-split level sampler with per-level failure scores
+ * (challenge_training::ChallengeTraining, challenge_training.hpp:53-427). All
+ * arrays are env-major over settings.environment_count environments; a
+ * schedule is uint32[env][horizon+1]; rollout evidence is [tick][env]. */
+typedef struct mdn_challenge mdn_challenge;
+int mdn_challenge_create(const char* bank_jsonl, const char* expected_world_sha256,
+                         const mdn_challenge_settings* settings, mdn_challenge** out);
+int mdn_challenge_destroy(mdn_challenge* sampler);
+/* The loaded train split (owned by the sampler). */
+int mdn_challenge_bank(mdn_challenge* sampler, const mdn_bank** out);
+int mdn_challenge_control(const mdn_challenge* sampler, mdn_bank_control* out);
+/* initial_schedule (:106-124): a fresh run's schedule; sets the active ids. */
+int mdn_challenge_initial_schedule(mdn_challenge* sampler, uint32_t* schedule);
+/* next_schedule (:128-154): slot 0 keeps each env's active level, slots
+ * 1..horizon are sampled for resets within the next rollout. */
+int mdn_challenge_next_schedule(mdn_challenge* sampler, const uint32_t* active_ids, uint64_t rollout_index,
+                                uint32_t* schedule);
+int mdn_challenge_active_ids(const mdn_challenge* sampler, uint32_t* out);
+/* observe_raw_gae (:160-199): accumulate per-episode mean |GAE| into level
+ * scores from one rollout's raw GAE, terminal flags and transition level ids. */
+int mdn_challenge_observe_raw_gae(mdn_challenge* sampler, const float* raw_gae, const uint8_t* terminated,
+                                  const uint8_t* truncated, const uint32_t* transition_ids, uint64_t rollout_index);
+int mdn_challenge_level_stats(const mdn_challenge* sampler, uint32_t level, float* score,
+                              uint64_t* completed_episodes, uint64_t* last_visit_rollout);
+/* The CHTRN1 version-3 sidecar (save_state/load_state, :204-277), byte for
+ * byte the reference's format; checkpoint_sha256 = 64 hex digits. load_state
+ * writes the restored active ids (environment_count values) to active_ids. */
+int mdn_challenge_save_state(mdn_challenge* sampler, const char* path, const char* checkpoint_sha256,
+                             uint64_t completed_rollouts, const uint32_t* active_ids);
+int mdn_challenge_load_state(mdn_challenge* sampler, const char* path, const char* checkpoint_sha256,
+                             uint64_t completed_rollouts, uint32_t* active_ids);
 
 /* ---- multi-GPU (no reference counterpart: the reference is one Apple GPU) */
 /* Fill a 128-byte NCCL unique id (rank 0) to share through any host channel. */

@@ -10,8 +10,8 @@ import pathlib
 import subprocess
 
 from . import layouts  # noqa: F401
-from .capi import (Device, MdnError, PPOTrainer, Sim, default_raptor, lib, task_control, task_settings,  # noqa: F401
-                   write_policy)
+from .capi import (ChallengeBank, ChallengeSampler, Device, MdnError, PPOTrainer, Sim, challenge_settings,  # noqa: F401
+                   default_raptor, lib, sha256_file, task_control, task_settings, write_policy)
 
 PACKAGE_DIR = pathlib.Path(__file__).resolve().parent
 

@@ -83,6 +83,28 @@ SIGNATURES = {
     "mdn_ppo_checkpoint_load": (ctypes.c_int, [_P, ctypes.c_char_p, _U, _U, _U, _U]),
     "mdn_gae_normalize_static": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _U, _U, ctypes.c_float,
                                                  ctypes.c_float, _P]),
+    "mdn_sim_set_challenge_bank": (ctypes.c_int, [_P, _P, _P]),
+    "mdn_sha256_file": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p]),
+    "mdn_bank_load": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "mdn_bank_free": (ctypes.c_int, [_P]),
+    "mdn_bank_info": (ctypes.c_int, [_P, ctypes.POINTER(_U), ctypes.c_char_p]),
+    "mdn_bank_level_get": (ctypes.c_int, [_P, _U, _P, _P]),
+    "mdn_bank_worlds": (ctypes.c_int, [_P, _P, _U]),
+    "mdn_bank_level_text": (ctypes.c_char_p, [_P, _U, ctypes.c_int]),
+    "mdn_bank_witness_route": (ctypes.c_int, [_P, _U, _P, _U, ctypes.POINTER(_U)]),
+    "mdn_challenge_settings_default": (None, [_P]),
+    "mdn_challenge_create": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, _P, ctypes.POINTER(_P)]),
+    "mdn_challenge_destroy": (ctypes.c_int, [_P]),
+    "mdn_challenge_bank": (ctypes.c_int, [_P, ctypes.POINTER(_P)]),
+    "mdn_challenge_control": (ctypes.c_int, [_P, _P]),
+    "mdn_challenge_initial_schedule": (ctypes.c_int, [_P, _P]),
+    "mdn_challenge_next_schedule": (ctypes.c_int, [_P, _P, ctypes.c_uint64, _P]),
+    "mdn_challenge_active_ids": (ctypes.c_int, [_P, _P]),
+    "mdn_challenge_observe_raw_gae": (ctypes.c_int, [_P, _P, _P, _P, _P, ctypes.c_uint64]),
+    "mdn_challenge_level_stats": (ctypes.c_int, [_P, _U, ctypes.POINTER(ctypes.c_float),
+                                                  ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
+    "mdn_challenge_save_state": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_uint64, _P]),
+    "mdn_challenge_load_state": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_uint64, _P]),
     "mdn_comm_unique_id": (ctypes.c_int, [_P]),
     "mdn_comm_init": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, _P]),
     "mdn_comm_destroy": (ctypes.c_int, [_P]),
@@ -269,6 +291,26 @@ class Sim:
         """Deployable actor file (NAVPOL1, or NAVWID4 for a wide actor)."""
         check(lib().mdn_sim_export_policy(self.h, str(path).encode(), str(source_checkpoint).encode(), max_speed_mps))
 
+    def set_challenge_bank(self, worlds, control=None, horizon=None):
+        """Frozen challenge-bank training (mdn_sim_set_challenge_bank).
+
+        worlds: WORLD array of the bank levels; control: a BANK_CONTROL value
+        (default: enabled, len(worlds) levels, horizon+1 schedule slots for
+        this simulator's horizon). worlds=None switches banks off."""
+        if worlds is None:
+            check(lib().mdn_sim_set_challenge_bank(self.h, None, None))
+            return
+        w = np.ascontiguousarray(worlds, layouts.WORLD)
+        if control is None:
+            h = self.horizon if horizon is None else int(horizon)
+            control = (1, len(w), h + 1, h)
+        c = np.array(tuple(control) if not isinstance(control, np.ndarray) else control, layouts.BANK_CONTROL)
+        check(lib().mdn_sim_set_challenge_bank(self.h, _ptr(w) if len(w) else None, _ptr(c)))
+
+    def set_bank_schedule(self, schedule):
+        """Upload this simulator's schedule rows: uint32 [n][schedule_stride]."""
+        self.upload("bank_schedule", np.ascontiguousarray(schedule, np.uint32))
+
     def configure_tasks(self, control, domain_amplitude=0.0):
         """navigation_training::configure: enable goal-arrival tasks and reset."""
         ctl = np.array(control, layouts.TASK_CONTROL)
@@ -362,3 +404,141 @@ def write_policy(path, actor, hidden, source_checkpoint, max_speed_mps=1.5):
     a = np.ascontiguousarray(actor, np.float32)
     check(lib().mdn_policy_write(str(path).encode(), _ptr(a), int(hidden), str(source_checkpoint).encode(),
                                  max_speed_mps))
+
+
+def sha256_file(path):
+    """SHA-256 hex digest of a file (mdn_sha256_file)."""
+    out = ctypes.create_string_buffer(65)
+    check(lib().mdn_sha256_file(str(path).encode(), out))
+    return out.value.decode()
+
+
+class ChallengeBank:
+    """One split of a frozen challenge-bank JSONL file (challenge_evaluation::
+    load_split, challenge_evaluation.hpp:282-313), validated record by record."""
+
+    def __init__(self, path=None, split="train", world_sha256=None, _handle=None, _owner=None):
+        self._owner = _owner
+        if _handle is not None:
+            self.h, self._owns = _handle, False
+        else:
+            h = _P()
+            check(lib().mdn_bank_load(str(path).encode(), split.encode(),
+                                      None if world_sha256 is None else world_sha256.encode(), ctypes.byref(h)))
+            self.h, self._owns = h, True
+        count = _U()
+        digest = ctypes.create_string_buffer(65)
+        check(lib().mdn_bank_info(self.h, ctypes.byref(count), digest))
+        self.count, self.bank_sha256 = count.value, digest.value.decode()
+
+    def __len__(self):
+        return self.count
+
+    def close(self):
+        if self.h and self._owns:
+            lib().mdn_bank_free(self.h)
+        self.h = None
+
+    def worlds(self):
+        out = np.zeros(self.count, layouts.WORLD)
+        check(lib().mdn_bank_worlds(self.h, _ptr(out), self.count))
+        return out
+
+    def level(self, index):
+        """Numeric fields, text fields and the witness route of one level."""
+        info = np.zeros((), layouts.BANK_LEVEL)
+        check(lib().mdn_bank_level_get(self.h, index, _ptr(info), None))
+        rec = {k: info[k].item() for k in layouts.BANK_LEVEL.names}
+        for i, name in enumerate(layouts.BANK_TEXT):
+            rec[name] = lib().mdn_bank_level_text(self.h, index, i).decode()
+        count = _U()
+        check(lib().mdn_bank_witness_route(self.h, index, None, 0, ctypes.byref(count)))
+        route = np.zeros((count.value, 3), np.float32)
+        check(lib().mdn_bank_witness_route(self.h, index, _ptr(route), count.value, ctypes.byref(count)))
+        rec["witness_route"] = route
+        return rec
+
+
+def challenge_settings(**overrides):
+    """challenge_training::Settings defaults (challenge_training.hpp:40-49) with overrides."""
+    s = np.zeros((), layouts.CHALLENGE_SETTINGS)
+    lib().mdn_challenge_settings_default(_ptr(s))
+    for k, v in overrides.items():
+        s[k] = v
+    return s
+
+
+class ChallengeSampler:
+    """challenge_training::ChallengeTraining (challenge_training.hpp:53-427): the
+    train-split level sampler with failure scores and its CHTRN1 sidecar."""
+
+    def __init__(self, bank_path, world_sha256, settings=None, **overrides):
+        s = challenge_settings() if settings is None else np.array(settings, layouts.CHALLENGE_SETTINGS)
+        for k, v in overrides.items():
+            s[k] = v
+        self.settings = s
+        h = _P()
+        check(lib().mdn_challenge_create(str(bank_path).encode(), world_sha256.encode(), _ptr(s), ctypes.byref(h)))
+        self.h = h
+        self.envs, self.horizon = int(s["environment_count"]), int(s["horizon"])
+        bank = _P()
+        check(lib().mdn_challenge_bank(self.h, ctypes.byref(bank)))
+        self.bank = ChallengeBank(_handle=bank, _owner=self)
+
+    def close(self):
+        if self.h:
+            lib().mdn_challenge_destroy(self.h)
+        self.h = None
+
+    def control(self):
+        c = np.zeros((), layouts.BANK_CONTROL)
+        check(lib().mdn_challenge_control(self.h, _ptr(c)))
+        return c
+
+    def _schedule(self):
+        return np.zeros((self.envs, self.horizon + 1), np.uint32)
+
+    def initial_schedule(self):
+        out = self._schedule()
+        check(lib().mdn_challenge_initial_schedule(self.h, _ptr(out)))
+        return out
+
+    def next_schedule(self, active_ids, rollout_index):
+        a = np.ascontiguousarray(active_ids, np.uint32)
+        if a.size != self.envs:
+            raise MdnError(ERR["INVALID"], "challenge active-level id count differs from environment count")
+        out = self._schedule()
+        check(lib().mdn_challenge_next_schedule(self.h, _ptr(a), rollout_index, _ptr(out)))
+        return out
+
+    def active_ids(self):
+        out = np.zeros(self.envs, np.uint32)
+        check(lib().mdn_challenge_active_ids(self.h, _ptr(out)))
+        return out
+
+    def observe_raw_gae(self, raw_gae, terminated, truncated, transition_ids, rollout_index):
+        rows = self.envs * self.horizon
+        arrays = [np.ascontiguousarray(raw_gae, np.float32), np.ascontiguousarray(terminated, np.uint8),
+                  np.ascontiguousarray(truncated, np.uint8), np.ascontiguousarray(transition_ids, np.uint32)]
+        if any(a.size != rows for a in arrays):
+            raise MdnError(ERR["INVALID"], f"rollout evidence must hold horizon x environments = {rows} rows")
+        check(lib().mdn_challenge_observe_raw_gae(self.h, *[_ptr(a) for a in arrays], rollout_index))
+
+    def level_stats(self, level):
+        score, done, visit = ctypes.c_float(), ctypes.c_uint64(), ctypes.c_uint64()
+        check(lib().mdn_challenge_level_stats(self.h, level, ctypes.byref(score), ctypes.byref(done),
+                                              ctypes.byref(visit)))
+        return score.value, done.value, visit.value
+
+    def save_state(self, path, checkpoint_sha256, completed_rollouts, active_ids):
+        a = np.ascontiguousarray(active_ids, np.uint32)
+        if a.size != self.envs:
+            raise MdnError(ERR["INVALID"], "challenge active-level id count differs from environment count")
+        check(lib().mdn_challenge_save_state(self.h, str(path).encode(), checkpoint_sha256.encode(),
+                                             completed_rollouts, _ptr(a)))
+
+    def load_state(self, path, checkpoint_sha256, completed_rollouts):
+        out = np.zeros(self.envs, np.uint32)
+        check(lib().mdn_challenge_load_state(self.h, str(path).encode(), checkpoint_sha256.encode(),
+                                             completed_rollouts, _ptr(out)))
+        return out

@@ -235,6 +235,14 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
     a.wide_slices = wide ? actor_hidden / 128 : 0;
     a.audit = audit_enabled ? static_cast<mdn_contact_audit*>(buf[MDN_BUF_CONTACT_AUDIT]) : nullptr;
     a.audit_margin = audit_margin;
+    a.bank_enabled = bank.enabled;
+    a.bank_count = bank.enabled ? bank.bank_count : 0;
+    a.bank_stride = bank.schedule_stride;
+    a.bank_worlds = static_cast<const mdn_world*>(buf[MDN_BUF_BANK_WORLDS]);
+    a.bank_schedule = static_cast<const uint32_t*>(buf[MDN_BUF_BANK_SCHEDULE]);
+    a.bank_active = static_cast<uint32_t*>(buf[MDN_BUF_BANK_ACTIVE_IDS]);
+    a.bank_transition = bytes[MDN_BUF_BANK_TRANSITION_IDS] ? static_cast<uint32_t*>(buf[MDN_BUF_BANK_TRANSITION_IDS])
+                                                           : nullptr;
     return a;
 }
 
@@ -351,6 +359,11 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         b[MDN_BUF_PHYSICS] = sizeof(mdn_physics_params);
         b[MDN_BUF_TASK_STATES] = n * sizeof(mdn_task_state);
         b[MDN_BUF_CONTACT_AUDIT] = 0;  // allocated when the audit is enabled
+        b[MDN_BUF_BANK_ACTIVE_IDS] = n * sizeof(uint32_t);
+        // Bank worlds, schedule, transition ids and raw advantages are
+        // allocated by mdn_sim_set_challenge_bank.
+        for (int id : {MDN_BUF_BANK_WORLDS, MDN_BUF_BANK_SCHEDULE, MDN_BUF_BANK_TRANSITION_IDS, MDN_BUF_RAW_ADVANTAGES})
+            b[id] = 0;
         for (int id = 0; id < MDN_BUF_COUNT; id++) {
             const cudaError_t e = cudaMalloc(&sim->buf[id], std::max<size_t>(b[id], 16));
             if (e != cudaSuccess) {
@@ -414,6 +427,8 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
                        MDN_BUF_NEXT_VALUES, MDN_BUF_TERMINATED, MDN_BUF_TRUNCATED, MDN_BUF_ADVANTAGES, MDN_BUF_RETURNS,
                        MDN_BUF_CONTACT_ID, MDN_BUF_TASK_STATES})
             cuda_check(cudaMemsetAsync(sim->buf[id], 0, b[id], sim->stream), "clear rollout buffers");
+        cuda_check(cudaMemsetAsync(sim->buf[MDN_BUF_BANK_ACTIVE_IDS], 0xff, b[MDN_BUF_BANK_ACTIVE_IDS], sim->stream),
+                   "clear bank ids");
         // Launch shapes; MDN_ADVANCE_GROUP (1 or 2) overrides the advance
         // kernel's lanes per environment, for tuning.
         const char* group_env = std::getenv("MDN_ADVANCE_GROUP");
@@ -527,6 +542,60 @@ extern "C" int mdn_sim_set_contact_audit(mdn_sim* sim, int enabled, float safety
         }
         sim->audit_enabled = enabled != 0;
         sim->audit_margin = safety_margin_m;
+        sim->release_graphs();  // kernel arguments are captured by value
+    });
+}
+
+namespace {
+// (Re)allocate a simulator buffer of `bytes` filled with byte `fill`.
+void sim_realloc(mdn_sim* sim, int id, size_t bytes, int fill) {
+    void* p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, std::max<size_t>(bytes, 16));
+    require(e == cudaSuccess, MDN_ERR_NOMEM, std::string("challenge bank buffer: ") + cudaGetErrorString(e));
+    const cudaError_t m = cudaMemset(p, fill, std::max<size_t>(bytes, 16));
+    if (m != cudaSuccess) {
+        cudaFree(p);
+        cuda_check(m, "clear challenge bank buffer");
+    }
+    cudaFree(sim->buf[id]);
+    sim->buf[id] = p;
+    sim->bytes[id] = bytes;
+}
+}  // namespace
+
+extern "C" int mdn_sim_set_challenge_bank(mdn_sim* sim, const mdn_world* bank_worlds, const mdn_bank_control* control) {
+    return guarded([&] {
+        checked(sim);
+        cuda_check(cudaStreamSynchronize(sim->stream), "challenge bank");
+        if (!control || control->enabled == 0) {
+            sim->bank = mdn_bank_control{};
+            sim->release_graphs();
+            return;
+        }
+        const mdn_bank_control c = *control;
+        require(c.schedule_stride >= 1 && c.schedule_stride <= 65536, MDN_ERR_INVALID,
+                "challenge bank: schedule_stride must be 1..65536");
+        require(c.bank_count <= (1u << 20), MDN_ERR_INVALID, "challenge bank: at most 2^20 levels");
+        require(c.bank_count == 0 || bank_worlds != nullptr, MDN_ERR_INVALID, "challenge bank: null worlds");
+        for (uint32_t k = 0; k < c.bank_count; k++) {
+            const mdn_world& w = bank_worlds[k];
+            require(w.count <= 16, MDN_ERR_INVALID, "challenge bank: a world holds more than 16 obstacles");
+            for (uint32_t o = 0; o < w.count; o++)
+                require(w.obstacles[o].kind <= 3, MDN_ERR_INVALID, "challenge bank: unknown obstacle kind");
+        }
+        const size_t n = sim->n;
+        sim_realloc(sim, MDN_BUF_BANK_WORLDS, size_t(c.bank_count) * sizeof(mdn_world), 0);
+        if (c.bank_count)
+            cuda_check(cudaMemcpy(sim->buf[MDN_BUF_BANK_WORLDS], bank_worlds, size_t(c.bank_count) * sizeof(mdn_world),
+                                  cudaMemcpyHostToDevice),
+                       "upload challenge bank");
+        if (sim->bytes[MDN_BUF_BANK_SCHEDULE] != n * c.schedule_stride * sizeof(uint32_t))
+            sim_realloc(sim, MDN_BUF_BANK_SCHEDULE, n * c.schedule_stride * sizeof(uint32_t), 0);
+        const size_t rows = n * sim->horizon;
+        if (sim->bytes[MDN_BUF_BANK_TRANSITION_IDS] == 0)
+            sim_realloc(sim, MDN_BUF_BANK_TRANSITION_IDS, rows * sizeof(uint32_t), 0xff);
+        if (sim->bytes[MDN_BUF_RAW_ADVANTAGES] == 0) sim_realloc(sim, MDN_BUF_RAW_ADVANTAGES, rows * sizeof(float), 0);
+        sim->bank = c;
         sim->release_graphs();  // kernel arguments are captured by value
     });
 }

@@ -81,6 +81,15 @@ struct SimArgs {
     // Mechanical contact audit (null = off): results[tick][n], safety margin.
     mdn_contact_audit* audit;
     float audit_margin;
+    // Frozen challenge bank (ChallengeBankControl, sim.metal:13): level worlds,
+    // the env-major schedule [n][bank_stride] of level ids, the level each env
+    // plays (0xffffffff: none / rehearsal) and, per row, the level that the
+    // transition belongs to (null until a bank is configured).
+    uint32_t bank_enabled, bank_count, bank_stride;
+    const mdn_world* bank_worlds;
+    const uint32_t* bank_schedule;
+    uint32_t* bank_active;
+    uint32_t* bank_transition;
 };
 
 }  // namespace mdn

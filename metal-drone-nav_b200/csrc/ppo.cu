@@ -56,6 +56,7 @@ __global__ void __launch_bounds__(kGaeThreads) k_gae_sum(PpoArgs p) {
             const float delta = p.rewards[k] + p.gamma * bootstrap - value;
             carry = delta + (boundary ? 0.0f : p.gamma * p.lambda * carry);
             p.advantages[k] = carry;
+            if (p.raw_advantages) p.raw_advantages[k] = carry;
             p.returns[k] = carry + value;
             local += double(carry);
         }

@@ -19,6 +19,7 @@ struct PpoArgs {
     const uint8_t* truncated;
     float* advantages;
     float* returns;
+    float* raw_advantages;        // [rows] GAE before normalisation, or null (challenge banks)
     double* stat_partials;        // [gae blocks]
     double* stats;                // [2] sum, sum of squares (allreduced under NCCL)
     float* stat_values;           // [2] mean, inverse std

@@ -63,6 +63,12 @@ struct mdn_ppo {
 namespace {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// The raw-GAE copy that challenge-bank training scores levels with
+// (main.mm:1325-1328); null while the simulator has no bank.
+float* raw_advantages_of(const mdn_sim* sim) {
+    return sim->bytes[MDN_BUF_RAW_ADVANTAGES] ? static_cast<float*>(sim->buf[MDN_BUF_RAW_ADVANTAGES]) : nullptr;
+}
+
 mdn_ppo* checked(mdn_ppo* p) {
     require(p != nullptr && p->sim != nullptr, MDN_ERR_INVALID, "null mdn_ppo");
     cuda_check(cudaSetDevice(p->sim->dev->gpu), "cudaSetDevice");
@@ -214,6 +220,7 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
         a.truncated = static_cast<uint8_t*>(sim->buf[MDN_BUF_TRUNCATED]);
         a.advantages = static_cast<float*>(sim->buf[MDN_BUF_ADVANTAGES]);
         a.returns = static_cast<float*>(sim->buf[MDN_BUF_RETURNS]);
+        a.raw_advantages = raw_advantages_of(sim);
         a.obs = static_cast<float*>(sim->buf[MDN_BUF_OBS]);
         a.co = static_cast<float*>(sim->buf[MDN_BUF_CO]);
         a.actions = static_cast<float*>(sim->buf[MDN_BUF_ACTIONS]);
@@ -371,9 +378,11 @@ extern "C" int mdn_ppo_rollout_update(mdn_ppo* t, uint32_t rollout_index) {
         mdn_sim* sim = t->sim;
         // PPOTrainer reads the learning rate and entropy coefficient from the
         // simulator config (main.mm:1193,1368); they are graph arguments here.
-        if (sim->cfg.learning_rate != t->args.learning_rate || sim->cfg.entropy_coef != t->args.entropy_coef) {
+        if (sim->cfg.learning_rate != t->args.learning_rate || sim->cfg.entropy_coef != t->args.entropy_coef ||
+            raw_advantages_of(sim) != t->args.raw_advantages) {
             t->args.learning_rate = sim->cfg.learning_rate;
             t->args.entropy_coef = sim->cfg.entropy_coef;
+            t->args.raw_advantages = raw_advantages_of(sim);
             if (t->graph) {
                 cudaGraphExecDestroy(t->graph);
                 t->graph = nullptr;

@@ -29,7 +29,7 @@ __device__ float g_pool_ray[80 * 3];        // nav_ray(row, col, 0.75), guidance
 __global__ void k_reset(SimArgs a, int first) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     const bool active = i < a.n;
-    if (active) episode_reset(a, i, first != 0);
+    if (active) episode_reset(a, i, first != 0, 0);
     const unsigned mask = __ballot_sync(0xffffffffu, active);
     refill_rings(a, (blockIdx.x * blockDim.x) + (threadIdx.x & ~31u), mask);
 }
@@ -1242,6 +1242,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                     a.truncated[row] = timeout && !term;
                 }
                 a.next_values[row] = value;
+                if (a.bank_transition) a.bank_transition[row] = a.bank_enabled ? a.bank_active[i] : 0xffffffffu;
                 if (success || collision || timeout) {
                     run.successes += success;
                     run.collisions += collision;
@@ -1251,7 +1252,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                     run.total_path += path;
                     run.total_elapsed += elapsed;
                     run.final_progress += 1.0f - after / smax(run.initial_distance, 1.0e-4f);
-                    if (!c.eval) refill = episode_reset(a, i, false);
+                    if (!c.eval) refill = episode_reset(a, i, false, a.tick + 1);
                 }
             }
         }

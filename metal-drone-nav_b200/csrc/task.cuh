@@ -278,11 +278,14 @@ __device__ TaskStep task_step(mdn_task_state& task, const mdn_task_config& c, co
     return r;
 }
 
-// Episode reset with the task contract: sim_reset_one, then
+// Episode reset with the task contract: sim_reset_one, the challenge-bank
+// world of schedule slot `slot` (sim.metal:143,330), then
 // sim_reset_navigation_task (sim.metal:125-141), then the SoA world mirror.
 // Returns true (the caller refills the env's range ring).
-__device__ __noinline__ bool episode_reset(const SimArgs& a, uint32_t i, bool first) {
+__device__ __noinline__ bool episode_reset(const SimArgs& a, uint32_t i, bool first, uint32_t slot) {
     reset_env(a, i, first);
+    if (a.bank_enabled) apply_challenge_world(a, i, slot);
+    else a.bank_active[i] = 0xffffffffu;
     mdn_task_state& task = a.tasks[i];
     task = mdn_task_state{};
     if (a.task_ctl.enabled) {

@@ -417,6 +417,40 @@ __device__ bool reset_env(const SimArgs& a, uint32_t i, bool first) {
     return true;
 }
 
+// sim_apply_challenge_world (sim.metal:95-122): after the procedural reset,
+// replace env i's world by the frozen bank level that its schedule names for
+// `slot` (0 at sim_reset, tick + 1 for a reset inside step `tick`), or, for the
+// level id 0xffffffff, by a rehearsal world of the short-task mixture (training
+// family 12 on even, 13 on odd environments, 4 m goals). A slot beyond the
+// schedule or an unknown level id keeps the procedural world and leaves the
+// env's active id unchanged, as the reference does.
+__device__ __forceinline__ void apply_challenge_world(const SimArgs& a, uint32_t i, uint32_t slot) {
+    if (a.bank_count == 0 || slot >= a.bank_stride) return;
+    const uint32_t gid = a.env_base + i;
+    const uint32_t level = a.bank_schedule[size_t(i) * a.bank_stride + slot];
+    mdn_sim_run& run = a.runs[i];
+    mdn_world& w = a.worlds[i];
+    if (level == 0xffffffffu) {
+        uint32_t rng = run.rng;
+        const uint32_t family = training_family(gid % 2 == 0 ? 12u : 13u, rng);
+        generate_world(w, wrng(rng), family, 4.0f);
+        run.rng = rng;
+    } else {
+        if (level >= a.bank_count) return;
+        w = a.bank_worlds[level];
+    }
+    w.wind[0] = clean_env(a.cfg, gid) ? 0.0f : a.cfg.wind;
+    w.wind[1] = 0;
+    w.wind[2] = 0;
+    run.initial_distance = len3(w.goal[0], w.goal[1], w.goal[2] - 1.5f);
+    if (w.family == 10 || w.family == 11) {
+        a.states[i].linear_velocity[0] = a.cfg.speed;
+        run.desired_velocity[0] = a.cfg.speed;
+        run.previous_nav[0] = 1.0f;
+    }
+    a.bank_active[i] = level;
+}
+
 // Refill when each environment is served by a group of `g` lanes and `mask`
 // holds the groups' leader lanes: lane l stands for environment first_env + l / g.
 __device__ __forceinline__ void refill_rings_grouped(const SimArgs& a, uint32_t first_env, unsigned mask, int g) {

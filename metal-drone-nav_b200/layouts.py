@@ -75,15 +75,32 @@ BUF = {
     "states": 0, "runs": 1, "worlds": 2, "sensors": 3, "poses": 4, "commands": 5, "actor": 6, "critic": 7,
     "obs": 8, "co": 9, "actions": 10, "logp": 11, "values": 12, "rewards": 13, "next_values": 14,
     "terminated": 15, "truncated": 16, "advantages": 17, "returns": 18, "raptor": 19, "physics": 20,
-    "contact_id": 21, "task_states": 22, "contact_audit": 23,
+    "contact_id": 21, "task_states": 22, "contact_audit": 23, "bank_worlds": 24, "bank_schedule": 25,
+    "bank_active_ids": 26, "bank_transition_ids": 27, "raw_advantages": 28,
 }
 CONTACT_AUDIT = np.dtype([("physical_clearance_m", "<f4"), ("safety_clearance_m", "<f4"), ("contact", "<u4"),
                           ("ambiguous", "<u4")])
 BUF_DTYPE = {
     "states": STATE, "runs": RUN, "worlds": WORLD, "raptor": RAPTOR, "physics": PARAMS,
     "terminated": np.dtype(np.uint8), "truncated": np.dtype(np.uint8), "contact_id": np.dtype(np.int32),
-    "task_states": TASK_STATE, "contact_audit": CONTACT_AUDIT,
+    "task_states": TASK_STATE, "contact_audit": CONTACT_AUDIT, "bank_worlds": WORLD,
+    "bank_schedule": np.dtype(np.uint32), "bank_active_ids": np.dtype(np.uint32),
+    "bank_transition_ids": np.dtype(np.uint32),
 }
+# ChallengeBankControl (sim.metal:13) and challenge_training::Settings
+# (challenge_training.hpp:40-49); mdn_bank_level = the numeric fields of
+# challenge_evaluation::Level (challenge_evaluation.hpp:36-45).
+BANK_CONTROL = np.dtype([("enabled", "<u4"), ("bank_count", "<u4"), ("schedule_stride", "<u4"), ("horizon", "<u4")])
+CHALLENGE_SETTINGS = np.dtype([
+    ("environment_count", "<u4"), ("horizon", "<u4"), ("sampler_seed", "<u4"), ("rehearsal_environments", "<u4"),
+    ("selection", "<u4"), ("uniform_floor", "<f4"), ("score_staleness_mix", "<f4"), ("focus_family", "<u4")])
+BANK_LEVEL = np.dtype([
+    ("family", "<u4"), ("seed", "<u4"), ("base_seed", "<u4"), ("environment_index", "<u4"), ("distance", "<f4"),
+    ("difficulty", "<f4"), ("direct_route_clearance_m", "<f4"), ("witness_min_clearance_m", "<f4"),
+    ("witness_sample_count", "<u4"), ("witness_point_count", "<u4"), ("mirrored", "<u4"), ("line_number", "<u4")])
+BANK_TEXT = ("failure_id", "split", "family_name", "geometry_contract", "difficulty_band", "scene_sha256",
+             "world_source_sha256")
+INVALID_LEVEL = 0xFFFFFFFF
 
 # Fixed PPO parameter offsets for the 184/64/4 actor and 32/64/1 critic (ppo.hpp:35-45).
 ACTOR_OBS, CRITIC_OBS, HIDDEN, ACTIONS = 184, 32, 64, 4

@@ -1384,6 +1384,10 @@ struct o_sim {
     float* pixel_rays; /* [320][3] */
     mdn_task_control task_ctl; /* goal-arrival tasks (navigation_training::configure) */
     mdn_task_state* tasks;
+    /* frozen challenge bank (ChallengeBankControl, sim.metal:13) */
+    mdn_bank_control bank;
+    mdn_world* bank_worlds;
+    uint32_t *bank_schedule, *bank_active, *bank_transition;
 };
 
 uint32_t o_actor_param_count(void) { return A_P; }
@@ -1430,6 +1434,10 @@ o_sim* o_sim_create_shard(const mdn_sim_config* cfg, uint32_t horizon, const mdn
     s->contact = zalloc(rows * 4);
     s->pixel_rays = zalloc(NPIX * 3 * 4);
     s->tasks = zalloc(n * sizeof(mdn_task_state));
+    s->bank_active = zalloc(n * 4);
+    s->bank_transition = zalloc(rows * 4);
+    for (size_t k = 0; k < n; k++) s->bank_active[k] = 0xffffffffu;
+    for (size_t k = 0; k < rows; k++) s->bank_transition[k] = 0xffffffffu;
     for (uint32_t k = 0; k < NPIX; k++) o_pixel_ray(1.0f, 0.75f, k, s->pixel_rays + 3 * k);
     /* Policy initialisation, cpu_reference.hpp:89-103 (== main.mm:548-555). */
     uint32_t seed = 1789;
@@ -1453,12 +1461,27 @@ void o_sim_destroy(o_sim* s) {
     void* bufs[] = {s->states, s->runs, s->worlds, s->sensors, s->poses, s->commands, s->actor, s->critic,
                     s->actor_m, s->actor_v, s->critic_m, s->critic_v, s->obs, s->co, s->actions, s->logp,
                     s->values, s->rewards, s->next_values, s->adv, s->ret, s->term, s->trunc, s->contact,
-                    s->pixel_rays, s->tasks};
+                    s->pixel_rays, s->tasks, s->bank_worlds, s->bank_schedule, s->bank_active,
+                    s->bank_transition};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++) free(bufs[i]);
     free(s);
 }
 void o_sim_set_config(o_sim* s, const mdn_sim_config* cfg) { s->cfg = *cfg; }
 void o_sim_set_task_control(o_sim* s, const mdn_task_control* ctl) { s->task_ctl = *ctl; }
+/* Bank worlds and a zeroed env-major schedule [n][stride] (main.mm:543-547,
+ * 2351-2353); enabled == 0 switches banks off. */
+void o_sim_set_challenge_bank(o_sim* s, const mdn_world* worlds, const mdn_bank_control* ctl) {
+    free(s->bank_worlds);
+    free(s->bank_schedule);
+    s->bank_worlds = NULL;
+    s->bank_schedule = NULL;
+    memset(&s->bank, 0, sizeof(s->bank));
+    if (!ctl || !ctl->enabled) return;
+    s->bank = *ctl;
+    s->bank_worlds = zalloc((size_t)ctl->bank_count * sizeof(mdn_world));
+    if (ctl->bank_count) memcpy(s->bank_worlds, worlds, (size_t)ctl->bank_count * sizeof(mdn_world));
+    s->bank_schedule = zalloc((size_t)s->cfg.n * ctl->schedule_stride * 4);
+}
 void* o_sim_buffer(o_sim* s, int id, size_t* bytes) {
     const size_t n = s->cfg.n, rows = n * s->horizon;
     switch (id) {
@@ -1485,6 +1508,10 @@ void* o_sim_buffer(o_sim* s, int id, size_t* bytes) {
         case MDN_BUF_PHYSICS: *bytes = sizeof(mdn_physics_params); return &s->physics;
         case MDN_BUF_CONTACT_ID: *bytes = rows * 4; return s->contact;
         case MDN_BUF_TASK_STATES: *bytes = n * sizeof(mdn_task_state); return s->tasks;
+        case MDN_BUF_BANK_WORLDS: *bytes = (size_t)s->bank.bank_count * sizeof(mdn_world); return s->bank_worlds;
+        case MDN_BUF_BANK_SCHEDULE: *bytes = s->bank_schedule ? n * s->bank.schedule_stride * 4 : 0; return s->bank_schedule;
+        case MDN_BUF_BANK_ACTIVE_IDS: *bytes = n * 4; return s->bank_active;
+        case MDN_BUF_BANK_TRANSITION_IDS: *bytes = rows * 4; return s->bank_transition;
         case 100: *bytes = A_P * 4; return s->actor_m;
         case 101: *bytes = A_P * 4; return s->actor_v;
         case 102: *bytes = C_P * 4; return s->critic_m;
@@ -1508,8 +1535,38 @@ static float sim_normal(uint32_t* rng) { /* sim.metal:49, cpu_reference.hpp:76-8
     return sqrtf(-2.0f * logf(u)) * cosf(6.28318530718f * v);
 }
 
-/* sim.metal:55-94 (cpu_reference.hpp:240-273); runtime domain randomisation off. */
-static void reset_one(o_sim* s, uint32_t n, int first) {
+/* sim_apply_challenge_world, sim.metal:95-122. */
+static void apply_challenge_world(o_sim* s, uint32_t n, uint32_t slot) {
+    const mdn_bank_control* b = &s->bank;
+    if (b->enabled == 0 || b->bank_count == 0 || n >= s->cfg.n || slot >= b->schedule_stride) return;
+    const uint32_t gid = s->env_base + n;
+    const uint32_t level = s->bank_schedule[(size_t)n * b->schedule_stride + slot];
+    mdn_sim_run* run = &s->runs[n];
+    mdn_world* w = &s->worlds[n];
+    if (level == 0xffffffffu) {
+        uint32_t rng = run->rng;
+        const uint32_t family = o_wtraining_family(gid % 2 == 0 ? 12u : 13u, &rng);
+        o_wgenerate(w, o_wrng(&rng), family, 4.0f);
+        run->rng = rng;
+    } else {
+        if (level >= b->bank_count) return;
+        *w = s->bank_worlds[level];
+    }
+    w->wind[0] = clean_env(&s->cfg, gid) ? 0.0f : s->cfg.wind;
+    w->wind[1] = 0;
+    w->wind[2] = 0;
+    run->initial_distance = len3(w->goal[0], w->goal[1], w->goal[2] - 1.5f);
+    if (w->family == 10 || w->family == 11) {
+        s->states[n].linear_velocity[0] = s->cfg.speed;
+        run->desired_velocity[0] = s->cfg.speed;
+        run->previous_nav[0] = 1.0f;
+    }
+    s->bank_active[n] = level;
+}
+
+/* sim.metal:55-94 (cpu_reference.hpp:240-273); runtime domain randomisation off;
+ * then the challenge-bank world of schedule slot `slot` (sim.metal:143,330). */
+static void reset_one(o_sim* s, uint32_t n, int first, uint32_t slot) {
     const mdn_sim_config* c = &s->cfg;
     mdn_physics_state* st = &s->states[n];
     mdn_sim_run* run = &s->runs[n];
@@ -1559,6 +1616,8 @@ static void reset_one(o_sim* s, uint32_t n, int first) {
         run->success_time = run->total_path = run->total_elapsed = run->final_progress = 0;
         for (uint32_t j = 0; j < NFRAMES * 12; j++) s->poses[(size_t)n * NFRAMES * 12 + j] = 0;
     }
+    if (s->bank.enabled) apply_challenge_world(s, n, slot);
+    else s->bank_active[n] = 0xffffffffu;
     /* sim_reset_navigation_task, sim.metal:125-141 */
     mdn_task_state* task = &s->tasks[n];
     memset(task, 0, sizeof(*task));
@@ -1580,7 +1639,7 @@ static void reset_one(o_sim* s, uint32_t n, int first) {
     }
 }
 void o_sim_reset(o_sim* s) {
-    for (uint32_t n = 0; n < s->cfg.n; n++) reset_one(s, n, 1);
+    for (uint32_t n = 0; n < s->cfg.n; n++) reset_one(s, n, 1, 0);
 }
 
 /* sim.metal:145-158 (cpu_reference.hpp:278-302) */
@@ -1918,6 +1977,7 @@ static void advance_env(o_sim* s, uint32_t t, uint32_t n) {
     float co[COBS], hidden[HID];
     critic_obs(s, &st, w, run, co);
     s->next_values[row] = critic_forward_row(s->critic, co, hidden);
+    s->bank_transition[row] = s->bank.enabled ? s->bank_active[n] : 0xffffffffu; /* sim.metal:326 */
     if (success || collision || timeout) {
         run->successes += success;
         run->collisions += collision;
@@ -1927,7 +1987,7 @@ static void advance_env(o_sim* s, uint32_t t, uint32_t n) {
         run->total_path += run->path;
         run->total_elapsed += run->elapsed;
         run->final_progress += 1.0f - after / smax(run->initial_distance, 1.0e-4f);
-        if (!c->eval) reset_one(s, n, 0);
+        if (!c->eval) reset_one(s, n, 0, t + 1);
     }
 }
 

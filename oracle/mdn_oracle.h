@@ -70,6 +70,7 @@ o_sim* o_sim_create_shard(const mdn_sim_config* cfg, uint32_t horizon, const mdn
                           const mdn_physics_params* physics, const float* room, uint32_t env_base);
 void o_sim_rows_grad(o_sim* s, const uint32_t* rows, uint32_t count, float batch, float* grad);
 void o_sim_set_task_control(o_sim* s, const mdn_task_control* ctl);
+void o_sim_set_challenge_bank(o_sim* s, const mdn_world* worlds, const mdn_bank_control* ctl);
 /* navigation_tasks.hpp */
 uint32_t o_generate_task(mdn_world* w, mdn_task_state* task, uint32_t* rng, const mdn_task_config* c, const float* room);
 void o_task_apply_start(const mdn_task_state* task, mdn_physics_state* s);

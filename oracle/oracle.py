@@ -82,6 +82,7 @@ def load_oracle():
     d("o_sim_train_rollout", None, _P, _U, _U, _P, _U, _P, _P, _P, _P)
     d("o_set_threads", None, ctypes.c_int)
     d("o_sim_set_task_control", None, _P, _P)
+    d("o_sim_set_challenge_bank", None, _P, _P, _P)
     d("o_generate_task", _U, _P, _P, _P, _P, _P)
     d("o_task_apply_start", None, _P, _P)
     d("o_task_step", None, _P, _P, _P, _P, _P, _U, _U, _P)
@@ -117,6 +118,27 @@ def load_ref_deploy():
     d("refd_write_navpol", ctypes.c_int, ctypes.c_char_p, _P, _F, ctypes.c_char_p)
     d("refd_load_navpol", ctypes.c_int, ctypes.c_char_p, _P, _P, _P)
     d("refd_wide_eval", _U, ctypes.c_char_p, _P, _U, _P, _P, _P)
+    return lib
+
+
+def load_ref_bank():
+    """The reference's challenge-bank sampler (oracle/_ref/libref_bank.so), or
+    None when it was never built (no reference sources)."""
+    so = HERE / "_ref" / "libref_bank.so"
+    if not so.exists():
+        return None
+    lib = ctypes.CDLL(str(so))
+    d = lambda n, r, *a: _declare(lib, n, r, *a)
+    d("refb_error", ctypes.c_char_p)
+    d("refb_create", ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p, _P, _F, _F, ctypes.POINTER(_P))
+    d("refb_destroy", None, _P)
+    d("refb_control", ctypes.c_int, _P, _P)
+    d("refb_initial_schedule", ctypes.c_int, _P, _P)
+    d("refb_next_schedule", ctypes.c_int, _P, _P, _U, ctypes.c_uint64, _P)
+    d("refb_observe", ctypes.c_int, _P, _P, _P, _P, _P, ctypes.c_uint64)
+    d("refb_level", ctypes.c_int, _P, _U, _P, _P)
+    d("refb_save", ctypes.c_int, _P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_uint64, _P, _U)
+    d("refb_load", ctypes.c_int, _P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_uint64, _P)
     return lib
 
 
@@ -225,6 +247,12 @@ class OracleSim(_Buffers):
         """navigation_training::configure without the reset (call reset())."""
         self.task_control = np.array(control, self.layouts.TASK_CONTROL)
         self.lib.o_sim_set_task_control(self.h, ptr(self.task_control))
+
+    def set_challenge_bank(self, worlds, control):
+        """Bank worlds + control; the schedule buffer starts zeroed."""
+        self.bank_worlds = np.ascontiguousarray(worlds, self.layouts.WORLD)
+        self.bank_control = np.array(tuple(control), self.layouts.BANK_CONTROL)
+        self.lib.o_sim_set_challenge_bank(self.h, ptr(self.bank_worlds), ptr(self.bank_control))
 
     def step(self, tick):
         self.lib.o_sim_step(self.h, tick)
