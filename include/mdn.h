@@ -161,6 +161,23 @@ typedef struct mdn_task_control {
     mdn_task_config config;
 } mdn_task_control;
 
+/* RLPhysicsDomainRange (physics_domain.hpp:17-24) and NavigationRuntimeConfig
+ * (navigation_runtime.hpp:9-14): per-episode plant stress variation. */
+typedef struct mdn_domain_range {
+    float mass_scale_min, mass_scale_max;
+    float inertia_axis_scale_min, inertia_axis_scale_max;
+    float thrust_gain_min, thrust_gain_max;
+    float rising_lag_scale_min, rising_lag_scale_max;
+    float falling_lag_scale_min, falling_lag_scale_max;
+    float minimum_thrust_to_weight;
+} mdn_domain_range;
+typedef struct mdn_runtime_config {
+    uint32_t enabled;
+    float domain_amplitude;  /* 0..1; 0 keeps the nominal plant */
+    uint32_t domain_seed;
+    mdn_domain_range domain_range;
+} mdn_runtime_config;
+
 /* NavigationTaskState (navigation_tasks.hpp:147-177, 192 bytes), one per env. */
 typedef struct mdn_task_state {
     uint32_t generation_status, valid, generation_attempts, family, stage, objective, max_nav_steps, step_count;
@@ -220,7 +237,10 @@ enum {
     MDN_BUF_BANK_ACTIVE_IDS = 26,     /* uint32[n] level each env plays           */
     MDN_BUF_BANK_TRANSITION_IDS = 27, /* uint32[T][n] level of each transition    */
     MDN_BUF_RAW_ADVANTAGES = 28,      /* float[T][n] GAE before normalisation     */
-    MDN_BUF_COUNT = 29
+    MDN_BUF_ENV_PHYSICS = 29,         /* mdn_physics_params[n] each env's episode
+                                         plant (environment_physics, main.mm:537);
+                                         allocated while a runtime config is on  */
+    MDN_BUF_COUNT = 30
 };
 
 /* ---- library / device --------------------------------------------------- */
@@ -272,18 +292,32 @@ int mdn_sim_upload(mdn_sim* sim, int id, const void* host, size_t offset, size_t
  * min_clearance, peak_speed. */
 int mdn_sim_report(mdn_sim* sim, double out[10]);
 int mdn_sim_dims(mdn_sim* sim, uint32_t* n, uint32_t* horizon, uint32_t* actor_params, uint32_t* critic_params);
+/* rl_physics_domain_stress_range (physics_domain.hpp:37-40). */
+void mdn_domain_stress_range(mdn_domain_range* out);
+/* Sim.runtime_control (main.mm:532-537): with runtime->enabled != 0 every
+ * episode reset draws the env's plant (rl_physics_sample_domain,
+ * physics_domain.hpp:99-157, seeded per env and episode as
+ * sim_domain_episode_seed, sim.metal:50-54), stores it in MDN_BUF_ENV_PHYSICS
+ * and hovers each rotor at that plant's thrust (sim.metal:62-82); the advance
+ * integrates each env with its own plant (sim.metal:287). A rejected draw
+ * stores the nominal plant with a NaN mass, which mdn_sim_validate_tasks
+ * reports. Takes effect at the next reset. NULL or enabled == 0: the shared
+ * nominal plant. */
+int mdn_sim_set_runtime(mdn_sim* sim, const mdn_runtime_config* runtime);
 /* navigation_task_default_config (navigation_tasks.hpp:97-142) followed by the
  * overrides of navigation_training::task_settings (navigation_training.hpp:7-14).
  * Returns MDN_ERR_INVALID for an unsupported stage/family/difficulty. */
 int mdn_task_settings(uint32_t stage, uint32_t family, float difficulty, mdn_task_config* out);
 /* navigation_training::configure (navigation_training.hpp:16-25): enable the
- * goal-arrival task generator and reward for every env and reset the sim.
- * domain_amplitude must be 0 in this build (per-episode plant randomisation,
- * physics_domain.hpp, is not implemented); the task's nav period must equal
- * substeps x 10 ms. Passing control->enabled == 0 returns to legacy episodes. */
+ * goal-arrival task generator and reward for every env, switch the runtime
+ * config on with domain_amplitude (0..1), seed 0x3f84d5b5 and the stress range,
+ * and reset the sim. The task's nav period must equal substeps x 10 ms and no
+ * challenge bank may be enabled. Passing control->enabled == 0 returns to legacy
+ * episodes (tasks and runtime config off). */
 int mdn_sim_configure_tasks(mdn_sim* sim, const mdn_task_control* control, float domain_amplitude);
 /* navigation_training::validate_rollout (navigation_training.hpp:27-35):
- * MDN_ERR_STATE naming the first env whose task generation was rejected. */
+ * MDN_ERR_STATE naming the first env whose task generation was rejected, or
+ * whose episode plant draw was rejected while the runtime config is on. */
 int mdn_sim_validate_tasks(mdn_sim* sim);
 /* Pose-aware mechanical contact audit (vehicle_geometry.hpp:241-376, run as
  * navigation_contact.metal:3-25 runs it), enabled per simulator: every policy
@@ -351,11 +385,21 @@ int mdn_minibatch_order(uint32_t rows, uint32_t minibatch, uint32_t epochs, uint
 int mdn_ppo_minibatch_order(mdn_ppo* ppo, uint32_t rollout_index, uint32_t* out, size_t count);
 /* Device time of the last rollout update (CUDA events). */
 int mdn_ppo_last_update_ms(mdn_ppo* ppo, float* ms);
-/* PPOTrainer::save_checkpoint / load_checkpoint (main.mm:1209-1320): PPOFIX1 v6. */
+/* PPOTrainer::save_checkpoint / load_checkpoint (main.mm:1209-1320): PPOFIX1.
+ * Save writes version 6, or version 8 while the runtime config or the task
+ * generator is on (plus the runtime/task configuration, per-env episode plants
+ * and task states, nominal plant and RAPTOR weights). Load reads versions 3-8;
+ * a version 7-8 file's runtime and task configuration must equal the
+ * simulator's (set them first: mdn_sim_configure_tasks / mdn_sim_set_runtime);
+ * versions 9-10 (reward shaping, calibrated camera) return MDN_ERR_MISMATCH. */
 int mdn_ppo_checkpoint_save(mdn_ppo* ppo, const char* path, uint32_t family, uint32_t seed,
                             uint32_t completed_rollouts);
 int mdn_ppo_checkpoint_load(mdn_ppo* ppo, const char* path, uint32_t family, uint32_t horizon,
                             uint32_t n, uint32_t seed);
+/* Read a checkpoint's header and, for versions 7-8, its runtime and task
+ * configuration (zeroed below version 7) on the host, without a device. */
+int mdn_checkpoint_inspect(const char* path, mdn_checkpoint_header* header, mdn_runtime_config* runtime,
+                           mdn_task_control* tasks);
 
 /* GAE + advantage normalisation of one rollout that allocates no memory.
  * No counterpart in the reference. For callers that cannot call cudaMalloc:

@@ -84,6 +84,9 @@ SIGNATURES = {
     "mdn_gae_normalize_static": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _U, _U, ctypes.c_float,
                                                  ctypes.c_float, _P]),
     "mdn_sim_set_challenge_bank": (ctypes.c_int, [_P, _P, _P]),
+    "mdn_domain_stress_range": (None, [_P]),
+    "mdn_sim_set_runtime": (ctypes.c_int, [_P, _P]),
+    "mdn_checkpoint_inspect": (ctypes.c_int, [ctypes.c_char_p, _P, _P, _P]),
     "mdn_sha256_file": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p]),
     "mdn_bank_load": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(_P)]),
     "mdn_bank_free": (ctypes.c_int, [_P]),
@@ -311,6 +314,14 @@ class Sim:
         """Upload this simulator's schedule rows: uint32 [n][schedule_stride]."""
         self.upload("bank_schedule", np.ascontiguousarray(schedule, np.uint32))
 
+    def set_runtime(self, runtime=None):
+        """Per-episode plant variation (mdn_sim_set_runtime); None switches it off."""
+        if runtime is None:
+            check(lib().mdn_sim_set_runtime(self.h, None))
+            return
+        r = np.array(runtime, layouts.RUNTIME_CONFIG)
+        check(lib().mdn_sim_set_runtime(self.h, _ptr(r)))
+
     def configure_tasks(self, control, domain_amplitude=0.0):
         """navigation_training::configure: enable goal-arrival tasks and reset."""
         ctl = np.array(control, layouts.TASK_CONTROL)
@@ -404,6 +415,29 @@ def write_policy(path, actor, hidden, source_checkpoint, max_speed_mps=1.5):
     a = np.ascontiguousarray(actor, np.float32)
     check(lib().mdn_policy_write(str(path).encode(), _ptr(a), int(hidden), str(source_checkpoint).encode(),
                                  max_speed_mps))
+
+
+def checkpoint_inspect(path):
+    """Header, runtime config and task control of a PPOFIX1 file (mdn_checkpoint_inspect)."""
+    h = np.zeros((), layouts.CHECKPOINT_HEADER)
+    rt = np.zeros((), layouts.RUNTIME_CONFIG)
+    tc = np.zeros((), layouts.TASK_CONTROL)
+    check(lib().mdn_checkpoint_inspect(str(path).encode(), _ptr(h), _ptr(rt), _ptr(tc)))
+    return h, rt, tc
+
+
+def runtime_config(domain_amplitude, domain_seed=0x3F84D5B5, enabled=1, domain_range=None):
+    """NavigationRuntimeConfig with the stress range (rl_physics_domain_stress_range)
+    unless a DOMAIN_RANGE value is given; the defaults are navigation_training::configure's."""
+    r = np.zeros((), layouts.RUNTIME_CONFIG)
+    r["enabled"], r["domain_amplitude"], r["domain_seed"] = enabled, domain_amplitude, domain_seed
+    if domain_range is None:
+        rng = np.zeros((), layouts.DOMAIN_RANGE)
+        lib().mdn_domain_stress_range(_ptr(rng))
+        r["domain_range"] = rng
+    else:
+        r["domain_range"] = np.array(domain_range, layouts.DOMAIN_RANGE)
+    return r
 
 
 def sha256_file(path):

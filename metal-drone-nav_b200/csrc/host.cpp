@@ -243,6 +243,8 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
     a.bank_active = static_cast<uint32_t*>(buf[MDN_BUF_BANK_ACTIVE_IDS]);
     a.bank_transition = bytes[MDN_BUF_BANK_TRANSITION_IDS] ? static_cast<uint32_t*>(buf[MDN_BUF_BANK_TRANSITION_IDS])
                                                            : nullptr;
+    a.runtime = runtime;
+    a.env_physics = static_cast<mdn_physics_params*>(buf[MDN_BUF_ENV_PHYSICS]);
     return a;
 }
 
@@ -362,8 +364,9 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         b[MDN_BUF_BANK_ACTIVE_IDS] = n * sizeof(uint32_t);
         // Bank worlds, schedule, transition ids and raw advantages are
         // allocated by mdn_sim_set_challenge_bank.
-        for (int id : {MDN_BUF_BANK_WORLDS, MDN_BUF_BANK_SCHEDULE, MDN_BUF_BANK_TRANSITION_IDS, MDN_BUF_RAW_ADVANTAGES})
-            b[id] = 0;
+        for (int id : {MDN_BUF_BANK_WORLDS, MDN_BUF_BANK_SCHEDULE, MDN_BUF_BANK_TRANSITION_IDS, MDN_BUF_RAW_ADVANTAGES,
+                       MDN_BUF_ENV_PHYSICS})
+            b[id] = 0;  // MDN_BUF_ENV_PHYSICS: allocated by mdn_sim_set_runtime
         for (int id = 0; id < MDN_BUF_COUNT; id++) {
             const cudaError_t e = cudaMalloc(&sim->buf[id], std::max<size_t>(b[id], 16));
             if (e != cudaSuccess) {
@@ -433,6 +436,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         // kernel's lanes per environment, for tuning.
         const char* group_env = std::getenv("MDN_ADVANCE_GROUP");
         sim->plan = plan_step(n, dev->sm_count, group_env ? std::atoi(group_env) : 0);
+        mdn_domain_stress_range(&sim->runtime.domain_range);  // runtime config off (main.mm:532)
         cuda_check(launch_reset(sim->args(0), true, sim->stream), "reset");
         cuda_check(cudaStreamSynchronize(sim->stream), "mdn_sim_create");
         dev->sims.push_back(sim.get());
@@ -597,6 +601,37 @@ extern "C" int mdn_sim_set_challenge_bank(mdn_sim* sim, const mdn_world* bank_wo
         if (sim->bytes[MDN_BUF_RAW_ADVANTAGES] == 0) sim_realloc(sim, MDN_BUF_RAW_ADVANTAGES, rows * sizeof(float), 0);
         sim->bank = c;
         sim->release_graphs();  // kernel arguments are captured by value
+    });
+}
+
+extern "C" void mdn_domain_stress_range(mdn_domain_range* out) {
+    if (out) *out = mdn_domain_range{0.90f, 1.10f, 0.90f, 1.10f, 0.90f, 1.10f, 0.75f, 1.35f, 0.75f, 1.35f, 1.15f};
+}
+
+namespace mdn {
+// Sim.runtime_control (main.mm:532-537); the per-env plant buffer is
+// allocated the first time the config is switched on.
+// The reference's initial runtime buffer (main.mm:532): off, with the stress
+// range filled in. Checkpoints store these bytes and compare them on resume.
+mdn_runtime_config default_runtime() {
+    mdn_runtime_config r{};
+    mdn_domain_stress_range(&r.domain_range);
+    return r;
+}
+
+void set_runtime(mdn_sim* sim, const mdn_runtime_config* runtime) {
+    cuda_check(cudaStreamSynchronize(sim->stream), "runtime config");
+    if (runtime && runtime->enabled && sim->bytes[MDN_BUF_ENV_PHYSICS] == 0)
+        sim_realloc(sim, MDN_BUF_ENV_PHYSICS, size_t(sim->n) * sizeof(mdn_physics_params), 0);
+    sim->runtime = runtime ? *runtime : default_runtime();
+    sim->release_graphs();  // kernel arguments are captured by value
+}
+}  // namespace mdn
+
+extern "C" int mdn_sim_set_runtime(mdn_sim* sim, const mdn_runtime_config* runtime) {
+    return guarded([&] {
+        checked(sim);
+        set_runtime(sim, runtime);
     });
 }
 
@@ -814,14 +849,20 @@ extern "C" int mdn_sim_configure_tasks(mdn_sim* sim, const mdn_task_control* con
         checked(sim);
         require(control != nullptr, MDN_ERR_INVALID, "null task control");
         require(std::isfinite(domain_amplitude) && domain_amplitude >= 0.0f && domain_amplitude <= 1.0f,
-                MDN_ERR_INVALID, "domain amplitude must be 0..1");
-        require(domain_amplitude == 0.0f, MDN_ERR_INVALID,
-                "domain amplitude > 0 (per-episode plant randomisation) is not supported by this build");
+                MDN_ERR_INVALID, "domain amplitude must be0..1");
         if (control->enabled) {
             require(std::fabs(control->config.nav_period_s - float(sim->cfg.substeps) * 0.01f) < 1e-6f,
                     MDN_ERR_INVALID, "task/simulator clock mismatch");
+            require(sim->bank.enabled == 0, MDN_ERR_INVALID, "task generator and frozen bank cannot both own the world");
         }
         cuda_check(cudaStreamSynchronize(sim->stream), "configure tasks");
+        mdn_runtime_config runtime = default_runtime();
+        if (control->enabled) {
+            runtime.enabled = 1;
+            runtime.domain_amplitude = domain_amplitude;
+            runtime.domain_seed = 0x3f84d5b5u;
+        }
+        set_runtime(sim, &runtime);
         sim->task_ctl = *control;
         sim->task_config_ok = task_config_ok(control->config) ? 1u : 0u;
         sim->release_graphs();  // kernel arguments captured by value
@@ -837,9 +878,20 @@ extern "C" int mdn_sim_validate_tasks(mdn_sim* sim) {
         cuda_check(cudaMemcpyAsync(tasks.data(), sim->buf[MDN_BUF_TASK_STATES], sim->bytes[MDN_BUF_TASK_STATES],
                                    cudaMemcpyDeviceToHost, sim->stream), "download task states");
         cuda_check(cudaStreamSynchronize(sim->stream), "validate tasks");
-        for (uint32_t env = 0; env < sim->n; env++)
+        std::vector<mdn_physics_params> plants;
+        if (sim->runtime.enabled) {
+            plants.resize(sim->n);
+            cuda_check(cudaMemcpyAsync(plants.data(), sim->buf[MDN_BUF_ENV_PHYSICS], sim->bytes[MDN_BUF_ENV_PHYSICS],
+                                       cudaMemcpyDeviceToHost, sim->stream), "download episode plants");
+            cuda_check(cudaStreamSynchronize(sim->stream), "validate tasks");
+        }
+        for (uint32_t env = 0; env < sim->n; env++) {
             require(tasks[env].valid && tasks[env].generation_status == 4u, MDN_ERR_STATE,
                     "task generation rejected env=" + std::to_string(env) +
                         " status=" + std::to_string(tasks[env].generation_status));
+            if (!plants.empty())
+                require(std::isfinite(plants[env].mass) && plants[env].mass > 0, MDN_ERR_STATE,
+                        "episode dynamics sample rejected");
+        }
     });
 }

@@ -87,6 +87,7 @@ struct mdn_sim {
     bool audit_enabled = false;                             // mechanical contact audit (mdn_sim_set_contact_audit)
     float audit_margin = 0.04f;
     mdn_bank_control bank{};                                // frozen challenge bank (mdn_sim_set_challenge_bank)
+    mdn_runtime_config runtime{};                           // per-episode plant variation (mdn_sim_set_runtime)
     size_t bytes[MDN_BUF_COUNT] = {};
     float room_lo[3], room_hi[3], room_c[3], room_e[3];
     mdn::StepPlan plan;

@@ -90,6 +90,10 @@ struct SimArgs {
     const uint32_t* bank_schedule;
     uint32_t* bank_active;
     uint32_t* bank_transition;
+    // Per-episode plant (NavigationRuntimeConfig, navigation_runtime.hpp:9-14):
+    // while runtime.enabled, each env's plant lives in env_physics[n].
+    mdn_runtime_config runtime;
+    mdn_physics_params* env_physics;
 };
 
 }  // namespace mdn

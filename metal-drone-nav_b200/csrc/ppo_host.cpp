@@ -503,8 +503,34 @@ void download(void* dst, const T* src, size_t bytes, cudaStream_t s) {
 }
 }  // namespace
 
-// PPOTrainer::save_checkpoint (main.mm:1287-1320), version 6 layout: header,
-// actor, critic, Adam moments, then the full simulator state.
+// read_checkpoint_header (main.mm:993-1000): the 136-byte header of any
+// version 3..10, with the fields older versions lack filled as the reference
+// fills them.
+static void read_checkpoint_header(std::ifstream& f, mdn_checkpoint_header& h) {
+    std::memset(&h, 0, sizeof(h));
+    f.read(reinterpret_cast<char*>(&h), 48);
+    require(bool(f) && std::memcmp(h.magic, "PPOFIX1", 7) == 0 && h.version >= 3 && h.version <= 10, MDN_ERR_IO,
+            "checkpoint prefix/version");
+    f.read(reinterpret_cast<char*>(&h.config), 64);
+    if (h.version >= 4) {
+        f.read(reinterpret_cast<char*>(&h) + 112, 16);
+        if (h.version >= 6) f.read(reinterpret_cast<char*>(&h) + 128, 8);
+        else h.config.geometry_memory = 0;
+        if (h.version == 4) h.config.velocity_contract = 0;
+    } else {
+        h.config.risk_coef = 0;
+        h.config.entropy_coef = h.family == 7 ? .002f : .005f;
+        h.config.learning_rate = .0003f;
+        h.config.velocity_contract = 0;
+        h.config.geometry_memory = 0;
+    }
+    require(bool(f), MDN_ERR_IO, "checkpoint header truncated");
+}
+
+// PPOTrainer::save_checkpoint (main.mm:1287-1320): header, actor, critic, Adam
+// moments, the simulator state, and from version 8 (runtime config or tasks
+// on) the runtime and task configuration, each env's episode plant and task
+// state, the nominal plant and the RAPTOR controller.
 extern "C" int mdn_ppo_checkpoint_save(mdn_ppo* t, const char* path, uint32_t family, uint32_t seed,
                                        uint32_t completed_rollouts) {
     return guarded([&] {
@@ -517,7 +543,8 @@ extern "C" int mdn_ppo_checkpoint_save(mdn_ppo* t, const char* path, uint32_t fa
         mdn_checkpoint_header h;
         std::memset(&h, 0, sizeof(h));
         std::memcpy(h.magic, "PPOFIX1", 7);
-        h.version = 6;
+        const bool extended = sim->runtime.enabled || sim->task_ctl.enabled;
+        h.version = extended ? 8 : 6;
         h.actor_count = sim->actor_params;
         h.critic_count = kCriticParams;
         h.horizon = sim->horizon;
@@ -544,6 +571,27 @@ extern "C" int mdn_ppo_checkpoint_save(mdn_ppo* t, const char* path, uint32_t fa
         append_device(t->args.critic_v, kCriticParams * 4);
         for (int id : {MDN_BUF_STATES, MDN_BUF_RUNS, MDN_BUF_WORLDS, MDN_BUF_SENSORS, MDN_BUF_POSES, MDN_BUF_COMMANDS})
             append_device(sim->buf[id], sim->bytes[id]);
+        if (extended) {
+            auto append_host = [&](const void* p, size_t bytes) {
+                const size_t o = blob.size();
+                blob.resize(o + bytes);
+                std::memcpy(blob.data() + o, p, bytes);
+            };
+            append_host(&sim->runtime, sizeof(sim->runtime));
+            append_host(&sim->task_ctl, sizeof(sim->task_ctl));
+            if (sim->bytes[MDN_BUF_ENV_PHYSICS]) {
+                append_device(sim->buf[MDN_BUF_ENV_PHYSICS], sim->bytes[MDN_BUF_ENV_PHYSICS]);
+            } else {  // runtime config never on: every env flies the nominal plant (sim.metal:62,69)
+                cuda_check(cudaStreamSynchronize(sim->stream), "checkpoint download");
+                mdn_physics_params nominal;
+                download(&nominal, sim->buf[MDN_BUF_PHYSICS], sizeof(nominal), sim->stream);
+                cuda_check(cudaStreamSynchronize(sim->stream), "checkpoint download");
+                for (uint32_t e = 0; e < sim->n; e++) append_host(&nominal, sizeof(nominal));
+            }
+            append_device(sim->buf[MDN_BUF_TASK_STATES], sim->bytes[MDN_BUF_TASK_STATES]);
+            append_device(sim->buf[MDN_BUF_PHYSICS], sizeof(mdn_physics_params));
+            append_device(sim->buf[MDN_BUF_RAPTOR], sizeof(mdn_raptor_weights));
+        }
         cuda_check(cudaStreamSynchronize(sim->stream), "checkpoint download");
         const std::string tmp = std::string(path) + ".tmp";
         {
@@ -557,8 +605,11 @@ extern "C" int mdn_ppo_checkpoint_save(mdn_ppo* t, const char* path, uint32_t fa
     });
 }
 
-// PPOTrainer::load_checkpoint (main.mm:1209-1286) and read_checkpoint_header
-// (main.mm:993-1000) for versions 3..6 (no runtime/task/shaping blocks).
+// PPOTrainer::load_checkpoint (main.mm:1209-1286) for versions 3..8. Versions
+// 7-8 carry the runtime and task configuration, which must equal the
+// simulator's byte for byte (configure it first; mdn_checkpoint_inspect reads
+// them). Versions 9-10 (geodesic reward shaping, calibrated camera) are
+// rejected: this build implements neither.
 extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t family, uint32_t horizon, uint32_t n,
                                        uint32_t seed) {
     return guarded([&] {
@@ -568,26 +619,9 @@ extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t fa
         std::ifstream f(path, std::ios::binary);
         require(bool(f), MDN_ERR_IO, std::string("cannot open checkpoint ") + path);
         mdn_checkpoint_header h;
-        std::memset(&h, 0, sizeof(h));
-        f.read(reinterpret_cast<char*>(&h), 48);
-        require(bool(f) && std::memcmp(h.magic, "PPOFIX1", 7) == 0 && h.version >= 3 && h.version <= 10, MDN_ERR_IO,
-                "checkpoint prefix/version");
-        f.read(reinterpret_cast<char*>(&h.config), 64);
-        if (h.version >= 4) {
-            f.read(reinterpret_cast<char*>(&h) + 112, 16);
-            if (h.version >= 6) f.read(reinterpret_cast<char*>(&h) + 128, 8);
-            else h.config.geometry_memory = 0;
-            if (h.version == 4) h.config.velocity_contract = 0;
-        } else {
-            h.config.risk_coef = 0;
-            h.config.entropy_coef = h.family == 7 ? .002f : .005f;
-            h.config.learning_rate = .0003f;
-            h.config.velocity_contract = 0;
-            h.config.geometry_memory = 0;
-        }
-        require(bool(f), MDN_ERR_IO, "checkpoint header truncated");
-        require(h.version <= 6, MDN_ERR_MISMATCH,
-                "checkpoint version 7+ carries runtime/task/shaping state this build does not implement");
+        read_checkpoint_header(f, h);
+        require(h.version <= 8, MDN_ERR_MISMATCH,
+                "checkpoint version 9+ carries reward-shaping or calibrated-camera state this build does not implement");
         require(h.actor_count == sim->actor_params && h.critic_count == kCriticParams, MDN_ERR_MISMATCH,
                 "PPO checkpoint dimensions mismatch");
         require(h.family == family && h.horizon == horizon && h.n == n && h.base_seed == seed, MDN_ERR_MISMATCH,
@@ -621,6 +655,42 @@ extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t fa
         if (h.version >= 6) read_to_device(sim->buf[MDN_BUF_POSES], sim->bytes[MDN_BUF_POSES]);
         else cuda_check(cudaMemsetAsync(sim->buf[MDN_BUF_POSES], 0, sim->bytes[MDN_BUF_POSES], sim->stream), "poses");
         read_to_device(sim->buf[MDN_BUF_COMMANDS], sim->bytes[MDN_BUF_COMMANDS]);
+        if (h.version >= 7) {
+            mdn_runtime_config saved_runtime{};
+            mdn_task_control saved_tasks{};
+            f.read(reinterpret_cast<char*>(&saved_runtime), sizeof(saved_runtime));
+            f.read(reinterpret_cast<char*>(&saved_tasks), h.version >= 8 ? sizeof(saved_tasks) : 144);
+            require(h.version >= 8 || saved_tasks.enabled == 0, MDN_ERR_MISMATCH,
+                    "task-generator semantics changed; use an explicit parameter warmstart from version7");
+            require(bool(f), MDN_ERR_IO, "truncated navigation runtime configuration");
+            require(std::memcmp(&saved_runtime, &sim->runtime, sizeof(saved_runtime)) == 0 &&
+                        std::memcmp(&saved_tasks, &sim->task_ctl, sizeof(saved_tasks)) == 0,
+                    MDN_ERR_MISMATCH, "checkpoint dynamics/task configuration mismatch");
+            const size_t plants = size_t(sim->n) * sizeof(mdn_physics_params);
+            if (sim->bytes[MDN_BUF_ENV_PHYSICS]) {
+                read_to_device(sim->buf[MDN_BUF_ENV_PHYSICS], plants);
+            } else {  // runtime config off: the stored plants are the nominal one, unused
+                tmp.resize(plants);
+                f.read(tmp.data(), std::streamsize(plants));
+                require(bool(f), MDN_ERR_IO, "truncated PPO simulator checkpoint");
+            }
+            read_to_device(sim->buf[MDN_BUF_TASK_STATES], sim->bytes[MDN_BUF_TASK_STATES]);
+            mdn_physics_params saved_nominal{}, nominal{};
+            mdn_raptor_weights saved_raptor{};
+            f.read(reinterpret_cast<char*>(&saved_nominal), sizeof(saved_nominal));
+            f.read(reinterpret_cast<char*>(&saved_raptor), sizeof(saved_raptor));
+            require(bool(f), MDN_ERR_IO, "truncated checkpoint nominal plant/controller");
+            std::vector<mdn_raptor_weights> raptor(1);
+            download(&nominal, sim->buf[MDN_BUF_PHYSICS], sizeof(nominal), sim->stream);
+            download(raptor.data(), sim->buf[MDN_BUF_RAPTOR], sizeof(mdn_raptor_weights), sim->stream);
+            cuda_check(cudaStreamSynchronize(sim->stream), "checkpoint compare");
+            require(std::memcmp(&saved_nominal, &nominal, sizeof(nominal)) == 0 &&
+                        std::memcmp(&saved_raptor, raptor.data(), sizeof(saved_raptor)) == 0,
+                    MDN_ERR_MISMATCH, "checkpoint nominal plant/controller mismatch");
+        } else {
+            require(sim->runtime.enabled == 0 && sim->task_ctl.enabled == 0, MDN_ERR_MISMATCH,
+                    "legacy resume cannot infer new dynamics/task state; use explicit parameter warmstart");
+        }
         refresh_world_mirror(sim);
         char extra;
         require(!f.read(&extra, 1), MDN_ERR_IO, "PPO checkpoint has trailing data");
@@ -638,6 +708,35 @@ extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t fa
         t->optimizer_step = h.optimizer_step;
         t->completed_rollouts = h.completed_rollouts;
         cuda_check(cudaStreamSynchronize(sim->stream), "checkpoint load");
+    });
+}
+
+// The header and the version 7-8 runtime/task blocks of a checkpoint, read
+// on the host (main.mm:993-1000, 1238-1240).
+extern "C" int mdn_checkpoint_inspect(const char* path, mdn_checkpoint_header* header, mdn_runtime_config* runtime,
+                                      mdn_task_control* tasks) {
+    return guarded([&] {
+        require(path != nullptr, MDN_ERR_INVALID, "null path");
+        std::ifstream f(path, std::ios::binary);
+        require(bool(f), MDN_ERR_IO, std::string("cannot open checkpoint ") + path);
+        mdn_checkpoint_header h;
+        read_checkpoint_header(f, h);
+        if (header) *header = h;
+        mdn_runtime_config rt{};
+        mdn_task_control tc{};
+        if (h.version >= 7) {
+            const uint64_t n = h.n;
+            const uint64_t skip = (uint64_t(h.actor_count) * 3 + uint64_t(h.critic_count) * 3) * 4 +
+                                  n * (sizeof(mdn_physics_state) + sizeof(mdn_sim_run) + sizeof(mdn_world) +
+                                       uint64_t(kFrames) * kPixels * 4 + uint64_t(kFrames) * 12 * 4 +
+                                       uint64_t(kFrames) * kActions * 4);
+            f.seekg(std::streamoff(skip), std::ios::cur);
+            f.read(reinterpret_cast<char*>(&rt), sizeof(rt));
+            f.read(reinterpret_cast<char*>(&tc), h.version >= 8 ? sizeof(tc) : 144);
+            require(bool(f), MDN_ERR_IO, "truncated navigation runtime configuration");
+        }
+        if (runtime) *runtime = rt;
+        if (tasks) *tasks = tc;
     });
 }
 

@@ -1032,7 +1032,9 @@ __device__ __forceinline__ void raptor_forward_group(const float* __restrict__ w
     }
 }
 
-template <int G>
+// kEnvPhysics: each env integrates its own episode plant (runtime config on,
+// sim.metal:287) instead of the block's shared copy of the nominal one.
+template <int G, bool kEnvPhysics>
 __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(SimArgs a) {
     using L = RaptorSmem<G>;
     constexpr int kGroups = kAdvanceThreads / G;
@@ -1092,7 +1094,8 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
             bool collision = false;
             float step_clearance = 12.0f;
             int32_t contact = -1;
-            const float wind[3] = {w.wind[0] * params.mass, w.wind[1] * params.mass, w.wind[2] * params.mass};
+            const mdn_physics_params& plant = kEnvPhysics ? a.env_physics[i] : params;
+            const float wind[3] = {w.wind[0] * plant.mass, w.wind[1] * plant.mass, w.wind[2] * plant.mass};
             float refp[3] = {run.reference_position[0], run.reference_position[1], run.reference_position[2]};
             const float dv_[3] = {run.desired_velocity[0], run.desired_velocity[1], run.desired_velocity[2]};
             float path = run.path, elapsed = run.elapsed, min_clear = run.min_clearance, peak = run.peak_speed;
@@ -1120,7 +1123,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
 #pragma unroll
                 for (int j = 0; j < 4; j++) motors[j] = smax(-1.0f, smin(1.0f, motors[j]));
                 float nx[17];
-                l2f_step(params, s, motors, wind, nx);
+                l2f_step(plant, s, motors, wind, nx);
                 bool valid = true;
 #pragma unroll
                 for (int j = 0; j < 17; j++) valid = valid && isfinite(nx[j]);
@@ -1266,15 +1269,22 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
 template <int G>
 static int advance_blocks_per_sm() {
     int blocks = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_advance<G>, kAdvanceThreads, 0) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_advance<G, false>, kAdvanceThreads, 0) != cudaSuccess)
         blocks = 1;
     return blocks > 0 ? blocks : 1;
 }
 
 static cudaError_t launch_advance(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
+    const bool own = a.runtime.enabled != 0;
     switch (plan.advance_group) {
-        case 2: k_advance<2><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a); break;
-        default: k_advance<1><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a); break;
+        case 2:
+            if (own) k_advance<2, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
+            else k_advance<2, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
+            break;
+        default:
+            if (own) k_advance<1, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
+            else k_advance<1, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
+            break;
     }
     return cudaGetLastError();
 }

@@ -1,6 +1,7 @@
 // Procedural world families and episode reset on the device.
 // world.hpp:104-318 (generators) and sim.metal:55-94 (sim_reset_one).
 #pragma once
+#include "domain.cuh"
 #include "mdn_device.cuh"
 
 namespace mdn {
@@ -385,13 +386,36 @@ __device__ bool reset_env(const SimArgs& a, uint32_t i, bool first) {
     s.orientation_wxyz[0] = 1;
     s.orientation_wxyz[1] = s.orientation_wxyz[2] = s.orientation_wxyz[3] = 0;
     const mdn_physics_params& p = *a.physics;
-    const float target = p.mass * 9.81f / 4;
-    const float c0 = p.rotor_thrust_coefficients[0], c1 = p.rotor_thrust_coefficients[1],
-                c2 = p.rotor_thrust_coefficients[2];
-    const float hover = clampf((-c1 + sqrtf(c1 * c1 - 4 * c2 * (c0 - target))) / (2 * c2), p.action_min, p.action_max);
+    float hover[4];
+    if (!a.runtime.enabled) {
+        const float target = p.mass * 9.81f / 4;
+        const float c0 = p.rotor_thrust_coefficients[0], c1 = p.rotor_thrust_coefficients[1],
+                    c2 = p.rotor_thrust_coefficients[2];
+        const float h = clampf((-c1 + sqrtf(c1 * c1 - 4 * c2 * (c0 - target))) / (2 * c2), p.action_min, p.action_max);
+        for (int j = 0; j < 4; j++) hover[j] = h;
+    } else {
+        // The episode's own plant (sim.metal:62-69), then per-rotor hover at
+        // its thrust curve (sim.metal:75-80).
+        mdn_physics_params& ep = a.env_physics[i];
+        ep = p;
+        if (a.runtime.domain_amplitude > 0.0f) {
+            uint32_t drng = domain_episode_seed(a.runtime, c.seed, gid, first ? 0u : run.episodes);
+            mdn_physics_params varied;
+            if (sample_domain(p, drng, a.runtime.domain_amplitude, a.runtime.domain_range, varied)) ep = varied;
+            else ep.mass = __int_as_float(0x7fc00000);
+        }
+        const float target = ep.mass * 9.81f / 4;
+        for (int rotor = 0; rotor < 4; rotor++) {
+            const float c0 = ep.rotor_thrust_coefficients[3 * rotor], c1 = ep.rotor_thrust_coefficients[3 * rotor + 1],
+                        c2 = ep.rotor_thrust_coefficients[3 * rotor + 2];
+            const float disc = c1 * c1 - 4 * c2 * (c0 - target);
+            hover[rotor] = disc >= 0.0f ? clampf((-c1 + sqrtf(disc)) / (2 * c2), ep.action_min, ep.action_max)
+                                        : ep.action_max;
+        }
+    }
     for (int j = 0; j < 16; j++) run.hidden[j] = a.raptor->initial_hidden_state[j];
     for (int j = 0; j < 4; j++) {
-        s.rpm[j] = hover;
+        s.rpm[j] = hover[j];
         run.motors[j] = 0;
         run.previous_nav[j] = 0;
     }

@@ -76,7 +76,7 @@ BUF = {
     "obs": 8, "co": 9, "actions": 10, "logp": 11, "values": 12, "rewards": 13, "next_values": 14,
     "terminated": 15, "truncated": 16, "advantages": 17, "returns": 18, "raptor": 19, "physics": 20,
     "contact_id": 21, "task_states": 22, "contact_audit": 23, "bank_worlds": 24, "bank_schedule": 25,
-    "bank_active_ids": 26, "bank_transition_ids": 27, "raw_advantages": 28,
+    "bank_active_ids": 26, "bank_transition_ids": 27, "raw_advantages": 28, "env_physics": 29,
 }
 CONTACT_AUDIT = np.dtype([("physical_clearance_m", "<f4"), ("safety_clearance_m", "<f4"), ("contact", "<u4"),
                           ("ambiguous", "<u4")])
@@ -85,8 +85,17 @@ BUF_DTYPE = {
     "terminated": np.dtype(np.uint8), "truncated": np.dtype(np.uint8), "contact_id": np.dtype(np.int32),
     "task_states": TASK_STATE, "contact_audit": CONTACT_AUDIT, "bank_worlds": WORLD,
     "bank_schedule": np.dtype(np.uint32), "bank_active_ids": np.dtype(np.uint32),
-    "bank_transition_ids": np.dtype(np.uint32),
+    "bank_transition_ids": np.dtype(np.uint32), "env_physics": PARAMS,
 }
+# RLPhysicsDomainRange (physics_domain.hpp:17-24), NavigationRuntimeConfig
+# (navigation_runtime.hpp:9-14).
+DOMAIN_RANGE = np.dtype([(k, "<f4") for k in (
+    "mass_scale_min", "mass_scale_max", "inertia_axis_scale_min", "inertia_axis_scale_max", "thrust_gain_min",
+    "thrust_gain_max", "rising_lag_scale_min", "rising_lag_scale_max", "falling_lag_scale_min",
+    "falling_lag_scale_max", "minimum_thrust_to_weight")])
+RUNTIME_CONFIG = np.dtype([("enabled", "<u4"), ("domain_amplitude", "<f4"), ("domain_seed", "<u4"),
+                           ("domain_range", DOMAIN_RANGE)])
+assert DOMAIN_RANGE.itemsize == 44 and RUNTIME_CONFIG.itemsize == 56
 # ChallengeBankControl (sim.metal:13) and challenge_training::Settings
 # (challenge_training.hpp:40-49); mdn_bank_level = the numeric fields of
 # challenge_evaluation::Level (challenge_evaluation.hpp:36-45).

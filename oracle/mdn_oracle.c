@@ -1384,6 +1384,9 @@ struct o_sim {
     float* pixel_rays; /* [320][3] */
     mdn_task_control task_ctl; /* goal-arrival tasks (navigation_training::configure) */
     mdn_task_state* tasks;
+    /* per-episode plants (NavigationRuntimeConfig, navigation_runtime.hpp:9-14) */
+    mdn_runtime_config runtime;
+    mdn_physics_params* env_physics;
     /* frozen challenge bank (ChallengeBankControl, sim.metal:13) */
     mdn_bank_control bank;
     mdn_world* bank_worlds;
@@ -1434,6 +1437,7 @@ o_sim* o_sim_create_shard(const mdn_sim_config* cfg, uint32_t horizon, const mdn
     s->contact = zalloc(rows * 4);
     s->pixel_rays = zalloc(NPIX * 3 * 4);
     s->tasks = zalloc(n * sizeof(mdn_task_state));
+    s->env_physics = zalloc(n * sizeof(mdn_physics_params));
     s->bank_active = zalloc(n * 4);
     s->bank_transition = zalloc(rows * 4);
     for (size_t k = 0; k < n; k++) s->bank_active[k] = 0xffffffffu;
@@ -1462,12 +1466,16 @@ void o_sim_destroy(o_sim* s) {
                     s->actor_m, s->actor_v, s->critic_m, s->critic_v, s->obs, s->co, s->actions, s->logp,
                     s->values, s->rewards, s->next_values, s->adv, s->ret, s->term, s->trunc, s->contact,
                     s->pixel_rays, s->tasks, s->bank_worlds, s->bank_schedule, s->bank_active,
-                    s->bank_transition};
+                    s->bank_transition, s->env_physics};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++) free(bufs[i]);
     free(s);
 }
 void o_sim_set_config(o_sim* s, const mdn_sim_config* cfg) { s->cfg = *cfg; }
 void o_sim_set_task_control(o_sim* s, const mdn_task_control* ctl) { s->task_ctl = *ctl; }
+void o_sim_set_runtime(o_sim* s, const mdn_runtime_config* rt) {
+    memset(&s->runtime, 0, sizeof(s->runtime));
+    if (rt && rt->enabled) s->runtime = *rt;
+}
 /* Bank worlds and a zeroed env-major schedule [n][stride] (main.mm:543-547,
  * 2351-2353); enabled == 0 switches banks off. */
 void o_sim_set_challenge_bank(o_sim* s, const mdn_world* worlds, const mdn_bank_control* ctl) {
@@ -1512,6 +1520,7 @@ void* o_sim_buffer(o_sim* s, int id, size_t* bytes) {
         case MDN_BUF_BANK_SCHEDULE: *bytes = s->bank_schedule ? n * s->bank.schedule_stride * 4 : 0; return s->bank_schedule;
         case MDN_BUF_BANK_ACTIVE_IDS: *bytes = n * 4; return s->bank_active;
         case MDN_BUF_BANK_TRANSITION_IDS: *bytes = rows * 4; return s->bank_transition;
+        case MDN_BUF_ENV_PHYSICS: *bytes = n * sizeof(mdn_physics_params); return s->env_physics;
         case 100: *bytes = A_P * 4; return s->actor_m;
         case 101: *bytes = A_P * 4; return s->actor_v;
         case 102: *bytes = C_P * 4; return s->critic_m;
@@ -1533,6 +1542,106 @@ static void rotation(const float q[4], float r[9]) { /* sim.metal:43-48, cpu_ref
 static float sim_normal(uint32_t* rng) { /* sim.metal:49, cpu_reference.hpp:76-80 */
     const float u = smax(o_wurand(rng), 1e-7f), v = o_wurand(rng);
     return sqrtf(-2.0f * logf(u)) * cosf(6.28318530718f * v);
+}
+
+/* ---- per-episode plant variation, physics_domain.hpp:43-157 ---- */
+static uint32_t domain_next(uint32_t* state) { /* :43-48 */
+    uint32_t v = *state ? *state : 1u;
+    v ^= v << 13;
+    v ^= v >> 17;
+    v ^= v << 5;
+    *state = v ? v : 1u;
+    return *state;
+}
+static float domain_scale(uint32_t* state, float low, float high, float amplitude) { /* :50-58 */
+    const float u = (float)(domain_next(state) >> 8) * (1.0f / 16777216.0f);
+    const float draw = low + (high - low) * u;
+    return 1.0f + amplitude * (draw - 1.0f);
+}
+static int domain_inverse3(const float* m, float* inv) { /* :60-83 */
+    const float a = m[0], b = m[1], c = m[2], d = m[3], e = m[4], f = m[5], g = m[6], h = m[7], i = m[8];
+    for (int j = 0; j < 9; j++)
+        if (!isfinite(m[j])) return 0;
+    if (fabsf(b - d) > 1.0e-6f || fabsf(c - g) > 1.0e-6f || fabsf(f - h) > 1.0e-6f) return 0;
+    const float minor2 = a * e - b * d;
+    const float det = a * (e * i - f * h) - b * (d * i - f * g) + c * (d * h - e * g);
+    if (!(a > 0.0f) || !(minor2 > 0.0f) || !(det > 0.0f) || !isfinite(det)) return 0;
+    const float rcp = 1.0f / det;
+    inv[0] = (e * i - f * h) * rcp; inv[1] = (c * h - b * i) * rcp; inv[2] = (b * f - c * e) * rcp;
+    inv[3] = (f * g - d * i) * rcp; inv[4] = (a * i - c * g) * rcp; inv[5] = (c * d - a * f) * rcp;
+    inv[6] = (d * h - e * g) * rcp; inv[7] = (b * g - a * h) * rcp; inv[8] = (a * e - b * d) * rcp;
+    for (int j = 0; j < 9; j++)
+        if (!isfinite(inv[j])) return 0;
+    return 1;
+}
+static float domain_thrust_to_weight(const mdn_physics_params* p) { /* :85-95 */
+    float thrust = 0.0f;
+    const float action = p->action_max;
+    for (int r = 0; r < 4; r++) {
+        const float* k = p->rotor_thrust_coefficients + 3 * r;
+        const float magnitude = k[0] + k[1] * action + k[2] * action * action;
+        thrust += p->rotor_thrust_directions[3 * r + 2] * magnitude;
+    }
+    const float weight = p->mass * fabsf(p->gravity_world[2]);
+    return weight > 0.0f ? thrust / weight : 0.0f;
+}
+/* rl_physics_sample_domain (:100-157). sample_out (may be NULL) receives the
+ * 17 floats of RLPhysicsDomainSample. */
+int o_physics_sample_domain(const mdn_physics_params* nominal, uint32_t* rng, float amplitude,
+                            const mdn_domain_range* r, mdn_physics_params* varied, float* sample_out) {
+    if (!isfinite(amplitude) || amplitude < 0.0f || amplitude > 1.0f || !isfinite(r->minimum_thrust_to_weight) ||
+        r->minimum_thrust_to_weight < 1.0f || !isfinite(r->mass_scale_min) || !isfinite(r->mass_scale_max) ||
+        !isfinite(r->inertia_axis_scale_min) || !isfinite(r->inertia_axis_scale_max) ||
+        !isfinite(r->thrust_gain_min) || !isfinite(r->thrust_gain_max) || !isfinite(r->rising_lag_scale_min) ||
+        !isfinite(r->rising_lag_scale_max) || !isfinite(r->falling_lag_scale_min) ||
+        !isfinite(r->falling_lag_scale_max) || !(r->mass_scale_min > 0.0f && r->mass_scale_min <= r->mass_scale_max) ||
+        !(r->inertia_axis_scale_min > 0.0f && r->inertia_axis_scale_min <= r->inertia_axis_scale_max) ||
+        !(r->thrust_gain_min > 0.0f && r->thrust_gain_min <= r->thrust_gain_max) ||
+        !(r->rising_lag_scale_min > 0.0f && r->rising_lag_scale_min <= r->rising_lag_scale_max) ||
+        !(r->falling_lag_scale_min > 0.0f && r->falling_lag_scale_min <= r->falling_lag_scale_max))
+        return 0;
+    float sm[17]; /* mass, inertia axes[3], gain[4], rising[4], falling[4], thrust-to-weight */
+    for (int k = 0; k < 16; k++) sm[k] = 1.0f;
+    sm[16] = 0.0f;
+    *varied = *nominal;
+    if (amplitude > 0.0f) {
+        sm[0] = domain_scale(rng, r->mass_scale_min, r->mass_scale_max, amplitude);
+        for (int k = 0; k < 3; k++) sm[1 + k] = domain_scale(rng, r->inertia_axis_scale_min, r->inertia_axis_scale_max, amplitude);
+        for (int k = 0; k < 4; k++) {
+            sm[4 + k] = domain_scale(rng, r->thrust_gain_min, r->thrust_gain_max, amplitude);
+            sm[8 + k] = domain_scale(rng, r->rising_lag_scale_min, r->rising_lag_scale_max, amplitude);
+            sm[12 + k] = domain_scale(rng, r->falling_lag_scale_min, r->falling_lag_scale_max, amplitude);
+        }
+        varied->mass = nominal->mass * sm[0];
+        float root[3];
+        for (int k = 0; k < 3; k++) root[k] = sqrtf(sm[1 + k]);
+        for (int row = 0; row < 3; row++)
+            for (int col = 0; col < 3; col++)
+                varied->inertia[3 * row + col] = nominal->inertia[3 * row + col] * sm[0] * root[row] * root[col];
+        if (!domain_inverse3(varied->inertia, varied->inertia_inverse)) {
+            if (sample_out) memcpy(sample_out, sm, sizeof(sm));
+            return 0;
+        }
+        for (int k = 0; k < 4; k++) {
+            for (int j = 0; j < 3; j++)
+                varied->rotor_thrust_coefficients[3 * k + j] = nominal->rotor_thrust_coefficients[3 * k + j] * sm[4 + k];
+            varied->rotor_time_constants_rising[k] = nominal->rotor_time_constants_rising[k] * sm[8 + k];
+            varied->rotor_time_constants_falling[k] = nominal->rotor_time_constants_falling[k] * sm[12 + k];
+        }
+    }
+    sm[16] = domain_thrust_to_weight(varied);
+    if (sample_out) memcpy(sample_out, sm, sizeof(sm));
+    return sm[16] >= r->minimum_thrust_to_weight;
+}
+/* sim_domain_episode_seed, sim.metal:50-54. */
+uint32_t o_domain_episode_seed(const mdn_runtime_config* rt, uint32_t cfg_seed, uint32_t env, uint32_t episode) {
+    uint32_t seed = rt->domain_seed ^ cfg_seed ^ ((env + 1u) * 0x9e3779b9u) ^ ((episode + 1u) * 0x85ebca6bu);
+    seed ^= seed >> 16;
+    seed *= 0x7feb352du;
+    seed ^= seed >> 15;
+    seed *= 0x846ca68bu;
+    seed ^= seed >> 16;
+    return seed ? seed : 1u;
 }
 
 /* sim_apply_challenge_world, sim.metal:95-122. */
@@ -1588,13 +1697,39 @@ static void reset_one(o_sim* s, uint32_t n, int first, uint32_t slot) {
     st->orientation_wxyz[0] = 1;
     for (int j = 1; j < 4; j++) st->orientation_wxyz[j] = 0;
     const mdn_physics_params* p = &s->physics;
-    const float target = p->mass * 9.81f / 4;
-    const float c0 = p->rotor_thrust_coefficients[0], c1 = p->rotor_thrust_coefficients[1],
-                c2 = p->rotor_thrust_coefficients[2];
-    const float hover = clampf_((-c1 + sqrtf(c1 * c1 - 4 * c2 * (c0 - target))) / (2 * c2), p->action_min, p->action_max);
+    float hover[4];
+    /* sim.metal:62-82: the episode's plant, then hover at its thrust curve */
+    mdn_physics_params* ep = &s->env_physics[n];
+    *ep = *p;
+    if (s->runtime.enabled && s->runtime.domain_amplitude > 0.0f) {
+        uint32_t drng = o_domain_episode_seed(&s->runtime, c->seed, gid, first ? 0u : run->episodes);
+        mdn_physics_params varied;
+        if (o_physics_sample_domain(p, &drng, s->runtime.domain_amplitude, &s->runtime.domain_range, &varied, NULL))
+            *ep = varied;
+        else {
+            const uint32_t qnan = 0x7fc00000u;
+            memcpy(&ep->mass, &qnan, 4);
+        }
+    }
+    if (!s->runtime.enabled) {
+        const float target = p->mass * 9.81f / 4;
+        const float c0 = p->rotor_thrust_coefficients[0], c1 = p->rotor_thrust_coefficients[1],
+                    c2 = p->rotor_thrust_coefficients[2];
+        const float h = clampf_((-c1 + sqrtf(c1 * c1 - 4 * c2 * (c0 - target))) / (2 * c2), p->action_min, p->action_max);
+        for (int j = 0; j < 4; j++) hover[j] = h;
+    } else {
+        const float target = ep->mass * 9.81f / 4;
+        for (int r = 0; r < 4; r++) {
+            const float c0 = ep->rotor_thrust_coefficients[3 * r], c1 = ep->rotor_thrust_coefficients[3 * r + 1],
+                        c2 = ep->rotor_thrust_coefficients[3 * r + 2];
+            const float disc = c1 * c1 - 4 * c2 * (c0 - target);
+            hover[r] = disc >= 0.0f ? clampf_((-c1 + sqrtf(disc)) / (2 * c2), ep->action_min, ep->action_max)
+                                    : ep->action_max;
+        }
+    }
     memcpy(run->hidden, s->raptor.initial_hidden_state, sizeof(run->hidden));
     for (int j = 0; j < 4; j++) {
-        st->rpm[j] = hover;
+        st->rpm[j] = hover[j];
         run->motors[j] = 0;
         run->previous_nav[j] = 0;
     }
@@ -1903,7 +2038,9 @@ static void advance_env(o_sim* s, uint32_t t, uint32_t n) {
     int collision = 0;
     float step_clearance = 12.0f;
     int32_t contact = -1;
-    const float wind[3] = {w->wind[0] * p->mass, w->wind[1] * p->mass, w->wind[2] * p->mass};
+    /* sim.metal:287: the episode plant integrates while the runtime config is on */
+    const mdn_physics_params* plant = s->runtime.enabled ? &s->env_physics[n] : p;
+    const float wind[3] = {w->wind[0] * plant->mass, w->wind[1] * plant->mass, w->wind[2] * plant->mass};
     for (uint32_t step = 0; step < c->substeps; step++) {
         float mo[22];
         const float v[3] = {run->desired_velocity[0], run->desired_velocity[1], run->desired_velocity[2]};
@@ -1928,7 +2065,7 @@ static void advance_env(o_sim* s, uint32_t t, uint32_t n) {
         o_raptor_forward(&s->raptor, mo, h, motors);
         for (int j = 0; j < 4; j++) motors[j] = smax(-1.0f, smin(1.0f, motors[j])); /* raptor.hpp:95-97 */
         mdn_physics_state next;
-        o_physics_step(&st, motors, wind, p, &next);
+        o_physics_step(&st, motors, wind, plant, &next);
         const int valid = finite3(next.position) && finite3(next.linear_velocity) && finite3(next.angular_velocity_body) &&
                           isfinite(next.orientation_wxyz[0]) && isfinite(next.orientation_wxyz[1]) &&
                           isfinite(next.orientation_wxyz[2]) && isfinite(next.orientation_wxyz[3]) &&

@@ -71,6 +71,10 @@ o_sim* o_sim_create_shard(const mdn_sim_config* cfg, uint32_t horizon, const mdn
 void o_sim_rows_grad(o_sim* s, const uint32_t* rows, uint32_t count, float batch, float* grad);
 void o_sim_set_task_control(o_sim* s, const mdn_task_control* ctl);
 void o_sim_set_challenge_bank(o_sim* s, const mdn_world* worlds, const mdn_bank_control* ctl);
+void o_sim_set_runtime(o_sim* s, const mdn_runtime_config* rt);
+int o_physics_sample_domain(const mdn_physics_params* nominal, uint32_t* rng, float amplitude,
+                            const mdn_domain_range* r, mdn_physics_params* varied, float* sample_out);
+uint32_t o_domain_episode_seed(const mdn_runtime_config* rt, uint32_t cfg_seed, uint32_t env, uint32_t episode);
 /* navigation_tasks.hpp */
 uint32_t o_generate_task(mdn_world* w, mdn_task_state* task, uint32_t* rng, const mdn_task_config* c, const float* room);
 void o_task_apply_start(const mdn_task_state* task, mdn_physics_state* s);

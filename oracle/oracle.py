@@ -83,6 +83,9 @@ def load_oracle():
     d("o_set_threads", None, ctypes.c_int)
     d("o_sim_set_task_control", None, _P, _P)
     d("o_sim_set_challenge_bank", None, _P, _P, _P)
+    d("o_sim_set_runtime", None, _P, _P)
+    d("o_physics_sample_domain", ctypes.c_int, _P, _P, _F, _P, _P, _P)
+    d("o_domain_episode_seed", _U, _P, _U, _U, _U)
     d("o_generate_task", _U, _P, _P, _P, _P, _P)
     d("o_task_apply_start", None, _P, _P)
     d("o_task_step", None, _P, _P, _P, _P, _P, _U, _U, _P)
@@ -192,6 +195,8 @@ def load_ref():
     d("ref_task_step", None, _P, _P, _P, _P, _P, _U, _U, _P)
     d("ref_task_segment_clearance", _F, _P, _P, _P)
     d("ref_vg_world_contact", None, _P, _P, _P, _F, _F, _P)
+    d("ref_physics_sample_domain", ctypes.c_int, _P, _P, _F, _P, _P, _P)
+    d("ref_domain_stress_range", None, _P)
     return lib
 
 
@@ -253,6 +258,11 @@ class OracleSim(_Buffers):
         self.bank_worlds = np.ascontiguousarray(worlds, self.layouts.WORLD)
         self.bank_control = np.array(tuple(control), self.layouts.BANK_CONTROL)
         self.lib.o_sim_set_challenge_bank(self.h, ptr(self.bank_worlds), ptr(self.bank_control))
+
+    def set_runtime(self, runtime):
+        """Sim.runtime_control; takes effect at the next reset."""
+        self.runtime = np.array(runtime, self.layouts.RUNTIME_CONFIG)
+        self.lib.o_sim_set_runtime(self.h, ptr(self.runtime))
 
     def step(self, tick):
         self.lib.o_sim_step(self.h, tick)

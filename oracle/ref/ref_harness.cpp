@@ -67,6 +67,28 @@ void ref_vg_world_contact(const float* position, const float* orientation_wxyz, 
     std::memcpy(out, &r, sizeof(r));
 }
 
+/* rl_physics_sample_domain (physics_domain.hpp:100-157): the varied plant and
+ * the 17 floats of RLPhysicsDomainSample; rl_physics_domain_stress_range. */
+int ref_physics_sample_domain(const mdn_physics_params* nominal, uint32_t* rng, float amplitude,
+                              const mdn_domain_range* range, mdn_physics_params* varied, float* sample) {
+    RLPhysicsParams n, v{};
+    std::memcpy(&n, nominal, sizeof(n));
+    RLPhysicsDomainRange r;
+    std::memcpy(&r, range, sizeof(r));
+    RLPhysicsDomainSample out{};
+    const bool ok = rl_physics_sample_domain(n, *rng, amplitude, r, v, out);
+    std::memcpy(varied, &v, sizeof(v));
+    std::memcpy(sample, &out, sizeof(out));
+    return ok ? 1 : 0;
+}
+void ref_domain_stress_range(mdn_domain_range* out) {
+    const RLPhysicsDomainRange r = rl_physics_domain_stress_range();
+    std::memcpy(out, &r, sizeof(r));
+}
+static_assert(sizeof(RLPhysicsDomainRange) == sizeof(mdn_domain_range), "domain range layout");
+static_assert(sizeof(NavigationRuntimeConfig) == sizeof(mdn_runtime_config), "runtime config layout");
+static_assert(sizeof(RLPhysicsDomainSample) == 17 * sizeof(float), "domain sample layout");
+
 /* ---------------- whole-trainer handle ---------------- */
 void* ref_trainer_create(const mdn_sim_config* cfg, uint32_t horizon, const void* raptor, const void* physics) {
     RaptorWeights w;

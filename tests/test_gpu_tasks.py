@@ -69,11 +69,12 @@ def compare_tasks(g, o, what):
         close(g[f], o[f], f"{what} task.{f}")
 
 
-def pair(pkg, om, device, raptor, cfg, T, control):
+def pair(pkg, om, device, raptor, cfg, T, control, domain_amplitude=0.0):
     gpu = pkg.Sim(device, cfg, T, raptor=raptor)
-    gpu.configure_tasks(control)
+    gpu.configure_tasks(control, domain_amplitude)
     ora = om.OracleSim(pkg.layouts, cfg, T, raptor)
     ora.set_task_control(control)
+    ora.set_runtime(pkg.runtime_config(domain_amplitude))  # navigation_training.hpp:20-22
     ora.reset()
     return gpu, ora
 
@@ -191,8 +192,9 @@ def test_validate_tasks_and_config_checks(pkg, device, raptor):
         bad["config"]["nav_period_s"] = np.float32(0.04)
         with pytest.raises(pkg.MdnError):
             sim.configure_tasks(bad)  # task/simulator clock mismatch
-        with pytest.raises(pkg.MdnError):
-            sim.configure_tasks(control, domain_amplitude=0.5)
+        for amplitude in (1.5, -0.1, float("nan")):
+            with pytest.raises(pkg.MdnError):
+                sim.configure_tasks(control, domain_amplitude=amplitude)  # domain amplitude must be 0..1
         invalid = control.copy()
         invalid["config"]["goal_radius_m"] = np.float32(0.0)
         sim.configure_tasks(invalid)  # accepted like the reference; every env reports status 1
