@@ -518,6 +518,26 @@ int mdn_challenge_save_state(mdn_challenge* sampler, const char* path, const cha
 int mdn_challenge_load_state(mdn_challenge* sampler, const char* path, const char* checkpoint_sha256,
                              uint64_t completed_rollouts, uint32_t* active_ids);
 
+/* challenge_evaluation::BankScore (challenge_evaluation.hpp:53-66); family
+ * slots are families 14, 15, 16. */
+typedef struct mdn_bank_score {
+    uint64_t episodes, successes, collisions, timeouts;
+    uint64_t family_episodes[3], family_successes[3];
+    double successful_time_s;
+} mdn_bank_score;
+/* challenge_evaluation::run (challenge_evaluation.hpp:352-497): evaluate a
+ * PPOFIX1 checkpoint's actor and critic (versions 3-9) on every level of one
+ * split. Levels run in batches of 128 on an evaluation-mode simulator (one
+ * episode per env; no delays, noise or dropout; each level's stored wind), with
+ * the level's world, its simulator policy seed and a fresh start, for
+ * `max_steps` policy steps. One CSV row per level (the reference's 38 columns),
+ * written to a temporary file and renamed into place, and the aggregate score.
+ * mode 2, 13 or 17; speed in (0, 3]; max_steps 1..400; raptor as for
+ * mdn_sim_create. */
+int mdn_bank_evaluate(mdn_device* dev, const mdn_raptor_weights* raptor, const char* checkpoint_path,
+                      const char* bank_jsonl, const char* split, const char* world_sha256, const char* output_csv,
+                      uint32_t mode, float speed, uint32_t max_steps, mdn_bank_score* score);
+
 /* ---- multi-GPU (no reference counterpart: the reference is one Apple GPU) */
 /* Fill a 128-byte NCCL unique id (rank 0) to share through any host channel. */
 int mdn_comm_unique_id(uint8_t id[128]);

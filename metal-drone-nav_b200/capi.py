@@ -87,6 +87,8 @@ SIGNATURES = {
     "mdn_domain_stress_range": (None, [_P]),
     "mdn_sim_set_runtime": (ctypes.c_int, [_P, _P]),
     "mdn_checkpoint_inspect": (ctypes.c_int, [ctypes.c_char_p, _P, _P, _P]),
+    "mdn_bank_evaluate": (ctypes.c_int, [_P, _P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
+                                         ctypes.c_char_p, _U, ctypes.c_float, _U, _P]),
     "mdn_sha256_file": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p]),
     "mdn_bank_load": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(_P)]),
     "mdn_bank_free": (ctypes.c_int, [_P]),
@@ -576,3 +578,17 @@ class ChallengeSampler:
         check(lib().mdn_challenge_load_state(self.h, str(path).encode(), checkpoint_sha256.encode(),
                                              completed_rollouts, _ptr(out)))
         return out
+
+
+def evaluate_bank(device, checkpoint, bank_path, split, world_sha256, output_csv, mode=17, speed=1.5, max_steps=400,
+                  raptor=None):
+    """challenge_evaluation::run (mdn_bank_evaluate): one CSV row per level of
+    `split` and the aggregate BankScore as a dict."""
+    r = np.array(default_raptor() if raptor is None else raptor, layouts.RAPTOR)
+    score = np.zeros((), layouts.BANK_SCORE)
+    check(lib().mdn_bank_evaluate(device.h, _ptr(r), str(checkpoint).encode(), str(bank_path).encode(),
+                                  split.encode(), world_sha256.encode(), str(output_csv).encode(), mode, speed,
+                                  max_steps, _ptr(score)))
+    out = {k: score[k].item() if score[k].ndim == 0 else score[k].tolist() for k in layouts.BANK_SCORE.names}
+    out["success_rate"] = out["successes"] / out["episodes"] if out["episodes"] else 0.0
+    return out

@@ -14,9 +14,12 @@
 #include <cstring>
 #include <filesystem>
 #include <fstream>
+#include <iomanip>
+#include <locale>
 #include <map>
 #include <memory>
 #include <set>
+#include <sstream>
 #include <string>
 #include <vector>
 
@@ -1178,5 +1181,220 @@ extern "C" int mdn_challenge_load_state(mdn_challenge* sampler, const char* path
         require(path && active_ids, MDN_ERR_INVALID, "challenge sampler: null argument");
         sampler_of(sampler).load_state(path, hash_arg(checkpoint_sha256, "challenge sampler"), completed_rollouts,
                                        active_ids);
+    });
+}
+
+// ------------------------------------------------------------------ evaluation
+// challenge_evaluation::run (challenge_evaluation.hpp:352-497).
+namespace mdn {
+namespace {
+
+std::string csv_cell(const std::string& value) {  // :316-321
+    if (value.find_first_of(",\"\r\n") == std::string::npos) return value;
+    std::string escaped = "\"";
+    for (char c : value) {
+        if (c == '"') escaped += '"';
+        escaped += c;
+    }
+    return escaped + '"';
+}
+std::string number_cell(double value) {  // :323-328
+    std::ostringstream out;
+    out.imbue(std::locale::classic());
+    out << std::setprecision(9) << value;
+    return out.str();
+}
+std::string uint_cell(uint64_t value) { return std::to_string(value); }
+std::string witness_route_cell(const Level& level) {  // :332-342
+    std::ostringstream out;
+    out.imbue(std::locale::classic());
+    out << std::setprecision(9) << '[';
+    for (size_t i = 0; i < level.witness_route.size() / 3; ++i) {
+        if (i) out << ',';
+        out << '[' << level.witness_route[3 * i] << ',' << level.witness_route[3 * i + 1] << ','
+            << level.witness_route[3 * i + 2] << ']';
+    }
+    out << ']';
+    return out.str();
+}
+void write_csv_row(std::ofstream& file, const std::vector<std::string>& cells) {
+    for (size_t i = 0; i < cells.size(); ++i) {
+        if (i) file << ',';
+        file << csv_cell(cells[i]);
+    }
+    file << '\n';
+}
+
+// Status -> exception, for calls into this library's own C-ABI.
+void ok(int status) {
+    if (status != MDN_OK) throw Error(status, mdn_last_error());
+}
+
+struct SimGuard {
+    mdn_sim* sim = nullptr;
+    ~SimGuard() {
+        if (sim) mdn_sim_destroy(sim);
+    }
+};
+
+mdn_bank_score evaluate(mdn_device* dev, const mdn_raptor_weights* raptor, const std::string& checkpoint_path,
+                        const std::string& bank_path, const std::string& split, const std::string& world_hash,
+                        const std::string& output_path, uint32_t mode, float speed, uint32_t max_steps) {
+    auto fail = [](const std::string& m) { bank_fail(m); };
+    if (mode != 2 && mode != 13 && mode != 17) fail("mode must be 2, 13, or 17");
+    if (!std::isfinite(speed) || speed <= 0 || speed > 3.0f) fail("speed must be finite and in (0,3]");
+    if (max_steps == 0 || max_steps > 400) fail("max_steps must be in 1..400 (maximum 20 seconds)");
+    require(dev != nullptr && raptor != nullptr, MDN_ERR_INVALID, "challenge bank: null device or controller");
+
+    const std::string checkpoint_hash = sha256_file(checkpoint_path);
+    std::ifstream checkpoint(checkpoint_path, std::ios::binary);
+    if (!checkpoint) throw Error(MDN_ERR_IO, "challenge bank: cannot open checkpoint: " + checkpoint_path);
+    mdn_checkpoint_header header;
+    read_checkpoint_header(checkpoint, header);
+    // The actor may be the 64-unit one or a wide one (hidden*189 + 8 floats).
+    const uint32_t hidden = header.actor_count >= 8 ? (header.actor_count - 8) / 189 : 0;
+    const bool actor_ok = header.actor_count == actor_param_count(hidden) &&
+                          (hidden == uint32_t(kHidden) || (hidden % 256 == 0 && hidden >= 256 && hidden <= 8192));
+    if (!actor_ok || header.critic_count != uint32_t(kCriticParams) || header.version < 3 || header.version > 9)
+        fail("checkpoint header/dimensions are unsupported");
+    std::vector<float> actor(header.actor_count), critic(header.critic_count);
+    checkpoint.read(reinterpret_cast<char*>(actor.data()), std::streamsize(actor.size() * sizeof(float)));
+    checkpoint.read(reinterpret_cast<char*>(critic.data()), std::streamsize(critic.size() * sizeof(float)));
+    if (!checkpoint) fail("checkpoint is missing actor or critic weights");
+    auto finite = [](float v) { return std::isfinite(v); };
+    if (!std::all_of(actor.begin(), actor.end(), finite) || !std::all_of(critic.begin(), critic.end(), finite))
+        fail("checkpoint contains non-finite weights");
+
+    BankData bank;
+    load_split(bank_path, split, world_hash, bank);
+    const std::vector<Level>& levels = bank.levels;
+    const std::filesystem::path output_file(output_path);
+    if (output_file.has_parent_path()) std::filesystem::create_directories(output_file.parent_path());
+    const std::filesystem::path temporary_output = output_file.string() + ".tmp";
+    std::ofstream csv(temporary_output, std::ios::out | std::ios::trunc);
+    if (!csv) throw Error(MDN_ERR_IO, "challenge bank: cannot write output CSV: " + temporary_output.string());
+    csv.imbue(std::locale::classic());
+    write_csv_row(csv, {"failure_id", "scene_sha256", "split", "family", "family_name", "seed", "base_seed",
+                        "environment_index", "distance_m", "geometry_contract", "difficulty", "difficulty_band", "mode",
+                        "speed_mps", "max_steps", "wind_x", "wind_y", "wind_z", "obstacle_count", "witness_route_json",
+                        "episodes", "success", "collision", "timeout", "progress", "path_m", "elapsed_s",
+                        "goal_time_s", "mean_speed_mps", "peak_speed_mps", "min_clearance_m", "physics_invalid",
+                        "direct_route_clearance_m", "witness_min_clearance_m", "witness_sample_count",
+                        "checkpoint_sha256", "bank_sha256", "world_source_sha256"});
+
+    mdn_bank_score score{};
+    constexpr uint32_t kBatch = 128;  // challenge_evaluation.hpp:30
+    for (size_t begin = 0; begin < levels.size(); begin += kBatch) {
+        const uint32_t count = uint32_t(std::min<size_t>(kBatch, levels.size() - begin));
+        mdn_sim_config config;
+        mdn_sim_config_default(&config);
+        config.n = count;
+        config.family = 0;  // the bank's geometry replaces the reset's worlds before any observation
+        config.mode = mode;
+        config.seed = levels[begin].info.seed;
+        config.eval = 1;
+        config.speed = speed;
+        config.distance = levels[begin].info.distance;
+        config.max_steps = max_steps;
+        config.sensor_delay = 0;
+        config.command_delay = 0;
+        config.wind = 0;
+        config.depth_noise = 0;
+        config.dropout = 0;
+        config.velocity_contract = header.config.velocity_contract;
+        config.geometry_memory = header.config.geometry_memory;
+        mdn_rollout_shape shape;
+        mdn_rollout_shape_default(&shape);
+        shape.actor_hidden = hidden;
+        SimGuard guard;
+        ok(mdn_sim_create(dev, &config, &shape, 32, raptor, nullptr, &guard.sim));
+        mdn_sim* sim = guard.sim;
+        ok(mdn_sim_upload(sim, MDN_BUF_ACTOR, actor.data(), 0, actor.size() * sizeof(float)));
+        ok(mdn_sim_upload(sim, MDN_BUF_CRITIC, critic.data(), 0, critic.size() * sizeof(float)));
+        std::vector<mdn_world> worlds(count);
+        std::vector<mdn_sim_run> runs(count);
+        ok(mdn_sim_download(sim, MDN_BUF_RUNS, runs.data(), 0, runs.size() * sizeof(mdn_sim_run)));
+        for (uint32_t n = 0; n < count; ++n) {
+            const Level& level = levels[begin + n];
+            worlds[n] = level.world;
+            // The reset's policy-sampling seed of this bank environment, independent of its batch slot.
+            runs[n].rng = level.info.base_seed + level.info.environment_index * kEnvStride + kEnvOffset;
+            runs[n].steps = 0;
+            const float* g = level.world.goal;
+            runs[n].initial_distance = std::sqrt(g[0] * g[0] + g[1] * g[1] + (g[2] - 1.5f) * (g[2] - 1.5f));
+            runs[n].reference_position[0] = 0;
+            runs[n].reference_position[1] = 0;
+            runs[n].reference_position[2] = 1.5f;
+        }
+        ok(mdn_sim_upload(sim, MDN_BUF_WORLDS, worlds.data(), 0, worlds.size() * sizeof(mdn_world)));
+        ok(mdn_sim_upload(sim, MDN_BUF_RUNS, runs.data(), 0, runs.size() * sizeof(mdn_sim_run)));
+        ok(mdn_sim_collect(sim, max_steps));
+        ok(mdn_sync(dev, nullptr));
+        std::vector<mdn_physics_state> states(count);
+        ok(mdn_sim_download(sim, MDN_BUF_RUNS, runs.data(), 0, runs.size() * sizeof(mdn_sim_run)));
+        ok(mdn_sim_download(sim, MDN_BUF_STATES, states.data(), 0, states.size() * sizeof(mdn_physics_state)));
+        for (uint32_t n = 0; n < count; ++n) {
+            const Level& level = levels[begin + n];
+            const mdn_sim_run& run = runs[n];
+            if (run.episodes != 1 || run.successes + run.collisions + run.timeouts != 1)
+                fail("level did not produce exactly one terminal outcome: " + level.failure_id);
+            const float progress = run.final_progress;
+            const float mean_speed = run.elapsed > 0 ? run.path / run.elapsed : 0;
+            const float values[] = {progress, run.path, run.elapsed, run.success_time, mean_speed, run.peak_speed,
+                                    run.min_clearance};
+            if (!std::all_of(std::begin(values), std::end(values), finite))
+                fail("non-finite episode metric for " + level.failure_id);
+            for (int j = 0; j < 3; ++j)
+                if (!std::isfinite(states[n].position[j]) || !std::isfinite(states[n].linear_velocity[j]))
+                    fail("non-finite terminal simulator state for " + level.failure_id);
+            score.episodes += run.episodes;
+            score.successes += run.successes;
+            score.collisions += run.collisions;
+            score.timeouts += run.timeouts;
+            score.successful_time_s += run.success_time;
+            const size_t slot = level.info.family - 14;
+            score.family_episodes[slot] += run.episodes;
+            score.family_successes[slot] += run.successes;
+            const mdn_bank_level& i = level.info;
+            write_csv_row(csv, {level.failure_id, level.scene_sha256, level.split, uint_cell(i.family), level.family_name,
+                                uint_cell(i.seed), uint_cell(i.base_seed), uint_cell(i.environment_index),
+                                number_cell(i.distance), level.geometry_contract, number_cell(i.difficulty),
+                                level.difficulty_band, uint_cell(mode), number_cell(speed), uint_cell(max_steps),
+                                number_cell(level.world.wind[0]), number_cell(level.world.wind[1]),
+                                number_cell(level.world.wind[2]), uint_cell(level.world.count),
+                                witness_route_cell(level), uint_cell(run.episodes), uint_cell(run.successes),
+                                uint_cell(run.collisions), uint_cell(run.timeouts), number_cell(progress),
+                                number_cell(run.path), number_cell(run.elapsed),
+                                run.successes ? number_cell(run.success_time) : "", number_cell(mean_speed),
+                                number_cell(run.peak_speed), number_cell(run.min_clearance), "not_instrumented",
+                                number_cell(i.direct_route_clearance_m), number_cell(i.witness_min_clearance_m),
+                                uint_cell(i.witness_sample_count), checkpoint_hash, bank.bank_hash,
+                                level.world_source_sha256});
+        }
+        csv.flush();
+        if (!csv) throw Error(MDN_ERR_IO, "challenge bank: write failed for output CSV: " + temporary_output.string());
+    }
+    csv.close();
+    if (!csv) throw Error(MDN_ERR_IO, "challenge bank: close failed for output CSV: " + temporary_output.string());
+    std::error_code rename_error;
+    std::filesystem::rename(temporary_output, output_file, rename_error);
+    if (rename_error)
+        throw Error(MDN_ERR_IO, "challenge bank: cannot atomically publish output CSV: " + rename_error.message());
+    return score;
+}
+
+}  // namespace
+}  // namespace mdn
+
+extern "C" int mdn_bank_evaluate(mdn_device* dev, const mdn_raptor_weights* raptor, const char* checkpoint_path,
+                                 const char* bank_jsonl, const char* split, const char* world_sha256,
+                                 const char* output_csv, uint32_t mode, float speed, uint32_t max_steps,
+                                 mdn_bank_score* score) {
+    return guarded([&] {
+        require(checkpoint_path && bank_jsonl && split && world_sha256 && output_csv, MDN_ERR_INVALID,
+                "challenge bank: null argument");
+        const mdn_bank_score s = mdn::evaluate(dev, raptor, checkpoint_path, bank_jsonl, split, world_sha256,
+                                               output_csv, mode, speed, max_steps);
+        if (score) *score = s;
     });
 }

@@ -4,6 +4,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <fstream>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -57,6 +58,10 @@ cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStr
                                  const WideStep* wide);
 cudaError_t fp32_peak(int sm_count, double* tflops);
 int kernels_per_step(const mdn_sim_config& c, bool wide);
+
+// read_checkpoint_header (main.mm:993-1000) for PPOFIX1 versions 3..10
+// (ppo_host.cpp); throws on a bad prefix, version or truncation.
+void read_checkpoint_header(std::ifstream& f, mdn_checkpoint_header& h);
 
 }  // namespace mdn
 

@@ -506,7 +506,7 @@ void download(void* dst, const T* src, size_t bytes, cudaStream_t s) {
 // read_checkpoint_header (main.mm:993-1000): the 136-byte header of any
 // version 3..10, with the fields older versions lack filled as the reference
 // fills them.
-static void read_checkpoint_header(std::ifstream& f, mdn_checkpoint_header& h) {
+void mdn::read_checkpoint_header(std::ifstream& f, mdn_checkpoint_header& h) {
     std::memset(&h, 0, sizeof(h));
     f.read(reinterpret_cast<char*>(&h), 48);
     require(bool(f) && std::memcmp(h.magic, "PPOFIX1", 7) == 0 && h.version >= 3 && h.version <= 10, MDN_ERR_IO,

@@ -110,6 +110,9 @@ BANK_LEVEL = np.dtype([
 BANK_TEXT = ("failure_id", "split", "family_name", "geometry_contract", "difficulty_band", "scene_sha256",
              "world_source_sha256")
 INVALID_LEVEL = 0xFFFFFFFF
+# challenge_evaluation::BankScore (challenge_evaluation.hpp:53-66).
+BANK_SCORE = np.dtype([("episodes", "<u8"), ("successes", "<u8"), ("collisions", "<u8"), ("timeouts", "<u8"),
+                       ("family_episodes", "<u8", 3), ("family_successes", "<u8", 3), ("successful_time_s", "<f8")])
 
 # Fixed PPO parameter offsets for the 184/64/4 actor and 32/64/1 critic (ppo.hpp:35-45).
 ACTOR_OBS, CRITIC_OBS, HIDDEN, ACTIONS = 184, 32, 64, 4

@@ -37,7 +37,7 @@ def ranges(layouts):
     base = stress(layouts)
     out = [("stress", base)]
     strict = base.copy()
-    strict["minimum_thrust_to_weight"] = 2.2  # the Crazyflie sits near 2.2: some draws fail
+    strict["minimum_thrust_to_weight"] = 1.46  # draws span about 1.26-1.70 at amplitude 1: some fail
     out.append(("strict", strict))
     wide = base.copy()
     wide["mass_scale_min"], wide["mass_scale_max"] = 0.5, 1.6

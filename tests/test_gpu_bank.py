@@ -189,3 +189,74 @@ def test_bank_training_loop():
         sampler.close()
         sim.close()
         dev.close()
+
+
+def test_bank_evaluate_matches_oracle(tmp_path):
+    """challenge_evaluation::run (challenge_evaluation.hpp:352-497) through
+    mdn_bank_evaluate: the 38-column CSV and the BankScore of a checkpoint on the
+    train split equal an oracle replay of the same batch (worlds, per-level policy
+    seeds, evaluation mode); outcomes bitwise, episode metrics within 1e-3."""
+    import csv
+    pkg, om = load_package(), load_oracle_module()
+    L = pkg.layouts
+    dev = pkg.Device(0)
+    cfg = L.default_config(n=64, family=1, speed=1.0, distance=3.0, seed=8)
+    sim = pkg.Sim(dev, cfg, 8)
+    tr = pkg.PPOTrainer(sim)
+    try:
+        sim.collect()
+        tr.rollout_update(0)
+        ck = tmp_path / "ck.bin"
+        tr.save_checkpoint(ck, 1, 8, 1)
+        actor, critic = sim.download("actor"), sim.download("critic")
+        steps = 30
+        out = tmp_path / "eval" / "train.csv"
+        score = pkg.evaluate_bank(dev, ck, SMALL, "train", world_hash(), out, mode=17, speed=1.5, max_steps=steps)
+        rows = list(csv.reader(out.open()))
+        header, rows = rows[0], rows[1:]
+        assert len(header) == 38 and header[0] == "failure_id" and header[-1] == "world_source_sha256"
+        assert len(rows) == 12 and not (tmp_path / "eval" / "train.csv.tmp").exists()
+        bank = pkg.ChallengeBank(SMALL, "train", world_hash())
+        levels = [bank.level(i) for i in range(12)]
+        worlds = bank.worlds()
+        col = {name: k for k, name in enumerate(header)}
+        for r, lv in zip(rows, levels):
+            assert r[col["failure_id"]] == lv["failure_id"] and r[col["split"]] == "train"
+            assert r[col["checkpoint_sha256"]] == pkg.sha256_file(ck) and r[col["bank_sha256"]] == bank.bank_sha256
+            assert r[col["physics_invalid"]] == "not_instrumented" and int(r[col["max_steps"]]) == steps
+            assert json.loads(r[col["witness_route_json"]]) == pytest.approx(lv["witness_route"].tolist())
+        ocfg = L.default_config(n=12, family=0, mode=17, seed=levels[0]["seed"], eval=1, speed=1.5,
+                                distance=levels[0]["distance"], max_steps=steps, wind=0.0,
+                                velocity_contract=int(cfg["velocity_contract"]), geometry_memory=0)
+        ora = om.OracleSim(L, ocfg, 32, pkg.default_raptor())
+        ora.buf("actor")[:] = actor
+        ora.buf("critic")[:] = critic
+        ora.buf("worlds")[:] = worlds
+        runs = ora.buf("runs")
+        for i, lv in enumerate(levels):
+            runs["rng"][i] = (lv["base_seed"] + lv["environment_index"] * 747796405 + 2891336453) & 0xFFFFFFFF
+            runs["steps"][i] = 0
+            g = worlds["goal"][i].astype(np.float32)
+            runs["initial_distance"][i] = np.sqrt(g[0] * g[0] + g[1] * g[1] + (g[2] - np.float32(1.5)) ** 2)
+            runs["reference_position"][i] = (0.0, 0.0, 1.5)
+        for t in range(steps):
+            ora.step(t % 32)
+        runs = ora.buf("runs")
+        for i, r in enumerate(rows):
+            for name, field in (("episodes", "episodes"), ("success", "successes"), ("collision", "collisions"),
+                                ("timeout", "timeouts")):
+                assert int(r[col[name]]) == int(runs[field][i]), (i, name)
+            for name, value in (("progress", runs["final_progress"][i]), ("path_m", runs["path"][i]),
+                                ("elapsed_s", runs["elapsed"][i]), ("peak_speed_mps", runs["peak_speed"][i]),
+                                ("min_clearance_m", runs["min_clearance"][i])):
+                assert float(r[col[name]]) == pytest.approx(float(value), rel=1e-3, abs=1e-3), (i, name)
+        assert score["episodes"] == 12 and score["successes"] == int(runs["successes"].sum())
+        assert score["family_episodes"] == [4, 4, 4]
+        with pytest.raises(pkg.MdnError):
+            pkg.evaluate_bank(dev, ck, SMALL, "train", world_hash(), out, mode=5)
+        with pytest.raises(pkg.MdnError):
+            pkg.evaluate_bank(dev, ck, SMALL, "train", world_hash(), out, max_steps=401)
+    finally:
+        tr.close()
+        sim.close()
+        dev.close()
