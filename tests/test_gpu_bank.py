@@ -224,7 +224,8 @@ def test_bank_evaluate_matches_oracle(tmp_path):
             assert r[col["failure_id"]] == lv["failure_id"] and r[col["split"]] == "train"
             assert r[col["checkpoint_sha256"]] == pkg.sha256_file(ck) and r[col["bank_sha256"]] == bank.bank_sha256
             assert r[col["physics_invalid"]] == "not_instrumented" and int(r[col["max_steps"]]) == steps
-            assert json.loads(r[col["witness_route_json"]]) == pytest.approx(lv["witness_route"].tolist())
+            route = np.array(json.loads(r[col["witness_route_json"]]), np.float32)
+            assert np.array_equal(route, lv["witness_route"])  # 9 significant digits round-trip float32
         ocfg = L.default_config(n=12, family=0, mode=17, seed=levels[0]["seed"], eval=1, speed=1.5,
                                 distance=levels[0]["distance"], max_steps=steps, wind=0.0,
                                 velocity_contract=int(cfg["velocity_contract"]), geometry_memory=0)
