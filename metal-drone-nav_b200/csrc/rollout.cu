@@ -20,9 +20,8 @@ namespace mdn {
 
 // Camera tables in global memory, read through the L1: lanes index them with
 // different pixels, which the constant cache would serialise.
-__device__ float g_pixel_ray[kPixels * 3];  // nav_sensor_pixel_ray(1, 0.75, k), sensor_profile.hpp:89-91
-__device__ float g_pool_ray[80 * 3];        // nav_ray(row, col, 0.75), guidance.hpp:22-26
-#define c_pixel_ray_at(i) __ldg(&g_pixel_ray[(i)])
+__device__ float4 g_pixel_ray[kPixels];  // nav_sensor_pixel_ray(1, 0.75, k) as (x, y, z, 0), sensor_profile.hpp:89-91
+__device__ float g_pool_ray[80 * 3];      // nav_ray(row, col, 0.75), guidance.hpp:22-26
 #define c_pool_ray_at(i) __ldg(&g_pool_ray[(i)])
 
 // ------------------------------------------------------------------ reset
@@ -51,13 +50,14 @@ __global__ void k_world_mirror(SimArgs a) {
 constexpr int kSenseWarps = 8;
 
 struct WarpScene {
+    // Obstacles that can be seen this step, compacted and packed for 128-bit
+    // loads in the ray loop: cull = (centre relative to the camera, inflated
+    // bounding radius), cull2 = (squared distance, radius squared, kind bits),
+    // geom = (centre, size x), geom2 = (size y, size z).
+    float4 cull[16], cull2[16], geom[16], geom2[16];
     float cx[16], cy[16], cz[16];   // obstacle centres at the step's time
     float sx[16], sy[16], sz[16];   // sizes
     uint32_t kind[16];
-    // obstacles that can be seen this step, compacted: index, centre relative
-    // to the camera, squared distance, inflated bounding radius (and square)
-    int cand[16];
-    float qx[16], qy[16], qz[16], q2[16], rb[16], rb2[16];
     float cur[80], prev[80];        // pooled ranges (metres, obs*12 as the reference re-derives them)
     float risk_term[80];            // guidance.hpp:59-66 contribution of each cell as a neighbour
     float ctx[24];
@@ -184,9 +184,10 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
             const unsigned vis = __ballot_sync(0xffffffffu, visible);
             if (visible) {
                 const int slot = __popc(vis & ((1u << lane) - 1u));
-                ws.cand[slot] = lane;
-                ws.qx[slot] = qx; ws.qy[slot] = qy; ws.qz[slot] = qz;
-                ws.q2[slot] = q2; ws.rb[slot] = rbi; ws.rb2[slot] = rbi * rbi;
+                ws.cull[slot] = make_float4(qx, qy, qz, rbi);
+                ws.cull2[slot] = make_float4(q2, rbi * rbi, __uint_as_float(ws.kind[lane]), 0.0f);
+                ws.geom[slot] = make_float4(ws.cx[lane], ws.cy[lane], ws.cz[lane], ws.sx[lane]);
+                ws.geom2[slot] = make_float4(ws.sy[lane], ws.sz[lane], 0.0f, 0.0f);
             }
             ncand = __popc(vis);
             __syncwarp();
@@ -199,7 +200,8 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
         for (int tile = 0; tile < kPixels / 32; tile++) {
             const int col = (tile % 5) * 4 + (lane & 3), prow = (tile / 5) * 8 + (lane >> 2);
             const int k = prow * 20 + col;
-            const float rx = c_pixel_ray_at(3 * k), ry = c_pixel_ray_at(3 * k + 1), rz = c_pixel_ray_at(3 * k + 2);
+            const float4 pr = __ldg(&g_pixel_ray[k]);
+            const float rx = pr.x, ry = pr.y, rz = pr.z;
             const float dx = r[0] * rx + r[1] * ry + r[2] * rz;
             const float dy = r[3] * rx + r[4] * ry + r[5] * rz;
             const float dz = r[6] * rx + r[7] * ry + r[8] * rz;
@@ -223,19 +225,22 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
                 // Per-ray bounding-sphere test: behind the camera, beyond the
                 // current nearest hit, or passing outside the sphere -> the
                 // exact test could only return a miss or a larger range.
-                const float tc = ws.qx[j] * dx + ws.qy[j] * dy + ws.qz[j] * dz;
-                const float rbj = ws.rb[j];
-                if (tc + rbj < 0.0f || tc - rbj >= best) continue;
-                if (ws.q2[j] - tc * tc > ws.rb2[j]) continue;
-                const int o = ws.cand[j];
-                const uint32_t kind = ws.kind[o];
+                const float4 cu = ws.cull[j];
+                const float tc = cu.x * dx + cu.y * dy + cu.z * dz;
+                if (tc + cu.w < 0.0f || tc - cu.w >= best) continue;
+                const float4 cu2 = ws.cull2[j];
+                if (cu2.x - tc * tc > cu2.y) continue;
+                const uint32_t kind = __float_as_uint(cu2.z);
+                const float4 g = ws.geom[j];
                 float t = 1000.0f;
-                if (kind == 0)
-                    t = ray_box(ox, oy, oz, dx, dy, dz, ws.cx[o], ws.cy[o], ws.cz[o], ws.sx[o], ws.sy[o], ws.sz[o]);
-                else if (kind == 1 || kind == 3)
-                    t = ray_sphere(ox, oy, oz, dx, dy, dz, ws.cx[o], ws.cy[o], ws.cz[o], ws.sx[o]);
-                else if (kind == 2)
-                    t = ray_cylinder(ox, oy, oz, dx, dy, dz, ws.cx[o], ws.cy[o], ws.cz[o], ws.sx[o], ws.sz[o]);
+                if (kind == 0) {
+                    const float4 g2 = ws.geom2[j];
+                    t = ray_box(ox, oy, oz, dx, dy, dz, g.x, g.y, g.z, g.w, g2.x, g2.y);
+                } else if (kind == 1 || kind == 3) {
+                    t = ray_sphere(ox, oy, oz, dx, dy, dz, g.x, g.y, g.z, g.w);
+                } else if (kind == 2) {
+                    t = ray_cylinder(ox, oy, oz, dx, dy, dz, g.x, g.y, g.z, g.w, ws.geom2[j].y);
+                }
                 best = fminf(best, t);
             }
             float depth = fmaxf(0.0f, best);
@@ -1293,7 +1298,10 @@ static cudaError_t launch_advance(const SimArgs& a, const StepPlan& plan, cudaSt
 static inline unsigned blocks_for(uint32_t n, int per_block) { return (n + per_block - 1) / per_block; }
 
 cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays) {
-    cudaError_t e = cudaMemcpyToSymbol(g_pixel_ray, pixel_rays, sizeof(float) * kPixels * 3);
+    float4 rays[kPixels];
+    for (int k = 0; k < kPixels; k++)
+        rays[k] = make_float4(pixel_rays[3 * k], pixel_rays[3 * k + 1], pixel_rays[3 * k + 2], 0.0f);
+    cudaError_t e = cudaMemcpyToSymbol(g_pixel_ray, rays, sizeof(rays));
     if (e != cudaSuccess) return e;
     return cudaMemcpyToSymbol(g_pool_ray, pool_rays, sizeof(float) * 80 * 3);
 }
