@@ -22,6 +22,10 @@ namespace mdn {
 // different pixels, which the constant cache would serialise.
 __device__ float4 g_pixel_ray[kPixels];  // nav_sensor_pixel_ray(1, 0.75, k) as (x, y, z, 0), sensor_profile.hpp:89-91
 __device__ float g_pool_ray[80 * 3];      // nav_ray(row, col, 0.75), guidance.hpp:22-26
+// Cone around each 4x8 pixel tile's rays (camera frame): unit axis and the
+// cosine / sine of a half-angle that covers all 32 rays with a margin.
+__device__ float4 g_tile_cone[kPixels / 32];  // (axis, cos)
+__device__ float g_tile_sin[kPixels / 32];
 #define c_pool_ray_at(i) __ldg(&g_pool_ray[(i)])
 
 // ------------------------------------------------------------------ reset
@@ -55,6 +59,7 @@ struct WarpScene {
     // bounding radius), cull2 = (squared distance, radius squared, kind bits),
     // geom = (centre, size x), geom2 = (size y, size z).
     float4 cull[16], cull2[16], geom[16], geom2[16];
+    uint32_t tile_mask[kPixels / 32];  // candidates that can reach each pixel tile
     float cx[16], cy[16], cz[16];   // obstacle centres at the step's time
     float sx[16], sy[16], sz[16];   // sizes
     uint32_t kind[16];
@@ -117,7 +122,7 @@ __device__ __forceinline__ float cell_risk(const WarpScene& ws, int row, int col
     return risk;
 }
 
-__global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
+__global__ void __launch_bounds__(kSenseWarps * 32, 4) k_sense(SimArgs a) {
     __shared__ WarpScene scenes[kSenseWarps];
     const int lane = threadIdx.x & 31;
     const int wid = threadIdx.x >> 5;
@@ -192,6 +197,45 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
             ncand = __popc(vis);
             __syncwarp();
         }
+        // Tile cull: lanes 0-15 test candidate `lane` against tile u, lanes
+        // 16-31 candidate `lane - 16` against tile u + 5. A candidate is kept
+        // for a tile when its bounding sphere may meet the tile's ray cone:
+        // the camera is inside the sphere, or the angle between the cone axis
+        // and the centre is at most the cone half-angle plus the sphere's
+        // angular radius (with 1 mm per metre of slack). A dropped candidate
+        // cannot lower any of the tile's ranges, so they stay bit-identical.
+        {
+            const int jc = lane & 15;
+            const bool live = jc < ncand;
+            float4 cu = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float qn = 0.0f, sb = 0.0f, cb = 1.0f;
+            bool inside = false;
+            if (live) {
+                cu = ws.cull[jc];
+                const float q2 = ws.cull2[jc].x;
+                inside = q2 <= cu.w * cu.w;
+                qn = sqrtf(q2);
+                sb = inside ? 1.0f : cu.w / qn;
+                cb = sqrtf(fmaxf(0.0f, 1.0f - sb * sb));
+            }
+#pragma unroll
+            for (int u = 0; u < kPixels / 64; u++) {
+                const int t = u + (lane >> 4) * (kPixels / 64);
+                const float4 cone = __ldg(&g_tile_cone[t]);
+                const float sa = __ldg(&g_tile_sin[t]);
+                const float ax = r[0] * cone.x + r[1] * cone.y + r[2] * cone.z;
+                const float ay = r[3] * cone.x + r[4] * cone.y + r[5] * cone.z;
+                const float az = r[6] * cone.x + r[7] * cone.y + r[8] * cone.z;
+                const float qa = cu.x * ax + cu.y * ay + cu.z * az;
+                const bool keep = live && (inside || qa >= qn * (cone.w * cb - sa * sb) - 1e-3f * qn);
+                const unsigned b = __ballot_sync(0xffffffffu, keep);
+                if (lane == 0) {
+                    ws.tile_mask[u] = b & 0xffffu;
+                    ws.tile_mask[u + kPixels / 64] = b >> 16;
+                }
+            }
+            __syncwarp();
+        }
         const float rp[3] = {ox - a.room_c[0], oy - a.room_c[1], oz - a.room_c[2]};
         const float re[3] = {a.room_e[0], a.room_e[1], a.room_e[2]};
         const bool inside_room = fabsf(rp[0]) < re[0] && fabsf(rp[1]) < re[1] && fabsf(rp[2]) < re[2];
@@ -221,7 +265,8 @@ __global__ void __launch_bounds__(kSenseWarps * 32) k_sense(SimArgs a) {
                 best = fminf(best, ray_box(ox, oy, oz, dx, dy, dz, a.room_c[0], a.room_c[1], a.room_c[2], a.room_e[0],
                                            a.room_e[1], a.room_e[2]));
             }
-            for (int j = 0; j < ncand; j++) {
+            for (unsigned m = ws.tile_mask[tile]; m; m &= m - 1) {
+                const int j = __ffs(m) - 1;
                 // Per-ray bounding-sphere test: behind the camera, beyond the
                 // current nearest hit, or passing outside the sphere -> the
                 // exact test could only return a miss or a larger range.
@@ -1302,6 +1347,37 @@ cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays
     for (int k = 0; k < kPixels; k++)
         rays[k] = make_float4(pixel_rays[3 * k], pixel_rays[3 * k + 1], pixel_rays[3 * k + 2], 0.0f);
     cudaError_t e = cudaMemcpyToSymbol(g_pixel_ray, rays, sizeof(rays));
+    if (e != cudaSuccess) return e;
+    // Tile cones, in double: axis = normalised sum of the tile's rays,
+    // half-angle = the widest ray's angle + 3 mrad; cosine rounded down and
+    // sine rounded up so the float test only errs towards keeping.
+    float4 cones[kPixels / 32];
+    float sines[kPixels / 32];
+    for (int t = 0; t < kPixels / 32; t++) {
+        double axis[3] = {0.0, 0.0, 0.0};
+        int ks[32];
+        for (int l = 0; l < 32; l++) {
+            const int col = (t % 5) * 4 + (l & 3), prow = (t / 5) * 8 + (l >> 2);
+            ks[l] = prow * 20 + col;
+            for (int j = 0; j < 3; j++) axis[j] += pixel_rays[3 * ks[l] + j];
+        }
+        const double norm = std::sqrt(axis[0] * axis[0] + axis[1] * axis[1] + axis[2] * axis[2]);
+        for (int j = 0; j < 3; j++) axis[j] /= norm;
+        double widest = 0.0;
+        for (int l = 0; l < 32; l++) {
+            const float* ray = pixel_rays + 3 * ks[l];
+            const double rn = std::sqrt(double(ray[0]) * ray[0] + double(ray[1]) * ray[1] + double(ray[2]) * ray[2]);
+            const double dot = (axis[0] * ray[0] + axis[1] * ray[1] + axis[2] * ray[2]) / rn;
+            widest = std::max(widest, std::acos(std::min(1.0, dot)));
+        }
+        const double half = widest + 3e-3;
+        cones[t] = make_float4(float(axis[0]), float(axis[1]), float(axis[2]),
+                               std::nextafter(float(std::cos(half)), -1.0f));
+        sines[t] = std::nextafter(float(std::sin(half)), 2.0f);
+    }
+    e = cudaMemcpyToSymbol(g_tile_cone, cones, sizeof(cones));
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpyToSymbol(g_tile_sin, sines, sizeof(sines));
     if (e != cudaSuccess) return e;
     return cudaMemcpyToSymbol(g_pool_ray, pool_rays, sizeof(float) * 80 * 3);
 }
