@@ -708,6 +708,208 @@ __device__ __forceinline__ float overhead_scale(const float* ob) {
     return 0.25f + 0.75f * (overhead / 20.0f);
 }
 
+// The rest of sim_act for env i at `row` once its actor mean and critic value
+// are known (sim.metal:229-271): mode blends, sampling, log-prob, command ring
+// and delay, desired velocity and yaw. `ob` is the env's observation row.
+__device__ __noinline__ void act_finish(const SimArgs& a, uint32_t i, size_t row, const float* ob,
+                                        const float* mean_in, float value, const float* log_std) {
+    const mdn_sim_config& c = a.cfg;
+    mdn_sim_run& run = a.runs[i];
+    a.values[row] = value;
+    const float* prior = ob + kActorObs - 3;
+    const uint32_t mode = c.mode;
+    float mean[4] = {mean_in[0], mean_in[1], mean_in[2], mean_in[3]};
+    // Geometry-prior blends of the evaluation modes 9-21 (sim.metal:233).
+    if (mode >= 9u && mode <= 21u) {
+        float scale = (mode == 9u || mode == 13u) ? 0.0f
+                    : ((mode == 10u || mode == 14u || mode == 16u) ? 0.25f : (mode == 15u ? 1.0f : 0.5f));
+        if (mode >= 17u) scale = overhead_scale(ob);
+        if (mode == 12u) {
+            float near_ = 12.0f;
+            for (int k = 0; k < 80; k++) near_ = smin(near_, ob[k] * 12.0f);
+            scale = clampf((near_ - 0.3f) / 2.0f, 0.2f, 1.0f);
+        }
+        for (int j = 0; j < 3; j++) mean[j] = prior[j] + scale * (mean[j] - prior[j]);
+        mean[3] *= scale;
+        if (mode == 16u) {
+            const float yaw = atan2f(ob[161], ob[160]);
+            const float x = clampf(yaw * 1.5f, -0.85f, 0.85f);
+            mean[3] += 0.5f * logf((1.0f + x) / (1.0f - x));  // nav_atanh, guidance.hpp:35
+        }
+    }
+    // Mode 22 trains the deployed mode-17 action map (sim.metal:235-256).
+    const float deployed = mode == 22u ? overhead_scale(ob) : 1.0f;
+    uint32_t rng = run.rng;
+    const uint32_t steps = run.steps;
+    float act[4];
+    float* cmd = a.commands + size_t(i) * kFrames * kActions;
+    for (int j = 0; j < 4; j++) {
+        act[j] = mean[j] + ((mode == 0u || mode == 22u) ? expf(log_std[j]) * sim_normal(rng) : 0.0f);
+        if (mode == 1u) act[j] = sim_normal(rng);
+        a.actions[row * kActions + j] = act[j];
+        float executed = act[j];
+        if (mode == 22u) executed = j < 3 ? prior[j] + deployed * (act[j] - prior[j]) : deployed * act[j];
+        cmd[(steps % kFrames) * kActions + j] = tanhf(executed);
+    }
+    float lp = 0.0f;  // gaussian_log_prob, ppo.hpp:95-103
+    for (int j = 0; j < 4; j++) {
+        const float inv_std = expf(-log_std[j]);
+        const float d = (act[j] - mean[j]) * inv_std;
+        lp += -0.5f * (d * d + 2.0f * log_std[j] + kLogTwoPi);
+    }
+    a.logp[row] = lp;
+    run.rng = rng;
+    const mdn_physics_state& st = a.states[i];
+    const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2],
+                        st.orientation_wxyz[3]};
+    float r[9];
+    rotation(q, r);
+    if (mode == 2u || mode == 3u || mode == 20u) {  // scripted goal pursuit, sim.metal:257-263
+        const mdn_world& w = a.worlds[i];
+        float d[3] = {w.goal[0] - st.position[0], w.goal[1] - st.position[1], w.goal[2] - st.position[2]};
+        const float len = len3(d[0], d[1], d[2]);
+        const float inv = 1.0f / len, keep = smin(len, c.speed);
+        for (int j = 0; j < 3; j++) d[j] = d[j] * inv * keep;
+        float* slot = cmd + (steps % kFrames) * kActions;
+        slot[0] = (r[0] * d[0] + r[3] * d[1] + r[6] * d[2]) / c.speed;
+        slot[1] = (r[1] * d[0] + r[4] * d[1] + r[7] * d[2]) / c.speed;
+        slot[2] = (r[2] * d[0] + r[5] * d[1] + r[8] * d[2]) / c.speed;
+        slot[3] = 0.0f;
+    }
+    const uint32_t gid = a.env_base + i;
+    const uint32_t delay = clean_env(c, gid) ? 0u : c.command_delay;
+    const uint32_t applied = steps > delay ? steps - delay : 0;
+    float pn[4];
+    for (int j = 0; j < 4; j++) {
+        pn[j] = steps < delay ? 0.0f : cmd[(applied % kFrames) * kActions + j];
+        run.previous_nav[j] = pn[j];
+    }
+    float v[3] = {pn[0] * c.speed, pn[1] * c.speed, pn[2] * c.speed * (c.velocity_contract == 0 ? 0.5f : 1.0f)};
+    if (c.velocity_contract == 1) {
+        const float scale = smin(1.0f, c.speed / smax(len3(v[0], v[1], v[2]), 1e-8f));
+        for (int j = 0; j < 3; j++) v[j] *= scale;
+    }
+    if (mode == 19u) {  // fixed-speed command, sim.metal:269
+        const float magnitude = len3(v[0], v[1], v[2]);
+        if (magnitude > 1e-8f) {
+            const float scale = c.speed / magnitude;
+            for (int j = 0; j < 3; j++) v[j] *= scale;
+        }
+    }
+    for (int j = 0; j < 3; j++) run.desired_velocity[j] = r[j * 3] * v[0] + r[j * 3 + 1] * v[1] + r[j * 3 + 2] * v[2];
+    run.yaw += pn[3] * a.physics->dt * float(c.substeps) * 0.5f;
+}
+
+// The 64-unit actor and the critic with one thread per environment: W1 is
+// held k-major in shared memory, so the warp reads one broadcast 128-bit word
+// per 4 hidden units and every thread keeps its environment's 64
+// pre-activations in registers (4 FMAs per shared load). Pre-activations are
+// the same in-order fmaf chains from zero as k_act's, then the bias; the heads
+// sum the hidden units in order (cpu_reference.hpp:437-458).
+constexpr int kRowThreads = 256;
+constexpr int kRowSmemFloats = kActorObs * kHidden + kCriticObs * kHidden + kHidden + kActions * kHidden + kHidden +
+                               kHidden + 4 + 4 + 4;
+
+__global__ void __launch_bounds__(kRowThreads, 2) k_act_rows(SimArgs a) {
+    extern __shared__ float4 smem4[];
+    float* w1t = reinterpret_cast<float*>(smem4);  // [184][64]: w1t[k * 64 + h] = W1[h][k]
+    float* cw1t = w1t + kActorObs * kHidden;       // [32][64]
+    float* b1 = cw1t + kCriticObs * kHidden;       // [64]
+    float* w2 = b1 + kHidden;                      // [4][64]
+    float* cb1 = w2 + kActions * kHidden;          // [64]
+    float* cw2 = cb1 + kHidden;                    // [64]
+    float* b2 = cw2 + kHidden;                     // [4]
+    float* log_std = b2 + 4;                       // [4]
+    float* cb2 = log_std + 4;                      // [1]
+    const int tid = threadIdx.x;
+    for (int k = tid; k < kActorObs * kHidden; k += blockDim.x) {
+        const int h = k % kHidden, col = k / kHidden;
+        w1t[k] = a.actor[h * kActorObs + col];
+    }
+    for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
+        const int h = k % kHidden, col = k / kHidden;
+        cw1t[k] = a.critic[h * kCriticObs + col];
+    }
+    for (int k = tid; k < kHidden; k += blockDim.x) {
+        b1[k] = a.actor[kActorB1 + k];
+        cb1[k] = a.critic[kCriticB1 + k];
+        cw2[k] = a.critic[kCriticW2 + k];
+    }
+    for (int k = tid; k < kActions * kHidden; k += blockDim.x) w2[k] = a.actor[kActorW2 + k];
+    if (tid < kActions) {
+        b2[tid] = a.actor[a.actor_b2 + tid];
+        log_std[tid] = a.actor[a.actor_log_std + tid];
+    }
+    if (tid == 0) cb2[0] = a.critic[kCriticB2];
+    __syncthreads();
+    const mdn_sim_config& c = a.cfg;
+    for (uint32_t i = blockIdx.x * blockDim.x + tid; i < a.n; i += gridDim.x * blockDim.x) {
+        if (c.eval && a.runs[i].episodes) continue;
+        const size_t row = size_t(a.tick) * a.n + i;
+        const float* ob = a.obs + row * kActorObs;
+        float z[kHidden];
+#pragma unroll
+        for (int h = 0; h < kHidden; h++) z[h] = 0.0f;
+        const float4* ob4 = reinterpret_cast<const float4*>(ob);
+#pragma unroll 1
+        for (int k4 = 0; k4 < kActorObs / 4; k4++) {
+            const float4 o4 = __ldg(ob4 + k4);
+            const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                const float4* wr = reinterpret_cast<const float4*>(w1t + (k4 * 4 + kk) * kHidden);
+#pragma unroll
+                for (int h4 = 0; h4 < kHidden / 4; h4++) {
+                    const float4 w = wr[h4];
+                    z[4 * h4] = fmaf(ov[kk], w.x, z[4 * h4]);
+                    z[4 * h4 + 1] = fmaf(ov[kk], w.y, z[4 * h4 + 1]);
+                    z[4 * h4 + 2] = fmaf(ov[kk], w.z, z[4 * h4 + 2]);
+                    z[4 * h4 + 3] = fmaf(ov[kk], w.w, z[4 * h4 + 3]);
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < kHidden; h++) z[h] = tanhf(z[h] + b1[h]);
+        float mean[4];
+#pragma unroll
+        for (int j = 0; j < kActions; j++) {
+            float m = 0.0f;
+#pragma unroll
+            for (int h = 0; h < kHidden; h++) m = fmaf(z[h], w2[j * kHidden + h], m);
+            mean[j] = m + b2[j];
+        }
+        const float4 pr = make_float4(__ldg(ob + kActorObs - 3), __ldg(ob + kActorObs - 2), __ldg(ob + kActorObs - 1), 0.0f);
+        mean[0] += pr.x;  // geometry prior, ppo.hpp:77
+        mean[1] += pr.y;
+        mean[2] += pr.z;
+        const float4* co4 = reinterpret_cast<const float4*>(a.co + row * kCriticObs);
+#pragma unroll
+        for (int h = 0; h < kHidden; h++) z[h] = 0.0f;
+#pragma unroll 1
+        for (int k4 = 0; k4 < kCriticObs / 4; k4++) {
+            const float4 o4 = __ldg(co4 + k4);
+            const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                const float4* wr = reinterpret_cast<const float4*>(cw1t + (k4 * 4 + kk) * kHidden);
+#pragma unroll
+                for (int h4 = 0; h4 < kHidden / 4; h4++) {
+                    const float4 w = wr[h4];
+                    z[4 * h4] = fmaf(ov[kk], w.x, z[4 * h4]);
+                    z[4 * h4 + 1] = fmaf(ov[kk], w.y, z[4 * h4 + 1]);
+                    z[4 * h4 + 2] = fmaf(ov[kk], w.z, z[4 * h4 + 2]);
+                    z[4 * h4 + 3] = fmaf(ov[kk], w.w, z[4 * h4 + 3]);
+                }
+            }
+        }
+        float value = 0.0f;
+#pragma unroll
+        for (int h = 0; h < kHidden; h++) value = fmaf(tanhf(z[h] + cb1[h]), cw2[h], value);
+        value += cb2[0];
+        act_finish(a, i, row, ob, mean, value, log_std);
+    }
+}
+
 // kWide: the actor mean comes from the tensor-core forward's slice sums.
 template <bool kWide>
 __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
@@ -834,96 +1036,8 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
         }
         __syncwarp();
         const uint32_t i = base + uint32_t(lane);
-        if (lane < envs) {
-            mdn_sim_run& run = a.runs[i];
-            if (!(c.eval && run.episodes)) {
-                const size_t row = row0 + lane;
-                a.values[row] = value_mine;
-                const float* ob = my_obs + lane * kActorObs;
-                const float* prior = ob + kActorObs - 3;
-                const uint32_t mode = c.mode;
-                float mean[4] = {mean_mine[0], mean_mine[1], mean_mine[2], mean_mine[3]};
-                // Geometry-prior blends of the evaluation modes 9-21 (sim.metal:233).
-                if (mode >= 9u && mode <= 21u) {
-                    float scale = (mode == 9u || mode == 13u) ? 0.0f
-                                : ((mode == 10u || mode == 14u || mode == 16u) ? 0.25f : (mode == 15u ? 1.0f : 0.5f));
-                    if (mode >= 17u) scale = overhead_scale(ob);
-                    if (mode == 12u) {
-                        float near_ = 12.0f;
-                        for (int k = 0; k < 80; k++) near_ = smin(near_, ob[k] * 12.0f);
-                        scale = clampf((near_ - 0.3f) / 2.0f, 0.2f, 1.0f);
-                    }
-                    for (int j = 0; j < 3; j++) mean[j] = prior[j] + scale * (mean[j] - prior[j]);
-                    mean[3] *= scale;
-                    if (mode == 16u) {
-                        const float yaw = atan2f(ob[161], ob[160]);
-                        const float x = clampf(yaw * 1.5f, -0.85f, 0.85f);
-                        mean[3] += 0.5f * logf((1.0f + x) / (1.0f - x));  // nav_atanh, guidance.hpp:35
-                    }
-                }
-                // Mode 22 trains the deployed mode-17 action map (sim.metal:235-256).
-                const float deployed = mode == 22u ? overhead_scale(ob) : 1.0f;
-                uint32_t rng = run.rng;
-                const uint32_t steps = run.steps;
-                float act[4];
-                float* cmd = a.commands + size_t(i) * kFrames * kActions;
-                for (int j = 0; j < 4; j++) {
-                    act[j] = mean[j] + ((mode == 0u || mode == 22u) ? expf(log_std[j]) * sim_normal(rng) : 0.0f);
-                    if (mode == 1u) act[j] = sim_normal(rng);
-                    a.actions[row * kActions + j] = act[j];
-                    float executed = act[j];
-                    if (mode == 22u) executed = j < 3 ? prior[j] + deployed * (act[j] - prior[j]) : deployed * act[j];
-                    cmd[(steps % kFrames) * kActions + j] = tanhf(executed);
-                }
-                float lp = 0.0f;  // gaussian_log_prob, ppo.hpp:95-103
-                for (int j = 0; j < 4; j++) {
-                    const float inv_std = expf(-log_std[j]);
-                    const float d = (act[j] - mean[j]) * inv_std;
-                    lp += -0.5f * (d * d + 2.0f * log_std[j] + kLogTwoPi);
-                }
-                a.logp[row] = lp;
-                run.rng = rng;
-                const mdn_physics_state& st = a.states[i];
-                const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2],
-                                    st.orientation_wxyz[3]};
-                float r[9];
-                rotation(q, r);
-                if (mode == 2u || mode == 3u || mode == 20u) {  // scripted goal pursuit, sim.metal:257-263
-                    const mdn_world& w = a.worlds[i];
-                    float d[3] = {w.goal[0] - st.position[0], w.goal[1] - st.position[1], w.goal[2] - st.position[2]};
-                    const float len = len3(d[0], d[1], d[2]);
-                    const float inv = 1.0f / len, keep = smin(len, c.speed);
-                    for (int j = 0; j < 3; j++) d[j] = d[j] * inv * keep;
-                    float* slot = cmd + (steps % kFrames) * kActions;
-                    slot[0] = (r[0] * d[0] + r[3] * d[1] + r[6] * d[2]) / c.speed;
-                    slot[1] = (r[1] * d[0] + r[4] * d[1] + r[7] * d[2]) / c.speed;
-                    slot[2] = (r[2] * d[0] + r[5] * d[1] + r[8] * d[2]) / c.speed;
-                    slot[3] = 0.0f;
-                }
-                const uint32_t gid = a.env_base + i;
-                const uint32_t delay = clean_env(c, gid) ? 0u : c.command_delay;
-                const uint32_t applied = steps > delay ? steps - delay : 0;
-                float pn[4];
-                for (int j = 0; j < 4; j++) {
-                    pn[j] = steps < delay ? 0.0f : cmd[(applied % kFrames) * kActions + j];
-                    run.previous_nav[j] = pn[j];
-                }
-                float v[3] = {pn[0] * c.speed, pn[1] * c.speed, pn[2] * c.speed * (c.velocity_contract == 0 ? 0.5f : 1.0f)};
-                if (c.velocity_contract == 1) {
-                    const float scale = smin(1.0f, c.speed / smax(len3(v[0], v[1], v[2]), 1e-8f));
-                    for (int j = 0; j < 3; j++) v[j] *= scale;
-                }
-                if (mode == 19u) {  // fixed-speed command, sim.metal:269
-                    const float magnitude = len3(v[0], v[1], v[2]);
-                    if (magnitude > 1e-8f) {
-                        const float scale = c.speed / magnitude;
-                        for (int j = 0; j < 3; j++) v[j] *= scale;
-                    }
-                }
-                for (int j = 0; j < 3; j++) run.desired_velocity[j] = r[j * 3] * v[0] + r[j * 3 + 1] * v[1] + r[j * 3 + 2] * v[2];
-                run.yaw += pn[3] * a.physics->dt * float(c.substeps) * 0.5f;
-            }
-        }
+        if (lane < envs && !(c.eval && a.runs[i].episodes))
+            act_finish(a, i, row0 + lane, my_obs + lane * kActorObs, mean_mine, value_mine, log_std);
         __syncwarp();
     }
 }
@@ -1393,12 +1507,13 @@ cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s) {
 }
 
 size_t act_smem_bytes() { return sizeof(float) * kActSmemFloats; }
+static size_t act_rows_smem_bytes() { return sizeof(float) * kRowSmemFloats; }
 
 static void launch_act(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
     if (a.wide_slices)
         k_act<true><<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
     else
-        k_act<false><<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
+        k_act_rows<<<plan.act_rows_grid, kRowThreads, act_rows_smem_bytes(), s>>>(a);
 }
 
 // The wide actor's tensor-core forward over this tick's observation rows.
@@ -1443,6 +1558,7 @@ cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStr
 StepPlan plan_step(uint32_t n, int sm_count, int group_override) {
     StepPlan p{};
     p.act_grid = int(std::min<size_t>((size_t(n) + 31) / 32, size_t(sm_count) * 2));
+    p.act_rows_grid = int(std::min<size_t>((size_t(n) + kRowThreads - 1) / kRowThreads, size_t(sm_count) * 2));
     int g = size_t(n) <= size_t(sm_count) * 128 ? 2 : 1;
     if (group_override == 1 || group_override == 2) g = group_override;
     p.advance_group = g;
@@ -1498,7 +1614,10 @@ cudaError_t fp32_peak(int sm_count, double* tflops) {
 int kernels_per_step(const mdn_sim_config& c, bool wide) { return 3 + (c.geometry_memory ? 1 : 0) + (wide ? 1 : 0); }
 
 cudaError_t configure_kernels() {
-    cudaError_t e = cudaFuncSetAttribute(k_act<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
+    cudaError_t e = cudaFuncSetAttribute(k_act_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(act_rows_smem_bytes()));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_act<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_act<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
     if (e != cudaSuccess) return e;
