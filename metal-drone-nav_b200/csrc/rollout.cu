@@ -1263,6 +1263,8 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
             float refp[3] = {run.reference_position[0], run.reference_position[1], run.reference_position[2]};
             const float dv_[3] = {run.desired_velocity[0], run.desired_velocity[1], run.desired_velocity[2]};
             float path = run.path, elapsed = run.elapsed, min_clear = run.min_clearance, peak = run.peak_speed;
+            float clear_now = 0.0f;
+            bool clear_valid = false;
             for (uint32_t step = 0; step < c.substeps; step++) {
                 float mo[22];
                 for (int j = 0; j < 3; j++) refp[j] += dv_[j] * params.dt;
@@ -1301,6 +1303,8 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                 elapsed += params.dt;
                 int32_t id;
                 const float clearance = world_clearance_soa(a, i, s, elapsed, &id);
+                clear_now = clearance;  // the clearance at (s, elapsed) from here on
+                clear_valid = true;
                 if (clearance < step_clearance) contact = id;
                 step_clearance = smin(step_clearance, clearance);
                 min_clear = smin(min_clear, clearance);
@@ -1328,7 +1332,9 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                     co[j + 16] = (refp[j] - s[j]) * 2.0f;
                 }
                 for (int j = 0; j < 4; j++) co[9 + j] = s[3 + j];
-                co[19] = world_clearance_soa(a, i, s, elapsed, nullptr) / 5.0f;
+                // wclearance of the final pose: the last substep's value unless
+                // the first substep already stopped on an invalid state.
+                co[19] = (clear_valid ? clear_now : world_clearance_soa(a, i, s, elapsed, nullptr)) / 5.0f;
                 co[20] = float(steps) / 200.0f;
                 for (int j = 21; j < 30; j++) co[j] = 0.0f;
                 const uint32_t m = count < 3u ? count : 3u;
