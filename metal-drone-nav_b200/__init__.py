@@ -11,8 +11,8 @@ import subprocess
 
 from . import layouts  # noqa: F401
 from .capi import (ChallengeBank, ChallengeSampler, Device, MdnError, PPOTrainer, Sim, challenge_settings,  # noqa: F401
-                   checkpoint_inspect, default_raptor, evaluate_bank, lib, runtime_config, sha256_file,
-                   task_control, task_settings, write_policy)
+                   checkpoint_inspect, default_raptor, evaluate_bank, gather_rollout_evidence, lib, runtime_config,
+                   sha256_file, task_control, task_settings, write_policy)
 
 PACKAGE_DIR = pathlib.Path(__file__).resolve().parent
 

@@ -592,3 +592,27 @@ def evaluate_bank(device, checkpoint, bank_path, split, world_sha256, output_csv
     out = {k: score[k].item() if score[k].ndim == 0 else score[k].tolist() for k in layouts.BANK_SCORE.names}
     out["success_rate"] = out["successes"] / out["episodes"] if out["episodes"] else 0.0
     return out
+
+
+def gather_rollout_evidence(raw_gae, terminated, truncated, transition_ids):
+    """Under several ranks (torch.distributed initialised, environments sharded
+    evenly and in rank order), assemble every rank's [T][n_local] rollout
+    evidence into the [T][n_total] arrays that ChallengeSampler.observe_raw_gae
+    takes, on every rank, so that all ranks keep identical sampler state."""
+    import torch
+    import torch.distributed as dist
+    device = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend() == "nccl" \
+        else torch.device("cpu")
+    out = []
+    for array, dtype in ((raw_gae, np.float32), (terminated, np.uint8), (truncated, np.uint8),
+                         (transition_ids, np.uint32)):
+        a = np.ascontiguousarray(array, dtype)
+        if a.ndim != 2:
+            raise MdnError(ERR["INVALID"], "rollout evidence must be [horizon][local environments]")
+        wire = a.view(np.int32) if a.dtype == np.uint32 else a.astype(np.int32) if a.dtype == np.uint8 else a
+        local = torch.from_numpy(np.ascontiguousarray(wire)).to(device)
+        parts = [torch.empty_like(local) for _ in range(dist.get_world_size())]
+        dist.all_gather(parts, local)
+        full = np.concatenate([p.cpu().numpy() for p in parts], axis=1)
+        out.append(full.view(np.uint32) if dtype == np.uint32 else full.astype(dtype))
+    return tuple(out)

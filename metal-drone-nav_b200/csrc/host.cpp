@@ -245,6 +245,8 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
                                                            : nullptr;
     a.runtime = runtime;
     a.env_physics = static_cast<mdn_physics_params*>(buf[MDN_BUF_ENV_PHYSICS]);
+    a.reset_list = reset_mem;
+    a.reset_count = reset_mem ? reset_mem + n : nullptr;
     return a;
 }
 
@@ -375,9 +377,13 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
             }
         }
         {
-            const cudaError_t e = cudaMalloc(&sim->world_soa, n * kWorldSoaWords * sizeof(float));
+            cudaError_t e = cudaMalloc(&sim->world_soa, n * kWorldSoaWords * sizeof(float));
+            if (e == cudaSuccess) e = cudaMalloc(&sim->reset_mem, (n + 32) * sizeof(uint32_t));
+            if (e == cudaSuccess) e = cudaMemset(sim->reset_mem, 0, (n + 32) * sizeof(uint32_t));
             if (e != cudaSuccess) {
                 for (int k = 0; k < MDN_BUF_COUNT; k++) cudaFree(sim->buf[k]);
+                cudaFree(sim->world_soa);
+                cudaFree(sim->reset_mem);
                 throw Error(MDN_ERR_NOMEM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
             }
         }
@@ -388,6 +394,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
             if (e != cudaSuccess) {
                 for (int k = 0; k < MDN_BUF_COUNT; k++) cudaFree(sim->buf[k]);
                 cudaFree(sim->world_soa);
+                cudaFree(sim->reset_mem);
                 cudaFree(sim->wide_partials);
                 throw Error(MDN_ERR_NOMEM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
             }
@@ -452,6 +459,7 @@ extern "C" int mdn_sim_destroy(mdn_sim* sim) {
         sim->release_graphs();
         for (int id = 0; id < MDN_BUF_COUNT; id++) cudaFree(sim->buf[id]);
         cudaFree(sim->world_soa);
+        cudaFree(sim->reset_mem);
         cudaFree(sim->wide_partials);
         cudaFree(sim->wide_error);
         delete sim->wide;

@@ -84,6 +84,7 @@ struct mdn_sim {
     cudaStream_t stream = nullptr;
     void* buf[MDN_BUF_COUNT] = {};
     float* world_soa = nullptr;  // device mirror of the worlds, structure of arrays
+    uint32_t* reset_mem = nullptr;  // [n] reset list, then its count (k_advance -> k_reset_list)
     uint32_t actor_hidden = mdn::kHidden;                   // 64, or a wide actor (multiple of 256)
     uint32_t actor_params = mdn::actor_param_count(mdn::kHidden);
     float* wide_partials = nullptr;                         // [hidden/128][n][4] slice sums of the wide forward

@@ -35,6 +35,7 @@ struct StepPlan {
     int act_rows_grid = 1;  // persistent k_act_rows CTAs (64-unit actor)
     int advance_group = 1;  // lanes per environment in k_advance (1 or 2)
     int advance_grid = 1;   // k_advance CTAs (grid-stride over environments)
+    int reset_grid = 1;     // k_reset_list CTAs (grid-stride over the step's reset list)
 };
 
 // Everything one launch of a rollout kernel needs (passed by value).
@@ -95,6 +96,10 @@ struct SimArgs {
     // while runtime.enabled, each env's plant lives in env_physics[n].
     mdn_runtime_config runtime;
     mdn_physics_params* env_physics;
+    // Episodes that ended in this step: k_advance appends, k_reset_list
+    // resets them, k_sense of the next step empties the list.
+    uint32_t* reset_list;  // [n]
+    uint32_t* reset_count;
 };
 
 }  // namespace mdn

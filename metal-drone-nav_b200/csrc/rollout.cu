@@ -37,6 +37,34 @@ __global__ void k_reset(SimArgs a, int first) {
     refill_rings(a, (blockIdx.x * blockDim.x) + (threadIdx.x & ~31u), mask);
 }
 
+// In-step episode resets (sim.metal:330) of the environments k_advance listed,
+// one thread per listed environment: a warp resets 32 environments side by
+// side instead of each reset holding up its advance warp. Schedule slot tick+1
+// as in the advance; the ranges are then refilled by the whole warp.
+__global__ void __launch_bounds__(128) k_reset_list(SimArgs a) {
+    const uint32_t count = *reinterpret_cast<volatile uint32_t*>(a.reset_count);
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t base = blockIdx.x * blockDim.x; base < count; base += stride) {
+        const uint32_t k = base + threadIdx.x;
+        const bool active = k < count;
+        uint32_t i = 0;
+        if (active) {
+            i = a.reset_list[k];
+            episode_reset(a, i, false, a.tick + 1);
+        }
+        const int lane = threadIdx.x & 31;
+        unsigned mask = __ballot_sync(0xffffffffu, active);
+        const float4 twelve = make_float4(12.0f, 12.0f, 12.0f, 12.0f);
+        while (mask) {
+            const int src = __ffs(mask) - 1;
+            mask &= mask - 1;
+            const uint32_t env = __shfl_sync(0xffffffffu, i, src);
+            float4* ring = reinterpret_cast<float4*>(a.sensors + size_t(env) * kFrames * kPixels);
+            for (int j = lane; j < kFrames * kPixels / 4; j += 32) ring[j] = twelve;
+        }
+    }
+}
+
 // Refresh the structure-of-arrays mirror from the AoS worlds (after an upload
 // or a checkpoint load replaced them).
 __global__ void k_world_mirror(SimArgs a) {
@@ -124,6 +152,7 @@ __device__ __forceinline__ float cell_risk(const WarpScene& ws, int row, int col
 
 __global__ void __launch_bounds__(kSenseWarps * 32, 4) k_sense(SimArgs a) {
     __shared__ WarpScene scenes[kSenseWarps];
+    if (blockIdx.x == 0 && threadIdx.x == 0) *a.reset_count = 0;  // this step's reset list starts empty
     const int lane = threadIdx.x & 31;
     const int wid = threadIdx.x >> 5;
     const uint32_t i = blockIdx.x * kSenseWarps + wid;
@@ -1425,14 +1454,20 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                     run.total_path += path;
                     run.total_elapsed += elapsed;
                     run.final_progress += 1.0f - after / smax(run.initial_distance, 1.0e-4f);
-                    if (!c.eval) refill = episode_reset(a, i, false, a.tick + 1);
+                    refill = !c.eval;  // reset by k_reset_list after this launch
                 }
             }
         }
-        // Range rings of the environments that reset (their leader lanes),
-        // refilled by the whole warp.
+        // Environments whose episode ended (their leader lanes) join the
+        // step's reset list: one atomic per warp, slots in lane order.
         const unsigned m = __ballot_sync(0xffffffffu, refill);
-        if (m) refill_rings_grouped(a, tile + uint32_t((tid & ~31) / G), m, G);
+        if (m) {
+            const int leader = __ffs(m) - 1;
+            uint32_t slot = 0;
+            if (lane == leader) slot = atomicAdd(a.reset_count, uint32_t(__popc(m)));
+            slot = __shfl_sync(0xffffffffu, slot, leader);
+            if (refill) a.reset_list[slot + uint32_t(__popc(m & ((1u << lane) - 1u)))] = i;
+        }
     }
 }
 
@@ -1442,6 +1477,10 @@ static int advance_blocks_per_sm() {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_advance<G, false>, kAdvanceThreads, 0) != cudaSuccess)
         blocks = 1;
     return blocks > 0 ? blocks : 1;
+}
+
+static void launch_reset_list(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
+    k_reset_list<<<plan.reset_grid, 128, 0, s>>>(a);
 }
 
 static cudaError_t launch_advance(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
@@ -1537,7 +1576,10 @@ cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s, 
     cudaError_t e = launch_wide(a, wide, s);
     if (e != cudaSuccess) return e;
     launch_act(a, plan, s);
-    return launch_advance(a, plan, s);
+    e = launch_advance(a, plan, s);
+    if (e != cudaSuccess) return e;
+    launch_reset_list(a, plan, s);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4],
@@ -1552,8 +1594,10 @@ cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStr
     launch_act(a, plan, s);
     cudaEventRecord(ev[2], s);
     const cudaError_t e = launch_advance(a, plan, s);
+    if (e != cudaSuccess) return e;
+    launch_reset_list(a, plan, s);
     cudaEventRecord(ev[3], s);
-    return e;
+    return cudaGetLastError();
 }
 
 // Launch shapes of one policy step for n environments. k_advance takes a lane
@@ -1571,6 +1615,7 @@ StepPlan plan_step(uint32_t n, int sm_count, int group_override) {
     const int per_sm = g == 1 ? advance_blocks_per_sm<1>() : advance_blocks_per_sm<2>();
     const size_t need = (size_t(n) * g + kAdvanceThreads - 1) / kAdvanceThreads;
     p.advance_grid = int(std::max<size_t>(1, std::min<size_t>(need, size_t(sm_count) * per_sm)));
+    p.reset_grid = int(std::max<size_t>(1, std::min<size_t>((size_t(n) + 127) / 128, size_t(sm_count) * 4)));
     return p;
 }
 
@@ -1617,7 +1662,7 @@ cudaError_t fp32_peak(int sm_count, double* tflops) {
     return e;
 }
 
-int kernels_per_step(const mdn_sim_config& c, bool wide) { return 3 + (c.geometry_memory ? 1 : 0) + (wide ? 1 : 0); }
+int kernels_per_step(const mdn_sim_config& c, bool wide) { return 4 + (c.geometry_memory ? 1 : 0) + (wide ? 1 : 0); }
 
 cudaError_t configure_kernels() {
     cudaError_t e = cudaFuncSetAttribute(k_act_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,

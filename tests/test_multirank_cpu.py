@@ -109,3 +109,50 @@ def test_failed_rank_ends_the_job():
         mp.spawn(_failing_worker, args=(2, _free_port()), nprocs=2, join=True)
     assert "rank 1 fails" in str(info.value) or "ProcessRaisedException" in type(info.value).__name__ \
         or "process" in str(info.value).lower()
+
+
+def _bank_worker(rank, world, port):
+    """Challenge-bank sampler state stays identical on every rank when each
+    rank contributes its environments' rollout evidence through
+    gather_rollout_evidence (equal to one process observing all of it)."""
+    _init(rank, world, port)
+    import json
+    pkg = load_package()
+    bank = os.path.join(os.path.dirname(__file__), "golden", "challenge_bank_small.jsonl")
+    h = json.loads(open(bank).readline())["world_source_sha256"]
+    n_total, horizon = 12, 5
+    n = n_total // world
+    mine = pkg.ChallengeSampler(bank, h, environment_count=n_total, horizon=horizon, selection=1,
+                                rehearsal_environments=2)
+    solo = pkg.ChallengeSampler(bank, h, environment_count=n_total, horizon=horizon, selection=1,
+                                rehearsal_environments=2)
+    sched = mine.initial_schedule()
+    assert np.array_equal(sched, solo.initial_schedule())
+    active = sched[:, 0].copy()
+    rng = np.random.default_rng(5)  # the same full evidence on every rank; each rank sends its slice
+    for rollout in range(3):
+        if rollout:
+            sched = mine.next_schedule(active, rollout)
+            assert np.array_equal(sched, solo.next_schedule(active, rollout))
+        ids = np.zeros((horizon, n_total), np.uint32)
+        term = np.zeros((horizon, n_total), np.uint8)
+        for t in range(horizon):
+            for e in range(n_total):
+                ids[t, e] = active[e]
+                if rng.random() < 0.4:
+                    term[t, e] = 1
+                    active[e] = sched[e, t + 1]
+        gae = rng.normal(0, 1, (horizon, n_total)).astype(np.float32)
+        trunc = np.zeros_like(term)
+        cols = slice(rank * n, (rank + 1) * n)
+        full = pkg.gather_rollout_evidence(gae[:, cols], term[:, cols], trunc[:, cols], ids[:, cols])
+        assert all(np.array_equal(a, b) for a, b in zip(full, (gae, term, trunc, ids)))
+        mine.observe_raw_gae(*full, rollout)
+        solo.observe_raw_gae(gae, term, trunc, ids, rollout)
+        for lvl in range(len(mine.bank)):
+            assert mine.level_stats(lvl) == solo.level_stats(lvl)
+    dist.destroy_process_group()
+
+
+def test_bank_sampler_across_ranks():
+    mp.spawn(_bank_worker, args=(2, _free_port()), nprocs=2, join=True)
