@@ -29,39 +29,32 @@ __device__ float g_tile_sin[kPixels / 32];
 #define c_pool_ray_at(i) __ldg(&g_pool_ray[(i)])
 
 // ------------------------------------------------------------------ reset
-__global__ void k_reset(SimArgs a, int first) {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    const bool active = i < a.n;
-    if (active) episode_reset(a, i, first != 0, 0);
-    const unsigned mask = __ballot_sync(0xffffffffu, active);
-    refill_rings(a, (blockIdx.x * blockDim.x) + (threadIdx.x & ~31u), mask);
+// Range ring of environment i refilled with 12 m by the whole warp.
+__device__ __forceinline__ void refill_ring_warp(const SimArgs& a, uint32_t i) {
+    const float4 twelve = make_float4(12.0f, 12.0f, 12.0f, 12.0f);
+    float4* ring = reinterpret_cast<float4*>(a.sensors + size_t(i) * kFrames * kPixels);
+    for (int j = threadIdx.x & 31; j < kFrames * kPixels / 4; j += 32) ring[j] = twelve;
+}
+
+// sim_reset: one warp per environment (episode_reset is warp-cooperative).
+__global__ void __launch_bounds__(128) k_reset(SimArgs a, int first) {
+    const uint32_t i = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (i >= a.n) return;  // warp-uniform
+    episode_reset(a, i, first != 0, 0);
+    refill_ring_warp(a, i);
 }
 
 // In-step episode resets (sim.metal:330) of the environments k_advance listed,
-// one thread per listed environment: a warp resets 32 environments side by
-// side instead of each reset holding up its advance warp. Schedule slot tick+1
-// as in the advance; the ranges are then refilled by the whole warp.
+// one warp per listed environment (episode_reset is warp-cooperative), so a
+// reset neither holds up an advance warp nor runs its generator's checks on
+// one lane. Schedule slot tick + 1 as in the advance.
 __global__ void __launch_bounds__(128) k_reset_list(SimArgs a) {
     const uint32_t count = *reinterpret_cast<volatile uint32_t*>(a.reset_count);
-    const uint32_t stride = gridDim.x * blockDim.x;
-    for (uint32_t base = blockIdx.x * blockDim.x; base < count; base += stride) {
-        const uint32_t k = base + threadIdx.x;
-        const bool active = k < count;
-        uint32_t i = 0;
-        if (active) {
-            i = a.reset_list[k];
-            episode_reset(a, i, false, a.tick + 1);
-        }
-        const int lane = threadIdx.x & 31;
-        unsigned mask = __ballot_sync(0xffffffffu, active);
-        const float4 twelve = make_float4(12.0f, 12.0f, 12.0f, 12.0f);
-        while (mask) {
-            const int src = __ffs(mask) - 1;
-            mask &= mask - 1;
-            const uint32_t env = __shfl_sync(0xffffffffu, i, src);
-            float4* ring = reinterpret_cast<float4*>(a.sensors + size_t(env) * kFrames * kPixels);
-            for (int j = lane; j < kFrames * kPixels / 4; j += 32) ring[j] = twelve;
-        }
+    const uint32_t warps = gridDim.x * (blockDim.x / 32);
+    for (uint32_t k = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); k < count; k += warps) {
+        const uint32_t i = a.reset_list[k];
+        episode_reset(a, i, false, a.tick + 1);
+        refill_ring_warp(a, i);
     }
 }
 
@@ -1547,7 +1540,7 @@ cudaError_t launch_world_mirror(const SimArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s) {
-    k_reset<<<blocks_for(a.n, 128), 128, 0, s>>>(a, first ? 1 : 0);
+    k_reset<<<blocks_for(a.n, 4), 128, 0, s>>>(a, first ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -1615,7 +1608,7 @@ StepPlan plan_step(uint32_t n, int sm_count, int group_override) {
     const int per_sm = g == 1 ? advance_blocks_per_sm<1>() : advance_blocks_per_sm<2>();
     const size_t need = (size_t(n) * g + kAdvanceThreads - 1) / kAdvanceThreads;
     p.advance_grid = int(std::max<size_t>(1, std::min<size_t>(need, size_t(sm_count) * per_sm)));
-    p.reset_grid = int(std::max<size_t>(1, std::min<size_t>((size_t(n) + 127) / 128, size_t(sm_count) * 4)));
+    p.reset_grid = int(std::max<size_t>(1, std::min<size_t>((size_t(n) + 3) / 4, size_t(sm_count) * 8)));
     return p;
 }
 

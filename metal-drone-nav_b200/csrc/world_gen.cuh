@@ -78,9 +78,36 @@ __device__ __forceinline__ void clutter_boxes(mdn_world& w, uint32_t& rng, int b
             }
         }
 }
+// Whether a bounded mover (centre c, unit direction d, amplitude) clears its
+// whole swept segment (17 samples): the static boxes by radius + 0.05 m, the
+// start by radius + 0.5 m and the goal by radius + 0.3 m. Called by a whole
+// converged warp with identical arguments: lane l tests the (sample, box)
+// pairs l, l + 32, ... (the last "box" of a sample stands for the start and
+// goal tests) and the warp ANDs the results, which is the serial answer.
+__device__ __forceinline__ bool mover_clear(const mdn_world& w, uint32_t statics, const float c[3], const float d[3],
+                                            float radius, float amplitude) {
+    const int lane = threadIdx.x & 31;
+    const int per_sample = int(statics) + 1;
+    bool ok = true;
+    for (int q = lane; q < 17 * per_sample; q += 32) {
+        const int k = q / per_sample, o = q % per_sample;
+        const float f = amplitude * (float(k) / 8.0f - 1.0f);
+        const float p[3] = {c[0] + d[0] * f, c[1] + d[1] * f, c[2] + d[2] * f};
+        if (o < int(statics)) {
+            const mdn_obstacle& ob = w.obstacles[o];
+            if (!(box_distance(ob.size, p[0] - ob.center[0], p[1] - ob.center[1], p[2] - ob.center[2]) > radius + 0.05f))
+                ok = false;
+        } else {
+            const float ds = len3(p[0] - 0.0f, p[1] - 0.0f, p[2] - 1.5f);
+            const float dg = len3(p[0] - w.goal[0], p[1] - w.goal[1], p[2] - w.goal[2]);
+            if (!(ds > radius + 0.5f) || !(dg > radius + 0.3f)) ok = false;
+        }
+    }
+    return __all_sync(0xffffffffu, ok);
+}
 // Bounded moving spheres (kind 3, world.hpp:32-41) whose whole swept segment
-// (17 samples) clears the static boxes by radius + 0.05 m, the start by
-// radius + 0.5 m and the goal by radius + 0.3 m (8 tries each, else left out).
+// clears the boxes, start and goal (mover_clear; 8 tries each, else left out).
+// Warp-cooperative: see mover_clear.
 __device__ __forceinline__ void clutter_movers(mdn_world& w, uint32_t& rng, int movers) {
     const uint32_t statics = w.count;
     for (int i = 0; i < movers && w.count < 16; i++)
@@ -94,21 +121,7 @@ __device__ __forceinline__ void clutter_movers(mdn_world& w, uint32_t& rng, int 
             const float norm = sqrtf(ux * ux + uy * uy + uz * uz);
             if (!(norm > 0.1f && norm <= 1.0f)) continue;
             const float d[3] = {ux / norm, uy / norm, uz / norm};
-            bool ok = true;
-            for (int k = 0; k <= 16 && ok; k++) {
-                const float f = amplitude * (float(k) / 8.0f - 1.0f);
-                const float p[3] = {c[0] + d[0] * f, c[1] + d[1] * f, c[2] + d[2] * f};
-                for (uint32_t o = 0; o < statics && ok; o++) {
-                    const mdn_obstacle& ob = w.obstacles[o];
-                    if (!(box_distance(ob.size, p[0] - ob.center[0], p[1] - ob.center[1], p[2] - ob.center[2]) >
-                          radius + 0.05f))
-                        ok = false;
-                }
-                const float ds = len3(p[0] - 0.0f, p[1] - 0.0f, p[2] - 1.5f);
-                const float dg = len3(p[0] - w.goal[0], p[1] - w.goal[1], p[2] - w.goal[2]);
-                if (!(ds > radius + 0.5f) || !(dg > radius + 0.3f)) ok = false;
-            }
-            if (ok) {
+            if (mover_clear(w, statics, c, d, radius, amplitude)) {
                 WorldBuilder{w}.add(3, c[0], c[1], c[2], radius, amplitude, phase, d[0] * speed, d[1] * speed,
                                     d[2] * speed);
                 break;
@@ -363,7 +376,10 @@ __device__ __forceinline__ void mirror_world(const SimArgs& a, uint32_t i) {
 
 // sim_reset_one (sim.metal:55-94) for one environment, except the 8x320 range
 // ring refill, which the caller performs cooperatively (returns true when the
-// ring must be refilled with 12 m).
+// ring must be refilled with 12 m). Run by a whole converged warp for the same
+// environment: every lane computes the same values and stores them (identical
+// stores to one address), and the generators' heavy checks are split over the
+// lanes (mover_clear).
 __device__ bool reset_env(const SimArgs& a, uint32_t i, bool first) {
     const mdn_sim_config& c = a.cfg;
     const uint32_t gid = a.env_base + i;
@@ -473,31 +489,6 @@ __device__ __forceinline__ void apply_challenge_world(const SimArgs& a, uint32_t
         run.previous_nav[0] = 1.0f;
     }
     a.bank_active[i] = level;
-}
-
-// Refill when each environment is served by a group of `g` lanes and `mask`
-// holds the groups' leader lanes: lane l stands for environment first_env + l / g.
-__device__ __forceinline__ void refill_rings_grouped(const SimArgs& a, uint32_t first_env, unsigned mask, int g) {
-    const int lane = threadIdx.x & 31;
-    const float4 twelve = make_float4(12.0f, 12.0f, 12.0f, 12.0f);
-    while (mask) {
-        const int src = __ffs(mask) - 1;
-        mask &= mask - 1;
-        float4* ring = reinterpret_cast<float4*>(a.sensors + size_t(first_env + uint32_t(src / g)) * kFrames * kPixels);
-        for (int j = lane; j < kFrames * kPixels / 4; j += 32) ring[j] = twelve;
-    }
-}
-
-// Warp-cooperative refill of the range rings of the lanes in `mask` with 12 m.
-__device__ __forceinline__ void refill_rings(const SimArgs& a, uint32_t base_env, unsigned mask) {
-    const int lane = threadIdx.x & 31;
-    const float4 twelve = make_float4(12.0f, 12.0f, 12.0f, 12.0f);
-    while (mask) {
-        const int src = __ffs(mask) - 1;
-        mask &= mask - 1;
-        float4* ring = reinterpret_cast<float4*>(a.sensors + size_t(base_env + src) * kFrames * kPixels);
-        for (int j = lane; j < kFrames * kPixels / 4; j += 32) ring[j] = twelve;
-    }
 }
 
 }  // namespace mdn
