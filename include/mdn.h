@@ -359,6 +359,11 @@ int mdn_launch_counts(mdn_sim* sim, mdn_ppo* ppo, uint32_t* per_policy_step, uin
 /* Measured dense FP32 FMA throughput of this device (TFLOP/s), a pure-FMA
  * kernel over every SM: the denominator of the CUDA-core roofline. */
 int mdn_device_fp32_peak(mdn_device* dev, double* tflops);
+/* Self-test of the depth kernel's divide-free quotient (a * RN(1/d) with two
+ * fused residual corrections) against IEEE division over `samples` random
+ * operand pairs of the ray tests' ranges; *mismatches counts differing bit
+ * patterns (0 expected). */
+int mdn_selftest_division(mdn_device* dev, uint64_t samples, uint64_t seed, uint64_t* mismatches);
 
 /* ---- trainer: PPOTrainer (main.mm:1110-1476) ----------------------------- */
 /* PPOTrainer(Sim&, epochs) main.mm:1159-1208; epochs 1..4; minibatch_rows 0 =

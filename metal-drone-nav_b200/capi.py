@@ -68,6 +68,7 @@ SIGNATURES = {
     "mdn_sim_export_policy": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_float]),
     "mdn_sim_set_contact_audit": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_float]),
     "mdn_device_fp32_peak": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_double)]),
+    "mdn_selftest_division": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
     "mdn_ppo_create": (ctypes.c_int, [_P, _U, _U, ctypes.POINTER(_P)]),
     "mdn_ppo_destroy": (ctypes.c_int, [_P]),
     "mdn_ppo_rollout_update": (ctypes.c_int, [_P, _U]),
@@ -188,6 +189,12 @@ class Device:
         v = ctypes.c_double()
         check(lib().mdn_device_fp32_peak(self.h, ctypes.byref(v)))
         return v.value
+
+    def selftest_division(self, samples, seed=1):
+        """Mismatches of the depth kernel's divide-free quotient vs IEEE division."""
+        out = ctypes.c_uint64()
+        check(lib().mdn_selftest_division(self.h, samples, seed, ctypes.byref(out)))
+        return out.value
 
     def comm_init(self, rank, world, unique_id):
         buf = np.frombuffer(bytes(unique_id), np.uint8).copy()

@@ -737,6 +737,14 @@ extern "C" int mdn_sim_profile_step(mdn_sim* sim, uint32_t tick, float ms[3]) {
     });
 }
 
+extern "C" int mdn_selftest_division(mdn_device* dev, uint64_t samples, uint64_t seed, uint64_t* mismatches) {
+    return guarded([&] {
+        require(dev != nullptr && mismatches != nullptr, MDN_ERR_INVALID, "division self-test: null argument");
+        use_device(dev);
+        cuda_check(division_check(samples, seed, mismatches, dev->sm_count), "division self-test");
+    });
+}
+
 extern "C" int mdn_device_fp32_peak(mdn_device* dev, double* tflops) {
     return guarded([&] {
         require(dev && tflops, MDN_ERR_INVALID, "null argument");

@@ -57,6 +57,7 @@ size_t act_smem_bytes();
 cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4],
                                  const WideStep* wide);
 cudaError_t fp32_peak(int sm_count, double* tflops);
+cudaError_t division_check(uint64_t samples, uint64_t seed, uint64_t* mismatches, int sm_count);
 int kernels_per_step(const mdn_sim_config& c, bool wide);
 
 // read_checkpoint_header (main.mm:993-1000) for PPOFIX1 versions 3..10

@@ -56,6 +56,41 @@ __device__ __forceinline__ void obstacle_center(uint32_t kind, const float* c, c
     out[2] = c[2] + t * v[2];
 }
 
+// a / d rounded to nearest, from y = RN(1/d) and no divide instruction:
+// q0 = a*y, then two residual corrections with fused multiply-adds. Markstein
+// ("Computation of elementary functions on the IBM RISC System/6000 processor",
+// IBM J. Res. Dev. 34(1), 1990) shows that when y is the correctly rounded
+// reciprocal and q is faithful, RN(q + (a - d*q)*y) = RN(a/d), the residual
+// being exact; the first correction makes q0 faithful, the second rounds.
+// Used where d is a ray direction component with |d| >= 1e-8 and |a| is a
+// room-scale distance, so no intermediate overflows or becomes subnormal.
+// mdn_selftest_division compares it with IEEE division on the GPU.
+__device__ __forceinline__ float div_by_rcp(float a, float d, float y) {
+    const float q0 = a * y;
+    const float q1 = fmaf(fmaf(-d, q0, a), y, q0);
+    return fmaf(fmaf(-d, q1, a), y, q1);
+}
+
+// Slab test with the ray's reciprocal direction components (rcp[j] =
+// __frcp_rn(d[j]) where |d[j]| >= 1e-8): ray_box below, bit for bit.
+__device__ __forceinline__ float ray_box_rcp(float px, float py, float pz, const float dd[3], const float rcp[3],
+                                             float cx, float cy, float cz, float ex, float ey, float ez) {
+    float lo = -1e20f, hi = 1e20f;
+    const float pp[3] = {px - cx, py - cy, pz - cz}, ee[3] = {ex, ey, ez};
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        if (fabsf(dd[j]) < 1e-8f) {
+            if (fabsf(pp[j]) > ee[j]) return 1000.0f;
+        } else {
+            const float a = div_by_rcp(-ee[j] - pp[j], dd[j], rcp[j]), b = div_by_rcp(ee[j] - pp[j], dd[j], rcp[j]);
+            lo = fmaxf(lo, fminf(a, b));
+            hi = fminf(hi, fmaxf(a, b));
+        }
+    }
+    if (hi < fmaxf(lo, 0.0f)) return 1000.0f;
+    return lo >= 0 ? lo : hi;
+}
+
 // Slab test, world.hpp:48-57 (same operation order; IEEE division).
 __device__ __forceinline__ float ray_box(float px, float py, float pz, float dx, float dy, float dz, float cx, float cy,
                                          float cz, float ex, float ey, float ez) {

@@ -271,6 +271,10 @@ __global__ void __launch_bounds__(kSenseWarps * 32, 4) k_sense(SimArgs a) {
             const float dx = r[0] * rx + r[1] * ry + r[2] * rz;
             const float dy = r[3] * rx + r[4] * ry + r[5] * rz;
             const float dz = r[6] * rx + r[7] * ry + r[8] * rz;
+            const float dd[3] = {dx, dy, dz};
+            float rcp[3];
+#pragma unroll
+            for (int j = 0; j < 3; j++) rcp[j] = fabsf(dd[j]) < 1e-8f ? 0.0f : __frcp_rn(dd[j]);
             float best = 12.0f;
             if (inside_room) {
                 // Origin strictly inside the room box: on every axis the two slab
@@ -278,14 +282,14 @@ __global__ void __launch_bounds__(kSenseWarps * 32, 4) k_sense(SimArgs a) {
                 // hi = min over axes of the non-negative one. Computing only that
                 // division gives the same float as world.hpp:48-57.
                 float hi = 1e20f;
-                const float dd[3] = {dx, dy, dz};
 #pragma unroll
                 for (int j = 0; j < 3; j++)
-                    if (!(fabsf(dd[j]) < 1e-8f)) hi = fminf(hi, ((dd[j] > 0.0f ? re[j] : -re[j]) - rp[j]) / dd[j]);
+                    if (!(fabsf(dd[j]) < 1e-8f))
+                        hi = fminf(hi, div_by_rcp((dd[j] > 0.0f ? re[j] : -re[j]) - rp[j], dd[j], rcp[j]));
                 best = fminf(best, hi);
             } else {
-                best = fminf(best, ray_box(ox, oy, oz, dx, dy, dz, a.room_c[0], a.room_c[1], a.room_c[2], a.room_e[0],
-                                           a.room_e[1], a.room_e[2]));
+                best = fminf(best, ray_box_rcp(ox, oy, oz, dd, rcp, a.room_c[0], a.room_c[1], a.room_c[2],
+                                               a.room_e[0], a.room_e[1], a.room_e[2]));
             }
             for (unsigned m = ws.tile_mask[tile]; m; m &= m - 1) {
                 const int j = __ffs(m) - 1;
@@ -302,7 +306,7 @@ __global__ void __launch_bounds__(kSenseWarps * 32, 4) k_sense(SimArgs a) {
                 float t = 1000.0f;
                 if (kind == 0) {
                     const float4 g2 = ws.geom2[j];
-                    t = ray_box(ox, oy, oz, dx, dy, dz, g.x, g.y, g.z, g.w, g2.x, g2.y);
+                    t = ray_box_rcp(ox, oy, oz, dd, rcp, g.x, g.y, g.z, g.w, g2.x, g2.y);
                 } else if (kind == 1 || kind == 3) {
                     t = ray_sphere(ox, oy, oz, dx, dy, dz, g.x, g.y, g.z, g.w);
                 } else if (kind == 2) {
@@ -1610,6 +1614,47 @@ StepPlan plan_step(uint32_t n, int sm_count, int group_override) {
     p.advance_grid = int(std::max<size_t>(1, std::min<size_t>(need, size_t(sm_count) * per_sm)));
     p.reset_grid = int(std::max<size_t>(1, std::min<size_t>((size_t(n) + 3) / 4, size_t(sm_count) * 8)));
     return p;
+}
+
+// div_by_rcp against IEEE division on the ray tests' operand ranges: a is 0
+// or of magnitude 2^-24..2^6, d of magnitude 2^-26..2^0 (random signs and
+// mantissas from a per-thread hash); counts the mismatched bit patterns.
+__global__ void k_division_check(uint64_t samples, uint64_t seed, unsigned long long* mismatches) {
+    unsigned long long local = 0;
+    for (uint64_t k = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; k < samples;
+         k += uint64_t(gridDim.x) * blockDim.x) {
+        uint64_t h = (k + 1) * 0x9e3779b97f4a7c15ull ^ seed;
+        h ^= h >> 31;
+        h *= 0xbf58476d1ce4e5b9ull;
+        h ^= h >> 27;
+        h *= 0x94d049bb133111ebull;
+        h ^= h >> 31;
+        const uint32_t u = uint32_t(h), v = uint32_t(h >> 32);
+        const uint32_t ea = 127u - 24u + (u >> 24) % 31u, ed = 127u - 26u + (v >> 24) % 27u;
+        float a = __uint_as_float((u & 0x80000000u) | (ea << 23) | (u & 0x7fffffu));
+        const float d = __uint_as_float((v & 0x80000000u) | (ed << 23) | (v & 0x7fffffu));
+        if ((u & 0xff000000u) == 0u) a = 0.0f;
+        if (!(fabsf(d) >= 1e-8f)) continue;
+        const float q = div_by_rcp(a, d, __frcp_rn(d));
+        if (__float_as_uint(q) != __float_as_uint(a / d)) local++;
+    }
+    if (local) atomicAdd(mismatches, local);
+}
+
+cudaError_t division_check(uint64_t samples, uint64_t seed, uint64_t* mismatches, int sm_count) {
+    unsigned long long* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, sizeof(*d));
+    if (e != cudaSuccess) return e;
+    e = cudaMemset(d, 0, sizeof(*d));
+    if (e == cudaSuccess) {
+        k_division_check<<<sm_count * 8, 256>>>(samples, seed, d);
+        e = cudaGetLastError();
+    }
+    unsigned long long h = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&h, d, sizeof(h), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    *mismatches = h;
+    return e;
 }
 
 // Pure FP32 FMA stream: 8 independent chains per thread, `iters` rounds.
