@@ -440,9 +440,11 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         cuda_check(cudaMemsetAsync(sim->buf[MDN_BUF_BANK_ACTIVE_IDS], 0xff, b[MDN_BUF_BANK_ACTIVE_IDS], sim->stream),
                    "clear bank ids");
         // Launch shapes; MDN_ADVANCE_GROUP (1 or 2) overrides the advance
-        // kernel's lanes per environment, for tuning.
+        // kernel's lanes per environment and MDN_ACT_THREADS (1 or 4) the
+        // actor's threads per environment, for tuning.
         const char* group_env = std::getenv("MDN_ADVANCE_GROUP");
-        sim->plan = plan_step(n, dev->sm_count, group_env ? std::atoi(group_env) : 0);
+        const char* act_env = std::getenv("MDN_ACT_THREADS");
+        sim->plan = plan_step(n, dev->sm_count, group_env ? std::atoi(group_env) : 0, act_env ? std::atoi(act_env) : 0);
         mdn_domain_stress_range(&sim->runtime.domain_range);  // runtime config off (main.mm:532)
         cuda_check(launch_reset(sim->args(0), true, sim->stream), "reset");
         cuda_check(cudaStreamSynchronize(sim->stream), "mdn_sim_create");

@@ -51,7 +51,7 @@ cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays
 cudaError_t configure_kernels();
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s);
 cudaError_t launch_world_mirror(const SimArgs& a, cudaStream_t s);
-StepPlan plan_step(uint32_t n, int sm_count, int group_override);
+StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_override);
 cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s, const WideStep* wide);
 size_t act_smem_bytes();
 cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4],

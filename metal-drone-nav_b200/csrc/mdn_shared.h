@@ -32,7 +32,8 @@ constexpr uint32_t actor_param_count(uint32_t h) { return h * kActorObs + h + kA
 // Launch shapes of one policy step (rollout.cu plan_step).
 struct StepPlan {
     int act_grid = 1;       // persistent k_act CTAs (wide actor)
-    int act_rows_grid = 1;  // persistent k_act_rows CTAs (64-unit actor)
+    int act_rows_grid = 1;  // persistent k_act_rows / k_act_quads CTAs (64-unit actor)
+    int act_quads = 0;      // 1: four threads per environment (small shards)
     int advance_group = 1;  // lanes per environment in k_advance (1 or 2)
     int advance_grid = 1;   // k_advance CTAs (grid-stride over environments)
     int reset_grid = 1;     // k_reset_list CTAs (grid-stride over the step's reset list)

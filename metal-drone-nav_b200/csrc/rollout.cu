@@ -836,38 +836,54 @@ constexpr int kRowThreads = 256;
 constexpr int kRowSmemFloats = kActorObs * kHidden + kCriticObs * kHidden + kHidden + kActions * kHidden + kHidden +
                                kHidden + 4 + 4 + 4;
 
-__global__ void __launch_bounds__(kRowThreads, 2) k_act_rows(SimArgs a) {
-    extern __shared__ float4 smem4[];
-    float* w1t = reinterpret_cast<float*>(smem4);  // [184][64]: w1t[k * 64 + h] = W1[h][k]
-    float* cw1t = w1t + kActorObs * kHidden;       // [32][64]
-    float* b1 = cw1t + kCriticObs * kHidden;       // [64]
-    float* w2 = b1 + kHidden;                      // [4][64]
-    float* cb1 = w2 + kActions * kHidden;          // [64]
-    float* cw2 = cb1 + kHidden;                    // [64]
-    float* b2 = cw2 + kHidden;                     // [4]
-    float* log_std = b2 + 4;                       // [4]
-    float* cb2 = log_std + 4;                      // [1]
+// The 64-unit actor's and the critic's weights in shared memory, W1 k-major
+// (w1t[k * 64 + h] = W1[h][k]) so that a thread reads 4 hidden units' weights
+// of one input in one 128-bit word.
+struct ActSmem {
+    float *w1t, *cw1t, *b1, *w2, *cb1, *cw2, *b2, *log_std, *cb2;
+};
+__device__ __forceinline__ ActSmem act_weights_fill(const SimArgs& a, float* base) {
+    ActSmem m;
+    m.w1t = base;                              // [184][64]
+    m.cw1t = m.w1t + kActorObs * kHidden;      // [32][64]
+    m.b1 = m.cw1t + kCriticObs * kHidden;      // [64]
+    m.w2 = m.b1 + kHidden;                     // [4][64]
+    m.cb1 = m.w2 + kActions * kHidden;         // [64]
+    m.cw2 = m.cb1 + kHidden;                   // [64]
+    m.b2 = m.cw2 + kHidden;                    // [4]
+    m.log_std = m.b2 + 4;                      // [4]
+    m.cb2 = m.log_std + 4;                     // [1]
     const int tid = threadIdx.x;
     for (int k = tid; k < kActorObs * kHidden; k += blockDim.x) {
         const int h = k % kHidden, col = k / kHidden;
-        w1t[k] = a.actor[h * kActorObs + col];
+        m.w1t[k] = a.actor[h * kActorObs + col];
     }
     for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
         const int h = k % kHidden, col = k / kHidden;
-        cw1t[k] = a.critic[h * kCriticObs + col];
+        m.cw1t[k] = a.critic[h * kCriticObs + col];
     }
     for (int k = tid; k < kHidden; k += blockDim.x) {
-        b1[k] = a.actor[kActorB1 + k];
-        cb1[k] = a.critic[kCriticB1 + k];
-        cw2[k] = a.critic[kCriticW2 + k];
+        m.b1[k] = a.actor[kActorB1 + k];
+        m.cb1[k] = a.critic[kCriticB1 + k];
+        m.cw2[k] = a.critic[kCriticW2 + k];
     }
-    for (int k = tid; k < kActions * kHidden; k += blockDim.x) w2[k] = a.actor[kActorW2 + k];
+    for (int k = tid; k < kActions * kHidden; k += blockDim.x) m.w2[k] = a.actor[kActorW2 + k];
     if (tid < kActions) {
-        b2[tid] = a.actor[a.actor_b2 + tid];
-        log_std[tid] = a.actor[a.actor_log_std + tid];
+        m.b2[tid] = a.actor[a.actor_b2 + tid];
+        m.log_std[tid] = a.actor[a.actor_log_std + tid];
     }
-    if (tid == 0) cb2[0] = a.critic[kCriticB2];
+    if (tid == 0) m.cb2[0] = a.critic[kCriticB2];
     __syncthreads();
+    return m;
+}
+
+
+__global__ void __launch_bounds__(kRowThreads, 2) k_act_rows(SimArgs a) {
+    extern __shared__ float4 smem4[];
+    const ActSmem m = act_weights_fill(a, reinterpret_cast<float*>(smem4));
+    const float *w1t = m.w1t, *cw1t = m.cw1t, *b1 = m.b1, *w2 = m.w2, *cb1 = m.cb1, *cw2 = m.cw2, *b2 = m.b2,
+                *log_std = m.log_std, *cb2 = m.cb2;
+    const int tid = threadIdx.x;
     const mdn_sim_config& c = a.cfg;
     for (uint32_t i = blockIdx.x * blockDim.x + tid; i < a.n; i += gridDim.x * blockDim.x) {
         if (c.eval && a.runs[i].episodes) continue;
@@ -933,6 +949,96 @@ __global__ void __launch_bounds__(kRowThreads, 2) k_act_rows(SimArgs a) {
         for (int h = 0; h < kHidden; h++) value = fmaf(tanhf(z[h] + cb1[h]), cw2[h], value);
         value += cb2[0];
         act_finish(a, i, row, ob, mean, value, log_std);
+    }
+}
+
+// k_act_rows with four threads per environment, for shards too small to
+// fill the GPU with one thread per environment: each thread owns 16 hidden
+// units (same k-major weights), the four partial head sums are combined in a
+// fixed tree, and the first thread of the quad finishes sim_act.
+constexpr int kQuadSplit = 4;
+constexpr int kQuadUnits = kHidden / kQuadSplit;
+
+__device__ __forceinline__ float quad_sum(float v) {  // ((t0 + t1) + (t2 + t3)) on every lane of the quad
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    return v + __shfl_xor_sync(0xffffffffu, v, 2);
+}
+
+__global__ void __launch_bounds__(kRowThreads) k_act_quads(SimArgs a) {
+    extern __shared__ float4 smem4[];
+    const ActSmem m = act_weights_fill(a, reinterpret_cast<float*>(smem4));
+    const float *w1t = m.w1t, *cw1t = m.cw1t, *b1 = m.b1, *w2 = m.w2, *cb1 = m.cb1, *cw2 = m.cw2, *b2 = m.b2,
+                *log_std = m.log_std, *cb2 = m.cb2;
+    const int tid = threadIdx.x;
+    const mdn_sim_config& c = a.cfg;
+    const int part = tid % kQuadSplit, h0 = part * kQuadUnits;
+    const uint32_t per_block = kRowThreads / kQuadSplit;
+    // Every lane of a quad runs the loop the same number of times (the
+    // shuffles need the whole quad); `live` masks the tail.
+    for (uint32_t base = blockIdx.x * per_block; base < a.n; base += gridDim.x * per_block) {
+        const uint32_t i = base + uint32_t(tid / kQuadSplit);
+        const bool live = i < a.n && !(c.eval && a.runs[i].episodes);
+        const size_t row = size_t(a.tick) * a.n + (live ? i : 0);
+        const float* ob = a.obs + row * kActorObs;
+        float z[kQuadUnits];
+#pragma unroll
+        for (int h = 0; h < kQuadUnits; h++) z[h] = 0.0f;
+        const float4* ob4 = reinterpret_cast<const float4*>(ob);
+#pragma unroll 2
+        for (int k4 = 0; k4 < kActorObs / 4; k4++) {
+            const float4 o4 = __ldg(ob4 + k4);
+            const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                const float4* wr = reinterpret_cast<const float4*>(w1t + (k4 * 4 + kk) * kHidden + h0);
+#pragma unroll
+                for (int u4 = 0; u4 < kQuadUnits / 4; u4++) {
+                    const float4 w = wr[u4];
+                    z[4 * u4] = fmaf(ov[kk], w.x, z[4 * u4]);
+                    z[4 * u4 + 1] = fmaf(ov[kk], w.y, z[4 * u4 + 1]);
+                    z[4 * u4 + 2] = fmaf(ov[kk], w.z, z[4 * u4 + 2]);
+                    z[4 * u4 + 3] = fmaf(ov[kk], w.w, z[4 * u4 + 3]);
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < kQuadUnits; h++) z[h] = tanhf(z[h] + b1[h0 + h]);
+        float mean[4];
+#pragma unroll
+        for (int j = 0; j < kActions; j++) {
+            float m = 0.0f;
+#pragma unroll
+            for (int h = 0; h < kQuadUnits; h++) m = fmaf(z[h], w2[j * kHidden + h0 + h], m);
+            mean[j] = quad_sum(m) + b2[j];
+        }
+        mean[0] += __ldg(ob + kActorObs - 3);  // geometry prior, ppo.hpp:77
+        mean[1] += __ldg(ob + kActorObs - 2);
+        mean[2] += __ldg(ob + kActorObs - 1);
+        const float4* co4 = reinterpret_cast<const float4*>(a.co + row * kCriticObs);
+#pragma unroll
+        for (int h = 0; h < kQuadUnits; h++) z[h] = 0.0f;
+#pragma unroll 2
+        for (int k4 = 0; k4 < kCriticObs / 4; k4++) {
+            const float4 o4 = __ldg(co4 + k4);
+            const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                const float4* wr = reinterpret_cast<const float4*>(cw1t + (k4 * 4 + kk) * kHidden + h0);
+#pragma unroll
+                for (int u4 = 0; u4 < kQuadUnits / 4; u4++) {
+                    const float4 w = wr[u4];
+                    z[4 * u4] = fmaf(ov[kk], w.x, z[4 * u4]);
+                    z[4 * u4 + 1] = fmaf(ov[kk], w.y, z[4 * u4 + 1]);
+                    z[4 * u4 + 2] = fmaf(ov[kk], w.z, z[4 * u4 + 2]);
+                    z[4 * u4 + 3] = fmaf(ov[kk], w.w, z[4 * u4 + 3]);
+                }
+            }
+        }
+        float value = 0.0f;
+#pragma unroll
+        for (int h = 0; h < kQuadUnits; h++) value = fmaf(tanhf(z[h] + cb1[h0 + h]), cw2[h0 + h], value);
+        value = quad_sum(value) + cb2[0];
+        if (live && part == 0) act_finish(a, i, row, ob, mean, value, log_std);
     }
 }
 
@@ -1554,6 +1660,8 @@ static size_t act_rows_smem_bytes() { return sizeof(float) * kRowSmemFloats; }
 static void launch_act(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
     if (a.wide_slices)
         k_act<true><<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
+    else if (plan.act_quads)
+        k_act_quads<<<plan.act_rows_grid, kRowThreads, act_rows_smem_bytes(), s>>>(a);
     else
         k_act_rows<<<plan.act_rows_grid, kRowThreads, act_rows_smem_bytes(), s>>>(a);
 }
@@ -1602,10 +1710,16 @@ cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStr
 // B200: 18,944), where the per-environment chain sets its time (8,192
 // environments: 0.107 vs 0.140 ms per launch), and one lane per environment
 // above that, where occupancy does (65,536: 0.283 vs 0.406 ms).
-StepPlan plan_step(uint32_t n, int sm_count, int group_override) {
+StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_override) {
     StepPlan p{};
     p.act_grid = int(std::min<size_t>((size_t(n) + 31) / 32, size_t(sm_count) * 2));
-    p.act_rows_grid = int(std::min<size_t>((size_t(n) + kRowThreads - 1) / kRowThreads, size_t(sm_count) * 2));
+    // Four threads per environment when one per environment would leave the
+    // SMs with under two warps each (measured: 8,192 envs 0.062 vs 0.073 ms;
+    // 16,384 envs 0.094 vs 0.074 ms).
+    p.act_quads = size_t(n) <= size_t(sm_count) * 64 ? 1 : 0;
+    if (act_override == 1 || act_override == 4) p.act_quads = act_override == 4 ? 1 : 0;
+    const size_t per_block = p.act_quads ? kRowThreads / kQuadSplit : kRowThreads;
+    p.act_rows_grid = int(std::min<size_t>((size_t(n) + per_block - 1) / per_block, size_t(sm_count) * 2));
     int g = size_t(n) <= size_t(sm_count) * 128 ? 2 : 1;
     if (group_override == 1 || group_override == 2) g = group_override;
     p.advance_group = g;
@@ -1705,6 +1819,8 @@ int kernels_per_step(const mdn_sim_config& c, bool wide) { return 4 + (c.geometr
 cudaError_t configure_kernels() {
     cudaError_t e = cudaFuncSetAttribute(k_act_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(act_rows_smem_bytes()));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_act_quads, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_rows_smem_bytes()));
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_act<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
     if (e != cudaSuccess) return e;

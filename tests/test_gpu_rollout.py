@@ -241,3 +241,32 @@ def test_rejects_unsupported_config(pkg, raptor):
         pkg.Sim(pkg_device(), pkg.layouts.default_config(n=8, sensor_delay=7), 4, raptor=raptor)
     with pytest.raises(pkg.MdnError):
         pkg.Sim(pkg_device(), pkg.layouts.default_config(n=0), 4, raptor=raptor)
+
+
+@pytest.mark.parametrize("threads", [1, 4])
+def test_actor_kernels_match_oracle(pkg, om, raptor, threads, monkeypatch):
+    """Both 64-unit actor kernels (one thread per environment, and four threads
+    per environment for small shards; MDN_ACT_THREADS picks one at simulator
+    creation) against the oracle, teacher-forced."""
+    monkeypatch.setenv("MDN_ACT_THREADS", str(threads))
+    n, T = 320, 6
+    cfg = pkg.layouts.default_config(n=n, family=18, speed=1.0, distance=3.0, seed=13, sensor_delay=2,
+                                     command_delay=2, mode=17)
+    gpu, ora = make_pair(pkg, om, raptor, cfg, T)
+    try:
+        for t in range(T):
+            for name in STATE_KEYS:
+                gpu.upload(name, ora.buf(name))
+            gpu.step(t)
+            ora.step(t)
+            rows = slice(t * n, (t + 1) * n)
+            for name in ("actions", "logp", "values"):
+                g = gpu.download(name).reshape(T * n, -1)[rows]
+                o = ora.buf(name).reshape(T * n, -1)[rows]
+                close(g, o, f"t={t} {name}", atol=1e-4 if name == "logp" else ATOL)
+            close(gpu.download("commands"), ora.buf("commands"), f"t={t} commands")
+            rs_g, rs_o = gpu.download("runs"), ora.buf("runs")
+            assert np.array_equal(rs_g["rng"], rs_o["rng"]), f"t={t} rng"
+            close(rs_g["desired_velocity"], rs_o["desired_velocity"], f"t={t} desired velocity")
+    finally:
+        gpu.close()
