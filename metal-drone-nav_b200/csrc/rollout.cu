@@ -1589,6 +1589,10 @@ static void launch_reset_list(const SimArgs& a, const StepPlan& plan, cudaStream
 static cudaError_t launch_advance(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
     const bool own = a.runtime.enabled != 0;
     switch (plan.advance_group) {
+        case 4:
+            if (own) k_advance<4, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
+            else k_advance<4, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
+            break;
         case 2:
             if (own) k_advance<2, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
             else k_advance<2, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
@@ -1705,11 +1709,10 @@ cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStr
     return cudaGetLastError();
 }
 
-// Launch shapes of one policy step for n environments. k_advance takes a lane
-// pair per environment for shards of at most 128 environments per SM (on a
-// B200: 18,944), where the per-environment chain sets its time (8,192
-// environments: 0.107 vs 0.140 ms per launch), and one lane per environment
-// above that, where occupancy does (65,536: 0.283 vs 0.406 ms).
+// Launch shapes of one policy step for n environments. On small shards the
+// per-environment chain of k_advance sets its time, so the RAPTOR units and the
+// bootstrap critic are split over 2 or 4 lanes; on large ones occupancy does,
+// and one lane per environment is fastest (65,536: 0.283 vs 0.406 ms with 2).
 StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_override) {
     StepPlan p{};
     p.act_grid = int(std::min<size_t>((size_t(n) + 31) / 32, size_t(sm_count) * 2));
@@ -1720,10 +1723,13 @@ StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_overrid
     if (act_override == 1 || act_override == 4) p.act_quads = act_override == 4 ? 1 : 0;
     const size_t per_block = p.act_quads ? kRowThreads / kQuadSplit : kRowThreads;
     p.act_rows_grid = int(std::min<size_t>((size_t(n) + per_block - 1) / per_block, size_t(sm_count) * 2));
-    int g = size_t(n) <= size_t(sm_count) * 128 ? 2 : 1;
-    if (group_override == 1 || group_override == 2) g = group_override;
+    // Lanes per environment for k_advance: 4 on shards of at most 64
+    // environments per SM (8,192 envs: 0.151 vs 0.164 ms with 2), 2 up to 128
+    // (16,384: 0.179 vs 0.244 ms with 4), else 1.
+    int g = size_t(n) <= size_t(sm_count) * 64 ? 4 : (size_t(n) <= size_t(sm_count) * 128 ? 2 : 1);
+    if (group_override == 1 || group_override == 2 || group_override == 4) g = group_override;
     p.advance_group = g;
-    const int per_sm = g == 1 ? advance_blocks_per_sm<1>() : advance_blocks_per_sm<2>();
+    const int per_sm = g == 1 ? advance_blocks_per_sm<1>() : (g == 2 ? advance_blocks_per_sm<2>() : advance_blocks_per_sm<4>());
     const size_t need = (size_t(n) * g + kAdvanceThreads - 1) / kAdvanceThreads;
     p.advance_grid = int(std::max<size_t>(1, std::min<size_t>(need, size_t(sm_count) * per_sm)));
     p.reset_grid = int(std::max<size_t>(1, std::min<size_t>((size_t(n) + 3) / 4, size_t(sm_count) * 8)));

@@ -270,3 +270,42 @@ def test_actor_kernels_match_oracle(pkg, om, raptor, threads, monkeypatch):
             close(rs_g["desired_velocity"], rs_o["desired_velocity"], f"t={t} desired velocity")
     finally:
         gpu.close()
+
+
+GROUP_CASES = [dict(family=18, sensor_delay=2, command_delay=2), dict(family=12, depth_noise=0.05, wind=0.3),
+               dict(family=13, max_steps=5, risk_coef=0.5)]
+
+
+@pytest.mark.parametrize("group", [1, 2, 4])
+@pytest.mark.parametrize("case", range(len(GROUP_CASES)))
+def test_advance_lane_groups_match_oracle(pkg, om, raptor, group, case, monkeypatch):
+    """k_advance with 1, 2 and 4 lanes per environment (plan_step picks by shard
+    size; MDN_ADVANCE_GROUP forces one) against the oracle, teacher-forced, with
+    episode ends and resets inside the window."""
+    monkeypatch.setenv("MDN_ADVANCE_GROUP", str(group))
+    n, T = 256, 8
+    cfg = pkg.layouts.default_config(**{**dict(n=n, speed=1.0, distance=3.0, seed=31 + case, max_steps=6),
+                                        **GROUP_CASES[case]})
+    gpu, ora = make_pair(pkg, om, raptor, cfg, T)
+    movers = 1e-4 if int(cfg["family"]) in (18, 20) else 0.0
+    try:
+        for t in range(T):
+            for name in STATE_KEYS:
+                gpu.upload(name, ora.buf(name))
+            gpu.step(t)
+            ora.step(t)
+            rows = slice(t * n, (t + 1) * n)
+            for name in ("terminated", "truncated", "contact_id"):
+                assert np.array_equal(gpu.download(name)[rows], ora.buf(name)[rows]), f"t={t} {name}"
+            for name in ("rewards", "next_values"):
+                close(gpu.download(name)[rows], ora.buf(name)[rows], f"t={t} {name}")
+            rs_g, rs_o = gpu.download("runs"), ora.buf("runs")
+            for f in ("steps", "episodes", "rng"):
+                assert np.array_equal(rs_g[f], rs_o[f]), f"t={t} runs.{f}"
+            close(floats(gpu.download("states")), floats(ora.buf("states")), f"t={t} states")
+            assert gpu.download("worlds").tobytes() == ora.buf("worlds").tobytes(), f"t={t} worlds"
+            if movers:
+                close(gpu.download("sensors"), ora.buf("sensors"), f"t={t} sensors", grazing=movers)
+        assert ora.buf("runs")["episodes"].sum() > 0
+    finally:
+        gpu.close()
