@@ -826,27 +826,29 @@ __device__ __noinline__ void act_finish(const SimArgs& a, uint32_t i, size_t row
     run.yaw += pn[3] * a.physics->dt * float(c.substeps) * 0.5f;
 }
 
-// The 64-unit actor and the critic with one thread per environment: W1 is
-// held k-major in shared memory, so the warp reads one broadcast 128-bit word
-// per 4 hidden units and every thread keeps its environment's 64
-// pre-activations in registers (4 FMAs per shared load). Pre-activations are
-// the same in-order fmaf chains from zero as k_act's, then the bias; the heads
+// The 64-unit actor and the critic with one thread per environment: every
+// thread keeps its environment's 64 pre-activations in registers and the warp
+// reads one broadcast 128-bit word of W1 (4 inputs of one unit) per 4 FMAs.
+// Pre-activations are in-order fmaf chains from zero, then the bias; the heads
 // sum the hidden units in order (cpu_reference.hpp:437-458).
 constexpr int kRowThreads = 256;
-constexpr int kRowSmemFloats = kActorObs * kHidden + kCriticObs * kHidden + kHidden + kActions * kHidden + kHidden +
+constexpr int kW1Pitch = kActorObs + 4;    // padded W1 rows: 16-byte aligned, rows 1..3 apart on other banks
+constexpr int kCw1Pitch = kCriticObs + 4;
+constexpr int kRowSmemFloats = kHidden * kW1Pitch + kHidden * kCw1Pitch + kHidden + kActions * kHidden + kHidden +
                                kHidden + 4 + 4 + 4;
 
-// The 64-unit actor's and the critic's weights in shared memory, W1 k-major
-// (w1t[k * 64 + h] = W1[h][k]) so that a thread reads 4 hidden units' weights
-// of one input in one 128-bit word.
+// The 64-unit actor's and the critic's weights in shared memory, W1 in its
+// own row-major layout (unit h's inputs at w1[h * kW1Pitch + k]): the fill is
+// a straight, coalesced 128-bit copy, and a thread reads 4 inputs of one unit
+// per 128-bit word (a broadcast when the warp's threads share the unit).
 struct ActSmem {
-    float *w1t, *cw1t, *b1, *w2, *cb1, *cw2, *b2, *log_std, *cb2;
+    float *w1, *cw1, *b1, *w2, *cb1, *cw2, *b2, *log_std, *cb2;
 };
 __device__ __forceinline__ ActSmem act_weights_fill(const SimArgs& a, float* base) {
     ActSmem m;
-    m.w1t = base;                              // [184][64]
-    m.cw1t = m.w1t + kActorObs * kHidden;      // [32][64]
-    m.b1 = m.cw1t + kCriticObs * kHidden;      // [64]
+    m.w1 = base;                               // [64][188]
+    m.cw1 = m.w1 + kHidden * kW1Pitch;         // [64][36]
+    m.b1 = m.cw1 + kHidden * kCw1Pitch;        // [64]
     m.w2 = m.b1 + kHidden;                     // [4][64]
     m.cb1 = m.w2 + kActions * kHidden;         // [64]
     m.cw2 = m.cb1 + kHidden;                   // [64]
@@ -854,13 +856,15 @@ __device__ __forceinline__ ActSmem act_weights_fill(const SimArgs& a, float* bas
     m.log_std = m.b2 + 4;                      // [4]
     m.cb2 = m.log_std + 4;                     // [1]
     const int tid = threadIdx.x;
-    for (int k = tid; k < kActorObs * kHidden; k += blockDim.x) {
-        const int h = k % kHidden, col = k / kHidden;
-        m.w1t[k] = a.actor[h * kActorObs + col];
+    const float4* actor4 = reinterpret_cast<const float4*>(a.actor);
+    const float4* critic4 = reinterpret_cast<const float4*>(a.critic);
+    for (int k = tid; k < kHidden * (kActorObs / 4); k += blockDim.x) {
+        const int h = k / (kActorObs / 4), c4 = k % (kActorObs / 4);
+        *reinterpret_cast<float4*>(m.w1 + h * kW1Pitch + 4 * c4) = __ldg(actor4 + k);
     }
-    for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
-        const int h = k % kHidden, col = k / kHidden;
-        m.cw1t[k] = a.critic[h * kCriticObs + col];
+    for (int k = tid; k < kHidden * (kCriticObs / 4); k += blockDim.x) {
+        const int h = k / (kCriticObs / 4), c4 = k % (kCriticObs / 4);
+        *reinterpret_cast<float4*>(m.cw1 + h * kCw1Pitch + 4 * c4) = __ldg(critic4 + k);
     }
     for (int k = tid; k < kHidden; k += blockDim.x) {
         m.b1[k] = a.actor[kActorB1 + k];
@@ -877,11 +881,10 @@ __device__ __forceinline__ ActSmem act_weights_fill(const SimArgs& a, float* bas
     return m;
 }
 
-
 __global__ void __launch_bounds__(kRowThreads, 2) k_act_rows(SimArgs a) {
     extern __shared__ float4 smem4[];
     const ActSmem m = act_weights_fill(a, reinterpret_cast<float*>(smem4));
-    const float *w1t = m.w1t, *cw1t = m.cw1t, *b1 = m.b1, *w2 = m.w2, *cb1 = m.cb1, *cw2 = m.cw2, *b2 = m.b2,
+    const float *w1 = m.w1, *cw1 = m.cw1, *b1 = m.b1, *w2 = m.w2, *cb1 = m.cb1, *cw2 = m.cw2, *b2 = m.b2,
                 *log_std = m.log_std, *cb2 = m.cb2;
     const int tid = threadIdx.x;
     const mdn_sim_config& c = a.cfg;
@@ -896,18 +899,13 @@ __global__ void __launch_bounds__(kRowThreads, 2) k_act_rows(SimArgs a) {
 #pragma unroll 1
         for (int k4 = 0; k4 < kActorObs / 4; k4++) {
             const float4 o4 = __ldg(ob4 + k4);
-            const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-                const float4* wr = reinterpret_cast<const float4*>(w1t + (k4 * 4 + kk) * kHidden);
-#pragma unroll
-                for (int h4 = 0; h4 < kHidden / 4; h4++) {
-                    const float4 w = wr[h4];
-                    z[4 * h4] = fmaf(ov[kk], w.x, z[4 * h4]);
-                    z[4 * h4 + 1] = fmaf(ov[kk], w.y, z[4 * h4 + 1]);
-                    z[4 * h4 + 2] = fmaf(ov[kk], w.z, z[4 * h4 + 2]);
-                    z[4 * h4 + 3] = fmaf(ov[kk], w.w, z[4 * h4 + 3]);
-                }
+            for (int h = 0; h < kHidden; h++) {  // inputs 4k4..4k4+3 of unit h, in order
+                const float4 w = *reinterpret_cast<const float4*>(w1 + h * kW1Pitch + 4 * k4);
+                z[h] = fmaf(o4.x, w.x, z[h]);
+                z[h] = fmaf(o4.y, w.y, z[h]);
+                z[h] = fmaf(o4.z, w.z, z[h]);
+                z[h] = fmaf(o4.w, w.w, z[h]);
             }
         }
 #pragma unroll
@@ -930,18 +928,13 @@ __global__ void __launch_bounds__(kRowThreads, 2) k_act_rows(SimArgs a) {
 #pragma unroll 1
         for (int k4 = 0; k4 < kCriticObs / 4; k4++) {
             const float4 o4 = __ldg(co4 + k4);
-            const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-                const float4* wr = reinterpret_cast<const float4*>(cw1t + (k4 * 4 + kk) * kHidden);
-#pragma unroll
-                for (int h4 = 0; h4 < kHidden / 4; h4++) {
-                    const float4 w = wr[h4];
-                    z[4 * h4] = fmaf(ov[kk], w.x, z[4 * h4]);
-                    z[4 * h4 + 1] = fmaf(ov[kk], w.y, z[4 * h4 + 1]);
-                    z[4 * h4 + 2] = fmaf(ov[kk], w.z, z[4 * h4 + 2]);
-                    z[4 * h4 + 3] = fmaf(ov[kk], w.w, z[4 * h4 + 3]);
-                }
+            for (int h = 0; h < kHidden; h++) {
+                const float4 w = *reinterpret_cast<const float4*>(cw1 + h * kCw1Pitch + 4 * k4);
+                z[h] = fmaf(o4.x, w.x, z[h]);
+                z[h] = fmaf(o4.y, w.y, z[h]);
+                z[h] = fmaf(o4.z, w.z, z[h]);
+                z[h] = fmaf(o4.w, w.w, z[h]);
             }
         }
         float value = 0.0f;
@@ -953,9 +946,11 @@ __global__ void __launch_bounds__(kRowThreads, 2) k_act_rows(SimArgs a) {
 }
 
 // k_act_rows with four threads per environment, for shards too small to
-// fill the GPU with one thread per environment: each thread owns 16 hidden
-// units (same k-major weights), the four partial head sums are combined in a
-// fixed tree, and the first thread of the quad finishes sim_act.
+// fill the GPU with one thread per environment: thread `part` of a quad owns
+// the 16 hidden units part, part + 4, ... (its four rows of W1 are 1 row
+// apart, so the quad's 128-bit reads fall on different banks), the four
+// partial head sums are combined in a fixed tree, and the first thread of the
+// quad finishes sim_act.
 constexpr int kQuadSplit = 4;
 constexpr int kQuadUnits = kHidden / kQuadSplit;
 
@@ -967,11 +962,11 @@ __device__ __forceinline__ float quad_sum(float v) {  // ((t0 + t1) + (t2 + t3))
 __global__ void __launch_bounds__(kRowThreads) k_act_quads(SimArgs a) {
     extern __shared__ float4 smem4[];
     const ActSmem m = act_weights_fill(a, reinterpret_cast<float*>(smem4));
-    const float *w1t = m.w1t, *cw1t = m.cw1t, *b1 = m.b1, *w2 = m.w2, *cb1 = m.cb1, *cw2 = m.cw2, *b2 = m.b2,
+    const float *w1 = m.w1, *cw1 = m.cw1, *b1 = m.b1, *w2 = m.w2, *cb1 = m.cb1, *cw2 = m.cw2, *b2 = m.b2,
                 *log_std = m.log_std, *cb2 = m.cb2;
     const int tid = threadIdx.x;
     const mdn_sim_config& c = a.cfg;
-    const int part = tid % kQuadSplit, h0 = part * kQuadUnits;
+    const int part = tid % kQuadSplit;  // this thread's units: part, part + 4, ..., part + 60
     const uint32_t per_block = kRowThreads / kQuadSplit;
     // Every lane of a quad runs the loop the same number of times (the
     // shuffles need the whole quad); `live` masks the tail.
@@ -987,28 +982,23 @@ __global__ void __launch_bounds__(kRowThreads) k_act_quads(SimArgs a) {
 #pragma unroll 2
         for (int k4 = 0; k4 < kActorObs / 4; k4++) {
             const float4 o4 = __ldg(ob4 + k4);
-            const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-                const float4* wr = reinterpret_cast<const float4*>(w1t + (k4 * 4 + kk) * kHidden + h0);
-#pragma unroll
-                for (int u4 = 0; u4 < kQuadUnits / 4; u4++) {
-                    const float4 w = wr[u4];
-                    z[4 * u4] = fmaf(ov[kk], w.x, z[4 * u4]);
-                    z[4 * u4 + 1] = fmaf(ov[kk], w.y, z[4 * u4 + 1]);
-                    z[4 * u4 + 2] = fmaf(ov[kk], w.z, z[4 * u4 + 2]);
-                    z[4 * u4 + 3] = fmaf(ov[kk], w.w, z[4 * u4 + 3]);
-                }
+            for (int u = 0; u < kQuadUnits; u++) {  // unit part + 4u
+                const float4 w = *reinterpret_cast<const float4*>(w1 + (part + kQuadSplit * u) * kW1Pitch + 4 * k4);
+                z[u] = fmaf(o4.x, w.x, z[u]);
+                z[u] = fmaf(o4.y, w.y, z[u]);
+                z[u] = fmaf(o4.z, w.z, z[u]);
+                z[u] = fmaf(o4.w, w.w, z[u]);
             }
         }
 #pragma unroll
-        for (int h = 0; h < kQuadUnits; h++) z[h] = tanhf(z[h] + b1[h0 + h]);
+        for (int h = 0; h < kQuadUnits; h++) z[h] = tanhf(z[h] + b1[part + kQuadSplit * h]);
         float mean[4];
 #pragma unroll
         for (int j = 0; j < kActions; j++) {
             float m = 0.0f;
 #pragma unroll
-            for (int h = 0; h < kQuadUnits; h++) m = fmaf(z[h], w2[j * kHidden + h0 + h], m);
+            for (int h = 0; h < kQuadUnits; h++) m = fmaf(z[h], w2[j * kHidden + part + kQuadSplit * h], m);
             mean[j] = quad_sum(m) + b2[j];
         }
         mean[0] += __ldg(ob + kActorObs - 3);  // geometry prior, ppo.hpp:77
@@ -1020,23 +1010,18 @@ __global__ void __launch_bounds__(kRowThreads) k_act_quads(SimArgs a) {
 #pragma unroll 2
         for (int k4 = 0; k4 < kCriticObs / 4; k4++) {
             const float4 o4 = __ldg(co4 + k4);
-            const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-                const float4* wr = reinterpret_cast<const float4*>(cw1t + (k4 * 4 + kk) * kHidden + h0);
-#pragma unroll
-                for (int u4 = 0; u4 < kQuadUnits / 4; u4++) {
-                    const float4 w = wr[u4];
-                    z[4 * u4] = fmaf(ov[kk], w.x, z[4 * u4]);
-                    z[4 * u4 + 1] = fmaf(ov[kk], w.y, z[4 * u4 + 1]);
-                    z[4 * u4 + 2] = fmaf(ov[kk], w.z, z[4 * u4 + 2]);
-                    z[4 * u4 + 3] = fmaf(ov[kk], w.w, z[4 * u4 + 3]);
-                }
+            for (int u = 0; u < kQuadUnits; u++) {
+                const float4 w = *reinterpret_cast<const float4*>(cw1 + (part + kQuadSplit * u) * kCw1Pitch + 4 * k4);
+                z[u] = fmaf(o4.x, w.x, z[u]);
+                z[u] = fmaf(o4.y, w.y, z[u]);
+                z[u] = fmaf(o4.z, w.z, z[u]);
+                z[u] = fmaf(o4.w, w.w, z[u]);
             }
         }
         float value = 0.0f;
 #pragma unroll
-        for (int h = 0; h < kQuadUnits; h++) value = fmaf(tanhf(z[h] + cb1[h0 + h]), cw2[h0 + h], value);
+        for (int h = 0; h < kQuadUnits; h++) value = fmaf(tanhf(z[h] + cb1[part + kQuadSplit * h]), cw2[part + kQuadSplit * h], value);
         value = quad_sum(value) + cb2[0];
         if (live && part == 0) act_finish(a, i, row, ob, mean, value, log_std);
     }
