@@ -425,6 +425,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         mdn_physics_params params;
         if (physics) params = *physics;
         else mdn_physics_crazyflie_default(&params);
+        sim->nominal = params;
         cuda_check(cudaMemcpyAsync(sim->buf[MDN_BUF_ACTOR], actor.data(), b[MDN_BUF_ACTOR], cudaMemcpyHostToDevice,
                                    sim->stream), "upload actor");
         cuda_check(cudaMemcpyAsync(sim->buf[MDN_BUF_CRITIC], critic.data(), b[MDN_BUF_CRITIC], cudaMemcpyHostToDevice,
@@ -506,7 +507,7 @@ extern "C" int mdn_sim_step(mdn_sim* sim, uint32_t tick) {
     return guarded([&] {
         checked(sim);
         require(tick < sim->horizon, MDN_ERR_INVALID, "tick must be below the horizon");
-        cuda_check(launch_step(sim->args(tick), sim->plan, sim->stream, sim->wide), "step");
+        cuda_check(launch_step(sim->args(tick), sim->plan, sim->nominal, sim->stream, sim->wide), "step");
     });
 }
 
@@ -524,7 +525,7 @@ extern "C" int mdn_sim_collect(mdn_sim* sim, uint32_t steps) {
             cuda_check(cudaStreamBeginCapture(sim->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
             cudaError_t launch = cudaSuccess;
             for (uint32_t t = 0; t < steps && launch == cudaSuccess; t++)
-                launch = launch_step(sim->args(t % sim->horizon), sim->plan, sim->stream, sim->wide);
+                launch = launch_step(sim->args(t % sim->horizon), sim->plan, sim->nominal, sim->stream, sim->wide);
             const cudaError_t end = cudaStreamEndCapture(sim->stream, &graph);
             cuda_check(launch, "capture step");
             cuda_check(end, "end capture");
@@ -690,6 +691,10 @@ extern "C" int mdn_sim_upload(mdn_sim* sim, int id, const void* host, size_t off
                                    sim->stream), "upload");
         if (id == MDN_BUF_WORLDS) cuda_check(launch_world_mirror(sim->args(0), sim->stream), "world mirror");
         cuda_check(cudaStreamSynchronize(sim->stream), "upload");
+        if (id == MDN_BUF_PHYSICS) {  // k_advance takes the nominal plant by value
+            std::memcpy(reinterpret_cast<char*>(&sim->nominal) + offset, host, bytes);
+            sim->release_graphs();
+        }
     });
 }
 
@@ -730,7 +735,7 @@ extern "C" int mdn_sim_profile_step(mdn_sim* sim, uint32_t tick, float ms[3]) {
         require(ms != nullptr && tick < sim->horizon, MDN_ERR_INVALID, "profile_step: bad argument");
         cudaEvent_t ev[4];
         for (auto& e : ev) cuda_check(cudaEventCreate(&e), "event");
-        const cudaError_t launch = launch_step_profiled(sim->args(tick), sim->plan, sim->stream, ev, sim->wide);
+        const cudaError_t launch = launch_step_profiled(sim->args(tick), sim->plan, sim->nominal, sim->stream, ev, sim->wide);
         const cudaError_t wait = cudaEventSynchronize(ev[3]);
         for (int k = 0; k < 3 && launch == cudaSuccess && wait == cudaSuccess; k++) cudaEventElapsedTime(&ms[k], ev[k], ev[k + 1]);
         for (auto& e : ev) cudaEventDestroy(e);

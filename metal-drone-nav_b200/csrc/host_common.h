@@ -52,10 +52,11 @@ cudaError_t configure_kernels();
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s);
 cudaError_t launch_world_mirror(const SimArgs& a, cudaStream_t s);
 StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_override);
-cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s, const WideStep* wide);
+cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, const mdn_physics_params& nominal, cudaStream_t s,
+                        const WideStep* wide);
 size_t act_smem_bytes();
-cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4],
-                                 const WideStep* wide);
+cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, const mdn_physics_params& nominal, cudaStream_t s,
+                                 cudaEvent_t ev[4], const WideStep* wide);
 cudaError_t fp32_peak(int sm_count, double* tflops);
 cudaError_t division_check(uint64_t samples, uint64_t seed, uint64_t* mismatches, int sm_count);
 int kernels_per_step(const mdn_sim_config& c, bool wide);
@@ -94,6 +95,7 @@ struct mdn_sim {
     bool audit_enabled = false;                             // mechanical contact audit (mdn_sim_set_contact_audit)
     float audit_margin = 0.04f;
     mdn_bank_control bank{};                                // frozen challenge bank (mdn_sim_set_challenge_bank)
+    mdn_physics_params nominal{};  // host mirror of MDN_BUF_PHYSICS (k_advance takes it by value)
     mdn_runtime_config runtime{};                           // per-episode plant variation (mdn_sim_set_runtime)
     size_t bytes[MDN_BUF_COUNT] = {};
     float room_lo[3], room_hi[3], room_c[3], room_e[3];

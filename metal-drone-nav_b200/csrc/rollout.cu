@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "contact.cuh"
 #include "mdn_device.cuh"
@@ -1213,6 +1214,101 @@ struct RaptorSmem {
     }
 };
 
+// Shared-memory layout of the RAPTOR weights for one lane per environment:
+// the reference's row-major order (raptor.hpp:11-21) with the input rows
+// padded from 22 to 24 floats, so that every row starts on a 16-byte
+// boundary and a unit's weights stream in as float4 loads.
+struct RaptorRows {
+    static constexpr int kIn = 0;               // [16 units][24]
+    static constexpr int kInB = kIn + 16 * 24;  // [16]
+    static constexpr int kGi = kInB + 16;       // [3 gates][16 units][16 cols]
+    static constexpr int kGh = kGi + 768;       // [3 gates][16 units][16 cols]
+    static constexpr int kGiB = kGh + 768;      // [3][16]
+    static constexpr int kGhB = kGiB + 48;      // [3][16]
+    static constexpr int kOut = kGhB + 48;      // [4 rows][16 cols]
+    static constexpr int kOutB = kOut + 64;     // [4]
+    static constexpr int kFloats = kOutB + 4;
+    __device__ static void fill(float* s, const float* rw, int tid, int threads) {
+        for (int k = tid; k < 16 * 24; k += threads) s[kIn + k] = k % 24 < 22 ? rw[(k / 24) * 22 + k % 24] : 0.0f;
+        for (int k = tid; k < 16; k += threads) s[kInB + k] = rw[352 + k];
+        for (int k = tid; k < 1536; k += threads) s[kGi + k] = rw[368 + k];   // gi then gh
+        for (int k = tid; k < 96; k += threads) s[kGiB + k] = rw[1904 + k];   // gi_b then gh_b
+        for (int k = tid; k < 68; k += threads) s[kOut + k] = rw[2016 + k];   // out_w then out_b
+    }
+};
+
+// Dense(22,16)-ReLU -> GRU(16) -> Dense(16,4) (raptor.hpp:52-92) for one
+// environment on one lane, unit by unit: only one unit's six gate sums are
+// live at a time (column by column, all 96 are, and the kernel spills).
+// Every sum starts from its bias and runs over the columns in order.
+__device__ __forceinline__ void raptor_forward_rows(const float* __restrict__ w, const float obs[22], float h[16],
+                                                    float action[4]) {
+    using L = RaptorRows;
+    float x[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const float4* row = reinterpret_cast<const float4*>(w + L::kIn + u * 24);
+        float acc = w[L::kInB + u];
+#pragma unroll
+        for (int q = 0; q < 6; q++) {
+            const float4 v = row[q];
+            acc = fmaf(v.x, obs[4 * q], acc);
+            acc = fmaf(v.y, obs[4 * q + 1], acc);
+            if (q < 5) {  // columns 22, 23 are padding
+                acc = fmaf(v.z, obs[4 * q + 2], acc);
+                acc = fmaf(v.w, obs[4 * q + 3], acc);
+            }
+        }
+        x[u] = smax(acc, 0.0f);
+    }
+    float nh[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        float ir = w[L::kGiB + u], hr = w[L::kGhB + u], iz = w[L::kGiB + 16 + u], hz = w[L::kGhB + 16 + u],
+              in_ = w[L::kGiB + 32 + u], hn = w[L::kGhB + 32 + u];
+        const float4* gi = reinterpret_cast<const float4*>(w + L::kGi + u * 16);
+        const float4* gh = reinterpret_cast<const float4*>(w + L::kGh + u * 16);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float4 a0 = gi[q], a1 = gi[64 + q], a2 = gi[128 + q];  // gates r, z, n (256 floats apart)
+            const float4 b0 = gh[q], b1 = gh[64 + q], b2 = gh[128 + q];
+            const float ar[4] = {a0.x, a0.y, a0.z, a0.w}, az[4] = {a1.x, a1.y, a1.z, a1.w},
+                        an[4] = {a2.x, a2.y, a2.z, a2.w};
+            const float br[4] = {b0.x, b0.y, b0.z, b0.w}, bz[4] = {b1.x, b1.y, b1.z, b1.w},
+                        bn[4] = {b2.x, b2.y, b2.z, b2.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int col = 4 * q + e;
+                ir = fmaf(ar[e], x[col], ir);
+                hr = fmaf(br[e], h[col], hr);
+                iz = fmaf(az[e], x[col], iz);
+                hz = fmaf(bz[e], h[col], hz);
+                in_ = fmaf(an[e], x[col], in_);
+                hn = fmaf(bn[e], h[col], hn);
+            }
+        }
+        const float reset = 1.0f / (1.0f + expf(-(ir + hr)));
+        const float update = 1.0f / (1.0f + expf(-(iz + hz)));
+        const float cand = tanhf(in_ + reset * hn);
+        nh[u] = (1.0f - update) * cand + update * h[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 16; u++) h[u] = nh[u];
+#pragma unroll
+    for (int row = 0; row < 4; ++row) {
+        float value = w[L::kOutB + row];
+#pragma unroll
+        for (int col = 0; col < 16; col += 4) {
+            const float4 ow = *reinterpret_cast<const float4*>(w + L::kOut + row * 16 + col);
+            value = fmaf(ow.x, h[col], value);
+            value = fmaf(ow.y, h[col + 1], value);
+            value = fmaf(ow.z, h[col + 2], value);
+            value = fmaf(ow.w, h[col + 3], value);
+        }
+        action[row] = value;
+    }
+}
+
 // U consecutive floats of shared memory (U = 1, 2, 4, 8 or 16; 16-byte
 // aligned for U >= 4) into registers.
 template <int U>
@@ -1315,16 +1411,18 @@ __device__ __forceinline__ void raptor_forward_group(const float* __restrict__ w
 
 // kEnvPhysics: each env integrates its own episode plant (runtime config on,
 // sim.metal:287) instead of the block's shared copy of the nominal one.
+// `nominal` is the plant of MDN_BUF_PHYSICS by value: as a kernel argument it
+// sits in the constant bank, and every use is an instruction operand, so the
+// integrator keeps none of its 88 coefficients in registers.
 template <int G, bool kEnvPhysics>
-__global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(SimArgs a) {
-    using L = RaptorSmem<G>;
+__global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(SimArgs a, mdn_physics_params nominal) {
+    using L = std::conditional_t<G == 1, RaptorRows, RaptorSmem<G>>;
     constexpr int kGroups = kAdvanceThreads / G;
     constexpr int V = kHidden / G;             // bootstrap critic hidden units per lane
     __shared__ __align__(16) float raptor_w[L::kFloats];
     __shared__ __align__(16) float cw1p[kCriticObs * kHidden];  // [32 inputs][G][V] critic W1
     __shared__ __align__(16) float cb1p[kHidden], cw2p[kHidden];  // [G][V]
     __shared__ float cb2;
-    __shared__ mdn_physics_params params;
     const int tid = threadIdx.x;
     {
         L::fill(raptor_w, reinterpret_cast<const float*>(a.raptor), tid, blockDim.x);
@@ -1337,9 +1435,6 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
             cw2p[(k % G) * V + k / G] = a.critic[kCriticW2 + k];
         }
         if (tid == 0) cb2 = a.critic[kCriticB2];
-        const float* pw = reinterpret_cast<const float*>(a.physics);
-        float* pd = reinterpret_cast<float*>(&params);
-        for (int k = tid; k < 88; k += blockDim.x) pd[k] = pw[k];
     }
     __syncthreads();
 
@@ -1375,7 +1470,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
             bool collision = false;
             float step_clearance = 12.0f;
             int32_t contact = -1;
-            const mdn_physics_params& plant = kEnvPhysics ? a.env_physics[i] : params;
+            const mdn_physics_params& plant = kEnvPhysics ? a.env_physics[i] : nominal;
             const float wind[3] = {w.wind[0] * plant.mass, w.wind[1] * plant.mass, w.wind[2] * plant.mass};
             float refp[3] = {run.reference_position[0], run.reference_position[1], run.reference_position[2]};
             const float dv_[3] = {run.desired_velocity[0], run.desired_velocity[1], run.desired_velocity[2]};
@@ -1384,7 +1479,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
             bool clear_valid = false;
             for (uint32_t step = 0; step < c.substeps; step++) {
                 float mo[22];
-                for (int j = 0; j < 3; j++) refp[j] += dv_[j] * params.dt;
+                for (int j = 0; j < 3; j++) refp[j] += dv_[j] * nominal.dt;
                 const float dp0 = s[0] - refp[0], dp1 = s[1] - refp[1], dp2 = s[2] - refp[2];
                 const float dvx = s[7] - dv_[0], dvy = s[8] - dv_[1], dvz = s[9] - dv_[2];
                 mo[0] = clampf(cy * dp0 + sy * dp1, -.5f, .5f);
@@ -1402,7 +1497,8 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                 mo[15] = s[10]; mo[16] = s[11]; mo[17] = s[12];
 #pragma unroll
                 for (int j = 0; j < 4; j++) mo[18 + j] = motors[j];
-                raptor_forward_group<G>(raptor_w, mo, h, motors, mask, base, r);
+                if constexpr (G == 1) raptor_forward_rows(raptor_w, mo, h, motors);
+                else raptor_forward_group<G>(raptor_w, mo, h, motors, mask, base, r);
 #pragma unroll
                 for (int j = 0; j < 4; j++) motors[j] = smax(-1.0f, smin(1.0f, motors[j]));
                 float nx[17];
@@ -1417,7 +1513,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                 path += len3(s[0] - nx[0], s[1] - nx[1], s[2] - nx[2]);
 #pragma unroll
                 for (int j = 0; j < 17; j++) s[j] = nx[j];
-                elapsed += params.dt;
+                elapsed += nominal.dt;
                 int32_t id;
                 const float clearance = world_clearance_soa(a, i, s, elapsed, &id);
                 clear_now = clearance;  // the clearance at (s, elapsed) from here on
@@ -1571,20 +1667,21 @@ static void launch_reset_list(const SimArgs& a, const StepPlan& plan, cudaStream
     k_reset_list<<<plan.reset_grid, 128, 0, s>>>(a);
 }
 
-static cudaError_t launch_advance(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
+static cudaError_t launch_advance(const SimArgs& a, const StepPlan& plan, const mdn_physics_params& nominal,
+                                  cudaStream_t s) {
     const bool own = a.runtime.enabled != 0;
     switch (plan.advance_group) {
         case 4:
-            if (own) k_advance<4, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
-            else k_advance<4, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
+            if (own) k_advance<4, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a, nominal);
+            else k_advance<4, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a, nominal);
             break;
         case 2:
-            if (own) k_advance<2, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
-            else k_advance<2, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
+            if (own) k_advance<2, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a, nominal);
+            else k_advance<2, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a, nominal);
             break;
         default:
-            if (own) k_advance<1, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
-            else k_advance<1, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a);
+            if (own) k_advance<1, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a, nominal);
+            else k_advance<1, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a, nominal);
             break;
     }
     return cudaGetLastError();
@@ -1663,21 +1760,22 @@ static cudaError_t launch_wide(const SimArgs& a, const WideStep* wide, cudaStrea
     return launch_wide_forward(wide->obs_map, wide->w1_map, p, wide->sm_count, s);
 }
 
-cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, cudaStream_t s, const WideStep* wide) {
+cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, const mdn_physics_params& nominal, cudaStream_t s,
+                        const WideStep* wide) {
     k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
     if (a.cfg.geometry_memory)
         k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
     cudaError_t e = launch_wide(a, wide, s);
     if (e != cudaSuccess) return e;
     launch_act(a, plan, s);
-    e = launch_advance(a, plan, s);
+    e = launch_advance(a, plan, nominal, s);
     if (e != cudaSuccess) return e;
     launch_reset_list(a, plan, s);
     return cudaGetLastError();
 }
 
-cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStream_t s, cudaEvent_t ev[4],
-                                 const WideStep* wide) {
+cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, const mdn_physics_params& nominal, cudaStream_t s,
+                                 cudaEvent_t ev[4], const WideStep* wide) {
     cudaEventRecord(ev[0], s);
     k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
     if (a.cfg.geometry_memory)
@@ -1687,7 +1785,7 @@ cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, cudaStr
     if (we != cudaSuccess) return we;
     launch_act(a, plan, s);
     cudaEventRecord(ev[2], s);
-    const cudaError_t e = launch_advance(a, plan, s);
+    const cudaError_t e = launch_advance(a, plan, nominal, s);
     if (e != cudaSuccess) return e;
     launch_reset_list(a, plan, s);
     cudaEventRecord(ev[3], s);
