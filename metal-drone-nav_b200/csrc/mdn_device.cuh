@@ -218,6 +218,50 @@ __device__ __forceinline__ float world_clearance_soa(const SimArgs& a, uint32_t 
     return best;
 }
 
+// world_clearance_soa on a group of G lanes that share environment i (lane r
+// of the group takes obstacles r, r + G, ...). Each lane keeps the smallest
+// clearance of its obstacles and the first index that reached it below the
+// room's; the group then keeps the smallest value, and on a tie the smaller
+// index (equal values are either both the room's, index -1, or both below
+// it). That is the value and index of the sequential scan.
+template <int G>
+__device__ __forceinline__ float world_clearance_lanes(const SimArgs& a, uint32_t i, const float p[3], float t,
+                                                       int32_t* argmin, int r, unsigned mask) {
+    if constexpr (G == 1) {
+        return world_clearance_soa(a, i, p, t, argmin);
+    } else {
+        const float* soa = a.world_soa;
+        const size_t n = a.n;
+        float best = room_clearance(a, p);
+        int32_t id = -1;
+        uint32_t count = __float_as_uint(__ldg(&soa[160 * n + i]));
+        count = count < 16u ? count : 16u;
+        for (uint32_t o = uint32_t(r); o < count; o += G) {
+            const float* f = soa + size_t(o) * 10 * n + i;
+            const uint32_t kind = __float_as_uint(__ldg(f));
+            const float c[3] = {__ldg(f + n), __ldg(f + 2 * n), __ldg(f + 3 * n)};
+            const float size[3] = {__ldg(f + 4 * n), __ldg(f + 5 * n), __ldg(f + 6 * n)};
+            const float v[3] = {__ldg(f + 7 * n), __ldg(f + 8 * n), __ldg(f + 9 * n)};
+            float cc[3];
+            obstacle_center(kind, c, size, v, t, cc);
+            const float cand = obstacle_clearance(kind, size, p[0] - cc[0], p[1] - cc[1], p[2] - cc[2]);
+            if (cand < best) id = int32_t(o);
+            best = fminf(best, cand);
+        }
+#pragma unroll
+        for (int off = G / 2; off > 0; off >>= 1) {
+            const float ob = __shfl_xor_sync(mask, best, off);
+            const int32_t oi = __shfl_xor_sync(mask, id, off);
+            if (ob < best || (ob == best && oi < id)) {
+                best = ob;
+                id = oi;
+            }
+        }
+        if (argmin) *argmin = id;
+        return best;
+    }
+}
+
 // Body-to-world rotation from a wxyz quaternion, sim.metal:43-48.
 __device__ __forceinline__ void rotation(const float q[4], float r[9]) {
     const float w = q[0], x = q[1], y = q[2], z = q[3];

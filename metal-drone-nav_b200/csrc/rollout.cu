@@ -1515,7 +1515,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                 for (int j = 0; j < 17; j++) s[j] = nx[j];
                 elapsed += nominal.dt;
                 int32_t id;
-                const float clearance = world_clearance_soa(a, i, s, elapsed, &id);
+                const float clearance = world_clearance_lanes<G>(a, i, s, elapsed, &id, r, mask);
                 clear_now = clearance;  // the clearance at (s, elapsed) from here on
                 clear_valid = true;
                 if (clearance < step_clearance) contact = id;
@@ -1528,10 +1528,6 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                 }
             }
             const uint32_t steps = run.steps + 1;
-            if (a.audit && r == 0) {  // mechanical contact audit of the post-integration pose
-                const float pos[3] = {s[0], s[1], s[2]}, orient[4] = {s[3], s[4], s[5], s[6]};
-                a.audit[row] = contact::world_contact(pos, orient, w, elapsed, a.audit_margin);
-            }
             // Bootstrap value of the post-step critic observation (sim.metal:327),
             // hidden units r, r+G, ... on lane r.
             float value;
@@ -1547,7 +1543,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                 for (int j = 0; j < 4; j++) co[9 + j] = s[3 + j];
                 // wclearance of the final pose: the last substep's value unless
                 // the first substep already stopped on an invalid state.
-                co[19] = (clear_valid ? clear_now : world_clearance_soa(a, i, s, elapsed, nullptr)) / 5.0f;
+                co[19] = (clear_valid ? clear_now : world_clearance_lanes<G>(a, i, s, elapsed, nullptr, r, mask)) / 5.0f;
                 co[20] = float(steps) / 200.0f;
                 for (int j = 21; j < 30; j++) co[j] = 0.0f;
                 const uint32_t m = count < 3u ? count : 3u;
@@ -1639,6 +1635,13 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                     run.total_elapsed += elapsed;
                     run.final_progress += 1.0f - after / smax(run.initial_distance, 1.0e-4f);
                     refill = !c.eval;  // reset by k_reset_list after this launch
+                }
+                if (a.audit) {  // mechanical contact audit of the post-integration pose
+                    // Called last, with the pose read back from the stores above, so
+                    // that little is live across this out-of-line call.
+                    const float* sp = reinterpret_cast<const float*>(&a.states[i]);
+                    const float pos[3] = {sp[0], sp[1], sp[2]}, orient[4] = {sp[3], sp[4], sp[5], sp[6]};
+                    a.audit[row] = contact::world_contact(pos, orient, w, run.elapsed, a.audit_margin);
                 }
             }
         }
