@@ -1796,9 +1796,10 @@ cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, const m
 }
 
 // Launch shapes of one policy step for n environments. On small shards the
-// per-environment chain of k_advance sets its time, so the RAPTOR units and the
-// bootstrap critic are split over 2 or 4 lanes; on large ones occupancy does,
-// and one lane per environment is fastest (65,536: 0.283 vs 0.406 ms with 2).
+// per-environment chain of k_advance sets its time, so the RAPTOR units, the
+// clearance scan and the bootstrap critic are split over 2 or 4 lanes; on
+// large ones occupancy does, and one lane per environment is fastest (65,536:
+// 0.272 vs 0.384 ms with 2).
 StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_override) {
     StepPlan p{};
     p.act_grid = int(std::min<size_t>((size_t(n) + 31) / 32, size_t(sm_count) * 2));
@@ -1810,9 +1811,11 @@ StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_overrid
     const size_t per_block = p.act_quads ? kRowThreads / kQuadSplit : kRowThreads;
     p.act_rows_grid = int(std::min<size_t>((size_t(n) + per_block - 1) / per_block, size_t(sm_count) * 2));
     // Lanes per environment for k_advance: 4 on shards of at most 64
-    // environments per SM (8,192 envs: 0.151 vs 0.164 ms with 2), 2 up to 128
-    // (16,384: 0.179 vs 0.244 ms with 4), else 1.
-    int g = size_t(n) <= size_t(sm_count) * 64 ? 4 : (size_t(n) <= size_t(sm_count) * 128 ? 2 : 1);
+    // environments per SM (8,192 envs: 0.151 vs 0.163 ms with 2), 2 while the
+    // pairs fit one wave of three 128-thread blocks per SM, 192 environments
+    // (16,384: 0.167 vs 0.214 ms with 1; 24,576: 0.179 vs 0.222), else 1
+    // (32,768: 0.224 vs 0.263 ms with 2).
+    int g = size_t(n) <= size_t(sm_count) * 64 ? 4 : (size_t(n) <= size_t(sm_count) * 192 ? 2 : 1);
     if (group_override == 1 || group_override == 2 || group_override == 4) g = group_override;
     p.advance_group = g;
     const int per_sm = g == 1 ? advance_blocks_per_sm<1>() : (g == 2 ? advance_blocks_per_sm<2>() : advance_blocks_per_sm<4>());
