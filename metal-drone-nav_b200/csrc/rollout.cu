@@ -39,9 +39,10 @@ __device__ __forceinline__ void refill_ring_warp(const SimArgs& a, uint32_t i) {
 
 // sim_reset: one warp per environment (episode_reset is warp-cooperative).
 __global__ void __launch_bounds__(128) k_reset(SimArgs a, int first) {
+    __shared__ mdn_world scratch[4];  // one world per warp of the 128-thread block
     const uint32_t i = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (i >= a.n) return;  // warp-uniform
-    episode_reset(a, i, first != 0, 0);
+    episode_reset(a, i, first != 0, 0, scratch[threadIdx.x >> 5]);
     refill_ring_warp(a, i);
 }
 
@@ -50,11 +51,12 @@ __global__ void __launch_bounds__(128) k_reset(SimArgs a, int first) {
 // reset neither holds up an advance warp nor runs its generator's checks on
 // one lane. Schedule slot tick + 1 as in the advance.
 __global__ void __launch_bounds__(128) k_reset_list(SimArgs a) {
+    __shared__ mdn_world scratch[4];  // one world per warp of the 128-thread block
     const uint32_t count = *reinterpret_cast<volatile uint32_t*>(a.reset_count);
     const uint32_t warps = gridDim.x * (blockDim.x / 32);
     for (uint32_t k = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); k < count; k += warps) {
         const uint32_t i = a.reset_list[k];
-        episode_reset(a, i, false, a.tick + 1);
+        episode_reset(a, i, false, a.tick + 1, scratch[threadIdx.x >> 5]);
         refill_ring_warp(a, i);
     }
 }

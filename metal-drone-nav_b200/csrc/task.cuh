@@ -282,8 +282,9 @@ __device__ TaskStep task_step(mdn_task_state& task, const mdn_task_config& c, co
 // world of schedule slot `slot` (sim.metal:143,330), then
 // sim_reset_navigation_task (sim.metal:125-141), then the SoA world mirror.
 // Returns true (the caller refills the env's range ring).
-__device__ __noinline__ bool episode_reset(const SimArgs& a, uint32_t i, bool first, uint32_t slot) {
-    reset_env(a, i, first);
+__device__ __noinline__ bool episode_reset(const SimArgs& a, uint32_t i, bool first, uint32_t slot,
+                                           mdn_world& scratch) {
+    reset_env(a, i, first, scratch);
     if (a.bank_enabled) apply_challenge_world(a, i, slot);
     else a.bank_active[i] = 0xffffffffu;
     mdn_task_state& task = a.tasks[i];
@@ -317,7 +318,8 @@ __device__ __noinline__ bool episode_reset(const SimArgs& a, uint32_t i, bool fi
             w.wind[2] = 0;
         }
     }
-    mirror_world(a, i);
+    __syncwarp();
+    mirror_world_warp(a, i);
     return true;
 }
 

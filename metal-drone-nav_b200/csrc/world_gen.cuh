@@ -373,19 +373,36 @@ __device__ __forceinline__ void mirror_world(const SimArgs& a, uint32_t i) {
     for (int k = 0; k < 160; k++) a.world_soa[size_t(k) * a.n + i] = words[k];
     a.world_soa[size_t(160) * a.n + i] = __uint_as_float(w.count);
 }
+// The same from a whole warp, words split over the lanes (word 160 = count).
+__device__ __forceinline__ void mirror_world_warp(const SimArgs& a, uint32_t i) {
+    const float* words = reinterpret_cast<const float*>(&a.worlds[i]);
+    static_assert(offsetof(mdn_world, count) == 160 * sizeof(float), "count follows the 16 obstacles");
+    for (int k = threadIdx.x & 31; k < 161; k += 32) a.world_soa[size_t(k) * a.n + i] = words[k];
+}
+// Whole-warp copy of one world (169 words), then a warp barrier, so that
+// every lane sees the copy.
+__device__ __forceinline__ void copy_world_warp(mdn_world& dst, const mdn_world& src) {
+    constexpr int kWords = int(sizeof(mdn_world) / sizeof(uint32_t));
+    const uint32_t* s = reinterpret_cast<const uint32_t*>(&src);
+    uint32_t* d = reinterpret_cast<uint32_t*>(&dst);
+    for (int k = threadIdx.x & 31; k < kWords; k += 32) d[k] = s[k];
+    __syncwarp();
+}
 
 // sim_reset_one (sim.metal:55-94) for one environment, except the 8x320 range
 // ring refill, which the caller performs cooperatively (returns true when the
 // ring must be refilled with 12 m). Run by a whole converged warp for the same
 // environment: every lane computes the same values and stores them (identical
 // stores to one address), and the generators' heavy checks are split over the
-// lanes (mover_clear).
-__device__ bool reset_env(const SimArgs& a, uint32_t i, bool first) {
+// lanes (mover_clear). The world is generated in `w`, the warp's copy in shared
+// memory (the generators read back what they wrote, which in global memory
+// would cost an L2 round trip each time), and then stored to a.worlds[i].
+__device__ bool reset_env(const SimArgs& a, uint32_t i, bool first, mdn_world& w) {
     const mdn_sim_config& c = a.cfg;
     const uint32_t gid = a.env_base + i;
     mdn_sim_run& run = a.runs[i];
     mdn_physics_state& s = a.states[i];
-    mdn_world& w = a.worlds[i];
+    copy_world_warp(w, a.worlds[i]);  // fields a generator leaves alone keep their bytes
     uint32_t rng = first ? (c.seed + gid * 747796405u + 2891336453u) : run.rng;
     const uint32_t family = c.family == 18u ? mixed_lane_family(gid) : training_family(c.family, rng);
     generate_world(w, wrng(rng), family, c.distance);
@@ -454,6 +471,8 @@ __device__ bool reset_env(const SimArgs& a, uint32_t i, bool first) {
         float* pose = a.poses + size_t(i) * kFrames * 12;
         for (int j = 0; j < kFrames * 12; j++) pose[j] = 0;
     }
+    __syncwarp();
+    copy_world_warp(a.worlds[i], w);
     return true;
 }
 
