@@ -740,8 +740,8 @@ __device__ __forceinline__ float overhead_scale(const float* ob) {
 // The rest of sim_act for env i at `row` once its actor mean and critic value
 // are known (sim.metal:229-271): mode blends, sampling, log-prob, command ring
 // and delay, desired velocity and yaw. `ob` is the env's observation row.
-__device__ __noinline__ void act_finish(const SimArgs& a, uint32_t i, size_t row, const float* ob,
-                                        const float* mean_in, float value, const float* log_std) {
+__device__ __forceinline__ void act_finish_body(const SimArgs& a, uint32_t i, size_t row, const float* ob,
+                                                const float* mean_in, float value, const float* log_std) {
     const mdn_sim_config& c = a.cfg;
     mdn_sim_run& run = a.runs[i];
     a.values[row] = value;
@@ -827,6 +827,14 @@ __device__ __noinline__ void act_finish(const SimArgs& a, uint32_t i, size_t row
     }
     for (int j = 0; j < 3; j++) run.desired_velocity[j] = r[j * 3] * v[0] + r[j * 3 + 1] * v[1] + r[j * 3 + 2] * v[2];
     run.yaw += pn[3] * a.physics->dt * float(c.substeps) * 0.5f;
+}
+
+// Out of line for the thread-per-environment actor, whose 128 registers are
+// better spent on the dot products; the quad actor inlines the body (8,192
+// envs: 0.037 vs 0.039 ms).
+__device__ __noinline__ void act_finish(const SimArgs& a, uint32_t i, size_t row, const float* ob,
+                                        const float* mean_in, float value, const float* log_std) {
+    act_finish_body(a, i, row, ob, mean_in, value, log_std);
 }
 
 // The 64-unit actor and the critic with one thread per environment: every
@@ -1026,7 +1034,7 @@ __global__ void __launch_bounds__(kRowThreads) k_act_quads(SimArgs a) {
 #pragma unroll
         for (int h = 0; h < kQuadUnits; h++) value = fmaf(tanhf(z[h] + cb1[part + kQuadSplit * h]), cw2[part + kQuadSplit * h], value);
         value = quad_sum(value) + cb2[0];
-        if (live && part == 0) act_finish(a, i, row, ob, mean, value, log_std);
+        if (live && part == 0) act_finish_body(a, i, row, ob, mean, value, log_std);
     }
 }
 
