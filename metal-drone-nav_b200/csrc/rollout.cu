@@ -964,6 +964,8 @@ __global__ void __launch_bounds__(kRowThreads, 2) k_act_rows(SimArgs a) {
 // quad finishes sim_act.
 constexpr int kQuadSplit = 4;
 constexpr int kQuadUnits = kHidden / kQuadSplit;
+constexpr int kQuadEnvs = kRowThreads / kQuadSplit;  // environments per block pass
+static_assert(kRowSmemFloats % 4 == 0, "the staged observations start on a 16-byte boundary");
 
 __device__ __forceinline__ float quad_sum(float v) {  // ((t0 + t1) + (t2 + t3)) on every lane of the quad
     v += __shfl_xor_sync(0xffffffffu, v, 1);
@@ -978,7 +980,10 @@ __global__ void __launch_bounds__(kRowThreads) k_act_quads(SimArgs a) {
     const int tid = threadIdx.x;
     const mdn_sim_config& c = a.cfg;
     const int part = tid % kQuadSplit;  // this thread's units: part, part + 4, ..., part + 60
-    const uint32_t per_block = kRowThreads / kQuadSplit;
+    const uint32_t per_block = kQuadEnvs;
+    // The pass's observation rows (contiguous in HBM) staged in shared memory by
+    // the whole block, so the dot products wait on one load round trip.
+    float4* obs_s = smem4 + kRowSmemFloats / 4;  // [kQuadEnvs][46]
     // Every lane of a quad runs the loop the same number of times (the
     // shuffles need the whole quad); `live` masks the tail.
     for (uint32_t base = blockIdx.x * per_block; base < a.n; base += gridDim.x * per_block) {
@@ -986,13 +991,20 @@ __global__ void __launch_bounds__(kRowThreads) k_act_quads(SimArgs a) {
         const bool live = i < a.n && !(c.eval && a.runs[i].episodes);
         const size_t row = size_t(a.tick) * a.n + (live ? i : 0);
         const float* ob = a.obs + row * kActorObs;
+        {
+            const uint32_t rows = min(per_block, a.n - base);
+            const float4* src = reinterpret_cast<const float4*>(a.obs + (size_t(a.tick) * a.n + base) * kActorObs);
+            __syncthreads();  // the previous pass is done with the staged rows
+            for (uint32_t k = tid; k < rows * (kActorObs / 4); k += kRowThreads) obs_s[k] = __ldg(src + k);
+            __syncthreads();
+        }
         float z[kQuadUnits];
 #pragma unroll
         for (int h = 0; h < kQuadUnits; h++) z[h] = 0.0f;
-        const float4* ob4 = reinterpret_cast<const float4*>(ob);
+        const float4* ob4 = obs_s + (tid / kQuadSplit) * (kActorObs / 4);
 #pragma unroll 2
         for (int k4 = 0; k4 < kActorObs / 4; k4++) {
-            const float4 o4 = __ldg(ob4 + k4);
+            const float4 o4 = ob4[k4];
 #pragma unroll
             for (int u = 0; u < kQuadUnits; u++) {  // unit part + 4u
                 const float4 w = *reinterpret_cast<const float4*>(w1 + (part + kQuadSplit * u) * kW1Pitch + 4 * k4);
@@ -1755,12 +1767,13 @@ cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s) {
 
 size_t act_smem_bytes() { return sizeof(float) * kActSmemFloats; }
 static size_t act_rows_smem_bytes() { return sizeof(float) * kRowSmemFloats; }
+static size_t act_quads_smem_bytes() { return sizeof(float) * (kRowSmemFloats + size_t(kQuadEnvs) * kActorObs); }
 
 static void launch_act(const SimArgs& a, const StepPlan& plan, cudaStream_t s) {
     if (a.wide_slices)
         k_act<true><<<plan.act_grid, kActWarps * 32, act_smem_bytes(), s>>>(a);
     else if (plan.act_quads)
-        k_act_quads<<<plan.act_rows_grid, kRowThreads, act_rows_smem_bytes(), s>>>(a);
+        k_act_quads<<<plan.act_rows_grid, kRowThreads, act_quads_smem_bytes(), s>>>(a);
     else
         k_act_rows<<<plan.act_rows_grid, kRowThreads, act_rows_smem_bytes(), s>>>(a);
 }
@@ -1925,7 +1938,7 @@ cudaError_t configure_kernels() {
     cudaError_t e = cudaFuncSetAttribute(k_act_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(act_rows_smem_bytes()));
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(k_act_quads, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_rows_smem_bytes()));
+    e = cudaFuncSetAttribute(k_act_quads, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_quads_smem_bytes()));
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_act<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(act_smem_bytes()));
     if (e != cudaSuccess) return e;
