@@ -8,6 +8,7 @@
 // The device side (sim_apply_challenge_world) is apply_challenge_world in
 // world_gen.cuh; mdn_sim_set_challenge_bank in host.cpp wires the two.
 #include <algorithm>
+#include <array>
 #include <cfloat>
 #include <cmath>
 #include <cstdio>
@@ -624,159 +625,226 @@ static void load_split(const std::string& path, const std::string& split, const 
 }
 
 // ------------------------------------------------------------------ sampler
-// challenge_training::ChallengeTraining (challenge_training.hpp:53-427).
+// Train-split level sampler of frozen-bank training. It reproduces the
+// schedules, failure scores and CHTRN1 sidecar of challenge_training.hpp:53-427
+// from this specification:
+//
+//  * Pools. The train levels fall into three family pools, 14, 15 and 16, each
+//    listing its levels in bank order. All three must be non-empty.
+//  * Quotas. Environments below `rehearsal_environments` never hold a bank
+//    level: their slots are kInvalidLevel. Every other environment draws from
+//    one fixed pool: the focus family when one is set, else pool
+//    (env - rehearsal) mod 3 in the order 14, 15, 16.
+//  * Schedules are env-major rows of horizon + 1 slots. A new run draws every
+//    slot. Each later rollout keeps the caller's live level in slot 0 (checked
+//    against the quota) and draws slots 1..horizon. Draws run environment by
+//    environment, slot by slot, from one xorshift32 stream (shifts 13, 17, 5;
+//    a zero state becomes 1; seed 0 means 1).
+//  * One draw. Uniform selection: index = (u32 * pool size) >> 32. Failure-
+//    weighted selection: u = u32 / 2^32 first; below the uniform floor, a
+//    uniform index from the next draw; otherwise the next draw times the
+//    pool's weight total is a remainder from which the weights are subtracted
+//    in pool order, and the first level that takes it to zero or below wins.
+//  * Weights, refreshed before each schedule: mix / (score rank + 1) +
+//    (1 - mix) / (staleness rank + 1) in double. Score rank orders the pool by
+//    failure score, highest first; staleness rank by the rollout of the last
+//    visit, oldest first; equal keys go by level index.
+//  * Scores. Each bank transition adds |raw GAE| to its environment's open
+//    episode and stamps the level with the rollout index. When the episode
+//    ends, the level's score becomes the episode's mean |GAE| and its
+//    completion count grows.
+//  * Sidecar CHTRN1 v3: a 256-byte header, the per-level ledger (scores f32,
+//    last visit u64, last score u64, completions u64), the open episodes
+//    (|GAE| sums f64, sample counts u32, levels u32) and the active ids u32.
+//    Versions 1 and 2 load when no focus family is set.
+namespace {
+
+struct SamplerRng {
+    uint32_t state = 1;
+    uint32_t next() {
+        uint32_t x = state ? state : 1u;
+        x ^= x << 13;
+        x ^= x >> 17;
+        x ^= x << 5;
+        state = x ? x : 1u;
+        return state;
+    }
+    // in [0, 1): multiplying by 2^-32 is exact, as dividing by 2^32 is
+    double unit() { return double(next()) * 0x1p-32; }
+    size_t below(size_t count) { return size_t((uint64_t(next()) * count) >> 32); }
+};
+
+struct FamilyPool {
+    uint32_t family = 0;
+    std::vector<uint32_t> levels;  // bank indices, ascending
+    std::vector<double> weight;    // failure-weighted replay weight of each entry
+    double weight_total = 0.0;     // their sum in pool order
+};
+
+// Zero-based position of each pool entry once the entries are put in the
+// strict total order `before`.
+template <class Before>
+std::vector<uint32_t> pool_ranks(const std::vector<uint32_t>& levels, Before before) {
+    std::vector<uint32_t> order(levels.size());
+    for (uint32_t i = 0; i < order.size(); i++) order[i] = i;
+    std::sort(order.begin(), order.end(), [&](uint32_t x, uint32_t y) { return before(levels[x], levels[y]); });
+    std::vector<uint32_t> rank(levels.size());
+    for (uint32_t r = 0; r < order.size(); r++) rank[order[r]] = r;
+    return rank;
+}
+
+// What the sampler knows about each train level.
+struct LevelLedger {
+    std::vector<float> score;         // mean |GAE| of the level's last completed episode
+    std::vector<uint64_t> visited;    // rollout of the last transition on the level
+    std::vector<uint64_t> scored;     // rollout of the last score
+    std::vector<uint64_t> completed;  // completed episodes
+    void reset(size_t levels) {
+        score.assign(levels, 0.0f);
+        visited.assign(levels, 0);
+        scored.assign(levels, 0);
+        completed.assign(levels, 0);
+    }
+};
+
+// The episode each environment is in the middle of.
+struct OpenEpisodes {
+    std::vector<double> abs_gae;   // sum of |GAE| so far
+    std::vector<uint32_t> samples; // transitions so far
+    std::vector<uint32_t> level;   // its level, kInvalidLevel when none is open
+    void reset(size_t envs) {
+        abs_gae.assign(envs, 0.0);
+        samples.assign(envs, 0);
+        level.assign(envs, kInvalidLevel);
+    }
+};
+
+// The CHTRN1 sidecar header (challenge_training.hpp:281-287): a file format.
+struct SidecarHeader {
+    char magic[8];
+    uint32_t version, selection, environment_count, horizon, level_count, rng_state, focus_family, rehearsal;
+    uint64_t last_rollout, completed_rollouts;
+    float uniform_floor, score_staleness_mix;
+    char bank_hash[64], world_hash[64], checkpoint_hash[64];
+};
+static_assert(sizeof(SidecarHeader) == 256, "challenge sidecar header layout");
+constexpr char kSidecarMagic[8] = {'C', 'H', 'T', 'R', 'N', '1', 0, 0};
+constexpr uint32_t kSidecarVersion = 3;
+
+struct ByteSpan {
+    void* data;
+    size_t bytes;
+};
+template <class T>
+ByteSpan span_of(std::vector<T>& v) {
+    return {v.data(), v.size() * sizeof(T)};
+}
+
+// The sidecar body after the header, in file order.
+std::vector<ByteSpan> sidecar_body(LevelLedger& l, OpenEpisodes& e, std::vector<uint32_t>& active) {
+    return {span_of(l.score), span_of(l.visited), span_of(l.scored), span_of(l.completed),
+            span_of(e.abs_gae), span_of(e.samples), span_of(e.level), span_of(active)};
+}
+
+}  // namespace
+
 class ChallengeSampler {
 public:
     ChallengeSampler(const std::string& bank_jsonl, const std::string& world_hash, const mdn_challenge_settings& s)
-        : settings_(s) {
-        auto fail = [](const char* m) { throw Error(MDN_ERR_INVALID, m); };
-        if (s.environment_count == 0 || s.horizon == 0) fail("challenge training needs nonzero environments and horizon");
-        if (s.environment_count < 3 || s.rehearsal_environments > s.environment_count - 3)
-            fail("rehearsal must leave at least three bank environments");
-        if (s.focus_family != 0u && s.focus_family != 14u && s.focus_family != 15u && s.focus_family != 16u)
-            fail("focused challenge family must be14,15,16 or0 for balanced");
-        if (s.selection != 0u && s.selection != 1u) fail("unsupported challenge level selection mode");
-        if (!std::isfinite(s.uniform_floor) || s.uniform_floor < 0.5f || s.uniform_floor > 1.0f)
-            fail("failure-weighted replay uniform floor must be in [0.5,1]");
-        if (!std::isfinite(s.score_staleness_mix) || s.score_staleness_mix < 0.0f || s.score_staleness_mix > 1.0f)
-            fail("score/staleness mix must be in [0,1]");
-        // A schedule is environment_count x (horizon + 1) ids; keep it addressable.
-        if (uint64_t(s.environment_count) * (uint64_t(s.horizon) + 1) > (uint64_t(1) << 31))
-            fail("challenge schedule larger than 2^31 slots");
+        : settings_(s), world_hash_(world_hash) {
+        check_settings(s);
         load_split(bank_jsonl, "train", world_hash, bank_);
-        world_hash_ = world_hash;
-        for (uint32_t i = 0; i < bank_.levels.size(); ++i) {
-            if (bank_.levels[i].split != "train") fail("train loader returned a non-train challenge level");
-            family_levels_[bank_.levels[i].info.family].push_back(i);
-        }
-        if (family_levels_.size() < 3) fail("train bank must contain each family 14, 15, and 16");
-        for (uint32_t family : {14u, 15u, 16u}) {
-            auto found = family_levels_.find(family);
-            if (found == family_levels_.end() || found->second.empty())
-                throw Error(MDN_ERR_INVALID, "train bank is missing family " + std::to_string(family));
-            families_.push_back(family);
-        }
-        const size_t L = bank_.levels.size(), E = s.environment_count;
-        scores_.assign(L, 0.0f);
-        last_visit_.assign(L, 0);
-        last_score_.assign(L, 0);
-        completed_.assign(L, 0);
-        episode_abs_gae_.assign(E, 0.0);
-        episode_count_.assign(E, 0);
-        episode_level_.assign(E, kInvalidLevel);
-        rng_ = s.sampler_seed ? s.sampler_seed : 1;
+        build_pools();
+        ledger_.reset(bank_.levels.size());
+        open_.reset(s.environment_count);
+        rng_.state = s.sampler_seed ? s.sampler_seed : 1u;
     }
 
     const BankData& bank() const { return bank_; }
     mdn_bank_control control() const {
         return {1u, uint32_t(bank_.levels.size()), settings_.horizon + 1, settings_.horizon};
     }
-    size_t stride() const { return size_t(settings_.horizon) + 1; }
-
-    void initial_schedule(uint32_t* schedule) {
-        refresh_priorities();
-        const uint32_t E = settings_.environment_count, H = settings_.horizon;
-        for (uint32_t env = 0; env < E; ++env) {
-            uint32_t* row = schedule + size_t(env) * stride();
-            if (env < settings_.rehearsal_environments) {
-                for (uint32_t tick = 0; tick <= H; tick++) row[tick] = kInvalidLevel;
-                continue;
-            }
-            const uint32_t family = family_for_env(env);
-            for (uint32_t tick = 0; tick <= H; ++tick) row[tick] = sample_level_for_family(family);
-        }
-        active_.resize(E);
-        for (uint32_t env = 0; env < E; ++env) active_[env] = schedule[size_t(env) * stride()];
-    }
-
-    void next_schedule(const uint32_t* active, uint64_t rollout_index, uint32_t* schedule) {
-        const uint32_t E = settings_.environment_count, H = settings_.horizon;
-        last_rollout_ = rollout_index;
-        refresh_priorities();
-        for (uint32_t env = 0; env < E; ++env) {
-            validate_active_id(env, active[env]);
-            schedule[size_t(env) * stride()] = active[env];
-        }
-        active_.assign(active, active + E);
-        for (uint32_t env = 0; env < E; ++env) {
-            uint32_t* row = schedule + size_t(env) * stride();
-            if (env < settings_.rehearsal_environments) {
-                for (uint32_t tick = 1; tick <= H; tick++) row[tick] = kInvalidLevel;
-                continue;
-            }
-            const uint32_t family = family_for_env(env);
-            for (uint32_t tick = 1; tick <= H; ++tick) row[tick] = sample_level_for_family(family);
-        }
-    }
-
     const std::vector<uint32_t>& active_ids() const { return active_; }
 
+    // A new run: every slot of every row is drawn; slot 0 becomes the active ids.
+    void initial_schedule(uint32_t* schedule) {
+        refresh_weights();
+        const size_t stride = size_t(settings_.horizon) + 1;
+        active_.resize(settings_.environment_count);
+        for (uint32_t env = 0; env < settings_.environment_count; ++env) {
+            uint32_t* row = schedule + env * stride;
+            fill_row(env, row, 0);
+            active_[env] = row[0];
+        }
+    }
+
+    // A later rollout: slot 0 keeps each environment's live level; slots
+    // 1..horizon serve the resets inside the rollout.
+    void next_schedule(const uint32_t* active, uint64_t rollout_index, uint32_t* schedule) {
+        last_rollout_ = rollout_index;
+        refresh_weights();
+        const uint32_t envs = settings_.environment_count;
+        const size_t stride = size_t(settings_.horizon) + 1;
+        for (uint32_t env = 0; env < envs; ++env) {
+            check_active(env, active[env]);
+            schedule[env * stride] = active[env];
+        }
+        active_.assign(active, active + envs);
+        for (uint32_t env = 0; env < envs; ++env) fill_row(env, schedule + env * stride, 1);
+    }
+
+    // Rollout evidence in [tick][env] order: raw (unnormalised) GAE, episode
+    // ends and the level of every transition.
     void observe_raw_gae(const float* raw_gae, const uint8_t* terminated, const uint8_t* truncated,
                          const uint32_t* transition_ids, uint64_t rollout_index) {
         if (!raw_gae || !terminated || !truncated || !transition_ids)
             throw Error(MDN_ERR_INVALID, "challenge rollout evidence buffer is null");
-        const uint32_t E = settings_.environment_count;
-        for (uint32_t tick = 0; tick < settings_.horizon; ++tick) {
-            for (uint32_t env = 0; env < E; ++env) {
-                const size_t row = size_t(tick) * E + env;
+        const uint32_t envs = settings_.environment_count;
+        for (uint32_t tick = 0; tick < settings_.horizon; ++tick)
+            for (uint32_t env = 0; env < envs; ++env) {
+                const size_t row = size_t(tick) * envs + env;
                 const uint32_t level = transition_ids[row];
-                if (env < settings_.rehearsal_environments) {
+                if (is_rehearsal(env)) {
                     if (level != kInvalidLevel) throw Error(MDN_ERR_INVALID, "rehearsal transition contains a bank level");
                     continue;
                 }
                 if (level >= bank_.levels.size())
                     throw Error(MDN_ERR_INVALID, "transition level id is outside the frozen train bank");
-                uint32_t& active = episode_level_[env];
-                if (active == kInvalidLevel) active = level;
-                if (active != level)
+                uint32_t& open_level = open_.level[env];
+                if (open_level == kInvalidLevel)
+                    open_level = level;
+                else if (open_level != level)
                     throw Error(MDN_ERR_INVALID, "active challenge level changed before episode completion");
-                const float value = raw_gae[row];
-                if (!std::isfinite(value)) throw Error(MDN_ERR_INVALID, "raw GAE is non-finite");
-                episode_abs_gae_[env] += std::fabs(double(value));
-                ++episode_count_[env];
-                last_visit_[level] = rollout_index;
-                if (terminated[row] || truncated[row]) {
-                    const uint32_t count = episode_count_[env];
-                    if (count == 0) throw Error(MDN_ERR_INVALID, "completed challenge episode has no GAE samples");
-                    scores_[level] = float(episode_abs_gae_[env] / count);
-                    last_score_[level] = rollout_index;
-                    ++completed_[level];
-                    episode_abs_gae_[env] = 0.0;
-                    episode_count_[env] = 0;
-                    active = kInvalidLevel;
-                }
+                if (!std::isfinite(raw_gae[row])) throw Error(MDN_ERR_INVALID, "raw GAE is non-finite");
+                open_.abs_gae[env] += std::fabs(double(raw_gae[row]));
+                open_.samples[env] += 1;
+                ledger_.visited[level] = rollout_index;
+                if (terminated[row] || truncated[row]) close_episode(env, level, rollout_index);
             }
-        }
         last_rollout_ = rollout_index;
     }
 
     void level_stats(uint32_t level, float* score, uint64_t* completed, uint64_t* last_visit) const {
         require(level < bank_.levels.size(), MDN_ERR_INVALID, "challenge level index out of range");
-        if (score) *score = scores_[level];
-        if (completed) *completed = completed_[level];
-        if (last_visit) *last_visit = last_visit_[level];
+        if (score) *score = ledger_.score[level];
+        if (completed) *completed = ledger_.completed[level];
+        if (last_visit) *last_visit = ledger_.visited[level];
     }
 
+    // Written to `path`.tmp, then renamed over `path`.
     void save_state(const std::string& path, const std::string& checkpoint_sha256, uint64_t completed_rollouts,
                     const uint32_t* active) {
-        const uint32_t E = settings_.environment_count;
-        for (uint32_t env = 0; env < E; env++) validate_active_id(env, active[env]);
-        active_.assign(active, active + E);
-        const DiskHeader header = make_header(checkpoint_sha256, completed_rollouts);
+        for (uint32_t env = 0; env < settings_.environment_count; env++) check_active(env, active[env]);
+        active_.assign(active, active + settings_.environment_count);
+        const SidecarHeader header = sidecar_header(checkpoint_sha256, completed_rollouts);
+        const std::filesystem::path target(path);
+        if (target.has_parent_path()) std::filesystem::create_directories(target.parent_path());
         const std::string temporary = path + ".tmp";
-        const std::filesystem::path parent = std::filesystem::path(path).parent_path();
-        if (!parent.empty()) std::filesystem::create_directories(parent);
         std::ofstream file(temporary, std::ios::binary | std::ios::trunc);
         if (!file) throw Error(MDN_ERR_IO, "cannot write challenge sampler state: " + temporary);
-        write_exact(file, &header, sizeof(header));
-        write_exact(file, scores_.data(), scores_.size() * sizeof(float));
-        write_exact(file, last_visit_.data(), last_visit_.size() * sizeof(uint64_t));
-        write_exact(file, last_score_.data(), last_score_.size() * sizeof(uint64_t));
-        write_exact(file, completed_.data(), completed_.size() * sizeof(uint64_t));
-        write_exact(file, episode_abs_gae_.data(), episode_abs_gae_.size() * sizeof(double));
-        write_exact(file, episode_count_.data(), episode_count_.size() * sizeof(uint32_t));
-        write_exact(file, episode_level_.data(), episode_level_.size() * sizeof(uint32_t));
-        write_exact(file, active_.data(), active_.size() * sizeof(uint32_t));
+        std::vector<ByteSpan> parts{{const_cast<SidecarHeader*>(&header), sizeof(header)}};
+        for (const ByteSpan& b : sidecar_body(ledger_, open_, active_)) parts.push_back(b);
+        for (const ByteSpan& b : parts) file.write(static_cast<const char*>(b.data), std::streamsize(b.bytes));
         file.flush();
         if (!file) throw Error(MDN_ERR_IO, "challenge sampler state write failed: " + temporary);
         file.close();
@@ -784,161 +852,174 @@ public:
             throw Error(MDN_ERR_IO, "cannot replace challenge sampler state: " + path);
     }
 
+    // The state is read into copies and checked before it replaces the live
+    // one, so a rejected sidecar leaves the sampler unchanged.
     void load_state(const std::string& path, const std::string& checkpoint_sha256, uint64_t completed_rollouts,
                     uint32_t* active_out) {
         std::ifstream file(path, std::ios::binary);
         if (!file) throw Error(MDN_ERR_IO, "cannot open challenge sampler state: " + path);
-        DiskHeader header{};
-        read_exact(file, &header, sizeof(header));
-        validate_header(header, checkpoint_sha256, completed_rollouts);
-        // Read into copies: a rejected file leaves the sampler as it was.
-        std::vector<float> scores(scores_.size());
-        std::vector<uint64_t> last_visit(last_visit_.size()), last_score(last_score_.size()), completed(completed_.size());
-        std::vector<double> abs_gae(episode_abs_gae_.size());
-        std::vector<uint32_t> count(episode_count_.size()), level(episode_level_.size()),
-            active(settings_.environment_count);
-        read_exact(file, scores.data(), scores.size() * sizeof(float));
-        read_exact(file, last_visit.data(), last_visit.size() * sizeof(uint64_t));
-        read_exact(file, last_score.data(), last_score.size() * sizeof(uint64_t));
-        read_exact(file, completed.data(), completed.size() * sizeof(uint64_t));
-        read_exact(file, abs_gae.data(), abs_gae.size() * sizeof(double));
-        read_exact(file, count.data(), count.size() * sizeof(uint32_t));
-        read_exact(file, level.data(), level.size() * sizeof(uint32_t));
-        read_exact(file, active.data(), active.size() * sizeof(uint32_t));
+        SidecarHeader header{};
+        read_span(file, {&header, sizeof(header)});
+        if (!header_matches(header, checkpoint_sha256, completed_rollouts))
+            throw Error(MDN_ERR_MISMATCH,
+                        "challenge sampler sidecar does not match bank, world, PPO checkpoint, or rollout");
+        LevelLedger ledger;
+        ledger.reset(bank_.levels.size());
+        OpenEpisodes open;
+        open.reset(settings_.environment_count);
+        std::vector<uint32_t> active(settings_.environment_count);
+        for (const ByteSpan& b : sidecar_body(ledger, open, active)) read_span(file, b);
         char extra;
         if (file.read(&extra, 1)) throw Error(MDN_ERR_MISMATCH, "challenge sampler state has trailing bytes");
-        for (size_t i = 0; i < scores.size(); ++i) {
-            if (!std::isfinite(scores[i]) || scores[i] < 0.0f || last_visit[i] > header.last_rollout ||
-                last_score[i] > header.last_rollout)
-                throw Error(MDN_ERR_MISMATCH, "challenge sampler sidecar has invalid priority data");
+        for (size_t i = 0; i < ledger.score.size(); ++i) {
+            const bool sane = std::isfinite(ledger.score[i]) && ledger.score[i] >= 0.0f &&
+                              ledger.visited[i] <= header.last_rollout && ledger.scored[i] <= header.last_rollout;
+            if (!sane) throw Error(MDN_ERR_MISMATCH, "challenge sampler sidecar has invalid priority data");
         }
-        for (uint32_t env = 0; env < settings_.environment_count; env++) validate_active_id(env, active[env]);
+        for (uint32_t env = 0; env < settings_.environment_count; env++) check_active(env, active[env]);
         for (uint32_t env = 0; env < settings_.environment_count; ++env) {
-            const uint32_t partial = level[env];
-            if (!std::isfinite(abs_gae[env]) || abs_gae[env] < 0.0 || ((count[env] == 0) != (partial == kInvalidLevel)))
+            const bool has_open = open.level[env] != kInvalidLevel;
+            if (!std::isfinite(open.abs_gae[env]) || open.abs_gae[env] < 0.0 || has_open != (open.samples[env] != 0))
                 throw Error(MDN_ERR_MISMATCH, "challenge sampler sidecar has invalid partial-episode state");
-            if (partial != kInvalidLevel && partial != active[env])
+            if (has_open && open.level[env] != active[env])
                 throw Error(MDN_ERR_MISMATCH, "challenge active id does not match partial episode score state");
         }
-        scores_.swap(scores);
-        last_visit_.swap(last_visit);
-        last_score_.swap(last_score);
-        completed_.swap(completed);
-        episode_abs_gae_.swap(abs_gae);
-        episode_count_.swap(count);
-        episode_level_.swap(level);
+        std::swap(ledger_, ledger);
+        std::swap(open_, open);
         active_.swap(active);
-        rng_ = header.rng_state;
+        rng_.state = header.rng_state;
         last_rollout_ = header.last_rollout;
         std::copy(active_.begin(), active_.end(), active_out);
     }
 
 private:
-    // 256-byte sidecar header (challenge_training.hpp:281-287).
-    struct DiskHeader {
-        char magic[8];
-        uint32_t version, selection, environment_count, horizon, level_count, rng_state, focus_family, reserved;
-        uint64_t last_rollout, completed_rollouts;
-        float uniform_floor, score_staleness_mix;
-        char bank_hash[64], world_hash[64], checkpoint_hash[64];
-    };
-    static_assert(sizeof(DiskHeader) == 256, "challenge sidecar header layout");
-    static constexpr uint32_t kStateVersion = 3;
-
     mdn_challenge_settings settings_;
-    BankData bank_;
     std::string world_hash_;
-    std::vector<uint32_t> families_;
-    std::map<uint32_t, std::vector<uint32_t>> family_levels_;
-    std::map<uint32_t, std::vector<double>> family_weights_;
-    std::vector<float> scores_;
-    std::vector<uint64_t> last_visit_, last_score_, completed_;
-    std::vector<double> episode_abs_gae_;
-    std::vector<uint32_t> episode_count_, episode_level_, active_;
-    uint32_t rng_ = 1;
+    BankData bank_;
+    std::array<FamilyPool, 3> pools_;  // families 14, 15, 16
+    LevelLedger ledger_;
+    OpenEpisodes open_;
+    std::vector<uint32_t> active_;
+    SamplerRng rng_;
     uint64_t last_rollout_ = 0;
 
-    uint32_t random_u32() {  // xorshift32, never zero
-        uint32_t x = rng_ ? rng_ : 1;
-        x ^= x << 13;
-        x ^= x >> 17;
-        x ^= x << 5;
-        rng_ = x ? x : 1;
-        return rng_;
+    static void check_settings(const mdn_challenge_settings& s) {
+        auto fail = [](const char* m) { throw Error(MDN_ERR_INVALID, m); };
+        if (s.environment_count == 0 || s.horizon == 0) fail("challenge training needs nonzero environments and horizon");
+        if (s.environment_count < 3 || s.rehearsal_environments > s.environment_count - 3)
+            fail("rehearsal must leave at least three bank environments");
+        if (s.focus_family != 0u && (s.focus_family < 14u || s.focus_family > 16u))
+            fail("focused challenge family must be 14, 15, 16, or 0 for balanced");
+        if (s.selection > 1u) fail("unsupported challenge level selection mode");
+        if (!(s.uniform_floor >= 0.5f && s.uniform_floor <= 1.0f))
+            fail("failure-weighted replay uniform floor must be in [0.5,1]");
+        if (!(s.score_staleness_mix >= 0.0f && s.score_staleness_mix <= 1.0f))
+            fail("score/staleness mix must be in [0,1]");
+        // a schedule holds environment_count x (horizon + 1) ids; keep it addressable
+        if (uint64_t(s.environment_count) * (uint64_t(s.horizon) + 1) > (uint64_t(1) << 31))
+            fail("challenge schedule larger than 2^31 slots");
     }
-    double uniform() { return double(random_u32()) / 4294967296.0; }
-    uint32_t uniform_index(const std::vector<uint32_t>& candidates) {
-        return candidates[(uint64_t(random_u32()) * candidates.size()) >> 32];
+
+    void build_pools() {
+        std::set<uint32_t> families;
+        for (size_t i = 0; i < 3; i++) pools_[i].family = 14u + uint32_t(i);
+        for (uint32_t i = 0; i < bank_.levels.size(); ++i) {
+            const Level& level = bank_.levels[i];
+            if (level.split != "train") throw Error(MDN_ERR_INVALID, "train loader returned a non-train challenge level");
+            families.insert(level.info.family);
+            if (level.info.family >= 14u && level.info.family <= 16u) pools_[level.info.family - 14u].levels.push_back(i);
+        }
+        if (families.size() < 3) throw Error(MDN_ERR_INVALID, "train bank must contain each family 14, 15, and 16");
+        for (const FamilyPool& pool : pools_)
+            if (pool.levels.empty())
+                throw Error(MDN_ERR_INVALID, "train bank is missing family " + std::to_string(pool.family));
     }
-    uint32_t family_for_env(uint32_t env) const {
-        if (settings_.focus_family != 0u) return settings_.focus_family;
-        return families_[(env - settings_.rehearsal_environments) % families_.size()];
+
+    bool is_rehearsal(uint32_t env) const { return env < settings_.rehearsal_environments; }
+    const FamilyPool& pool_of(uint32_t env) const {
+        if (settings_.focus_family != 0u) return pools_[settings_.focus_family - 14u];
+        return pools_[(env - settings_.rehearsal_environments) % 3u];
     }
-    void validate_active_id(uint32_t env, uint32_t id) const {
-        if (env < settings_.rehearsal_environments) {
+
+    void check_active(uint32_t env, uint32_t id) const {
+        if (is_rehearsal(env)) {
             if (id != kInvalidLevel) throw Error(MDN_ERR_INVALID, "rehearsal environment contains a bank level");
             return;
         }
         if (id >= bank_.levels.size()) throw Error(MDN_ERR_INVALID, "active challenge id is outside the train bank");
-        if (bank_.levels[id].info.family != family_for_env(env))
+        if (bank_.levels[id].info.family != pool_of(env).family)
             throw Error(MDN_ERR_INVALID, "active challenge id violates its fixed per-environment family quota");
     }
-    // Rank mixture of failure score (high first) and staleness (oldest visit
-    // first), ties by level index (challenge_training.hpp:326-354).
-    void refresh_priorities() {
-        family_weights_.clear();
-        if (settings_.selection != 1u) return;
-        std::vector<uint32_t> score_position(bank_.levels.size()), age_position(bank_.levels.size());
-        for (uint32_t family : families_) {
-            const auto& candidates = family_levels_.at(family);
-            std::vector<uint32_t> score_rank = candidates, age_rank = candidates;
-            std::stable_sort(score_rank.begin(), score_rank.end(), [&](uint32_t a, uint32_t b) {
-                if (scores_[a] != scores_[b]) return scores_[a] > scores_[b];
-                return a < b;
+
+    void fill_row(uint32_t env, uint32_t* row, uint32_t first_slot) {
+        uint32_t* end = row + settings_.horizon + 1;
+        if (is_rehearsal(env)) {
+            std::fill(row + first_slot, end, kInvalidLevel);
+            return;
+        }
+        const FamilyPool& pool = pool_of(env);
+        for (uint32_t* slot = row + first_slot; slot != end; ++slot) *slot = draw(pool);
+    }
+
+    uint32_t draw(const FamilyPool& pool) {
+        // the floor's draw is taken only under failure-weighted selection
+        const bool weighted = settings_.selection == 1u && !(rng_.unit() < settings_.uniform_floor);
+        if (!weighted) return pool.levels[rng_.below(pool.levels.size())];
+        double remainder = rng_.unit() * pool.weight_total;
+        const size_t last = pool.levels.size() - 1;
+        for (size_t i = 0; i < last; ++i) {
+            remainder -= pool.weight[i];
+            if (remainder <= 0.0) return pool.levels[i];
+        }
+        return pool.levels[last];
+    }
+
+    void refresh_weights() {
+        const double mix = settings_.score_staleness_mix;
+        for (FamilyPool& pool : pools_) {
+            pool.weight.clear();
+            pool.weight_total = 0.0;
+            if (settings_.selection != 1u) continue;
+            const std::vector<float>& score = ledger_.score;
+            const std::vector<uint64_t>& visited = ledger_.visited;
+            const auto by_score = pool_ranks(pool.levels, [&](uint32_t a, uint32_t b) {
+                return score[a] != score[b] ? score[a] > score[b] : a < b;
             });
-            std::stable_sort(age_rank.begin(), age_rank.end(), [&](uint32_t a, uint32_t b) {
-                if (last_visit_[a] != last_visit_[b]) return last_visit_[a] < last_visit_[b];
-                return a < b;
+            const auto by_age = pool_ranks(pool.levels, [&](uint32_t a, uint32_t b) {
+                return visited[a] != visited[b] ? visited[a] < visited[b] : a < b;
             });
-            for (uint32_t rank = 0; rank < candidates.size(); ++rank) {
-                score_position[score_rank[rank]] = rank;
-                age_position[age_rank[rank]] = rank;
-            }
-            auto& weights = family_weights_[family];
-            weights.resize(candidates.size());
-            for (size_t i = 0; i < candidates.size(); ++i) {
-                const uint32_t level = candidates[i];
-                weights[i] = settings_.score_staleness_mix / double(score_position[level] + 1) +
-                             (1.0 - settings_.score_staleness_mix) / double(age_position[level] + 1);
+            pool.weight.resize(pool.levels.size());
+            for (size_t i = 0; i < pool.levels.size(); ++i) {
+                pool.weight[i] = mix / double(by_score[i] + 1) + (1.0 - mix) / double(by_age[i] + 1);
+                pool.weight_total += pool.weight[i];
             }
         }
     }
-    uint32_t sample_level_for_family(uint32_t family) {
-        const auto& candidates = family_levels_.at(family);
-        if (settings_.selection == 0u || uniform() < settings_.uniform_floor) return uniform_index(candidates);
-        const auto& weights = family_weights_.at(family);
-        double total = 0;
-        for (double weight : weights) total += weight;
-        double target = uniform() * total;
-        for (size_t i = 0; i < candidates.size(); ++i) {
-            target -= weights[i];
-            if (target <= 0) return candidates[i];
-        }
-        return candidates.back();
+
+    void close_episode(uint32_t env, uint32_t level, uint64_t rollout_index) {
+        const uint32_t samples = open_.samples[env];
+        if (samples == 0) throw Error(MDN_ERR_INVALID, "completed challenge episode has no GAE samples");
+        ledger_.score[level] = float(open_.abs_gae[env] / samples);
+        ledger_.scored[level] = rollout_index;
+        ledger_.completed[level] += 1;
+        open_.abs_gae[env] = 0.0;
+        open_.samples[env] = 0;
+        open_.level[env] = kInvalidLevel;
     }
-    DiskHeader make_header(const std::string& checkpoint_hash, uint64_t completed_rollouts) const {
+
+    SidecarHeader sidecar_header(const std::string& checkpoint_hash, uint64_t completed_rollouts) const {
         if (checkpoint_hash.size() != 64)
             throw Error(MDN_ERR_INVALID, "challenge state requires a SHA-256 checkpoint hash");
-        DiskHeader h{};
-        std::memcpy(h.magic, "CHTRN1\0", 8);
-        h.version = kStateVersion;
+        SidecarHeader h{};
+        std::memcpy(h.magic, kSidecarMagic, 8);
+        h.version = kSidecarVersion;
         h.selection = settings_.selection;
         h.environment_count = settings_.environment_count;
         h.horizon = settings_.horizon;
         h.level_count = uint32_t(bank_.levels.size());
-        h.reserved = settings_.rehearsal_environments;
-        h.rng_state = rng_;
+        h.rng_state = rng_.state;
         h.focus_family = settings_.focus_family;
+        h.rehearsal = settings_.rehearsal_environments;
         h.last_rollout = last_rollout_;
         h.completed_rollouts = completed_rollouts;
         h.uniform_floor = settings_.uniform_floor;
@@ -948,33 +1029,31 @@ private:
         std::memcpy(h.checkpoint_hash, checkpoint_hash.data(), 64);
         return h;
     }
-    void validate_header(const DiskHeader& h, const std::string& checkpoint_hash, uint64_t completed_rollouts) const {
-        const bool rollout_pair_matches =
-            completed_rollouts == 0 ? h.last_rollout == 0 : h.last_rollout + 1 == completed_rollouts;
-        const bool known_version = h.version == 1u || h.version == 2u || h.version == kStateVersion;
-        const bool focus_matches = h.version == kStateVersion ? h.focus_family == settings_.focus_family
-                                                              : h.focus_family == 0u && settings_.focus_family == 0u;
-        if (std::memcmp(h.magic, "CHTRN1\0", 8) != 0 || !known_version || !focus_matches ||
-            h.selection != settings_.selection || h.environment_count != settings_.environment_count ||
-            h.horizon != settings_.horizon || h.level_count != bank_.levels.size() ||
-            h.completed_rollouts != completed_rollouts || !rollout_pair_matches || (h.version == 1 && h.reserved != 0) ||
-            h.reserved != settings_.rehearsal_environments || h.rng_state == 0 ||
-            std::fabs(h.uniform_floor - settings_.uniform_floor) > 1e-7f ||
-            std::fabs(h.score_staleness_mix - settings_.score_staleness_mix) > 1e-7f ||
-            std::memcmp(h.bank_hash, bank_.bank_hash.data(), 64) != 0 ||
-            std::memcmp(h.world_hash, world_hash_.data(), 64) != 0 || !is_sha256(checkpoint_hash) ||
-            std::memcmp(h.checkpoint_hash, checkpoint_hash.data(), 64) != 0)
-            throw Error(MDN_ERR_MISMATCH,
-                        "challenge sampler sidecar does not match bank, world, PPO checkpoint, or rollout");
+
+    // The header must describe this sampler, this bank and world, the given
+    // checkpoint, and the rollout boundary the checkpoint was taken at.
+    bool header_matches(const SidecarHeader& h, const std::string& checkpoint_hash, uint64_t completed_rollouts) const {
+        const auto& s = settings_;
+        const bool current = h.version == kSidecarVersion;
+        if (std::memcmp(h.magic, kSidecarMagic, 8) != 0 || h.version < 1u || h.version > kSidecarVersion) return false;
+        // before version 3 the field was zero and no focus family existed
+        if (current ? h.focus_family != s.focus_family : (h.focus_family != 0u || s.focus_family != 0u)) return false;
+        if (h.version == 1u && h.rehearsal != 0u) return false;
+        if (h.selection != s.selection || h.environment_count != s.environment_count || h.horizon != s.horizon ||
+            h.level_count != bank_.levels.size() || h.rehearsal != s.rehearsal_environments || h.rng_state == 0u)
+            return false;
+        const uint64_t expected_last = completed_rollouts == 0 ? 0 : completed_rollouts - 1;
+        if (h.completed_rollouts != completed_rollouts || h.last_rollout != expected_last) return false;
+        if (std::fabs(h.uniform_floor - s.uniform_floor) > 1e-7f ||
+            std::fabs(h.score_staleness_mix - s.score_staleness_mix) > 1e-7f)
+            return false;
+        return std::memcmp(h.bank_hash, bank_.bank_hash.data(), 64) == 0 &&
+               std::memcmp(h.world_hash, world_hash_.data(), 64) == 0 && is_sha256(checkpoint_hash) &&
+               std::memcmp(h.checkpoint_hash, checkpoint_hash.data(), 64) == 0;
     }
-    template <typename T>
-    static void write_exact(std::ofstream& file, const T* values, size_t bytes) {
-        file.write(reinterpret_cast<const char*>(values), std::streamsize(bytes));
-        if (!file) throw Error(MDN_ERR_IO, "challenge sampler state write failed");
-    }
-    template <typename T>
-    static void read_exact(std::ifstream& file, T* values, size_t bytes) {
-        file.read(reinterpret_cast<char*>(values), std::streamsize(bytes));
+
+    static void read_span(std::ifstream& file, const ByteSpan& b) {
+        file.read(static_cast<char*>(b.data), std::streamsize(b.bytes));
         if (!file) throw Error(MDN_ERR_MISMATCH, "challenge sampler state is truncated");
     }
 };

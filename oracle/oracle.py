@@ -18,6 +18,12 @@ HERE = pathlib.Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libref_oracle.so"
 
+
+def reference_root(override=None):
+    """The reference checkout: `override`, else $MDN_REFERENCE, else a folder
+    named `reference` beside this repository (the layout the build used)."""
+    return pathlib.Path(override or os.environ.get("MDN_REFERENCE") or HERE.parents[1] / "reference")
+
 _P = ctypes.c_void_p
 _F = ctypes.c_float
 _U = ctypes.c_uint32
@@ -27,10 +33,10 @@ def ptr(a):
     return a.ctypes.data_as(_P) if a is not None else None
 
 
-def build(reference_root=None):
+def build(reference_root_override=None):
     """Compile liboracle.so, and oracle/_ref when the reference sources exist."""
     subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
-    ref = pathlib.Path(reference_root or os.environ.get("MDN_REFERENCE", "/root/reference"))
+    ref = reference_root(reference_root_override)
     if (ref / "cpu_reference.hpp").exists():
         subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref}"], check=True)
 

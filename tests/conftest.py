@@ -1,5 +1,6 @@
 """Shared fixtures. `gpu` marks tests that need a CUDA device (run on a B200)."""
 import importlib.util
+import os
 import pathlib
 import sys
 
@@ -8,6 +9,9 @@ import pytest
 
 ROOT = pathlib.Path(__file__).resolve().parents[1]
 GOLDEN = ROOT / "tests" / "golden"
+# The reference checkout (read only by CPU pin tests that skip without it):
+# $MDN_REFERENCE, else a folder named `reference` beside this repository.
+REFERENCE = pathlib.Path(os.environ.get("MDN_REFERENCE") or ROOT.parent / "reference")
 
 
 def pytest_configure(config):

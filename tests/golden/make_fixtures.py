@@ -1,6 +1,7 @@
 """Regenerate the golden fixtures in this folder from the reference checkout.
 
-Run in a container that has the reference sources (default /root/reference):
+Run where the reference sources are present ($MDN_REFERENCE, else a folder
+named `reference` beside this repository):
     python tests/golden/make_fixtures.py [reference_root]
 
 Copies, byte for byte, the reference's golden data files that the tests
@@ -34,8 +35,9 @@ def _load(name, path, pkg_dir=None):
     return mod
 
 
-def main(ref_root="/root/reference"):
-    ref = pathlib.Path(ref_root)
+def main(ref_root=None):
+    import os
+    ref = pathlib.Path(ref_root or os.environ.get("MDN_REFERENCE") or ROOT.parent / "reference")
     shutil.copyfile(ref / "assets" / "raptor.bin", HERE / "raptor.bin")
     shutil.copyfile(ref / "assets" / "physics.bin", HERE / "physics.bin")
     (ROOT / "metal-drone-nav_b200" / "assets").mkdir(parents=True, exist_ok=True)

@@ -20,11 +20,11 @@ import pathlib
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, ROOT, _load_module, load_oracle_module, load_package
+from conftest import GOLDEN, REFERENCE, ROOT, _load_module, load_oracle_module, load_package
 
 SMALL = GOLDEN / "challenge_bank_small.jsonl"
 MIRRORED = GOLDEN / "challenge_bank_mirrored_small.jsonl"
-REFERENCE_BANKS = pathlib.Path("/root/reference/evidence/inputs")
+REFERENCE_BANKS = REFERENCE / "evidence" / "inputs"
 INVALID = 0xFFFFFFFF
 
 
@@ -70,14 +70,14 @@ def test_reference_bank_files(name):
     assert total == len((REFERENCE_BANKS / f"{name}.jsonl").read_text().splitlines())
 
 
-@pytest.mark.skipif(not pathlib.Path("/root/reference/challenge_bank.py").exists(),
+@pytest.mark.skipif(not (REFERENCE / "challenge_bank.py").exists(),
                     reason="reference generator not on this machine")
 def test_fixtures_come_from_the_reference_generator(tmp_path):
     import importlib.util
-    spec = importlib.util.spec_from_file_location("rcb", "/root/reference/challenge_bank.py")
+    spec = importlib.util.spec_from_file_location("rcb", str(REFERENCE / "challenge_bank.py"))
     gen = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(gen)
-    h = hashlib.sha256(pathlib.Path("/root/reference/world.hpp").read_bytes()).hexdigest()
+    h = hashlib.sha256((REFERENCE / "world.hpp").read_bytes()).hexdigest()
     records = gen.build_records(20261001, 4, 8.0, [14, 15, 16], h, False)
     text = "".join(json.dumps(r, sort_keys=True, separators=(",", ":")) + "\n" for r in records)
     assert text == SMALL.read_text()

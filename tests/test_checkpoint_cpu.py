@@ -11,9 +11,9 @@ import pathlib
 import numpy as np
 import pytest
 
-from conftest import load_package
+from conftest import REFERENCE, load_package
 
-CKPTS = pathlib.Path("/root/reference/assets/checkpoints")
+CKPTS = REFERENCE / "assets" / "checkpoints"
 
 
 def v6_bytes(h):

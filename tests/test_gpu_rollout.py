@@ -243,15 +243,24 @@ def test_rejects_unsupported_config(pkg, raptor):
         pkg.Sim(pkg_device(), pkg.layouts.default_config(n=0), 4, raptor=raptor)
 
 
-@pytest.mark.parametrize("threads", [1, 4])
-def test_actor_kernels_match_oracle(pkg, om, raptor, threads, monkeypatch):
+ACTOR_CASES = [(1, 320, {}), (4, 320, {}),
+               # a partial last 64-environment pass of the quad actor's staged rows
+               (4, 333, {}),
+               # more than 2 x SMs x 64 environments: quad blocks loop over several passes
+               (4, 19000, {}),
+               # evaluation mode skips environments whose episode has finished
+               (4, 333, dict(eval=1, max_steps=3)), (1, 333, dict(eval=1, max_steps=3))]
+
+
+@pytest.mark.parametrize("threads,n,extra", ACTOR_CASES, ids=[f"t{t}-n{n}-{e}" for t, n, e in ACTOR_CASES])
+def test_actor_kernels_match_oracle(pkg, om, raptor, threads, n, extra, monkeypatch):
     """Both 64-unit actor kernels (one thread per environment, and four threads
     per environment for small shards; MDN_ACT_THREADS picks one at simulator
     creation) against the oracle, teacher-forced."""
     monkeypatch.setenv("MDN_ACT_THREADS", str(threads))
-    n, T = 320, 6
-    cfg = pkg.layouts.default_config(n=n, family=18, speed=1.0, distance=3.0, seed=13, sensor_delay=2,
-                                     command_delay=2, mode=17)
+    T = 6
+    cfg = pkg.layouts.default_config(**{**dict(n=n, family=18, speed=1.0, distance=3.0, seed=13, sensor_delay=2,
+                                               command_delay=2, mode=17), **extra})
     gpu, ora = make_pair(pkg, om, raptor, cfg, T)
     try:
         for t in range(T):
