@@ -327,6 +327,13 @@ int mdn_sim_validate_tasks(mdn_sim* sim);
  * observation, reward or termination (those keep the 0.18 m sphere contact).
  * safety_margin_m: 0.04 = VG_DEFAULT_SAFETY_MARGIN_M. enabled = 0 turns it off. */
 int mdn_sim_set_contact_audit(mdn_sim* sim, int enabled, float safety_margin_m);
+/* Delay rehearsal: the reference's NAV_DELAY_REHEARSAL build switch of its
+ * delay-training target (sim.metal:14-24, cpu_reference.hpp:1-3,219-223,
+ * CMakeLists.txt:72-76), here a run-time switch per simulator. While it is on
+ * and cfg.mode == 22 (not evaluation), environments with (global id / 4) even
+ * train "clean": no sensor or command delay, wind, depth noise or dropout.
+ * Off by default, as in every other reference build. */
+int mdn_sim_set_delay_rehearsal(mdn_sim* sim, int enabled);
 /* ChallengeBankControl (sim.metal:13, challenge_training.hpp:33-38). */
 typedef struct mdn_bank_control {
     uint32_t enabled, bank_count, schedule_stride, horizon;

@@ -67,6 +67,7 @@ SIGNATURES = {
     "mdn_policy_write": (ctypes.c_int, [ctypes.c_char_p, _P, _U, ctypes.c_char_p, ctypes.c_float]),
     "mdn_sim_export_policy": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_float]),
     "mdn_sim_set_contact_audit": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_float]),
+    "mdn_sim_set_delay_rehearsal": (ctypes.c_int, [_P, ctypes.c_int]),
     "mdn_device_fp32_peak": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_double)]),
     "mdn_selftest_division": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
     "mdn_ppo_create": (ctypes.c_int, [_P, _U, _U, ctypes.POINTER(_P)]),
@@ -298,6 +299,12 @@ class Sim:
     def set_contact_audit(self, enabled=True, safety_margin_m=0.04):
         """Per-step mechanical contact audit into buffer 'contact_audit' [T][n]."""
         check(lib().mdn_sim_set_contact_audit(self.h, 1 if enabled else 0, safety_margin_m))
+
+    def set_delay_rehearsal(self, enabled=True):
+        """NAV_DELAY_REHEARSAL (sim.metal:14-24) as a run-time switch: under
+        mode 22, environments with (global id / 4) even train without delays,
+        wind, depth noise or dropout."""
+        check(lib().mdn_sim_set_delay_rehearsal(self.h, 1 if enabled else 0))
 
     def export_policy(self, path, source_checkpoint, max_speed_mps=1.5):
         """Deployable actor file (NAVPOL1, or NAVWID4 for a wide actor)."""

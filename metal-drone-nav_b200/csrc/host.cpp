@@ -235,6 +235,7 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
     a.wide_slices = wide ? actor_hidden / 128 : 0;
     a.audit = audit_enabled ? static_cast<mdn_contact_audit*>(buf[MDN_BUF_CONTACT_AUDIT]) : nullptr;
     a.audit_margin = audit_margin;
+    a.delay_rehearsal = delay_rehearsal ? 1u : 0u;
     a.bank_enabled = bank.enabled;
     a.bank_count = bank.enabled ? bank.bank_count : 0;
     a.bank_stride = bank.schedule_stride;
@@ -557,6 +558,15 @@ extern "C" int mdn_sim_set_contact_audit(mdn_sim* sim, int enabled, float safety
         }
         sim->audit_enabled = enabled != 0;
         sim->audit_margin = safety_margin_m;
+        sim->release_graphs();  // kernel arguments are captured by value
+    });
+}
+
+extern "C" int mdn_sim_set_delay_rehearsal(mdn_sim* sim, int enabled) {
+    return guarded([&] {
+        checked(sim);
+        cuda_check(cudaStreamSynchronize(sim->stream), "delay rehearsal");
+        sim->delay_rehearsal = enabled != 0;
         sim->release_graphs();  // kernel arguments are captured by value
     });
 }

@@ -92,6 +92,7 @@ struct mdn_sim {
     float* wide_partials = nullptr;                         // [hidden/128][n][4] slice sums of the wide forward
     uint32_t* wide_error = nullptr;                         // barrier-timeout flag of the wide kernels
     mdn::WideStep* wide = nullptr;                          // tensor maps + launch arguments (wide actors)
+    bool delay_rehearsal = false;                           // mdn_sim_set_delay_rehearsal
     bool audit_enabled = false;                             // mechanical contact audit (mdn_sim_set_contact_audit)
     float audit_margin = 0.04f;
     mdn_bank_control bank{};                                // frozen challenge bank (mdn_sim_set_challenge_bank)

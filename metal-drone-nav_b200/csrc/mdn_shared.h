@@ -44,6 +44,10 @@ struct SimArgs {
     mdn_sim_config cfg;
     uint32_t n;          // local environments on this GPU
     uint32_t env_base;   // global id of local env 0 (seeds, clean-env parity)
+    // Delay rehearsal (NAV_DELAY_REHEARSAL of the reference's delay-training
+    // build): under mode 22, every other group of four environments trains
+    // without delays, wind or depth noise.
+    uint32_t delay_rehearsal;
     uint32_t tick;       // row block tick*n .. tick*n+n-1
     float room_lo[3], room_hi[3], room_c[3], room_e[3];
     mdn_physics_state* states;

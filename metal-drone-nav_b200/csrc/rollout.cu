@@ -182,8 +182,8 @@ __global__ void __launch_bounds__(kSenseWarps * 32, 4) k_sense(SimArgs a) {
     if (steps % c.sensor_period == 0) {
         const uint32_t frame = (steps / c.sensor_period) % kFrames;
         const float ox = pos[0] + 0.0f * r[0], oy = pos[1] + 0.0f * r[3], oz = pos[2] + 0.0f * r[6];  // mount 0
-        const float noise = clean_env(c, gid) ? 0.0f : c.depth_noise;
-        const float dropout = clean_env(c, gid) ? 0.0f : c.dropout;
+        const float noise = clean_env(a, gid) ? 0.0f : c.depth_noise;
+        const float dropout = clean_env(a, gid) ? 0.0f : c.dropout;
         // Visibility cull, one obstacle per lane: the obstacle's bounding sphere
         // (inflated by 0.01% + 1 mm, far above the float error of the exact
         // tests) must reach into the camera frustum |y| <= x, |z| <= 0.75 x
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kSenseWarps * 32, 4) k_sense(SimArgs a) {
     }
 
     // ---- observation (sim_observe)
-    const uint32_t delay = clean_env(c, gid) ? 0u : c.sensor_delay;
+    const uint32_t delay = clean_env(a, gid) ? 0u : c.sensor_delay;
     const uint32_t available = steps / c.sensor_period;
     const uint32_t frame = available > delay ? available - delay : 0;
     const uint32_t prevf = frame > 0 ? frame - 1 : 0;
@@ -524,7 +524,7 @@ __global__ void __launch_bounds__(kMemWarps * 32) k_memory_hint(SimArgs a) {
     rotation(q, r);
     const size_t row = size_t(a.tick) * a.n + i;
     float* obs = a.obs + row * kActorObs;
-    const uint32_t delay = clean_env(c, gid) ? 0u : c.sensor_delay;
+    const uint32_t delay = clean_env(a, gid) ? 0u : c.sensor_delay;
     const uint32_t available = steps / c.sensor_period;
     const uint32_t frame = available > delay ? available - delay : 0;
     const uint32_t valid = available >= delay ? min(frame + 1u, uint32_t(kFrames) - delay) : 0u;
@@ -806,7 +806,7 @@ __device__ __forceinline__ void act_finish_body(const SimArgs& a, uint32_t i, si
         slot[3] = 0.0f;
     }
     const uint32_t gid = a.env_base + i;
-    const uint32_t delay = clean_env(c, gid) ? 0u : c.command_delay;
+    const uint32_t delay = clean_env(a, gid) ? 0u : c.command_delay;
     const uint32_t applied = steps > delay ? steps - delay : 0;
     float pn[4];
     for (int j = 0; j < 4; j++) {

@@ -313,7 +313,7 @@ __device__ __noinline__ bool episode_reset(const SimArgs& a, uint32_t i, bool fi
                 run.reference_position[ax] = s.position[ax];
                 run.desired_velocity[ax] = s.linear_velocity[ax];
             }
-            w.wind[0] = clean_env(a.cfg, gid) ? 0.0f : a.cfg.wind;
+            w.wind[0] = clean_env(a, gid) ? 0.0f : a.cfg.wind;
             w.wind[1] = 0;
             w.wind[2] = 0;
         }

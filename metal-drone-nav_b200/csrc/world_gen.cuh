@@ -361,9 +361,15 @@ __device__ __forceinline__ uint32_t training_family(uint32_t family, uint32_t& r
     return family;
 }
 
-// Clean-sensing training environments (sim.metal:17-21, NAV_DELAY_REHEARSAL 0).
-__device__ __forceinline__ bool clean_env(const mdn_sim_config& c, uint32_t gid) {
-    return c.eval == 0 && ((c.family == 12 || c.family == 13) && gid % 2 == 0);
+// Clean-sensing training environments (sim.metal:17-21): the even
+// environments of families 12 and 13 and, with delay rehearsal on, mode-22
+// environments of even four-environment groups. Never in evaluation.
+__device__ __forceinline__ bool clean_env(const SimArgs& a, uint32_t gid) {
+    const mdn_sim_config& c = a.cfg;
+    if (c.eval != 0) return false;
+    const bool clean_family = (c.family == 12 || c.family == 13) && gid % 2 == 0;
+    const bool rehearsal = a.delay_rehearsal != 0 && c.mode == 22 && (gid / 4) % 2 == 0;
+    return clean_family || rehearsal;
 }
 
 // Copy env i's obstacle block into the structure-of-arrays mirror.
@@ -406,7 +412,7 @@ __device__ bool reset_env(const SimArgs& a, uint32_t i, bool first, mdn_world& w
     uint32_t rng = first ? (c.seed + gid * 747796405u + 2891336453u) : run.rng;
     const uint32_t family = c.family == 18u ? mixed_lane_family(gid) : training_family(c.family, rng);
     generate_world(w, wrng(rng), family, c.distance);
-    w.wind[0] = clean_env(c, gid) ? 0.0f : c.wind;
+    w.wind[0] = clean_env(a, gid) ? 0.0f : c.wind;
     w.wind[1] = 0;
     w.wind[2] = 0;
     for (int j = 0; j < 3; j++) {
@@ -498,7 +504,7 @@ __device__ __forceinline__ void apply_challenge_world(const SimArgs& a, uint32_t
         if (level >= a.bank_count) return;
         w = a.bank_worlds[level];
     }
-    w.wind[0] = clean_env(a.cfg, gid) ? 0.0f : a.cfg.wind;
+    w.wind[0] = clean_env(a, gid) ? 0.0f : a.cfg.wind;
     w.wind[1] = 0;
     w.wind[2] = 0;
     run.initial_distance = len3(w.goal[0], w.goal[1], w.goal[2] - 1.5f);

@@ -1370,6 +1370,7 @@ struct o_sim {
     mdn_sim_config cfg;
     uint32_t horizon;
     uint32_t env_base; /* global id of local env 0 (a rank's shard) */
+    int delay_rehearsal; /* NAV_DELAY_REHEARSAL, off by default */
     mdn_raptor_weights raptor;
     mdn_physics_params physics;
     float room[6];
@@ -1394,6 +1395,7 @@ struct o_sim {
 };
 
 uint32_t o_actor_param_count(void) { return A_P; }
+void o_sim_set_delay_rehearsal(o_sim* s, int enabled) { s->delay_rehearsal = enabled != 0; }
 uint32_t o_critic_param_count(void) { return C_P; }
 void o_set_threads(int n) {
 #ifdef _OPENMP
@@ -1529,9 +1531,12 @@ void* o_sim_buffer(o_sim* s, int id, size_t* bytes) {
     }
 }
 
-/* sim.metal:17-36 (cpu_reference.hpp:219-238) with NAV_DELAY_REHEARSAL == 0. */
-static int clean_env(const mdn_sim_config* c, uint32_t n) {
-    return c->eval == 0 && ((c->family == 12 || c->family == 13) && n % 2 == 0);
+/* sim.metal:14-36 (cpu_reference.hpp:1-3,219-238); delay_rehearsal stands for
+ * the NAV_DELAY_REHEARSAL build switch. */
+static int clean_env(const o_sim* s, uint32_t n) {
+    const mdn_sim_config* c = &s->cfg;
+    return c->eval == 0 && (((c->family == 12 || c->family == 13) && n % 2 == 0) ||
+                            (s->delay_rehearsal && c->mode == 22 && (n / 4) % 2 == 0));
 }
 static void rotation(const float q[4], float r[9]) { /* sim.metal:43-48, cpu_reference.hpp:82-87 */
     const float w = q[0], x = q[1], y = q[2], z = q[3];
@@ -1661,7 +1666,7 @@ static void apply_challenge_world(o_sim* s, uint32_t n, uint32_t slot) {
         if (level >= b->bank_count) return;
         *w = s->bank_worlds[level];
     }
-    w->wind[0] = clean_env(&s->cfg, gid) ? 0.0f : s->cfg.wind;
+    w->wind[0] = clean_env(s, gid) ? 0.0f : s->cfg.wind;
     w->wind[1] = 0;
     w->wind[2] = 0;
     run->initial_distance = len3(w->goal[0], w->goal[1], w->goal[2] - 1.5f);
@@ -1684,7 +1689,7 @@ static void reset_one(o_sim* s, uint32_t n, int first, uint32_t slot) {
     uint32_t rng = first ? (c->seed + gid * 747796405u + 2891336453u) : run->rng;
     const uint32_t family = c->family == 18u ? o_mixed_lane_family(gid) : o_wtraining_family(c->family, &rng);
     o_wgenerate(w, o_wrng(&rng), family, c->distance);
-    w->wind[0] = clean_env(c, gid) ? 0.0f : c->wind;
+    w->wind[0] = clean_env(s, gid) ? 0.0f : c->wind;
     w->wind[1] = 0;
     w->wind[2] = 0;
     for (int j = 0; j < 3; j++) {
@@ -1767,7 +1772,7 @@ static void reset_one(o_sim* s, uint32_t n, int first, uint32_t slot) {
                 run->reference_position[a] = st->position[a];
                 run->desired_velocity[a] = st->linear_velocity[a];
             }
-            w->wind[0] = clean_env(c, gid) ? 0.0f : c->wind;
+            w->wind[0] = clean_env(s, gid) ? 0.0f : c->wind;
             w->wind[1] = 0;
             w->wind[2] = 0;
         }
@@ -1792,7 +1797,7 @@ static void depth_env(o_sim* s, uint32_t n) {
     pose[0] = origin[0]; pose[1] = origin[1]; pose[2] = origin[2];
     for (int j = 0; j < 9; j++) pose[3 + j] = r[j];
     const uint32_t gid = s->env_base + n;
-    const float noise = clean_env(c, gid) ? 0.0f : c->depth_noise, dropout = clean_env(c, gid) ? 0.0f : c->dropout;
+    const float noise = clean_env(s, gid) ? 0.0f : c->depth_noise, dropout = clean_env(s, gid) ? 0.0f : c->dropout;
     for (uint32_t k = 0; k < NPIX; k++) {
         const float* ray = s->pixel_rays + 3 * k;
         const float d[3] = {r[0] * ray[0] + r[1] * ray[1] + r[2] * ray[2], r[3] * ray[0] + r[4] * ray[1] + r[5] * ray[2],
@@ -1842,7 +1847,7 @@ static void observe_env(o_sim* s, uint32_t t, uint32_t n) {
     const mdn_world* w = &s->worlds[n];
     float r[9];
     rotation(st->orientation_wxyz, r);
-    const uint32_t delay = clean_env(c, s->env_base + n) ? 0 : c->sensor_delay;
+    const uint32_t delay = clean_env(s, s->env_base + n) ? 0 : c->sensor_delay;
     const uint32_t available = run->steps / c->sensor_period;
     const uint32_t frame = available > delay ? available - delay : 0;
     const uint32_t prev = frame > 0 ? frame - 1 : 0;
@@ -1996,7 +2001,7 @@ static void act_env(o_sim* s, uint32_t t, uint32_t n) {
                              (r[2] * d[0] + r[5] * d[1] + r[8] * d[2]) / c->speed, 0.0f};
         for (int j = 0; j < 4; j++) cmd[(run->steps % NFRAMES) * ACT + j] = sc[j];
     }
-    const uint32_t delay = clean_env(c, s->env_base + n) ? 0 : c->command_delay;
+    const uint32_t delay = clean_env(s, s->env_base + n) ? 0 : c->command_delay;
     const uint32_t applied = run->steps > delay ? run->steps - delay : 0;
     for (uint32_t j = 0; j < ACT; j++) run->previous_nav[j] = run->steps < delay ? 0.0f : cmd[(applied % NFRAMES) * ACT + j];
     float r[9];

@@ -72,6 +72,8 @@ void o_sim_rows_grad(o_sim* s, const uint32_t* rows, uint32_t count, float batch
 void o_sim_set_task_control(o_sim* s, const mdn_task_control* ctl);
 void o_sim_set_challenge_bank(o_sim* s, const mdn_world* worlds, const mdn_bank_control* ctl);
 void o_sim_set_runtime(o_sim* s, const mdn_runtime_config* rt);
+/* NAV_DELAY_REHEARSAL (sim.metal:14-24) as a switch; off after create. */
+void o_sim_set_delay_rehearsal(o_sim* s, int enabled);
 int o_physics_sample_domain(const mdn_physics_params* nominal, uint32_t* rng, float amplitude,
                             const mdn_domain_range* r, mdn_physics_params* varied, float* sample_out);
 uint32_t o_domain_episode_seed(const mdn_runtime_config* rt, uint32_t cfg_seed, uint32_t env, uint32_t episode);

@@ -90,6 +90,7 @@ def load_oracle():
     d("o_sim_set_task_control", None, _P, _P)
     d("o_sim_set_challenge_bank", None, _P, _P, _P)
     d("o_sim_set_runtime", None, _P, _P)
+    d("o_sim_set_delay_rehearsal", None, _P, ctypes.c_int)
     d("o_physics_sample_domain", ctypes.c_int, _P, _P, _F, _P, _P, _P)
     d("o_domain_episode_seed", _U, _P, _U, _U, _U)
     d("o_generate_task", _U, _P, _P, _P, _P, _P)
@@ -151,11 +152,14 @@ def load_ref_bank():
     return lib
 
 
-def load_ref():
-    """The compiled reference, or None when it was never built (no sources)."""
-    if not REF_SO.exists():
+def load_ref(rehearsal=False):
+    """The compiled reference, or None when it was never built (no sources).
+    rehearsal=True: the same CPU path built with NAV_DELAY_REHEARSAL=1, the
+    switch of the reference's delay-training target (CMakeLists.txt:72-76)."""
+    so = HERE / "_ref" / "libref_rehearsal.so" if rehearsal else REF_SO
+    if not so.exists():
         return None
-    lib = ctypes.CDLL(str(REF_SO))
+    lib = ctypes.CDLL(str(so))
     d = lambda n, r, *a: _declare(lib, n, r, *a)
     d("ref_trainer_create", _P, _P, _U, _P, _P)
     d("ref_trainer_destroy", None, _P)
@@ -269,6 +273,10 @@ class OracleSim(_Buffers):
         """Sim.runtime_control; takes effect at the next reset."""
         self.runtime = np.array(runtime, self.layouts.RUNTIME_CONFIG)
         self.lib.o_sim_set_runtime(self.h, ptr(self.runtime))
+
+    def set_delay_rehearsal(self, enabled=True):
+        """NAV_DELAY_REHEARSAL as a switch; takes effect at the next reset / step."""
+        self.lib.o_sim_set_delay_rehearsal(self.h, 1 if enabled else 0)
 
     def step(self, tick):
         self.lib.o_sim_step(self.h, tick)

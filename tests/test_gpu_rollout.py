@@ -318,3 +318,50 @@ def test_advance_lane_groups_match_oracle(pkg, om, raptor, group, case, monkeypa
         assert ora.buf("runs")["episodes"].sum() > 0
     finally:
         gpu.close()
+
+
+def test_delay_rehearsal_teacher_forced(pkg, om, raptor):
+    """Delay rehearsal (NAV_DELAY_REHEARSAL, sim.metal:14-24) switched on at
+    run time under mode 22: every other group of four environments trains
+    without delays, wind, depth noise or dropout. Reset and teacher-forced
+    steps against the oracle with the same switch; the clean groups are
+    checked directly too (zero wind)."""
+    n, T = 256, 8
+    cfg = pkg.layouts.default_config(n=n, family=1, mode=22, speed=1.0, distance=3.0, seed=17, sensor_delay=2,
+                                     command_delay=2, wind=0.4, depth_noise=0.05, dropout=0.1, max_steps=6)
+    gpu, ora = make_pair(pkg, om, raptor, cfg, T)
+    try:
+        gpu.set_delay_rehearsal(True)
+        gpu.reset()
+        ora.set_delay_rehearsal(True)
+        ora.reset()
+        for name in STATE_KEYS:
+            assert gpu.download(name).tobytes() == ora.buf(name).tobytes(), f"reset {name}"
+        clean = (np.arange(n) // 4) % 2 == 0
+        wind = gpu.download("worlds")["wind"][:, 0]
+        assert (wind[clean] == 0).all() and (wind[~clean] != 0).all()
+        for t in range(T):
+            for name in STATE_KEYS:
+                gpu.upload(name, ora.buf(name))
+            gpu.step(t)
+            ora.step(t)
+            rows = slice(t * n, (t + 1) * n)
+            # depth noise goes through logf/cosf: ranges and features at 1e-5
+            close(gpu.download("obs").reshape(T * n, 184)[rows], ora.buf("obs").reshape(T * n, 184)[rows],
+                  f"t={t} obs")
+            close(gpu.download("co").reshape(T * n, 32)[rows], ora.buf("co").reshape(T * n, 32)[rows], f"t={t} co")
+            for name in ("actions", "values", "rewards", "next_values"):
+                close(gpu.download(name).reshape(T * n, -1)[rows], ora.buf(name).reshape(T * n, -1)[rows],
+                      f"t={t} {name}")
+            for name in ("terminated", "truncated", "contact_id"):
+                assert np.array_equal(gpu.download(name)[rows], ora.buf(name)[rows]), f"t={t} {name}"
+            rs_g, rs_o = gpu.download("runs"), ora.buf("runs")
+            for f in ("steps", "episodes", "rng"):
+                assert np.array_equal(rs_g[f], rs_o[f]), f"t={t} runs.{f}"
+            for f in ("previous_nav", "desired_velocity"):
+                close(rs_g[f], rs_o[f], f"t={t} runs.{f}")
+            close(floats(gpu.download("states")), floats(ora.buf("states")), f"t={t} states")
+            assert gpu.download("worlds").tobytes() == ora.buf("worlds").tobytes(), f"t={t} worlds"
+        assert ora.buf("runs")["episodes"].sum() > 0
+    finally:
+        gpu.close()

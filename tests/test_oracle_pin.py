@@ -361,3 +361,39 @@ def test_minibatch_update_bitwise(oracle_mod, layouts, raptor, olib, rlib):
     for i in range(100, 104):
         _compare(osim.buf(i), ref.buf(i), ("moment", i))
     assert np.array_equal(out_o, out_r)
+
+
+def test_delay_rehearsal_matches_reference_build(oracle_mod, layouts, raptor, olib):
+    """NAV_DELAY_REHEARSAL (sim.metal:14-24, cpu_reference.hpp:219-223): the
+    restatement's switch against cpu_reference compiled with
+    -DNAV_DELAY_REHEARSAL=1 (oracle/_ref/libref_rehearsal.so), under mode 22.
+    The reference's CPU sampling loop has no mode-22 action map, so the pin is
+    taken where the switch acts before the action: the reset's wind, and the
+    observation's sensor delay, depth noise and dropout, teacher-forced step by
+    step. The command delay reads the same predicate."""
+    rl = oracle_mod.load_ref(rehearsal=True)
+    if rl is None:
+        pytest.skip("oracle/_ref not built: the reference sources are not on this machine")
+    n, T = 48, 6
+    cfg = layouts.default_config(n=n, family=1, mode=22, speed=1.0, distance=3.0, seed=5, sensor_delay=2,
+                                 command_delay=2, wind=0.4, depth_noise=0.05, dropout=0.1)
+    osim = oracle_mod.OracleSim(layouts, cfg, T, raptor, lib=olib)
+    osim.set_delay_rehearsal(True)
+    osim.reset()
+    ref = oracle_mod.RefTrainer(layouts, cfg, T, raptor, lib=rl)
+    for name in ("states", "runs", "worlds", "sensors", "commands"):
+        _compare(osim.buf(name), ref.buf(name), ("reset", name))
+    clean = (np.arange(n) // 4) % 2 == 0
+    wind = osim.buf("worlds")["wind"][:, 0]
+    assert (wind[clean] == 0).all() and (wind[~clean] != 0).all()
+    for t in range(T):
+        for name in ("states", "runs", "worlds", "sensors", "poses", "commands"):
+            ref.buf(name)[:] = osim.buf(name)
+        osim.observe(t)
+        rl.ref_step_observe(ref.h, t)
+        for name in ("obs", "co"):
+            width = 184 if name == "obs" else 32
+            _compare(osim.buf(name).reshape(T, n, width)[t], ref.buf(name).reshape(T, n, width)[t], (t, name))
+        _compare(osim.buf("sensors"), ref.buf("sensors"), (t, "sensors"))
+        osim.act(t)
+        osim.advance(t)
