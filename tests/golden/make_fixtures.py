@@ -11,6 +11,12 @@ replay, and the frozen RAPTOR controller the product ships as runtime data:
   physics.bin  RLPHYS1 L2F fixtures, 64 cases x 8 steps generated from rl-tools
                (assets/physics.bin; format main.mm:138-176, reference.cpp:83-156)
   ../../metal-drone-nav_b200/assets/raptor.bin  the same RAPTOR1 file
+  ref_ckpt_v6_guided_stress.bin   PPOFIX1 v6 checkpoint of the reference's own
+               training (assets/checkpoints/guided-stress.bin.best; layout
+               main.mm:978-1000,1209-1320): 128 envs, family 7, geometry memory
+  ref_ckpt_v8_local_waypoint.bin  PPOFIX1 v8 checkpoint with the runtime and
+               task blocks (assets/checkpoints/local-waypoint-fast-experimental
+               .bin.best): 128 envs, mode 22, goal-arrival tasks
 Then writes ref_trace.npz: a short teacher-forced trace of the reference's own
 CPU path (oracle/_ref, compiled unmodified), used by GPU tests on machines
 without the reference sources.
@@ -35,9 +41,24 @@ def _load(name, path, pkg_dir=None):
     return mod
 
 
-def main(ref_root=None):
+CHECKPOINTS = {"ref_ckpt_v6_guided_stress.bin": "guided-stress.bin.best",
+               "ref_ckpt_v8_local_waypoint.bin": "local-waypoint-fast-experimental.bin.best"}
+
+
+def copy_checkpoints(ref):
+    """The reference's own training checkpoints the resume tests load."""
+    for mine, theirs in CHECKPOINTS.items():
+        shutil.copyfile(ref / "assets" / "checkpoints" / theirs, HERE / mine)
+
+
+def reference_root(ref_root=None):
     import os
-    ref = pathlib.Path(ref_root or os.environ.get("MDN_REFERENCE") or ROOT.parent / "reference")
+    return pathlib.Path(ref_root or os.environ.get("MDN_REFERENCE") or ROOT.parent / "reference")
+
+
+def main(ref_root=None):
+    ref = reference_root(ref_root)
+    copy_checkpoints(ref)
     shutil.copyfile(ref / "assets" / "raptor.bin", HERE / "raptor.bin")
     shutil.copyfile(ref / "assets" / "physics.bin", HERE / "physics.bin")
     (ROOT / "metal-drone-nav_b200" / "assets").mkdir(parents=True, exist_ok=True)
