@@ -102,7 +102,7 @@ def check_loaded(pkg, sim, tr, blocks):
             assert sim.download(name).tobytes() == blocks[name], f"loaded {name}"
 
 
-def teacher_forced(gpu, ora, T, n, keys, hint_tol=1e-5):
+def teacher_forced(gpu, ora, T, n, keys, hint_tol=1e-5, tasks=False):
     for t in range(T):
         for name in keys:
             gpu.upload(name, ora.buf(name))
@@ -121,7 +121,14 @@ def teacher_forced(gpu, ora, T, n, keys, hint_tol=1e-5):
         for f in ("steps", "episodes", "successes", "collisions", "timeouts", "rng"):
             assert np.array_equal(rs_g[f], rs_o[f]), f"t={t} runs.{f}"
         close(floats(gpu.download("states")), floats(ora.buf("states")), f"t={t} states")
-        assert gpu.download("worlds").tobytes() == ora.buf("worlds").tobytes(), f"t={t} worlds"
+        wg, wo = gpu.download("worlds"), ora.buf("worlds")
+        if tasks:
+            # task resets draw goal directions with cosf/sinf (navigation_tasks.hpp:400-482):
+            # last-ulp goal differences, as in tests/test_gpu_tasks.py
+            assert np.array_equal(wg["count"], wo["count"]), f"t={t} world counts"
+            close(floats(wg), floats(wo), f"t={t} worlds")
+        else:
+            assert wg.tobytes() == wo.tobytes(), f"t={t} worlds"
 
 
 def bias(olib, steps):
@@ -191,7 +198,7 @@ def test_reference_v8_checkpoint_loads_and_resumes(pkg, om, device):
         keys = STATE_KEYS + ("task_states", "env_physics")
         for name in ("actor", "critic") + keys:
             ora.buf(name)[:] = sim.download(name)
-        teacher_forced(sim, ora, T, n, keys)
+        teacher_forced(sim, ora, T, n, keys, tasks=True)
         for f in ("step_count", "terminal", "stable_ticks", "generation_status", "valid"):
             assert np.array_equal(sim.download("task_states")[f], ora.buf("task_states")[f]), f
         tr.rollout_update(int(h["completed_rollouts"]))
