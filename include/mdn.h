@@ -397,6 +397,15 @@ int mdn_minibatch_order(uint32_t rows, uint32_t minibatch, uint32_t epochs, uint
 int mdn_ppo_minibatch_order(mdn_ppo* ppo, uint32_t rollout_index, uint32_t* out, size_t count);
 /* Device time of the last rollout update (CUDA events). */
 int mdn_ppo_last_update_ms(mdn_ppo* ppo, float* ms);
+/* Minibatch arithmetic of the 64-unit actor and critic (ppo_actor_forward /
+ * ppo_sample_loss_grad / ppo_actor_grad_direct and the critic kernels,
+ * ppo.metal:193-657; cpu_reference.hpp:515-551): enabled = 0 (default) runs
+ * the fp32 CUDA-core kernel whose sums follow the reference's order (the
+ * parity path); enabled = 1 runs the tcgen05 tensor-core kernel, TF32
+ * products with fp32 accumulation (gradients within ~1e-2 relative of fp32),
+ * for large minibatches. Clip, Adam and the GAE stay fp32 either way. Not for
+ * the wide actor, whose products already run on the tensor cores. */
+int mdn_ppo_set_tensor_cores(mdn_ppo* ppo, int enabled);
 /* PPOTrainer::save_checkpoint / load_checkpoint (main.mm:1209-1320): PPOFIX1.
  * Save writes version 6, or version 8 while the runtime config or the task
  * generator is on (plus the runtime/task configuration, per-env episode plants

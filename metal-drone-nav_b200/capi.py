@@ -81,6 +81,7 @@ SIGNATURES = {
     "mdn_minibatch_order": (ctypes.c_int, [_U, _U, _U, _U, _P, ctypes.c_size_t]),
     "mdn_ppo_minibatch_order": (ctypes.c_int, [_P, _U, _P, ctypes.c_size_t]),
     "mdn_ppo_last_update_ms": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float)]),
+    "mdn_ppo_set_tensor_cores": (ctypes.c_int, [_P, ctypes.c_int]),
     "mdn_ppo_checkpoint_save": (ctypes.c_int, [_P, ctypes.c_char_p, _U, _U, _U]),
     "mdn_ppo_checkpoint_load": (ctypes.c_int, [_P, ctypes.c_char_p, _U, _U, _U, _U]),
     "mdn_gae_normalize_static": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _U, _U, ctypes.c_float,
@@ -413,6 +414,12 @@ class PPOTrainer:
         a, b = _U(), _U()
         check(lib().mdn_launch_counts(self.sim.h, self.h, ctypes.byref(a), ctypes.byref(b)))
         return a.value, b.value
+
+    def set_tensor_cores(self, enabled=True):
+        """Minibatch products of the 64-unit networks on the tcgen05 tensor
+        cores in TF32 (enabled) or in fp32 on the CUDA cores in the
+        reference's summation order (the default)."""
+        check(lib().mdn_ppo_set_tensor_cores(self.h, 1 if enabled else 0))
 
     def last_update_ms(self):
         ms = ctypes.c_float()

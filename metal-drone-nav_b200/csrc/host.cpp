@@ -185,6 +185,7 @@ extern "C" int mdn_sync(mdn_device* dev, double* gpu_seconds) {
                         "wide actor kernel: a barrier wait gave up (flag " + std::to_string(flag) + ")");
             }
         }
+        check_trainer_errors(dev);
         cuda_check(cudaGetLastError(), "device error");
         if (gpu_seconds) *gpu_seconds = total;
     });

@@ -64,6 +64,9 @@ int kernels_per_step(const mdn_sim_config& c, bool wide);
 // read_checkpoint_header (main.mm:993-1000) for PPOFIX1 versions 3..10
 // (ppo_host.cpp); throws on a bad prefix, version or truncation.
 void read_checkpoint_header(std::ifstream& f, mdn_checkpoint_header& h);
+// Raises MDN_ERR_TIMEOUT when a trainer's tensor-core minibatch kernel gave up
+// on a barrier wait (ppo_host.cpp); the device's streams must be idle.
+void check_trainer_errors(struct ::mdn_device* dev);
 
 }  // namespace mdn
 

@@ -874,6 +874,10 @@ cudaError_t launch_minibatch(const PpoArgs& p, uint32_t update, uint32_t chunks,
     if (chunks > 1) k_grad_reduce<<<(kPpoParams + 255) / 256, 256, 0, s>>>(p, chunks);
     return cudaGetLastError();
 }
+cudaError_t launch_grad_reduce(const PpoArgs& p, uint32_t chunks, cudaStream_t s) {
+    k_grad_reduce<<<(kPpoParams + 255) / 256, 256, 0, s>>>(p, chunks);
+    return cudaGetLastError();
+}
 cudaError_t launch_clip_adam(const PpoArgs& p, uint32_t update, uint32_t chunks, cudaStream_t s) {
     k_clip_adam<<<2, kAdamThreads, 0, s>>>(p, update, chunks > 1 ? p.grad : p.grad_partials, 0);
     return cudaGetLastError();

@@ -58,6 +58,8 @@ struct PpoArgs {
     uint32_t actor_b2, actor_log_std;
     const float* wide_partials;
     uint32_t wide_slices, wide_rows_cap;
+    // barrier-timeout flag of the tensor-core minibatch kernel (ppo_tc.cu)
+    uint32_t* tc_error;
 };
 
 cudaError_t configure_ppo_kernels();
@@ -69,6 +71,8 @@ cudaError_t launch_adv_sq(const PpoArgs& p, cudaStream_t s);
 cudaError_t launch_adv_apply(const PpoArgs& p, int sm_count, cudaStream_t s);
 cudaError_t launch_minibatch(const PpoArgs& p, uint32_t update, uint32_t chunks, cudaStream_t s);
 cudaError_t launch_clip_adam(const PpoArgs& p, uint32_t update, uint32_t chunks, cudaStream_t s);
+// Fixed-order sum of `chunks` gradient partials into p.grad.
+cudaError_t launch_grad_reduce(const PpoArgs& p, uint32_t chunks, cudaStream_t s);
 // Critic-only clip + Adam (plus the update's metric row) reading the critic
 // gradient at grad_critic; the wide actor's step runs in wide.cu.
 cudaError_t launch_clip_adam_critic(const PpoArgs& p, uint32_t update, const float* grad_critic, cudaStream_t s);

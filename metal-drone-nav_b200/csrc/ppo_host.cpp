@@ -18,6 +18,7 @@
 
 #include "host_common.h"
 #include "ppo_args.h"
+#include "ppo_tc.h"
 
 using namespace mdn;
 
@@ -58,6 +59,12 @@ struct mdn_ppo {
     float* wide_grad = nullptr;       // [actor params + critic params]
     float* wide_norm_parts = nullptr; // [2 * SMs]
     WideMap obs32_map{}, delta_map{}, obs256_map{}, w1_128_map{};
+    // 64-unit actor on the tensor cores (mdn_ppo_set_tensor_cores, ppo_tc.cu)
+    bool tensor_cores = false;
+    bool tc_maps_ready = false;
+    TcMaps tc_maps{};
+    uint32_t tc_grid = 1;
+    uint32_t* tc_error = nullptr;
 };
 
 namespace {
@@ -154,6 +161,15 @@ void enqueue_update(mdn_ppo* t) {
             cuda_check(launch_clip_adam_critic(p, u, t->wide_grad + sim->actor_params, s), "critic clip+adam");
             continue;
         }
+        if (t->tensor_cores) {
+            // one gradient partial per CTA, summed in CTA order into p.grad
+            PpoArgs pt = p;
+            pt.fwd_grid = multi ? std::max<uint32_t>(t->tc_grid, 2) : t->tc_grid;
+            cuda_check(launch_minibatch_tc(pt, t->tc_maps, u, pt.fwd_grid, s), "tensor-core minibatch");
+            if (multi) cuda_check(comm_allreduce_float(dev, pt.grad, kPpoParams, s, err), err.c_str());
+            cuda_check(launch_clip_adam(pt, u, pt.fwd_grid, s), "clip+adam");
+            continue;
+        }
         cuda_check(launch_minibatch(p, u, chunks, s), "minibatch");
         if (multi) cuda_check(comm_allreduce_float(dev, p.grad, kPpoParams, s, err), err.c_str());
         cuda_check(launch_clip_adam(p, u, chunks, s), "clip+adam");
@@ -198,7 +214,7 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
                      o_ch = carve(mb * 64 * 4), o_ad = carve(mb * 64 * 4), o_cd = carve(mb * 64 * 4),
                      o_dm = carve(mb * 4 * 4), o_dls = carve(mb * 4 * 4), o_dv = carve(mb * 4),
                      o_gp = carve(size_t(chunk_bufs) * P * 4), o_g = carve(P * 4), o_lp = carve(U * t->fwd_grid * 4 * 4),
-                     o_mr = carve(U * 4 * 4), o_mm = carve(4 * 4), o_gn = carve(U * 2 * 4);
+                     o_mr = carve(U * 4 * 4), o_mm = carve(4 * 4), o_gn = carve(U * 2 * 4), o_err = carve(4);
         const cudaError_t e = cudaMalloc(&t->mem, off);
         require(e == cudaSuccess, MDN_ERR_NOMEM, std::string("cudaMalloc trainer: ") + cudaGetErrorString(e));
         char* base = static_cast<char*>(t->mem);
@@ -253,6 +269,8 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
         a.metric_rows = reinterpret_cast<float*>(base + o_mr);
         a.metric_mean = reinterpret_cast<float*>(base + o_mm);
         a.grad_norms = reinterpret_cast<float*>(base + o_gn);
+        t->tc_error = reinterpret_cast<uint32_t*>(base + o_err);
+        a.tc_error = t->tc_error;
         a.fwd_grid = t->fwd_grid;
         a.grad_chunk = t->grad_chunk;
         a.actor_b2 = sim->actor_hidden * (kActorObs + 1 + kActions);
@@ -436,6 +454,45 @@ extern "C" int mdn_ppo_rollout_update(mdn_ppo* t, uint32_t rollout_index) {
         t->completed_rollouts = rollout_index + 1;
     });
 }
+
+extern "C" int mdn_ppo_set_tensor_cores(mdn_ppo* t, int enabled) {
+    return guarded([&] {
+        checked(t);
+        mdn_sim* sim = t->sim;
+        require(!(enabled && sim->wide), MDN_ERR_INVALID,
+                "tensor-core minibatch path: the wide actor already runs on the tensor cores");
+        cuda_check(cudaStreamSynchronize(sim->stream), "set tensor cores");
+        if (enabled && !t->tc_maps_ready) {
+            cuda_check(tc_make_maps(&t->tc_maps, static_cast<const float*>(sim->buf[MDN_BUF_OBS]),
+                                    static_cast<const float*>(sim->buf[MDN_BUF_CO]), uint64_t(sim->n) * sim->horizon,
+                                    static_cast<const float*>(sim->buf[MDN_BUF_ACTOR]),
+                                    static_cast<const float*>(sim->buf[MDN_BUF_CRITIC])),
+                       "tensor-core minibatch tensor maps");
+            cuda_check(configure_tc_kernels(), "tensor-core minibatch kernel attributes");
+            t->tc_grid = tc_grid(t->minibatch, sim->dev->sm_count);
+            t->tc_maps_ready = true;
+        }
+        if (t->tensor_cores != (enabled != 0) && t->graph) {
+            cudaGraphExecDestroy(t->graph);  // the update graph is captured per path
+            t->graph = nullptr;
+        }
+        t->tensor_cores = enabled != 0;
+    });
+}
+
+namespace mdn {
+// A barrier wait of the tensor-core minibatch kernel that gave up (called by
+// mdn_sync once the streams are idle).
+void check_trainer_errors(mdn_device* dev) {
+    for (mdn_ppo* t : dev->trainers) {
+        if (!t->tensor_cores) continue;
+        uint32_t flag = 0;
+        cuda_check(cudaMemcpy(&flag, t->tc_error, sizeof(flag), cudaMemcpyDeviceToHost), "tensor-core error flag");
+        require(flag == 0, MDN_ERR_TIMEOUT,
+                "tensor-core minibatch kernel: a barrier wait gave up (flag " + std::to_string(flag) + ")");
+    }
+}
+}  // namespace mdn
 
 extern "C" int mdn_ppo_last_update_ms(mdn_ppo* t, float* ms) {
     return guarded([&] {
