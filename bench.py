@@ -74,6 +74,10 @@ def parse():
     ap.add_argument("--actor-hidden", type=int, default=64,
                     help="64 = the reference's 12,104-parameter actor; 5120 = the 967,688-parameter wide actor "
                          "(BASELINE config 3), evaluated on the tcgen05 tensor cores")
+    ap.add_argument("--ppo-fp32", action="store_true",
+                    help="run the timed PPO updates on the fp32 parity path instead of the tcgen05 TF32 kernel")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the BASELINE config 0 and config 1 measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-wide", action="store_true", help="skip the wide-actor (BASELINE config 3) measurement")
     return ap.parse_args()
@@ -199,6 +203,38 @@ def kernel_work(mean_obstacles):
     }
 
 
+# PPO update, per row and epoch of a minibatch: HBM bytes the minibatch kernel
+# must read (observation 184 floats, critic observation 32, action 4, old
+# log-prob, advantage, return) and its arithmetic (forward, deltas and weight
+# gradients of both networks, cpu_reference.hpp:437-551).
+PPO_BYTES_PER_ROW = 184 * 4 + 32 * 4 + 4 * 4 + 4 + 4 + 4
+PPO_GEMM_FLOP_PER_ROW = 2 * 2 * (184 + 32) * 64          # forward + weight-gradient products
+PPO_FLOP_PER_ROW = PPO_GEMM_FLOP_PER_ROW + 2 * (64 * 4 + 64) * 2 + 6 * 64 * 2 + 2 * 64 * 4 + 200
+
+
+def ppo_roofline(trainer, minibatch_rows, dist, peaks, fp32_peak):
+    """Minibatch kernel of the update (one launch = one minibatch's gradient
+    partials and their sum), timed with CUDA events on the simulator stream,
+    against the measured HBM copy peak (its bound) and the tensor / FP32 peak."""
+    ms = float(np.median([trainer.profile_minibatch(u % trainer.updates) for u in range(3)]))
+    (ms,) = dist.max([ms])
+    t = ms * 1e-3
+    gbs = minibatch_rows * PPO_BYTES_PER_ROW / t / 1e9
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    tensor = trainer.tensor_cores
+    tflops = minibatch_rows * (PPO_GEMM_FLOP_PER_ROW if tensor else PPO_FLOP_PER_ROW) / t / 1e12
+    compute_peak = peaks.get("bf16_tflops", 1590.0) / 2.0 if tensor else fp32_peak
+    return {"kernel": "k_mb_tc" if tensor else "k_mb_fused", "ms_per_minibatch": ms, "minibatch_rows": minibatch_rows,
+            "bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+            "bytes_per_row_epoch": PPO_BYTES_PER_ROW,
+            "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+            "compute": {"achieved": tflops, "unit": "TFLOP/s", "peak": compute_peak,
+                        "frac": tflops / compute_peak,
+                        "flop_per_row_epoch": PPO_GEMM_FLOP_PER_ROW if tensor else PPO_FLOP_PER_ROW,
+                        "peak_source": "half the measured bf16 dense rate (TF32 tensor cores)" if tensor
+                        else "measured pure-FMA FP32 kernel, this run"}}
+
+
 def read_profile_traffic(kernel):
     """DRAM bytes per environment measured by ncu (profiles/<kernel>_traffic.txt)."""
     f = ROOT / "profiles" / f"{kernel}_traffic.txt"
@@ -260,11 +296,25 @@ def measure_wide(pkg, dev, dist, args, peaks):
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_reference_sample(layouts, n, policy_steps, family, warmup=0, threads=None, delay=0):
+def cpu_model():
+    """The host CPU's model name (first /proc/cpuinfo entry)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_reference_sample(layouts, n, policy_steps, family, warmup=0, threads=None, delay=0, ppo=True,
+                         own_update=False):
     """The reference's own CPU path (oracle/_ref: cpu_reference.hpp compiled
-    unmodified) on a bounded sample: `n` environments with the benchmark's
-    family-17 worlds, `warmup` untimed then `policy_steps` timed policy steps,
-    then the PPO cost per row-epoch."""
+    unmodified) on a bounded sample: `n` environments of the benchmark's
+    worlds, `warmup` untimed then `policy_steps` timed policy steps (each one
+    ref_step over every environment, timed on its own), then the PPO cost per
+    row-epoch."""
     om = oracle_module()
     ref = om.load_ref()
     kind = "reference"
@@ -277,37 +327,134 @@ def cpu_reference_sample(layouts, n, policy_steps, family, warmup=0, threads=Non
     raptor = layouts.load_raptor_file(ROOT / "metal-drone-nav_b200" / "assets" / "raptor.bin")
     tr = om.RefTrainer(layouts, cfg, warmup + policy_steps, raptor, lib=ref)
     worlds = tr.buf("worlds")
+    runs = tr.buf("runs")
     # The benchmark's worlds (families 17-20) drawn as the simulator's reset
     # draws them (seed per env, sim.metal:56-58), generated by the C
-    # restatement: the reference has no generator for these families. Later
-    # resets inside the sample use family 1.
+    # restatement: the reference has no generator for these families.
     rng = np.zeros(1, np.uint32)
-    for i in range(n):
-        rng[0] = (42 + i * 747796405 + 2891336453) & 0xFFFFFFFF
-        fam = olib.o_mixed_lane_family(i) if family == 18 else olib.o_wtraining_family(family, om.ptr(rng))
+
+    def world_for(i):
+        fam = olib.o_mixed_lane_family(int(i)) if family == 18 else olib.o_wtraining_family(family, om.ptr(rng))
         seed = olib.o_wrng(om.ptr(rng))
         olib.o_wgenerate(om.ptr(worlds[i:i + 1]), seed, fam, 4.0)
-    for t in range(warmup):
+
+    for i in range(n):
+        rng[0] = (42 + i * 747796405 + 2891336453) & 0xFFFFFFFF
+        world_for(i)
+    step_s = []
+    for t in range(warmup + policy_steps):
+        before = runs["episodes"].copy()
+        t0 = time.perf_counter()
         ref.ref_step(tr.h, t)
-    t0 = time.perf_counter()
-    for t in range(warmup, warmup + policy_steps):
-        ref.ref_step(tr.h, t)
-    collect_s = time.perf_counter() - t0
-    # PPO: one train_rollout over a small trainer -> seconds per row-epoch
-    small = om.RefTrainer(layouts, layouts.default_config(n=1024, family=1, seed=42), 4, raptor, lib=ref)
-    for t in range(4):
-        ref.ref_step(small.h, t)
-    ref.ref_gae_normalize(small.h)
-    loss = np.zeros(4, np.float32)
-    t1 = time.perf_counter()
-    ref.ref_train_rollout(small.h, 0, om.ptr(loss))
-    update_s = time.perf_counter() - t1
-    per_row_epoch = update_s / (1024 * 4 * 2)
-    return {"env_steps_per_s": n * policy_steps / collect_s, "collect_s": collect_s, "threads": threads,
-            "per_row_epoch_s": per_row_epoch, "kind": kind,
-            "sample": f"{n} envs x {policy_steps} policy steps of cpu_reference::Trainer (compiled unmodified, "
-                      f"OpenMP stand-ins for GCD/Accelerate) on family-{family} worlds, delays {delay}; PPO cost from one "
-                      f"train_rollout over 1024x4 rows (2 epochs x 256-row chunks)"}
+        if t >= warmup:
+            step_s.append(time.perf_counter() - t0)
+        # An episode the reference reset inside the step (cpu_reference.hpp
+        # reset_env, its own family-1 generator, inside the timed step) gets a
+        # world of the benchmark's families for its next steps, outside the
+        # timed region.
+        for i in np.nonzero(runs["episodes"] != before)[0]:
+            rng[0] = runs["rng"][i]
+            world_for(i)
+    collect_s = float(sum(step_s))
+    update_ms = None
+    if own_update:
+        # the reference's own update of this rollout: GAE + normalisation, then
+        # 2 epochs of shuffled 256-row chunks (cpu_reference.hpp:571-608)
+        loss = np.zeros(4, np.float32)
+        t1 = time.perf_counter()
+        ref.ref_gae_normalize(tr.h)
+        ref.ref_train_rollout(tr.h, 0, om.ptr(loss))
+        update_ms = (time.perf_counter() - t1) * 1e3
+    out = {"env_steps_per_s": n * policy_steps / collect_s, "collect_s": collect_s, "threads": threads,
+           "step_ms": collect_s / policy_steps * 1e3, "kind": kind, "cpu_model": cpu_model(), "update_ms": update_ms,
+           "sample": f"{n} envs x {policy_steps} policy steps of cpu_reference::Trainer (compiled unmodified, "
+                     f"OpenMP stand-ins for GCD/Accelerate) on family-{family} worlds (also after in-step resets), "
+                     f"delays {delay}, {threads} threads"}
+    if ppo:
+        # PPO: one train_rollout over a small trainer -> seconds per row-epoch
+        small = om.RefTrainer(layouts, layouts.default_config(n=1024, family=1, seed=42), 4, raptor, lib=ref)
+        for t in range(4):
+            ref.ref_step(small.h, t)
+        ref.ref_gae_normalize(small.h)
+        loss = np.zeros(4, np.float32)
+        t1 = time.perf_counter()
+        ref.ref_train_rollout(small.h, 0, om.ptr(loss))
+        update_s = time.perf_counter() - t1
+        out["per_row_epoch_s"] = update_s / (1024 * 4 * 2)
+        out["sample"] += "; PPO cost from one train_rollout over 1024x4 rows (2 epochs x 256-row chunks)"
+    return out
+
+
+def measure_config0(pkg, dev):
+    """BASELINE config 0, the reference's own CPU-runnable workload: 512
+    environments of the baseline clutter scenes (family 17), T = 64, then GAE
+    and the reference's update schedule (2 epochs x 256-row chunks) on the
+    fp32 parity path. The reference's CPU path runs the same rollout and
+    update at all host cores and at one core."""
+    L = pkg.layouts
+    n, T = 512, 64
+    sim = pkg.Sim(dev, L.default_config(n=n, family=17, seed=0), T)
+    tr = pkg.PPOTrainer(sim, epochs=2, minibatch=256)
+    try:
+        sim.collect()
+        tr.rollout_update(0)
+        dev.finish()
+        c, u = [], []
+        for k in range(3):
+            sim.collect()
+            c.append(sim.last_collect_ms())
+            tr.rollout_update(k + 1)
+            u.append(tr.last_update_ms())
+        dev.finish()
+    finally:
+        tr.close()
+        sim.close()
+    out = {"config": "BASELINE config 0: 512 envs, family-17 scenes (16 boxes, goal 2-8 m), T=64, GAE, "
+                     "PPO 2 epochs x 256-row chunks (fp32 parity path)",
+           "gpu": {"env_steps_per_s": n * T / (np.mean(c) * 1e-3), "rollout_ms": float(np.mean(c)),
+                   "ppo_update_ms": float(np.mean(u))}}
+    for label, threads in (("cpu_all_cores", None), ("cpu_one_core", 1)):
+        r = cpu_reference_sample(L, n, T, 17, threads=threads, ppo=False, own_update=True)
+        if r is not None:
+            out[label] = {"env_steps_per_s": r["env_steps_per_s"], "rollout_ms": r["collect_s"] * 1e3,
+                          "ppo_update_ms": r["update_ms"], "cores": r["threads"], "cpu_model": r["cpu_model"],
+                          "kind": r["kind"]}
+    return out
+
+
+def measure_config1(pkg, dev):
+    """8,192 environments on the goal-arrival task path
+    (navigation_tasks.hpp clutter stage, family 1 static rooms, goal band
+    2-20 m), T = 128, PPO 4 epochs x 8 minibatches on the tensor-core path."""
+    L = pkg.layouts
+    n, T = 8192, 128
+    sim = pkg.Sim(dev, L.default_config(n=n, family=1, mode=22, speed=1.5, distance=8.0, seed=7, max_steps=400), T)
+    control = pkg.task_control(2, 1)
+    control["config"]["goal_distance_max_m"] = 20.0
+    sim.configure_tasks(control, 0.0)
+    tr = pkg.PPOTrainer(sim, epochs=4, minibatch=n * T // 8)
+    tr.set_tensor_cores(True)
+    try:
+        sim.collect()
+        tr.rollout_update(0)
+        dev.finish()
+        c, u = [], []
+        for k in range(2):
+            sim.collect()
+            c.append(sim.last_collect_ms())
+            tr.rollout_update(k + 1)
+            u.append(tr.last_update_ms())
+        tr.set_tensor_cores(False)
+        tr.rollout_update(3)
+        dev.finish()
+        fp32_ms = tr.last_update_ms()
+    finally:
+        tr.close()
+        sim.close()
+    return {"config": "BASELINE config 1: 8,192 envs, goal-arrival tasks (clutter stage, family-1 rooms, goals "
+                      "2-20 m), T=128, PPO 4 epochs x 8 minibatches of 131,072 rows",
+            "env_steps_per_s": n * T / (np.mean(c) * 1e-3), "rollout_ms": float(np.mean(c)),
+            "ppo_update_ms": float(np.mean(u)), "ppo_update_ms_fp32_path": fp32_ms}
 
 
 def run_reference_arm(args, dist, out_fd):
@@ -319,21 +466,20 @@ def run_reference_arm(args, dist, out_fd):
     if om.load_ref() is None:
         emit({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}, out_fd)
         return 0
-    # warm-up and timed steps: each step = one policy step over all environments
-    samples = []
-    per_row = None
+    # each step = one policy step over all environments, timed on its own
     s = cpu_reference_sample(layouts, envs, args.steps, args.family, warmup=args.warmup, delay=args.delay)
     value = s["env_steps_per_s"]
-    per_row = s["per_row_epoch_s"]
     rows = envs * args.horizon
-    ppo_ms = per_row * rows * args.epochs * 1e3
     line = {
         "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": envs * args.horizon / value * 1e3 + ppo_ms,
+        "warmup": args.warmup, "ms_per_step": s["step_ms"],
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "impl": "reference",
         "config": workload_config(args),
-        "ppo_update_ms": ppo_ms,
+        "step": f"one policy step of all {envs:,} environments (the GPU arm's step is a {args.horizon}-step rollout "
+                f"plus a PPO update)",
+        "ppo_update_ms_extrapolated": s["per_row_epoch_s"] * rows * args.epochs * 1e3,
+        "cpu_model": s["cpu_model"],
         "cpu_baseline": {"value": value, "unit": "env-steps/s", "cores": s["threads"], "kind": s["kind"],
                          "sample": s["sample"] + f" ({args.warmup} untimed warm-up steps)"},
         "e2e": {"value": value, "unit": "env-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -389,6 +535,8 @@ def main():
     rows = n * args.horizon
     minibatch = rows // args.minibatches
     trainer = pkg.PPOTrainer(sim, epochs=args.epochs, minibatch=minibatch)
+    if args.actor_hidden == 64 and not args.ppo_fp32:
+        trainer.set_tensor_cores(True)  # the minibatch products on tcgen05 (TF32)
 
     for w in range(args.warmup):
         sim.collect()
@@ -446,6 +594,8 @@ def main():
     (e2e_wall,) = dist.max([time.perf_counter() - e0])
     e2e_value = env_steps / e2e_wall
 
+    peaks_file = ROOT / "MEASURED_PEAKS.json"
+    peaks = json.loads(peaks_file.read_text()) if peaks_file.exists() else {}
     # ---- per-kernel roofline of one policy step (CUDA events between launches)
     prof = np.mean([sim.profile_step(t % args.horizon) for t in range(8)], axis=0)
     prof = dist.max(prof.tolist())
@@ -454,8 +604,6 @@ def main():
     worlds = sim.download("worlds")
     mean_obstacles = float(np.mean(worlds["count"]))
     work = kernel_work(mean_obstacles)
-    peaks_file = ROOT / "MEASURED_PEAKS.json"
-    peaks = json.loads(peaks_file.read_text()) if peaks_file.exists() else {}
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
     hbm_src = "measured" if "hbm_gbs" in peaks else "fallback"
     fp32_peak = dev.fp32_peak_tflops()
@@ -470,12 +618,31 @@ def main():
                        "tflop_s": work[nm]["flop"] * n / ts / 1e12,
                        "fp32_frac": work[nm]["flop"] * n / ts / 1e12 / fp32_peak}
 
+    # ---- PPO update: the minibatch kernel against its roof, and the fp32
+    # parity path of the same update (one more rollout update, after timing)
+    ppo_roof, ppo_fp32 = None, None
+    if args.actor_hidden == 64:
+        ppo_roof = ppo_roofline(trainer, minibatch, dist, peaks, fp32_peak)
+        if trainer.tensor_cores:
+            trainer.set_tensor_cores(False)
+            trainer.rollout_update(args.warmup + args.steps)
+            dev.finish()
+            (fp32_ms,) = dist.max([trainer.last_update_ms()])
+            ppo_fp32 = {"ppo_update_ms": fp32_ms, "roofline": ppo_roofline(trainer, minibatch, dist, peaks, fp32_peak),
+                        "note": "the fp32 CUDA-core kernel that keeps the reference's summation order (the parity "
+                                "path), one update of the same workload after the timed region"}
+            trainer.set_tensor_cores(True)
+
     line = {
         "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": (c_ms + u_ms) / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (procedural worlds, seeded)",
         "config": workload_config(args),
         "ppo_update_ms": u_ms / args.steps,
+        "ppo_path": ("tcgen05 TF32 minibatch products, fp32 accumulation, GAE / clip / Adam in fp32"
+                     if trainer.tensor_cores else "fp32 CUDA cores in the reference's summation order"),
+        "ppo_roofline": ppo_roof,
+        "ppo_update_fp32": ppo_fp32,
         "rollout_ms": c_ms / args.steps,
         "wall_s": wall_max,
         "e2e": {"value": e2e_value, "unit": "env-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -493,13 +660,18 @@ def main():
     }
     if not args.no_wide and args.actor_hidden == 64:
         line["wide_actor"] = measure_wide(pkg, dev, dist, args, peaks)
+    if world == 1 and not args.no_secondary:
+        line["baseline_configs"] = {"0": measure_config0(pkg, dev), "1": measure_config1(pkg, dev)}
     if world == 1 and dist.rank == 0 and not args.no_cpu_baseline:
         s = cpu_reference_sample(L, args.envs, 2, args.family, warmup=1, delay=args.delay)
         if s is not None:
+            one = cpu_reference_sample(L, 4096, 2, args.family, warmup=1, threads=1, delay=args.delay, ppo=False)
             line["cpu_baseline"] = {"value": s["env_steps_per_s"], "unit": "env-steps/s", "cores": s["threads"],
-                                    "kind": s["kind"], "sample": s["sample"],
+                                    "kind": s["kind"], "sample": s["sample"], "cpu_model": s["cpu_model"],
                                     "ppo_update_ms_extrapolated": s["per_row_epoch_s"] * args.envs * args.horizon
-                                    * args.epochs * 1e3}
+                                    * args.epochs * 1e3,
+                                    "one_core": {"value": one["env_steps_per_s"], "unit": "env-steps/s", "cores": 1,
+                                                 "sample": one["sample"]}}
     if dist.rank == 0:
         emit(line, out_fd)
     trainer.close()

@@ -371,6 +371,12 @@ int mdn_device_fp32_peak(mdn_device* dev, double* tflops);
  * operand pairs of the ray tests' ranges; *mismatches counts differing bit
  * patterns (0 expected). */
 int mdn_selftest_division(mdn_device* dev, uint64_t samples, uint64_t seed, uint64_t* mismatches);
+/* The bounded shared-memory barrier wait of the tensor-core kernels, alone in
+ * a one-thread kernel: with arrive = 0 nothing arrives, the wait gives up after
+ * limit_cycles and the call returns MDN_ERR_TIMEOUT (the status a kernel's
+ * timed-out wait surfaces as); with arrive = 1 it returns MDN_OK. No reference
+ * counterpart (the reference's Metal waits are unbounded). */
+int mdn_selftest_barrier_timeout(mdn_device* dev, uint64_t limit_cycles, int arrive);
 
 /* ---- trainer: PPOTrainer (main.mm:1110-1476) ----------------------------- */
 /* PPOTrainer(Sim&, epochs) main.mm:1159-1208; epochs 1..4; minibatch_rows 0 =
@@ -406,6 +412,12 @@ int mdn_ppo_last_update_ms(mdn_ppo* ppo, float* ms);
  * for large minibatches. Clip, Adam and the GAE stay fp32 either way. Not for
  * the wide actor, whose products already run on the tensor cores. */
 int mdn_ppo_set_tensor_cores(mdn_ppo* ppo, int enabled);
+/* Device time of one launch of the minibatch gradient kernels (the gradient
+ * partials and their sum, no clip/Adam) for minibatch `update` of the last
+ * rollout update, CUDA events on the sim stream: the roofline numerator of
+ * the update. Writes only trainer scratch; parameters and moments are
+ * untouched. 64-unit actor only. */
+int mdn_ppo_profile_minibatch(mdn_ppo* ppo, uint32_t update, float* ms);
 /* PPOTrainer::save_checkpoint / load_checkpoint (main.mm:1209-1320): PPOFIX1.
  * Save writes version 6, or version 8 while the runtime config or the task
  * generator is on (plus the runtime/task configuration, per-env episode plants

@@ -69,6 +69,7 @@ SIGNATURES = {
     "mdn_sim_set_contact_audit": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_float]),
     "mdn_sim_set_delay_rehearsal": (ctypes.c_int, [_P, ctypes.c_int]),
     "mdn_device_fp32_peak": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_double)]),
+    "mdn_selftest_barrier_timeout": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_int]),
     "mdn_selftest_division": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
     "mdn_ppo_create": (ctypes.c_int, [_P, _U, _U, ctypes.POINTER(_P)]),
     "mdn_ppo_destroy": (ctypes.c_int, [_P]),
@@ -82,6 +83,7 @@ SIGNATURES = {
     "mdn_ppo_minibatch_order": (ctypes.c_int, [_P, _U, _P, ctypes.c_size_t]),
     "mdn_ppo_last_update_ms": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float)]),
     "mdn_ppo_set_tensor_cores": (ctypes.c_int, [_P, ctypes.c_int]),
+    "mdn_ppo_profile_minibatch": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.POINTER(ctypes.c_float)]),
     "mdn_ppo_checkpoint_save": (ctypes.c_int, [_P, ctypes.c_char_p, _U, _U, _U]),
     "mdn_ppo_checkpoint_load": (ctypes.c_int, [_P, ctypes.c_char_p, _U, _U, _U, _U]),
     "mdn_gae_normalize_static": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _U, _U, ctypes.c_float,
@@ -197,6 +199,11 @@ class Device:
         out = ctypes.c_uint64()
         check(lib().mdn_selftest_division(self.h, samples, seed, ctypes.byref(out)))
         return out.value
+
+    def selftest_barrier_timeout(self, limit_cycles, arrive=False):
+        """One bounded barrier wait on the device; raises MdnError (TIMEOUT)
+        when nothing arrives within limit_cycles."""
+        check(lib().mdn_selftest_barrier_timeout(self.h, int(limit_cycles), 1 if arrive else 0))
 
     def comm_init(self, rank, world, unique_id):
         buf = np.frombuffer(bytes(unique_id), np.uint8).copy()
@@ -363,6 +370,10 @@ class PPOTrainer:
         self.sim = sim
         self.h = _P()
         check(lib().mdn_ppo_create(sim.h, epochs, minibatch, ctypes.byref(self.h)))
+        rows = int(sim.cfg["n"]) * sim.horizon
+        self.minibatch = min(minibatch or 256, rows)
+        self.updates = epochs * (-(-rows // self.minibatch))
+        self.tensor_cores = False
 
     def close(self):
         if self.h:
@@ -420,6 +431,13 @@ class PPOTrainer:
         cores in TF32 (enabled) or in fp32 on the CUDA cores in the
         reference's summation order (the default)."""
         check(lib().mdn_ppo_set_tensor_cores(self.h, 1 if enabled else 0))
+        self.tensor_cores = bool(enabled)
+
+    def profile_minibatch(self, update=0):
+        """Device ms of one launch of the minibatch gradient kernels."""
+        ms = ctypes.c_float()
+        check(lib().mdn_ppo_profile_minibatch(self.h, update, ctypes.byref(ms)))
+        return ms.value
 
     def last_update_ms(self):
         ms = ctypes.c_float()

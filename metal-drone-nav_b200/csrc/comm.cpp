@@ -7,8 +7,13 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
 #include <cstdlib>
 #include <mutex>
+#include <thread>
+
+#include <algorithm>
+#include <cstring>
 
 #include "host_common.h"
 
@@ -20,7 +25,9 @@ namespace mdn {
 namespace {
 struct Nccl {
     decltype(&ncclGetUniqueId) get_unique_id = nullptr;
-    decltype(&ncclCommInitRank) init_rank = nullptr;
+    decltype(&ncclCommInitRankConfig) init_rank_config = nullptr;
+    decltype(&ncclCommGetAsyncError) async_error = nullptr;
+    decltype(&ncclCommAbort) abort = nullptr;
     decltype(&ncclAllReduce) all_reduce = nullptr;
     decltype(&ncclCommDestroy) destroy = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
@@ -41,11 +48,14 @@ const Nccl& nccl() {
             return;
         }
         n.get_unique_id = reinterpret_cast<decltype(n.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
-        n.init_rank = reinterpret_cast<decltype(n.init_rank)>(dlsym(h, "ncclCommInitRank"));
+        n.init_rank_config = reinterpret_cast<decltype(n.init_rank_config)>(dlsym(h, "ncclCommInitRankConfig"));
+        n.async_error = reinterpret_cast<decltype(n.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+        n.abort = reinterpret_cast<decltype(n.abort)>(dlsym(h, "ncclCommAbort"));
         n.all_reduce = reinterpret_cast<decltype(n.all_reduce)>(dlsym(h, "ncclAllReduce"));
         n.destroy = reinterpret_cast<decltype(n.destroy)>(dlsym(h, "ncclCommDestroy"));
         n.error_string = reinterpret_cast<decltype(n.error_string)>(dlsym(h, "ncclGetErrorString"));
-        n.ok = n.get_unique_id && n.init_rank && n.all_reduce && n.destroy && n.error_string;
+        n.ok = n.get_unique_id && n.init_rank_config && n.async_error && n.abort && n.all_reduce && n.destroy &&
+               n.error_string;
         if (!n.ok) n.why = "NCCL library lacks required symbols";
     });
     return n;
@@ -57,24 +67,94 @@ const Nccl& need_nccl() {
 }
 }  // namespace
 
-cudaError_t comm_allreduce_double(mdn_device* dev, double* buf, size_t count, cudaStream_t s, std::string& err) {
-    if (dev->world <= 1 || !dev->nccl_comm) return cudaSuccess;
-    const ncclResult_t r = nccl().all_reduce(buf, buf, count, ncclFloat64, ncclSum, static_cast<ncclComm_t>(dev->nccl_comm), s);
+namespace {
+using Clock = std::chrono::steady_clock;
+double seconds_since(Clock::time_point t0) { return std::chrono::duration<double>(Clock::now() - t0).count(); }
+
+// Abort the communicator (NCCL kernels waiting on a peer return), let the
+// stream drain and mark the device so no later update enqueues a collective.
+[[noreturn]] void abort_comm(mdn_device* dev, cudaStream_t s, const std::string& why) {
+    if (dev->nccl_comm && nccl().ok) nccl().abort(static_cast<ncclComm_t>(dev->nccl_comm));
+    dev->nccl_comm = nullptr;
+    dev->comm_failed = true;
+    if (s) cudaStreamSynchronize(s);
+    cudaGetLastError();
+    throw Error(MDN_ERR_NCCL, why);
+}
+
+// Poll `ready` (a stream or an event) and the communicator's asynchronous
+// error until the work is done, the communicator reports an error, or the
+// device's deadline passes.
+template <class Ready>
+void poll_until(mdn_device* dev, cudaStream_t s, const char* what, Ready ready) {
+    const auto t0 = Clock::now();
+    for (;;) {
+        const cudaError_t q = ready();
+        if (q != cudaErrorNotReady) {
+            cuda_check(q, what);
+            return;
+        }
+        ncclResult_t state = ncclSuccess;
+        nccl().async_error(static_cast<ncclComm_t>(dev->nccl_comm), &state);
+        if (state != ncclSuccess && state != ncclInProgress)
+            abort_comm(dev, s, std::string(what) + ": NCCL communicator error: " + nccl().error_string(state));
+        if (seconds_since(t0) > dev->nccl_timeout_s)
+            abort_comm(dev, s, std::string(what) + ": collective did not complete within " +
+                                   std::to_string(dev->nccl_timeout_s) + " s (a peer rank is gone or stalled)");
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
+// A non-blocking communicator may answer a call with ncclInProgress; wait
+// (bounded) until it has taken the call.
+ncclResult_t settle(mdn_device* dev, ncclResult_t r) {
+    const auto t0 = Clock::now();
+    while (r == ncclInProgress) {
+        nccl().async_error(static_cast<ncclComm_t>(dev->nccl_comm), &r);
+        if (r == ncclInProgress && seconds_since(t0) > dev->nccl_timeout_s) return ncclInternalError;
+        if (r == ncclInProgress) std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+    return r;
+}
+
+cudaError_t allreduce(mdn_device* dev, void* buf, size_t count, ncclDataType_t type, cudaStream_t s, std::string& err) {
+    if (dev->world <= 1) return cudaSuccess;
+    if (!dev->nccl_comm) {
+        err = dev->comm_failed ? "NCCL communicator was aborted after a failure" : "no NCCL communicator";
+        return cudaErrorUnknown;
+    }
+    const ncclResult_t r = settle(
+        dev, nccl().all_reduce(buf, buf, count, type, ncclSum, static_cast<ncclComm_t>(dev->nccl_comm), s));
     if (r != ncclSuccess) {
         err = std::string("ncclAllReduce: ") + nccl().error_string(r);
         return cudaErrorUnknown;
     }
     return cudaSuccess;
 }
+}  // namespace
+
+cudaError_t comm_allreduce_double(mdn_device* dev, double* buf, size_t count, cudaStream_t s, std::string& err) {
+    return allreduce(dev, buf, count, ncclFloat64, s, err);
+}
 
 cudaError_t comm_allreduce_float(mdn_device* dev, float* buf, size_t count, cudaStream_t s, std::string& err) {
-    if (dev->world <= 1 || !dev->nccl_comm) return cudaSuccess;
-    const ncclResult_t r = nccl().all_reduce(buf, buf, count, ncclFloat32, ncclSum, static_cast<ncclComm_t>(dev->nccl_comm), s);
-    if (r != ncclSuccess) {
-        err = std::string("ncclAllReduce: ") + nccl().error_string(r);
-        return cudaErrorUnknown;
+    return allreduce(dev, buf, count, ncclFloat32, s, err);
+}
+
+void sync_stream(mdn_device* dev, cudaStream_t s, const char* what) {
+    if (dev->world <= 1 || !dev->nccl_comm) {
+        cuda_check(cudaStreamSynchronize(s), what);
+        return;
     }
-    return cudaSuccess;
+    poll_until(dev, s, what, [&] { return cudaStreamQuery(s); });
+}
+
+void sync_event(mdn_device* dev, cudaEvent_t e, const char* what) {
+    if (dev->world <= 1 || !dev->nccl_comm) {
+        cuda_check(cudaEventSynchronize(e), what);
+        return;
+    }
+    poll_until(dev, nullptr, what, [&] { return cudaEventQuery(e); });
 }
 
 }  // namespace mdn
@@ -105,9 +185,27 @@ extern "C" int mdn_comm_init(mdn_device* dev, int rank, int world, const uint8_t
         const Nccl& nc = need_nccl();
         ncclUniqueId uid;
         std::memcpy(&uid, id, 128);
-        ncclComm_t comm;
-        const ncclResult_t r = nc.init_rank(&comm, world, uid, rank);
-        require(r == ncclSuccess, MDN_ERR_NCCL, std::string("ncclCommInitRank: ") + nc.error_string(r));
+        const char* limit = std::getenv("MDN_NCCL_TIMEOUT_S");
+        if (limit && *limit) dev->nccl_timeout_s = std::max(1.0, std::atof(limit));
+        // Non-blocking communicator: the host polls its state against the
+        // deadline instead of blocking inside NCCL.
+        ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+        config.blocking = 0;
+        ncclComm_t comm = nullptr;
+        ncclResult_t r = nc.init_rank_config(&comm, world, uid, rank, &config);
+        const auto t0 = Clock::now();
+        while (r == ncclInProgress && comm) {
+            nc.async_error(comm, &r);
+            if (r == ncclInProgress && seconds_since(t0) > dev->nccl_timeout_s) {
+                nc.abort(comm);
+                throw Error(MDN_ERR_NCCL, "ncclCommInitRankConfig: the ranks did not all join within " +
+                                              std::to_string(dev->nccl_timeout_s) + " s");
+            }
+            if (r == ncclInProgress) std::this_thread::sleep_for(std::chrono::milliseconds(1));
+        }
+        if (r != ncclSuccess && comm) nc.abort(comm);
+        require(r == ncclSuccess, MDN_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + nc.error_string(r));
+        dev->comm_failed = false;
         dev->nccl_comm = comm;
     });
 }
@@ -120,6 +218,7 @@ extern "C" int mdn_comm_destroy(mdn_device* dev) {
             if (nccl().ok) nccl().destroy(static_cast<ncclComm_t>(dev->nccl_comm));
             dev->nccl_comm = nullptr;
         }
+        dev->comm_failed = false;
         dev->rank = 0;
         dev->world = 1;
     });

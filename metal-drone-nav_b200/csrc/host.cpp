@@ -13,6 +13,7 @@
 #include <string>
 
 #include "host_common.h"
+#include "ppo_tc.h"
 
 namespace mdn {
 static thread_local std::string g_last_error;
@@ -176,7 +177,7 @@ extern "C" int mdn_sync(mdn_device* dev, double* gpu_seconds) {
         use_device(dev);
         double total = 0.0;
         for (mdn_sim* s : dev->sims) {
-            cuda_check(cudaStreamSynchronize(s->stream), "stream synchronize");
+            sync_stream(dev, s->stream, "stream synchronize");
             total += s->last_collect_ms * 1e-3;
             if (s->wide_error) {
                 uint32_t flag = 0;
@@ -660,7 +661,7 @@ extern "C" int mdn_sim_set_runtime(mdn_sim* sim, const mdn_runtime_config* runti
 extern "C" int mdn_sim_last_collect_ms(mdn_sim* sim, float* ms) {
     return guarded([&] {
         checked(sim);
-        cuda_check(cudaEventSynchronize(sim->ev_stop), "event sync");
+        sync_event(sim->dev, sim->ev_stop, "event sync");
         cuda_check(cudaEventElapsedTime(&sim->last_collect_ms, sim->ev_start, sim->ev_stop), "elapsed");
         if (ms) *ms = sim->last_collect_ms;
     });
@@ -688,7 +689,7 @@ extern "C" int mdn_sim_download(mdn_sim* sim, int id, void* host, size_t offset,
         require(offset <= sim->bytes[id] && bytes <= sim->bytes[id] - offset, MDN_ERR_INVALID, "download out of range");
         cuda_check(cudaMemcpyAsync(host, static_cast<char*>(sim->buf[id]) + offset, bytes, cudaMemcpyDeviceToHost,
                                    sim->stream), "download");
-        cuda_check(cudaStreamSynchronize(sim->stream), "download");
+        sync_stream(sim->dev, sim->stream, "download");
     });
 }
 
@@ -716,7 +717,7 @@ extern "C" int mdn_sim_report(mdn_sim* sim, double out[10]) {
         std::vector<mdn_sim_run> runs(sim->n);
         cuda_check(cudaMemcpyAsync(runs.data(), sim->buf[MDN_BUF_RUNS], sim->bytes[MDN_BUF_RUNS], cudaMemcpyDeviceToHost,
                                    sim->stream), "report");
-        cuda_check(cudaStreamSynchronize(sim->stream), "report");
+        sync_stream(sim->dev, sim->stream, "report");
         // Sim::report, main.mm:599-602
         double v[10] = {0, 0, 0, 0, 0, 0, 0, 0, 12.0, 0.0};
         for (const auto& r : runs) {
@@ -760,6 +761,18 @@ extern "C" int mdn_selftest_division(mdn_device* dev, uint64_t samples, uint64_t
         require(dev != nullptr && mismatches != nullptr, MDN_ERR_INVALID, "division self-test: null argument");
         use_device(dev);
         cuda_check(division_check(samples, seed, mismatches, dev->sm_count), "division self-test");
+    });
+}
+
+extern "C" int mdn_selftest_barrier_timeout(mdn_device* dev, uint64_t limit_cycles, int arrive) {
+    return guarded([&] {
+        require(dev != nullptr && limit_cycles > 0 && limit_cycles < (uint64_t(1) << 40), MDN_ERR_INVALID,
+                "barrier self-test: bad argument");
+        use_device(dev);
+        uint32_t timed_out = 0;
+        cuda_check(barrier_selftest((long long)limit_cycles, arrive, &timed_out), "barrier self-test");
+        require(timed_out == 0, MDN_ERR_TIMEOUT,
+                "barrier self-test: the bounded wait gave up after " + std::to_string(limit_cycles) + " cycles");
     });
 }
 

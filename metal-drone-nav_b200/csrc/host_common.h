@@ -67,6 +67,13 @@ void read_checkpoint_header(std::ifstream& f, mdn_checkpoint_header& h);
 // Raises MDN_ERR_TIMEOUT when a trainer's tensor-core minibatch kernel gave up
 // on a barrier wait (ppo_host.cpp); the device's streams must be idle.
 void check_trainer_errors(struct ::mdn_device* dev);
+// Host waits of a device's work (comm.cpp). On one GPU they are
+// cudaStreamSynchronize / cudaEventSynchronize. Under NCCL they poll, so a
+// collective stuck on a lost peer cannot block the host forever: a
+// communicator error, or no completion within the device's deadline, aborts
+// the communicator and raises MDN_ERR_NCCL.
+void sync_stream(struct ::mdn_device* dev, cudaStream_t s, const char* what);
+void sync_event(struct ::mdn_device* dev, cudaEvent_t e, const char* what);
 
 }  // namespace mdn
 
@@ -77,6 +84,8 @@ struct mdn_device {
     // multi-GPU
     int rank = 0, world = 1;
     void* nccl_comm = nullptr;
+    bool comm_failed = false;     // the communicator was aborted (a peer failed or timed out)
+    double nccl_timeout_s = 600;  // host deadline of a collective (MDN_NCCL_TIMEOUT_S)
     std::vector<struct mdn_sim*> sims;
     std::vector<struct mdn_ppo*> trainers;
 };

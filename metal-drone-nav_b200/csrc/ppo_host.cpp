@@ -408,7 +408,9 @@ extern "C" int mdn_ppo_rollout_update(mdn_ppo* t, uint32_t rollout_index) {
         }
         std::vector<uint32_t> order;
         chunk_order(t, rollout_index, order);
-        cuda_check(cudaEventSynchronize(t->staged), "staging reuse");
+        require(!sim->dev->comm_failed, MDN_ERR_NCCL,
+                "rollout update: the NCCL communicator was aborted after a failure; re-create it (mdn_comm_init)");
+        sync_event(sim->dev, t->staged, "staging reuse");
         const uint32_t U = t->updates;
         for (uint32_t u = 0; u < U; u++) {
             const uint32_t begin = order[u];
@@ -497,7 +499,7 @@ void check_trainer_errors(mdn_device* dev) {
 extern "C" int mdn_ppo_last_update_ms(mdn_ppo* t, float* ms) {
     return guarded([&] {
         checked(t);
-        cuda_check(cudaEventSynchronize(t->ev_stop), "event sync");
+        sync_event(t->sim->dev, t->ev_stop, "event sync");
         cuda_check(cudaEventElapsedTime(&t->last_update_ms, t->ev_start, t->ev_stop), "elapsed");
         if (ms) *ms = t->last_update_ms;
     });
@@ -508,7 +510,7 @@ extern "C" int mdn_ppo_metrics(mdn_ppo* t, float out[4]) {
         checked(t);
         require(out != nullptr, MDN_ERR_INVALID, "null out");
         cuda_check(cudaMemcpyAsync(out, t->args.metric_mean, 16, cudaMemcpyDeviceToHost, t->sim->stream), "metrics");
-        cuda_check(cudaStreamSynchronize(t->sim->stream), "metrics");
+        sync_stream(t->sim->dev, t->sim->stream, "metrics");
     });
 }
 
@@ -538,7 +540,7 @@ extern "C" int mdn_ppo_moments(mdn_ppo* t, int which, float* host, size_t count,
         cuda_check(upload ? cudaMemcpyAsync(d, host, n * 4, cudaMemcpyHostToDevice, t->sim->stream)
                           : cudaMemcpyAsync(host, d, n * 4, cudaMemcpyDeviceToHost, t->sim->stream),
                    "moments");
-        cuda_check(cudaStreamSynchronize(t->sim->stream), "moments");
+        sync_stream(t->sim->dev, t->sim->stream, "moments");
     });
 }
 
@@ -548,7 +550,7 @@ extern "C" int mdn_ppo_grad_norms(mdn_ppo* t, float* host_rows, size_t count) {
         require(host_rows && count == size_t(t->updates) * 2, MDN_ERR_INVALID, "grad norms: count must be 2*updates");
         cuda_check(cudaMemcpyAsync(host_rows, t->args.grad_norms, count * 4, cudaMemcpyDeviceToHost, t->sim->stream),
                    "grad norms");
-        cuda_check(cudaStreamSynchronize(t->sim->stream), "grad norms");
+        sync_stream(t->sim->dev, t->sim->stream, "grad norms");
     });
 }
 
@@ -794,6 +796,35 @@ extern "C" int mdn_checkpoint_inspect(const char* path, mdn_checkpoint_header* h
         }
         if (runtime) *runtime = rt;
         if (tasks) *tasks = tc;
+    });
+}
+
+extern "C" int mdn_ppo_profile_minibatch(mdn_ppo* t, uint32_t update, float* ms) {
+    return guarded([&] {
+        checked(t);
+        require(ms != nullptr && update < t->updates, MDN_ERR_INVALID, "profile minibatch: bad argument");
+        require(t->graph != nullptr, MDN_ERR_STATE, "profile minibatch: run one rollout update first");
+        require(!t->wide, MDN_ERR_INVALID, "profile minibatch: the 64-unit actor's minibatch kernels only");
+        mdn_sim* sim = t->sim;
+        cudaStream_t s = sim->stream;
+        const bool multi = sim->dev->world > 1;
+        cudaEvent_t e0, e1;
+        cuda_check(cudaEventCreate(&e0), "event");
+        cuda_check(cudaEventCreate(&e1), "event");
+        cuda_check(cudaEventRecord(e0, s), "event");
+        if (t->tensor_cores) {
+            PpoArgs pt = t->args;
+            pt.fwd_grid = multi ? std::max<uint32_t>(t->tc_grid, 2) : t->tc_grid;
+            cuda_check(launch_minibatch_tc(pt, t->tc_maps, update, pt.fwd_grid, s), "tensor-core minibatch");
+        } else {
+            const uint32_t chunks = multi ? std::max<uint32_t>(t->grad_chunks, 2) : t->grad_chunks;
+            cuda_check(launch_minibatch(t->args, update, chunks, s), "minibatch");
+        }
+        cuda_check(cudaEventRecord(e1, s), "event");
+        cuda_check(cudaEventSynchronize(e1), "event");
+        cuda_check(cudaEventElapsedTime(ms, e0, e1), "event");
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
     });
 }
 

@@ -25,9 +25,9 @@
 // once from HBM. At the end each CTA writes its gradient partial in the layout
 // of k_mb_fused, so k_grad_reduce / k_clip_adam apply unchanged.
 //
-// Warp roles: warp 0 issues TMA loads (one ring of 16 KB row panels for
-// both layouts), warp 1 owns tensor memory and issues the MMAs, warps 2-9 are
-// the epilogue. Every barrier wait is bounded; a wait that gives up sets a
+// Warp roles: warp 0 loads the forward panels, warp 10 the weight-gradient
+// panels (two rings of 16 KB row panels), warp 1 owns tensor memory and
+// issues the MMAs, warps 2-9 are the epilogue. Every barrier wait is bounded; a wait that gives up sets a
 // bit of the error flag and the kernel winds down.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -46,12 +46,18 @@ constexpr int kTcRows = 128;                  // rows per tile
 constexpr int kTcPanel = 32;                  // fp32 columns per 128-byte panel
 constexpr int kTcObsPanels = 6;               // 184 inputs padded to 192 (TMA zero-fills)
 constexpr int kTcInPanels = kTcObsPanels + 1; // + the critic's 32 inputs
-constexpr int kTcStages = 6;
+// Two rings of 128-row panels: the K-major panels of the forward (read from
+// HBM) and the MN-major panels of the weight gradients (re-read from L2),
+// each with its own producer warp, so forward loads keep streaming while
+// weight-gradient panels wait for a tile's deltas.
+constexpr int kKStages = 4;
+constexpr int kMStages = 2;
 constexpr int kTcStageBytes = kTcRows * 128;  // one 128-row panel
 constexpr int kTcWPanelBytes = kHidden * 128; // one 64-row weight panel
 constexpr int kTcDeltaBytes = kHidden * 128;  // 64 hidden x 32 rows, K-major
 constexpr int kTcEpiWarps = 8;
-constexpr int kTcThreads = (2 + kTcEpiWarps) * 32;
+constexpr int kWarpKProducer = 0, kWarpMma = 1, kWarpEpi0 = 2, kWarpMProducer = 2 + kTcEpiWarps;
+constexpr int kTcThreads = (kWarpMProducer + 1) * 32;
 constexpr int kTcChunks = 15;                 // per-lane small-gradient columns (see epilogue)
 constexpr long long kTcWaitLimit = 2000000000ll;
 
@@ -61,8 +67,9 @@ constexpr uint32_t kColGa = 256;   // G_a panel p at 256 + 32 p (p < 6)
 constexpr uint32_t kColGc = 448;   // G_c
 
 // shared-memory layout (from a 1024-byte aligned base)
-constexpr size_t kOffRing = 0;
-constexpr size_t kOffW1 = kOffRing + size_t(kTcStages) * kTcStageBytes;
+constexpr size_t kOffKRing = 0;
+constexpr size_t kOffMRing = kOffKRing + size_t(kKStages) * kTcStageBytes;
+constexpr size_t kOffW1 = kOffMRing + size_t(kMStages) * kTcStageBytes;
 constexpr size_t kOffCw1 = kOffW1 + size_t(kTcObsPanels) * kTcWPanelBytes;
 constexpr size_t kOffDa = kOffCw1 + kTcWPanelBytes;
 constexpr size_t kOffDc = kOffDa + 4 * size_t(kTcDeltaBytes);
@@ -72,20 +79,22 @@ constexpr int kParFloats = 64 + 256 + 64 + 64 + 4 + 4 + 4;
 constexpr size_t kOffBar = kOffPar + kParFloats * sizeof(float);
 
 struct TcBarriers {
-    uint64_t full[kTcStages];
-    uint64_t empty[kTcStages];
-    uint64_t fwd_full[2];
-    uint64_t fwd_empty[2];
-    uint64_t delta_full;
-    uint64_t delta_empty;
+    uint64_t kfull[kKStages];
+    uint64_t kempty[kKStages];
+    uint64_t mfull[kMStages];
+    uint64_t mempty[kMStages];
+    uint64_t fwd_full[2];     // per accumulator buffer: forward of its tile done
+    uint64_t fwd_empty[2];    // per accumulator buffer: the epilogue has read it
+    uint64_t delta_full;      // a tile's deltas are in shared memory (4 warps)
+    uint64_t delta_empty[2];  // the weight gradients of an even / odd tile are done
     uint64_t weights;
     uint64_t final_mma;
     uint32_t tmem_base;
 };
 constexpr size_t kTcSmem = 1024 + kOffBar + sizeof(TcBarriers);
 static_assert(kTcSmem <= 227 * 1024, "tensor-core minibatch kernel exceeds the shared-memory budget");
-static_assert(size_t(kTcEpiWarps) * kTcChunks * 32 * sizeof(float) <= size_t(kTcStages) * kTcStageBytes,
-              "final reduction staging reuses the ring");
+static_assert(size_t(kTcEpiWarps) * kTcChunks * 32 * sizeof(float) <= size_t(kKStages) * kTcStageBytes,
+              "final reduction staging reuses the K ring");
 
 // tanh(x) = 1 - 2 / (1 + e^(2x)) on the hardware base-2 exponential and
 // reciprocal (ex2.approx / rcp.approx): absolute error ~1e-7, far below the
@@ -97,20 +106,27 @@ __device__ __forceinline__ float tc_tanh(float x) {
     return fmaf(-2.0f, r, 1.0f);
 }
 
+// One step of the halving tree: lanes with bit S set keep the upper half of
+// x[0..2S) (added to the partner's copy of it), the others the lower half.
+template <int S>
+__device__ __forceinline__ void column_sum_step(float (&x)[32], int lane) {
+    const bool upper = (lane & S) != 0;
+#pragma unroll
+    for (int i = 0; i < S; i++) {
+        const float send = upper ? x[i] : x[i + S];
+        const float keep = upper ? x[i + S] : x[i];
+        x[i] = keep + __shfl_xor_sync(0xffffffffu, send, S);
+    }
+}
 // Sum of x[i] over the warp's 32 lanes; lane j receives the total of column
 // j. A fixed halving tree (31 exchanges), so the result does not depend on
 // scheduling.
 __device__ __forceinline__ float lane_column_sum(float (&x)[32], int lane) {
-#pragma unroll
-    for (int s = 16; s >= 1; s >>= 1) {
-        const bool upper = (lane & s) != 0;
-#pragma unroll
-        for (int i = 0; i < s; i++) {
-            const float send = upper ? x[i] : x[i + s];
-            const float keep = upper ? x[i + s] : x[i];
-            x[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
-        }
-    }
+    column_sum_step<16>(x, lane);
+    column_sum_step<8>(x, lane);
+    column_sum_step<4>(x, lane);
+    column_sum_step<2>(x, lane);
+    column_sum_step<1>(x, lane);
     return x[0];
 }
 
@@ -129,7 +145,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t update) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* ring = smem + kOffRing;
+    uint8_t* kring = smem + kOffKRing;
+    uint8_t* mring = smem + kOffMRing;
     uint8_t* w1s = smem + kOffW1;
     uint8_t* cw1s = smem + kOffCw1;
     uint8_t* da = smem + kOffDa;
@@ -145,16 +162,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto tile_row0 = [&](uint32_t j) { return int32_t(begin + (blockIdx.x + j * gridDim.x) * kTcRows); };
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kTcStages; i++) {
-            tc::mbar_init(&s.full[i], 1);
-            tc::mbar_init(&s.empty[i], 1);
+        for (int i = 0; i < kKStages; i++) {
+            tc::mbar_init(&s.kfull[i], 1);
+            tc::mbar_init(&s.kempty[i], 1);
+        }
+        for (int i = 0; i < kMStages; i++) {
+            tc::mbar_init(&s.mfull[i], 1);
+            tc::mbar_init(&s.mempty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
             tc::mbar_init(&s.fwd_full[i], 1);
             tc::mbar_init(&s.fwd_empty[i], 4);
+            tc::mbar_init(&s.delta_empty[i], 1);
         }
         tc::mbar_init(&s.delta_full, 4);
-        tc::mbar_init(&s.delta_empty, 1);
         tc::mbar_init(&s.weights, 1);
         tc::mbar_init(&s.final_mma, 1);
         tc::fence_barrier_init();
@@ -163,7 +184,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc::prefetch_tmap(&co_k);
         tc::prefetch_tmap(&co_mn);
     }
-    if (warp == 1) {
+    if (warp == kWarpMma) {
         tc::tmem_alloc(&s.tmem_base, 512);
         tc::tmem_relinquish();
     }
@@ -184,132 +205,138 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc::fence_after_sync();
     const uint32_t tmem = s.tmem_base;
 
-    if (warp == 0 && lane == 0) {
-        // ------------------------------------------------------ TMA producer
-        // order: K(0); then for s >= 1: K(s), MN(s - 1) -- the next tile's
-        // forward panels go ahead of this tile's weight-gradient panels.
+    // One ring of 16 KB panels: `it` counts the panels through it.
+    auto ring_load = [&](uint8_t* ring, uint64_t* full, uint64_t* empty, int stages, uint32_t& it,
+                         const CUtensorMap* map, int32_t x, int32_t y) {
+        const uint32_t st = it % stages, use = it / stages;
+        if (use > 0 && !tc::mbar_wait(&empty[st], (use - 1) & 1, kTcWaitLimit)) return false;
+        tc::mbar_arrive_expect_tx(&full[st], kTcStageBytes);
+        tc::tma_load_2d(ring + size_t(st) * kTcStageBytes, map, x, y, &full[st]);
+        it++;
+        return true;
+    };
+    auto ring_drain = [&](uint64_t* full, int stages, uint32_t it) {
+        // every copy this warp issued has landed before the CTA may exit
         bool ok = true;
+        for (uint32_t k = it > uint32_t(stages) ? it - stages : 0; k < it; k++)
+            if (!tc::mbar_wait(&full[k % stages], (k / stages) & 1, kTcWaitLimit)) ok = false;
+        return ok;
+    };
+
+    if (warp == kWarpKProducer && lane == 0) {
+        // ------------------------------------- forward panels (K-major, HBM)
+        bool ok = true;
+        uint32_t it = 0;
         if (count > 0) {
             tc::mbar_arrive_expect_tx(&s.weights, (kTcObsPanels + 1) * kTcWPanelBytes);
             for (int q = 0; q < kTcObsPanels; q++)
                 tc::tma_load_2d(w1s + q * kTcWPanelBytes, &w1_map, q * kTcPanel, 0, &s.weights);
             tc::tma_load_2d(cw1s, &cw1_map, 0, 0, &s.weights);
         }
-        uint32_t it = 0;
-        auto load = [&](const CUtensorMap* map, int32_t x, int32_t y) {
-            const uint32_t st = it % kTcStages, use = it / kTcStages;
-            if (use > 0 && !tc::mbar_wait(&s.empty[st], (use - 1) & 1, kTcWaitLimit)) return false;
-            tc::mbar_arrive_expect_tx(&s.full[st], kTcStageBytes);
-            tc::tma_load_2d(ring + size_t(st) * kTcStageBytes, map, x, y, &s.full[st]);
-            it++;
-            return true;
-        };
-        for (uint32_t t = 0; t <= count && ok && count > 0; t++) {
-            if (t < count) {
-                const int32_t y = tile_row0(t);
-                for (int q = 0; q < kTcObsPanels && ok; q++) ok = load(&obs_k, q * kTcPanel, y);
-                if (ok) ok = load(&co_k, 0, y);
-            }
-            if (t >= 1 && ok) {
-                const int32_t y = tile_row0(t - 1);
-                for (int q = 0; q < kTcObsPanels && ok; q++) ok = load(&obs_mn, q * kTcPanel, y);
-                if (ok) ok = load(&co_mn, 0, y);
-            }
+        for (uint32_t t = 0; t < count && ok; t++) {
+            const int32_t y = tile_row0(t);
+            for (int q = 0; q < kTcObsPanels && ok; q++)
+                ok = ring_load(kring, s.kfull, s.kempty, kKStages, it, &obs_k, q * kTcPanel, y);
+            if (ok) ok = ring_load(kring, s.kfull, s.kempty, kKStages, it, &co_k, 0, y);
         }
-        // every copy this CTA issued has landed before it may exit
-        for (uint32_t k = it > kTcStages ? it - kTcStages : 0; k < it; k++)
-            if (!tc::mbar_wait(&s.full[k % kTcStages], (k / kTcStages) & 1, kTcWaitLimit)) ok = false;
+        if (!ring_drain(s.kfull, kKStages, it)) ok = false;
         if (count > 0 && !tc::mbar_wait(&s.weights, 0, kTcWaitLimit)) ok = false;
         if (!ok) atomicOr(p.tc_error, 1u);
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == kWarpMProducer && lane == 0) {
+        // -------------------------------- weight-gradient panels (MN-major, L2)
+        bool ok = true;
+        uint32_t it = 0;
+        for (uint32_t t = 0; t < count && ok; t++) {
+            const int32_t y = tile_row0(t);
+            for (int q = 0; q < kTcObsPanels && ok; q++)
+                ok = ring_load(mring, s.mfull, s.mempty, kMStages, it, &obs_mn, q * kTcPanel, y);
+            if (ok) ok = ring_load(mring, s.mfull, s.mempty, kMStages, it, &co_mn, 0, y);
+        }
+        if (!ring_drain(s.mfull, kMStages, it)) ok = false;
+        if (!ok) atomicOr(p.tc_error, 16u);
+    } else if (warp == kWarpMma && lane == 0) {
         // ------------------------------------------------------- MMA issuer
+        // Event loop over two streams of work, each advanced one panel at a
+        // time when its inputs are ready: forwards (tile f, panel fp) run up to
+        // two tiles ahead of the epilogue (two accumulator buffers); weight
+        // gradients (tile w, panel wp) follow each tile's deltas.
         constexpr uint32_t idesc_fwd = tc::tf32_idesc(kTcRows, kHidden, 0, 0);
         constexpr uint32_t idesc_wg = tc::tf32_idesc(kHidden, kTcPanel, 0, 1);
         bool ok = count == 0 || tc::mbar_wait(&s.weights, 0, kTcWaitLimit);
-        uint32_t it = 0;
-        auto take = [&](uint32_t& addr) {
-            const uint32_t st = it % kTcStages;
-            if (!tc::mbar_wait(&s.full[st], (it / kTcStages) & 1, kTcWaitLimit)) return false;
-            tc::fence_after_sync();
-            addr = tc::smem_u32(ring + size_t(st) * kTcStageBytes);
-            return true;
-        };
-        auto release = [&]() {
-            tc::mma_commit(&s.empty[it % kTcStages]);
-            it++;
-        };
-        for (uint32_t t = 0; t <= count && ok && count > 0; t++) {
-            if (t < count) {
-                // forward of tile t into accumulator buffer t & 1
-                const uint32_t buf = t & 1;
-                if (t >= 2 && !tc::mbar_wait(&s.fwd_empty[buf], ((t >> 1) - 1) & 1, kTcWaitLimit)) {
-                    ok = false;
-                    break;
+        uint32_t f = 0, fp = 0, w = 0, wp = 0, kit = 0, mit = 0;
+        bool f_ready = false, w_ready = false;
+        long long idle_since = clock64();
+        while (ok && w < count) {
+            bool progressed = false;
+            if (f < count) {
+                if (!f_ready) {
+                    f_ready = f < 2 || tc::mbar_test_wait(&s.fwd_empty[f & 1], ((f >> 1) - 1) & 1);
+                    if (f_ready) tc::fence_after_sync();
                 }
-                tc::fence_after_sync();
-                const uint32_t d_a = tmem + kColD + 128 * buf, d_c = d_a + 64;
-                for (int q = 0; q < kTcInPanels && ok; q++) {
-                    uint32_t a_addr;
-                    if (!take(a_addr)) {
-                        ok = false;
-                        break;
-                    }
-                    const bool critic = q == kTcObsPanels;
-                    const uint32_t b_addr = tc::smem_u32(critic ? cw1s : w1s + q * kTcWPanelBytes);
+                if (f_ready && tc::mbar_test_wait(&s.kfull[kit % kKStages], (kit / kKStages) & 1)) {
+                    tc::fence_after_sync();
+                    const uint32_t a_addr = tc::smem_u32(kring + size_t(kit % kKStages) * kTcStageBytes);
+                    const bool critic = fp == kTcObsPanels;
+                    const uint32_t b_addr = tc::smem_u32(critic ? cw1s : w1s + fp * kTcWPanelBytes);
+                    const uint32_t d = tmem + kColD + 128 * (f & 1) + (critic ? 64 : 0);
 #pragma unroll
                     for (int kk = 0; kk < kTcPanel / 8; kk++)
-                        tc::mma_tf32(critic ? d_c : d_a, tc::sw128_desc(a_addr + kk * 32, 16, 1024),
+                        tc::mma_tf32(d, tc::sw128_desc(a_addr + kk * 32, 16, 1024),
                                      tc::sw128_desc(b_addr + kk * 32, 16, 1024), idesc_fwd,
-                                     (!critic && q != 0) || kk != 0 ? 1u : 0u);
-                    release();
-                }
-                if (!ok) break;
-                tc::mma_commit(&s.fwd_full[buf]);
-            }
-            if (t >= 1) {
-                // weight gradients of tile j = t - 1 once its deltas are in shared memory
-                const uint32_t j = t - 1;
-                if (!tc::mbar_wait(&s.delta_full, j & 1, kTcWaitLimit)) {
-                    ok = false;
-                    break;
-                }
-                tc::fence_after_sync();
-                for (int q = 0; q < kTcInPanels && ok; q++) {
-                    uint32_t b_addr;
-                    if (!take(b_addr)) {
-                        ok = false;
-                        break;
+                                     (!critic && fp != 0) || kk != 0 ? 1u : 0u);
+                    tc::mma_commit(&s.kempty[kit % kKStages]);
+                    kit++;
+                    progressed = true;
+                    if (++fp == kTcInPanels) {
+                        tc::mma_commit(&s.fwd_full[f & 1]);
+                        f++;
+                        fp = 0;
+                        f_ready = false;
                     }
-                    const bool critic = q == kTcObsPanels;
+                }
+            }
+            if (w < f) {  // a tile's deltas exist only after its forward
+                if (!w_ready) {
+                    w_ready = tc::mbar_test_wait(&s.delta_full, w & 1);
+                    if (w_ready) tc::fence_after_sync();
+                }
+                if (w_ready && tc::mbar_test_wait(&s.mfull[mit % kMStages], (mit / kMStages) & 1)) {
+                    tc::fence_after_sync();
+                    const uint32_t b_addr = tc::smem_u32(mring + size_t(mit % kMStages) * kTcStageBytes);
+                    const bool critic = wp == kTcObsPanels;
                     const uint32_t a_base = tc::smem_u32(critic ? dc : da);
-                    const uint32_t d = tmem + (critic ? kColGc : kColGa + 32 * q);
+                    const uint32_t d = tmem + (critic ? kColGc : kColGa + 32 * wp);
 #pragma unroll
-                    for (int w = 0; w < 4; w++)          // the tile's four 32-row groups (K)
+                    for (int g = 0; g < 4; g++)          // the tile's four 32-row groups (K)
 #pragma unroll
                         for (int kk = 0; kk < 4; kk++)   // 8 rows per MMA
-                            tc::mma_tf32(d, tc::sw128_desc(a_base + w * kTcDeltaBytes + kk * 32, 16, 1024),
-                                         tc::sw128b32_desc(b_addr + (32 * w + 8 * kk) * 128, kTcStageBytes, 512),
-                                         idesc_wg, (j | w | kk) != 0 ? 1u : 0u);
-                    release();
+                            tc::mma_tf32(d, tc::sw128_desc(a_base + g * kTcDeltaBytes + kk * 32, 16, 1024),
+                                         tc::sw128b32_desc(b_addr + (32 * g + 8 * kk) * 128, kTcStageBytes, 512),
+                                         idesc_wg, (w | g | kk) != 0 ? 1u : 0u);
+                    tc::mma_commit(&s.mempty[mit % kMStages]);
+                    mit++;
+                    progressed = true;
+                    if (++wp == kTcInPanels) {
+                        tc::mma_commit(&s.delta_empty[w & 1]);
+                        w++;
+                        wp = 0;
+                        w_ready = false;
+                    }
                 }
-                if (!ok) break;
-                tc::mma_commit(&s.delta_empty);
+            }
+            if (progressed) {
+                idle_since = clock64();
+            } else if (clock64() - idle_since > kTcWaitLimit) {
+                ok = false;
             }
         }
         tc::mma_commit(&s.final_mma);
         if (!ok) atomicOr(p.tc_error, 2u);
-    } else if (warp >= 2) {
+    } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + kTcEpiWarps) {
         // --------------------------------------------------------- epilogue
-        const int ew = warp - 2;   // 0..7
-        const int g = ew >> 2;     // this group takes the tiles j with j % 2 == g (accumulator buffer g)
-        const int q = warp & 3;    // tensor-memory lanes 32q..32q+31 = rows 32q..32q+31 of a tile
-        const float* b1 = par;
-        const float* w2 = par + 64;
-        const float* cb1 = par + 320;
-        const float* cw2 = par + 384;
-        const float* b2 = par + 448;
-        const float* log_std = par + 452;
-        const float cb2 = par[456];
+        const int ew = warp - kWarpEpi0;  // 0..7
+        const int g = ew >> 2;            // this group takes the tiles j with j % 2 == g (accumulator buffer g)
+        const int q = warp & 3;           // tensor-memory lanes 32q..32q+31 = rows 32q..32q+31 of a tile
         const float scale = 1.0f / fmaxf(float(p.global_batch[update]), 1.0f);
         // Per-lane running sums, lane j holding column j of each chunk:
         // 0-7 dW2[a][32c + j] (chunk 2a + c), 8-9 critic w2, 10-11 b1,
@@ -324,39 +351,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 break;
             }
             tc::fence_after_sync();
+            // The parameters are re-read from shared memory every tile: the
+            // opaque pointer keeps the compiler from hoisting ~450 loop-invariant
+            // loads into registers (and spilling them).
+            const float* pr = par;
+            asm volatile("" : "+l"(pr));
+            const float* b1 = pr;
+            const float* w2 = pr + 64;
+            const float* cb1 = pr + 320;
+            const float* cw2 = pr + 384;
+            const float* b2 = pr + 448;
+            const float* log_std = pr + 452;
+            const float cb2 = pr[456];
             const uint32_t local = (blockIdx.x + j * gridDim.x) * kTcRows + 32 * q + lane;  // row of the minibatch
             const bool valid = local < b;
             const size_t src = size_t(begin) + local;
             const uint32_t lane_addr = tmem + (uint32_t(32 * q) << 16) + kColD + 128 * g;
-            float hc[64], hh[64];
+            // Activations: the value and means are formed in fp32 as the tanh
+            // values are produced, and the tanh values replace the
+            // pre-activations in tensor memory, where the backward reads them
+            // 32 at a time (the buffer is released at the end of the tile).
+            float value = cb2, mean[4];
+#pragma unroll
+            for (int a = 0; a < 4; a++) mean[a] = b2[a];
             {
                 float v[32];
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     tc::tmem_ld32(lane_addr + 64 + 32 * c, v);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) hc[32 * c + i] = tc_tanh(v[i] + cb1[32 * c + i]);
+                    for (int i = 0; i < 32; i++) {
+                        v[i] = tc_tanh(v[i] + cb1[32 * c + i]);
+                        value = fmaf(cw2[32 * c + i], v[i], value);
+                    }
+                    tc::tmem_st32(lane_addr + 64 + 32 * c, v);
                 }
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     tc::tmem_ld32(lane_addr + 32 * c, v);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) hh[32 * c + i] = tc_tanh(v[i] + b1[32 * c + i]);
+                    for (int i = 0; i < 32; i++) {
+                        v[i] = tc_tanh(v[i] + b1[32 * c + i]);
+#pragma unroll
+                        for (int a = 0; a < 4; a++) mean[a] = fmaf(w2[a * 64 + 32 * c + i], v[i], mean[a]);
+                    }
+                    tc::tmem_st32(lane_addr + 32 * c, v);
                 }
-            }
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&s.fwd_empty[g]);  // the accumulator buffer is free again
-            float value = cb2;
-#pragma unroll
-            for (int i = 0; i < 64; i++) value = fmaf(cw2[i], hc[i], value);
-            float mean[4];
-#pragma unroll
-            for (int a = 0; a < 4; a++) {
-                float m = b2[a];
-#pragma unroll
-                for (int i = 0; i < 64; i++) m = fmaf(w2[a * 64 + i], hh[i], m);
-                mean[a] = m;
+                tc::tmem_wait_st();
             }
             // clipped-PPO loss and derivatives (ppo.hpp:144-181)
             float dm[4] = {0, 0, 0, 0}, dls[4] = {0, 0, 0, 0}, dvalue = 0.0f, loss[4] = {0, 0, 0, 0};
@@ -396,35 +437,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 loss[2] = entropy;
                 loss[3] = ratio;
             }
-            float x[32];
-            // dW2[a][h] = sum over rows of d_mean[a] tanh_h; critic w2 = sum d_value tanh_c
-#pragma unroll
-            for (int a = 0; a < 4; a++)
-#pragma unroll
-                for (int c = 0; c < 2; c++) {
-#pragma unroll
-                    for (int i = 0; i < 32; i++) x[i] = dm[a] * hh[32 * c + i];
-                    acc[2 * a + c] += lane_column_sum(x, lane);
-                }
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
-#pragma unroll
-                for (int i = 0; i < 32; i++) x[i] = dvalue * hc[32 * c + i];
-                acc[8 + c] += lane_column_sum(x, lane);
-            }
-            // hidden deltas, in place: (W2^T d_mean)(1 - h^2) and d_value cw2 (1 - hc^2)
-#pragma unroll
-            for (int i = 0; i < 64; i++) {
-                float sv = dm[0] * w2[i];
-                sv = fmaf(dm[1], w2[64 + i], sv);
-                sv = fmaf(dm[2], w2[128 + i], sv);
-                sv = fmaf(dm[3], w2[192 + i], sv);
-                hh[i] = sv * (1.0f - hh[i] * hh[i]);
-                hc[i] = dvalue * cw2[i] * (1.0f - hc[i] * hc[i]);
-            }
-            // The previous tile's weight-gradient MMAs must be done reading the
-            // delta operands before they are overwritten.
-            if (j >= 1 && !tc::mbar_wait(&s.delta_empty, (j - 1) & 1, kTcWaitLimit)) {
+            // hidden deltas (W2^T d_mean)(1 - h^2) and d_value cw2 (1 - hc^2)
+            // The previous tile's weight-gradient MMAs (tile j - 1, the other
+            // group's) must be done reading the delta operands first.
+            if (j >= 1 && !tc::mbar_wait(&s.delta_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, kTcWaitLimit)) {
                 ok = false;
                 break;
             }
@@ -436,24 +452,66 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 uint8_t* pc = dc + q * kTcDeltaBytes;
                 const uint32_t in_granule = (lane & 3) * 4;
 #pragma unroll
-                for (int h = 0; h < 64; h++) {
-                    const uint32_t off = (h >> 3) * 1024 + (h & 7) * 128 + ((((lane >> 2) ^ (h & 7))) << 4) + in_granule;
-                    *reinterpret_cast<float*>(pa + off) = hh[h];
-                    *reinterpret_cast<float*>(pc + off) = hc[h];
+                for (int c = 0; c < 2; c++) {
+                    float ha[32], hv[32];
+                    tc::tmem_ld32(lane_addr + 32 * c, ha);
+                    tc::tmem_ld32(lane_addr + 64 + 32 * c, hv);
+#pragma unroll
+                    for (int hb = 0; hb < 32; hb += 8) {
+#pragma unroll
+                        for (int i = hb; i < hb + 8; i++) {
+                            const int h = 32 * c + i;
+                            const uint32_t off =
+                                (h >> 3) * 1024 + (h & 7) * 128 + ((((lane >> 2) ^ (h & 7))) << 4) + in_granule;
+                            float sv = dm[0] * w2[h];
+                            sv = fmaf(dm[1], w2[64 + h], sv);
+                            sv = fmaf(dm[2], w2[128 + h], sv);
+                            sv = fmaf(dm[3], w2[192 + h], sv);
+                            // hidden deltas (W2^T d_mean)(1 - h^2) and d_value cw2 (1 - hc^2)
+                            *reinterpret_cast<float*>(pa + off) = sv * (1.0f - ha[i] * ha[i]);
+                            *reinterpret_cast<float*>(pc + off) = dvalue * cw2[h] * (1.0f - hv[i] * hv[i]);
+                        }
+                        // keeps the next block's weight loads below this point: the
+                        // compiler would otherwise issue all of them up front
+                        asm volatile("" ::: "memory");
+                    }
                 }
+            }
+            // this thread's delta of hidden unit h, read back from the operand it was stored to
+#define delta_smem(base, h)                                                                           \
+    (*reinterpret_cast<const float*>((base) + q * kTcDeltaBytes + ((h) >> 3) * 1024 + ((h) & 7) * 128 + \
+                                     ((((lane >> 2) ^ ((h) & 7))) << 4) + (lane & 3) * 4))
+            // b1 and critic b1 (sums of the deltas), read back before the operand
+            // is handed over: once delta_full completes, the other group may
+            // overwrite it with the next tile's deltas.
+            float x[32];
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+#pragma unroll
+                for (int i = 0; i < 32; i++) x[i] = delta_smem(da, 32 * c + i);
+                acc[10 + c] += lane_column_sum(x, lane);
+#pragma unroll
+                for (int i = 0; i < 32; i++) x[i] = delta_smem(dc, 32 * c + i);
+                acc[12 + c] += lane_column_sum(x, lane);
             }
             fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor cores
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&s.delta_full);
-            // b1 and critic b1: sums of the deltas
+            // the other small gradients, summed over the warp's rows
 #pragma unroll
             for (int c = 0; c < 2; c++) {
+                float v[32];
+                tc::tmem_ld32(lane_addr + 64 + 32 * c, v);
 #pragma unroll
-                for (int i = 0; i < 32; i++) x[i] = hh[32 * c + i];
-                acc[10 + c] += lane_column_sum(x, lane);
+                for (int i = 0; i < 32; i++) x[i] = dvalue * v[i];  // critic w2
+                acc[8 + c] += lane_column_sum(x, lane);
+                tc::tmem_ld32(lane_addr + 32 * c, v);
 #pragma unroll
-                for (int i = 0; i < 32; i++) x[i] = hc[32 * c + i];
-                acc[12 + c] += lane_column_sum(x, lane);
+                for (int a = 0; a < 4; a++) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) x[i] = dm[a] * v[i];  // dW2[a][h]
+                    acc[2 * a + c] += lane_column_sum(x, lane);
+                }
             }
 #pragma unroll
             for (int i = 0; i < 32; i++) x[i] = 0.0f;
@@ -465,12 +523,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             x[8] = dvalue;
             acc[14] += lane_column_sum(x, lane);
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&s.fwd_empty[g]);  // the accumulator buffer is free again
         }
+#undef delta_smem
         if (!ok) atomicOr(p.tc_error, 4u);
-        // every MMA is done: the weight-gradient accumulators are final and the ring is free
+        // every MMA is done: the weight-gradient accumulators are final and the rings are free
         const bool mma_done = count == 0 || tc::mbar_wait(&s.final_mma, 0, kTcWaitLimit);
         tc::fence_after_sync();
-        float* red = reinterpret_cast<float*>(ring);
+        float* red = reinterpret_cast<float*>(kring);
 #pragma unroll
         for (int k = 0; k < kTcChunks; k++) red[(ew * kTcChunks + k) * 32 + lane] = acc[k];
         epilogue_bar_sync();
@@ -511,10 +573,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kWarpMma) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, 512);
     }
+}
+
+// Bounded-wait self-test: one thread waits on a shared-memory mbarrier with
+// the same bounded wait the tensor-core kernels use. With arrive = 0 nothing
+// ever arrives, the wait gives up after `limit` cycles and the kernel records
+// it in *flag (no TMA, no MMA, no tensor memory); with arrive = 1 the thread
+// arrives first and the wait succeeds.
+__global__ void k_barrier_selftest(uint32_t* flag, long long limit, int arrive) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    tc::mbar_init(&bar, 1);
+    tc::fence_barrier_init();
+    if (arrive) tc::mbar_arrive(&bar);
+    *flag = tc::mbar_wait(&bar, 0, limit) ? 0u : 1u;
+}
+
+cudaError_t barrier_selftest(long long limit, int arrive, uint32_t* timed_out) {
+    uint32_t* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, sizeof(uint32_t));
+    if (e != cudaSuccess) return e;
+    k_barrier_selftest<<<1, 32>>>(d, limit, arrive);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpy(timed_out, d, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    return e;
 }
 
 // ------------------------------------------------------------- launchers

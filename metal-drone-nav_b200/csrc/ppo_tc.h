@@ -23,6 +23,9 @@ cudaError_t configure_tc_kernels();
 uint32_t tc_grid(uint32_t minibatch, int sm_count);
 // Gradient partials of minibatch `update` (grid CTAs, one partial each, in the
 // layout of the fp32 kernel) and their fixed-order sum into p.grad when grid > 1.
+// One bounded mbarrier wait on the device (k_barrier_selftest): *timed_out = 1
+// when it gave up after `limit` clock cycles.
+cudaError_t barrier_selftest(long long limit, int arrive, uint32_t* timed_out);
 cudaError_t launch_minibatch_tc(const PpoArgs& p, const TcMaps& m, uint32_t update, uint32_t grid, cudaStream_t s);
 
 }  // namespace mdn

@@ -8,7 +8,7 @@ one PPO update whose gradients and advantage statistics are allreduced by
 libmdn over NCCL, and saves its buffers to <outdir>/rank<r>.npz for the parent
 test to compare with a one-GPU run of all environments.
 
-  argv: outdir envs_per_rank horizon epochs minibatch_time_steps
+  argv: outdir envs_per_rank horizon epochs minibatch_time_steps tensor_cores(0|1)
 """
 import datetime
 import os
@@ -30,7 +30,7 @@ def config(pkg, n):
 
 def main():
     outdir = pathlib.Path(sys.argv[1])
-    n, horizon, epochs, mb_steps = (int(x) for x in sys.argv[2:6])
+    n, horizon, epochs, mb_steps, tensor_cores = (int(x) for x in sys.argv[2:7])
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -43,6 +43,7 @@ def main():
     dev.comm_init(rank, world, obj[0])
     sim = pkg.Sim(dev, config(pkg, n), horizon)
     tr = pkg.PPOTrainer(sim, epochs=epochs, minibatch=mb_steps * n)
+    tr.set_tensor_cores(bool(tensor_cores))
     sim.collect()
     tr.rollout_update(0)
     dev.finish()

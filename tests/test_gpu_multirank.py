@@ -18,8 +18,9 @@ rows and the same 1/B loss scale:
   gradient sums add the same rows in another order), except parameters whose
   accumulated gradient is at rounding level, bounded by 2*lr per update.
 
-Needs two GPUs; NVLS is off (NCCL_NVLS_ENABLE=0), the default actor path has
-no TMA.
+Both update paths run: the fp32 kernel and the tensor-core kernel (whose
+TMA loads read only this GPU's own memory). Needs two GPUs; NVLS is off
+(NCCL_NVLS_ENABLE=0).
 """
 import os
 import pathlib
@@ -52,12 +53,13 @@ def gpu_count():
 
 
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
-def test_two_ranks_equal_one_gpu(tmp_path):
+@pytest.mark.parametrize("tensor_cores", [False, True], ids=["fp32_update", "tensor_core_update"])
+def test_two_ranks_equal_one_gpu(tmp_path, tensor_cores):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={WORLD}", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
            str(ROOT / "tests" / "multirank_gpu_worker.py"), str(tmp_path), str(N_RANK), str(HORIZON), str(EPOCHS),
-           str(MB_STEPS)]
+           str(MB_STEPS), str(int(tensor_cores))]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     ranks = [np.load(tmp_path / f"rank{k}.npz") for k in range(WORLD)]
@@ -69,6 +71,7 @@ def test_two_ranks_equal_one_gpu(tmp_path):
     n = N_RANK * WORLD
     sim = pkg.Sim(dev, worker.config(pkg, n), HORIZON)
     tr = pkg.PPOTrainer(sim, epochs=EPOCHS, minibatch=MB_STEPS * n)
+    tr.set_tensor_cores(tensor_cores)
     try:
         sim.collect()
         U = EPOCHS * (HORIZON // MB_STEPS)
