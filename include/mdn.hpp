@@ -31,6 +31,8 @@
 namespace mdn {
 namespace host {
 
+static_assert(sizeof(mdn_checkpoint_header) == 136, "PPOFIX1 header (main.mm:978-984)");
+
 struct Error : std::runtime_error {
     int code;
     Error(int c, const std::string& what) : std::runtime_error(what), code(c) {}
@@ -193,3 +195,231 @@ private:
     Sim* sim_;
     mdn_ppo* h_ = nullptr;
 };
+
+// ---------------------------------------------------------------------------
+// navigation_training (navigation_training.hpp:7-170): goal-arrival task
+// settings, configuration and validation, actor loading, evaluation and the
+// training loop, over the classes above.
+namespace navigation_training {
+
+// task_settings (navigation_training.hpp:7-14): navigation_task_default_config
+// plus the trainer's overrides, as an enabled task control.
+inline mdn_task_control task_settings(uint32_t stage, uint32_t family) {
+    mdn_task_control control{};
+    control.enabled = 1;
+    check(mdn_task_settings(stage, family, 0.5f, &control.config));
+    return control;
+}
+
+// configure (:16-25): per-episode plant variation at `amplitude` and the task
+// control, then a reset of every environment.
+inline void configure(Sim& sim, const mdn_task_control& tasks, float amplitude) {
+    check(mdn_sim_configure_tasks(sim.get(), &tasks, amplitude));
+}
+
+// validate_rollout (:27-35): every task generated and every plant valid.
+inline void validate_rollout(Sim& sim) { check(mdn_sim_validate_tasks(sim.get())); }
+
+// load_actor (:37-61): the actor (and optionally the critic) of a PPOFIX1
+// checkpoint into `sim`, without its optimiser or simulator state. A critic of
+// another size is an incompatible warm start (this build's critic has the
+// reference's 32 inputs, so the 32 -> 64-input migration never applies).
+inline void load_actor(Sim& sim, const std::string& path, bool critic = false) {
+    mdn_checkpoint_header h{};
+    check(mdn_checkpoint_inspect(path.c_str(), &h, nullptr, nullptr));
+    require(h.actor_count == sim.actor_params, "task actor dimensions");
+    std::ifstream file(path, std::ios::binary);
+    require(bool(file), "cannot open " + path);
+    file.seekg(sizeof(mdn_checkpoint_header));  // the parameters follow the header
+    std::vector<float> actor(h.actor_count);
+    file.read(reinterpret_cast<char*>(actor.data()), std::streamsize(actor.size() * sizeof(float)));
+    require(bool(file), "task parameter load failed");
+    sim.upload(MDN_BUF_ACTOR, actor);
+    if (critic) {
+        require(h.critic_count == sim.critic_params, "task critic dimensions: incompatible warmstart");
+        std::vector<float> values(h.critic_count);
+        file.read(reinterpret_cast<char*>(values.data()), std::streamsize(values.size() * sizeof(float)));
+        require(bool(file), "task parameter load failed");
+        sim.upload(MDN_BUF_CRITIC, values);
+    }
+}
+
+struct Score {
+    double success = 0, collision = 0, timeout = 0, successful_time_s = 0;
+};
+
+// evaluate (:63-113): 128 evaluation environments of the task stage, one
+// 400-step episode each with the given actor, the per-environment CSV
+// (when `output` is set) and the success / collision / timeout fractions.
+inline Score evaluate(Device& device, const float* actor, uint32_t stage, uint32_t family, float amplitude,
+                      uint32_t seed, const std::string& output = "", uint32_t mode = 17) {
+    mdn_sim_config config;
+    mdn_sim_config_default(&config);
+    config.n = 128;
+    config.eval = 1;
+    config.mode = mode;
+    config.seed = seed;
+    config.family = family;
+    config.speed = 1.5f;
+    config.distance = 8;
+    config.max_steps = 400;
+    config.geometry_memory = 1;
+    Sim sim(device, config, 32);
+    const mdn_task_control settings = task_settings(stage, family);
+    configure(sim, settings, amplitude);
+    sim.upload(MDN_BUF_ACTOR, actor, sim.actor_params * sizeof(float));
+    validate_rollout(sim);
+    const auto tasks0 = sim.download<mdn_task_state>(MDN_BUF_TASK_STATES);
+    sim.collect(400);
+    device.finish();
+    validate_rollout(sim);
+    std::ofstream file;
+    if (!output.empty()) {
+        const std::filesystem::path destination(output);
+        if (destination.has_parent_path()) std::filesystem::create_directories(destination.parent_path());
+        file.open(output);
+        require(bool(file), "cannot write task evaluation");
+        file << "seed,env,stage,family,mode,domain_amplitude,start_x,start_y,start_z,start_yaw,initial_vx,initial_vy,"
+                "initial_vz,goal_x,goal_y,goal_z,initial_distance_m,direct_clearance_m,witness_length_m,mass_kg,"
+                "success,collision,timeout,time_s,path_m,goal_error_m,final_speed_mps,hold_s,peak_speed_mps,"
+                "min_sphere_clearance_m,success_rule\n";
+    }
+    const auto runs = sim.download<mdn_sim_run>(MDN_BUF_RUNS);
+    const auto states = sim.download<mdn_physics_state>(MDN_BUF_STATES);
+    const auto tasks = sim.download<mdn_task_state>(MDN_BUF_TASK_STATES);
+    const auto plants = sim.download<mdn_physics_params>(MDN_BUF_ENV_PHYSICS);
+    const auto nominal = sim.download<mdn_physics_params>(MDN_BUF_PHYSICS);
+    Score result;
+    for (uint32_t env = 0; env < config.n; env++) {
+        const mdn_sim_run& run = runs[env];
+        const mdn_task_state& task = tasks0[env];
+        const mdn_physics_state& state = states[env];
+        require(run.episodes == 1, "evaluation must complete exactly one task per environment");
+        result.success += run.successes;
+        result.collision += run.collisions;
+        result.timeout += run.timeouts;
+        result.successful_time_s += run.success_time;
+        const float dx = task.goal_position[0] - state.position[0], dy = task.goal_position[1] - state.position[1],
+                    dz = task.goal_position[2] - state.position[2];
+        const float error = std::sqrt(dx * dx + dy * dy + dz * dz);
+        const float speed = std::sqrt(state.linear_velocity[0] * state.linear_velocity[0] +
+                                      state.linear_velocity[1] * state.linear_velocity[1] +
+                                      state.linear_velocity[2] * state.linear_velocity[2]);
+        if (run.successes)
+            require(error <= settings.config.goal_radius_m + 1e-5f &&
+                        speed <= settings.config.stable_speed_mps + 1e-5f && tasks[env].stable_time_s >= .2f - 1e-6f,
+                    "stable-arrival invariant failed");
+        if (file.is_open()) {
+            const float mass = plants.size() == config.n ? plants[env].mass : nominal[0].mass;
+            file << seed << ',' << env << ',' << stage << ',' << task.family << ',' << mode << ',' << amplitude;
+            for (float v : task.start_position) file << ',' << v;
+            file << ',' << task.start_yaw_rad;
+            for (float v : task.start_velocity_world) file << ',' << v;
+            for (float v : task.goal_position) file << ',' << v;
+            file << ',' << task.initial_distance_m << ',' << task.direct_segment_clearance_m << ','
+                 << task.witness_length_m << ',' << mass << ',' << run.successes << ',' << run.collisions << ','
+                 << run.timeouts << ',' << run.elapsed << ',' << run.path << ',' << error << ',' << speed << ','
+                 << tasks[env].stable_time_s << ',' << run.peak_speed << ',' << run.min_clearance
+                 << ",radius0.35_speed0.5_hold0.2\n";
+        }
+    }
+    result.success /= config.n;
+    result.collision /= config.n;
+    result.timeout /= config.n;
+    if (result.success > 0) result.successful_time_s /= result.success * config.n;
+    std::cout << "task_eval stage=" << stage << " family=" << family << " seed=" << seed << " amplitude=" << amplitude
+              << " mode=" << mode << " success=" << result.success << " collision=" << result.collision
+              << " timeout=" << result.timeout << " mean_arrival_s=" << result.successful_time_s << "\n";
+    return result;
+}
+
+// train (:115-170): task PPO with periodic checkpoints, evaluation and a
+// kept best checkpoint (success first, then fewer collisions, then faster
+// arrival), resuming from `checkpoint` when it exists.
+inline void train(Device& device, uint32_t rollouts, const std::string& checkpoint, const std::string& warmstart,
+                  uint32_t stage, uint32_t family, float amplitude, uint32_t seed, uint32_t every = 50) {
+    require(rollouts > 0, "task training requires positive rollouts");
+    mdn_sim_config config;
+    mdn_sim_config_default(&config);
+    config.n = 128;
+    config.mode = 22;
+    config.family = family;
+    config.seed = seed;
+    config.speed = 1.5f;
+    config.distance = 8;
+    config.max_steps = 400;
+    config.geometry_memory = 1;
+    config.entropy_coef = .001f;
+    config.learning_rate = .0001f;
+    Sim sim(device, config, 32);
+    configure(sim, task_settings(stage, family), amplitude);
+    PPOTrainer trainer(sim);
+    const bool resume = std::filesystem::exists(checkpoint);
+    if (resume) {
+        trainer.load_checkpoint(checkpoint, family, 32, config.n, seed);
+    } else {
+        load_actor(sim, warmstart, true);
+        auto actor = sim.download<float>(MDN_BUF_ACTOR);
+        for (uint32_t a = 0; a < 4; a++) actor[actor.size() - 4 + a] = -1.0f;  // log_std
+        sim.upload(MDN_BUF_ACTOR, actor);
+    }
+    validate_rollout(sim);
+    const std::filesystem::path path(checkpoint);
+    if (path.has_parent_path()) std::filesystem::create_directories(path.parent_path());
+    std::ofstream history(checkpoint + ".history.csv", std::ios::app);
+    require(bool(history), "task history write");
+    if (!resume)
+        history << "rollout,total_transitions,wall_s,collect_gpu_s,update_gpu_s,policy_loss,value_loss,ratio,success,"
+                   "collision,timeout,mean_arrival_s\n";
+    const uint32_t finish = trainer.completed_rollouts() + rollouts;
+    auto evaluate_current = [&](const std::string& output) {
+        const auto actor = sim.download<float>(MDN_BUF_ACTOR);
+        return evaluate(device, actor.data(), stage, family, amplitude, 800001, output);
+    };
+    Score best;
+    if (resume && std::filesystem::exists(checkpoint + ".best")) {
+        Sim selected(device, config, 32);
+        load_actor(selected, checkpoint + ".best");
+        const auto actor = selected.download<float>(MDN_BUF_ACTOR);
+        best = evaluate(device, actor.data(), stage, family, amplitude, 800001);
+    }
+    if (!resume) {
+        best = evaluate_current(checkpoint + ".initial-dev.csv");
+        trainer.save_checkpoint(checkpoint + ".best", family, seed, trainer.completed_rollouts());
+        history << 0 << ",0,0,0,0,0,0,1," << best.success << ',' << best.collision << ',' << best.timeout << ','
+                << best.successful_time_s << '\n';
+        history.flush();
+    }
+    for (uint32_t rollout = trainer.completed_rollouts(); rollout < finish; rollout++) {
+        // generation or dynamics errors are rejected before their transitions reach PPO
+        sim.collect();
+        const double collect_s = device.finish();
+        validate_rollout(sim);
+        trainer.rollout_update(rollout);
+        device.finish();
+        const double update_s = trainer.last_update_ms() * 1e-3;
+        trainer.set_completed_rollouts(rollout + 1);
+        if ((rollout + 1) % every == 0 || rollout + 1 == finish) {
+            trainer.save_checkpoint(checkpoint, family, seed, rollout + 1);
+            const Score score = evaluate_current(checkpoint + ".dev.csv");
+            if (score.success > best.success || (score.success == best.success && score.collision < best.collision) ||
+                (score.success == best.success && score.collision == best.collision &&
+                 score.successful_time_s < best.successful_time_s)) {
+                best = score;
+                trainer.save_checkpoint(checkpoint + ".best", family, seed, rollout + 1);
+                std::filesystem::copy_file(checkpoint + ".dev.csv", checkpoint + ".best-dev.csv",
+                                           std::filesystem::copy_options::overwrite_existing);
+            }
+            const auto metrics = trainer.metric_mean();
+            history << rollout + 1 << ',' << uint64_t(rollout + 1) * config.n * 32 << ",0," << collect_s << ','
+                    << update_s << ',' << metrics[0] << ',' << metrics[1] << ',' << metrics[3] << ',' << score.success
+                    << ',' << score.collision << ',' << score.timeout << ',' << score.successful_time_s << '\n';
+            history.flush();
+            sim.report("train-arrival", 0);
+        }
+    }
+}
+
+}  // namespace navigation_training
+}  // namespace host
+}  // namespace mdn

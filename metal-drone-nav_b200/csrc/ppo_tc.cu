@@ -326,8 +326,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (progressed) {
                 idle_since = clock64();
-            } else if (clock64() - idle_since > kTcWaitLimit) {
-                ok = false;
+            } else {
+                if (clock64() - idle_since > kTcWaitLimit) ok = false;
+                __nanosleep(32);  // leave the issue slots to the epilogue warps
             }
         }
         tc::mma_commit(&s.final_mma);
@@ -346,6 +347,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int k = 0; k < kTcChunks; k++) acc[k] = 0.0f;
         bool ok = true;
         for (uint32_t j = g; j < count; j += 2) {
+            const uint32_t local = (blockIdx.x + j * gridDim.x) * kTcRows + 32 * q + lane;  // row of the minibatch
+            const bool valid = local < b;
+            const size_t src = size_t(begin) + local;
+            // The row's own inputs of the loss, requested before waiting for the
+            // forward so their memory latency overlaps it.
+            float4 act4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float hint[3] = {0.0f, 0.0f, 0.0f}, adv = 0.0f, ret = 0.0f, old_logp = 0.0f;
+            if (valid) {
+                act4 = __ldg(reinterpret_cast<const float4*>(p.actions + src * kActions));
+#pragma unroll
+                for (int a = 0; a < 3; a++) hint[a] = __ldg(p.obs + src * kActorObs + kActorObs - 3 + a);
+                adv = __ldg(p.advantages + src);
+                ret = __ldg(p.returns + src);
+                old_logp = __ldg(p.logp + src);
+            }
             if (!tc::mbar_wait(&s.fwd_full[g], (j >> 1) & 1, kTcWaitLimit)) {
                 ok = false;
                 break;
@@ -363,9 +379,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const float* b2 = pr + 448;
             const float* log_std = pr + 452;
             const float cb2 = pr[456];
-            const uint32_t local = (blockIdx.x + j * gridDim.x) * kTcRows + 32 * q + lane;  // row of the minibatch
-            const bool valid = local < b;
-            const size_t src = size_t(begin) + local;
             const uint32_t lane_addr = tmem + (uint32_t(32 * q) << 16) + kColD + 128 * g;
             // Activations: the value and means are formed in fp32 as the tanh
             // values are produced, and the tanh values replace the
@@ -403,16 +416,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             float dm[4] = {0, 0, 0, 0}, dls[4] = {0, 0, 0, 0}, dvalue = 0.0f, loss[4] = {0, 0, 0, 0};
             if (valid) {
 #pragma unroll
-                for (int a = 0; a < 3; a++) mean[a] += __ldg(p.obs + src * kActorObs + kActorObs - 3 + a);
-                const float* act = p.actions + src * kActions;
+                for (int a = 0; a < 3; a++) mean[a] += hint[a];
+                const float act[4] = {act4.x, act4.y, act4.z, act4.w};
                 float logp = 0.0f;
 #pragma unroll
                 for (int a = 0; a < 4; a++) {
                     const float d = (act[a] - mean[a]) * expf(-log_std[a]);
                     logp += -0.5f * (d * d + 2.0f * log_std[a] + kLogTwoPi);
                 }
-                const float adv = p.advantages[src], ret = p.returns[src];
-                const float raw = logp - p.logp[src];
+                const float raw = logp - old_logp;
                 const float ratio = expf(clampf(raw, -20.0f, 20.0f));
                 const float clipped = clampf(ratio, 1.0f - p.clip, 1.0f + p.clip);
                 const float chosen = smin(ratio * adv, clipped * adv);
