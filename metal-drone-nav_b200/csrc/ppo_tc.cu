@@ -74,8 +74,10 @@ constexpr size_t kOffCw1 = kOffW1 + size_t(kTcObsPanels) * kTcWPanelBytes;
 constexpr size_t kOffDa = kOffCw1 + kTcWPanelBytes;
 constexpr size_t kOffDc = kOffDa + 4 * size_t(kTcDeltaBytes);
 constexpr size_t kOffPar = kOffDc + 4 * size_t(kTcDeltaBytes);
-// b1[64], W2[4][64], cb1[64], cw2[64], b2[4], log_std[4], cb2, pad
-constexpr int kParFloats = 64 + 256 + 64 + 64 + 4 + 4 + 4;
+// b1[64], W2[4][64], cb1[64], cw2[64], b2[4], log_std[4], cb2, pad,
+// then W2 transposed [64][4] (one 128-bit load per hidden unit)
+constexpr int kParW2t = 64 + 256 + 64 + 64 + 4 + 4 + 4;
+constexpr int kParFloats = kParW2t + 256;
 constexpr size_t kOffBar = kOffPar + kParFloats * sizeof(float);
 
 struct TcBarriers {
@@ -198,6 +200,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         else if (k < 452) v = p.actor[kActorB2 + (k - 448)];
         else if (k < 456) v = p.actor[kActorLogStd + (k - 452)];
         else if (k == 456) v = p.critic[kCriticB2];
+        else if (k >= kParW2t) v = p.actor[kActorW2 + ((k - kParW2t) & 3) * 64 + ((k - kParW2t) >> 2)];
         par[k] = v;
     }
     tc::fence_before_sync();
@@ -449,7 +452,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 loss[2] = entropy;
                 loss[3] = ratio;
             }
-            // hidden deltas (W2^T d_mean)(1 - h^2) and d_value cw2 (1 - hc^2)
+            float x[32];
+            // dW2[a][h] = sum over rows of d_mean[a] tanh_h, critic w2 = sum
+            // d_value tanh_c: before the delta handover, off its critical path
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                float v[32];
+                tc::tmem_ld32(lane_addr + 64 + 32 * c, v);
+#pragma unroll
+                for (int i = 0; i < 32; i++) x[i] = dvalue * v[i];
+                acc[8 + c] += lane_column_sum(x, lane);
+                tc::tmem_ld32(lane_addr + 32 * c, v);
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) x[i] = dm[a] * v[i];
+                    acc[2 * a + c] += lane_column_sum(x, lane);
+                }
+            }
             // The previous tile's weight-gradient MMAs (tile j - 1, the other
             // group's) must be done reading the delta operands first.
             if (j >= 1 && !tc::mbar_wait(&s.delta_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, kTcWaitLimit)) {
@@ -458,72 +478,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             tc::fence_after_sync();
             {
-                // K-major 128-byte swizzle: hidden unit h is a 128-byte row of the
-                // [64 x 32 rows] operand, this thread's row is column `lane`.
-                uint8_t* pa = da + q * kTcDeltaBytes;
-                uint8_t* pc = dc + q * kTcDeltaBytes;
-                const uint32_t in_granule = (lane & 3) * 4;
+                // hidden deltas (W2^T d_mean)(1 - h^2) and d_value cw2 (1 - hc^2)
+                // into the K-major 128-byte-swizzled operands: hidden unit h is a
+                // 128-byte row of the [64 x 32 rows] operand, this thread's row is
+                // column `lane`; the row's 16-byte granule is (lane / 4) ^ (h % 8).
+                uint8_t* pa = da + q * kTcDeltaBytes + (lane & 3) * 4;
+                uint8_t* pc = dc + q * kTcDeltaBytes + (lane & 3) * 4;
+                uint32_t gran[8];
+#pragma unroll
+                for (int r8 = 0; r8 < 8; r8++) gran[r8] = r8 * 128 + (((lane >> 2) ^ r8) << 4);
+                const float4* w2t = reinterpret_cast<const float4*>(pr + kParW2t);
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     float ha[32], hv[32];
                     tc::tmem_ld32(lane_addr + 32 * c, ha);
                     tc::tmem_ld32(lane_addr + 64 + 32 * c, hv);
 #pragma unroll
-                    for (int hb = 0; hb < 32; hb += 8) {
-#pragma unroll
-                        for (int i = hb; i < hb + 8; i++) {
-                            const int h = 32 * c + i;
-                            const uint32_t off =
-                                (h >> 3) * 1024 + (h & 7) * 128 + ((((lane >> 2) ^ (h & 7))) << 4) + in_granule;
-                            float sv = dm[0] * w2[h];
-                            sv = fmaf(dm[1], w2[64 + h], sv);
-                            sv = fmaf(dm[2], w2[128 + h], sv);
-                            sv = fmaf(dm[3], w2[192 + h], sv);
-                            // hidden deltas (W2^T d_mean)(1 - h^2) and d_value cw2 (1 - hc^2)
-                            *reinterpret_cast<float*>(pa + off) = sv * (1.0f - ha[i] * ha[i]);
-                            *reinterpret_cast<float*>(pc + off) = dvalue * cw2[h] * (1.0f - hv[i] * hv[i]);
-                        }
-                        // keeps the next block's weight loads below this point: the
-                        // compiler would otherwise issue all of them up front
-                        asm volatile("" ::: "memory");
+                    for (int i = 0; i < 32; i++) {
+                        const int h = 32 * c + i;
+                        const float4 wc = w2t[h];
+                        const float sv = fmaf(dm[3], wc.w, fmaf(dm[2], wc.z, fmaf(dm[1], wc.y, dm[0] * wc.x)));
+                        ha[i] = sv * (1.0f - ha[i] * ha[i]);
+                        hv[i] = dvalue * cw2[h] * (1.0f - hv[i] * hv[i]);
+                        const uint32_t off = (h >> 3) * 1024 + gran[h & 7];
+                        *reinterpret_cast<float*>(pa + off) = ha[i];
+                        *reinterpret_cast<float*>(pc + off) = hv[i];
                     }
+                    // b1 and critic b1: sums of the deltas, from the registers
+                    acc[10 + c] += lane_column_sum(ha, lane);
+                    acc[12 + c] += lane_column_sum(hv, lane);
                 }
-            }
-            // this thread's delta of hidden unit h, read back from the operand it was stored to
-#define delta_smem(base, h)                                                                           \
-    (*reinterpret_cast<const float*>((base) + q * kTcDeltaBytes + ((h) >> 3) * 1024 + ((h) & 7) * 128 + \
-                                     ((((lane >> 2) ^ ((h) & 7))) << 4) + (lane & 3) * 4))
-            // b1 and critic b1 (sums of the deltas), read back before the operand
-            // is handed over: once delta_full completes, the other group may
-            // overwrite it with the next tile's deltas.
-            float x[32];
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
-#pragma unroll
-                for (int i = 0; i < 32; i++) x[i] = delta_smem(da, 32 * c + i);
-                acc[10 + c] += lane_column_sum(x, lane);
-#pragma unroll
-                for (int i = 0; i < 32; i++) x[i] = delta_smem(dc, 32 * c + i);
-                acc[12 + c] += lane_column_sum(x, lane);
             }
             fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor cores
+            tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&s.delta_full);
-            // the other small gradients, summed over the warp's rows
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
-                float v[32];
-                tc::tmem_ld32(lane_addr + 64 + 32 * c, v);
-#pragma unroll
-                for (int i = 0; i < 32; i++) x[i] = dvalue * v[i];  // critic w2
-                acc[8 + c] += lane_column_sum(x, lane);
-                tc::tmem_ld32(lane_addr + 32 * c, v);
-#pragma unroll
-                for (int a = 0; a < 4; a++) {
-#pragma unroll
-                    for (int i = 0; i < 32; i++) x[i] = dm[a] * v[i];  // dW2[a][h]
-                    acc[2 * a + c] += lane_column_sum(x, lane);
-                }
+            if (lane == 0) {
+                tc::mbar_arrive(&s.delta_full);
+                tc::mbar_arrive(&s.fwd_empty[g]);  // the accumulator buffer is free again
             }
 #pragma unroll
             for (int i = 0; i < 32; i++) x[i] = 0.0f;
@@ -535,11 +526,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             x[8] = dvalue;
             acc[14] += lane_column_sum(x, lane);
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&s.fwd_empty[g]);  // the accumulator buffer is free again
         }
-#undef delta_smem
         if (!ok) atomicOr(p.tc_error, 4u);
         // every MMA is done: the weight-gradient accumulators are final and the rings are free
         const bool mma_done = count == 0 || tc::mbar_wait(&s.final_mma, 0, kTcWaitLimit);
