@@ -500,7 +500,8 @@ def workload_config(args):
             "epochs": args.epochs,
             "minibatches": args.minibatches, "actor_hidden": args.actor_hidden,
             "parallelism": f"dp{args.gpus} (envs sharded)",
-            "l2": "inputs larger than L2 (obs buffer > 6 GB per rollout)"}
+            "l2": f"inputs larger than L2 (obs buffer {args.envs * args.horizon * 184 * 4 / 1e9:.2f} GB per rollout "
+                  f"against a 126 MB L2)"}
 
 
 # ------------------------------------------------------------------ main

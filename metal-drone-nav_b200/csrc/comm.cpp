@@ -7,8 +7,10 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <atomic>
 #include <chrono>
 #include <cstdlib>
+#include <memory>
 #include <mutex>
 #include <thread>
 
@@ -71,15 +73,47 @@ namespace {
 using Clock = std::chrono::steady_clock;
 double seconds_since(Clock::time_point t0) { return std::chrono::duration<double>(Clock::now() - t0).count(); }
 
+// Poll `ready` until it reports something other than cudaErrorNotReady or
+// `limit_s` passes; true when the work completed (with any status).
+template <class Ready>
+bool drained_within(Ready ready, double limit_s) {
+    const auto t0 = Clock::now();
+    for (;;) {
+        if (ready() != cudaErrorNotReady) return true;
+        if (seconds_since(t0) > limit_s) return false;
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+}
+
 // Abort the communicator (NCCL kernels waiting on a peer return), let the
 // stream drain and mark the device so no later update enqueues a collective.
+// Both steps are bounded: ncclCommAbort runs on a helper thread that is left
+// behind if it does not return in time, and the stream is polled, not
+// synchronised. The error names what did not finish.
 [[noreturn]] void abort_comm(mdn_device* dev, cudaStream_t s, const std::string& why) {
-    if (dev->nccl_comm && nccl().ok) nccl().abort(static_cast<ncclComm_t>(dev->nccl_comm));
+    const double limit = std::min(dev->nccl_timeout_s, 30.0);
+    bool aborted = true;
+    if (dev->nccl_comm && nccl().ok) {
+        auto done = std::make_shared<std::atomic<bool>>(false);
+        ncclComm_t comm = static_cast<ncclComm_t>(dev->nccl_comm);
+        const int gpu = dev->gpu;
+        std::thread([comm, done, gpu] {
+            cudaSetDevice(gpu);
+            nccl().abort(comm);
+            done->store(true);
+        }).detach();
+        const auto t0 = Clock::now();
+        while (!done->load() && seconds_since(t0) < limit) std::this_thread::sleep_for(std::chrono::milliseconds(1));
+        aborted = done->load();
+    }
     dev->nccl_comm = nullptr;
     dev->comm_failed = true;
-    if (s) cudaStreamSynchronize(s);
+    const bool drained = !s || drained_within([&] { return cudaStreamQuery(s); }, limit);
     cudaGetLastError();
-    throw Error(MDN_ERR_NCCL, why);
+    std::string msg = why;
+    if (!aborted) msg += "; ncclCommAbort did not return within " + std::to_string(limit) + " s";
+    if (!drained) msg += "; the stream did not drain within " + std::to_string(limit) + " s";
+    throw Error(MDN_ERR_NCCL, msg);
 }
 
 // Poll `ready` (a stream or an event) and the communicator's asynchronous
@@ -141,7 +175,17 @@ cudaError_t comm_allreduce_float(mdn_device* dev, float* buf, size_t count, cuda
     return allreduce(dev, buf, count, ncclFloat32, s, err);
 }
 
+// After an abort, work queued behind a collective that never finished may
+// stay blocked: waits on such a device are bounded and raise MDN_ERR_NCCL.
+template <class Ready>
+void wait_after_abort(mdn_device* dev, const char* what, Ready ready) {
+    if (!drained_within(ready, std::min(dev->nccl_timeout_s, 30.0)))
+        throw Error(MDN_ERR_NCCL, std::string(what) + ": work is still blocked behind an aborted NCCL collective");
+    cuda_check(ready(), what);
+}
+
 void sync_stream(mdn_device* dev, cudaStream_t s, const char* what) {
+    if (dev->comm_failed) return wait_after_abort(dev, what, [&] { return cudaStreamQuery(s); });
     if (dev->world <= 1 || !dev->nccl_comm) {
         cuda_check(cudaStreamSynchronize(s), what);
         return;
@@ -150,6 +194,7 @@ void sync_stream(mdn_device* dev, cudaStream_t s, const char* what) {
 }
 
 void sync_event(mdn_device* dev, cudaEvent_t e, const char* what) {
+    if (dev->comm_failed) return wait_after_abort(dev, what, [&] { return cudaEventQuery(e); });
     if (dev->world <= 1 || !dev->nccl_comm) {
         cuda_check(cudaEventSynchronize(e), what);
         return;

@@ -1,7 +1,8 @@
 // Goal-arrival task contract on the device (navigation_tasks.hpp:196-548):
 // bounded task generation with a validated witness path, the physical start,
-// and the stable-hold step reward. Runs only at episode resets (generation)
-// and once per env-step (step), thread per environment.
+// and the stable-hold step reward. Generation runs at episode resets on a whole
+// converged warp per environment (the witness checks' samples are split over
+// the lanes); the step runs once per env-step, thread per environment.
 #pragma once
 #include "world_gen.cuh"
 
@@ -33,29 +34,52 @@ __device__ __forceinline__ void task_random_point(uint32_t& rng, const float* lo
 __device__ __forceinline__ bool task_inside(const float p[3], const float* low, const float* high) {
     return p[0] >= low[0] && p[0] <= high[0] && p[1] >= low[1] && p[1] <= high[1] && p[2] >= low[2] && p[2] <= high[2];
 }
-__device__ float task_segment_clearance(const SimArgs& a, const mdn_world& w, const float* p0, const float* p1) {
-    const float d[3] = {p1[0] - p0[0], p1[1] - p0[1], p1[2] - p0[2]};  // :240-252
+// Minimum clearance of the samples every 5 cm along a segment (:240-252), by a
+// whole converged warp: lane l takes samples l, l+32, ... and the lanes' minima
+// are combined by shuffles. A minimum does not depend on the order of its
+// terms, so the value equals the serial loop's. With `stop_at` above -inf the
+// scan ends after the first round of 32 samples whose minimum is <= stop_at
+// and returns that partial minimum: the caller only needs to know that the
+// path fails its clearance test then.
+__device__ __forceinline__ float warp_min(float v) {
+    for (int m = 16; m > 0; m >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+__device__ float task_segment_clearance(const SimArgs& a, const mdn_world& w, const float* p0, const float* p1,
+                                        float stop_at) {
+    const float d[3] = {p1[0] - p0[0], p1[1] - p0[1], p1[2] - p0[2]};
     const float distance = len3(d[0], d[1], d[2]);
     uint32_t count = uint32_t(ceilf(distance / 0.05f));
     if (count < 1u) count = 1u;
     if (count > 512u) return -1e6f;
+    const uint32_t lane = threadIdx.x & 31u;
     float minimum = 1e20f;
-    for (uint32_t sample = 0; sample <= count; sample++) {
-        const float t = float(sample) / float(count);
-        const float pt[3] = {p0[0] + d[0] * t, p0[1] + d[1] * t, p0[2] + d[2] * t};
-        minimum = fminf(minimum, world_clearance(a, w, pt, 0.0f, nullptr));
+    for (uint32_t base = 0; base <= count; base += 32u) {
+        const uint32_t sample = base + lane;
+        if (sample <= count) {
+            const float t = float(sample) / float(count);
+            const float pt[3] = {p0[0] + d[0] * t, p0[1] + d[1] * t, p0[2] + d[2] * t};
+            minimum = fminf(minimum, world_clearance(a, w, pt, 0.0f, nullptr));
+        }
+        if (stop_at > -INFINITY && warp_min(minimum) <= stop_at) break;
     }
-    return minimum;
+    return warp_min(minimum);
 }
 struct TaskWitness {
     float p[kTaskMaxWitness][3];
     uint32_t count;
     float min_clearance, length;
 };
-__device__ float task_test_path(const SimArgs& a, const mdn_world& w, const float (*pts)[3], uint32_t count) {
-    if (count < 2u || count > kTaskMaxWitness) return -1e6f;  // :253-259
+// :253-259. `stop_at` as for task_segment_clearance: a path whose minimum is
+// known to be <= stop_at skips its remaining segments.
+__device__ float task_test_path(const SimArgs& a, const mdn_world& w, const float (*pts)[3], uint32_t count,
+                                float stop_at = -INFINITY) {
+    if (count < 2u || count > kTaskMaxWitness) return -1e6f;
     float minimum = 1e20f;
-    for (uint32_t k = 0; k + 1u < count; k++) minimum = fminf(minimum, task_segment_clearance(a, w, pts[k], pts[k + 1]));
+    for (uint32_t k = 0; k + 1u < count; k++) {
+        minimum = fminf(minimum, task_segment_clearance(a, w, pts[k], pts[k + 1], stop_at));
+        if (minimum <= stop_at) break;
+    }
     return minimum;
 }
 __device__ void task_save(TaskWitness& out, const float (*pts)[3], uint32_t count, float clearance) {  // :260-273
@@ -68,7 +92,9 @@ __device__ void task_save(TaskWitness& out, const float (*pts)[3], uint32_t coun
     for (uint32_t i = 0; i < kTaskMaxWitness; i++)
         for (int j = 0; j < 3; j++) out.p[i][j] = i < count ? pts[i][j] : 0.0f;
 }
-// :276-333: the direct line, or one of a bounded set of doglegs.
+// :276-333: the direct line, or one of a bounded set of doglegs. The direct
+// line's clearance is recorded in the task, so it is always scanned in full; a
+// dogleg's is recorded only when it passes, so a failing dogleg stops early.
 __device__ bool task_find_witness(const SimArgs& a, const mdn_world& w, const float st[3], const float gl[3],
                                   const mdn_task_config& c, TaskWitness& wit, float& direct_clearance) {
     const float direct[2][3] = {{st[0], st[1], st[2]}, {gl[0], gl[1], gl[2]}};
@@ -86,7 +112,7 @@ __device__ bool task_find_witness(const SimArgs& a, const mdn_world& w, const fl
             const float t = x_fraction[i];
             const float path[3][3] = {{st[0], st[1], st[2]}, {st[0] + t * delta[0], side_y[side], st[2] + t * delta[2]},
                                       {gl[0], gl[1], gl[2]}};
-            const float cl = task_test_path(a, w, path, 3u);
+            const float cl = task_test_path(a, w, path, 3u, c.minimum_witness_clearance_m);
             if (cl > c.minimum_witness_clearance_m) {
                 task_save(wit, path, 3u, cl);
                 return true;
@@ -99,7 +125,7 @@ __device__ bool task_find_witness(const SimArgs& a, const mdn_world& w, const fl
                                   {st[0] + t * delta[0], task_clamp((st[1] + gl[1]) * 0.5f + side_offset[i], -4.60f, 4.60f),
                                    st[2] + t * delta[2]},
                                   {gl[0], gl[1], gl[2]}};
-        const float cl = task_test_path(a, w, path, 3u);
+        const float cl = task_test_path(a, w, path, 3u, c.minimum_witness_clearance_m);
         if (cl > c.minimum_witness_clearance_m) {
             task_save(wit, path, 3u, cl);
             return true;
@@ -109,7 +135,7 @@ __device__ bool task_find_witness(const SimArgs& a, const mdn_world& w, const fl
     for (uint32_t i = 0; i < 2u; i++) {
         const float path[3][3] = {{st[0], st[1], st[2]}, {st[0] + 0.5f * delta[0], st[1] + 0.5f * delta[1], detour_z[i]},
                                   {gl[0], gl[1], gl[2]}};
-        const float cl = task_test_path(a, w, path, 3u);
+        const float cl = task_test_path(a, w, path, 3u, c.minimum_witness_clearance_m);
         if (cl > c.minimum_witness_clearance_m) {
             task_save(wit, path, 3u, cl);
             return true;
@@ -121,7 +147,7 @@ __device__ bool task_find_witness(const SimArgs& a, const mdn_world& w, const fl
                                   {st[0] + 0.20f * delta[0], y, st[2] + 0.20f * delta[2]},
                                   {st[0] + 0.80f * delta[0], y, st[2] + 0.80f * delta[2]},
                                   {gl[0], gl[1], gl[2]}};
-        const float cl = task_test_path(a, w, path, 4u);
+        const float cl = task_test_path(a, w, path, 4u, c.minimum_witness_clearance_m);
         if (cl > c.minimum_witness_clearance_m) {
             task_save(wit, path, 4u, cl);
             return true;
@@ -281,7 +307,9 @@ __device__ TaskStep task_step(mdn_task_state& task, const mdn_task_config& c, co
 // Episode reset with the task contract: sim_reset_one, the challenge-bank
 // world of schedule slot `slot` (sim.metal:143,330), then
 // sim_reset_navigation_task (sim.metal:125-141), then the SoA world mirror.
-// Returns true (the caller refills the env's range ring).
+// Run by a whole converged warp. The task's scene is generated and its witness
+// checked in the warp's shared-memory world, then stored once. Returns true
+// (the caller refills the env's range ring).
 __device__ __noinline__ bool episode_reset(const SimArgs& a, uint32_t i, bool first, uint32_t slot,
                                            mdn_world& scratch) {
     reset_env(a, i, first, scratch);
@@ -293,7 +321,9 @@ __device__ __noinline__ bool episode_reset(const SimArgs& a, uint32_t i, bool fi
         const uint32_t gid = a.env_base + i;
         mdn_sim_run& run = a.runs[i];
         mdn_physics_state& s = a.states[i];
-        mdn_world& w = a.worlds[i];
+        mdn_world& w = scratch;
+        __syncwarp();
+        copy_world_warp(w, a.worlds[i]);  // the bank may have replaced the reset's world
         uint32_t rng = a.cfg.seed ^ ((gid + 1u) * 0x27d4eb2du) ^ ((run.episodes + 1u) * 0x165667b1u);
         task_generate(a, w, task, rng);
         if (task.valid) {  // navigation_task_apply_start, navigation_tasks.hpp:486-495
@@ -317,6 +347,8 @@ __device__ __noinline__ bool episode_reset(const SimArgs& a, uint32_t i, bool fi
             w.wind[1] = 0;
             w.wind[2] = 0;
         }
+        __syncwarp();
+        copy_world_warp(a.worlds[i], w);
     }
     __syncwarp();
     mirror_world_warp(a, i);

@@ -6,7 +6,8 @@ communicator. Then, between steps, with none of its kernels or collectives in
 flight, rank 1 leaves (exits). Rank 0 runs the next rollout and update: the
 update's allreduce can never complete, so libmdn's host wait must abort the
 communicator and raise MDN_ERR_NCCL within MDN_NCCL_TIMEOUT_S, and a further
-update must be refused at once. Rank 0 writes what it saw to <outdir>/rank0.txt.
+update must be refused at once. Rank 0 writes what it saw to <outdir>/rank0.txt
+and each phase it reaches, with its time, to <outdir>/rank0.progress.
 
   argv: outdir
 """
@@ -40,20 +41,30 @@ def main():
     dist.barrier()  # both ranks are between steps, nothing in flight
     if rank == 1:
         os._exit(0)  # leaves without a word, as a crashed rank would
-    sim.collect()
     t0 = time.time()
+    progress = open(outdir / "rank0.progress", "w", buffering=1)
+
+    def phase(name):
+        progress.write(f"{time.time() - t0:8.2f} {name}\n")
+
+    phase("rank 1 gone")
+    sim.collect()
+    phase("collect enqueued")
     try:
         tr.rollout_update(1)
+        phase("update enqueued")
         dev.finish()
         first = "no error"
     except pkg.MdnError as e:
         first = f"code {e.code}: {e}"
+    phase(f"first update: {first}")
     waited = time.time() - t0
     try:
         tr.rollout_update(2)
         second = "no error"
     except pkg.MdnError as e:
         second = f"code {e.code}: {e}"
+    phase(f"second update: {second}")
     (outdir / "rank0.txt").write_text(f"{first}\n{second}\n{waited:.1f}\n")
     os._exit(0)
 

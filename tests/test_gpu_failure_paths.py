@@ -58,7 +58,9 @@ def test_lost_rank_aborts_the_collective(tmp_path):
            str(ROOT / "tests" / "multirank_failure_worker.py"), str(tmp_path)]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     out = tmp_path / "rank0.txt"
-    assert out.exists(), r.stdout[-2000:] + r.stderr[-2000:]
+    progress = tmp_path / "rank0.progress"
+    seen = progress.read_text() if progress.exists() else "(no progress file)"
+    assert out.exists(), "rank 0 phases:\n" + seen + "\n" + r.stdout[-1500:] + r.stderr[-1500:]
     first, second, waited = out.read_text().splitlines()
     nccl = pkg_err_code("NCCL")
     assert first.startswith(f"code {nccl}"), first

@@ -113,6 +113,27 @@ def test_task_reset_matches_oracle(pkg, om, device, raptor, case):
         gpu.close()
 
 
+@pytest.mark.parametrize("family", [1, 2, 12])
+def test_task_detour_witnesses_match_oracle(pkg, om, device, raptor, family):
+    """Forced detours (require_detour) on long goals: every task's witness is a
+    dogleg, so the warp-split segment scan and its early stop on failing
+    doglegs are exercised; witness choice and clearances match the oracle."""
+    cfg = pkg.layouts.default_config(n=256, family=family, mode=22, speed=1.5, distance=8.0, seed=5, max_steps=400)
+    control = pkg.task_control(2, family)
+    control["config"]["require_detour"] = 1
+    control["config"]["goal_distance_max_m"] = 20.0
+    gpu, ora = pair(pkg, om, device, raptor, cfg, 4, control)
+    try:
+        to = ora.buf("task_states")
+        compare_tasks(gpu.download("task_states"), to, "detour reset")
+        ready = to["generation_status"] == 4
+        assert ready.mean() > 0.5
+        assert (to["witness_point_count"][ready] >= 3).all()
+        close(floats(gpu.download("worlds")), floats(ora.buf("worlds")), "detour worlds")
+    finally:
+        gpu.close()
+
+
 @pytest.mark.parametrize("case", TASK_CASES, ids=[str(c) for c in TASK_CASES])
 def test_task_teacher_forced_steps(pkg, om, device, raptor, case):
     case = dict(case)
