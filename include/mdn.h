@@ -437,8 +437,8 @@ int mdn_checkpoint_inspect(const char* path, mdn_checkpoint_header* header, mdn_
 /* GAE + advantage normalisation of one rollout that allocates no memory.
  * No counterpart in the reference. For callers that cannot call cudaMalloc:
  * code whose device memory is all owned by its own pool (a framework's caching
- * allocator), or code that must not allocate on its hot path (inside a stream
- * capture, or a fixed-latency training/evaluation loop). It computes what the
+ * allocator), or code that must not allocate on its hot path (a fixed-latency
+ * training/evaluation loop). It computes what the
  * first phase of mdn_ppo_rollout_update computes, from device pointers in the
  * reference's T-major [horizon][envs] layout: rewards, values, next_values
  * (float), terminated, truncated (uint8) in; advantages (normalised) and
@@ -447,7 +447,9 @@ int mdn_checkpoint_inspect(const char* path, mdn_checkpoint_header* header, mdn_
  * Its scratch is a fixed device array inside libmdn (33 KB on every GPU that
  * loads the library, held until exit): envs <= 1,048,576 (4,096 blocks of
  * 256); larger sizes return MDN_ERR_INVALID. The first call on a device looks
- * up that array's address, so make it before any stream capture. All calls
+ * up that array's address, so make it before any stream capture; the address
+ * is kept for the life of the device's primary context, so after a
+ * cudaDeviceReset unload and reload libmdn before calling again. All calls
  * share the array: calls that overlap on the GPU (different streams, or
  * different host threads) race and must be serialised by the caller. */
 int mdn_gae_normalize_static(const float* rewards, const float* values, const float* next_values,

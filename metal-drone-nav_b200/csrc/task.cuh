@@ -168,6 +168,7 @@ __device__ uint32_t task_generate(const SimArgs& a, mdn_world& w, mdn_task_state
     uint32_t attempts = c.max_generation_attempts;
     if (attempts > kTaskMaxAttempts) attempts = kTaskMaxAttempts;
     for (uint32_t attempt = 0; attempt < attempts; attempt++) {
+        __syncwarp();  // no lane still stores the previous attempt's fields (run by a whole warp)
         task.generation_attempts = attempt + 1u;
         const uint32_t scene_seed = wrng(rng);
         uint32_t scene_family = c.family;

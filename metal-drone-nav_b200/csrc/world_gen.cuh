@@ -6,12 +6,21 @@
 
 namespace mdn {
 
+// Run by a whole converged warp (every lane computes and stores the same
+// values). Fields that are rewritten and then read back - the obstacle count
+// here, the world at each new generation or task attempt - are fenced with
+// __syncwarp(), so that a lane that fell behind cannot overwrite a newer value
+// with an older one before another lane reads it.
 struct WorldBuilder {
     mdn_world& w;
     __device__ void add(uint32_t kind, float cx, float cy, float cz, float ex, float ey, float ez, float vx, float vy,
                         float vz) {  // world.hpp:104-111
-        if (w.count >= 16) return;
-        mdn_obstacle& o = w.obstacles[w.count++];
+        __syncwarp();  // every lane's earlier stores to w are done
+        const uint32_t slot = w.count;
+        __syncwarp();  // every lane has read the count before it changes
+        if (slot >= 16) return;
+        w.count = slot + 1;
+        mdn_obstacle& o = w.obstacles[slot];
         o.kind = kind;
         o.center[0] = cx; o.center[1] = cy; o.center[2] = cz;
         o.size[0] = ex; o.size[1] = ey; o.size[2] = ez;
@@ -137,7 +146,8 @@ __device__ __forceinline__ uint32_t mixed_lane_family(uint32_t gid) {
 }
 
 // wgenerate, world.hpp:299-318, with every family generator of world.hpp:138-291.
-__device__ void generate_world(mdn_world& w, uint32_t seed, uint32_t family, float distance) {
+__device__ void generate_world_body(mdn_world& w, uint32_t seed, uint32_t family, float distance) {
+    __syncwarp();  // stores of an earlier world or attempt are done before this one's
     uint32_t rng = seed ? seed : 1;
     w.seed = seed;
     w.family = family;
@@ -146,6 +156,7 @@ __device__ void generate_world(mdn_world& w, uint32_t seed, uint32_t family, flo
     w.goal[1] = (wurand(rng) - 0.5f) * 2;
     w.goal[2] = 1.5f + (wurand(rng) - 0.5f) * 0.8f;
     w.wind[0] = w.wind[1] = w.wind[2] = 0;
+    __syncwarp();  // the families below rewrite the count and goal set above, then read them
     WorldBuilder b{w};
     if (family == 4) {  // single doorway, :138-147
         w.count = 0;
@@ -344,6 +355,12 @@ __device__ void generate_world(mdn_world& w, uint32_t seed, uint32_t family, flo
     }
 }
 
+// The generator with a warp barrier on exit (see WorldBuilder).
+__device__ void generate_world(mdn_world& w, uint32_t seed, uint32_t family, float distance) {
+    generate_world_body(w, seed, family, distance);
+    __syncwarp();  // the new world is complete for every lane before anything reads it
+}
+
 // Training-only family mixture, world.hpp:293-298.
 __device__ __forceinline__ uint32_t training_family(uint32_t family, uint32_t& rng) {
     if (family == 7) return wrng(rng) % 7;
@@ -503,6 +520,7 @@ __device__ __forceinline__ void apply_challenge_world(const SimArgs& a, uint32_t
     } else {
         if (level >= a.bank_count) return;
         w = a.bank_worlds[level];
+        __syncwarp();  // the bank world's wind is stored by every lane before it is overwritten
     }
     w.wind[0] = clean_env(a, gid) ? 0.0f : a.cfg.wind;
     w.wind[1] = 0;

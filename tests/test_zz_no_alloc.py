@@ -1,8 +1,8 @@
 """mdn_gae_normalize_static: the allocation-free GAE + advantage normalisation.
 
 Some callers cannot call cudaMalloc on their hot path: a framework whose caching
-allocator owns all device memory, or a loop that runs inside a stream capture or
-under a fixed latency budget. For them libmdn offers this one entry point, whose
+allocator owns all device memory, or a loop that runs under a fixed latency
+budget. For them libmdn offers this one entry point, whose
 scratch is a fixed array compiled into the library. This test calls it through
 the C-ABI on a real rollout, twice in a row (the shared scratch keeps the first
 call's contents), and checks each result against the existing entry point,
