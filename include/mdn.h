@@ -129,12 +129,24 @@ typedef struct mdn_rollout_shape {
                                    navigation_wide_deployment.hpp:54-66), evaluated and
                                    trained on the tensor cores (TF32 products, fp32
                                    accumulation)                                          */
-    uint32_t critic_hidden;     /* 64 (the only critic width in this build)                  */
+    uint32_t critic_hidden;     /* 64 (ppo.hpp:41-45)                                        */
     uint32_t flags;             /* MDN_SHAPE_* bits                                          */
     float room_min[3];          /* wray/wclearance room, world.hpp:73-74,85: (-2,-5,0)       */
     float room_max[3];          /*                                        (14, 5,5)          */
+    /* Layered networks (no counterpart in the reference, whose actor and
+     * critic have one hidden layer of tanh units): hidden layers of the
+     * actor / critic (0 = 1) and their activation (MDN_ACT_*, 0 = tanh).
+     * Any of them, or a critic other than 64 units, selects the layered
+     * path for both networks: dense fp32 kernels, layer by layer, with the
+     * parameters flat per layer (W [out][in] then b), the actor's log_std[4]
+     * last; one tanh layer gives the reference's layout. actor_hidden and
+     * critic_hidden are then 1..2048 (0 = 64). */
+    uint32_t actor_layers, critic_layers;
+    uint32_t actor_activation, critic_activation;
 } mdn_rollout_shape;
 #define MDN_SHAPE_CUSTOM_ROOM 1u /* use room_min/room_max instead of the reference room */
+#define MDN_ACT_TANH 0u
+#define MDN_ACT_GELU 1u /* 0.5 z (1 + erf(z / sqrt 2)) */
 
 /* PpoCheckpointHeader prefix layout, main.mm:984-991 (136 bytes). */
 typedef struct mdn_checkpoint_header {

@@ -137,6 +137,8 @@ extern "C" int mdn_sim_export_policy(mdn_sim* sim, const char* path, const char*
                                      float max_speed_mps) {
     return guarded([&] {
         require(sim != nullptr, MDN_ERR_INVALID, "policy export: null simulator");
+        require(!sim->layered, MDN_ERR_INVALID,
+                "policy export: NAVPOL1/NAVWID4 hold one-hidden-layer tanh actors, not layered networks");
         cuda_check(cudaSetDevice(sim->dev->gpu), "cudaSetDevice");
         std::vector<float> actor(sim->actor_params);
         cuda_check(cudaMemcpyAsync(actor.data(), sim->buf[MDN_BUF_ACTOR], actor.size() * sizeof(float),

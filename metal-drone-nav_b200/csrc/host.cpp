@@ -235,6 +235,16 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
     a.actor_log_std = a.actor_b2 + kActions;
     a.wide_partials = wide_partials;
     a.wide_slices = wide ? actor_hidden / 128 : 0;
+    a.critic_values = nullptr;
+    a.next_co = nullptr;
+    if (lay) {  // layered networks: k_act adds b2 and the prior to the actor outputs, as for the wide actor
+        a.wide_partials = lay->out_a;
+        a.wide_slices = 1;
+        a.critic_values = lay->values;
+        a.next_co = lay->next_co;
+        a.actor_b2 = lay->actor.bias_offset(lay->actor.layers);
+        a.actor_log_std = lay->actor.param_count() - kActions;
+    }
     a.audit = audit_enabled ? static_cast<mdn_contact_audit*>(buf[MDN_BUF_CONTACT_AUDIT]) : nullptr;
     a.audit_margin = audit_margin;
     a.delay_rehearsal = delay_rehearsal ? 1u : 0u;
@@ -250,6 +260,8 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
     a.env_physics = static_cast<mdn_physics_params*>(buf[MDN_BUF_ENV_PHYSICS]);
     a.reset_list = reset_mem;
     a.reset_count = reset_mem ? reset_mem + n : nullptr;
+    a.reset_pending = reset_mem ? reinterpret_cast<uint8_t*>(reset_mem + n + 32) : nullptr;
+    a.phase = tick & 1u;
     return a;
 }
 
@@ -319,12 +331,27 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
                     "actor_obs_dim: this build implements the 184-input guided actor");
             require(shape->critic_obs_dim == 0 || shape->critic_obs_dim == kCriticObs, MDN_ERR_INVALID,
                     "critic_obs_dim: this build implements the 32-input critic");
-            const uint32_t ah = shape->actor_hidden;
-            require(ah == 0 || ah == uint32_t(kHidden) || (ah % 256 == 0 && ah >= 256 && ah <= 8192), MDN_ERR_INVALID,
-                    "actor_hidden: 64, or a multiple of 256 up to 8192 (tensor-core wide actor)");
-            require(shape->critic_hidden == 0 || shape->critic_hidden == uint32_t(kHidden), MDN_ERR_INVALID,
-                    "critic_hidden: this build implements the 64-unit critic");
+            const uint32_t ah = shape->actor_hidden, ch = shape->critic_hidden;
+            require(shape->actor_activation <= MDN_ACT_GELU && shape->critic_activation <= MDN_ACT_GELU,
+                    MDN_ERR_INVALID, "activation: MDN_ACT_TANH or MDN_ACT_GELU");
+            require(shape->actor_layers <= 8 && shape->critic_layers <= 8, MDN_ERR_INVALID,
+                    "layers: at most 8 hidden layers per network");
+            const bool layered = shape->actor_layers > 1 || shape->critic_layers > 1 || shape->actor_activation != 0 ||
+                                 shape->critic_activation != 0 || (ch != 0 && ch != uint32_t(kHidden));
+            if (layered) {
+                require(ah <= 2048 && ch <= 2048, MDN_ERR_INVALID,
+                        "layered networks: actor_hidden and critic_hidden 1..2048 (0 = 64)");
+            } else {
+                require(ah == 0 || ah == uint32_t(kHidden) || (ah % 256 == 0 && ah >= 256 && ah <= 8192), MDN_ERR_INVALID,
+                        "actor_hidden: 64, or a multiple of 256 up to 8192 (tensor-core wide actor)");
+            }
             if (ah != 0) sim->shape.actor_hidden = ah;
+            if (ch != 0) sim->shape.critic_hidden = ch;
+            sim->shape.actor_layers = shape->actor_layers ? shape->actor_layers : 1;
+            sim->shape.critic_layers = shape->critic_layers ? shape->critic_layers : 1;
+            sim->shape.actor_activation = shape->actor_activation;
+            sim->shape.critic_activation = shape->critic_activation;
+            sim->layered = layered;
             if (shape->flags & MDN_SHAPE_CUSTOM_ROOM) {
                 for (int j = 0; j < 3; j++) {
                     require(shape->room_max[j] > shape->room_min[j], MDN_ERR_INVALID, "room bounds");
@@ -343,7 +370,23 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         const size_t n = sim->n, rows = n * horizon;
         sim->actor_hidden = sim->shape.actor_hidden;
         sim->actor_params = actor_param_count(sim->actor_hidden);
-        const bool wide = sim->actor_hidden != uint32_t(kHidden);
+        MlpShape mlp_actor, mlp_critic;
+        if (sim->layered) {
+            mlp_actor.in = kActorObs;
+            mlp_actor.hidden = sim->shape.actor_hidden;
+            mlp_actor.layers = sim->shape.actor_layers;
+            mlp_actor.out = kActions;
+            mlp_actor.activation = sim->shape.actor_activation;
+            mlp_actor.log_std = true;
+            mlp_critic.in = kCriticObs;
+            mlp_critic.hidden = sim->shape.critic_hidden;
+            mlp_critic.layers = sim->shape.critic_layers;
+            mlp_critic.out = 1;
+            mlp_critic.activation = sim->shape.critic_activation;
+            sim->actor_params = mlp_actor.param_count();
+            sim->critic_params = mlp_critic.param_count();
+        }
+        const bool wide = !sim->layered && sim->actor_hidden != uint32_t(kHidden);
         require(!wide || rows < (size_t(1) << 31), MDN_ERR_INVALID, "wide actor: horizon x n must stay below 2^31 rows");
         size_t* b = sim->bytes;
         b[MDN_BUF_STATES] = n * sizeof(mdn_physics_state);
@@ -353,7 +396,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         b[MDN_BUF_POSES] = n * kFrames * 12 * sizeof(float);
         b[MDN_BUF_COMMANDS] = n * kFrames * kActions * sizeof(float);
         b[MDN_BUF_ACTOR] = size_t(sim->actor_params) * sizeof(float);
-        b[MDN_BUF_CRITIC] = kCriticParams * sizeof(float);
+        b[MDN_BUF_CRITIC] = size_t(sim->critic_params) * sizeof(float);
         b[MDN_BUF_OBS] = rows * kActorObs * sizeof(float);
         b[MDN_BUF_CO] = rows * kCriticObs * sizeof(float);
         b[MDN_BUF_ACTIONS] = rows * kActions * sizeof(float);
@@ -381,8 +424,9 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         }
         {
             cudaError_t e = cudaMalloc(&sim->world_soa, n * kWorldSoaWords * sizeof(float));
-            if (e == cudaSuccess) e = cudaMalloc(&sim->reset_mem, (n + 32) * sizeof(uint32_t));
-            if (e == cudaSuccess) e = cudaMemset(sim->reset_mem, 0, (n + 32) * sizeof(uint32_t));
+            const size_t reset_bytes = (n + 32) * sizeof(uint32_t) + ((size_t(n) + 15) & ~size_t(15));
+            if (e == cudaSuccess) e = cudaMalloc(&sim->reset_mem, reset_bytes);
+            if (e == cudaSuccess) e = cudaMemset(sim->reset_mem, 0, reset_bytes);
             if (e != cudaSuccess) {
                 for (int k = 0; k < MDN_BUF_COUNT; k++) cudaFree(sim->buf[k]);
                 cudaFree(sim->world_soa);
@@ -420,11 +464,50 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
             wa.error = sim->wide_error;
             sim->wide->sm_count = dev->sm_count;
         }
+        if (sim->layered) {
+            // Per-step scratch of the layered networks: two activation
+            // buffers of the wider network, the actor outputs, the values and
+            // the post-step critic observations.
+            const size_t widest = std::max(mlp_actor.hidden, mlp_critic.hidden);
+            const size_t act_floats = n * widest, bytes = (2 * act_floats + n * 4 + n + n * kCriticObs) * sizeof(float);
+            const cudaError_t e = cudaMalloc(&sim->lay_mem, bytes);
+            if (e != cudaSuccess) {
+                for (int k = 0; k < MDN_BUF_COUNT; k++) cudaFree(sim->buf[k]);
+                cudaFree(sim->world_soa);
+                cudaFree(sim->reset_mem);
+                throw Error(MDN_ERR_NOMEM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
+            }
+            float* f = static_cast<float*>(sim->lay_mem);
+            sim->lay = new LayeredStep{};
+            LayeredStep& L = *sim->lay;
+            L.actor = mlp_actor;
+            L.critic = mlp_critic;
+            L.actor_params = static_cast<const float*>(sim->buf[MDN_BUF_ACTOR]);
+            L.critic_params = static_cast<const float*>(sim->buf[MDN_BUF_CRITIC]);
+            L.obs = static_cast<const float*>(sim->buf[MDN_BUF_OBS]);
+            L.co = static_cast<const float*>(sim->buf[MDN_BUF_CO]);
+            L.act[0] = f;
+            L.act[1] = f + act_floats;
+            L.out_a = f + 2 * act_floats;
+            L.values = L.out_a + n * 4;
+            L.next_co = L.values + n;
+            L.next_values = static_cast<float*>(sim->buf[MDN_BUF_NEXT_VALUES]);
+        }
         cuda_check(cudaStreamCreateWithFlags(&sim->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        {
+            int least = 0, greatest = 0;
+            cuda_check(cudaDeviceGetStreamPriorityRange(&least, &greatest), "stream priority range");
+            sim->fork.priority = greatest;
+            cuda_check(cudaStreamCreateWithPriority(&sim->fork.side, cudaStreamNonBlocking, greatest),
+                       "cudaStreamCreate (reset branch)");
+            cuda_check(cudaEventCreateWithFlags(&sim->fork.fork, cudaEventDisableTiming), "cudaEventCreate");
+            cuda_check(cudaEventCreateWithFlags(&sim->fork.join, cudaEventDisableTiming), "cudaEventCreate");
+        }
         cuda_check(cudaEventCreate(&sim->ev_start), "cudaEventCreate");
         cuda_check(cudaEventCreate(&sim->ev_stop), "cudaEventCreate");
         std::vector<float> actor, critic;
-        init_policy(actor, critic, sim->actor_hidden);
+        if (sim->layered) init_layered(mlp_actor, mlp_critic, actor, critic);
+        else init_policy(actor, critic, sim->actor_hidden);
         mdn_physics_params params;
         if (physics) params = *physics;
         else mdn_physics_crazyflie_default(&params);
@@ -469,8 +552,13 @@ extern "C" int mdn_sim_destroy(mdn_sim* sim) {
         cudaFree(sim->wide_partials);
         cudaFree(sim->wide_error);
         delete sim->wide;
+        cudaFree(sim->lay_mem);
+        delete sim->lay;
         cudaEventDestroy(sim->ev_start);
         cudaEventDestroy(sim->ev_stop);
+        if (sim->fork.fork) cudaEventDestroy(sim->fork.fork);
+        if (sim->fork.join) cudaEventDestroy(sim->fork.join);
+        if (sim->fork.side) cudaStreamDestroy(sim->fork.side);
         cudaStreamDestroy(sim->stream);
         auto& v = sim->dev->sims;
         v.erase(std::remove(v.begin(), v.end(), sim), v.end());
@@ -510,7 +598,8 @@ extern "C" int mdn_sim_step(mdn_sim* sim, uint32_t tick) {
     return guarded([&] {
         checked(sim);
         require(tick < sim->horizon, MDN_ERR_INVALID, "tick must be below the horizon");
-        cuda_check(launch_step(sim->args(tick), sim->plan, sim->nominal, sim->stream, sim->wide), "step");
+        cuda_check(launch_step(sim->args(tick), sim->plan, sim->nominal, sim->stream, sim->wide, true, nullptr, sim->lay),
+                   "step");
     });
 }
 
@@ -527,8 +616,16 @@ extern "C" int mdn_sim_collect(mdn_sim* sim, uint32_t steps) {
             cudaGraph_t graph;
             cuda_check(cudaStreamBeginCapture(sim->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
             cudaError_t launch = cudaSuccess;
-            for (uint32_t t = 0; t < steps && launch == cudaSuccess; t++)
-                launch = launch_step(sim->args(t % sim->horizon), sim->plan, sim->nominal, sim->stream, sim->wide);
+            // Inside the rollout each step's ended episodes are reset by the
+            // next step's k_reset_sense, beside its k_sense; the last step
+            // flushes them, so the state after a collect is the same as after
+            // single steps.
+            for (uint32_t t = 0; t < steps && launch == cudaSuccess; t++) {
+                SimArgs a = sim->args(t % sim->horizon);
+                a.phase = t & 1u;
+                launch = launch_step(a, sim->plan, sim->nominal, sim->stream, sim->wide, t + 1 == steps,
+                                     t > 0 ? &sim->fork : nullptr, sim->lay);
+            }
             const cudaError_t end = cudaStreamEndCapture(sim->stream, &graph);
             cuda_check(launch, "capture step");
             cuda_check(end, "end capture");
@@ -737,7 +834,7 @@ extern "C" int mdn_sim_dims(mdn_sim* sim, uint32_t* n, uint32_t* horizon, uint32
         if (n) *n = sim->n;
         if (horizon) *horizon = sim->horizon;
         if (actor_params) *actor_params = sim->actor_params;
-        if (critic_params) *critic_params = kCriticParams;
+        if (critic_params) *critic_params = sim->critic_params;
     });
 }
 
@@ -747,7 +844,8 @@ extern "C" int mdn_sim_profile_step(mdn_sim* sim, uint32_t tick, float ms[3]) {
         require(ms != nullptr && tick < sim->horizon, MDN_ERR_INVALID, "profile_step: bad argument");
         cudaEvent_t ev[4];
         for (auto& e : ev) cuda_check(cudaEventCreate(&e), "event");
-        const cudaError_t launch = launch_step_profiled(sim->args(tick), sim->plan, sim->nominal, sim->stream, ev, sim->wide);
+        const cudaError_t launch =
+            launch_step_profiled(sim->args(tick), sim->plan, sim->nominal, sim->stream, ev, sim->wide, sim->lay);
         const cudaError_t wait = cudaEventSynchronize(ev[3]);
         for (int k = 0; k < 3 && launch == cudaSuccess && wait == cudaSuccess; k++) cudaEventElapsedTime(&ms[k], ev[k], ev[k + 1]);
         for (auto& e : ev) cudaEventDestroy(e);

@@ -11,6 +11,7 @@
 
 #include "mdn.h"
 #include "mdn_shared.h"
+#include "mlp.h"
 #include "wide.h"
 
 namespace mdn {
@@ -52,11 +53,15 @@ cudaError_t configure_kernels();
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s);
 cudaError_t launch_world_mirror(const SimArgs& a, cudaStream_t s);
 StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_override);
+// flush = false leaves the step's ended episodes to the next step, which
+// must then pass `fork` (only inside a collected rollout, whose last step
+// flushes): its listed resets run in k_reset_sense on the fork's side stream.
 cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, const mdn_physics_params& nominal, cudaStream_t s,
-                        const WideStep* wide);
+                        const WideStep* wide, bool flush = true, const StepFork* fork = nullptr,
+                        const LayeredStep* layered = nullptr);
 size_t act_smem_bytes();
 cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, const mdn_physics_params& nominal, cudaStream_t s,
-                                 cudaEvent_t ev[4], const WideStep* wide);
+                                 cudaEvent_t ev[4], const WideStep* wide, const LayeredStep* layered = nullptr);
 cudaError_t fp32_peak(int sm_count, double* tflops);
 cudaError_t division_check(uint64_t samples, uint64_t seed, uint64_t* mismatches, int sm_count);
 int kernels_per_step(const mdn_sim_config& c, bool wide);
@@ -96,11 +101,17 @@ struct mdn_sim {
     mdn_rollout_shape shape{};
     uint32_t horizon = 0, n = 0, env_base = 0;
     cudaStream_t stream = nullptr;
+    mdn::StepFork fork{};  // side stream + events of the collected rollout's forked sensing
     void* buf[MDN_BUF_COUNT] = {};
     float* world_soa = nullptr;  // device mirror of the worlds, structure of arrays
-    uint32_t* reset_mem = nullptr;  // [n] reset list, then its count (k_advance -> k_reset_list)
+    uint32_t* reset_mem = nullptr;  // [n] reset list, its two counts, then [n] pending bytes (k_advance -> k_sense / k_reset_list)
     uint32_t actor_hidden = mdn::kHidden;                   // 64, or a wide actor (multiple of 256)
     uint32_t actor_params = mdn::actor_param_count(mdn::kHidden);
+    uint32_t critic_params = mdn::kCriticParams;
+    // Layered networks (mlp.cu): shapes, step launch arguments, scratch.
+    bool layered = false;
+    mdn::LayeredStep* lay = nullptr;
+    void* lay_mem = nullptr;
     float* wide_partials = nullptr;                         // [hidden/128][n][4] slice sums of the wide forward
     uint32_t* wide_error = nullptr;                         // barrier-timeout flag of the wide kernels
     mdn::WideStep* wide = nullptr;                          // tensor maps + launch arguments (wide actors)

@@ -37,6 +37,16 @@ struct StepPlan {
     int advance_group = 1;  // lanes per environment in k_advance (1 or 2)
     int advance_grid = 1;   // k_advance CTAs (grid-stride over environments)
     int reset_grid = 1;     // k_reset_list CTAs (grid-stride over the step's reset list)
+    int sense_reset_blocks = 1;  // k_reset_sense blocks (the previous step's listed resets)
+};
+
+// Side stream and events of the forked sensing step inside a collected
+// rollout (k_reset_sense beside k_sense), and the launch priority of its
+// reset kernel.
+struct StepFork {
+    cudaStream_t side;
+    cudaEvent_t fork, join;
+    int priority;
 };
 
 // Everything one launch of a rollout kernel needs (passed by value).
@@ -85,6 +95,12 @@ struct SimArgs {
     uint32_t actor_hidden, actor_b2, actor_log_std;
     const float* wide_partials;
     uint32_t wide_slices;
+    // Layered networks (mlp.cu): the step's critic values come from
+    // critic_values[n], and k_advance stores the post-step critic observation
+    // in next_co[n][32] for the layered critic instead of evaluating the
+    // 64-unit one (both null otherwise).
+    const float* critic_values;
+    float* next_co;
     // Mechanical contact audit (null = off): results[tick][n], safety margin.
     mdn_contact_audit* audit;
     float audit_margin;
@@ -101,10 +117,18 @@ struct SimArgs {
     // while runtime.enabled, each env's plant lives in env_physics[n].
     mdn_runtime_config runtime;
     mdn_physics_params* env_physics;
-    // Episodes that ended in this step: k_advance appends, k_reset_list
-    // resets them, k_sense of the next step empties the list.
+    // Episodes that ended in a step: k_advance appends them to the list and
+    // counts them in reset_count[phase], and sets reset_pending[i] of every
+    // environment it advances (1 = listed). Inside a collected rollout the
+    // next step's k_reset_sense resets and senses the listed environments
+    // (reading reset_count[phase ^ 1]) while k_sense senses the others and
+    // zeroes reset_count[phase] for its own advance; a step whose state the
+    // host may read ends with the k_reset_list flush, which resets them at
+    // once and clears their flags.
     uint32_t* reset_list;  // [n]
-    uint32_t* reset_count;
+    uint32_t* reset_count;  // [2]
+    uint8_t* reset_pending;  // [n]
+    uint32_t phase;  // 0 / 1, alternating over the steps of a collected rollout
 };
 
 }  // namespace mdn

@@ -65,6 +65,22 @@ struct mdn_ppo {
     TcMaps tc_maps{};
     uint32_t tc_grid = 1;
     uint32_t* tc_error = nullptr;
+    // layered networks (mlp.cu): per hidden layer the activations y and
+    // pre-activations z of the minibatch rows, the output layers, two delta
+    // buffers, the weight-gradient partials and the flat gradient
+    bool layered = false;
+    void* lay_mem = nullptr;
+    std::vector<float*> lay_ya, lay_za, lay_yc, lay_zc;
+    float* lay_out_a = nullptr;   // [minibatch][4]
+    float* lay_out_c = nullptr;   // [minibatch]
+    float* lay_dout_a = nullptr;  // [minibatch][4]
+    float* lay_dout_c = nullptr;  // [minibatch]
+    float* lay_d[2] = {nullptr, nullptr};  // [minibatch][widest]
+    float* lay_part = nullptr;    // [chunks][largest layer's W + b]
+    float* lay_cta = nullptr;     // [loss CTAs][8]
+    float* lay_grad = nullptr;    // [actor params + critic params]
+    float* lay_norm = nullptr;    // [2 * SMs]
+    uint32_t lay_chunks = 1, lay_chunk_rows = 64, lay_loss_ctas = 1;
 };
 
 namespace {
@@ -83,6 +99,124 @@ mdn_ppo* checked(mdn_ppo* p) {
 }
 
 // Enqueue one whole rollout update on the sim stream (captured into a graph).
+// One minibatch of the layered networks: actor and critic forward storing
+// each hidden layer's activations and pre-activations, the loss, then layer
+// by layer from the top: weight-gradient partials of the layer (summed in
+// chunk order into the flat gradient) and the deltas of the layer below;
+// [allreduce]; clip + Adam per network (log-std clamp on the actor).
+void enqueue_layered_minibatch(mdn_ppo* t, uint32_t u, bool multi) {
+    mdn_sim* sim = t->sim;
+    mdn_device* dev = sim->dev;
+    const LayeredStep& L = *sim->lay;
+    const PpoArgs& p = t->args;
+    cudaStream_t s = sim->stream;
+    std::string err;
+    DenseRows R;
+    R.rows = t->minibatch;
+    R.rows_dev = p.batch;
+    R.row0_dev = p.starts;
+    R.index = u;
+    auto forward = [&](const MlpShape& net, const float* params, const float* x, const std::vector<float*>& ys,
+                       const std::vector<float*>& zs, float* out, bool out_bias) {
+        const float* in = x;
+        bool in_row0 = true;
+        for (uint32_t l = 0; l <= net.layers; l++) {
+            const bool last = l == net.layers;
+            DenseFwd f{};
+            f.x = in;
+            f.w = params + net.weight_offset(l);
+            f.b = (!last || out_bias) ? params + net.bias_offset(l) : nullptr;
+            f.y = last ? out : ys[l];
+            f.z = last ? nullptr : zs[l];
+            f.k = net.in_dim(l);
+            f.n = net.out_dim(l);
+            f.act = last ? -1 : int(net.activation);
+            cuda_check(launch_dense_fwd(f, R, in_row0, s), "layered forward");
+            in = f.y;
+            in_row0 = false;
+        }
+    };
+    auto backward = [&](const MlpShape& net, const float* params, const float* x0, const std::vector<float*>& ys,
+                        const std::vector<float*>& zs, const float* dout, float* grad) {
+        const float* dy = dout;
+        for (int l = int(net.layers); l >= 0; l--) {
+            DenseWgrad w{};
+            w.dy = dy;
+            w.x = l == 0 ? x0 : ys[l - 1];
+            w.x_row0 = l == 0;
+            w.part = t->lay_part;
+            w.k = net.in_dim(uint32_t(l));
+            w.n = net.out_dim(uint32_t(l));
+            w.chunk_rows = t->lay_chunk_rows;
+            cuda_check(launch_dense_wgrad(w, R, t->lay_chunks, s), "layered weight gradient");
+            cuda_check(launch_chunk_sum(t->lay_part, t->lay_chunks, size_t(w.n) * w.k + w.n,
+                                        grad + net.weight_offset(uint32_t(l)), s),
+                       "layered gradient sum");
+            if (l == 0) break;
+            DenseBwd b{};
+            b.dy = dy;
+            b.w = params + net.weight_offset(uint32_t(l));
+            b.zp = zs[l - 1];
+            b.dx = t->lay_d[(net.layers - uint32_t(l)) & 1u];
+            b.k = net.in_dim(uint32_t(l));
+            b.n = net.out_dim(uint32_t(l));
+            b.act = int(net.activation);
+            cuda_check(launch_dense_bwd(b, R, s), "layered deltas");
+            dy = b.dx;
+        }
+    };
+    const uint32_t actor_n = sim->actor_params;
+    float* grad_a = t->lay_grad;
+    float* grad_c = t->lay_grad + actor_n;
+    forward(L.actor, p.actor, p.obs, t->lay_ya, t->lay_za, t->lay_out_a, false);
+    forward(L.critic, p.critic, p.co, t->lay_yc, t->lay_zc, t->lay_out_c, true);
+    LayeredLoss lo{};
+    lo.out_a = t->lay_out_a;
+    lo.out_c = t->lay_out_c;
+    lo.obs = p.obs;
+    lo.actions = p.actions;
+    lo.logp = p.logp;
+    lo.advantages = p.advantages;
+    lo.returns = p.returns;
+    lo.b2 = p.actor + L.actor.bias_offset(L.actor.layers);
+    lo.log_std = p.actor + actor_n - kActions;
+    lo.global_batch = p.global_batch;
+    lo.clip = p.clip;
+    lo.value_coef = p.value_coef;
+    lo.entropy_coef = p.entropy_coef;
+    lo.d_out_a = t->lay_dout_a;
+    lo.d_out_c = t->lay_dout_c;
+    lo.cta_sums = t->lay_cta;
+    cuda_check(launch_layered_loss(lo, R, s), "layered loss");
+    backward(L.actor, p.actor, p.obs, t->lay_ya, t->lay_za, t->lay_dout_a, grad_a);
+    backward(L.critic, p.critic, p.co, t->lay_yc, t->lay_zc, t->lay_dout_c, grad_c);
+    cuda_check(launch_layered_finish(t->lay_cta, t->lay_loss_ctas, grad_a + actor_n - kActions, p.metric_rows + 4 * u,
+                                     p.batch, u, s),
+               "layered loss sums");
+    if (multi)
+        cuda_check(comm_allreduce_float(dev, t->lay_grad, size_t(actor_n) + sim->critic_params, s, err), err.c_str());
+    WideAdamArgs ad{};
+    ad.grad = grad_a;
+    ad.params = p.actor;
+    ad.m = p.actor_m;
+    ad.v = p.actor_v;
+    ad.count = actor_n;
+    ad.bias_corr = p.bias_corr + 2 * u;
+    ad.learning_rate = p.learning_rate;
+    ad.max_norm = p.max_norm;
+    ad.norm_out = p.grad_norms + 2 * u;
+    cuda_check(launch_wide_clip_adam(ad, t->lay_norm, dev->sm_count, s), "layered actor clip+adam");
+    WideAdamArgs ac = ad;
+    ac.grad = grad_c;
+    ac.params = p.critic;
+    ac.m = p.critic_m;
+    ac.v = p.critic_v;
+    ac.count = sim->critic_params;
+    ac.no_clamp = 1;
+    ac.norm_out = p.grad_norms + 2 * u + 1;
+    cuda_check(launch_wide_clip_adam(ac, t->lay_norm, dev->sm_count, s), "layered critic clip+adam");
+}
+
 void enqueue_update(mdn_ppo* t) {
     mdn_sim* sim = t->sim;
     mdn_device* dev = sim->dev;
@@ -101,6 +235,10 @@ void enqueue_update(mdn_ppo* t) {
     const bool multi = dev->world > 1;
     const uint32_t chunks = multi ? std::max<uint32_t>(t->grad_chunks, 2) : t->grad_chunks;
     for (uint32_t u = 0; u < t->updates; u++) {
+        if (t->layered) {
+            enqueue_layered_minibatch(t, u, multi);
+            continue;
+        }
         if (t->wide) {
             // Wide actor: tensor-core forward -> loss (+ critic, b2, log_std
             // gradients) -> tensor-core backward (deltas, db1/dW2 partials) ->
@@ -208,8 +346,9 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
         size_t off = 0;
         auto carve = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
         const size_t AP = sim->actor_params;
-        const size_t o_am = carve(AP * 4), o_av = carve(AP * 4), o_cm = carve(kCriticParams * 4),
-                     o_cv = carve(kCriticParams * 4), o_sp = carve(gae_blocks(sim->n) * 8), o_st = carve(2 * 8),
+        const size_t CP = sim->critic_params;
+        const size_t o_am = carve(AP * 4), o_av = carve(AP * 4), o_cm = carve(CP * 4),
+                     o_cv = carve(CP * 4), o_sp = carve(gae_blocks(sim->n) * 8), o_st = carve(2 * 8),
                      o_sv = carve(2 * 4), o_idx = carve(U * 3 * 4), o_bias = carve(U * 2 * 4), o_ah = carve(mb * 64 * 4),
                      o_ch = carve(mb * 64 * 4), o_ad = carve(mb * 64 * 4), o_cd = carve(mb * 64 * 4),
                      o_dm = carve(mb * 4 * 4), o_dls = carve(mb * 4 * 4), o_dv = carve(mb * 4),
@@ -316,6 +455,60 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
                                      kActorObs * 4, 128),
                        "actor W1 tensor map (128-row boxes)");
         }
+        if (sim->layered) {
+            t->layered = true;
+            const MlpShape& A = sim->lay->actor;
+            const MlpShape& C = sim->lay->critic;
+            a.actor_b2 = A.bias_offset(A.layers);
+            a.actor_log_std = A.param_count() - kActions;
+            // Weight-gradient chunks: about 24 runs of rows per minibatch.
+            t->lay_chunk_rows = std::max<uint32_t>(64, (t->minibatch / 24 + 15) / 16 * 16);
+            t->lay_chunks = (t->minibatch + t->lay_chunk_rows - 1) / t->lay_chunk_rows;
+            t->lay_loss_ctas = layered_loss_ctas(t->minibatch);
+            size_t largest = 0;
+            for (const MlpShape* net : {&A, &C})
+                for (uint32_t l = 0; l <= net->layers; l++)
+                    largest = std::max(largest, size_t(net->out_dim(l)) * net->in_dim(l) + net->out_dim(l));
+            const size_t widest = std::max(A.hidden, C.hidden);
+            size_t loff = 0;
+            auto lcarve = [&](size_t bytes) { const size_t o = loff; loff += align256(bytes); return o; };
+            std::vector<size_t> o_ya, o_za, o_yc, o_zc;
+            for (uint32_t l = 0; l < A.layers; l++) {
+                o_ya.push_back(lcarve(mb * A.hidden * 4));
+                o_za.push_back(lcarve(mb * A.hidden * 4));
+            }
+            for (uint32_t l = 0; l < C.layers; l++) {
+                o_yc.push_back(lcarve(mb * C.hidden * 4));
+                o_zc.push_back(lcarve(mb * C.hidden * 4));
+            }
+            const size_t l_oa = lcarve(mb * 16), l_oc = lcarve(mb * 4), l_da = lcarve(mb * 16), l_dc = lcarve(mb * 4),
+                         l_d0 = lcarve(mb * widest * 4), l_d1 = lcarve(mb * widest * 4),
+                         l_part = lcarve(size_t(t->lay_chunks) * largest * 4),
+                         l_cta = lcarve(size_t(t->lay_loss_ctas) * 8 * 4), l_g = lcarve((AP + CP) * 4),
+                         l_n = lcarve(size_t(sms) * 2 * 4);
+            const cudaError_t le = cudaMalloc(&t->lay_mem, loff);
+            if (le != cudaSuccess) {
+                cudaFree(t->mem);
+                throw Error(MDN_ERR_NOMEM, std::string("cudaMalloc layered trainer: ") + cudaGetErrorString(le));
+            }
+            char* lb = static_cast<char*>(t->lay_mem);
+            cuda_check(cudaMemsetAsync(lb, 0, loff, sim->stream), "clear layered trainer memory");
+            auto at = [&](size_t o) { return reinterpret_cast<float*>(lb + o); };
+            for (size_t o : o_ya) t->lay_ya.push_back(at(o));
+            for (size_t o : o_za) t->lay_za.push_back(at(o));
+            for (size_t o : o_yc) t->lay_yc.push_back(at(o));
+            for (size_t o : o_zc) t->lay_zc.push_back(at(o));
+            t->lay_out_a = at(l_oa);
+            t->lay_out_c = at(l_oc);
+            t->lay_dout_a = at(l_da);
+            t->lay_dout_c = at(l_dc);
+            t->lay_d[0] = at(l_d0);
+            t->lay_d[1] = at(l_d1);
+            t->lay_part = at(l_part);
+            t->lay_cta = at(l_cta);
+            t->lay_grad = at(l_g);
+            t->lay_norm = at(l_n);
+        }
         cuda_check(cudaMallocHost(&t->h_idx, U * 3 * 4), "pinned staging");
         cuda_check(cudaMallocHost(&t->h_bias, U * 2 * 4), "pinned staging");
         cuda_check(cudaEventCreateWithFlags(&t->staged, cudaEventDisableTiming), "event");
@@ -337,6 +530,7 @@ extern "C" int mdn_ppo_destroy(mdn_ppo* t) {
         if (t->graph) cudaGraphExecDestroy(t->graph);
         cudaFree(t->mem);
         cudaFree(t->wide_mem);
+        cudaFree(t->lay_mem);
         cudaFreeHost(t->h_idx);
         cudaFreeHost(t->h_bias);
         cudaEventDestroy(t->staged);
@@ -461,6 +655,8 @@ extern "C" int mdn_ppo_set_tensor_cores(mdn_ppo* t, int enabled) {
     return guarded([&] {
         checked(t);
         mdn_sim* sim = t->sim;
+        require(!(enabled && sim->layered), MDN_ERR_INVALID,
+                "tensor-core minibatch path: the 64-unit actor and critic only (not layered networks)");
         require(!(enabled && sim->wide), MDN_ERR_INVALID,
                 "tensor-core minibatch path: the wide actor already runs on the tensor cores");
         cuda_check(cudaStreamSynchronize(sim->stream), "set tensor cores");
@@ -535,7 +731,7 @@ extern "C" int mdn_ppo_moments(mdn_ppo* t, int which, float* host, size_t count,
         checked(t);
         require(which >= 0 && which < 4 && host, MDN_ERR_INVALID, "moments: bad argument");
         float* d = which == 0 ? t->args.actor_m : which == 1 ? t->args.actor_v : which == 2 ? t->args.critic_m : t->args.critic_v;
-        const size_t n = which < 2 ? size_t(t->sim->actor_params) : size_t(kCriticParams);
+        const size_t n = which < 2 ? size_t(t->sim->actor_params) : size_t(t->sim->critic_params);
         require(count == n, MDN_ERR_INVALID, "moments: count mismatch");
         cuda_check(upload ? cudaMemcpyAsync(d, host, n * 4, cudaMemcpyHostToDevice, t->sim->stream)
                           : cudaMemcpyAsync(host, d, n * 4, cudaMemcpyDeviceToHost, t->sim->stream),
@@ -596,6 +792,8 @@ extern "C" int mdn_ppo_checkpoint_save(mdn_ppo* t, const char* path, uint32_t fa
         checked(t);
         require(path != nullptr, MDN_ERR_INVALID, "null path");
         require(t->sim->dev->world == 1, MDN_ERR_INVALID, "checkpoint save: gather sharded state with world == 1");
+        require(!t->sim->layered, MDN_ERR_INVALID,
+                "checkpoint save: PPOFIX1 holds the one-hidden-layer tanh networks, not layered ones");
         mdn_sim* sim = t->sim;
         const std::filesystem::path p(path);
         if (p.has_parent_path()) std::filesystem::create_directories(p.parent_path());
@@ -675,6 +873,8 @@ extern "C" int mdn_ppo_checkpoint_load(mdn_ppo* t, const char* path, uint32_t fa
         checked(t);
         require(path != nullptr, MDN_ERR_INVALID, "null path");
         mdn_sim* sim = t->sim;
+        require(!sim->layered, MDN_ERR_INVALID,
+                "checkpoint load: PPOFIX1 holds the one-hidden-layer tanh networks, not layered ones");
         std::ifstream f(path, std::ios::binary);
         require(bool(f), MDN_ERR_IO, std::string("cannot open checkpoint ") + path);
         mdn_checkpoint_header h;
@@ -804,7 +1004,8 @@ extern "C" int mdn_ppo_profile_minibatch(mdn_ppo* t, uint32_t update, float* ms)
         checked(t);
         require(ms != nullptr && update < t->updates, MDN_ERR_INVALID, "profile minibatch: bad argument");
         require(t->graph != nullptr, MDN_ERR_STATE, "profile minibatch: run one rollout update first");
-        require(!t->wide, MDN_ERR_INVALID, "profile minibatch: the 64-unit actor's minibatch kernels only");
+        require(!t->wide && !t->layered, MDN_ERR_INVALID,
+                "profile minibatch: the 64-unit actor's minibatch kernels only");
         mdn_sim* sim = t->sim;
         cudaStream_t s = sim->stream;
         const bool multi = sim->dev->world > 1;

@@ -14,6 +14,7 @@
 #include "contact.cuh"
 #include "mdn_device.cuh"
 #include "task.cuh"
+#include "mlp.h"
 #include "wide.h"
 #include "world_gen.cuh"
 
@@ -44,20 +45,27 @@ __global__ void __launch_bounds__(128) k_reset(SimArgs a, int first) {
     if (i >= a.n) return;  // warp-uniform
     episode_reset(a, i, first != 0, 0, scratch[threadIdx.x >> 5]);
     refill_ring_warp(a, i);
+    if ((threadIdx.x & 31) == 0) a.reset_pending[i] = 0;
 }
 
 // In-step episode resets (sim.metal:330) of the environments k_advance listed,
 // one warp per listed environment (episode_reset is warp-cooperative), so a
 // reset neither holds up an advance warp nor runs its generator's checks on
-// one lane. Schedule slot tick + 1 as in the advance.
+// one lane. Schedule slot tick + 1 as in the advance. This is the flush that
+// ends a step whose state the host may read (a single step, the last step of
+// a collected rollout); inside a collected rollout the next step's
+// k_reset_sense runs the listed resets instead. Clears each environment's
+// pending flag.
 __global__ void __launch_bounds__(128) k_reset_list(SimArgs a) {
     __shared__ mdn_world scratch[4];  // one world per warp of the 128-thread block
-    const uint32_t count = *reinterpret_cast<volatile uint32_t*>(a.reset_count);
+    const uint32_t listed = a.reset_count[a.phase];
+    const uint32_t count = listed < a.n ? listed : a.n;
     const uint32_t warps = gridDim.x * (blockDim.x / 32);
     for (uint32_t k = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); k < count; k += warps) {
         const uint32_t i = a.reset_list[k];
         episode_reset(a, i, false, a.tick + 1, scratch[threadIdx.x >> 5]);
         refill_ring_warp(a, i);
+        if ((threadIdx.x & 31) == 0) a.reset_pending[i] = 0;
     }
 }
 
@@ -146,19 +154,14 @@ __device__ __forceinline__ float cell_risk(const WarpScene& ws, int row, int col
     return risk;
 }
 
-__global__ void __launch_bounds__(kSenseWarps * 32, 4) k_sense(SimArgs a) {
-    __shared__ WarpScene scenes[kSenseWarps];
-    if (blockIdx.x == 0 && threadIdx.x == 0) *a.reset_count = 0;  // this step's reset list starts empty
+// sim_depth + sim_observe + sim_critic_obs of environment i, by one warp.
+__device__ __forceinline__ void sense_env(const SimArgs& a, uint32_t i, WarpScene& ws) {
     const int lane = threadIdx.x & 31;
-    const int wid = threadIdx.x >> 5;
-    const uint32_t i = blockIdx.x * kSenseWarps + wid;
-    if (i >= a.n) return;
     const mdn_sim_config& c = a.cfg;
     const mdn_sim_run& run = a.runs[i];
     const uint32_t episodes = run.episodes, steps = run.steps;
     if (c.eval && episodes) return;
     const uint32_t gid = a.env_base + i;
-    WarpScene& ws = scenes[wid];
     const mdn_physics_state& st = a.states[i];
     const float pos[3] = {st.position[0], st.position[1], st.position[2]};
     const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2], st.orientation_wxyz[3]};
@@ -485,6 +488,52 @@ __global__ void __launch_bounds__(kSenseWarps * 32, 4) k_sense(SimArgs a) {
         } else if (j == 30) v = w.wind[0];
         else v = w.wind[1];
         co[j] = v;
+    }
+}
+
+// One policy step's sensing, one warp per environment. Environments whose
+// episode ended in the previous step of a collected rollout (reset_pending)
+// are left to k_reset_sense, which runs beside this kernel.
+__global__ void __launch_bounds__(kSenseWarps * 32, 4) k_sense(SimArgs a) {
+    __shared__ WarpScene scenes[kSenseWarps];
+    if (blockIdx.x == 0 && threadIdx.x == 0) a.reset_count[a.phase] = 0;  // this step's reset list starts empty
+    const int wid = threadIdx.x >> 5;
+    const uint32_t i = blockIdx.x * kSenseWarps + wid;
+    if (i >= a.n || a.reset_pending[i]) return;  // warp-uniform
+    sense_env(a, i, scenes[wid]);
+}
+
+// A warp's shared memory in k_reset_sense: the world that an episode reset
+// generates, then the scene of the environment it senses.
+union SenseSmem {
+    WarpScene scene;
+    mdn_world world;
+};
+
+// The episode resets of the previous step of a collected rollout (sim.metal:330,
+// schedule slot = this tick), each followed by that environment's sensing:
+// one warp per environment that k_advance listed. Launched on a forked branch
+// of the rollout graph beside k_sense (which skips these environments), with
+// a higher priority, so that the long world generations overlap the other
+// environments' sensing instead of running as a kernel of their own between
+// the advance and the next sense. A reset and the sensing after it are the
+// same per-environment computations as k_reset_list + k_sense, so the results
+// are unchanged.
+__global__ void __launch_bounds__(kSenseWarps * 32) k_reset_sense(SimArgs a) {
+    __shared__ SenseSmem smem[kSenseWarps];
+    const int wid = threadIdx.x >> 5;
+    const uint32_t listed = a.reset_count[a.phase ^ 1u];
+    const uint32_t count = listed < a.n ? listed : a.n;
+    for (uint32_t k = blockIdx.x * kSenseWarps + wid; k < count; k += gridDim.x * kSenseWarps) {
+        const uint32_t i = a.reset_list[k];
+        // An entry whose flag is clear was reset already (a list that a
+        // k_reset_list flush consumed).
+        if (i >= a.n || !a.reset_pending[i]) continue;
+        episode_reset(a, i, false, a.tick, smem[wid].world);
+        refill_ring_warp(a, i);
+        __syncwarp();
+        sense_env(a, i, smem[wid].scene);
+        __syncwarp();
     }
 }
 
@@ -1071,14 +1120,16 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
             const int h = k / kActorObs, col = k % kActorObs;
             w1p[h * kActW1Pitch + col] = a.actor[k];
         }
-    for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
-        const int h = k / kCriticObs, col = k % kCriticObs;
-        cw1p[h * kActCw1Pitch + col] = a.critic[k];
-    }
+    const bool own_critic = a.critic_values == nullptr;  // else the layered critic's values
+    if (own_critic)
+        for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
+            const int h = k / kCriticObs, col = k % kCriticObs;
+            cw1p[h * kActCw1Pitch + col] = a.critic[k];
+        }
     for (int k = tid; k < kHidden; k += blockDim.x) {
         if (!wide) b1[k] = a.actor[kActorB1 + k];
-        cb1[k] = a.critic[kCriticB1 + k];
-        cw2[k] = a.critic[kCriticW2 + k];
+        cb1[k] = own_critic ? a.critic[kCriticB1 + k] : 0.0f;
+        cw2[k] = own_critic ? a.critic[kCriticW2 + k] : 0.0f;
     }
     if (!wide)
         for (int k = tid; k < kActions * kHidden; k += blockDim.x) w2[k] = a.actor[kActorW2 + k];
@@ -1086,7 +1137,7 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
         b2[tid] = a.actor[a.actor_b2 + tid];
         log_std[tid] = a.actor[a.actor_log_std + tid];
     }
-    if (tid == 0) cb2[0] = a.critic[kCriticB2];
+    if (tid == 0) cb2[0] = own_critic ? a.critic[kCriticB2] : 0.0f;
     __syncthreads();
     const int lane = tid & 31, wid = tid >> 5;
     float* my_obs = rows + wid * kActEnvs * (kActorObs + kCriticObs);  // [4][184]
@@ -1170,9 +1221,13 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
                     if (lane == e) mean_mine[j] = m;
                 }
             }
-            const float v = warp_sum(fmaf(tanhf(y0[e] + cb1[lane]), cw2[lane],
-                                          tanhf(y1[e] + cb1[lane + 32]) * cw2[lane + 32])) + cb2[0];
-            if (lane == e) value_mine = v;
+            if (own_critic) {
+                const float v = warp_sum(fmaf(tanhf(y0[e] + cb1[lane]), cw2[lane],
+                                              tanhf(y1[e] + cb1[lane + 32]) * cw2[lane + 32])) + cb2[0];
+                if (lane == e) value_mine = v;
+            } else if (lane == e && e < envs) {
+                value_mine = a.critic_values[base + e];
+            }
         }
         __syncwarp();
         const uint32_t i = base + uint32_t(lane);
@@ -1448,15 +1503,17 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
     const int tid = threadIdx.x;
     {
         L::fill(raptor_w, reinterpret_cast<const float*>(a.raptor), tid, blockDim.x);
-        for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
-            const int hh = k / kCriticObs, col = k % kCriticObs;
-            cw1p[col * kHidden + (hh % G) * V + hh / G] = a.critic[k];
+        if (!a.next_co) {  // the 64-unit critic (a layered critic runs after this kernel)
+            for (int k = tid; k < kCriticObs * kHidden; k += blockDim.x) {
+                const int hh = k / kCriticObs, col = k % kCriticObs;
+                cw1p[col * kHidden + (hh % G) * V + hh / G] = a.critic[k];
+            }
+            for (int k = tid; k < kHidden; k += blockDim.x) {
+                cb1p[(k % G) * V + k / G] = a.critic[kCriticB1 + k];
+                cw2p[(k % G) * V + k / G] = a.critic[kCriticW2 + k];
+            }
+            if (tid == 0) cb2 = a.critic[kCriticB2];
         }
-        for (int k = tid; k < kHidden; k += blockDim.x) {
-            cb1p[(k % G) * V + k / G] = a.critic[kCriticB1 + k];
-            cw2p[(k % G) * V + k / G] = a.critic[kCriticW2 + k];
-        }
-        if (tid == 0) cb2 = a.critic[kCriticB2];
     }
     __syncthreads();
 
@@ -1585,6 +1642,11 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                 co[30] = w.wind[0];
                 co[31] = w.wind[1];
                 float part = 0.0f;
+                if (a.next_co) {  // layered critic: keep the observation for it
+                    if (r == 0)
+#pragma unroll
+                        for (int k = 0; k < kCriticObs; k++) a.next_co[size_t(i) * kCriticObs + k] = co[k];
+                } else
 #pragma unroll
                 for (int v0 = 0; v0 < V; v0 += 4) {
                     float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -1645,7 +1707,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                     a.terminated[row] = term;
                     a.truncated[row] = timeout && !term;
                 }
-                a.next_values[row] = value;
+                if (!a.next_co) a.next_values[row] = value;
                 if (a.bank_transition) a.bank_transition[row] = a.bank_enabled ? a.bank_active[i] : 0xffffffffu;
                 if (success || collision || timeout) {
                     run.successes += success;
@@ -1656,8 +1718,9 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                     run.total_path += path;
                     run.total_elapsed += elapsed;
                     run.final_progress += 1.0f - after / smax(run.initial_distance, 1.0e-4f);
-                    refill = !c.eval;  // reset by k_reset_list after this launch
+                    refill = !c.eval;  // reset by the next k_sense or by the k_reset_list flush
                 }
+                a.reset_pending[i] = refill ? 1 : 0;
                 if (a.audit) {  // mechanical contact audit of the post-integration pose
                     // Called last, with the pose read back from the stores above, so
                     // that little is live across this out-of-line call.
@@ -1668,12 +1731,13 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
             }
         }
         // Environments whose episode ended (their leader lanes) join the
-        // step's reset list: one atomic per warp, slots in lane order.
+        // step's reset list: one atomic per warp, slots in lane order. Every
+        // active environment's pending flag says whether it is listed.
         const unsigned m = __ballot_sync(0xffffffffu, refill);
         if (m) {
             const int leader = __ffs(m) - 1;
             uint32_t slot = 0;
-            if (lane == leader) slot = atomicAdd(a.reset_count, uint32_t(__popc(m)));
+            if (lane == leader) slot = atomicAdd(a.reset_count + a.phase, uint32_t(__popc(m)));
             slot = __shfl_sync(0xffffffffu, slot, leader);
             if (refill) a.reset_list[slot + uint32_t(__popc(m & ((1u << lane) - 1u)))] = i;
         }
@@ -1786,32 +1850,70 @@ static cudaError_t launch_wide(const SimArgs& a, const WideStep* wide, cudaStrea
     return launch_wide_forward(wide->obs_map, wide->w1_map, p, wide->sm_count, s);
 }
 
-cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, const mdn_physics_params& nominal, cudaStream_t s,
-                        const WideStep* wide) {
+static void launch_sense(const SimArgs& a, cudaStream_t s) {
     k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
+}
+
+// k_reset_sense on the fork's side stream, between an event recorded on `s`
+// and one that `s` waits on before the actor: inside a stream capture this is
+// a parallel branch of the graph beside k_sense.
+static cudaError_t launch_sense_with_resets(const SimArgs& a, const StepPlan& plan, cudaStream_t s,
+                                            const StepFork& fork) {
+    cudaError_t e = cudaEventRecord(fork.fork, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(fork.side, fork.fork, 0);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(plan.sense_reset_blocks));
+    cfg.blockDim = dim3(kSenseWarps * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = fork.side;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributePriority;
+    attr[0].val.priority = fork.priority;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, k_reset_sense, a);
+    if (e == cudaSuccess) launch_sense(a, s);
+    if (e == cudaSuccess) e = cudaEventRecord(fork.join, fork.side);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, fork.join, 0);
+    return e;
+}
+
+cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, const mdn_physics_params& nominal, cudaStream_t s,
+                        const WideStep* wide, bool flush, const StepFork* fork, const LayeredStep* layered) {
+    if (fork) {
+        const cudaError_t fe = launch_sense_with_resets(a, plan, s, *fork);
+        if (fe != cudaSuccess) return fe;
+    } else {
+        launch_sense(a, s);
+    }
     if (a.cfg.geometry_memory)
         k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
     cudaError_t e = launch_wide(a, wide, s);
+    if (e == cudaSuccess && layered) e = launch_layered_step_forward(*layered, a.n, a.tick, s);
     if (e != cudaSuccess) return e;
     launch_act(a, plan, s);
     e = launch_advance(a, plan, nominal, s);
+    if (e == cudaSuccess && layered) e = launch_layered_bootstrap(*layered, a.n, a.tick, s);
     if (e != cudaSuccess) return e;
-    launch_reset_list(a, plan, s);
+    if (flush) launch_reset_list(a, plan, s);
     return cudaGetLastError();
 }
 
 cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, const mdn_physics_params& nominal, cudaStream_t s,
-                                 cudaEvent_t ev[4], const WideStep* wide) {
+                                 cudaEvent_t ev[4], const WideStep* wide, const LayeredStep* layered) {
     cudaEventRecord(ev[0], s);
-    k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
+    launch_sense(a, s);
     if (a.cfg.geometry_memory)
         k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
     cudaEventRecord(ev[1], s);
-    const cudaError_t we = launch_wide(a, wide, s);
+    cudaError_t we = launch_wide(a, wide, s);
+    if (we == cudaSuccess && layered) we = launch_layered_step_forward(*layered, a.n, a.tick, s);
     if (we != cudaSuccess) return we;
     launch_act(a, plan, s);
     cudaEventRecord(ev[2], s);
-    const cudaError_t e = launch_advance(a, plan, nominal, s);
+    cudaError_t e = launch_advance(a, plan, nominal, s);
+    if (e == cudaSuccess && layered) e = launch_layered_bootstrap(*layered, a.n, a.tick, s);
     if (e != cudaSuccess) return e;
     launch_reset_list(a, plan, s);
     cudaEventRecord(ev[3], s);
@@ -1845,6 +1947,9 @@ StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_overrid
     const size_t need = (size_t(n) * g + kAdvanceThreads - 1) / kAdvanceThreads;
     p.advance_grid = int(std::max<size_t>(1, std::min<size_t>(need, size_t(sm_count) * per_sm)));
     p.reset_grid = int(std::max<size_t>(1, std::min<size_t>((size_t(n) + 3) / 4, size_t(sm_count) * 8)));
+    // k_reset_sense blocks: one per SM (eight warps), fewer on shards that
+    // have fewer sensing blocks.
+    p.sense_reset_blocks = int(std::max<size_t>(1, std::min<size_t>(blocks_for(n, kSenseWarps), size_t(sm_count))));
     return p;
 }
 

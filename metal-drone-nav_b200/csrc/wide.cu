@@ -628,7 +628,7 @@ __global__ void k_wide_adam(WideAdamArgs p) {
         p.v[i] = vi;
         const float mh = mi / b1c, vh = vi / b2c;
         float w = p.params[i] - lr * mh / (sqrtf(vh) + 1.0e-8f);
-        if (i >= p.count - kActions) w = fminf(fmaxf(w, -2.0f), 0.5f);
+        if (!p.no_clamp && i >= p.count - kActions) w = fminf(fmaxf(w, -2.0f), 0.5f);
         p.params[i] = w;
     }
 }

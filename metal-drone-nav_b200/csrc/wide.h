@@ -65,6 +65,7 @@ struct WideAdamArgs {
     const float* partials;      // set by the launcher
     uint32_t partial_count;
     float* norm_out;            // pre-clip norm (optional)
+    uint32_t no_clamp;          // 1: no log-std clamp on the last four (a critic)
 };
 
 // Everything a rollout step needs to run the wide forward (host side).

@@ -39,7 +39,8 @@ RAPTOR = np.dtype([
     ("initial_hidden_state", "<f4", 16), ("output_weights", "<f4", 4 * 16), ("output_bias", "<f4", 4)])
 SHAPE = np.dtype([
     ("actor_obs_dim", "<u4"), ("critic_obs_dim", "<u4"), ("actor_hidden", "<u4"), ("critic_hidden", "<u4"),
-    ("flags", "<u4"), ("room_min", "<f4", 3), ("room_max", "<f4", 3)])
+    ("flags", "<u4"), ("room_min", "<f4", 3), ("room_max", "<f4", 3),
+    ("actor_layers", "<u4"), ("critic_layers", "<u4"), ("actor_activation", "<u4"), ("critic_activation", "<u4")])
 TASK_CONFIG = np.dtype([
     ("family", "<u4"), ("stage", "<u4"), ("objective", "<u4"), ("require_detour", "<u4"),
     ("max_generation_attempts", "<u4"), ("max_nav_steps", "<u4"), ("scene_distance_m", "<f4"),
@@ -67,7 +68,7 @@ CHECKPOINT_HEADER = np.dtype([
 
 assert STATE.itemsize == 68 and PARAMS.itemsize == 352 and OBSTACLE.itemsize == 40
 assert WORLD.itemsize == 676 and RUN.itemsize == 184 and CONFIG.itemsize == 84
-assert RAPTOR.itemsize == 8336 and SHAPE.itemsize == 44 and CHECKPOINT_HEADER.itemsize == 136
+assert RAPTOR.itemsize == 8336 and SHAPE.itemsize == 60 and CHECKPOINT_HEADER.itemsize == 136
 assert TASK_CONFIG.itemsize == 144 and TASK_CONTROL.itemsize == 148 and TASK_STATE.itemsize == 192
 
 # Buffer ids (mdn.h MDN_BUF_*) with their element dtype and per-row shape.

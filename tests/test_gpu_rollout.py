@@ -175,20 +175,40 @@ def test_teacher_forced_steps(pkg, om, raptor, extra):
         gpu.close()
 
 
-def test_collect_graph_equals_steps(pkg, raptor):
-    """collect() replays a captured CUDA graph; it must equal step-by-step launches."""
-    cfg = pkg.layouts.default_config(n=1000, family=1, speed=1.0, distance=4.0, seed=3)
-    a = pkg.Sim(pkg_device(), cfg, 16, raptor=raptor)
-    b = pkg.Sim(pkg_device(), cfg, 16, raptor=raptor)
+GRAPH_CASES = [(dict(n=1000, family=1, speed=1.0, distance=4.0, seed=3), 16),
+               # short episodes: resets inside the rollout, run by the next step's k_sense
+               # (odd horizon: the reset-list phase restarts with each collect)
+               (dict(n=777, family=18, speed=1.0, distance=3.0, seed=5, sensor_delay=2, command_delay=2,
+                     max_steps=5), 7),
+               (dict(n=300, family=13, speed=1.0, distance=3.0, seed=7, max_steps=4, risk_coef=0.5,
+                     depth_noise=0.05, wind=0.3), 8),
+               (dict(n=333, family=18, speed=1.0, distance=3.0, seed=9, eval=1, max_steps=3), 6),
+               # more listed resets per step than the sensing kernel has reset-worker warps
+               (dict(n=20000, family=18, speed=1.0, distance=3.0, seed=11, sensor_delay=2, command_delay=2,
+                     max_steps=3), 6)]
+
+
+@pytest.mark.parametrize("case", range(len(GRAPH_CASES)))
+def test_collect_graph_equals_steps(pkg, raptor, case):
+    """collect() replays a captured CUDA graph in which each step's ended
+    episodes are reset by the next step's sensing kernel (the last step
+    flushes them); it must equal step-by-step launches, over two replays."""
+    fields, T = GRAPH_CASES[case]
+    cfg = pkg.layouts.default_config(**fields)
+    a = pkg.Sim(pkg_device(), cfg, T, raptor=raptor)
+    b = pkg.Sim(pkg_device(), cfg, T, raptor=raptor)
     try:
-        a.collect()
-        for t in range(16):
-            b.step(t)
-        for name in STATE_KEYS + ("obs", "co", "actions", "logp", "values", "rewards", "next_values",
-                                  "terminated", "truncated", "contact_id"):
-            assert a.download(name).tobytes() == b.download(name).tobytes(), name
-        a.collect()  # second replay continues the episodes
-        assert a.download("runs")["steps"].max() > 16 or a.download("runs")["episodes"].sum() > 0
+        for rep in range(2):  # the second replay continues the episodes
+            a.collect()
+            for t in range(T):
+                b.step(t)
+            for name in STATE_KEYS + ("obs", "co", "actions", "logp", "values", "rewards", "next_values",
+                                      "terminated", "truncated", "contact_id"):
+                assert a.download(name).tobytes() == b.download(name).tobytes(), f"replay {rep}: {name}"
+        runs = a.download("runs")
+        assert runs["steps"].max() > T or runs["episodes"].sum() > 0
+        if fields.get("max_steps", 1000) < T and not fields.get("eval"):
+            assert runs["episodes"].sum() >= fields["n"], "episodes ended inside the rollout"
     finally:
         a.close()
         b.close()
