@@ -225,16 +225,26 @@ class Device:
 class Sim:
     """Batched environment, the reference Sim (main.mm:516-603)."""
 
-    def __init__(self, device, cfg, horizon, raptor=None, physics=None, room=None, actor_hidden=None):
+    ACTIVATIONS = {"tanh": 0, "gelu": 1}
+
+    def __init__(self, device, cfg, horizon, raptor=None, physics=None, room=None, actor_hidden=None,
+                 actor_layers=None, critic_hidden=None, critic_layers=None, actor_activation=None,
+                 critic_activation=None):
         """actor_hidden: None/64 for the reference's 12,104-parameter actor, or a
         multiple of 256 (5120 = the 967,688-parameter wide actor) evaluated on
-        the tensor cores."""
+        the tensor cores. actor_layers / critic_hidden / critic_layers /
+        actor_activation / critic_activation ("tanh" or "gelu"): layered
+        networks (no counterpart in the reference), e.g. a 4 x 480 GELU actor
+        with a 2 x 512 critic; any of them selects the layered path for both
+        networks."""
         self.device = device
         self.cfg = np.array(cfg, layouts.CONFIG)
         self.horizon = int(horizon)
         self.raptor = default_raptor() if raptor is None else np.array(raptor, layouts.RAPTOR)
+        layered = dict(actor_layers=actor_layers, critic_hidden=critic_hidden, critic_layers=critic_layers,
+                       actor_activation=actor_activation, critic_activation=critic_activation)
         shape = None
-        if room is not None or actor_hidden is not None:
+        if room is not None or actor_hidden is not None or any(v is not None for v in layered.values()):
             shape = np.zeros((), layouts.SHAPE)
             lib().mdn_rollout_shape_default(_ptr(shape))
             if room is not None:
@@ -243,6 +253,10 @@ class Sim:
                 shape["room_max"] = room[3:]
             if actor_hidden is not None:
                 shape["actor_hidden"] = int(actor_hidden)
+            for key, value in layered.items():
+                if value is None:
+                    continue
+                shape[key] = self.ACTIVATIONS[value] if key.endswith("activation") else int(value)
         self.actor_hidden = 64 if actor_hidden is None else int(actor_hidden)
         phys = None if physics is None else np.array(physics, layouts.PARAMS)
         self.h = _P()
@@ -252,6 +266,7 @@ class Sim:
         dims = [_U() for _ in range(4)]
         check(lib().mdn_sim_dims(self.h, *[ctypes.byref(d) for d in dims]))
         self.actor_params = int(dims[2].value)
+        self.critic_params = int(dims[3].value)
 
     def close(self):
         if self.h:
@@ -402,7 +417,7 @@ class PPOTrainer:
         check(lib().mdn_ppo_set_state(self.h, optimizer_step, completed_rollouts))
 
     def moments(self, which):
-        n = self.sim.actor_params if which < 2 else layouts.CRITIC_PARAMS
+        n = self.sim.actor_params if which < 2 else self.sim.critic_params
         out = np.zeros(n, np.float32)
         check(lib().mdn_ppo_moments(self.h, which, _ptr(out), n, 0))
         return out

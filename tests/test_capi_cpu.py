@@ -36,6 +36,22 @@ def test_layout_sizes(pkg):
             L.RAPTOR.itemsize, L.CHECKPOINT_HEADER.itemsize) == (68, 352, 676, 184, 84, 8336, 136)
 
 
+def test_rollout_shape_layout(pkg):
+    """mdn_rollout_shape_default writes exactly the 60-byte struct the Python
+    layout describes (guard bytes after it stay untouched); the layered fields
+    default to one tanh hidden layer."""
+    L = pkg.layouts
+    raw = np.full(L.SHAPE.itemsize + 16, 0xA5, np.uint8)
+    pkg.lib().mdn_rollout_shape_default(raw.ctypes.data_as(ctypes.c_void_p))
+    assert np.all(raw[L.SHAPE.itemsize:] == 0xA5)
+    shape = raw[:L.SHAPE.itemsize].view(L.SHAPE)[0]
+    assert (shape["actor_obs_dim"], shape["critic_obs_dim"], shape["actor_hidden"], shape["critic_hidden"]) == \
+        (184, 32, 64, 64)
+    assert (shape["actor_layers"], shape["critic_layers"], shape["actor_activation"], shape["critic_activation"]) == \
+        (0, 0, 0, 0)
+    assert list(shape["room_min"]) == [-2.0, -5.0, 0.0] and list(shape["room_max"]) == [14.0, 5.0, 5.0]
+
+
 def test_defaults_match_reference(pkg, olib, oracle_mod):
     L = pkg.layouts
     lib = pkg.lib()
