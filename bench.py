@@ -457,6 +457,76 @@ def measure_config1(pkg, dev):
             "ppo_update_ms": float(np.mean(u)), "ppo_update_ms_fp32_path": fp32_ms}
 
 
+def layered_flop_per_row(actor, critic):
+    """Forward multiply-add FLOPs of one row through both layered networks
+    (the update does about three times this: forward, deltas, weight gradients)."""
+    def net(inp, hidden, layers, out):
+        dims = [(inp if l == 0 else hidden, hidden) for l in range(layers)] + [(hidden, out)]
+        return sum(2 * i * o for i, o in dims)
+    return net(184, actor[0], actor[1], 4) + net(32, critic[0], critic[1], 1)
+
+
+def measure_layered(pkg, dev, label, n, T, epochs, minibatch, shape, cfg, fp32_peak, steps=2, tasks=None):
+    """One BASELINE configuration with layered networks (fp32 dense kernels):
+    one warm-up rollout + update, then `steps` timed ones (CUDA events)."""
+    sim = pkg.Sim(dev, cfg, T, **shape)
+    if tasks is not None:
+        sim.configure_tasks(tasks, 0.0)
+    tr = pkg.PPOTrainer(sim, epochs=epochs, minibatch=minibatch)
+    try:
+        sim.collect()
+        tr.rollout_update(0)
+        dev.finish()
+        c, u = [], []
+        for k in range(steps):
+            sim.collect()
+            c.append(sim.last_collect_ms())
+            tr.rollout_update(k + 1)
+            u.append(tr.last_update_ms())
+        dev.finish()
+    finally:
+        tr.close()
+        sim.close()
+    a = (shape.get("actor_hidden", 64), shape.get("actor_layers", 1))
+    cr = (shape.get("critic_hidden", 64), shape.get("critic_layers", 1))
+    fwd = layered_flop_per_row(a, cr)
+    # update work: forward + weight gradients + deltas (all but the first layer's)
+    first = 2 * 184 * a[0] + 2 * 32 * cr[0]
+    update_flop = (3 * fwd - first) * n * T * epochs
+    upd_s = float(np.mean(u)) * 1e-3
+    return {"config": label, "env_steps_per_s": n * T / (np.mean(c) * 1e-3), "rollout_ms": float(np.mean(c)),
+            "ppo_update_ms": float(np.mean(u)),
+            "ppo_compute_roofline": {"bound": "fp32", "achieved": update_flop / upd_s / 1e12, "peak": fp32_peak,
+                                     "unit": "TFLOP/s", "frac": update_flop / upd_s / 1e12 / fp32_peak,
+                                     "flop_per_row_epoch": 3 * fwd - first,
+                                     "peak_source": "measured (pure-FMA kernel, this run)"}}
+
+
+def measure_layered_configs(pkg, dev, fp32_peak):
+    """The network shapes BASELINE configs 0, 1 and 3 name (the reference has
+    only one-hidden-layer tanh networks; these run on the layered path)."""
+    L = pkg.layouts
+    out = {}
+    out["0"] = measure_layered(
+        pkg, dev, "BASELINE config 0 with its 2x64 tanh actor: 512 envs, family 17, T=64, PPO 2 epochs x 256-row "
+                  "chunks", 512, 64, 2, 256, dict(actor_hidden=64, actor_layers=2),
+        L.default_config(n=512, family=17, seed=0), fp32_peak, steps=3)
+    control = pkg.task_control(2, 1)
+    control["config"]["goal_distance_max_m"] = 20.0
+    out["1"] = measure_layered(
+        pkg, dev, "BASELINE config 1 with its 2x128 critic: 8,192 envs, goal-arrival tasks (goals 2-20 m), T=128, "
+                  "PPO 4 epochs x 8 minibatches, fp32", 8192, 128, 4, 8192 * 128 // 8,
+        dict(critic_hidden=128, critic_layers=2),
+        L.default_config(n=8192, family=1, mode=22, speed=1.5, distance=8.0, seed=7, max_steps=400), fp32_peak,
+        tasks=control)
+    out["3"] = measure_layered(
+        pkg, dev, "BASELINE config 3 with its 4x480 GELU actor and 2x512 critic: 16,384 envs, family 17, T=128, "
+                  "PPO 4 epochs x 16 minibatches, fp32 CUDA cores", 16384, 128, 4, 16384 * 128 // 16,
+        dict(actor_hidden=480, actor_layers=4, actor_activation="gelu", critic_hidden=512, critic_layers=2),
+        L.default_config(n=16384, family=17, seed=43), fp32_peak, steps=1)
+    return out
+
+
 def run_reference_arm(args, dist, out_fd):
     if dist.rank != 0:
         return 0
@@ -663,6 +733,7 @@ def main():
         line["wide_actor"] = measure_wide(pkg, dev, dist, args, peaks)
     if world == 1 and not args.no_secondary:
         line["baseline_configs"] = {"0": measure_config0(pkg, dev), "1": measure_config1(pkg, dev)}
+        line["layered_networks"] = measure_layered_configs(pkg, dev, fp32_peak)
     if world == 1 and dist.rank == 0 and not args.no_cpu_baseline:
         s = cpu_reference_sample(L, args.envs, 2, args.family, warmup=1, delay=args.delay)
         if s is not None:

@@ -80,8 +80,19 @@ struct mdn_ppo {
     float* lay_cta = nullptr;     // [loss CTAs][8]
     float* lay_grad = nullptr;    // [actor params + critic params]
     float* lay_norm = nullptr;    // [2 * SMs]
-    uint32_t lay_chunks = 1, lay_chunk_rows = 64, lay_loss_ctas = 1;
+    uint32_t lay_loss_ctas = 1;
 };
+
+namespace {
+// Row chunks of one layer's weight-gradient launch: enough CTAs (k tiles x
+// n tiles x chunks) for two per SM, chunks of at least 64 rows.
+void layer_chunks(uint32_t k, uint32_t n, uint32_t rows, uint32_t sms, uint32_t& chunks, uint32_t& chunk_rows) {
+    const uint32_t tiles = ((k + 1 + 63) / 64) * ((n + 63) / 64);
+    const uint32_t want = std::max<uint32_t>(1, (2 * sms + tiles - 1) / tiles);
+    chunk_rows = std::max<uint32_t>(64, ((rows + want - 1) / want + 15) / 16 * 16);
+    chunks = (rows + chunk_rows - 1) / chunk_rows;
+}
+}  // namespace
 
 namespace {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -147,9 +158,10 @@ void enqueue_layered_minibatch(mdn_ppo* t, uint32_t u, bool multi) {
             w.part = t->lay_part;
             w.k = net.in_dim(uint32_t(l));
             w.n = net.out_dim(uint32_t(l));
-            w.chunk_rows = t->lay_chunk_rows;
-            cuda_check(launch_dense_wgrad(w, R, t->lay_chunks, s), "layered weight gradient");
-            cuda_check(launch_chunk_sum(t->lay_part, t->lay_chunks, size_t(w.n) * w.k + w.n,
+            uint32_t chunks = 1;
+            layer_chunks(w.k, w.n, t->minibatch, uint32_t(dev->sm_count), chunks, w.chunk_rows);
+            cuda_check(launch_dense_wgrad(w, R, chunks, s), "layered weight gradient");
+            cuda_check(launch_chunk_sum(t->lay_part, chunks, size_t(w.n) * w.k + w.n,
                                         grad + net.weight_offset(uint32_t(l)), s),
                        "layered gradient sum");
             if (l == 0) break;
@@ -461,14 +473,15 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
             const MlpShape& C = sim->lay->critic;
             a.actor_b2 = A.bias_offset(A.layers);
             a.actor_log_std = A.param_count() - kActions;
-            // Weight-gradient chunks: about 24 runs of rows per minibatch.
-            t->lay_chunk_rows = std::max<uint32_t>(64, (t->minibatch / 24 + 15) / 16 * 16);
-            t->lay_chunks = (t->minibatch + t->lay_chunk_rows - 1) / t->lay_chunk_rows;
             t->lay_loss_ctas = layered_loss_ctas(t->minibatch);
-            size_t largest = 0;
+            size_t largest = 0;  // weight-gradient partials of the largest layer launch
             for (const MlpShape* net : {&A, &C})
-                for (uint32_t l = 0; l <= net->layers; l++)
-                    largest = std::max(largest, size_t(net->out_dim(l)) * net->in_dim(l) + net->out_dim(l));
+                for (uint32_t l = 0; l <= net->layers; l++) {
+                    uint32_t chunks = 1, chunk_rows = 64;
+                    layer_chunks(net->in_dim(l), net->out_dim(l), t->minibatch, sms, chunks, chunk_rows);
+                    largest = std::max(largest, size_t(chunks) * (size_t(net->out_dim(l)) * net->in_dim(l) +
+                                                                   net->out_dim(l)));
+                }
             const size_t widest = std::max(A.hidden, C.hidden);
             size_t loff = 0;
             auto lcarve = [&](size_t bytes) { const size_t o = loff; loff += align256(bytes); return o; };
@@ -483,7 +496,7 @@ extern "C" int mdn_ppo_create(mdn_sim* sim, uint32_t epochs, uint32_t minibatch_
             }
             const size_t l_oa = lcarve(mb * 16), l_oc = lcarve(mb * 4), l_da = lcarve(mb * 16), l_dc = lcarve(mb * 4),
                          l_d0 = lcarve(mb * widest * 4), l_d1 = lcarve(mb * widest * 4),
-                         l_part = lcarve(size_t(t->lay_chunks) * largest * 4),
+                         l_part = lcarve(largest * 4),
                          l_cta = lcarve(size_t(t->lay_loss_ctas) * 8 * 4), l_g = lcarve((AP + CP) * 4),
                          l_n = lcarve(size_t(sms) * 2 * 4);
             const cudaError_t le = cudaMalloc(&t->lay_mem, loff);

@@ -8,7 +8,8 @@ one PPO update whose gradients and advantage statistics are allreduced by
 libmdn over NCCL, and saves its buffers to <outdir>/rank<r>.npz for the parent
 test to compare with a one-GPU run of all environments.
 
-  argv: outdir envs_per_rank horizon epochs minibatch_time_steps tensor_cores(0|1)
+  argv: outdir envs_per_rank horizon epochs minibatch_time_steps mode
+  mode: 0 fp32 update, 1 tensor-core update, 2 layered networks (LAYERED)
 """
 import datetime
 import os
@@ -24,13 +25,21 @@ SAVE = ("obs", "co", "actions", "logp", "values", "rewards", "next_values", "ter
         "advantages", "returns", "actor", "critic", "states", "sensors")
 
 
+# BASELINE config 0's 2 x 64 actor with config 1's 2 x 128 critic
+LAYERED = dict(actor_hidden=64, actor_layers=2, critic_hidden=128, critic_layers=2)
+
+
+def shape(mode):
+    return LAYERED if mode == 2 else {}
+
+
 def config(pkg, n):
     return pkg.layouts.default_config(n=n, family=18, seed=7, sensor_delay=2, command_delay=2, max_steps=10)
 
 
 def main():
     outdir = pathlib.Path(sys.argv[1])
-    n, horizon, epochs, mb_steps, tensor_cores = (int(x) for x in sys.argv[2:7])
+    n, horizon, epochs, mb_steps, mode = (int(x) for x in sys.argv[2:7])
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -41,9 +50,10 @@ def main():
     obj = [pkg.Device.comm_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(obj, src=0)
     dev.comm_init(rank, world, obj[0])
-    sim = pkg.Sim(dev, config(pkg, n), horizon)
+    sim = pkg.Sim(dev, config(pkg, n), horizon, **shape(mode))
     tr = pkg.PPOTrainer(sim, epochs=epochs, minibatch=mb_steps * n)
-    tr.set_tensor_cores(bool(tensor_cores))
+    if mode == 1:
+        tr.set_tensor_cores(True)
     sim.collect()
     tr.rollout_update(0)
     dev.finish()

@@ -18,9 +18,10 @@ rows and the same 1/B loss scale:
   gradient sums add the same rows in another order), except parameters whose
   accumulated gradient is at rounding level, bounded by 2*lr per update.
 
-Both update paths run: the fp32 kernel and the tensor-core kernel (whose
-TMA loads read only this GPU's own memory). Needs two GPUs; NVLS is off
-(NCCL_NVLS_ENABLE=0).
+Three update paths run: the fp32 kernel, the tensor-core kernel (whose
+TMA loads read only this GPU's own memory) and the layered networks (a 2 x 64
+actor and a 2 x 128 critic, whose flat gradient is allreduced the same way).
+Needs two GPUs; NVLS is off (NCCL_NVLS_ENABLE=0).
 """
 import os
 import pathlib
@@ -53,13 +54,13 @@ def gpu_count():
 
 
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("tensor_cores", [False, True], ids=["fp32_update", "tensor_core_update"])
-def test_two_ranks_equal_one_gpu(tmp_path, tensor_cores):
+@pytest.mark.parametrize("mode", [0, 1, 2], ids=["fp32_update", "tensor_core_update", "layered_update"])
+def test_two_ranks_equal_one_gpu(tmp_path, mode):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={WORLD}", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
            str(ROOT / "tests" / "multirank_gpu_worker.py"), str(tmp_path), str(N_RANK), str(HORIZON), str(EPOCHS),
-           str(MB_STEPS), str(int(tensor_cores))]
+           str(MB_STEPS), str(mode)]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     ranks = [np.load(tmp_path / f"rank{k}.npz") for k in range(WORLD)]
@@ -69,9 +70,10 @@ def test_two_ranks_equal_one_gpu(tmp_path, tensor_cores):
     pkg = load_package()
     dev = pkg.Device(0)
     n = N_RANK * WORLD
-    sim = pkg.Sim(dev, worker.config(pkg, n), HORIZON)
+    sim = pkg.Sim(dev, worker.config(pkg, n), HORIZON, **worker.shape(mode))
     tr = pkg.PPOTrainer(sim, epochs=EPOCHS, minibatch=MB_STEPS * n)
-    tr.set_tensor_cores(tensor_cores)
+    if mode == 1:
+        tr.set_tensor_cores(True)
     try:
         sim.collect()
         U = EPOCHS * (HORIZON // MB_STEPS)
