@@ -3,7 +3,8 @@
 // activation derivative fused, chunked weight-gradient partials summed in a
 // fixed order (results are deterministic run to run), and the clipped-PPO loss
 // of these networks. Register-tiled products: a 256-thread CTA computes a
-// 64 x 64 output tile, 4 x 4 per thread, from 16-deep shared-memory slices.
+// 128 x 64 output tile, 8 x 4 per thread, from 16-deep shared-memory slices,
+// the next slice loaded into registers while the current one is multiplied.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -23,7 +24,7 @@ uint32_t MlpShape::param_count() const { return weight_offset(layers + 1) + (log
 
 namespace {
 
-constexpr int kTM = 64, kTN = 64, kTK = 16, kDenseThreads = 256, kPad = 4;
+constexpr int kBM = 128, kBN = 64, kBK = 16, kDenseThreads = 256, kPad = 4;
 constexpr int kLossThreads = 256;
 
 __device__ __forceinline__ void resolve(const DenseRows& r, uint32_t& rows, uint32_t& row0) {
@@ -49,55 +50,109 @@ __device__ __forceinline__ float act_grad(int act, float z) {
     return 1.0f;
 }
 
-// 16-deep slice of the 4 x 4 register tile: acc[i][j] += a[i] * b[j], with the
-// operands as [k][m] and [k][n] slices in shared memory.
-__device__ __forceinline__ void tile_fma(const float (*as)[kTM + kPad], const float (*bs)[kTN + kPad], int ty, int tx,
-                                         float (&acc)[4][4]) {
+// One 128 x 64 output tile of C = A B over the reduction dimension kdim, by a
+// 256-thread CTA: thread (ty, tx) = (tid / 16, tid % 16) accumulates rows
+// 8 ty .. 8 ty + 7 and columns 4 tx .. 4 tx + 3, each sum in reduction order.
+// A(k, m) and B(k, n) come from the loaders `ga` / `gb` (which return 0 out
+// of bounds); A_KMAJOR / B_KMAJOR say which index is contiguous in memory, so
+// that consecutive threads load consecutive addresses. The next 16-deep
+// slice is loaded into registers while the current one is multiplied from
+// shared memory (two shared buffers, one barrier per slice).
+template <bool A_KMAJOR, bool B_KMAJOR, typename GA, typename GB>
+__device__ __forceinline__ void gemm_tile(uint32_t kdim, GA ga, GB gb, float (&acc)[8][4]) {
+    __shared__ __align__(16) float as[2][kBK][kBM + kPad];
+    __shared__ __align__(16) float bs[2][kBK][kBN + kPad];
+    const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
+    float ra[8], rb[4];
+    auto a_index = [&](int j, int& kk, int& mm) {
+        const int e = tid + kDenseThreads * j;
+        kk = A_KMAJOR ? e % kBK : e / kBM;
+        mm = A_KMAJOR ? e / kBK : e % kBM;
+    };
+    auto b_index = [&](int j, int& kk, int& nn) {
+        const int e = tid + kDenseThreads * j;
+        kk = B_KMAJOR ? e % kBK : e / kBN;
+        nn = B_KMAJOR ? e / kBK : e % kBN;
+    };
+    auto load = [&](uint32_t k0) {
 #pragma unroll
-    for (int kk = 0; kk < kTK; kk++) {
-        const float4 a = *reinterpret_cast<const float4*>(&as[kk][ty * 4]);
-        const float4 b = *reinterpret_cast<const float4*>(&bs[kk][tx * 4]);
-        const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+        for (int j = 0; j < 8; j++) {
+            int kk, mm;
+            a_index(j, kk, mm);
+            ra[j] = ga(k0 + kk, mm);
+        }
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int j = 0; j < 4; j++) {
+            int kk, nn;
+            b_index(j, kk, nn);
+            rb[j] = gb(k0 + kk, nn);
+        }
+    };
+    auto store = [&](int buf) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < 8; j++) {
+            int kk, mm;
+            a_index(j, kk, mm);
+            as[buf][kk][mm] = ra[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int kk, nn;
+            b_index(j, kk, nn);
+            bs[buf][kk][nn] = rb[j];
+        }
+    };
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+    load(0);
+    store(0);
+    __syncthreads();
+    int buf = 0;
+    for (uint32_t k0 = 0; k0 < kdim; k0 += kBK) {
+        const bool more = k0 + kBK < kdim;
+        if (more) load(k0 + kBK);
+#pragma unroll
+        for (int kk = 0; kk < kBK; kk++) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&as[buf][kk][ty * 8]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&as[buf][kk][ty * 8 + 4]);
+            const float4 b = *reinterpret_cast<const float4*>(&bs[buf][kk][tx * 4]);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        if (more) store(buf ^ 1);
+        __syncthreads();
+        buf ^= 1;
     }
 }
 
 __global__ void __launch_bounds__(kDenseThreads) k_dense_fwd(DenseFwd p, DenseRows r, int x_row0) {
-    __shared__ __align__(16) float xs[kTK][kTM + kPad];
-    __shared__ __align__(16) float ws[kTK][kTN + kPad];
     uint32_t rows, row0;
     resolve(r, rows, row0);
-    const uint32_t m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
+    const uint32_t m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
     if (m0 >= rows) return;  // CTA-uniform
     const float* x = p.x + (x_row0 ? size_t(row0) * p.k : 0);
-    const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
-    float acc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
-    for (uint32_t k0 = 0; k0 < p.k; k0 += kTK) {
-        for (int e = tid; e < kTM * kTK; e += kDenseThreads) {
-            const int mm = e / kTK, kk = e % kTK;
-            const uint32_t m = m0 + mm, k = k0 + kk;
-            xs[kk][mm] = (m < rows && k < p.k) ? x[size_t(m) * p.k + k] : 0.0f;
-        }
-        for (int e = tid; e < kTN * kTK; e += kDenseThreads) {
-            const int nn = e / kTK, kk = e % kTK;
-            const uint32_t n = n0 + nn, k = k0 + kk;
-            ws[kk][nn] = (n < p.n && k < p.k) ? p.w[size_t(n) * p.k + k] : 0.0f;
-        }
-        __syncthreads();
-        tile_fma(xs, ws, ty, tx, acc);
-        __syncthreads();
-    }
+    float acc[8][4];
+    gemm_tile<true, true>(
+        p.k,
+        [&](uint32_t k, int mm) {
+            const uint32_t m = m0 + mm;
+            return (m < rows && k < p.k) ? x[size_t(m) * p.k + k] : 0.0f;
+        },
+        [&](uint32_t k, int nn) {
+            const uint32_t n = n0 + nn;
+            return (n < p.n && k < p.k) ? p.w[size_t(n) * p.k + k] : 0.0f;
+        },
+        acc);
     // Dot from zero in k order, then the bias, then the activation.
+    const int ty = threadIdx.x / 16, tx = threadIdx.x % 16;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const uint32_t m = m0 + ty * 4 + i;
+    for (int i = 0; i < 8; i++) {
+        const uint32_t m = m0 + ty * 8 + i;
         if (m >= rows) continue;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
@@ -111,36 +166,26 @@ __global__ void __launch_bounds__(kDenseThreads) k_dense_fwd(DenseFwd p, DenseRo
 }
 
 __global__ void __launch_bounds__(kDenseThreads) k_dense_bwd(DenseBwd p, DenseRows r) {
-    __shared__ __align__(16) float ds[kTK][kTM + kPad];  // [n][m]
-    __shared__ __align__(16) float ws[kTK][kTN + kPad];  // [n][k]
     uint32_t rows, row0;
     resolve(r, rows, row0);
-    const uint32_t m0 = blockIdx.y * kTM, c0 = blockIdx.x * kTN;  // output rows, output columns (k)
+    const uint32_t m0 = blockIdx.y * kBM, c0 = blockIdx.x * kBN;  // output rows, output columns (k)
     if (m0 >= rows) return;
-    const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
-    float acc[4][4];
+    float acc[8][4];
+    gemm_tile<true, false>(
+        p.n,
+        [&](uint32_t n, int mm) {
+            const uint32_t m = m0 + mm;
+            return (m < rows && n < p.n) ? p.dy[size_t(m) * p.n + n] : 0.0f;
+        },
+        [&](uint32_t n, int cc) {
+            const uint32_t c = c0 + cc;
+            return (n < p.n && c < p.k) ? p.w[size_t(n) * p.k + c] : 0.0f;
+        },
+        acc);
+    const int ty = threadIdx.x / 16, tx = threadIdx.x % 16;
 #pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
-    for (uint32_t n0 = 0; n0 < p.n; n0 += kTK) {
-        for (int e = tid; e < kTM * kTK; e += kDenseThreads) {
-            const int mm = e / kTK, nn = e % kTK;
-            const uint32_t m = m0 + mm, n = n0 + nn;
-            ds[nn][mm] = (m < rows && n < p.n) ? p.dy[size_t(m) * p.n + n] : 0.0f;
-        }
-        for (int e = tid; e < kTN * kTK; e += kDenseThreads) {
-            const int nn = e / kTN, cc = e % kTN;
-            const uint32_t n = n0 + nn, c = c0 + cc;
-            ws[nn][cc] = (n < p.n && c < p.k) ? p.w[size_t(n) * p.k + c] : 0.0f;
-        }
-        __syncthreads();
-        tile_fma(ds, ws, ty, tx, acc);
-        __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const uint32_t m = m0 + ty * 4 + i;
+    for (int i = 0; i < 8; i++) {
+        const uint32_t m = m0 + ty * 8 + i;
         if (m >= rows) continue;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
@@ -152,43 +197,33 @@ __global__ void __launch_bounds__(kDenseThreads) k_dense_bwd(DenseBwd p, DenseRo
     }
 }
 
-// CTA (k tile, n tile, chunk): rows of the chunk in order, 16 at a time. The
-// input column k == K stands for the bias (X = 1).
+// CTA (k tile, n tile, chunk): the chunk's rows in order. The input column
+// k == K stands for the bias (X = 1).
 __global__ void __launch_bounds__(kDenseThreads) k_dense_wgrad(DenseWgrad p, DenseRows r) {
-    __shared__ __align__(16) float ds[kTK][kTM + kPad];  // [m][n]
-    __shared__ __align__(16) float xs[kTK][kTN + kPad];  // [m][k]
     uint32_t rows, row0;
     resolve(r, rows, row0);
-    const uint32_t k0 = blockIdx.x * kTN, n0 = blockIdx.y * kTM, c = blockIdx.z;
+    const uint32_t k0 = blockIdx.x * kBN, n0 = blockIdx.y * kBM, c = blockIdx.z;
     const uint32_t lo = c * p.chunk_rows, hi = lo + p.chunk_rows < rows ? lo + p.chunk_rows : rows;
     const float* x = p.x + (p.x_row0 ? size_t(row0) * p.k : 0);
-    const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
-    float acc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
-    for (uint32_t mb = lo; mb < hi; mb += kTK) {
-        for (int e = tid; e < kTM * kTK; e += kDenseThreads) {
-            const int mm = e / kTM, nn = e % kTM;
-            const uint32_t m = mb + mm, n = n0 + nn;
-            ds[mm][nn] = (m < hi && n < p.n) ? p.dy[size_t(m) * p.n + n] : 0.0f;
-        }
-        for (int e = tid; e < kTN * kTK; e += kDenseThreads) {
-            const int mm = e / kTN, kk = e % kTN;
-            const uint32_t m = mb + mm, k = k0 + kk;
-            float v = 0.0f;
-            if (m < hi) v = k < p.k ? x[size_t(m) * p.k + k] : (k == p.k ? 1.0f : 0.0f);
-            xs[mm][kk] = v;
-        }
-        __syncthreads();
-        tile_fma(ds, xs, ty, tx, acc);
-        __syncthreads();
-    }
+    float acc[8][4];
+    const uint32_t span = hi > lo ? hi - lo : 0;
+    gemm_tile<false, false>(
+        span,
+        [&](uint32_t dm, int nn) {
+            const uint32_t m = lo + dm, n = n0 + nn;
+            return (dm < span && n < p.n) ? p.dy[size_t(m) * p.n + n] : 0.0f;
+        },
+        [&](uint32_t dm, int kk) {
+            const uint32_t m = lo + dm, k = k0 + kk;
+            if (dm >= span) return 0.0f;
+            return k < p.k ? x[size_t(m) * p.k + k] : (k == p.k ? 1.0f : 0.0f);
+        },
+        acc);
     float* out = p.part + size_t(c) * (size_t(p.n) * p.k + p.n);
+    const int ty = threadIdx.x / 16, tx = threadIdx.x % 16;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const uint32_t n = n0 + ty * 4 + i;
+    for (int i = 0; i < 8; i++) {
+        const uint32_t n = n0 + ty * 8 + i;
         if (n >= p.n) continue;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
@@ -307,17 +342,17 @@ inline unsigned cdiv(size_t a, size_t b) { return unsigned((a + b - 1) / b); }
 }  // namespace
 
 cudaError_t launch_dense_fwd(const DenseFwd& p, const DenseRows& r, bool x_row0, cudaStream_t s) {
-    const dim3 grid(cdiv(p.n, kTN), cdiv(r.rows, kTM));
+    const dim3 grid(cdiv(p.n, kBN), cdiv(r.rows, kBM));
     k_dense_fwd<<<grid, kDenseThreads, 0, s>>>(p, r, x_row0 ? 1 : 0);
     return cudaGetLastError();
 }
 cudaError_t launch_dense_bwd(const DenseBwd& p, const DenseRows& r, cudaStream_t s) {
-    const dim3 grid(cdiv(p.k, kTN), cdiv(r.rows, kTM));
+    const dim3 grid(cdiv(p.k, kBN), cdiv(r.rows, kBM));
     k_dense_bwd<<<grid, kDenseThreads, 0, s>>>(p, r);
     return cudaGetLastError();
 }
 cudaError_t launch_dense_wgrad(const DenseWgrad& p, const DenseRows& r, uint32_t chunks, cudaStream_t s) {
-    const dim3 grid(cdiv(size_t(p.k) + 1, kTN), cdiv(p.n, kTM), chunks);
+    const dim3 grid(cdiv(size_t(p.k) + 1, kBN), cdiv(p.n, kBM), chunks);
     k_dense_wgrad<<<grid, kDenseThreads, 0, s>>>(p, r);
     return cudaGetLastError();
 }

@@ -87,7 +87,7 @@ namespace {
 // Row chunks of one layer's weight-gradient launch: enough CTAs (k tiles x
 // n tiles x chunks) for two per SM, chunks of at least 64 rows.
 void layer_chunks(uint32_t k, uint32_t n, uint32_t rows, uint32_t sms, uint32_t& chunks, uint32_t& chunk_rows) {
-    const uint32_t tiles = ((k + 1 + 63) / 64) * ((n + 63) / 64);
+    const uint32_t tiles = ((k + 1 + 63) / 64) * ((n + 127) / 128);  // k_dense_wgrad tiles: 128 units x 64 inputs
     const uint32_t want = std::max<uint32_t>(1, (2 * sms + tiles - 1) / tiles);
     chunk_rows = std::max<uint32_t>(64, ((rows + want - 1) / want + 15) / 16 * 16);
     chunks = (rows + chunk_rows - 1) / chunk_rows;
