@@ -482,6 +482,12 @@ int mdn_policy_write(const char* path, const float* actor, uint32_t hidden, cons
                      float max_speed_mps);
 /* The same for the simulator's current actor (downloaded from the device). */
 int mdn_sim_export_policy(mdn_sim* sim, const char* path, const char* source_checkpoint, float max_speed_mps);
+/* NavigationPolicy::raw_mean (deployment.hpp; the deployment probe of
+ * main.mm:1017-1042) batched on the GPU: the means of the simulator's current
+ * actor for `rows` observation rows (host [rows][184] in, host [rows][4] out:
+ * the output layer, its bias, then the geometry prior on means 0..2). fp32
+ * dense kernels, any actor shape. Allocates its own device scratch. */
+int mdn_sim_actor_means(mdn_sim* sim, const float* obs, uint32_t rows, float* means);
 
 /* ---- frozen challenge banks (challenge_evaluation.hpp, challenge_training.hpp) */
 /* SHA-256 of a file as 64 lowercase hex digits + NUL (challenge_evaluation::

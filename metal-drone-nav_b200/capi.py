@@ -63,6 +63,7 @@ SIGNATURES = {
     "mdn_sim_validate_tasks": (ctypes.c_int, [_P]),
     "mdn_sim_last_collect_ms": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float)]),
     "mdn_sim_profile_step": (ctypes.c_int, [_P, _U, _P]),
+    "mdn_sim_actor_means": (ctypes.c_int, [_P, _P, _U, _P]),
     "mdn_launch_counts": (ctypes.c_int, [_P, _P, ctypes.POINTER(_U), ctypes.POINTER(_U)]),
     "mdn_policy_write": (ctypes.c_int, [ctypes.c_char_p, _P, _U, ctypes.c_char_p, ctypes.c_float]),
     "mdn_sim_export_policy": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_float]),
@@ -291,6 +292,14 @@ class Sim:
         ms = ctypes.c_float()
         check(lib().mdn_sim_last_collect_ms(self.h, ctypes.byref(ms)))
         return ms.value
+
+    def actor_means(self, obs):
+        """The current actor's means for observation rows [rows][184] (the
+        deployment inference, on the GPU)."""
+        x = np.ascontiguousarray(obs, np.float32).reshape(-1, 184)
+        out = np.zeros((x.shape[0], 4), np.float32)
+        check(lib().mdn_sim_actor_means(self.h, _ptr(x), x.shape[0], _ptr(out)))
+        return out
 
     def profile_step(self, tick):
         """Device ms of (sense, act, advance) for one policy step (CUDA events)."""

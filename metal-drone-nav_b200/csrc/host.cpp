@@ -838,6 +838,45 @@ extern "C" int mdn_sim_dims(mdn_sim* sim, uint32_t* n, uint32_t* horizon, uint32
     });
 }
 
+extern "C" int mdn_sim_actor_means(mdn_sim* sim, const float* obs, uint32_t rows, float* means) {
+    return guarded([&] {
+        checked(sim);
+        require(obs != nullptr && means != nullptr && rows > 0, MDN_ERR_INVALID, "actor means: bad argument");
+        MlpShape net;
+        if (sim->layered) {
+            net = sim->lay->actor;
+        } else {
+            net.in = kActorObs;
+            net.hidden = sim->actor_hidden;
+            net.layers = 1;
+            net.out = kActions;
+            net.activation = kActTanh;
+            net.log_std = true;
+        }
+        const size_t x_floats = size_t(rows) * kActorObs, h_floats = size_t(rows) * net.hidden;
+        float* mem = nullptr;
+        const cudaError_t e = cudaMalloc(&mem, (x_floats + 2 * h_floats + size_t(rows) * kActions) * sizeof(float));
+        require(e == cudaSuccess, MDN_ERR_NOMEM, std::string("actor means: cudaMalloc failed: ") + cudaGetErrorString(e));
+        struct Free {
+            float* p;
+            ~Free() { cudaFree(p); }
+        } guard{mem};
+        float* out = mem + x_floats + 2 * h_floats;
+        cuda_check(cudaMemcpyAsync(mem, obs, x_floats * sizeof(float), cudaMemcpyHostToDevice, sim->stream),
+                   "actor means: upload");
+        cuda_check(launch_network_forward(net, static_cast<const float*>(sim->buf[MDN_BUF_ACTOR]), mem, rows,
+                                          mem + x_floats, mem + x_floats + h_floats, out, true, sim->stream),
+                   "actor means: forward");
+        cuda_check(cudaMemcpyAsync(means, out, size_t(rows) * kActions * sizeof(float), cudaMemcpyDeviceToHost,
+                                   sim->stream),
+                   "actor means: download");
+        sync_stream(sim->dev, sim->stream, "actor means");
+        // The geometry prior (ppo.hpp:77) after the output layer and its bias.
+        for (uint32_t r = 0; r < rows; r++)
+            for (int a = 0; a < 3; a++) means[size_t(r) * kActions + a] += obs[size_t(r) * kActorObs + kActorObs - 3 + a];
+    });
+}
+
 extern "C" int mdn_sim_profile_step(mdn_sim* sim, uint32_t tick, float ms[3]) {
     return guarded([&] {
         checked(sim);

@@ -403,6 +403,12 @@ cudaError_t network_forward(const MlpShape& net, const float* params, const floa
 }
 }  // namespace
 
+cudaError_t launch_network_forward(const MlpShape& net, const float* params, const float* x, uint32_t rows,
+                                   float* act0, float* act1, float* out, bool out_bias, cudaStream_t s) {
+    float* const act[2] = {act0, act1};
+    return network_forward(net, params, x, rows, 0, act, out, out_bias, s);
+}
+
 cudaError_t launch_layered_step_forward(const LayeredStep& L, uint32_t n, uint32_t tick, cudaStream_t s) {
     const cudaError_t e = network_forward(L.actor, L.actor_params, L.obs, n, tick * n, L.act, L.out_a, false, s);
     if (e != cudaSuccess) return e;

@@ -124,6 +124,12 @@ cudaError_t launch_layered_step_forward(const LayeredStep& L, uint32_t n, uint32
 // Critic over next_co into next_values[tick * n ...] (sim.metal:327's bootstrap value).
 cudaError_t launch_layered_bootstrap(const LayeredStep& L, uint32_t n, uint32_t tick, cudaStream_t s);
 
+// A network's forward over `rows` rows of x (device memory, from row 0):
+// hidden activations alternate between act0 and act1 ([rows][hidden] each),
+// the output layer writes out [rows][net.out] (with its bias when out_bias).
+cudaError_t launch_network_forward(const MlpShape& net, const float* params, const float* x, uint32_t rows,
+                                   float* act0, float* act1, float* out, bool out_bias, cudaStream_t s);
+
 // Initial parameters: the seed-1789 Box-Muller stream of main.mm:548-555,
 // actor first, then critic, layer by layer: the first layer's weights at the
 // reference's first-layer scale (0.04 actor, 0.15 critic), hidden-to-hidden

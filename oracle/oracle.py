@@ -128,6 +128,7 @@ def load_ref_deploy():
     d("refd_write_navpol", ctypes.c_int, ctypes.c_char_p, _P, _F, ctypes.c_char_p)
     d("refd_load_navpol", ctypes.c_int, ctypes.c_char_p, _P, _P, _P)
     d("refd_wide_eval", _U, ctypes.c_char_p, _P, _U, _P, _P, _P)
+    d("refd_navpol_eval", ctypes.c_int, ctypes.c_char_p, _P, _U, _P)
     return lib
 
 

@@ -54,4 +54,15 @@ uint32_t refd_wide_eval(const char* path, const float* obs, uint32_t rows, float
     return p.metadata().hidden_count_value;
 }
 
+// Load a NAVPOL1 file and evaluate NavigationPolicy::raw_mean on `rows`
+// observations (deployment.hpp), as the reference's deployment probe does
+// (main.mm:1017-1042). Returns 1, or 0 when the file or a row is rejected.
+int refd_navpol_eval(const char* path, const float* obs, uint32_t rows, float* mean_out) {
+    auto p = std::make_unique<nav_deployment::NavigationPolicy>();
+    if (!p->load(path)) return 0;
+    for (uint32_t r = 0; r < rows; r++)
+        if (!p->raw_mean(obs + size_t(r) * 184, mean_out + size_t(r) * 4)) return 0;
+    return 1;
+}
+
 }  // extern "C"

@@ -17,6 +17,10 @@ replay, and the frozen RAPTOR controller the product ships as runtime data:
   ref_ckpt_v8_local_waypoint.bin  PPOFIX1 v8 checkpoint with the runtime and
                task blocks (assets/checkpoints/local-waypoint-fast-experimental
                .bin.best): 128 envs, mode 22, goal-arrival tasks
+  ref_navpol_rooms.bin  a NAVPOL1 deployment file the reference exported from
+               its own training (assets/navigation-rooms-experimental.bin;
+               format deployment.hpp:41-88): trained actor weights for the
+               deployment probe (main.mm:1001-1042)
 Then writes ref_trace.npz: a short teacher-forced trace of the reference's own
 CPU path (oracle/_ref, compiled unmodified), used by GPU tests on machines
 without the reference sources.
@@ -59,6 +63,7 @@ def reference_root(ref_root=None):
 def main(ref_root=None):
     ref = reference_root(ref_root)
     copy_checkpoints(ref)
+    shutil.copyfile(ref / "assets" / "navigation-rooms-experimental.bin", HERE / "ref_navpol_rooms.bin")
     shutil.copyfile(ref / "assets" / "raptor.bin", HERE / "raptor.bin")
     shutil.copyfile(ref / "assets" / "physics.bin", HERE / "physics.bin")
     (ROOT / "metal-drone-nav_b200" / "assets").mkdir(parents=True, exist_ok=True)

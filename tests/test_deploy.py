@@ -126,3 +126,87 @@ def test_export_after_update(dlib, tmp_path, source, hidden):
         tr.close()
         sim.close()
         dev.close()
+
+
+# ----------------------------------------------------- deployment probe
+# The reference checks a deployed policy on eight probe observations
+# (main.mm:1001-1042): NavigationPolicy::raw_mean of the exported file must
+# equal the fixed PPO actor within 2e-5. Replayed here on the reference's own
+# exported policy (tests/golden/ref_navpol_rooms.bin, trained weights).
+PROBE_GATE = 2e-5
+
+
+def probe_observation(sample):
+    """deployment_probe_observation (main.mm:1001-1015)."""
+    obs = np.zeros(184, np.float32)
+    for i in range(160):
+        obs[i] = np.float32(0.20) + np.float32(0.01) * np.float32((i * 13 + sample * 7) % 70)
+    c = 160
+    angle = np.float32(-0.7) + np.float32(0.2) * np.float32(sample)
+    obs[c + 0] = np.cos(angle)
+    obs[c + 1] = np.sin(angle)
+    obs[c + 2] = 0.1
+    obs[c + 3] = np.float32(0.3) + np.float32(0.04) * np.float32(sample)
+    obs[c + 4:c + 21] = (0.1, -0.05, 0.02, 0.01, -0.02, 0.03, 0.0, 0.0, 1.0, 0.05, -0.03, 0.0, 0.02, 0.01, 0.02,
+                         -0.01, 0.0)
+    obs[181:184] = (0.08, -0.04, 0.02)
+    return obs
+
+
+def golden_policy():
+    from conftest import GOLDEN
+    path = GOLDEN / "ref_navpol_rooms.bin"
+    raw = path.read_bytes()
+    assert raw[:8] == b"NAVPOL1\x00"
+    header = np.frombuffer(raw, "<u4", 6, 8)
+    assert tuple(header) == (1, 184, 64, 4, 17, 12104)
+    return path, np.frombuffer(raw, np.float32, 12104, 64).copy()
+
+
+def f64_means(actor, obs):
+    w1 = actor[:64 * 184].reshape(64, 184).astype(np.float64)
+    b1 = actor[64 * 184:64 * 185].astype(np.float64)
+    w2 = actor[64 * 185:64 * 189].reshape(4, 64).astype(np.float64)
+    b2 = actor[64 * 189:64 * 189 + 4].astype(np.float64)
+    m = np.tanh(obs.astype(np.float64) @ w1.T + b1) @ w2.T + b2
+    m[:, :3] += obs[:, 181:184]
+    return m
+
+
+def test_reference_policy_probe_cpu(dlib):
+    """The reference's reader on its own exported policy against a float64
+    forward of the same weights (the probe's own gate)."""
+    path, actor = golden_policy()
+    obs = np.stack([probe_observation(s) for s in range(8)])
+    got = np.zeros((8, 4), np.float32)
+    assert dlib.refd_navpol_eval(str(path).encode(), obs.ctypes.data_as(ctypes.c_void_p), 8,
+                                 got.ctypes.data_as(ctypes.c_void_p)) == 1
+    assert np.max(np.abs(got - f64_means(actor, obs))) < PROBE_GATE
+
+
+@pytest.mark.gpu
+def test_reference_policy_probe_gpu():
+    """The reference's trained policy uploaded into a simulator, evaluated on
+    the GPU (mdn_sim_actor_means) on the probe observations: within the
+    probe's 2e-5 of the float64 forward and of the reference's own reader."""
+    pkg = load_package()
+    path, actor = golden_policy()
+    obs = np.stack([probe_observation(s) for s in range(8)])
+    dev = pkg.Device(0)
+    sim = pkg.Sim(dev, pkg.layouts.default_config(n=16, family=1), 2)
+    try:
+        sim.upload("actor", actor)
+        got = sim.actor_means(obs)
+        assert np.max(np.abs(got - f64_means(actor, obs))) < PROBE_GATE
+        lib = load_oracle_module().load_ref_deploy()
+        if lib is not None:
+            ref = np.zeros((8, 4), np.float32)
+            assert lib.refd_navpol_eval(str(path).encode(), obs.ctypes.data_as(ctypes.c_void_p), 8,
+                                        ref.ctypes.data_as(ctypes.c_void_p)) == 1
+            assert np.max(np.abs(got - ref)) < PROBE_GATE
+        # a trained actor also drives a rollout without non-finite values
+        sim.collect()
+        assert np.isfinite(sim.download("actions")).all()
+    finally:
+        sim.close()
+        dev.close()

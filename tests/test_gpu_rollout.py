@@ -385,3 +385,53 @@ def test_delay_rehearsal_teacher_forced(pkg, om, raptor):
         assert ora.buf("runs")["episodes"].sum() > 0
     finally:
         gpu.close()
+
+
+def test_bounded_mover_samples_gpu(pkg, om, raptor):
+    """The reference's bounded-motion check (navigation_motion_check.mm:19-32)
+    on the GPU: 1,001 environments, each with the one moving sphere at time
+    i * 0.02 s and the vehicle 1 m from its surface. The sensing kernel's
+    critic observation gives the clearance (feature 19, x5) and the sphere's
+    offset (features 21-23, x10): the clearance is 1 (gate 1e-5) and both
+    match the oracle's wclearance / wc within 1e-5."""
+    olib = om.load_oracle()
+    L = pkg.layouts
+    n = 1001
+    cfg = L.default_config(n=n, family=1, seed=2, max_steps=50)
+    sim = pkg.Sim(pkg_device(), cfg, 2, raptor=raptor)
+    try:
+        worlds = sim.download("worlds")
+        states = sim.download("states")
+        runs = sim.download("runs")
+        worlds[:] = np.zeros((), L.WORLD)
+        want_cl, want_c, points = [], [], []
+        for i in range(n):
+            w = worlds[i:i + 1]
+            w["count"] = 1
+            o = w["obstacles"][0, 0]
+            o["kind"] = 3
+            o["center"] = (6, 0, 1.5)
+            o["size"] = (0.28, 2.7, -1.57079632679)
+            o["velocity"] = (0, 0.8, 0)
+            w["goal"] = (8, 0, 1.5)
+            t = np.float32(i) * np.float32(0.02)
+            c = np.zeros(3, np.float32)
+            olib.o_wc(om.ptr(worlds[i]["obstacles"]), t, om.ptr(c))
+            p = np.array([c[0] + np.float32(0.28) + np.float32(0.18) + np.float32(1), c[1], c[2]], np.float32)
+            want_cl.append(olib.o_wclearance(om.ptr(worlds[i:i + 1]), None, om.ptr(p), t, None))
+            want_c.append(c)
+            points.append(p)
+            runs[i]["elapsed"] = t
+        points = np.array(points)
+        states["position"] = points
+        sim.upload("worlds", worlds)
+        sim.upload("states", states)
+        sim.upload("runs", runs)
+        sim.step(0)
+        co = sim.download("co").reshape(2, n, 32)[0].astype(np.float64)
+        cl = co[:, 19] * 5.0
+        assert np.all(np.abs(cl - 1.0) < 1e-5), np.max(np.abs(cl - 1.0))
+        close(cl, np.array(want_cl), "clearance vs oracle")
+        close(co[:, 21:24] * 10.0 + points, np.array(want_c), "sphere centre vs oracle")
+    finally:
+        sim.close()

@@ -160,6 +160,37 @@ def random_worlds(olib, layouts, count, seed):
     return worlds
 
 
+def motion_check_world(layouts):
+    """navigation_motion_check.mm:20-24: one bounded moving sphere (kind 3),
+    centre (6, 0, 1.5), radius 0.28, amplitude 2.7, phase -pi/2, speed 0.8
+    along y."""
+    w = np.zeros((), layouts.WORLD)
+    w["count"] = 1
+    o = w["obstacles"][0]
+    o["kind"] = 3
+    o["center"] = (6, 0, 1.5)
+    o["size"] = (0.28, 2.7, -1.57079632679)
+    o["velocity"] = (0, 0.8, 0)
+    return w
+
+
+def test_bounded_mover_samples(olib, rlib, layouts):
+    """The reference's bounded-motion check (navigation_motion_check.mm:19-32):
+    1,001 times over 20 s; 1 m from the sphere's surface the clearance is 1
+    and the depth along -x is 1.18 (gate 1e-5); restatement == reference."""
+    w = motion_check_world(layouts)
+    for i in range(1001):
+        t = np.float32(i) * np.float32(0.02)
+        c = np.zeros(3, np.float32)
+        olib.o_wc(P(w["obstacles"]), t, P(c))
+        point = np.array([c[0] + np.float32(0.28) + np.float32(0.18) + np.float32(1), c[1], c[2]], np.float32)
+        cl = olib.o_wclearance(P(w), None, P(point), t, None)
+        ray = olib.o_wray(P(w), None, P(point), P(f3(-1, 0, 0)), t)
+        assert abs(cl - 1) < 1e-5 and abs(ray - 1.18) < 1e-5, (i, cl, ray)
+        assert cl == rlib.ref_wclearance(P(w), P(point), t)
+        assert ray == rlib.ref_wray(P(w), P(point), P(f3(-1, 0, 0)), t)
+
+
 def test_world_rays_bitwise(olib, rlib, layouts):
     # main.mm:116-121 style: many worlds x 320 camera rays, CPU restatement vs reference.
     worlds = random_worlds(olib, layouts, 64, 1)
