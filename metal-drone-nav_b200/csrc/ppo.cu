@@ -186,9 +186,16 @@ __global__ void __launch_bounds__(kMbThreads) k_mb_forward(PpoArgs p, uint32_t u
         __syncthreads();
         const uint32_t rows = min(uint32_t(kMbRows), b - tile);
         const float* og = p.obs + (size_t(begin) + tile) * kActorObs;
-        for (int k = tid; k < kMbRows * kActorObs; k += kMbThreads) {
-            const int r = k / kActorObs, c = k % kActorObs;
-            if (!wide || c >= kActorObs - 3) obs_t[r * kObsPitch + c] = r < int(rows) ? og[k] : 0.0f;
+        if (wide) {  // the wide actor's means come from the tensor cores: only the geometry prior is read
+            for (int k = tid; k < kMbRows * 3; k += kMbThreads) {
+                const int r = k / 3, c = kActorObs - 3 + k % 3;
+                obs_t[r * kObsPitch + c] = r < int(rows) ? og[r * kActorObs + c] : 0.0f;
+            }
+        } else {
+            for (int k = tid; k < kMbRows * kActorObs; k += kMbThreads) {
+                const int r = k / kActorObs, c = k % kActorObs;
+                obs_t[r * kObsPitch + c] = r < int(rows) ? og[k] : 0.0f;
+            }
         }
         const float* cg = p.co + (size_t(begin) + tile) * kCriticObs;
         for (int k = tid; k < kMbRows * kCriticObs; k += kMbThreads) {
@@ -399,6 +406,9 @@ __global__ void __launch_bounds__(kGradThreads) k_mb_grad(PpoArgs p, uint32_t up
     // Thread t accumulates: W2 entry t (a = t/64, h = t%64); critic W1 entries
     // t + 256*j (j < 8); b1 (t<64), cb1 (64<=t<128), cw2 (128<=t<192), b2/ls (192..199), cb2 (200).
     float w2acc = 0.0f, cw1acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}, misc = 0.0f;
+    // Wide actor: its W1, b1 and W2 come from the tensor-core backward, so the
+    // actor's deltas, hidden activations and observations are not read here.
+    constexpr bool wide = kWide;
     for (uint32_t r0 = c0; r0 < c1; r0 += kGradTile) {
         const uint32_t nr = min(uint32_t(kGradTile), c1 - r0);
         __syncthreads();
@@ -406,15 +416,18 @@ __global__ void __launch_bounds__(kGradThreads) k_mb_grad(PpoArgs p, uint32_t up
             const int r = k / kHidden, h = k % kHidden;
             const bool v = r < int(nr);
             const size_t row = size_t(r0) + r;
-            dtile[r][h] = v ? p.mb_adelta[row * kHidden + h] : 0.0f;
+            if (!wide) {
+                dtile[r][h] = v ? p.mb_adelta[row * kHidden + h] : 0.0f;
+                htile[r][h] = v ? p.mb_ah[row * kHidden + h] : 0.0f;
+            }
             cdtile[r][h] = v ? p.mb_cdelta[row * kHidden + h] : 0.0f;
-            htile[r][h] = v ? p.mb_ah[row * kHidden + h] : 0.0f;
             chtile[r][h] = v ? p.mb_ch[row * kHidden + h] : 0.0f;
         }
-        for (int k = tid; k < kGradTile * kActorObs; k += kGradThreads) {
-            const int r = k / kActorObs, c = k % kActorObs;
-            otile[r][c] = r < int(nr) ? p.obs[(size_t(begin) + r0 + r) * kActorObs + c] : 0.0f;
-        }
+        if (!wide)
+            for (int k = tid; k < kGradTile * kActorObs; k += kGradThreads) {
+                const int r = k / kActorObs, c = k % kActorObs;
+                otile[r][c] = r < int(nr) ? p.obs[(size_t(begin) + r0 + r) * kActorObs + c] : 0.0f;
+            }
         for (int k = tid; k < kGradTile * kCriticObs; k += kGradThreads) {
             const int r = k / kCriticObs, c = k % kCriticObs;
             cotile[r][c] = r < int(nr) ? p.co[(size_t(begin) + r0 + r) * kCriticObs + c] : 0.0f;
@@ -426,14 +439,13 @@ __global__ void __launch_bounds__(kGradThreads) k_mb_grad(PpoArgs p, uint32_t up
         }
         if (tid < kGradTile) dvt[tid] = tid < int(nr) ? p.mb_dv[size_t(r0) + tid] : 0.0f;
         __syncthreads();
-        constexpr bool wide = kWide;  // actor W1/W2/b1 come from the tensor-core backward
         for (int r = 0; r < int(nr); r++) {
             if (tid < kActorObs && !wide) {
                 const float o = otile[r][tid];
 #pragma unroll
                 for (int h = 0; h < kHidden; h++) aw1[h] = fmaf(dtile[r][h], o, aw1[h]);
             }
-            {
+            if (!wide) {
                 const int a = tid >> 6, h = tid & 63;  // actor W2[a][h] = sum dm * hidden
                 w2acc = fmaf(dmt[r][a], htile[r][h], w2acc);
             }
