@@ -697,9 +697,22 @@ cudaError_t launch_wide_forward(const WideMap& obs_map, const WideMap& w1_map, c
     return cudaGetLastError();
 }
 
+// Row groups of the backward grid (hidden tiles x groups CTAs, one per SM at
+// a time): the smallest count that makes the grid whole waves of the SMs
+// (5120 hidden units: 40 tiles x 37 groups = 10 waves of 148), so no SM idles
+// while the others work; one wave of floor(SMs / tiles) groups when that
+// would take more than 16 waves.
 uint32_t wide_backward_groups(uint32_t hidden, int sm_count) {
-    const uint32_t n_tiles = hidden / kBackHidden;
-    const uint32_t g = uint32_t(sm_count) / n_tiles;
+    const uint32_t n_tiles = hidden / kBackHidden, sms = uint32_t(sm_count);
+    uint32_t a = n_tiles, b = sms;
+    while (b) {
+        const uint32_t t = a % b;
+        a = b;
+        b = t;
+    }
+    const uint32_t whole = sms / a;  // n_tiles * whole is a multiple of the SM count
+    if (size_t(n_tiles) * whole <= size_t(16) * sms) return whole;
+    const uint32_t g = sms / n_tiles;
     return g > 0 ? g : 1;
 }
 
