@@ -554,6 +554,7 @@ extern "C" int mdn_sim_destroy(mdn_sim* sim) {
         delete sim->wide;
         cudaFree(sim->lay_mem);
         delete sim->lay;
+        cudaFree(sim->report_dev);
         cudaEventDestroy(sim->ev_start);
         cudaEventDestroy(sim->ev_stop);
         if (sim->fork.fork) cudaEventDestroy(sim->fork.fork);
@@ -811,18 +812,14 @@ extern "C" int mdn_sim_report(mdn_sim* sim, double out[10]) {
     return guarded([&] {
         checked(sim);
         require(out != nullptr, MDN_ERR_INVALID, "null out");
-        std::vector<mdn_sim_run> runs(sim->n);
-        cuda_check(cudaMemcpyAsync(runs.data(), sim->buf[MDN_BUF_RUNS], sim->bytes[MDN_BUF_RUNS], cudaMemcpyDeviceToHost,
-                                   sim->stream), "report");
+        // Sim::report (main.mm:599-602), reduced on the GPU (k_report): the
+        // host reads back ten doubles instead of every run record.
+        if (!sim->report_dev)
+            cuda_check(cudaMalloc(&sim->report_dev, 10 * sizeof(double)), "report buffer");
+        cuda_check(launch_report(sim->args(0), sim->report_dev, sim->stream), "report");
+        double v[10];
+        cuda_check(cudaMemcpyAsync(v, sim->report_dev, sizeof(v), cudaMemcpyDeviceToHost, sim->stream), "report");
         sync_stream(sim->dev, sim->stream, "report");
-        // Sim::report, main.mm:599-602
-        double v[10] = {0, 0, 0, 0, 0, 0, 0, 0, 12.0, 0.0};
-        for (const auto& r : runs) {
-            v[0] += r.episodes; v[1] += r.successes; v[2] += r.collisions; v[3] += r.timeouts;
-            v[4] += r.success_time; v[5] += r.total_path; v[6] += r.total_elapsed; v[7] += r.final_progress;
-            v[8] = std::fmin(v[8], r.min_clearance);
-            v[9] = std::fmax(v[9], r.peak_speed);
-        }
         std::memcpy(out, v, sizeof(v));
     });
 }

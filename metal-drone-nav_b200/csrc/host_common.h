@@ -52,6 +52,8 @@ cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays
 cudaError_t configure_kernels();
 cudaError_t launch_reset(const SimArgs& a, bool first, cudaStream_t s);
 cudaError_t launch_world_mirror(const SimArgs& a, cudaStream_t s);
+// Sim::report's ten aggregates of the run records into out[10] (device).
+cudaError_t launch_report(const SimArgs& a, double* out, cudaStream_t s);
 StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_override);
 // flush = false leaves the step's ended episodes to the next step, which
 // must then pass `fork` (only inside a collected rollout, whose last step
@@ -113,6 +115,7 @@ struct mdn_sim {
     mdn::LayeredStep* lay = nullptr;
     void* lay_mem = nullptr;
     float* wide_partials = nullptr;                         // [hidden/128][n][4] slice sums of the wide forward
+    double* report_dev = nullptr;                           // [10] Sim::report aggregates (k_report)
     uint32_t* wide_error = nullptr;                         // barrier-timeout flag of the wide kernels
     mdn::WideStep* wide = nullptr;                          // tensor maps + launch arguments (wide actors)
     bool delay_rehearsal = false;                           // mdn_sim_set_delay_rehearsal

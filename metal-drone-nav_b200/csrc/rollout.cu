@@ -1819,6 +1819,61 @@ cudaError_t upload_camera_tables(const float* pixel_rays, const float* pool_rays
     return cudaMemcpyToSymbol(g_pool_ray, pool_rays, sizeof(float) * 80 * 3);
 }
 
+// Sim::report's aggregates (main.mm:599-602) over the run records, on the
+// GPU: one CTA; thread t adds environments t, t + 1024, ... in order (double
+// sums of the counters and float totals), then a fixed tree over the threads.
+// Only the ten results leave the device.
+constexpr int kReportThreads = 1024;
+__global__ void __launch_bounds__(kReportThreads) k_report(SimArgs a, double* out) {
+    __shared__ double part[8][kReportThreads / 32];
+    __shared__ float lo[kReportThreads / 32], hi[kReportThreads / 32];
+    double v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float mn = 12.0f, mx = 0.0f;
+    for (uint32_t i = threadIdx.x; i < a.n; i += kReportThreads) {
+        const mdn_sim_run& r = a.runs[i];
+        v[0] += r.episodes;
+        v[1] += r.successes;
+        v[2] += r.collisions;
+        v[3] += r.timeouts;
+        v[4] += r.success_time;
+        v[5] += r.total_path;
+        v[6] += r.total_elapsed;
+        v[7] += r.final_progress;
+        mn = fminf(mn, r.min_clearance);
+        mx = fmaxf(mx, r.peak_speed);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] += __shfl_xor_sync(0xffffffffu, v[k], off);
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) part[k][warp] = v[k];
+        lo[warp] = mn;
+        hi[warp] = mx;
+    }
+    __syncthreads();
+    if (threadIdx.x < 10) {
+        const int k = threadIdx.x;
+        double t = k == 8 ? 12.0 : 0.0;
+        for (int w = 0; w < kReportThreads / 32; w++) {
+            if (k < 8) t += part[k][w];
+            else if (k == 8) t = fmin(t, double(lo[w]));
+            else t = fmax(t, double(hi[w]));
+        }
+        out[k] = t;
+    }
+}
+
+cudaError_t launch_report(const SimArgs& a, double* out, cudaStream_t s) {
+    k_report<<<1, kReportThreads, 0, s>>>(a, out);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_world_mirror(const SimArgs& a, cudaStream_t s) {
     k_world_mirror<<<blocks_for(a.n, 128), 128, 0, s>>>(a);
     return cudaGetLastError();

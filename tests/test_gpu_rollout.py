@@ -435,3 +435,27 @@ def test_bounded_mover_samples_gpu(pkg, om, raptor):
         close(co[:, 21:24] * 10.0 + points, np.array(want_c), "sphere centre vs oracle")
     finally:
         sim.close()
+
+
+def test_report_matches_run_records(pkg, raptor):
+    """Sim::report (main.mm:599-602) reduced on the GPU equals the same
+    aggregates of the downloaded run records: counters exactly, float totals
+    (summed in double) within 1e-12 relative, minimum clearance and peak speed
+    exactly."""
+    cfg = pkg.layouts.default_config(n=5000, family=18, speed=1.0, distance=3.0, seed=21, max_steps=6)
+    sim = pkg.Sim(pkg_device(), cfg, 8, raptor=raptor)
+    try:
+        sim.collect()
+        sim.collect()
+        rep = sim.report()
+        runs = sim.download("runs")
+        assert runs["episodes"].sum() > 0
+        for key in ("episodes", "successes", "collisions", "timeouts"):
+            assert rep[key] == float(runs[key].astype(np.float64).sum()), key
+        for key in ("success_time", "total_path", "total_elapsed", "final_progress"):
+            want = float(runs[key].astype(np.float64).sum())
+            assert abs(rep[key] - want) <= 1e-12 * max(abs(want), 1.0), key
+        assert rep["min_clearance"] == float(min(12.0, runs["min_clearance"].min()))
+        assert rep["peak_speed"] == float(max(0.0, runs["peak_speed"].max()))
+    finally:
+        sim.close()
