@@ -2092,6 +2092,10 @@ cudaError_t fp32_peak(int sm_count, double* tflops) {
     return e;
 }
 
+// Launches per policy step of a collected rollout: sense, the previous step's
+// listed resets (k_reset_sense; the last step's k_reset_list flush instead for
+// the first step), act and advance, plus the geometry-memory hint and the
+// wide actor's tensor-core forward when they run.
 int kernels_per_step(const mdn_sim_config& c, bool wide) { return 4 + (c.geometry_memory ? 1 : 0) + (wide ? 1 : 0); }
 
 cudaError_t configure_kernels() {
