@@ -1760,6 +1760,10 @@ static cudaError_t launch_advance(const SimArgs& a, const StepPlan& plan, const 
                                   cudaStream_t s) {
     const bool own = a.runtime.enabled != 0;
     switch (plan.advance_group) {
+        case 8:
+            if (own) k_advance<8, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a, nominal);
+            else k_advance<8, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a, nominal);
+            break;
         case 4:
             if (own) k_advance<4, true><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a, nominal);
             else k_advance<4, false><<<plan.advance_grid, kAdvanceThreads, 0, s>>>(a, nominal);
@@ -1995,10 +1999,14 @@ StepPlan plan_step(uint32_t n, int sm_count, int group_override, int act_overrid
     // pairs fit one wave of three 128-thread blocks per SM, 192 environments
     // (16,384: 0.167 vs 0.214 ms with 1; 24,576: 0.179 vs 0.222), else 1
     // (32,768: 0.224 vs 0.263 ms with 2).
+    // Eight lanes on shards of at most 32 environments per SM (4,096 envs:
+    // 27.6 vs 26.0M env-steps/s with 4; 8,192: 37.5 vs 44.0M).
     int g = size_t(n) <= size_t(sm_count) * 64 ? 4 : (size_t(n) <= size_t(sm_count) * 192 ? 2 : 1);
-    if (group_override == 1 || group_override == 2 || group_override == 4) g = group_override;
+    if (size_t(n) <= size_t(sm_count) * 32) g = 8;
+    if (group_override == 1 || group_override == 2 || group_override == 4 || group_override == 8) g = group_override;
     p.advance_group = g;
-    const int per_sm = g == 1 ? advance_blocks_per_sm<1>() : (g == 2 ? advance_blocks_per_sm<2>() : advance_blocks_per_sm<4>());
+    const int per_sm = g == 1 ? advance_blocks_per_sm<1>()
+                     : (g == 2 ? advance_blocks_per_sm<2>() : (g == 4 ? advance_blocks_per_sm<4>() : advance_blocks_per_sm<8>()));
     const size_t need = (size_t(n) * g + kAdvanceThreads - 1) / kAdvanceThreads;
     p.advance_grid = int(std::max<size_t>(1, std::min<size_t>(need, size_t(sm_count) * per_sm)));
     p.reset_grid = int(std::max<size_t>(1, std::min<size_t>((size_t(n) + 3) / 4, size_t(sm_count) * 8)));

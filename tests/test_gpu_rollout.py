@@ -305,10 +305,10 @@ GROUP_CASES = [dict(family=18, sensor_delay=2, command_delay=2), dict(family=12,
                dict(family=13, max_steps=5, risk_coef=0.5)]
 
 
-@pytest.mark.parametrize("group", [1, 2, 4])
+@pytest.mark.parametrize("group", [1, 2, 4, 8])
 @pytest.mark.parametrize("case", range(len(GROUP_CASES)))
 def test_advance_lane_groups_match_oracle(pkg, om, raptor, group, case, monkeypatch):
-    """k_advance with 1, 2 and 4 lanes per environment (plan_step picks by shard
+    """k_advance with 1, 2, 4 and 8 lanes per environment (plan_step picks by shard
     size; MDN_ADVANCE_GROUP forces one) against the oracle, teacher-forced, with
     episode ends and resets inside the window."""
     monkeypatch.setenv("MDN_ADVANCE_GROUP", str(group))
