@@ -125,6 +125,14 @@ public:
                       << " timeout=" << r[3] << " wall_s=" << wall << "\n";
         return r;
     }
+    // NavigationPolicy::raw_mean (deployment.hpp) of the current actor for
+    // observation rows [rows][184], evaluated on the GPU: [rows][4] means.
+    std::vector<float> actor_means(const std::vector<float>& obs) const {
+        const uint32_t rows = uint32_t(obs.size() / 184);
+        std::vector<float> means(size_t(rows) * 4);
+        check(mdn_sim_actor_means(h_, obs.data(), rows, means.data()));
+        return means;
+    }
     float last_collect_ms() const {
         float ms = 0.0f;
         check(mdn_sim_last_collect_ms(h_, &ms));

@@ -5,6 +5,7 @@
 //   argv: workdir
 #include <cstdio>
 #include <string>
+#include <vector>
 
 #include "mdn.hpp"
 
@@ -29,6 +30,10 @@ int main(int argc, char** argv) {
         PPOTrainer warm_trainer(warm);
         warm_trainer.save_checkpoint(dir + "/warm.bin", 1, 11, 0);
         const auto actor = warm.download<float>(MDN_BUF_ACTOR);
+        // deployment inference of the fresh actor on a constant observation row
+        std::vector<float> row(184, 0.5f);
+        const auto means = warm.actor_means(row);
+        std::printf("means %.9g %.9g %.9g %.9g\n", means[0], means[1], means[2], means[3]);
         const auto a = navigation_training::evaluate(device, actor.data(), 2, 1, 0.0f, 800001, dir + "/eval.csv");
         const auto b = navigation_training::evaluate(device, actor.data(), 2, 1, 0.0f, 800001);
         std::printf("eval %.9g %.9g %.9g %.9g\n", a.success, a.collision, a.timeout, a.successful_time_s);

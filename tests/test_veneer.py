@@ -11,9 +11,10 @@ import os
 import pathlib
 import subprocess
 
+import numpy as np
 import pytest
 
-from conftest import ROOT, load_package
+from conftest import ROOT, load_oracle_module, load_package
 
 PROGRAM = ROOT / "tests" / "cpp" / "veneer_check.cpp"
 CSV_HEADER = ("seed,env,stage,family,mode,domain_amplitude,start_x,start_y,start_z,start_yaw,initial_vx,initial_vy,"
@@ -45,6 +46,19 @@ def test_veneer_evaluate_and_train(tmp_path):
     lines = {ln.split()[0]: ln.split()[1:] for ln in r.stdout.splitlines() if ln.split()}
     assert lines["eval"] == lines["eval_again"], "evaluation is not deterministic"
     success, collision, timeout, _ = (float(x) for x in lines["eval"])
+    # the fresh actor's means for an all-0.5 observation: the float64 forward
+    # of the reference's initial parameters (main.mm:548-555) within 1e-5
+    om = load_oracle_module()
+    olib = om.load_oracle()
+    actor = np.zeros(olib.o_wide_param_count(64), np.float32)
+    critic = np.zeros(olib.o_critic_param_count(), np.float32)
+    olib.o_wide_init(64, om.ptr(actor), om.ptr(critic))
+    x = np.full(184, 0.5)
+    w1, b1 = actor[:64 * 184].reshape(64, 184).astype(np.float64), actor[64 * 184:64 * 185].astype(np.float64)
+    w2, b2 = actor[64 * 185:64 * 189].reshape(4, 64).astype(np.float64), actor[64 * 189:64 * 189 + 4].astype(np.float64)
+    want = np.tanh(w1 @ x + b1) @ w2.T + b2
+    want[:3] += 0.5
+    assert np.allclose([float(v) for v in lines["means"]], want, rtol=1e-5, atol=1e-6)
     assert abs(success + collision + timeout - 1.0) < 1e-6
     rows = (tmp_path / "eval.csv").read_text().splitlines()
     assert rows[0] == CSV_HEADER and len(rows) == 129
