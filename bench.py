@@ -722,7 +722,9 @@ def main():
         "gpu_launches": args.steps * (args.horizon * per_step + per_update),
         "roofline": {"bound": "hbm", "kernel": "k_" + dom, "achieved": achieved_gbs,
                      "peak": hbm_peak, "unit": "GB/s", "frac": achieved_gbs / hbm_peak,
-                     "traffic": None if traffic is None else traffic * n, "peak_source": hbm_src},
+                     "traffic": None if traffic is None else traffic * n, "peak_source": hbm_src,
+                     "note": "the sensing kernel is bound by FP32 instruction issue, not HBM: its fraction of the "
+                             "FP32 peak is compute_roofline; this line is its bytes against the HBM roof"},
         "compute_roofline": {"bound": "fp32", "kernel": "k_" + dom, "achieved": kernels[dom]["tflop_s"],
                              "peak": fp32_peak, "unit": "TFLOP/s", "frac": kernels[dom]["fp32_frac"],
                              "peak_source": "measured (pure-FMA kernel, this run)"},
