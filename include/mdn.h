@@ -122,7 +122,14 @@ typedef struct mdn_raptor_weights {
  * Zero-initialised fields take the reference value (listed). */
 typedef struct mdn_rollout_shape {
     uint32_t actor_obs_dim;     /* 184: 2x80 pooled depth + 21 context + 3 hint (ppo.hpp:26-34) */
-    uint32_t critic_obs_dim;    /* 32 (ppo.hpp:14-16)                                        */
+    uint32_t critic_obs_dim;    /* 32 (ppo.hpp:14-16), or 64: the control-state critic of the
+                                   delay-training build (FIXED_PPO_CRITIC_OBS_DIM=64 with
+                                   NAV_CRITIC_CONTROL_STATE, sim.metal:166-180): inputs
+                                   32..63 are the RAPTOR hidden state, rotor speeds, yaw
+                                   error sine/cosine, last command, desired velocity / 2,
+                                   goal-closing speed / 4, goal distance / 10, speed / 4.
+                                   64 selects the layered networks (below), here a 64 x 64 x 1
+                                   tanh critic unless the layered fields say otherwise     */
     uint32_t actor_hidden;      /* 64 (ppo.hpp:17-19); or a multiple of 256 up to 8192: the
                                    one-hidden-layer tanh actor at that width (5120 = the
                                    967,688-parameter actor of FIXED_PPO_HIDDEN_DIM=5120,

@@ -230,20 +230,23 @@ class Sim:
 
     def __init__(self, device, cfg, horizon, raptor=None, physics=None, room=None, actor_hidden=None,
                  actor_layers=None, critic_hidden=None, critic_layers=None, actor_activation=None,
-                 critic_activation=None):
+                 critic_activation=None, critic_obs_dim=None):
         """actor_hidden: None/64 for the reference's 12,104-parameter actor, or a
         multiple of 256 (5120 = the 967,688-parameter wide actor) evaluated on
         the tensor cores. actor_layers / critic_hidden / critic_layers /
         actor_activation / critic_activation ("tanh" or "gelu"): layered
         networks (no counterpart in the reference), e.g. a 4 x 480 GELU actor
         with a 2 x 512 critic; any of them selects the layered path for both
-        networks."""
+        networks. critic_obs_dim=64: the control-state critic of the
+        reference's delay-training build (FIXED_PPO_CRITIC_OBS_DIM=64,
+        sim.metal:166-180), on the layered path."""
         self.device = device
         self.cfg = np.array(cfg, layouts.CONFIG)
         self.horizon = int(horizon)
         self.raptor = default_raptor() if raptor is None else np.array(raptor, layouts.RAPTOR)
         layered = dict(actor_layers=actor_layers, critic_hidden=critic_hidden, critic_layers=critic_layers,
-                       actor_activation=actor_activation, critic_activation=critic_activation)
+                       actor_activation=actor_activation, critic_activation=critic_activation,
+                       critic_obs_dim=critic_obs_dim)
         shape = None
         if room is not None or actor_hidden is not None or any(v is not None for v in layered.values()):
             shape = np.zeros((), layouts.SHAPE)
@@ -259,6 +262,7 @@ class Sim:
                     continue
                 shape[key] = self.ACTIVATIONS[value] if key.endswith("activation") else int(value)
         self.actor_hidden = 64 if actor_hidden is None else int(actor_hidden)
+        self.critic_obs_dim = 32 if critic_obs_dim is None else int(critic_obs_dim)
         phys = None if physics is None else np.array(physics, layouts.PARAMS)
         self.h = _P()
         check(lib().mdn_sim_create(device.h, _ptr(self.cfg), None if shape is None else _ptr(shape), self.horizon,

@@ -237,11 +237,14 @@ mdn::SimArgs mdn_sim::args(uint32_t tick) const {
     a.wide_slices = wide ? actor_hidden / 128 : 0;
     a.critic_values = nullptr;
     a.next_co = nullptr;
+    a.co_dim = co_dim;
+    a.next_co_full = nullptr;
     if (lay) {  // layered networks: k_act adds b2 and the prior to the actor outputs, as for the wide actor
         a.wide_partials = lay->out_a;
         a.wide_slices = 1;
         a.critic_values = lay->values;
         a.next_co = lay->next_co;
+        if (co_dim != kCriticObs) a.next_co_full = lay->next_critic_in;
         a.actor_b2 = lay->actor.bias_offset(lay->actor.layers);
         a.actor_log_std = lay->actor.param_count() - kActions;
     }
@@ -329,15 +332,20 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         if (shape) {
             require(shape->actor_obs_dim == 0 || shape->actor_obs_dim == kActorObs, MDN_ERR_INVALID,
                     "actor_obs_dim: this build implements the 184-input guided actor");
-            require(shape->critic_obs_dim == 0 || shape->critic_obs_dim == kCriticObs, MDN_ERR_INVALID,
-                    "critic_obs_dim: this build implements the 32-input critic");
+            require(shape->critic_obs_dim == 0 || shape->critic_obs_dim == kCriticObs ||
+                        shape->critic_obs_dim == kCriticObsControl,
+                    MDN_ERR_INVALID, "critic_obs_dim: 32, or 64 for the control-state critic");
             const uint32_t ah = shape->actor_hidden, ch = shape->critic_hidden;
             require(shape->actor_activation <= MDN_ACT_GELU && shape->critic_activation <= MDN_ACT_GELU,
                     MDN_ERR_INVALID, "activation: MDN_ACT_TANH or MDN_ACT_GELU");
             require(shape->actor_layers <= 8 && shape->critic_layers <= 8, MDN_ERR_INVALID,
                     "layers: at most 8 hidden layers per network");
+            // The control-state critic (64 inputs, sim.metal:166-180) runs on the
+            // layered kernels: the fused ones are built for 32 critic inputs.
+            const bool control_state = shape->critic_obs_dim == kCriticObsControl;
             const bool layered = shape->actor_layers > 1 || shape->critic_layers > 1 || shape->actor_activation != 0 ||
-                                 shape->critic_activation != 0 || (ch != 0 && ch != uint32_t(kHidden));
+                                 shape->critic_activation != 0 || (ch != 0 && ch != uint32_t(kHidden)) ||
+                                 control_state;
             if (layered) {
                 require(ah <= 2048 && ch <= 2048, MDN_ERR_INVALID,
                         "layered networks: actor_hidden and critic_hidden 1..2048 (0 = 64)");
@@ -352,6 +360,8 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
             sim->shape.actor_activation = shape->actor_activation;
             sim->shape.critic_activation = shape->critic_activation;
             sim->layered = layered;
+            sim->co_dim = control_state ? kCriticObsControl : kCriticObs;
+            sim->shape.critic_obs_dim = sim->co_dim;
             if (shape->flags & MDN_SHAPE_CUSTOM_ROOM) {
                 for (int j = 0; j < 3; j++) {
                     require(shape->room_max[j] > shape->room_min[j], MDN_ERR_INVALID, "room bounds");
@@ -378,7 +388,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
             mlp_actor.out = kActions;
             mlp_actor.activation = sim->shape.actor_activation;
             mlp_actor.log_std = true;
-            mlp_critic.in = kCriticObs;
+            mlp_critic.in = sim->co_dim;
             mlp_critic.hidden = sim->shape.critic_hidden;
             mlp_critic.layers = sim->shape.critic_layers;
             mlp_critic.out = 1;
@@ -398,7 +408,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         b[MDN_BUF_ACTOR] = size_t(sim->actor_params) * sizeof(float);
         b[MDN_BUF_CRITIC] = size_t(sim->critic_params) * sizeof(float);
         b[MDN_BUF_OBS] = rows * kActorObs * sizeof(float);
-        b[MDN_BUF_CO] = rows * kCriticObs * sizeof(float);
+        b[MDN_BUF_CO] = rows * sim->co_dim * sizeof(float);
         b[MDN_BUF_ACTIONS] = rows * kActions * sizeof(float);
         for (int id : {MDN_BUF_LOGP, MDN_BUF_VALUES, MDN_BUF_REWARDS, MDN_BUF_NEXT_VALUES, MDN_BUF_ADVANTAGES,
                        MDN_BUF_RETURNS, MDN_BUF_CONTACT_ID})
@@ -466,10 +476,13 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
         }
         if (sim->layered) {
             // Per-step scratch of the layered networks: two activation
-            // buffers of the wider network, the actor outputs, the values and
-            // the post-step critic observations.
+            // buffers of the wider network, the actor outputs, the values, the
+            // post-step critic observations and, for the control-state critic,
+            // its 64-input bootstrap rows.
             const size_t widest = std::max(mlp_actor.hidden, mlp_critic.hidden);
-            const size_t act_floats = n * widest, bytes = (2 * act_floats + n * 4 + n + n * kCriticObs) * sizeof(float);
+            const size_t act_floats = n * widest;
+            const size_t full_rows = sim->co_dim != kCriticObs ? n * sim->co_dim : 0;
+            const size_t bytes = (2 * act_floats + n * 4 + n + n * kCriticObs + full_rows) * sizeof(float);
             const cudaError_t e = cudaMalloc(&sim->lay_mem, bytes);
             if (e != cudaSuccess) {
                 for (int k = 0; k < MDN_BUF_COUNT; k++) cudaFree(sim->buf[k]);
@@ -491,6 +504,7 @@ extern "C" int mdn_sim_create(mdn_device* dev, const mdn_sim_config* cfg, const 
             L.out_a = f + 2 * act_floats;
             L.values = L.out_a + n * 4;
             L.next_co = L.values + n;
+            L.next_critic_in = sim->co_dim != kCriticObs ? L.next_co + n * kCriticObs : L.next_co;
             L.next_values = static_cast<float*>(sim->buf[MDN_BUF_NEXT_VALUES]);
         }
         cuda_check(cudaStreamCreateWithFlags(&sim->stream, cudaStreamNonBlocking), "cudaStreamCreate");

@@ -112,6 +112,7 @@ struct mdn_sim {
     uint32_t critic_params = mdn::kCriticParams;
     // Layered networks (mlp.cu): shapes, step launch arguments, scratch.
     bool layered = false;
+    uint32_t co_dim = mdn::kCriticObs;  // critic observation width: 32, or 64 (control-state critic)
     mdn::LayeredStep* lay = nullptr;
     void* lay_mem = nullptr;
     float* wide_partials = nullptr;                         // [hidden/128][n][4] slice sums of the wide forward

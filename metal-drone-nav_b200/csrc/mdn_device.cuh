@@ -166,6 +166,33 @@ __device__ __forceinline__ float obstacle_clearance(uint32_t kind, const float* 
     return distance - 0.18f;
 }
 
+// Input 32 + j of the control-state critic's observation (sim.metal:166-180,
+// built with FIXED_PPO_CRITIC_OBS_DIM=64 and NAV_CRITIC_CONTROL_STATE):
+// j 0-15 the RAPTOR hidden state, 16-19 the rotor speeds, 20-21 sine and cosine
+// of the run's yaw minus the body's yaw, 22-25 the last policy command, 26-28
+// the desired velocity / 2, 29 the goal-closing speed / 4, 30 the goal
+// distance / 10, 31 the speed / 4. The arguments describe the state the
+// observation is of: hidden, rpm, dvel (desired velocity) may live in
+// registers when j is a compile-time index, or in device memory.
+__device__ __forceinline__ float control_state_input(int j, const float* hidden, const float* rpm, const float q[4],
+                                                     const float pos[3], const float vel[3], const float* dvel,
+                                                     const mdn_sim_run& run, const mdn_world& w) {
+    if (j < 16) return hidden[j];
+    if (j < 20) return rpm[j - 16];
+    if (j < 22) {
+        const float body_yaw =
+            atan2f(2.0f * (q[0] * q[3] + q[1] * q[2]), 1.0f - 2.0f * (q[2] * q[2] + q[3] * q[3]));
+        return j == 20 ? sinf(run.yaw - body_yaw) : cosf(run.yaw - body_yaw);
+    }
+    if (j < 26) return run.previous_nav[j - 22];
+    if (j < 29) return dvel[j - 26] / 2.0f;
+    const float g0 = w.goal[0] - pos[0], g1 = w.goal[1] - pos[1], g2 = w.goal[2] - pos[2];
+    const float distance = len3(g0, g1, g2);
+    if (j == 29) return (g0 * vel[0] + g1 * vel[1] + g2 * vel[2]) / fmaxf(distance, 1e-6f) / 4.0f;
+    if (j == 30) return distance / 10.0f;
+    return len3(vel[0], vel[1], vel[2]) / 4.0f;
+}
+
 // Room term of wclearance, world.hpp:85 (p - lo == p + 2 etc. for the reference room).
 __device__ __forceinline__ float room_clearance(const SimArgs& a, const float p[3]) {
     return fminf(fminf(p[0] - a.room_lo[0], a.room_hi[0] - p[0]),

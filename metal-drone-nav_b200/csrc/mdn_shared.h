@@ -12,6 +12,11 @@ constexpr int kPixels = 320;
 constexpr int kFrames = 8;
 constexpr int kActorObs = 184;
 constexpr int kCriticObs = 32;
+// The control-state critic's inputs (FIXED_PPO_CRITIC_OBS_DIM=64 with
+// NAV_CRITIC_CONTROL_STATE, sim.metal:166-180): the 32 above, then 32
+// training-only inputs (RAPTOR hidden state, rotor speeds, yaw error, last
+// command, desired velocity, goal-closing speed, goal distance, speed).
+constexpr int kCriticObsControl = 64;
 constexpr int kHidden = 64;
 constexpr int kActions = 4;
 constexpr int kActorB1 = kHidden * kActorObs;
@@ -101,6 +106,12 @@ struct SimArgs {
     // 64-unit one (both null otherwise).
     const float* critic_values;
     float* next_co;
+    // Width of a critic observation row in co: kCriticObs, or
+    // kCriticObsControl for the control-state critic (layered networks only),
+    // whose bootstrap rows k_control_state assembles in next_co_full[n][64]
+    // (next_co stays [n][32]; null for the 32-input critic).
+    uint32_t co_dim;
+    float* next_co_full;
     // Mechanical contact audit (null = off): results[tick][n], safety margin.
     mdn_contact_audit* audit;
     float audit_margin;

@@ -416,7 +416,7 @@ cudaError_t launch_layered_step_forward(const LayeredStep& L, uint32_t n, uint32
 }
 
 cudaError_t launch_layered_bootstrap(const LayeredStep& L, uint32_t n, uint32_t tick, cudaStream_t s) {
-    return network_forward(L.critic, L.critic_params, L.next_co, n, 0, L.act, L.next_values + size_t(tick) * n, true, s);
+    return network_forward(L.critic, L.critic_params, L.next_critic_in, n, 0, L.act, L.next_values + size_t(tick) * n, true, s);
 }
 
 void init_layered(const MlpShape& actor, const MlpShape& critic, std::vector<float>& a, std::vector<float>& c) {

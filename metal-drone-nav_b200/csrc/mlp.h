@@ -117,11 +117,13 @@ struct LayeredStep {
     float* out_a;            // [n][4] actor output layer (no bias; k_act adds b2 and the prior)
     float* values;           // [n] critic values of this step's rows
     float* next_co;          // [n][32] post-step critic observations (k_advance)
+    float* next_critic_in;   // [n][critic.in] the bootstrap critic's inputs: next_co, or the
+                             // control-state critic's 64-input rows (k_control_state)
     float* next_values;      // rollout bootstrap values [horizon * n]
 };
 // Actor and critic forward over the step's rows (tick * n ...): out_a, values.
 cudaError_t launch_layered_step_forward(const LayeredStep& L, uint32_t n, uint32_t tick, cudaStream_t s);
-// Critic over next_co into next_values[tick * n ...] (sim.metal:327's bootstrap value).
+// Critic over next_critic_in into next_values[tick * n ...] (sim.metal:327's bootstrap value).
 cudaError_t launch_layered_bootstrap(const LayeredStep& L, uint32_t n, uint32_t tick, cudaStream_t s);
 
 // A network's forward over `rows` rows of x (device memory, from row 0):

@@ -468,7 +468,7 @@ __device__ __forceinline__ void sense_env(const SimArgs& a, uint32_t i, WarpScen
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) cand = fminf(cand, __shfl_xor_sync(0xffffffffu, cand, off));
         const float clearance = count ? fminf(room_clearance(a, pos), cand) : room_clearance(a, pos);
-        float* co = a.co + row * kCriticObs;
+        float* co = a.co + row * a.co_dim;
         float v = 0.0f;
         const int j = lane;
         if (j < 3) v = (w.goal[j] - pos[j]) / 10.0f;
@@ -487,8 +487,33 @@ __device__ __forceinline__ void sense_env(const SimArgs& a, uint32_t i, WarpScen
             }
         } else if (j == 30) v = w.wind[0];
         else v = w.wind[1];
-        co[j] = v;
+        co[j] = v;  // inputs 32..63 of the control-state critic: k_control_state
     }
+}
+
+// Inputs 32..63 of the control-state critic's observation (sim.metal:166-180),
+// one warp per environment, lane j writing input 32 + j, from the state in
+// device memory. Launched after the sensing kernels into this step's critic
+// observation rows (the state sim_observe sees), and after k_advance into
+// next_co_full, whose first 32 inputs it copies from the rows k_advance left
+// in next_co (the post-step state of the bootstrap value, sim.metal:327): the
+// episode resets of the step run later in both cases. Environments the
+// sensing skips in evaluation mode are skipped here too.
+constexpr int kControlWarps = 8;
+__global__ void __launch_bounds__(kControlWarps * 32) k_control_state(SimArgs a, int post_step) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t i = blockIdx.x * kControlWarps + (threadIdx.x >> 5);
+    if (i >= a.n) return;  // warp-uniform
+    const mdn_sim_run& run = a.runs[i];
+    if (!post_step && a.cfg.eval && run.episodes) return;
+    const mdn_physics_state& st = a.states[i];
+    const float q[4] = {st.orientation_wxyz[0], st.orientation_wxyz[1], st.orientation_wxyz[2], st.orientation_wxyz[3]};
+    const float pos[3] = {st.position[0], st.position[1], st.position[2]};
+    const float vel[3] = {st.linear_velocity[0], st.linear_velocity[1], st.linear_velocity[2]};
+    float* row = post_step ? a.next_co_full + size_t(i) * a.co_dim : a.co + (size_t(a.tick) * a.n + i) * a.co_dim;
+    if (post_step) row[lane] = a.next_co[size_t(i) * kCriticObs + lane];
+    row[kCriticObs + lane] = control_state_input(lane, run.hidden, st.rpm, q, pos, vel, run.desired_velocity, run,
+                                                 a.worlds[i]);
 }
 
 // One policy step's sensing, one warp per environment. Environments whose
@@ -1150,7 +1175,7 @@ __global__ void __launch_bounds__(kActWarps * 32) k_act(SimArgs a) {
         for (int e = 0; e < kActEnvs; e++) {
             const float* og = a.obs + (row0 + e) * kActorObs;
             for (int k = lane; k < kActorObs; k += 32) my_obs[e * kActorObs + k] = e < envs ? og[k] : 0.0f;
-            my_co[e * kCriticObs + lane] = e < envs ? a.co[(row0 + e) * kCriticObs + lane] : 0.0f;
+            if (own_critic) my_co[e * kCriticObs + lane] = e < envs ? a.co[(row0 + e) * kCriticObs + lane] : 0.0f;
         }
         __syncwarp();
         // actor pre-activations, in-order dot from zero then the bias (cpu_reference.hpp:437-442)
@@ -1643,7 +1668,7 @@ __global__ void __launch_bounds__(kAdvanceThreads, G == 1 ? 4 : 3) k_advance(Sim
                 co[31] = w.wind[1];
                 float part = 0.0f;
                 if (a.next_co) {  // layered critic: keep the observation for it
-                    if (r == 0)
+                    if (r == 0)  // (inputs 32..63 of the control-state critic: k_control_state)
 #pragma unroll
                         for (int k = 0; k < kCriticObs; k++) a.next_co[size_t(i) * kCriticObs + k] = co[k];
                 } else
@@ -1909,6 +1934,12 @@ static cudaError_t launch_wide(const SimArgs& a, const WideStep* wide, cudaStrea
     return launch_wide_forward(wide->obs_map, wide->w1_map, p, wide->sm_count, s);
 }
 
+// The control-state critic's extra inputs (nothing for the 32-input critic).
+static void launch_control_state(const SimArgs& a, bool post_step, cudaStream_t s) {
+    if (a.co_dim == kCriticObsControl)
+        k_control_state<<<blocks_for(a.n, kControlWarps), kControlWarps * 32, 0, s>>>(a, post_step ? 1 : 0);
+}
+
 static void launch_sense(const SimArgs& a, cudaStream_t s) {
     k_sense<<<blocks_for(a.n, kSenseWarps), kSenseWarps * 32, 0, s>>>(a);
 }
@@ -1948,11 +1979,13 @@ cudaError_t launch_step(const SimArgs& a, const StepPlan& plan, const mdn_physic
     }
     if (a.cfg.geometry_memory)
         k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
+    launch_control_state(a, false, s);
     cudaError_t e = launch_wide(a, wide, s);
     if (e == cudaSuccess && layered) e = launch_layered_step_forward(*layered, a.n, a.tick, s);
     if (e != cudaSuccess) return e;
     launch_act(a, plan, s);
     e = launch_advance(a, plan, nominal, s);
+    if (e == cudaSuccess) launch_control_state(a, true, s);
     if (e == cudaSuccess && layered) e = launch_layered_bootstrap(*layered, a.n, a.tick, s);
     if (e != cudaSuccess) return e;
     if (flush) launch_reset_list(a, plan, s);
@@ -1965,6 +1998,7 @@ cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, const m
     launch_sense(a, s);
     if (a.cfg.geometry_memory)
         k_memory_hint<<<blocks_for(a.n, kMemWarps), kMemWarps * 32, kMemWarps * sizeof(MemScene), s>>>(a);
+    launch_control_state(a, false, s);
     cudaEventRecord(ev[1], s);
     cudaError_t we = launch_wide(a, wide, s);
     if (we == cudaSuccess && layered) we = launch_layered_step_forward(*layered, a.n, a.tick, s);
@@ -1972,6 +2006,7 @@ cudaError_t launch_step_profiled(const SimArgs& a, const StepPlan& plan, const m
     launch_act(a, plan, s);
     cudaEventRecord(ev[2], s);
     cudaError_t e = launch_advance(a, plan, nominal, s);
+    if (e == cudaSuccess) launch_control_state(a, true, s);
     if (e == cudaSuccess && layered) e = launch_layered_bootstrap(*layered, a.n, a.tick, s);
     if (e != cudaSuccess) return e;
     launch_reset_list(a, plan, s);

@@ -1838,6 +1838,41 @@ static void critic_obs(const o_sim* s, const mdn_physics_state* st, const mdn_wo
     }
 }
 
+/* sim.metal:166-180, the control-state inputs 32..63 of the delay-training
+ * build's critic (FIXED_PPO_CRITIC_OBS_DIM=64, NAV_CRITIC_CONTROL_STATE=1;
+ * the reference has this only in its Metal kernel, so this restatement is the
+ * check). o points at input 32. */
+static void critic_control_state(const mdn_physics_state* st, const mdn_world* w, const mdn_sim_run* run, float* o) {
+    for (int j = 0; j < 16; j++) o[j] = run->hidden[j];
+    for (int j = 0; j < 4; j++) {
+        o[16 + j] = st->rpm[j];
+        o[22 + j] = run->previous_nav[j];
+    }
+    const float* q = st->orientation_wxyz;
+    const float yaw = atan2f(2.0f * (q[0] * q[3] + q[1] * q[2]), 1.0f - 2.0f * (q[2] * q[2] + q[3] * q[3]));
+    o[20] = sinf(run->yaw - yaw);
+    o[21] = cosf(run->yaw - yaw);
+    for (int j = 0; j < 3; j++) o[26 + j] = run->desired_velocity[j] / 2.0f;
+    const float g[3] = {w->goal[0] - st->position[0], w->goal[1] - st->position[1], w->goal[2] - st->position[2]};
+    const float* v = st->linear_velocity;
+    const float distance = sqrtf(g[0] * g[0] + g[1] * g[1] + g[2] * g[2]);
+    o[29] = (g[0] * v[0] + g[1] * v[1] + g[2] * v[2]) / fmaxf(distance, 1e-6f) / 4.0f;
+    o[30] = distance / 10.0f;
+    o[31] = sqrtf(v[0] * v[0] + v[1] * v[1] + v[2] * v[2]) / 4.0f;
+}
+
+/* The critic observation (sim_critic_obs, sim.metal:159-180) of `count`
+ * environments from their state, `dim` = 32 or 64 (control-state critic)
+ * floats per row; the room is the simulator's. */
+void o_critic_obs_rows(const o_sim* s, const mdn_physics_state* states, const mdn_world* worlds,
+                       const mdn_sim_run* runs, uint32_t count, uint32_t dim, float* out) {
+    for (uint32_t n = 0; n < count; n++) {
+        float* o = out + (size_t)n * dim;
+        critic_obs(s, &states[n], &worlds[n], &runs[n], o);
+        if (dim == 64) critic_control_state(&states[n], &worlds[n], &runs[n], o + COBS);
+    }
+}
+
 /* sim.metal:182-228 (cpu_reference.hpp:303-377) */
 static void observe_env(o_sim* s, uint32_t t, uint32_t n) {
     const mdn_sim_config* c = &s->cfg;

@@ -92,6 +92,10 @@ void o_sim_act(o_sim* s, uint32_t tick);
 void o_sim_advance(o_sim* s, uint32_t tick);
 void o_sim_step(o_sim* s, uint32_t tick);
 void o_sim_gae_normalize(o_sim* s, int normalize);
+/* sim_critic_obs (sim.metal:159-180) of `count` environments from their state:
+ * dim = 32, or 64 with the control-state inputs of the delay-training build. */
+void o_critic_obs_rows(const o_sim* s, const mdn_physics_state* states, const mdn_world* worlds,
+                       const mdn_sim_run* runs, uint32_t count, uint32_t dim, float* out);
 /* One PPO rollout update with the given chunk order (epochs x chunks) and the
  * per-update Adam bias corrections; out[4] = policy, value, entropy, ratio means.
  * grad_norms (optional) receives actor/critic pre-clip norms per update. */

@@ -85,6 +85,7 @@ def load_oracle():
     for n in ("o_sim_observe", "o_sim_act", "o_sim_advance", "o_sim_step"):
         d(n, None, _P, _U)
     d("o_sim_gae_normalize", None, _P, ctypes.c_int)
+    d("o_critic_obs_rows", None, _P, _P, _P, _P, _U, _U, _P)
     d("o_sim_train_rollout", None, _P, _U, _U, _P, _U, _P, _P, _P, _P)
     d("o_set_threads", None, ctypes.c_int)
     d("o_sim_set_task_control", None, _P, _P)
@@ -293,6 +294,17 @@ class OracleSim(_Buffers):
 
     def gae(self, normalize=True):
         self.lib.o_sim_gae_normalize(self.h, int(normalize))
+
+    def critic_obs_rows(self, states, worlds, runs, dim=32):
+        """sim_critic_obs (sim.metal:159-180) of the given environments' state
+        in this simulator's room: [count][dim], dim 64 = the control-state
+        critic's observation."""
+        states = np.ascontiguousarray(states, self.layouts.STATE)
+        worlds = np.ascontiguousarray(worlds, self.layouts.WORLD)
+        runs = np.ascontiguousarray(runs, self.layouts.RUN)
+        out = np.zeros((states.size, dim), np.float32)
+        self.lib.o_critic_obs_rows(self.h, ptr(states), ptr(worlds), ptr(runs), states.size, dim, ptr(out))
+        return out
 
     def rows_grad(self, rows, batch):
         """Raw [actor | critic] gradient over explicit rollout rows, loss scale 1/batch."""

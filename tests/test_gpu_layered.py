@@ -24,6 +24,9 @@ SHAPES = {
     # BASELINE config 3's 4 x 480 GELU actor with its 2 x 512 critic
     "4x480-gelu/2x512": dict(actor_hidden=480, actor_layers=4, actor_activation="gelu", critic_hidden=512,
                              critic_layers=2),
+    # the delay-training build's control-state critic: 64 inputs, 1 x 64 tanh
+    # (FIXED_PPO_CRITIC_OBS_DIM=64 with NAV_CRITIC_CONTROL_STATE, sim.metal:166-180)
+    "control-state-critic": dict(critic_obs_dim=64),
 }
 
 
@@ -33,9 +36,9 @@ def mlp():
 
 
 def nets(mlp, shape):
-    a = mlp.Net(184, shape["actor_hidden"], shape.get("actor_layers", 1), 4, shape.get("actor_activation", "tanh"),
+    a = mlp.Net(184, shape.get("actor_hidden", 64), shape.get("actor_layers", 1), 4, shape.get("actor_activation", "tanh"),
                 log_std=True)
-    c = mlp.Net(32, shape.get("critic_hidden", 64), shape.get("critic_layers", 1), 1,
+    c = mlp.Net(shape.get("critic_obs_dim", 32), shape.get("critic_hidden", 64), shape.get("critic_layers", 1), 1,
                 shape.get("critic_activation", "tanh"))
     return a, c
 
@@ -120,7 +123,7 @@ def test_layered_rollout_matches_f64(layouts, mlp, name, collect):
                 sim.step(t)
         dev.finish()
         obs = sim.download("obs").reshape(T, n, 184)
-        co = sim.download("co").reshape(T, n, 32)
+        co = sim.download("co").reshape(T, n, c_net.inp)
         acts = sim.download("actions").reshape(T, n, 4)
         values = sim.download("values").reshape(T, n)
         nxt = sim.download("next_values").reshape(T, n)
@@ -161,7 +164,7 @@ def test_layered_update_gradient(layouts, mlp, name):
         dev.finish()
         rows = n * T
         obs = sim.download("obs").reshape(rows, 184)
-        co = sim.download("co").reshape(rows, 32)
+        co = sim.download("co").reshape(rows, c_net.inp)
         acts = sim.download("actions").reshape(rows, 4)
         logp = sim.download("logp")
         tr.rollout_update(0)
@@ -184,6 +187,69 @@ def test_layered_update_gradient(layouts, mlp, name):
     finally:
         tr.close()
         sim.close()
+        dev.close()
+
+
+def test_control_state_observation_matches_oracle(layouts):
+    """The 64-input critic observation of every step, single steps through
+    episode ends, against the oracle's restatement of sim_critic_obs
+    (sim.metal:159-180) on the state the step started from. Inputs 0..31 and
+    the control-state inputs are bit-exact except 52/53 (sine and cosine of
+    the yaw error: CUDA's atan2f/sinf/cosf against the C library's, within
+    2e-6). Also: the 32-input simulator's rows are unchanged by the wider
+    layout (same seed, same first step)."""
+    pkg = load_package()
+    om = _load_module("mdn_oracle_py", ROOT / "oracle" / "oracle.py")
+    n, T = 700, 6
+    # family 17 (static clutter rooms): no sinf-placed movers, so the clearance
+    # and obstacle-offset inputs are bit-exact too
+    _, dev, sim = make(layouts, dict(critic_obs_dim=64), n, T, seed=21, family=17, speed=1.0, distance=3.0,
+                       max_steps=4, sensor_delay=2, command_delay=2)
+    ora = om.OracleSim(layouts, sim.cfg, T, sim.raptor)
+    try:
+        assert sim.critic_params == 64 * 64 + 64 + 64 + 1
+        ended, live = 0, 0.0
+        for t in range(T):
+            pre = {k: sim.download(k) for k in ("states", "worlds", "runs")}
+            sim.step(t)
+            dev.finish()
+            co = sim.download("co").reshape(T, n, 64)[t]
+            ref = ora.critic_obs_rows(pre["states"], pre["worlds"], pre["runs"], 64)
+            exact = np.r_[0:52, 54:64]
+            assert np.array_equal(co[:, exact], ref[:, exact]), f"t={t}: {np.argwhere(co[:, exact] != ref[:, exact])[:4]}"
+            assert np.max(np.abs(co[:, 52:54] - ref[:, 52:54])) <= 2e-6, t
+            live = max(live, float(np.abs(co[:, 32:48]).max()) * float(np.abs(co[:, 48:52]).max()))
+            ended += int((sim.download("terminated") | sim.download("truncated")).reshape(T, n)[t].sum())
+        assert ended > 0 and live > 0  # episode ends; a non-zero RAPTOR hidden state and rotor speeds
+    finally:
+        sim.close()
+        dev.close()
+    # the same first step of the 32-input simulator writes the same first 32 inputs
+    dev = pkg.Device(0)
+    cfg = layouts.default_config(n=n, family=18, seed=21, speed=1.0, distance=3.0, max_steps=4, sensor_delay=2,
+                                 command_delay=2)
+    narrow = pkg.Sim(dev, cfg, T)
+    wide = pkg.Sim(dev, cfg, T, critic_obs_dim=64)
+    try:
+        narrow.step(0)
+        wide.step(0)
+        dev.finish()
+        assert np.array_equal(narrow.download("co").reshape(T, n, 32)[0],
+                              wide.download("co").reshape(T, n, 64)[0, :, :32])
+    finally:
+        narrow.close()
+        wide.close()
+        dev.close()
+
+
+def test_control_state_rejects_other_widths(layouts):
+    pkg = load_package()
+    dev = pkg.Device(0)
+    try:
+        for dim in (16, 48, 128):
+            with pytest.raises(pkg.MdnError):
+                pkg.Sim(dev, layouts.default_config(n=64, family=17, seed=1), 2, critic_obs_dim=dim)
+    finally:
         dev.close()
 
 
