@@ -48,3 +48,24 @@ def test_control_state_rows(layouts, oracle_mod, raptor):
         seen_hidden = seen_hidden or np.abs(ctl[:, 0:16]).max() > 0
         seen_rpm = seen_rpm or np.abs(ctl[:, 16:20]).max() > 0
     assert seen_hidden and seen_rpm
+
+
+def test_control_state_at_the_goal(layouts, oracle_mod, raptor):
+    """Goal at the drone's position: the goal-closing speed divides by the
+    1e-6 floor of the distance (sim.metal:178), so it stays finite (zero), and
+    the distance input is zero. Identity attitude with run yaw 0.3: yaw error
+    0.3 (sine/cosine of it)."""
+    cfg = layouts.default_config(n=2, family=17, seed=3)
+    ora = oracle_mod.OracleSim(layouts, cfg, 1, raptor)
+    st, w, run = ora.buf("states").copy(), ora.buf("worlds").copy(), ora.buf("runs").copy()
+    st["orientation_wxyz"] = [1.0, 0.0, 0.0, 0.0]
+    st["linear_velocity"] = [[0.5, -1.0, 2.0], [0.0, 0.0, 0.0]]
+    w["goal"] = st["position"]
+    run["yaw"] = 0.3
+    ctl = ora.critic_obs_rows(st, w, run, 64)[:, 32:]
+    assert np.all(np.isfinite(ctl))
+    assert np.all(ctl[:, 29] == 0.0) and np.all(ctl[:, 30] == 0.0)
+    assert np.allclose(ctl[:, 20], np.sin(np.float32(0.3)), atol=1e-7)
+    assert np.allclose(ctl[:, 21], np.cos(np.float32(0.3)), atol=1e-7)
+    assert ctl[0, 31] == np.float32(np.sqrt(np.float32(0.25 + 1.0 + 4.0))) / np.float32(4)
+    assert ctl[1, 31] == 0.0
