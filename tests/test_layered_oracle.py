@@ -39,17 +39,18 @@ def test_layouts_and_counts(mlp):
     assert b_off == w_off + 4 * 480 and b_off + 4 + 4 == a.param_count()
 
 
-@pytest.mark.parametrize("kind", ["tanh", "gelu"])
-def test_gradient_matches_finite_differences(mlp, kind):
+@pytest.mark.parametrize("kind,critic_in", [("tanh", 32), ("gelu", 32), ("tanh", 64)])
+def test_gradient_matches_finite_differences(mlp, kind, critic_in):
+    """critic_in 64: the control-state critic's input width."""
     rng = np.random.default_rng(3)
     a_net = mlp.Net(184, 7, 3, 4, kind, log_std=True)
-    c_net = mlp.Net(32, 5, 2, 1, kind)
+    c_net = mlp.Net(critic_in, 5, 2, 1, kind)
     actor = rng.normal(0, 0.3, a_net.param_count())
     actor[-4:] = rng.uniform(-1.5, -0.5, 4)
     critic = rng.normal(0, 0.3, c_net.param_count())
     rows = 9
     obs = rng.normal(0, 1, (rows, 184))
-    co = rng.normal(0, 1, (rows, 32))
+    co = rng.normal(0, 1, (rows, critic_in))
     actions = rng.normal(0, 1, (rows, 4))
     adv = rng.normal(0, 1, rows)
     ret = rng.normal(0, 1, rows)
